@@ -1,0 +1,409 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized GEMV hot path (and, as extra keys, the MoE layer).
+
+Workload ("quantized GEMV sweep"): one step is one
+pass over all 16 cases {1536x1536, 6144x1536, 1536x6144, 262144x1536} x
+{Q8_0, Q4_K, Q6_K, BF16}, batch 1, W ~ N(0, 0.02) quantized by the build's
+own quantizer, x ~ N(0, 1), seed 1.  Metric: algorithmic HBM bytes
+(weights in block size + 4*cols + 4*rows) per second, whole job.  One step
+streams 1.9 GB, far more than the 126 MB L2, so no case finds its weights in
+L2 from the previous step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (under torchrun): every matrix is row-sharded across the ranks, each
+rank computes its rows and the output is all-gathered with NCCL
+(g4_matmul_sharded): strong scaling, value = full-job bytes / max-rank time.
+--impl reference times the CPU restatement of the reference Vector-API
+kernels (oracle/, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SHAPES = [(1536, 1536), (6144, 1536), (1536, 6144), (262144, 1536)]
+FORMATS = [("Q8_0", 8), ("Q4_K", 12), ("Q6_K", 14), ("BF16", 30)]
+METRIC = "quant GEMV HBM GB/s"
+FALLBACK_HBM = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def alg_bytes(t: int, rows: int, cols: int) -> int:
+    bs, ts = {8: (32, 34), 12: (256, 144), 14: (256, 210), 30: (1, 2), 0: (1, 4)}[t]
+    return rows * cols // bs * ts + 4 * cols + 4 * rows
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.proc = None
+        self.dev = device_index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def make_cases(seed: int = 1):
+    from gemma4_kt_b200 import synth
+
+    cases = []
+    for rows, cols in SHAPES:
+        rng = np.random.default_rng(seed)
+        w = synth.normal(rng, rows * cols)
+        x = rng.standard_normal(cols, dtype=np.float32)
+        for name, t in FORMATS:
+            cases.append({"name": name, "type": t, "rows": rows, "cols": cols, "raw": synth.quantize(t, w), "x": x})
+        del w
+    return cases
+
+
+# ------------------------------------------------------------------ CPU arm
+def cpu_sample_run(cases, budget_rows: int, threads: int):
+    """Oracle (reference restatement) over a bounded row sample of every case:
+    returns (bytes processed, seconds)."""
+    from oracle import oracle
+
+    total_b, total_t = 0, 0.0
+    for c in cases:
+        rows = min(c["rows"], budget_rows)
+        t0 = time.perf_counter()
+        oracle.matmul(c["type"], c["raw"], c["x"], rows, c["cols"], threads=threads)
+        total_t += time.perf_counter() - t0
+        total_b += alg_bytes(c["type"], rows, c["cols"])
+    return total_b, total_t
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    oracle.build()
+    cases = make_cases()
+    threads = os.cpu_count() or 1
+    budget = 16384  # rows per case per step: about 10 s of CPU work per step on 8 cores
+    for _ in range(args.warmup):
+        cpu_sample_run(cases, 1024, threads)
+    b_tot, t_tot = 0, 0.0
+    for _ in range(args.steps):
+        b, t = cpu_sample_run(cases, budget, threads)
+        b_tot += b
+        t_tot += t
+    gbs = b_tot / t_tot / 1e9
+    sample = f"first min(rows,{budget}) rows of each of the 16 sweep matrices per step"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_tot / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C2 quantized GEMV sweep (4 shapes x Q8_0/Q4_K/Q6_K/BF16), batch 1",
+                   "l2": "n/a (host CPU)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference Kotlin/JVM path cannot run on this image (no JVM); timed: the C restatement of its "
+                "512-bit vectorDot kernels in oracle/",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+
+    import __graft_entry__
+
+    g4 = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    ctx = g4.Context(local_rank)
+    if world > 1:
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        uid = (C.c_ubyte * 128)()
+        if rank == 0:
+            g4.lib().g4_dist_unique_id(uid)
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
+        from gemma4_kt_b200._lib import check
+
+        check(g4.lib().g4_dist_init(ctx.handle, rank, world, uid), ctx.handle, "g4_dist_init")
+
+    cases = make_cases()
+    step_bytes = sum(alg_bytes(c["type"], c["rows"], c["cols"]) for c in cases)
+    for c in cases:
+        if world > 1:
+            per = c["rows"] // world
+            c["w"] = g4.FloatTensorFactory.create_rows(ctx, c["type"], c["raw"], c["cols"], rank * per, per)
+        else:
+            c["w"] = g4.FloatTensorFactory.create(ctx, c["type"], c["raw"], c["rows"] * c["cols"])
+        c["xd"] = torch.from_numpy(c["x"]).to(dev)
+        c["yd"] = torch.empty(c["rows"], dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(dev)
+    sp = stream.cuda_stream
+    import ctypes as C
+
+    L = g4.lib()
+
+    def step(record=None):
+        for i, c in enumerate(cases):
+            if record is not None:
+                record[i][0].record(stream)
+            if world > 1:
+                rc = L.g4_matmul_sharded(ctx.handle, c["w"].handle, C.c_void_p(c["xd"].data_ptr()),
+                                         C.c_void_p(c["yd"].data_ptr()), c["rows"], c["cols"], C.c_void_p(sp))
+            else:
+                rc = L.g4_matmul(ctx.handle, c["w"].handle, 0, C.c_void_p(c["xd"].data_ptr()),
+                                 C.c_void_p(c["yd"].data_ptr()), c["rows"], c["cols"], C.c_void_p(sp))
+            if rc:
+                raise RuntimeError(ctx.last_error())
+            if record is not None:
+                record[i][1].record(stream)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    clk = ClockSampler(local_rank)
+    clk.__enter__()
+    time.sleep(0.3)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    ctx.sync(sp)
+
+    # instrumented pass: CUDA events around every launch (on the launching
+    # stream) give each kernel's average duration for the roofline
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in cases]
+          for _ in range(args.steps)]
+    for s_ in range(args.steps):
+        step(ev[s_])
+    torch.cuda.synchronize()
+    per_case = np.array([np.mean([ev[s_][i][0].elapsed_time(ev[s_][i][1]) for s_ in range(args.steps)])
+                         for i in range(len(cases))])
+
+    # headline: exactly K steps, barrier + synchronize on both sides
+    barrier()
+    torch.cuda.synchronize()
+    t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0e.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk.__exit__(None, None, None)
+    ms = t0e.elapsed_time(t1e) / args.steps
+    ctx.sync(sp)
+    if world > 1:
+        import torch.distributed as dist
+
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    value = step_bytes / (ms * 1e-3) / 1e9
+
+    # roofline of the dominant kernel
+    hbm, hbm_kind = peaks()
+    dom = int(np.argmax(per_case))
+    c = cases[dom]
+    dom_bytes = alg_bytes(c["type"], c["rows"], c["cols"]) / world
+    achieved = dom_bytes / (per_case[dom] * 1e-3) / 1e9
+    breakdown = []
+    for i, cc in enumerate(cases):
+        b = alg_bytes(cc["type"], cc["rows"], cc["cols"]) / world
+        breakdown.append({"case": f"{cc['name']} {cc['rows']}x{cc['cols']}", "us": round(per_case[i] * 1e3, 2),
+                          "GBps": round(b / (per_case[i] * 1e-3) / 1e9, 1)})
+
+    # end to end through the host-buffer API (pinned host arrays), N=1
+    e2e = None
+    if world == 1:
+        xs = [torch.from_numpy(cc["x"]).pin_memory() for cc in cases]
+        ys = [torch.empty(cc["rows"], dtype=torch.float32).pin_memory() for cc in cases]
+        h2d = sum(cc["cols"] * 4 for cc in cases)
+        d2h = sum(cc["rows"] * 4 for cc in cases)
+
+        def e2e_step():
+            for i, cc in enumerate(cases):
+                rc = L.g4_matmul_host(ctx.handle, cc["w"].handle, 0, C.c_void_p(xs[i].data_ptr()),
+                                      C.c_void_p(ys[i].data_ptr()), cc["rows"], cc["cols"])
+                if rc:
+                    raise RuntimeError(ctx.last_error())
+
+        for _ in range(2):
+            e2e_step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        e2e_s = (time.perf_counter() - t0) / args.steps
+        ok = all(np.allclose(ys[i].numpy(), cc["yd"].cpu().numpy(), rtol=0, atol=1e-5 * float(
+            np.abs(cc["yd"].cpu().numpy()).max() + 1)) for i, cc in enumerate(cases))
+        e2e = {"value": round(step_bytes / e2e_s / 1e9, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_s * 1e3, 3), "matches_device_path": bool(ok)}
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        b, t = cpu_sample_run(cases, 16384, threads)
+        cpu = {"value": round(b / t / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": "first min(rows,16384) rows of each of the 16 sweep matrices, oracle 512-bit vectorDot "
+                         "restatement, row-parallel over all host threads"}
+
+    moe = None
+    if world == 1 and rank == 0 and not args.no_moe:
+        moe = bench_moe(g4, ctx, torch, dev)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (u8/bf16 weight blocks)", "data": "synthetic",
+            "config": {"workload": "C2 quantized GEMV sweep: 4 shapes x {Q8_0,Q4_K,Q6_K,BF16}, batch 1, seed 1",
+                       "shapes": [f"{r}x{c}" for r, c in SHAPES], "bytes_per_step": step_bytes,
+                       "l2": "inputs larger than L2 (1.9 GB streamed per step)",
+                       "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "kernel": breakdown[dom]["case"], "achieved": round(achieved, 1),
+                         "peak": hbm, "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "traffic": None},
+            "breakdown": breakdown,
+            "clocks": clk.summary(),
+            "gpu_launches": len(cases) * args.steps * (2 if world > 1 else 1),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        if moe:
+            line["moe"] = moe
+        print(json.dumps(line), flush=True)
+    for cc in cases:
+        cc["w"].free()
+    ctx.close()
+
+
+def bench_moe(g4, ctx, torch, dev):
+    """MoE layer (config 3) microseconds per token at T = 1, 16, 256, 4096."""
+    from gemma4_kt_b200 import synth
+
+    d = synth.MoeLayerData(seed=2)
+    layer = g4.MoeLayer.upload(ctx, d)
+    res = {}
+    for T in (1, 16, 256, 4096):
+        x = torch.from_numpy(d.tokens(T)).to(dev)
+        out = torch.empty((T, d.dim), dtype=torch.float32, device=dev)
+        for _ in range(3):
+            layer.forward(x, out, T)
+        torch.cuda.synchronize()
+        reps = 20 if T <= 256 else 5
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            layer.forward(x, out, T)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        res[f"T{T}"] = {"us_per_layer": round(us, 2), "us_per_token": round(us / T, 3)}
+    ctx.sync()
+    return {"metric": "MoE layer us/token", "config": "hidden 2816, 128 experts top-8, ff 704, Q4_K, seed 2",
+            **res}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-moe", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,299 @@
+// g4_gemv.cuh -- per-format 16-element decode+dot units for the streaming
+// quantized GEMV, and the launch plan shared by host and device.
+//
+// A "unit" is 16 consecutive weights of one row: the same 16-lane slice the
+// reference's 512-bit vectorDot processes per FloatVector (e.g.
+// Q8_0FloatTensor.kt:64-78 handles a 32-weight block as two 16-lane halves;
+// Q4_KFloatTensor.kt:131-148 one 16-byte chunk of nibbles per lane vector).
+#pragma once
+#include "g4_common.cuh"
+
+namespace g4 {
+
+struct GemvPlan {
+  int type;
+  int rows, cols;
+  long long off;     // element offset into the tensor (thisOffset)
+  int pr;            // rows per virtual row (period after which blocks realign)
+  int nvrows;        // rows / pr
+  int vb;            // bytes per virtual row (whole blocks)
+  int units;         // 16-weight units per virtual row
+  int ncw;           // consumer warps per CTA (one producer warp besides)
+  int rw;            // virtual rows per consumer warp per tile
+  int tile_vrows;    // ncw * rw
+  int ntiles;
+  int stage_bytes;   // capacity of one smem stage (multiple of 128)
+  int nstages;
+  int grid;
+  int xbytes;        // bytes of x staged in smem (cols * 4 rounded to 128)
+  size_t smem;       // dynamic shared memory per CTA
+  int fast;          // 1: streaming kernel; 0: generic fallback
+};
+
+// Magic-number int->float: 2^23 + b as float bits, then subtract 2^23 (+bias).
+// Exact for 0 <= b < 2^23 and avoids the quarter-rate I2F path.
+__device__ __forceinline__ float byte_as_float(uint32_t word, uint32_t sel_byte) {
+  return __int_as_float((int)__byte_perm(word, 0x4B000000u, 0x7440u | sel_byte));
+}
+
+// ---- Q8_0: [fp16 d][int8 q x32] (Q8_0FloatTensor.kt:21-28,64-78) ----
+__device__ __forceinline__ float dot16_q8_0(const uint8_t* vb, int u, const float* x) {
+  const uint8_t* blk = vb + (u >> 1) * 34;
+  float d = f16_bits_to_f32(lds16(blk));
+  uint32_t w[4];
+  lds16B_unaligned(blk + 2 + (u & 1) * 16, w);
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t wk = w[k] ^ 0x80808080u;  // int8 q -> q + 128 as unsigned byte
+    s0 = fmaf(byte_as_float(wk, 0) - 8388736.0f, x[4 * k + 0], s0);
+    s1 = fmaf(byte_as_float(wk, 1) - 8388736.0f, x[4 * k + 1], s1);
+    s0 = fmaf(byte_as_float(wk, 2) - 8388736.0f, x[4 * k + 2], s0);
+    s1 = fmaf(byte_as_float(wk, 3) - 8388736.0f, x[4 * k + 3], s1);
+  }
+  return (s0 + s1) * d;
+}
+
+// ---- Q4_K: [fp16 d][fp16 dmin][scales 12][qs 128] (Q4_KFloatTensor.kt:23-55,70-84,116-148) ----
+// Unit u covers block u>>4, weights 16*(u&15) .. +16 of it: group g, nibble
+// half hi, 16-byte chunk c of the group's 32 qs bytes.
+__device__ __forceinline__ float dot16_q4_k(const uint8_t* vb, int u, const float* x, float sx) {
+  const uint8_t* blk = vb + (u >> 4) * 144;  // 144 = 9*16: blocks stay 16B aligned
+  int i0 = (u & 15) * 16;
+  int g = i0 >> 6, hi = (i0 >> 5) & 1, c = (i0 >> 4) & 1;
+  uint4 h = lds128(blk);
+  float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
+  float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+  // scale/min of sub-block j = 2g+hi, decoded as getScaleMinK4
+  int j = 2 * g + hi;
+  uint32_t sc, mn;
+  if (j < 4) {
+    sc = (h.y >> (8 * j)) & 63u;
+    mn = (h.z >> (8 * j)) & 63u;
+  } else {
+    int jj = j - 4;
+    uint32_t lo = (h.w >> (8 * jj)) & 0xFFu;
+    sc = (lo & 0xFu) | (((h.y >> (8 * jj + 6)) & 3u) << 4);
+    mn = (lo >> 4) | (((h.z >> (8 * jj + 6)) & 3u) << 4);
+  }
+  float d1 = d * (float)sc;
+  float m1 = dmin * (float)mn;
+  uint4 q = lds128(blk + 16 + g * 32 + c * 16);
+  uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t nib = (hi ? (qw[k] >> 4) : qw[k]) & 0x0F0F0F0Fu;
+    s0 = fmaf(byte_as_float(nib, 0) - 8388608.0f, x[4 * k + 0], s0);
+    s1 = fmaf(byte_as_float(nib, 1) - 8388608.0f, x[4 * k + 1], s1);
+    s0 = fmaf(byte_as_float(nib, 2) - 8388608.0f, x[4 * k + 2], s0);
+    s1 = fmaf(byte_as_float(nib, 3) - 8388608.0f, x[4 * k + 3], s1);
+  }
+  // sum_i (d1*q_i - m1) * x_i
+  return fmaf(d1, s0 + s1, -m1 * sx);
+}
+
+// ---- Q6_K: [ql 128][qh 64][int8 sc 16][fp16 d] (Q6_KFloatTensor.kt:26-73,144-205) ----
+__device__ __forceinline__ float dot16_q6_k(const uint8_t* vb, int u, const float* x) {
+  const uint8_t* blk = vb + (u >> 4) * 210;
+  int i0 = (u & 15) * 16;
+  int half = i0 >> 7, rem = i0 & 127, sub32 = rem >> 5, l0 = rem & 31;
+  uint32_t ql[4], qh[4];
+  lds16B_unaligned(blk + half * 64 + (sub32 & 1) * 32 + l0, ql);
+  lds16B_unaligned(blk + 128 + half * 32 + l0, qh);
+  int8_t scv = (int8_t)(lds16(blk + 192 + ((u & 15) & ~1)) >> (8 * (u & 1)));
+  float d = f16_bits_to_f32(lds16(blk + 208));
+  uint32_t nsh = (sub32 >> 1) * 4u, hsh = 2u * (uint32_t)sub32;
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t q6 = ((ql[k] >> nsh) & 0x0F0F0F0Fu) | (((qh[k] >> hsh) & 0x03030303u) << 4);
+    s0 = fmaf(byte_as_float(q6, 0) - 8388640.0f, x[4 * k + 0], s0);  // 2^23 + 32
+    s1 = fmaf(byte_as_float(q6, 1) - 8388640.0f, x[4 * k + 1], s1);
+    s0 = fmaf(byte_as_float(q6, 2) - 8388640.0f, x[4 * k + 2], s0);
+    s1 = fmaf(byte_as_float(q6, 3) - 8388640.0f, x[4 * k + 3], s1);
+  }
+  return (d * (float)scv) * (s0 + s1);
+}
+
+// ---- BF16 (BF16FloatTensor.kt:20-24,35-74) ----
+__device__ __forceinline__ float dot16_bf16(const uint8_t* vb, int u, const float* x) {
+  const uint8_t* p = vb + u * 32;
+  uint4 a = lds128(p), b = lds128(p + 16);
+  uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    s0 = fmaf(__uint_as_float(w[k] << 16), x[2 * k], s0);
+    s1 = fmaf(__uint_as_float(w[k] & 0xFFFF0000u), x[2 * k + 1], s1);
+  }
+  return s0 + s1;
+}
+
+// ---- F32 (F32FloatTensor.kt:18-20,37-66) ----
+__device__ __forceinline__ float dot16_f32(const uint8_t* vb, int u, const float* x) {
+  const uint8_t* p = vb + u * 64;
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint4 a = lds128(p + 16 * k);
+    s0 = fmaf(__uint_as_float(a.x), x[4 * k + 0], s0);
+    s1 = fmaf(__uint_as_float(a.y), x[4 * k + 1], s1);
+    s0 = fmaf(__uint_as_float(a.z), x[4 * k + 2], s0);
+    s1 = fmaf(__uint_as_float(a.w), x[4 * k + 3], s1);
+  }
+  return s0 + s1;
+}
+
+template <int FMT>
+__device__ __forceinline__ float dot16(const uint8_t* vb, int u, const float* x, float sx) {
+  if constexpr (FMT == Q8_0) return dot16_q8_0(vb, u, x);
+  else if constexpr (FMT == Q4_K) return dot16_q4_k(vb, u, x, sx);
+  else if constexpr (FMT == Q6_K) return dot16_q6_k(vb, u, x);
+  else if constexpr (FMT == BF16) return dot16_bf16(vb, u, x);
+  else return dot16_f32(vb, u, x);
+}
+
+// Element get() with the reference's rounding order, no contraction
+// (Q8_0FloatTensor.kt:21-28, Q4_KFloatTensor.kt:23-55, Q6_KFloatTensor.kt:26-73,
+// BF16FloatTensor.kt:20-24, F32FloatTensor.kt:18-20).  Used by the dequant
+// kernel (bit-exact check) and the generic GEMV fallback.
+__device__ __forceinline__ float get_elem(int type, const uint8_t* base, long long idx) {
+  switch (type) {
+    case F32: return __ldg(reinterpret_cast<const float*>(base) + idx);
+    case F16: {
+      const uint8_t* p = base + idx * 2;
+      return f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8)));
+    }
+    case BF16: {
+      const uint8_t* p = base + idx * 2;
+      return __uint_as_float((uint32_t)(p[0] | (p[1] << 8)) << 16);
+    }
+    case Q8_0: {
+      const uint8_t* blk = base + (idx >> 5) * 34;
+      float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+      return __fmul_rn((float)(int8_t)blk[2 + (idx & 31)], d);
+    }
+    case Q4_K: {
+      const uint8_t* blk = base + (idx >> 8) * 144;
+      int w = (int)(idx & 255);
+      float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+      float dmin = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+      const uint8_t* s = blk + 4;
+      int group = w >> 6, ig = w & 63;
+      int sub = group * 2 + (ig >= 32), nib = ig & 31;
+      int sc, m;
+      if (sub < 4) {
+        sc = s[sub] & 63;
+        m = s[sub + 4] & 63;
+      } else {
+        sc = (s[sub + 4] & 0xF) | (((s[sub - 4] >> 6) & 3) << 4);
+        m = (s[sub + 4] >> 4) | (((s[sub] >> 6) & 3) << 4);
+      }
+      uint8_t b = blk[16 + group * 32 + nib];
+      int q = ig >= 32 ? (b >> 4) : (b & 0xF);
+      float t = __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+      return __fsub_rn(t, __fmul_rn(dmin, (float)m));
+    }
+    case Q6_K: {
+      const uint8_t* blk = base + (idx >> 8) * 210;
+      int w = (int)(idx & 255);
+      int half = w >> 7, rem = w & 127, sub32 = rem >> 5, l = rem & 31;
+      const uint8_t* ql = blk + half * 64 + (sub32 & 1) * 32;
+      int nib = (sub32 >> 1) ? (ql[l] >> 4) : (ql[l] & 0xF);
+      int hb = (blk[128 + half * 32 + l] >> (2 * sub32)) & 3;
+      int q6 = (nib | (hb << 4)) - 32;
+      int sc = (int8_t)blk[192 + half * 8 + sub32 * 2 + l / 16];
+      float d = f16_bits_to_f32((uint16_t)(blk[208] | (blk[209] << 8)));
+      return __fmul_rn(__fmul_rn(d, (float)sc), (float)q6);
+    }
+    default: return __int_as_float(0x7fc00000);
+  }
+}
+
+}  // namespace g4
+
+namespace g4 {
+
+// Dequantize one 16-weight unit into registers (for multi-token products).
+// Q4_K uses the vectorDot form w = fma(q, d*sc, -(dmin*m)) (Q4_KFloatTensor.kt:145);
+// Q6_K w = q6 * (d*sc) (Q6_KFloatTensor.kt:201); Q8_0 w = q * d.
+template <int FMT>
+__device__ __forceinline__ void deq16(const uint8_t* vb, int u, float* w) {
+  if constexpr (FMT == Q8_0) {
+    const uint8_t* blk = vb + (u >> 1) * 34;
+    float d = f16_bits_to_f32(lds16(blk));
+    uint32_t q[4];
+    lds16B_unaligned(blk + 2 + (u & 1) * 16, q);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t wk = q[k] ^ 0x80808080u;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) w[4 * k + b] = (byte_as_float(wk, b) - 8388736.0f) * d;
+    }
+  } else if constexpr (FMT == Q4_K) {
+    const uint8_t* blk = vb + (u >> 4) * 144;
+    int i0 = (u & 15) * 16;
+    int g = i0 >> 6, hi = (i0 >> 5) & 1, c = (i0 >> 4) & 1;
+    uint4 h = lds128(blk);
+    float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
+    float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+    int j = 2 * g + hi;
+    uint32_t sc, mn;
+    if (j < 4) {
+      sc = (h.y >> (8 * j)) & 63u;
+      mn = (h.z >> (8 * j)) & 63u;
+    } else {
+      int jj = j - 4;
+      uint32_t lo = (h.w >> (8 * jj)) & 0xFFu;
+      sc = (lo & 0xFu) | (((h.y >> (8 * jj + 6)) & 3u) << 4);
+      mn = (lo >> 4) | (((h.z >> (8 * jj + 6)) & 3u) << 4);
+    }
+    float d1 = d * (float)sc, negm = -(dmin * (float)mn);
+    uint4 q = lds128(blk + 16 + g * 32 + c * 16);
+    uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t nib = (hi ? (qw[k] >> 4) : qw[k]) & 0x0F0F0F0Fu;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) w[4 * k + b] = fmaf(byte_as_float(nib, b) - 8388608.0f, d1, negm);
+    }
+  } else if constexpr (FMT == Q6_K) {
+    const uint8_t* blk = vb + (u >> 4) * 210;
+    int i0 = (u & 15) * 16;
+    int half = i0 >> 7, rem = i0 & 127, sub32 = rem >> 5, l0 = rem & 31;
+    uint32_t ql[4], qh[4];
+    lds16B_unaligned(blk + half * 64 + (sub32 & 1) * 32 + l0, ql);
+    lds16B_unaligned(blk + 128 + half * 32 + l0, qh);
+    int8_t scv = (int8_t)(lds16(blk + 192 + ((u & 15) & ~1)) >> (8 * (u & 1)));
+    float ds = f16_bits_to_f32(lds16(blk + 208)) * (float)scv;
+    uint32_t nsh = (sub32 >> 1) * 4u, hsh = 2u * (uint32_t)sub32;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t q6 = ((ql[k] >> nsh) & 0x0F0F0F0Fu) | (((qh[k] >> hsh) & 0x03030303u) << 4);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) w[4 * k + b] = (byte_as_float(q6, b) - 8388640.0f) * ds;
+    }
+  } else if constexpr (FMT == BF16) {
+    const uint8_t* p = vb + u * 32;
+    uint4 a = lds128(p), b = lds128(p + 16);
+    uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      w[2 * k] = __uint_as_float(v[k] << 16);
+      w[2 * k + 1] = __uint_as_float(v[k] & 0xFFFF0000u);
+    }
+  } else {
+    const uint8_t* p = vb + u * 64;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint4 a = lds128(p + 16 * k);
+      w[4 * k] = __uint_as_float(a.x);
+      w[4 * k + 1] = __uint_as_float(a.y);
+      w[4 * k + 2] = __uint_as_float(a.z);
+      w[4 * k + 3] = __uint_as_float(a.w);
+    }
+  }
+}
+
+}  // namespace g4

@@ -1,0 +1,21 @@
+// g4_internal.h -- declarations shared by the translation units of libg4b200.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace g4 {
+
+struct DeviceInfo {
+  int device;
+  int sms;
+  size_t smem_optin;
+};
+
+struct GemvPlan;
+
+GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols);
+int launch_gemv(const DeviceInfo& dev, int type, const uint8_t* w, long long off, int rows, int cols,
+                const float* x, float* y, unsigned* status, cudaStream_t st, GemvPlan* plan_out);
+int launch_dequant(int type, const uint8_t* w, long long off, long long n, float* out, cudaStream_t st);
+
+}  // namespace g4

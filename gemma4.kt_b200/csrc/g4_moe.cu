@@ -1,0 +1,709 @@
+// g4_moe.cu -- the expert half of gemma4.kt's MoE block (Llama.kt:247-346)
+// for a batch of tokens, as a short chain of sm_100a kernels:
+//
+//   moe_prep        moeInput = rmsnorm(x, pre_ffw_norm_2)            Llama.kt:248-254
+//                   router input x * rms/sqrt(dim) * gate_inp_scale   Llama.kt:257-268
+//   moe_router      logits = gate_inp . router input (F32)            Llama.kt:269-270
+//   moe_topk        softmax (double exp) + iterative top-k            Llama.kt:273-293
+//   moe_permute     per-expert counts, offsets, slot permutation      (implicit ki loop :300)
+//   moe_expert<GU>  grouped gate_up GEMV, epilogue gelu(gate)*up      Llama.kt:305-322
+//   moe_expert<DN>  grouped down GEMV                                  Llama.kt:325-332
+//   moe_combine     out = sum_k (prob_k*down_scale[e_k]) * down_k in k
+//                   order, then rmsnorm(post_ffw_norm_2)              Llama.kt:334-346
+//
+// A "slot" is one (token, k) selection: slot = token * n_used + k.  The expert
+// kernels stream each selected expert's weights once per token chunk with
+// cp.async.bulk into a shared-memory ring (as the GEMV does) and read the
+// chunk's activations through L1.  Every result is written to a fixed place,
+// so the combine is deterministic and in the reference's order.
+#include "g4.h"
+#include "g4_ctx.h"
+#include "g4_gemv.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace g4 {
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxUsed = 16;
+
+// ---------------------------------------------------------------- helpers
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < nw ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// Llama.gelu (Llama.kt:23-25): double precision, rounded to float.
+__device__ __forceinline__ float gelu_ref(float x) {
+  double xd = (double)x;
+  double inner = 0.7978845608028654 * (xd + 0.044715 * (xd * xd * xd));
+  return (float)(0.5 * xd * (1.0 + tanh(inner)));
+}
+
+// ---------------------------------------------------------------- prep
+
+__global__ void moe_prep_kernel(const float* __restrict__ x, const float* __restrict__ pre_norm,
+                                const float* __restrict__ gate_scale, float* __restrict__ moe_in,
+                                float* __restrict__ xr, int dim, float eps) {
+  __shared__ float red[33];
+  const float* xt = x + (size_t)blockIdx.x * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(xt[i], xt[i], ss);
+  ss = block_sum(ss, red);
+  // rmsnorm (Llama.kt:27-37): ss/size + eps, 1/sqrt in double
+  float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
+  float s_norm = (float)(1.0 / sqrt((double)m));
+  // router scale (Llama.kt:258-261): (float)(1/sqrt(ss)) / (float)sqrt(dim)
+  float s_router = __fdiv_rn(s_norm, (float)sqrt((double)dim));
+  float* mo = moe_in + (size_t)blockIdx.x * dim;
+  float* xo = xr + (size_t)blockIdx.x * dim;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    float v = xt[i];
+    mo[i] = __fmul_rn(pre_norm[i], __fmul_rn(s_norm, v));
+    xo[i] = __fmul_rn(__fmul_rn(v, s_router), gate_scale[i]);
+  }
+}
+
+// ---------------------------------------------------------------- router
+// logits[t][e] = sum_k Wr[e][k] * xr[t][k].  One warp per expert, TT tokens
+// per CTA sharing each weight load.
+template <int TT>
+__global__ void __launch_bounds__(256) moe_router_kernel(const float* __restrict__ wr, const float* __restrict__ xr,
+                                                         float* __restrict__ logits, int T, int dim, int n_expert) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + warp;
+  const int t0 = blockIdx.y * TT;
+  if (e >= n_expert) return;
+  const float4* w4 = reinterpret_cast<const float4*>(wr + (size_t)e * dim);
+  float acc[TT];
+#pragma unroll
+  for (int j = 0; j < TT; ++j) acc[j] = 0.f;
+  const int n4 = dim >> 2;
+  for (int k = lane; k < n4; k += 32) {
+    float4 w = __ldg(w4 + k);
+#pragma unroll
+    for (int j = 0; j < TT; ++j) {
+      if (t0 + j < T) {
+        float4 v = __ldg(reinterpret_cast<const float4*>(xr + (size_t)(t0 + j) * dim) + k);
+        acc[j] = fmaf(w.x, v.x, fmaf(w.y, v.y, fmaf(w.z, v.z, fmaf(w.w, v.w, acc[j]))));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < TT; ++j) {
+    float v = warp_sum(acc[j]);
+    if (lane == 0 && t0 + j < T) logits[(size_t)(t0 + j) * n_expert + e] = v;
+  }
+}
+
+// ---------------------------------------------------------------- softmax + top-k
+// One warp per token.  softmaxInPlace (MutableFloatTensor.kt:54-59): max,
+// exp((v-max) in double) -> float, sequential float sum, divide.  Top-k as
+// Llama.kt:280-293: strict '>' over ascending index, so ties go to the lowest
+// index; the selected entry is masked to -inf.
+__global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, int K,
+                                int32_t* __restrict__ idx_out, float* __restrict__ prob_out) {
+  __shared__ float probs[8][kMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const float* lg = logits + (size_t)t * E;
+  float* p = probs[warp];
+  float mx = -INFINITY;
+  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int e = lane; e < E; e += 32) p[e] = (float)exp((double)__fsub_rn(lg[e], mx));
+  __syncwarp();
+  float sum = 0.f;
+  if (lane == 0)
+    for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, p[e]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
+  __syncwarp();
+  for (int k = 0; k < K; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < E; e += 32) {
+      float v = p[e];
+      if (v > bv) {  // ascending e within the lane: first maximum wins
+        bv = v;
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (bi == 0x7fffffff) bi = 0;  // every entry -inf: the reference keeps bestIdx = 0
+    if (lane == 0) {
+      idx_out[(size_t)t * K + k] = bi;
+      prob_out[(size_t)t * K + k] = bv;
+      p[bi] = -INFINITY;
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------- permutation
+// Single CTA: counts per expert, exclusive offsets (offsets[E] = T*K), and
+// perm[offsets[e] + j] = slot for the j-th slot routed to e.
+__global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t* __restrict__ idx, int n_slots, int E,
+                                                           int32_t* __restrict__ offsets, int32_t* __restrict__ perm) {
+  __shared__ int cnt[kMaxExperts], off[kMaxExperts + 1], cur[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    cnt[e] = 0;
+    cur[e] = 0;
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) atomicAdd(&cnt[idx[s]], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int a = 0;
+    for (int e = 0; e < E; ++e) {
+      off[e] = a;
+      a += cnt[e];
+    }
+    off[E] = a;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off[e];
+  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
+    int e = idx[s];
+    int pos = off[e] + atomicAdd(&cur[e], 1);
+    perm[pos] = s;
+  }
+}
+
+// ---------------------------------------------------------------- grouped experts
+// Work item = (expert e, row tile, token chunk of <= NB slots).  Items of
+// expert e are tile-major with the chunk fastest, so CTAs working on the same
+// tile at the same time share its weights through L2.
+//
+// GATEUP: tile = NCW gate rows r and their up rows ff+r (one pair per consumer
+//         warp); epilogue g = gelu(gate) * up -> G[slot][r].
+// DOWN:   tile = NCW virtual rows (pr real rows each) of the [dim, ff] expert
+//         matrix; output D[slot][row].
+struct ExpertArgs {
+  const uint8_t* w;         // expert tensor block stream
+  const float* act;         // GATEUP: moe_in [T, K_in]; DOWN: G [slots, ff]
+  float* out;               // GATEUP: G [slots, ff]; DOWN: D [slots, dim]
+  const int32_t* offsets;   // [E+1]
+  const int32_t* perm;      // [slots]
+  unsigned* status;
+  int E, n_used;
+  int rows_e;               // output rows per expert (GATEUP: 2*ff; DOWN: dim)
+  int cols;                 // K (GATEUP: dim; DOWN: ff)
+  int ff;                   // expert_ff
+  int pr;                   // DOWN: rows per virtual row
+  int vb;                   // bytes per (virtual) row
+  int units;                // 16-weight units per (virtual) row
+  int tiles_e;              // row tiles per expert
+  int tile_rows;            // GATEUP: pairs per tile; DOWN: virtual rows per tile
+  int stage_bytes, nstages;
+  long long expert_elems;   // elements per expert matrix
+};
+
+template <int FMT, bool GATEUP, int PR, int NB, int NCW>
+__global__ void __launch_bounds__(32 * (NCW + 1)) moe_expert_kernel(const __grid_constant__ ExpertArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int BS = block_size(FMT), TS = type_size(FMT);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 4;
+  int* s_items = reinterpret_cast<int*>(smem + 64);            // [E+1] item prefix
+  int* s_chunks = s_items + (kMaxExperts + 1);                 // [E] chunks per expert
+  uint8_t* stages = smem + 64 + 4 * (2 * kMaxExperts + 8);
+  stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(stages) + 127) & ~uintptr_t(127));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NS = a.nstages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NCW);
+    }
+    fence_barrier_init();
+    int acc = 0;
+    for (int e = 0; e < a.E; ++e) {
+      int n = a.offsets[e + 1] - a.offsets[e];
+      int ch = (n + NB - 1) / NB;
+      s_chunks[e] = ch;
+      s_items[e] = acc;
+      acc += ch * a.tiles_e;
+    }
+    s_items[a.E] = acc;
+  }
+  __syncthreads();
+  const int n_items = s_items[a.E];
+
+  auto locate = [&](int item, int& e, int& tile, int& chunk) {
+    int lo = 0, hi = a.E - 1;  // last e with s_items[e] <= item
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (s_items[mid] <= item) lo = mid;
+      else hi = mid - 1;
+    }
+    e = lo;
+    int local = item - s_items[e];
+    tile = local / s_chunks[e];
+    chunk = local - tile * s_chunks[e];
+  };
+
+  if (warp == 0) {
+    if (lane != 0) return;
+    int it = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+      int s = it % NS;
+      if (it >= NS && !mbar_wait_bounded(&empty[s], ((it / NS) - 1) & 1)) {
+        record_error(a.status, ERR_TIMEOUT_EMPTY);
+        break;
+      }
+      int e, tile, chunk;
+      locate(item, e, tile, chunk);
+      uint8_t* dst = stages + (size_t)s * a.stage_bytes;
+      long long eb = (long long)e * a.expert_elems;  // expert's first element (block aligned)
+      if (GATEUP) {
+        int r0 = tile * a.tile_rows;
+        int nr = min(a.tile_rows, a.ff - r0);
+        long long g0 = (eb + (long long)r0 * a.cols) / BS * TS;
+        long long u0 = (eb + (long long)(a.ff + r0) * a.cols) / BS * TS;
+        uint32_t bytes = (uint32_t)nr * a.vb;  // rows of whole blocks, 16B multiples (checked on host)
+        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(dst, a.w + g0, bytes, &full[s]);
+        bulk_g2s(dst + (size_t)a.tile_rows * a.vb, a.w + u0, bytes, &full[s]);
+      } else {
+        int v0 = tile * a.tile_rows;
+        int nv = min(a.tile_rows, a.rows_e / PR - v0);
+        long long b0 = (eb + (long long)v0 * PR * a.cols) / BS * TS;
+        uint32_t bytes = (uint32_t)nv * a.vb;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        bulk_g2s(dst, a.w + b0, bytes, &full[s]);
+      }
+    }
+    for (int j = max(0, it - NS); j < it; ++j)
+      if (!mbar_wait_bounded(&full[j % NS], (j / NS) & 1)) record_error(a.status, ERR_TIMEOUT_DRAIN);
+    return;
+  }
+
+  const int cw = warp - 1;
+  int it = 0;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+    int s = it % NS;
+    if (!mbar_wait_bounded(&full[s], (it / NS) & 1)) {
+      record_error(a.status, ERR_TIMEOUT_FULL);
+      return;
+    }
+    int e, tile, chunk;
+    locate(item, e, tile, chunk);
+    const int p0 = a.offsets[e] + chunk * NB;
+    const int nb = min(NB, a.offsets[e + 1] - p0);
+    int slot[NB];
+    const float* xrow[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      slot[j] = j < nb ? a.perm[p0 + j] : 0;
+      // GATEUP reads the token's moeInput row, DOWN the slot's gelu*up row
+      xrow[j] = GATEUP ? a.act + (size_t)(slot[j] / a.n_used) * a.cols : a.act + (size_t)slot[j] * a.cols;
+    }
+    const uint8_t* st = stages + (size_t)s * a.stage_bytes;
+
+    if (GATEUP) {
+      const int r = tile * a.tile_rows + cw;  // gate row; up row = ff + r
+      const bool valid = r < a.ff;
+      const uint8_t* vg = st + (size_t)cw * a.vb;
+      const uint8_t* vu = st + (size_t)(a.tile_rows + cw) * a.vb;
+      float ag[NB], au[NB];
+#pragma unroll
+      for (int j = 0; j < NB; ++j) ag[j] = au[j] = 0.f;
+      if (valid) {
+        for (int u = lane; u < a.units; u += 32) {
+          float wg[16], wu[16];
+          deq16<FMT>(vg, u, wg);
+          deq16<FMT>(vu, u, wu);
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            if (j < nb) {
+              const float4* xp = reinterpret_cast<const float4*>(xrow[j] + u * 16);
+              float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                float4 v = __ldg(xp + k);
+                g0 = fmaf(wg[4 * k], v.x, g0);
+                g1 = fmaf(wg[4 * k + 1], v.y, g1);
+                g0 = fmaf(wg[4 * k + 2], v.z, g0);
+                g1 = fmaf(wg[4 * k + 3], v.w, g1);
+                u0 = fmaf(wu[4 * k], v.x, u0);
+                u1 = fmaf(wu[4 * k + 1], v.y, u1);
+                u0 = fmaf(wu[4 * k + 2], v.z, u0);
+                u1 = fmaf(wu[4 * k + 3], v.w, u1);
+              }
+              ag[j] += g0 + g1;
+              au[j] += u0 + u1;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        float g = warp_sum(ag[j]);
+        float up = warp_sum(au[j]);
+        if (lane == 0 && valid && j < nb) a.out[(size_t)slot[j] * a.ff + r] = __fmul_rn(gelu_ref(g), up);
+      }
+    } else {
+      const int v = tile * a.tile_rows + cw;
+      const bool valid = v < a.rows_e / PR;
+      const uint8_t* vbp = st + (size_t)cw * a.vb;
+      float acc[PR][NB];
+#pragma unroll
+      for (int r = 0; r < PR; ++r)
+#pragma unroll
+        for (int j = 0; j < NB; ++j) acc[r][j] = 0.f;
+      if (valid) {
+        for (int u = lane; u < a.units; u += 32) {
+          const int e0 = u * 16;
+          const int col = PR == 1 ? e0 : e0 % a.cols;
+          const int rip = PR == 1 ? 0 : e0 / a.cols;
+          float w[16];
+          deq16<FMT>(vbp, u, w);
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            if (j < nb) {
+              const float4* xp = reinterpret_cast<const float4*>(xrow[j] + col);
+              float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                float4 xv = __ldg(xp + k);
+                s0 = fmaf(w[4 * k], xv.x, s0);
+                s1 = fmaf(w[4 * k + 1], xv.y, s1);
+                s0 = fmaf(w[4 * k + 2], xv.z, s0);
+                s1 = fmaf(w[4 * k + 3], xv.w, s1);
+              }
+              float part = s0 + s1;
+#pragma unroll
+              for (int r = 0; r < PR; ++r) acc[r][j] += (rip == r) ? part : 0.f;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+      for (int r = 0; r < PR; ++r)
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          float sum = warp_sum(acc[r][j]);
+          if (lane == 0 && valid && j < nb) a.out[(size_t)slot[j] * a.rows_e + (size_t)v * PR + r] = sum;
+        }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- combine
+// moeOutput = 0; for ki: moeOutput += (prob*downScale) * down  (saxpyInPlace,
+// MutableFloatTensor.kt:61-66: product rounded, then added); then
+// rmsnorm(post_ffw_norm_2) (Llama.kt:340-346) when a weight is given.
+__global__ void moe_combine_kernel(const float* __restrict__ D, const int32_t* __restrict__ idx,
+                                   const float* __restrict__ prob, const float* __restrict__ down_scale,
+                                   const float* __restrict__ post_norm, float* __restrict__ out, int dim, int K,
+                                   float eps) {
+  __shared__ float red[33];
+  __shared__ float fw[kMaxUsed];
+  const int t = blockIdx.x;
+  if (threadIdx.x < K) {
+    int e = idx[(size_t)t * K + threadIdx.x];
+    fw[threadIdx.x] = __fmul_rn(prob[(size_t)t * K + threadIdx.x], down_scale[e]);
+  }
+  __syncthreads();
+  float* o = out + (size_t)t * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    float acc = 0.f;
+    for (int k = 0; k < K; ++k) acc = __fadd_rn(__fmul_rn(fw[k], D[((size_t)t * K + k) * dim + i]), acc);
+    o[i] = acc;
+    ss = fmaf(acc, acc, ss);
+  }
+  if (post_norm == nullptr) return;
+  ss = block_sum(ss, red);
+  float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
+  float sn = (float)(1.0 / sqrt((double)m));
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) o[i] = __fmul_rn(post_norm[i], __fmul_rn(sn, o[i]));
+}
+
+// ---------------------------------------------------------------- host side
+
+struct MoeScratch {
+  float *moe_in, *xr, *logits, *prob, *G, *D;
+  int32_t *idx, *offsets, *perm;
+};
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static size_t moe_scratch_bytes(int T, int dim, int E, int K, int ff) {
+  size_t s = 0;
+  s += align_up((size_t)T * dim * 4, 256) * 2;       // moe_in, xr
+  s += align_up((size_t)T * E * 4, 256);             // logits
+  s += align_up((size_t)T * K * 4, 256) * 3;         // prob, idx, perm
+  s += align_up((size_t)(E + 1) * 4, 256);           // offsets
+  s += align_up((size_t)T * K * ff * 4, 256);        // G
+  s += align_up((size_t)T * K * dim * 4, 256);       // D
+  return s;
+}
+
+static MoeScratch carve(uint8_t* base, int T, int dim, int E, int K, int ff) {
+  MoeScratch m;
+  size_t o = 0;
+  auto take = [&](size_t b) {
+    uint8_t* p = base + o;
+    o += align_up(b, 256);
+    return p;
+  };
+  m.moe_in = (float*)take((size_t)T * dim * 4);
+  m.xr = (float*)take((size_t)T * dim * 4);
+  m.logits = (float*)take((size_t)T * E * 4);
+  m.prob = (float*)take((size_t)T * K * 4);
+  m.idx = (int32_t*)take((size_t)T * K * 4);
+  m.perm = (int32_t*)take((size_t)T * K * 4);
+  m.offsets = (int32_t*)take((size_t)(E + 1) * 4);
+  m.G = (float*)take((size_t)T * K * ff * 4);
+  m.D = (float*)take((size_t)T * K * dim * 4);
+  return m;
+}
+
+using ExpertFn = void (*)(const ExpertArgs);
+
+template <int FMT, bool GU, int PR>
+static ExpertFn expert_fn(int nb) {
+  if (nb >= 8) return moe_expert_kernel<FMT, GU, PR, 8, 8>;
+  if (nb >= 4) return moe_expert_kernel<FMT, GU, PR, 4, 8>;
+  if (nb >= 2) return moe_expert_kernel<FMT, GU, PR, 2, 8>;
+  return moe_expert_kernel<FMT, GU, PR, 1, 8>;
+}
+
+template <bool GU, int PR>
+static ExpertFn expert_fn_t(int type, int nb) {
+  switch (type) {
+    case Q8_0: return expert_fn<Q8_0, GU, PR>(nb);
+    case Q4_K: return expert_fn<Q4_K, GU, PR>(nb);
+    case Q6_K: return expert_fn<Q6_K, GU, PR>(nb);
+    case BF16: return expert_fn<BF16, GU, PR>(nb);
+    case F32: return expert_fn<F32, GU, PR>(nb);
+  }
+  return nullptr;
+}
+
+static ExpertFn select_expert(int type, bool gu, int pr, int nb) {
+  if (gu) return expert_fn_t<true, 1>(type, nb);
+  if (pr == 1) return expert_fn_t<false, 1>(type, nb);
+  if (pr == 2) return expert_fn_t<false, 2>(type, nb);
+  if (pr == 4) return expert_fn_t<false, 4>(type, nb);
+  return nullptr;
+}
+
+static int gcd_i(int a, int b) {
+  while (b) {
+    int t = a % b;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
+static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const float* act, float* out,
+                         const MoeScratch& m, int E, int K, int dim, int ff, int T, cudaStream_t st) {
+  const int BS = block_size(type), TS = type_size(type);
+  ExpertArgs a{};
+  a.w = w;
+  a.act = act;
+  a.out = out;
+  a.offsets = m.offsets;
+  a.perm = m.perm;
+  a.status = c->status;
+  a.E = E;
+  a.n_used = K;
+  a.ff = ff;
+  const int NCW = 8;
+  if (gu) {
+    a.rows_e = 2 * ff;
+    a.cols = dim;
+    a.pr = 1;
+    if (dim % BS || dim % 16) return -1;
+    a.vb = dim / BS * TS;
+    if (a.vb % 16) return -1;  // gate/up row starts must be 16B aligned for the bulk copies
+    a.units = dim / 16;
+    a.tile_rows = NCW;
+    a.tiles_e = (ff + NCW - 1) / NCW;
+    a.stage_bytes = (int)align_up((size_t)2 * NCW * a.vb, 128);
+    a.expert_elems = (long long)2 * ff * dim;
+  } else {
+    a.rows_e = dim;
+    a.cols = ff;
+    if (ff % 16) return -1;
+    int pr = ff % BS == 0 ? 1 : BS / gcd_i(ff % BS, BS);
+    if (pr != 1 && pr != 2 && pr != 4) return -1;
+    if (dim % pr) return -1;
+    a.pr = pr;
+    a.vb = pr * ff / BS * TS;
+    if (a.vb % 16) return -1;
+    a.units = pr * ff / 16;
+    a.tile_rows = NCW;
+    a.tiles_e = (dim / pr + NCW - 1) / NCW;
+    a.stage_bytes = (int)align_up((size_t)NCW * a.vb, 128);
+    a.expert_elems = (long long)dim * ff;
+  }
+  if (a.expert_elems % BS) return -1;
+  a.nstages = 4;
+  // Token chunk: enough slots per expert on average -> wider chunks.
+  int avg = (T * K + E - 1) / E;
+  int nb = avg >= 8 ? 8 : avg >= 4 ? 4 : avg >= 2 ? 2 : 1;
+  ExpertFn fn = select_expert(type, gu, a.pr, nb);
+  if (!fn) return -1;
+  size_t smem = 64 + 4 * (2 * kMaxExperts + 8) + 128 + (size_t)a.nstages * a.stage_bytes;
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int occ = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, 32 * (NCW + 1), smem);
+  if (occ < 1) occ = 1;
+  // Upper bound on items: every slot in its own chunk.
+  long long max_items = (long long)std::min(T * K, E * ((T * K + nb - 1) / nb + 1)) * a.tiles_e;
+  int grid = (int)std::min<long long>(max_items, (long long)c->dev.sms * occ);
+  if (grid < 1) grid = 1;
+  fn<<<grid, 32 * (NCW + 1), smem, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+static int tensor_ok(const g4_tensor* t, int type, uint64_t n) {
+  return t && (type < 0 || t->type == type) && t->n_elems == n;
+}
+
+}  // namespace g4
+
+using namespace g4;
+
+extern "C" int g4_moe_topk(g4_ctx* c, const float* logits, int T, int E, int K, int32_t* idx, float* prob,
+                           void* stream) {
+  if (!c) return G4_E_ARG;
+  if (!logits || !idx || !prob || T < 0 || E < 1 || E > kMaxExperts || K < 1 || K > E || K > kMaxUsed) {
+    c->set_err("g4_moe_topk: bad argument");
+    return G4_E_ARG;
+  }
+  if (T == 0) return 0;
+  if (int r = c->bind()) return r;
+  moe_topk_kernel<<<(T + 7) / 8, 256, 0, (cudaStream_t)stream>>>(logits, T, E, K, idx, prob);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : c->cuda_fail(e, "g4_moe_topk");
+}
+
+extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, float* out, int T,
+                            int32_t* topk_idx, float* topk_prob, void* stream) {
+  if (!c) return G4_E_ARG;
+  if (!w || !x || !out || T < 0) {
+    c->set_err("g4_moe_layer: bad argument");
+    return G4_E_ARG;
+  }
+  const int dim = w->dim, E = w->n_expert, K = w->n_used, ff = w->expert_ff;
+  if (dim <= 0 || E < 1 || E > kMaxExperts || K < 1 || K > E || K > kMaxUsed || ff <= 0 || dim % 4) {
+    c->set_err("g4_moe_layer: unsupported geometry dim=%d experts=%d used=%d ff=%d", dim, E, K, ff);
+    return G4_E_ARG;
+  }
+  if (!tensor_ok(w->gate_inp, G4_TYPE_F32, (uint64_t)dim * E) ||
+      !tensor_ok(w->gate_inp_scale, G4_TYPE_F32, dim) || !tensor_ok(w->down_exps_scale, G4_TYPE_F32, E) ||
+      !tensor_ok(w->pre_ffw_norm_2, G4_TYPE_F32, dim) ||
+      (w->post_ffw_norm_2 && !tensor_ok(w->post_ffw_norm_2, G4_TYPE_F32, dim)) ||
+      !tensor_ok(w->gate_up_exps, -1, (uint64_t)dim * 2 * ff * E) ||
+      !tensor_ok(w->down_exps, -1, (uint64_t)ff * dim * E)) {
+    c->set_err("g4_moe_layer: a weight tensor is missing or has the wrong type/size");
+    return G4_E_ARG;
+  }
+  if (T == 0) return 0;
+  if ((long long)T * K > (1 << 24)) {
+    c->set_err("g4_moe_layer: too many tokens (%d)", T);
+    return G4_E_ARG;
+  }
+  if (int r = c->bind()) return r;
+  cudaStream_t st = (cudaStream_t)stream;
+  size_t need = moe_scratch_bytes(T, dim, E, K, ff);
+  uint8_t* base = (uint8_t*)c->scratch(need);
+  if (!base) {
+    c->set_err("g4_moe_layer: cannot allocate %zu bytes of scratch", need);
+    return G4_E_NOMEM;
+  }
+  MoeScratch m = carve(base, T, dim, E, K, ff);
+  const float* f_scale = (const float*)w->gate_inp_scale->d;
+  moe_prep_kernel<<<T, 256, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, f_scale, m.moe_in, m.xr, dim, w->eps);
+  dim3 rg((E + 7) / 8, (T + 7) / 8);
+  moe_router_kernel<8><<<rg, 256, 0, st>>>((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E);
+  moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(m.logits, T, E, K, m.idx, m.prob);
+  moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, T * K, E, m.offsets, m.perm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer launch");
+  int r = launch_expert(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m, E, K,
+                        dim, ff, T, st);
+  if (r == 0)
+    r = launch_expert(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K, dim, ff, T,
+                      st);
+  if (r == -1) {
+    c->set_err("g4_moe_layer: expert tensor layout not supported by the grouped kernels");
+    return G4_E_ARG;
+  }
+  if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer expert launch");
+  moe_combine_kernel<<<T, 256, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
+                                        w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr, out, dim,
+                                        K, w->eps);
+  if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
+  if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : c->cuda_fail(e, "g4_moe_layer");
+}
+
+extern "C" int g4_moe_layer_host(g4_ctx* c, const g4_moe_weights* w, const float* xh, float* outh, int T,
+                                 int32_t* idx_h, float* prob_h) {
+  if (!c) return G4_E_ARG;
+  if (!w || !xh || !outh || T < 0) {
+    c->set_err("g4_moe_layer_host: bad argument");
+    return G4_E_ARG;
+  }
+  if (T == 0) return 0;
+  if (int r = c->bind()) return r;
+  const int dim = w->dim, K = w->n_used;
+  size_t xb = align_up((size_t)T * dim * 4, 256), ib = align_up((size_t)T * K * 4, 256);
+  // The io buffers live in their own arena: the layer's scratch arena may grow.
+  size_t need = 2 * xb + 2 * ib;
+  void* io = c->io(need);
+  if (!io) {
+    c->set_err("g4_moe_layer_host: cannot allocate %zu bytes", need);
+    return G4_E_NOMEM;
+  }
+  uint8_t* b = (uint8_t*)io;
+  float* xd = (float*)b;
+  float* od = (float*)(b + xb);
+  int32_t* id = (int32_t*)(b + 2 * xb);
+  float* pd = (float*)(b + 2 * xb + ib);
+  cudaStream_t st = 0;
+  cudaError_t e = cudaMemcpyAsync(xd, xh, (size_t)T * dim * 4, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_host H2D");
+  int r = g4_moe_layer(c, w, xd, od, T, id, pd, st);
+  if (r) return r;
+  cudaMemcpyAsync(outh, od, (size_t)T * dim * 4, cudaMemcpyDeviceToHost, st);
+  if (idx_h) cudaMemcpyAsync(idx_h, id, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st);
+  if (prob_h) cudaMemcpyAsync(prob_h, pd, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st);
+  return c->check_status(st);
+}

@@ -1,0 +1,69 @@
+"""Host-side mirror of gemma4.kt's MoE block, backed by libg4b200.
+
+The reference inlines the block in Llama.forward (Llama.kt:226-353) and keeps
+its weights in LlamaWeights (LlamaWeights.kt:50-65: ffnGateInp,
+ffnGateInpScale, ffnGateUpExps, ffnDownExps, ffnDownExpsScale, preFfwNorm2,
+ffnPostNorm2).  `MoeLayer.forward` runs the expert half (Llama.kt:247-346)
+for a batch of tokens in one call of g4_moe_layer.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._lib import MoeWeightsStruct, check, lib
+from .floattensor import Context, CudaFloatTensor, FloatTensorFactory, GGMLType, _is_torch, _stream_ptr
+
+
+class MoeLayer:
+    def __init__(self, ctx: Context, *, dim: int, n_expert: int, n_used: int, expert_ff: int, eps: float,
+                 gate_inp: CudaFloatTensor, gate_inp_scale: CudaFloatTensor, gate_up_exps: CudaFloatTensor,
+                 down_exps: CudaFloatTensor, down_exps_scale: CudaFloatTensor, pre_ffw_norm_2: CudaFloatTensor,
+                 post_ffw_norm_2: CudaFloatTensor | None):
+        self.ctx = ctx
+        self.dim, self.n_expert, self.n_used, self.expert_ff = dim, n_expert, n_used, expert_ff
+        self._tensors = [gate_inp, gate_inp_scale, gate_up_exps, down_exps, down_exps_scale, pre_ffw_norm_2,
+                         post_ffw_norm_2]
+        self.w = MoeWeightsStruct(dim, n_expert, n_used, expert_ff, eps, gate_inp.handle, gate_inp_scale.handle,
+                                  gate_up_exps.handle, down_exps.handle, down_exps_scale.handle,
+                                  pre_ffw_norm_2.handle, post_ffw_norm_2.handle if post_ffw_norm_2 else None)
+
+    @staticmethod
+    def upload(ctx: Context, data, post_norm: bool = True) -> "MoeLayer":
+        """Upload a synth.MoeLayerData (or anything with the same fields)."""
+        f32 = GGMLType.F32
+        up = FloatTensorFactory.create
+        return MoeLayer(
+            ctx, dim=data.dim, n_expert=data.n_expert, n_used=data.n_used, expert_ff=data.ff, eps=data.eps,
+            gate_inp=up(ctx, f32, data.gate_inp, data.n_expert * data.dim),
+            gate_inp_scale=up(ctx, f32, data.gate_inp_scale, data.dim),
+            gate_up_exps=up(ctx, data.expert_type, data.gate_up, data.n_expert * 2 * data.ff * data.dim),
+            down_exps=up(ctx, data.expert_type, data.down, data.n_expert * data.dim * data.ff),
+            down_exps_scale=up(ctx, f32, data.down_scale, data.n_expert),
+            pre_ffw_norm_2=up(ctx, f32, data.pre_norm, data.dim),
+            post_ffw_norm_2=up(ctx, f32, data.post_norm, data.dim) if post_norm else None,
+        )
+
+    def forward(self, x, out, n_tokens: int, topk_idx=None, topk_prob=None, stream=None) -> None:
+        """x, out: [n_tokens, dim]; topk_idx (int32) / topk_prob: [n_tokens, n_used] or None.
+        torch CUDA tensors run asynchronously on `stream`; numpy arrays synchronously."""
+        if _is_torch(x):
+            p = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
+            rc = lib().g4_moe_layer(self.ctx.handle, C.byref(self.w), p(x), p(out), n_tokens, p(topk_idx),
+                                    p(topk_prob), C.c_void_p(_stream_ptr(stream)))
+            check(rc, self.ctx.handle, "g4_moe_layer")
+        else:
+            xa = np.ascontiguousarray(x, dtype=np.float32)
+            p = lambda a: a.ctypes.data_as(C.c_void_p) if a is not None else None
+            rc = lib().g4_moe_layer_host(self.ctx.handle, C.byref(self.w), p(xa), p(out), n_tokens, p(topk_idx),
+                                         p(topk_prob))
+            check(rc, self.ctx.handle, "g4_moe_layer_host")
+
+
+def topk(ctx: Context, logits, n_tokens: int, n_expert: int, k: int, idx_out, prob_out, stream=None) -> None:
+    """Softmax + iterative top-k on given router logits (Llama.kt:273-293)."""
+    rc = lib().g4_moe_topk(ctx.handle, C.c_void_p(logits.data_ptr()), n_tokens, n_expert, k,
+                           C.c_void_p(idx_out.data_ptr()), C.c_void_p(prob_out.data_ptr()),
+                           C.c_void_p(_stream_ptr(stream)))
+    check(rc, ctx.handle, "g4_moe_topk")

@@ -1,0 +1,168 @@
+/*
+ * g4.h -- C ABI of libg4b200: B200 (sm_100a) kernels for gemma4.kt's two hot
+ * paths, the quantized matrix-vector product and the mixture-of-experts layer.
+ *
+ * The Kotlin host binds these with java.lang.foreign (FFM) downcalls; see
+ * INTEGRATION.md.  Every reference interface below is cited by its file:line
+ * under lib/src/main/kotlin/io/github/lbenedetto/internal/.
+ *
+ * Conventions
+ *  - Every entry point returns 0 on success and a negative G4_E* code on
+ *    failure; g4_last_error() then describes the failure.  No C++ exception and
+ *    no abort ever crosses this boundary (the reference throws
+ *    UnsupportedOperationException / IllegalArgumentException instead:
+ *    FloatTensorFactory.kt:21, Q8_0FloatTensor.kt:130).
+ *  - A g4_ctx is bound to one CUDA device and is not thread-safe; use one per
+ *    host thread / LlamaState, as the reference uses one LlamaState per thread.
+ *  - Pointers named *_dev are device pointers; *_host are host pointers.
+ *    `stream` is a cudaStream_t (NULL = legacy default stream).  Device-pointer
+ *    calls are asynchronous on that stream; *_host calls are synchronous.
+ *  - Weights are uploaded once in their on-disk GGUF block layout (no
+ *    dequantization on load) and live until g4_tensor_free.
+ */
+#ifndef G4_H
+#define G4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G4_OK 0
+#define G4_E_ARG -1        /* bad argument (IllegalArgumentException) */
+#define G4_E_TYPE -2       /* unsupported GGML type (UnsupportedOperationException) */
+#define G4_E_CUDA -3       /* CUDA runtime error */
+#define G4_E_NOMEM -4      /* device allocation failed */
+#define G4_E_DEVICE -5     /* a kernel reported an error status (e.g. bounded wait expired) */
+#define G4_E_DIST -6       /* NCCL / multi-GPU error */
+
+/* GGML type ids accepted by g4_tensor_upload (GGMLType.kt:16-46) */
+#define G4_TYPE_F32 0
+#define G4_TYPE_Q8_0 8
+#define G4_TYPE_Q4_K 12
+#define G4_TYPE_Q6_K 14
+#define G4_TYPE_BF16 30
+
+typedef struct g4_ctx g4_ctx;
+typedef struct g4_tensor g4_tensor;
+
+/* Create a context on CUDA device `device`.  (No reference counterpart: the
+ * reference's "device" is the JVM heap plus an mmap, GGUF.kt:195-212.) */
+int g4_init(int device, g4_ctx **out);
+int g4_destroy(g4_ctx *ctx);
+
+/* Description of the last failure on this context ("" if none).  A NULL ctx
+ * returns the last failure of g4_init on this thread. */
+const char *g4_last_error(const g4_ctx *ctx);
+
+/* Upload a tensor's raw block stream (`nbytes` bytes holding `n_elems`
+ * elements of GGML type `ggml_type`) to HBM unchanged.
+ * Replaces FloatTensorFactory.create (FloatTensorFactory.kt:7-23) reached from
+ * ModelLoader.loadQuantized (ModelLoader.kt:268-271); `host_blocks` is the
+ * address of the tensor's mmap slice (GGUF.kt:195-212, GGMLTensorEntry.kt:5-11).
+ * nbytes must equal GGMLType.byteSizeFor(n_elems) (GGMLType.kt:58-62). */
+int g4_tensor_upload(g4_ctx *ctx, int ggml_type, const void *host_blocks, uint64_t nbytes,
+                     uint64_t n_elems, g4_tensor **out);
+
+/* Upload rows [row_begin, row_begin+row_count) of a row-major [rows, cols]
+ * tensor (one output-row shard).  `host_blocks` points at the FULL tensor;
+ * the shard's rows must start and end on block boundaries. */
+int g4_tensor_upload_rows(g4_ctx *ctx, int ggml_type, const void *host_blocks, uint64_t cols,
+                          uint64_t row_begin, uint64_t row_count, g4_tensor **out);
+int g4_tensor_free(g4_tensor *t);
+/* Device address of the tensor's block stream (for callers composing kernels). */
+const void *g4_tensor_device_ptr(const g4_tensor *t);
+uint64_t g4_tensor_nbytes(const g4_tensor *t);
+uint64_t g4_tensor_n_elems(const g4_tensor *t);
+int g4_tensor_type(const g4_tensor *t);
+
+/* out_dev[i] = dot(W[this_offset + i*dim1 ...], x_dev[0..dim1)), i < dim0.
+ * Replaces FloatTensor.matmul(that, out, dim0, dim1, thisOffset)
+ * (FloatTensor.kt:25-29) and matmul(that, out, dim0, dim1) (FloatTensor.kt:18-22,
+ * this_offset = 0), i.e. every XFloatTensor.vectorDot it fans out to
+ * (Q8_0FloatTensor.kt:39-142, Q4_KFloatTensor.kt:86-207,
+ * Q6_KFloatTensor.kt:111-250, BF16FloatTensor.kt:35-74, F32FloatTensor.kt:37-66).
+ * x_dev must hold dim1 floats, out_dev dim0 floats. */
+int g4_matmul(g4_ctx *ctx, const g4_tensor *w, int64_t this_offset, const float *x_dev, float *out_dev,
+              int dim0, int dim1, void *stream);
+
+/* Same with host arrays (the Kotlin heap FloatArrays ArrayFloatTensor.values,
+ * ArrayFloatTensor.kt:12-28): copies x in, runs, copies out, synchronizes. */
+int g4_matmul_host(g4_ctx *ctx, const g4_tensor *w, int64_t this_offset, const float *x_host,
+                   float *out_host, int dim0, int dim1);
+
+/* out_dev[i] = W.get(offset + i), i < n: the reference's element decoder
+ * (Q8_0FloatTensor.kt:21-28, Q4_KFloatTensor.kt:23-55, Q6_KFloatTensor.kt:26-73,
+ * BF16FloatTensor.kt:20-24, F32FloatTensor.kt:18-20), bit-exact. */
+int g4_dequant(g4_ctx *ctx, const g4_tensor *w, int64_t offset, int64_t n, float *out_dev, void *stream);
+
+/* Wait for all work issued through this context on `stream` and report any
+ * error status a kernel recorded (bounded waits that expired). */
+int g4_sync(g4_ctx *ctx, void *stream);
+
+/* ---------------- mixture-of-experts layer (Llama.kt:247-346) ----------------
+ * Weights of one MoE layer, all uploaded with g4_tensor_upload:
+ *   gate_inp        F32  [dim, n_expert]     blk.N.ffn_gate_inp.weight
+ *   gate_inp_scale  F32  [dim]               blk.N.ffn_gate_inp.scale
+ *   gate_up_exps    Q4_K/Q8_0/Q6_K/BF16/F32 [dim, 2*ff, n_expert] blk.N.ffn_gate_up_exps.weight
+ *   down_exps       same types [ff, dim, n_expert]              blk.N.ffn_down_exps.weight
+ *   down_exps_scale F32  [n_expert]          blk.N.ffn_down_exps.scale
+ *   pre_ffw_norm_2  F32  [dim]               blk.N.pre_ffw_norm_2.weight
+ *   post_ffw_norm_2 F32  [dim] or NULL       blk.N.post_ffw_norm_2.weight
+ * (tensor names: ModelLoader.kt:223-232; shapes: LlamaWeights.kt:50-65). */
+typedef struct {
+  int dim;        /* gemma4.embedding_length (2816) */
+  int n_expert;   /* gemma4.expert_count (128) */
+  int n_used;     /* gemma4.expert_used_count (8) */
+  int expert_ff;  /* gemma4.expert_feed_forward_length (704) */
+  float eps;      /* gemma4.attention.layer_norm_rms_epsilon */
+  const g4_tensor *gate_inp;
+  const g4_tensor *gate_inp_scale;
+  const g4_tensor *gate_up_exps;
+  const g4_tensor *down_exps;
+  const g4_tensor *down_exps_scale;
+  const g4_tensor *pre_ffw_norm_2;
+  const g4_tensor *post_ffw_norm_2;
+} g4_moe_weights;
+
+/* Expert half of the MoE block for n_tokens independent tokens
+ * (Llama.kt:247-346): moeInput = rmsnorm(x, pre_ffw_norm_2); router
+ * rms(x)/sqrt(dim)*gate_inp_scale -> gate_inp matmul -> softmax -> top-n_used
+ * (ties to the lowest index, probabilities not renormalised); per selected
+ * expert gate_up matmul -> gelu(gate)*up -> down matmul -> accumulate with
+ * weight prob*down_exps_scale[e] in selection order; then
+ * rmsnorm(post_ffw_norm_2) when given.
+ * x_dev: [n_tokens, dim] residual stream (state.x); out_dev: [n_tokens, dim].
+ * topk_idx_dev / topk_prob_dev: [n_tokens, n_used] or NULL. */
+int g4_moe_layer(g4_ctx *ctx, const g4_moe_weights *w, const float *x_dev, float *out_dev, int n_tokens,
+                 int32_t *topk_idx_dev, float *topk_prob_dev, void *stream);
+
+/* Host-buffer variant (synchronous), for the Kotlin heap arrays. */
+int g4_moe_layer_host(g4_ctx *ctx, const g4_moe_weights *w, const float *x_host, float *out_host,
+                      int n_tokens, int32_t *topk_idx_host, float *topk_prob_host);
+
+/* Router top-k alone on given logits (Llama.kt:273-293 + softmaxInPlace,
+ * MutableFloatTensor.kt:54-59): probs_dev/idx_dev [n_tokens, k]. */
+int g4_moe_topk(g4_ctx *ctx, const float *logits_dev, int n_tokens, int n_expert, int k,
+                int32_t *idx_dev, float *prob_dev, void *stream);
+
+/* ---------------- multi-GPU (one process per GPU, NCCL over NVLink) ----------------
+ * No reference counterpart: the reference is single-process (no distributed code). */
+#define G4_NCCL_ID_BYTES 128
+int g4_dist_unique_id(void *id_out /* G4_NCCL_ID_BYTES */);
+int g4_dist_init(g4_ctx *ctx, int rank, int world, const void *id /* G4_NCCL_ID_BYTES */);
+int g4_dist_rank(const g4_ctx *ctx);
+int g4_dist_world(const g4_ctx *ctx);
+
+/* Row-sharded matmul: this rank holds rows [rank*rows/world, (rank+1)*rows/world)
+ * of a [rows, cols] weight (uploaded with g4_tensor_upload_rows); computes
+ * them and all-gathers into out_dev[rows] on every rank. rows % world == 0. */
+int g4_matmul_sharded(g4_ctx *ctx, const g4_tensor *w_shard, const float *x_dev, float *out_dev, int rows,
+                      int cols, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* G4_H */

@@ -1,0 +1,451 @@
+/*
+ * g4_oracle.c -- CPU restatement of gemma4.kt's hot-path kernels.
+ * TEST INFRASTRUCTURE ONLY (see g4_oracle.h).  Build: oracle/Makefile
+ * (gcc -O2 -ffp-contract=off).
+ *
+ * Reference paths below are relative to
+ * lib/src/main/kotlin/io/github/lbenedetto/internal/.
+ */
+#include "g4_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define LANES 16 /* 512-bit FloatVector species, FloatTensorHelpers.kt:9-29 */
+#define QK_K 256 /* GGMLType.kt:5 */
+#define JAVA_PI 3.141592653589793 /* Math.PI */
+
+int o_block_size(int type) {
+  switch (type) {
+    case O_Q8_0: return 32;
+    case O_Q4_K: return QK_K;
+    case O_Q6_K: return QK_K;
+    default: return 1;
+  }
+}
+
+int o_type_size(int type) {
+  switch (type) {
+    case O_F32: return 4;
+    case O_F16: return 2;
+    case O_BF16: return 2;
+    case O_Q8_0: return 34;   /* GGMLType.kt:24 */
+    case O_Q4_K: return 144;  /* GGMLType.kt:28 */
+    case O_Q6_K: return 210;  /* GGMLType.kt:30 */
+    default: return 0;
+  }
+}
+
+static inline float bits_to_f32(uint32_t b) {
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+
+static inline uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* Exact binary16 -> binary32.  Same bit construction as
+ * Q6_KFloatTensor.fp16ToFloatNoIntrinsic (Q6_KFloatTensor.kt:87-109), which
+ * agrees with Float.float16ToFloat for every non-NaN input. */
+float o_f16_to_f32(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1Fu;
+  uint32_t man = h & 0x3FFu;
+  if (exp == 0) {
+    if (man == 0) return bits_to_f32(sign);
+    int e = 127 - 15 + 1;
+    while ((man & 0x400u) == 0) {
+      man <<= 1;
+      e--;
+    }
+    man &= 0x3FFu;
+    return bits_to_f32(sign | ((uint32_t)e << 23) | (man << 13));
+  }
+  if (exp == 0x1F) return bits_to_f32(sign | 0x7F800000u | (man << 13));
+  return bits_to_f32(sign | ((exp + (127 - 15)) << 23) | (man << 13));
+}
+
+static inline float rd_f16(const uint8_t *p) { return o_f16_to_f32(rd16(p)); }
+
+/* Q4_KFloatTensor.getScaleMinK4 (Q4_KFloatTensor.kt:70-84) */
+static int scale_min_k4(int j, const uint8_t *s, int is_min) {
+  if (j < 4) return s[is_min ? j + 4 : j] & 63;
+  int low = is_min ? (s[j + 4] >> 4) : (s[j + 4] & 0xF);
+  int high = (s[is_min ? j : j - 4] >> 6) & 0x3;
+  return low | (high << 4);
+}
+
+float o_get(int type, const uint8_t *base, int64_t index) {
+  switch (type) {
+    case O_F32: { /* F32FloatTensor.kt:18-20 */
+      float f;
+      memcpy(&f, base + index * 4, 4);
+      return f;
+    }
+    case O_F16:
+      return rd_f16(base + index * 2);
+    case O_BF16: /* BF16FloatTensor.kt:20-24 */
+      return bits_to_f32((uint32_t)rd16(base + index * 2) << 16);
+    case O_Q8_0: { /* Q8_0FloatTensor.kt:21-28: quant * scale, one rounding */
+      int64_t b = index / 32, w = index % 32;
+      const uint8_t *blk = base + b * 34;
+      float scale = rd_f16(blk);
+      return (float)(int8_t)blk[2 + w] * scale;
+    }
+    case O_Q4_K: { /* Q4_KFloatTensor.kt:23-55 */
+      int64_t b = index / QK_K;
+      int within = (int)(index % QK_K);
+      const uint8_t *blk = base + b * 144;
+      float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+      const uint8_t *sc = blk + 4, *qs = blk + 16;
+      int group = within / 64, in_group = within % 64;
+      int sub, nib, high;
+      if (in_group < 32) {
+        sub = group * 2;
+        nib = in_group;
+        high = 0;
+      } else {
+        sub = group * 2 + 1;
+        nib = in_group - 32;
+        high = 1;
+      }
+      int s = scale_min_k4(sub, sc, 0), m = scale_min_k4(sub, sc, 1);
+      uint8_t byte = qs[group * 32 + nib];
+      int q = high ? (byte >> 4) & 0xF : byte & 0xF;
+      /* d * sc * quant - dmin * m: ((d*sc)*q) - (dmin*m), each op rounded */
+      float t = d * (float)s;
+      t = t * (float)q;
+      float u = dmin * (float)m;
+      return t - u;
+    }
+    case O_Q6_K: { /* Q6_KFloatTensor.kt:26-73 */
+      int64_t b = index / QK_K;
+      int within = (int)(index % QK_K);
+      const uint8_t *blk = base + b * 210;
+      const uint8_t *qh = blk + 128;
+      const int8_t *sc = (const int8_t *)(blk + 192);
+      float d = rd_f16(blk + 208);
+      int half = within / 128, rem = within % 128, sub32 = rem / 32, l = rem % 32;
+      const uint8_t *ql = blk + half * 64;
+      const uint8_t *qhb = qh + half * 32;
+      int nib, shift;
+      switch (sub32) {
+        case 0: nib = ql[l] & 0xF; shift = 0; break;
+        case 1: nib = ql[32 + l] & 0xF; shift = 2; break;
+        case 2: nib = (ql[l] >> 4) & 0xF; shift = 4; break;
+        default: nib = (ql[32 + l] >> 4) & 0xF; shift = 6; break;
+      }
+      int hb = (qhb[l] >> shift) & 3;
+      int q6 = (nib | (hb << 4)) - 32;
+      int s = sc[half * 8 + sub32 * 2 + l / 16];
+      float t = d * (float)s;
+      return t * (float)q6;
+    }
+    default:
+      return NAN;
+  }
+}
+
+void o_dequant(int type, const uint8_t *base, int64_t offset, int64_t n, float *out) {
+  for (int64_t i = 0; i < n; i++) out[i] = o_get(type, base, offset + i);
+}
+
+/* FloatTensorHelpers.scalarDot (FloatTensorHelpers.kt:65-71): sequential,
+ * product rounded then added. */
+float o_scalar_dot(int type, const uint8_t *base, int64_t this_offset, const float *x, int size) {
+  float r = 0.0f;
+  for (int j = 0; j < size; j++) {
+    float p = o_get(type, base, this_offset + j) * x[j];
+    r = r + p;
+  }
+  return r;
+}
+
+/* FloatVector.reduceLanes(ADD): the JVM leaves the order unspecified; the
+ * oracle uses a fixed pairwise tree. */
+static float reduce_lanes(const float *v) {
+  float t[LANES];
+  memcpy(t, v, sizeof t);
+  for (int w = LANES / 2; w >= 1; w >>= 1)
+    for (int i = 0; i < w; i++) t[i] = t[i] + t[i + w];
+  return t[0];
+}
+
+/* Alignment head shared by the quantized vectorDots (e.g. Q8_0FloatTensor.kt:50-54):
+ * elements before the next block boundary go through scalarDot. */
+static int head_len(int64_t this_offset, int bs, int size) {
+  int64_t rem = this_offset % bs;
+  int h = rem == 0 ? 0 : (int)(bs - rem);
+  return h < size ? h : size;
+}
+
+/* Q8_0FloatTensor.vectorDot, 512-bit branch (Q8_0FloatTensor.kt:39-78,132-141) */
+static float dot_q8_0(const uint8_t *base, int64_t off, const float *x, int size) {
+  float result = 0.0f;
+  int j = head_len(off, 32, size);
+  if (j > 0) result += o_scalar_dot(O_Q8_0, base, off, x, j);
+  float acc[LANES] = {0};
+  const uint8_t *blk = base + (off + j) / 32 * 34;
+  int upper = j + (size - j) / 32 * 32;
+  for (; j < upper; j += 32, blk += 34) {
+    float d = rd_f16(blk);
+    const int8_t *q = (const int8_t *)(blk + 2);
+    for (int l = 0; l < LANES; l++) {
+      float s0 = x[j + l] * (float)q[l];
+      float s1 = x[j + LANES + l] * (float)q[LANES + l];
+      acc[l] = fmaf(s0 + s1, d, acc[l]);
+    }
+  }
+  result += reduce_lanes(acc);
+  if (j < size) result += o_scalar_dot(O_Q8_0, base, off + j, x + j, size - j);
+  return result;
+}
+
+/* Q4_KFloatTensor.vectorDot, 512-bit branch (Q4_KFloatTensor.kt:86-148,196-206) */
+static float dot_q4_k(const uint8_t *base, int64_t off, const float *x, int size) {
+  float result = 0.0f;
+  int j = head_len(off, QK_K, size);
+  if (j > 0) result += o_scalar_dot(O_Q4_K, base, off, x, j);
+  float v1[LANES] = {0}, v2[LANES] = {0};
+  const uint8_t *blk = base + (off + j) / QK_K * 144;
+  int upper = j + (size - j) / QK_K * QK_K;
+  for (; j < upper; j += QK_K, blk += 144) {
+    float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+    const uint8_t *sc = blk + 4, *qs = blk + 16;
+    for (int g = 0; g < 4; g++) {
+      float d1 = d * (float)scale_min_k4(2 * g, sc, 0);
+      float negm1 = -(dmin * (float)scale_min_k4(2 * g, sc, 1));
+      float d2 = d * (float)scale_min_k4(2 * g + 1, sc, 0);
+      float negm2 = -(dmin * (float)scale_min_k4(2 * g + 1, sc, 1));
+      for (int c = 0; c < 2; c++) {
+        const uint8_t *w = qs + g * 32 + c * 16;
+        const float *xlo = x + j + g * 64 + c * 16;
+        const float *xhi = x + j + g * 64 + 32 + c * 16;
+        for (int l = 0; l < LANES; l++) {
+          float lo = (float)(w[l] & 0xF), hi = (float)(w[l] >> 4);
+          v1[l] = fmaf(fmaf(lo, d1, negm1), xlo[l], v1[l]);
+          v2[l] = fmaf(fmaf(hi, d2, negm2), xhi[l], v2[l]);
+        }
+      }
+    }
+  }
+  float s[LANES];
+  for (int l = 0; l < LANES; l++) s[l] = v1[l] + v2[l];
+  result += reduce_lanes(s);
+  if (j < size) result += o_scalar_dot(O_Q4_K, base, off + j, x + j, size - j);
+  return result;
+}
+
+/* Q6_KFloatTensor.vectorDot, 512-bit branch (Q6_KFloatTensor.kt:111-205,239-249) */
+static float dot_q6_k(const uint8_t *base, int64_t off, const float *x, int size) {
+  float result = 0.0f;
+  int j = head_len(off, QK_K, size);
+  if (j > 0) result += o_scalar_dot(O_Q6_K, base, off, x, j);
+  float acc[LANES] = {0};
+  const uint8_t *blk = base + (off + j) / QK_K * 210;
+  int upper = j + (size - j) / QK_K * QK_K;
+  for (; j < upper; j += QK_K, blk += 210) {
+    const int8_t *sc = (const int8_t *)(blk + 192);
+    float d = rd_f16(blk + 208);
+    for (int h = 0; h < 2; h++) {
+      const uint8_t *ql = blk + h * 64, *qh = blk + 128 + h * 32;
+      const float *xb = x + j + h * 128;
+      for (int c = 0; c < 2; c++) {
+        const uint8_t *a = ql + c * 16, *b = ql + 32 + c * 16, *hv = qh + c * 16;
+        float ds0 = d * (float)sc[h * 8 + c];
+        float ds1 = d * (float)sc[h * 8 + 2 + c];
+        float ds2 = d * (float)sc[h * 8 + 4 + c];
+        float ds3 = d * (float)sc[h * 8 + 6 + c];
+        for (int l = 0; l < LANES; l++) {
+          int q0 = (int)(int8_t)(uint8_t)(((a[l] & 0xF) | ((hv[l] & 3) << 4)) - 32);
+          int q1 = (int)(int8_t)(uint8_t)(((b[l] & 0xF) | (((hv[l] >> 2) & 3) << 4)) - 32);
+          int q2 = (int)(int8_t)(uint8_t)(((a[l] >> 4) | (((hv[l] >> 4) & 3) << 4)) - 32);
+          int q3 = (int)(int8_t)(uint8_t)(((b[l] >> 4) | (((hv[l] >> 6) & 3) << 4)) - 32);
+          acc[l] = fmaf((float)q0 * ds0, xb[c * 16 + l], acc[l]);
+          acc[l] = fmaf((float)q1 * ds1, xb[32 + c * 16 + l], acc[l]);
+          acc[l] = fmaf((float)q2 * ds2, xb[64 + c * 16 + l], acc[l]);
+          acc[l] = fmaf((float)q3 * ds3, xb[96 + c * 16 + l], acc[l]);
+        }
+      }
+    }
+  }
+  result += reduce_lanes(acc);
+  if (j < size) result += o_scalar_dot(O_Q6_K, base, off + j, x + j, size - j);
+  return result;
+}
+
+/* BF16FloatTensor.vectorDot (BF16FloatTensor.kt:35-74) and
+ * F32FloatTensor.vectorDot (F32FloatTensor.kt:37-66): plain 16-lane fma over
+ * loopBound(size), then a sequential tail added onto the reduced sum. */
+static float dot_wide(int type, const uint8_t *base, int64_t off, const float *x, int size) {
+  float acc[LANES] = {0};
+  int upper = size / LANES * LANES;
+  for (int i = 0; i < upper; i += LANES)
+    for (int l = 0; l < LANES; l++) acc[l] = fmaf(o_get(type, base, off + i + l), x[i + l], acc[l]);
+  float result = reduce_lanes(acc);
+  if (type == O_BF16) {
+    if (upper < size) result += o_scalar_dot(type, base, off + upper, x + upper, size - upper);
+  } else {
+    for (int i = upper; i < size; i++) {
+      float p = o_get(type, base, off + i) * x[i];
+      result = result + p;
+    }
+  }
+  return result;
+}
+
+float o_vector_dot(int type, const uint8_t *base, int64_t this_offset, const float *x, int size) {
+  switch (type) {
+    case O_Q8_0: return dot_q8_0(base, this_offset, x, size);
+    case O_Q4_K: return dot_q4_k(base, this_offset, x, size);
+    case O_Q6_K: return dot_q6_k(base, this_offset, x, size);
+    case O_BF16:
+    case O_F32: return dot_wide(type, base, this_offset, x, size);
+    default: return o_scalar_dot(type, base, this_offset, x, size);
+  }
+}
+
+typedef struct {
+  int type, dim1, vector, r0, r1;
+  const uint8_t *base;
+  int64_t off;
+  const float *x;
+  float *out;
+} mm_job;
+
+static void *mm_worker(void *p) {
+  mm_job *jb = (mm_job *)p;
+  for (int i = jb->r0; i < jb->r1; i++) {
+    int64_t o = jb->off + (int64_t)i * jb->dim1;
+    jb->out[i] = jb->vector ? o_vector_dot(jb->type, jb->base, o, jb->x, jb->dim1)
+                            : o_scalar_dot(jb->type, jb->base, o, jb->x, jb->dim1);
+  }
+  return NULL;
+}
+
+void o_matmul(int type, const uint8_t *base, int64_t this_offset, const float *x, float *out,
+              int dim0, int dim1, int nthreads, int vector) {
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > dim0) nthreads = dim0 > 0 ? dim0 : 1;
+  mm_job jobs[256];
+  pthread_t th[256];
+  if (nthreads > 256) nthreads = 256;
+  for (int t = 0; t < nthreads; t++) {
+    jobs[t] = (mm_job){type, dim1, vector, (int)((int64_t)dim0 * t / nthreads),
+                       (int)((int64_t)dim0 * (t + 1) / nthreads), base, this_offset, x, out};
+  }
+  for (int t = 1; t < nthreads; t++) pthread_create(&th[t], NULL, mm_worker, &jobs[t]);
+  mm_worker(&jobs[0]);
+  for (int t = 1; t < nthreads; t++) pthread_join(th[t], NULL);
+}
+
+/* Llama.gelu (Llama.kt:23-25): evaluated in double, rounded to float */
+float o_gelu(float x) {
+  double xd = (double)x;
+  double inner = sqrt(2.0 / JAVA_PI) * (xd + 0.044715 * pow(xd, 3.0));
+  return (float)(0.5 * xd * (1.0 + tanh(inner)));
+}
+
+/* Llama.rmsnorm (Llama.kt:27-37): sequential float sum of squares, 1/sqrt in
+ * double, out[i] = w[i] * (ss * x[i]).  out may alias x. */
+void o_rmsnorm(float *out, const float *x, const float *w, int size, float eps) {
+  float ss = 0.0f;
+  for (int i = 0; i < size; i++) {
+    float sq = x[i] * x[i];
+    ss = ss + sq;
+  }
+  ss = ss / (float)size;
+  ss = ss + eps;
+  ss = (float)(1.0 / sqrt((double)ss));
+  for (int i = 0; i < size; i++) {
+    float t = ss * x[i];
+    out[i] = w[i] * t;
+  }
+}
+
+/* MutableFloatTensor.softmaxInPlace (MutableFloatTensor.kt:54-59) */
+void o_softmax(float *x, int n) {
+  float mx = -INFINITY;
+  for (int i = 0; i < n; i++) mx = fmaxf(mx, x[i]); /* Math::max */
+  for (int i = 0; i < n; i++) x[i] = (float)exp((double)(x[i] - mx));
+  float sum = 0.0f;
+  for (int i = 0; i < n; i++) sum = sum + x[i];
+  for (int i = 0; i < n; i++) x[i] = x[i] / sum;
+}
+
+/* Llama.kt:276-293 */
+void o_topk(float *probs, int n, int k, int32_t *idx, float *val) {
+  for (int ki = 0; ki < k; ki++) {
+    int best = 0;
+    float bv = -INFINITY;
+    for (int e = 0; e < n; e++) {
+      if (probs[e] > bv) {
+        bv = probs[e];
+        best = e;
+      }
+    }
+    idx[ki] = best;
+    val[ki] = bv;
+    probs[best] = -INFINITY;
+  }
+}
+
+/* Router input and logits, Llama.kt:257-270 */
+void o_moe_router_logits(const o_moe_weights *w, const float *x, float *logits) {
+  int dim = w->dim;
+  float ss = 0.0f;
+  for (int i = 0; i < dim; i++) {
+    float sq = x[i] * x[i];
+    ss = ss + sq;
+  }
+  ss = ss / (float)dim;
+  ss = ss + w->eps;
+  float rms = (float)(1.0 / sqrt((double)ss)) / (float)sqrt((double)dim);
+  float *xr = (float *)malloc(sizeof(float) * dim);
+  for (int i = 0; i < dim; i++) {
+    float t = x[i] * rms;
+    xr[i] = t * w->gate_inp_scale[i];
+  }
+  for (int e = 0; e < w->n_expert; e++)
+    logits[e] = o_vector_dot(O_F32, w->gate_inp, (int64_t)e * dim, xr, dim);
+  free(xr);
+}
+
+void o_moe_token(const o_moe_weights *w, const float *x, float *out, int32_t *topk_idx,
+                 float *topk_prob, float *router_logits_out, int nthreads) {
+  int dim = w->dim, ff = w->expert_ff, gu = 2 * ff;
+  float *moe_in = (float *)malloc(sizeof(float) * dim);
+  float *probs = (float *)malloc(sizeof(float) * w->n_expert);
+  float *gate_up = (float *)malloc(sizeof(float) * gu);
+  float *down = (float *)malloc(sizeof(float) * dim);
+  /* moeInput = rmsnorm(x, pre_ffw_norm_2), Llama.kt:248-254 */
+  o_rmsnorm(moe_in, x, w->pre_ffw_norm_2, dim, w->eps);
+  o_moe_router_logits(w, x, probs);
+  if (router_logits_out) memcpy(router_logits_out, probs, sizeof(float) * w->n_expert);
+  o_softmax(probs, w->n_expert); /* Llama.kt:273 */
+  o_topk(probs, w->n_expert, w->n_used, topk_idx, topk_prob);
+  for (int i = 0; i < dim; i++) out[i] = 0.0f; /* Llama.kt:298 */
+  for (int ki = 0; ki < w->n_used; ki++) {       /* Llama.kt:300-337 */
+    int e = topk_idx[ki];
+    float prob = topk_prob[ki];
+    float down_scale = w->down_exps_scale[e];
+    int64_t gu_off = (int64_t)e * gu * dim;
+    o_matmul(w->gate_up_type, w->gate_up_exps, gu_off, moe_in, gate_up, gu, dim, nthreads, 1);
+    for (int i = 0; i < ff; i++) gate_up[i] = o_gelu(gate_up[i]);
+    for (int i = 0; i < ff; i++) gate_up[i] = gate_up[i] * gate_up[ff + i];
+    int64_t dn_off = (int64_t)e * dim * ff;
+    o_matmul(w->down_type, w->down_exps, dn_off, gate_up, down, dim, ff, nthreads, 1);
+    float fw = prob * down_scale;
+    for (int i = 0; i < dim; i++) {
+      float p = fw * down[i];
+      out[i] = p + out[i];
+    }
+  }
+  if (w->post_ffw_norm_2) o_rmsnorm(out, out, w->post_ffw_norm_2, dim, w->eps); /* Llama.kt:340-346 */
+  free(moe_in);
+  free(probs);
+  free(gate_up);
+  free(down);
+}
