@@ -225,6 +225,8 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   const int BS = block_size(type), TS = type_size(type);
   if (TS == 0 || type == F16 || rows <= 0 || cols <= 0) return p;
   if (cols % 16 != 0 || off % BS != 0) return p;
+  // 16-byte shared loads of BF16/F32 units need 16-byte aligned tile starts.
+  if ((type == BF16 || type == F32) && ((off * TS) % 16) != 0) return p;
   int pr = BS / gcd_i(cols % BS == 0 ? BS : cols % BS, BS);
   if (cols % BS == 0) pr = 1;
   if (pr != 1 && pr != 2 && pr != 4) return p;

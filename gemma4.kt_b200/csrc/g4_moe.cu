@@ -219,6 +219,7 @@ struct ExpertArgs {
   int tiles_e;              // row tiles per expert
   int tile_rows;            // GATEUP: pairs per tile; DOWN: virtual rows per tile
   int stage_bytes, nstages;
+  int region_bytes;         // GATEUP: offset of the up-row region in a stage
   long long expert_elems;   // elements per expert matrix
 };
 
@@ -285,17 +286,20 @@ __global__ void __launch_bounds__(32 * (NCW + 1)) moe_expert_kernel(const __grid
         int nr = min(a.tile_rows, a.ff - r0);
         long long g0 = (eb + (long long)r0 * a.cols) / BS * TS;
         long long u0 = (eb + (long long)(a.ff + r0) * a.cols) / BS * TS;
-        uint32_t bytes = (uint32_t)nr * a.vb;  // rows of whole blocks, 16B multiples (checked on host)
-        mbar_arrive_expect_tx(&full[s], 2 * bytes);
-        bulk_g2s(dst, a.w + g0, bytes, &full[s]);
-        bulk_g2s(dst + (size_t)a.tile_rows * a.vb, a.w + u0, bytes, &full[s]);
+        long long bytes = (long long)nr * a.vb;
+        // copy the 16-byte aligned superset of each row range
+        long long ga = g0 & ~15ll, gb = (g0 + bytes + 15) & ~15ll;
+        long long ua = u0 & ~15ll, ub = (u0 + bytes + 15) & ~15ll;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)((gb - ga) + (ub - ua)));
+        bulk_g2s(dst, a.w + ga, (uint32_t)(gb - ga), &full[s]);
+        bulk_g2s(dst + a.region_bytes, a.w + ua, (uint32_t)(ub - ua), &full[s]);
       } else {
         int v0 = tile * a.tile_rows;
         int nv = min(a.tile_rows, a.rows_e / PR - v0);
         long long b0 = (eb + (long long)v0 * PR * a.cols) / BS * TS;
-        uint32_t bytes = (uint32_t)nv * a.vb;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(dst, a.w + b0, bytes, &full[s]);
+        long long ba = b0 & ~15ll, bb = (b0 + (long long)nv * a.vb + 15) & ~15ll;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(bb - ba));
+        bulk_g2s(dst, a.w + ba, (uint32_t)(bb - ba), &full[s]);
       }
     }
     for (int j = max(0, it - NS); j < it; ++j)
@@ -326,10 +330,14 @@ __global__ void __launch_bounds__(32 * (NCW + 1)) moe_expert_kernel(const __grid
     const uint8_t* st = stages + (size_t)s * a.stage_bytes;
 
     if (GATEUP) {
-      const int r = tile * a.tile_rows + cw;  // gate row; up row = ff + r
+      const int r0 = tile * a.tile_rows;
+      const int r = r0 + cw;  // gate row; up row = ff + r
       const bool valid = r < a.ff;
-      const uint8_t* vg = st + (size_t)cw * a.vb;
-      const uint8_t* vu = st + (size_t)(a.tile_rows + cw) * a.vb;
+      const long long eb = (long long)e * a.expert_elems;
+      const int gmis = (int)(((eb + (long long)r0 * a.cols) / BS * TS) & 15);
+      const int umis = (int)(((eb + (long long)(a.ff + r0) * a.cols) / BS * TS) & 15);
+      const uint8_t* vg = st + gmis + (size_t)cw * a.vb;
+      const uint8_t* vu = st + a.region_bytes + umis + (size_t)cw * a.vb;
       float ag[NB], au[NB];
 #pragma unroll
       for (int j = 0; j < NB; ++j) ag[j] = au[j] = 0.f;
@@ -372,7 +380,9 @@ __global__ void __launch_bounds__(32 * (NCW + 1)) moe_expert_kernel(const __grid
     } else {
       const int v = tile * a.tile_rows + cw;
       const bool valid = v < a.rows_e / PR;
-      const uint8_t* vbp = st + (size_t)cw * a.vb;
+      const long long eb = (long long)e * a.expert_elems;
+      const int mis = (int)(((eb + (long long)tile * a.tile_rows * PR * a.cols) / BS * TS) & 15);
+      const uint8_t* vbp = st + mis + (size_t)cw * a.vb;
       float acc[PR][NB];
 #pragma unroll
       for (int r = 0; r < PR; ++r)
@@ -548,11 +558,12 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
     a.pr = 1;
     if (dim % BS || dim % 16) return -1;
     a.vb = dim / BS * TS;
-    if (a.vb % 16) return -1;  // gate/up row starts must be 16B aligned for the bulk copies
+    if (a.vb % 2) return -1;
     a.units = dim / 16;
     a.tile_rows = NCW;
     a.tiles_e = (ff + NCW - 1) / NCW;
-    a.stage_bytes = (int)align_up((size_t)2 * NCW * a.vb, 128);
+    a.region_bytes = (int)align_up((size_t)NCW * a.vb + 32, 128);
+    a.stage_bytes = 2 * a.region_bytes;
     a.expert_elems = (long long)2 * ff * dim;
   } else {
     a.rows_e = dim;
@@ -563,11 +574,11 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
     if (dim % pr) return -1;
     a.pr = pr;
     a.vb = pr * ff / BS * TS;
-    if (a.vb % 16) return -1;
+    if (a.vb % 2) return -1;
     a.units = pr * ff / 16;
     a.tile_rows = NCW;
     a.tiles_e = (dim / pr + NCW - 1) / NCW;
-    a.stage_bytes = (int)align_up((size_t)NCW * a.vb, 128);
+    a.stage_bytes = (int)align_up((size_t)NCW * a.vb + 32, 128);
     a.expert_elems = (long long)dim * ff;
   }
   if (a.expert_elems % BS) return -1;
