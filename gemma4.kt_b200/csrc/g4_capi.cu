@@ -256,7 +256,15 @@ int g4_matmul(g4_ctx* c, const g4_tensor* w, int64_t off, const float* x, float*
     cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * dim0, st);
     return e == cudaSuccess ? 0 : c->cuda_fail(e, "g4_matmul");
   }
-  if (launch_gemv(c->dev, w->type, (const uint8_t*)w->d, off, dim0, dim1, x, y, c->status, st, nullptr)) {
+  const int xal = ((uintptr_t)x & 15u) == 0;
+  auto key = std::make_tuple(w->type, (long long)off, dim0, dim1, xal);
+  auto itp = c->gemv_plans.find(key);
+  if (itp == c->gemv_plans.end()) {
+    GemvPlan p = plan_gemv(c->dev, w->type, off, dim0, dim1);
+    if (!xal) p.fast = 0;
+    itp = c->gemv_plans.emplace(key, p).first;
+  }
+  if (launch_gemv(itp->second, (const uint8_t*)w->d, x, y, c->status, st)) {
     cudaError_t e = cudaGetLastError();
     return c->cuda_fail(e, "g4_matmul launch");
   }

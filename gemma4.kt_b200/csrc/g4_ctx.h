@@ -4,6 +4,10 @@
 #include <stdint.h>
 
 #include "g4_internal.h"
+#include "g4_gemv.cuh"
+
+#include <map>
+#include <tuple>
 
 struct g4_ctx {
   g4::DeviceInfo dev{};
@@ -18,6 +22,8 @@ struct g4_ctx {
   int rank = 0;
   int world = 1;
   char err[512] = {0};
+  // launch plans, keyed by (type, offset, rows, cols, x 16B-aligned)
+  std::map<std::tuple<int, long long, int, int, int>, g4::GemvPlan> gemv_plans;
 
   void set_err(const char* fmt, ...);
   int cuda_fail(cudaError_t e, const char* what);

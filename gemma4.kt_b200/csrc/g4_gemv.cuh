@@ -1,10 +1,6 @@
-// g4_gemv.cuh -- per-format 16-element decode+dot units for the streaming
-// quantized GEMV, and the launch plan shared by host and device.
-//
-// A "unit" is 16 consecutive weights of one row: the same 16-lane slice the
-// reference's 512-bit vectorDot processes per FloatVector (e.g.
-// Q8_0FloatTensor.kt:64-78 handles a 32-weight block as two 16-lane halves;
-// Q4_KFloatTensor.kt:131-148 one 16-byte chunk of nibbles per lane vector).
+// g4_gemv.cuh -- launch plan of the streaming GEMV, the reference-exact
+// element decoder (get) and the 16-weight unit dequantizer shared with the
+// MoE expert kernels.
 #pragma once
 #include "g4_common.cuh"
 
@@ -13,20 +9,21 @@ namespace g4 {
 struct GemvPlan {
   int type;
   int rows, cols;
-  long long off;     // element offset into the tensor (thisOffset)
-  int pr;            // rows per virtual row (period after which blocks realign)
+  long long off;     // element offset into the tensor (thisOffset), block aligned
+  int pr;            // rows per virtual row: after pr rows the block pattern repeats
   int nvrows;        // rows / pr
-  int vb;            // bytes per virtual row (whole blocks)
-  int units;         // 16-weight units per virtual row
-  int ncw;           // consumer warps per CTA (one producer warp besides)
-  int rw;            // virtual rows per consumer warp per tile
-  int tile_vrows;    // ncw * rw
-  int ntiles;
-  int stage_bytes;   // capacity of one smem stage (multiple of 128)
-  int nstages;
+  int bpv;           // blocks per virtual row
+  int cb;            // blocks per chunk (one bulk copy per row and chunk)
+  int nchunks;       // chunks per virtual row
+  int pitch;         // bytes per row slot in a stage (16 * odd: conflict-free)
+  int rl;            // virtual rows per lane
+  int ns;            // stages per warp
+  int warps;         // warps per CTA
+  int split;         // 1: persistent, each warp owns whole row groups; >1: CTA per group
+  int ngroups;       // row groups of 32*rl virtual rows
   int grid;
-  int xbytes;        // bytes of x staged in smem (cols * 4 rounded to 128)
-  size_t smem;       // dynamic shared memory per CTA
+  int xs_off, xsum_off, bar_off, ring_off, red_off;  // shared-memory carve-up
+  size_t smem;
   int fast;          // 1: streaming kernel; 0: generic fallback
 };
 
@@ -34,124 +31,6 @@ struct GemvPlan {
 // Exact for 0 <= b < 2^23 and avoids the quarter-rate I2F path.
 __device__ __forceinline__ float byte_as_float(uint32_t word, uint32_t sel_byte) {
   return __int_as_float((int)__byte_perm(word, 0x4B000000u, 0x7440u | sel_byte));
-}
-
-// ---- Q8_0: [fp16 d][int8 q x32] (Q8_0FloatTensor.kt:21-28,64-78) ----
-__device__ __forceinline__ float dot16_q8_0(const uint8_t* vb, int u, const float* x) {
-  const uint8_t* blk = vb + (u >> 1) * 34;
-  float d = f16_bits_to_f32(lds16(blk));
-  uint32_t w[4];
-  lds16B_unaligned(blk + 2 + (u & 1) * 16, w);
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uint32_t wk = w[k] ^ 0x80808080u;  // int8 q -> q + 128 as unsigned byte
-    s0 = fmaf(byte_as_float(wk, 0) - 8388736.0f, x[4 * k + 0], s0);
-    s1 = fmaf(byte_as_float(wk, 1) - 8388736.0f, x[4 * k + 1], s1);
-    s0 = fmaf(byte_as_float(wk, 2) - 8388736.0f, x[4 * k + 2], s0);
-    s1 = fmaf(byte_as_float(wk, 3) - 8388736.0f, x[4 * k + 3], s1);
-  }
-  return (s0 + s1) * d;
-}
-
-// ---- Q4_K: [fp16 d][fp16 dmin][scales 12][qs 128] (Q4_KFloatTensor.kt:23-55,70-84,116-148) ----
-// Unit u covers block u>>4, weights 16*(u&15) .. +16 of it: group g, nibble
-// half hi, 16-byte chunk c of the group's 32 qs bytes.
-__device__ __forceinline__ float dot16_q4_k(const uint8_t* vb, int u, const float* x, float sx) {
-  const uint8_t* blk = vb + (u >> 4) * 144;  // 144 = 9*16: blocks stay 16B aligned
-  int i0 = (u & 15) * 16;
-  int g = i0 >> 6, hi = (i0 >> 5) & 1, c = (i0 >> 4) & 1;
-  uint4 h = lds128(blk);
-  float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
-  float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
-  // scale/min of sub-block j = 2g+hi, decoded as getScaleMinK4
-  int j = 2 * g + hi;
-  uint32_t sc, mn;
-  if (j < 4) {
-    sc = (h.y >> (8 * j)) & 63u;
-    mn = (h.z >> (8 * j)) & 63u;
-  } else {
-    int jj = j - 4;
-    uint32_t lo = (h.w >> (8 * jj)) & 0xFFu;
-    sc = (lo & 0xFu) | (((h.y >> (8 * jj + 6)) & 3u) << 4);
-    mn = (lo >> 4) | (((h.z >> (8 * jj + 6)) & 3u) << 4);
-  }
-  float d1 = d * (float)sc;
-  float m1 = dmin * (float)mn;
-  uint4 q = lds128(blk + 16 + g * 32 + c * 16);
-  uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uint32_t nib = (hi ? (qw[k] >> 4) : qw[k]) & 0x0F0F0F0Fu;
-    s0 = fmaf(byte_as_float(nib, 0) - 8388608.0f, x[4 * k + 0], s0);
-    s1 = fmaf(byte_as_float(nib, 1) - 8388608.0f, x[4 * k + 1], s1);
-    s0 = fmaf(byte_as_float(nib, 2) - 8388608.0f, x[4 * k + 2], s0);
-    s1 = fmaf(byte_as_float(nib, 3) - 8388608.0f, x[4 * k + 3], s1);
-  }
-  // sum_i (d1*q_i - m1) * x_i
-  return fmaf(d1, s0 + s1, -m1 * sx);
-}
-
-// ---- Q6_K: [ql 128][qh 64][int8 sc 16][fp16 d] (Q6_KFloatTensor.kt:26-73,144-205) ----
-__device__ __forceinline__ float dot16_q6_k(const uint8_t* vb, int u, const float* x) {
-  const uint8_t* blk = vb + (u >> 4) * 210;
-  int i0 = (u & 15) * 16;
-  int half = i0 >> 7, rem = i0 & 127, sub32 = rem >> 5, l0 = rem & 31;
-  uint32_t ql[4], qh[4];
-  lds16B_unaligned(blk + half * 64 + (sub32 & 1) * 32 + l0, ql);
-  lds16B_unaligned(blk + 128 + half * 32 + l0, qh);
-  int8_t scv = (int8_t)(lds16(blk + 192 + ((u & 15) & ~1)) >> (8 * (u & 1)));
-  float d = f16_bits_to_f32(lds16(blk + 208));
-  uint32_t nsh = (sub32 >> 1) * 4u, hsh = 2u * (uint32_t)sub32;
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uint32_t q6 = ((ql[k] >> nsh) & 0x0F0F0F0Fu) | (((qh[k] >> hsh) & 0x03030303u) << 4);
-    s0 = fmaf(byte_as_float(q6, 0) - 8388640.0f, x[4 * k + 0], s0);  // 2^23 + 32
-    s1 = fmaf(byte_as_float(q6, 1) - 8388640.0f, x[4 * k + 1], s1);
-    s0 = fmaf(byte_as_float(q6, 2) - 8388640.0f, x[4 * k + 2], s0);
-    s1 = fmaf(byte_as_float(q6, 3) - 8388640.0f, x[4 * k + 3], s1);
-  }
-  return (d * (float)scv) * (s0 + s1);
-}
-
-// ---- BF16 (BF16FloatTensor.kt:20-24,35-74) ----
-__device__ __forceinline__ float dot16_bf16(const uint8_t* vb, int u, const float* x) {
-  const uint8_t* p = vb + u * 32;
-  uint4 a = lds128(p), b = lds128(p + 16);
-  uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    s0 = fmaf(__uint_as_float(w[k] << 16), x[2 * k], s0);
-    s1 = fmaf(__uint_as_float(w[k] & 0xFFFF0000u), x[2 * k + 1], s1);
-  }
-  return s0 + s1;
-}
-
-// ---- F32 (F32FloatTensor.kt:18-20,37-66) ----
-__device__ __forceinline__ float dot16_f32(const uint8_t* vb, int u, const float* x) {
-  const uint8_t* p = vb + u * 64;
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uint4 a = lds128(p + 16 * k);
-    s0 = fmaf(__uint_as_float(a.x), x[4 * k + 0], s0);
-    s1 = fmaf(__uint_as_float(a.y), x[4 * k + 1], s1);
-    s0 = fmaf(__uint_as_float(a.z), x[4 * k + 2], s0);
-    s1 = fmaf(__uint_as_float(a.w), x[4 * k + 3], s1);
-  }
-  return s0 + s1;
-}
-
-template <int FMT>
-__device__ __forceinline__ float dot16(const uint8_t* vb, int u, const float* x, float sx) {
-  if constexpr (FMT == Q8_0) return dot16_q8_0(vb, u, x);
-  else if constexpr (FMT == Q4_K) return dot16_q4_k(vb, u, x, sx);
-  else if constexpr (FMT == Q6_K) return dot16_q6_k(vb, u, x);
-  else if constexpr (FMT == BF16) return dot16_bf16(vb, u, x);
-  else return dot16_f32(vb, u, x);
 }
 
 // Element get() with the reference's rounding order, no contraction

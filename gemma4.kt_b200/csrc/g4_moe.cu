@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <map>
 
 namespace g4 {
 
@@ -589,10 +590,17 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   ExpertFn fn = select_expert(type, gu, a.pr, nb);
   if (!fn) return -1;
   size_t smem = 64 + 4 * (2 * kMaxExperts + 8) + 128 + (size_t)a.nstages * a.stage_bytes;
-  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  int occ = 1;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, 32 * (NCW + 1), smem);
-  if (occ < 1) occ = 1;
+  // kernel attributes and occupancy are queried once per (kernel, smem)
+  static std::map<std::pair<ExpertFn, size_t>, int> occ_cache;
+  auto key = std::make_pair(fn, smem);
+  auto itc = occ_cache.find(key);
+  if (itc == occ_cache.end()) {
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int o = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, 32 * (NCW + 1), smem);
+    itc = occ_cache.emplace(key, o < 1 ? 1 : o).first;
+  }
+  int occ = itc->second;
   // Upper bound on items: every slot in its own chunk.
   long long max_items = (long long)std::min(T * K, E * ((T * K + nb - 1) / nb + 1)) * a.tiles_e;
   int grid = (int)std::min<long long>(max_items, (long long)c->dev.sms * occ);
