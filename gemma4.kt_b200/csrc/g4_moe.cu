@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <cmath>
 #include <map>
+#include <mutex>
 
 namespace g4 {
 
@@ -725,4 +726,195 @@ extern "C" int g4_moe_layer_host(g4_ctx* c, const g4_moe_weights* w, const float
   if (idx_h) cudaMemcpyAsync(idx_h, id, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st);
   if (prob_h) cudaMemcpyAsync(prob_h, pd, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st);
   return c->check_status(st);
+}
+
+// ============================================================================
+// Allocation-free MoE layer.
+//
+// Some hosts cannot let a library allocate device memory once they are
+// running: a JVM host that reserves all free HBM for its own pool at start-up
+// (a later cudaMalloc would fail), or a decode loop that must not pay for the
+// device-wide synchronisation a cudaMalloc/cudaFree can cause mid-step.  For
+// them g4_moe_layer_noalloc runs the same kernels as g4_moe_layer with its
+// work buffers in one fixed array of device memory that belongs to the
+// library image (every GPU that loads the library holds it until exit).
+// ============================================================================
+namespace g4 {
+
+static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[G4_MOE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoallocMaxDevices];  // device address of the array, per device
+
+struct FixedOcc {
+  ExpertFn fn;
+  size_t smem;
+  int occ;
+};
+FixedOcc g_noalloc_occ[64];  // kernel set-up done by the no-alloc path (fixed table, no heap)
+int g_noalloc_occ_n = 0;
+
+// Device address of the scratch array on the current device.  The first call
+// per device resolves it (cudaGetSymbolAddress); the symbol's host-side name is
+// only a stand-in and must never be passed to a kernel.
+int noalloc_scratch(g4_ctx* c, uint8_t** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  const int d = c->dev.device;
+  if (d < 0 || d >= kNoallocMaxDevices) {
+    c->set_err("g4_moe_layer_noalloc: device id %d out of range", d);
+    return G4_E_ARG;
+  }
+  if (!g_noalloc_ptr[d]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+    if (e != cudaSuccess || !p) return c->cuda_fail(e, "g4_moe_layer_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[d] = p;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_ptr[d]);
+  return 0;
+}
+
+int noalloc_occ(ExpertFn fn, size_t smem, int threads, int* occ) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  for (int i = 0; i < g_noalloc_occ_n; ++i)
+    if (g_noalloc_occ[i].fn == fn && g_noalloc_occ[i].smem == smem) {
+      *occ = g_noalloc_occ[i].occ;
+      return 0;
+    }
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -1;
+  int o = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, threads, smem) != cudaSuccess) return -1;
+  if (o < 1) o = 1;
+  if (g_noalloc_occ_n < 64) g_noalloc_occ[g_noalloc_occ_n++] = FixedOcc{fn, smem, o};
+  *occ = o;
+  return 0;
+}
+
+// Same work decomposition as launch_expert, with the kernel set-up cached in a
+// fixed table.
+int launch_expert_noalloc(g4_ctx* c, int type, bool gu, const uint8_t* w, const float* act, float* out,
+                          const MoeScratch& m, int E, int K, int dim, int ff, int T, cudaStream_t st) {
+  const int BS = block_size(type), TS = type_size(type);
+  const int NCW = 8;
+  ExpertArgs a{};
+  a.w = w;
+  a.act = act;
+  a.out = out;
+  a.offsets = m.offsets;
+  a.perm = m.perm;
+  a.status = c->status;
+  a.E = E;
+  a.n_used = K;
+  a.ff = ff;
+  if (gu) {
+    a.rows_e = 2 * ff;
+    a.cols = dim;
+    a.pr = 1;
+    if (dim % BS || dim % 16) return -1;
+    a.vb = dim / BS * TS;
+    if (a.vb % 2) return -1;
+    a.units = dim / 16;
+    a.tile_rows = NCW;
+    a.tiles_e = (ff + NCW - 1) / NCW;
+    a.region_bytes = (int)align_up((size_t)NCW * a.vb + 32, 128);
+    a.stage_bytes = 2 * a.region_bytes;
+    a.expert_elems = (long long)2 * ff * dim;
+  } else {
+    a.rows_e = dim;
+    a.cols = ff;
+    if (ff % 16) return -1;
+    int pr = ff % BS == 0 ? 1 : BS / gcd_i(ff % BS, BS);
+    if (pr != 1 && pr != 2 && pr != 4) return -1;
+    if (dim % pr) return -1;
+    a.pr = pr;
+    a.vb = pr * ff / BS * TS;
+    if (a.vb % 2) return -1;
+    a.units = pr * ff / 16;
+    a.tile_rows = NCW;
+    a.tiles_e = (dim / pr + NCW - 1) / NCW;
+    a.stage_bytes = (int)align_up((size_t)NCW * a.vb + 32, 128);
+    a.expert_elems = (long long)dim * ff;
+  }
+  if (a.expert_elems % BS) return -1;
+  a.nstages = 4;
+  int avg = (T * K + E - 1) / E;
+  int nb = avg >= 8 ? 8 : avg >= 4 ? 4 : avg >= 2 ? 2 : 1;
+  ExpertFn fn = select_expert(type, gu, a.pr, nb);
+  if (!fn) return -1;
+  size_t smem = 64 + 4 * (2 * kMaxExperts + 8) + 128 + (size_t)a.nstages * a.stage_bytes;
+  int occ = 1;
+  if (noalloc_occ(fn, smem, 32 * (NCW + 1), &occ)) return -2;
+  long long max_items = (long long)std::min(T * K, E * ((T * K + nb - 1) / nb + 1)) * a.tiles_e;
+  int grid = (int)std::min<long long>(max_items, (long long)c->dev.sms * occ);
+  if (grid < 1) grid = 1;
+  fn<<<grid, 32 * (NCW + 1), smem, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+}  // namespace
+
+}  // namespace g4
+
+extern "C" int g4_moe_layer_noalloc(g4_ctx* c, const g4_moe_weights* w, const float* x, float* out, int T,
+                                    int32_t* topk_idx, float* topk_prob, void* stream) {
+  if (!c) return G4_E_ARG;
+  if (!w || !x || !out || T < 0) {
+    c->set_err("g4_moe_layer_noalloc: bad argument");
+    return G4_E_ARG;
+  }
+  const int dim = w->dim, E = w->n_expert, K = w->n_used, ff = w->expert_ff;
+  if (dim <= 0 || E < 1 || E > kMaxExperts || K < 1 || K > E || K > kMaxUsed || ff <= 0 || dim % 4) {
+    c->set_err("g4_moe_layer_noalloc: unsupported geometry dim=%d experts=%d used=%d ff=%d", dim, E, K, ff);
+    return G4_E_ARG;
+  }
+  if (!tensor_ok(w->gate_inp, G4_TYPE_F32, (uint64_t)dim * E) ||
+      !tensor_ok(w->gate_inp_scale, G4_TYPE_F32, dim) || !tensor_ok(w->down_exps_scale, G4_TYPE_F32, E) ||
+      !tensor_ok(w->pre_ffw_norm_2, G4_TYPE_F32, dim) ||
+      (w->post_ffw_norm_2 && !tensor_ok(w->post_ffw_norm_2, G4_TYPE_F32, dim)) ||
+      !tensor_ok(w->gate_up_exps, -1, (uint64_t)dim * 2 * ff * E) ||
+      !tensor_ok(w->down_exps, -1, (uint64_t)ff * dim * E)) {
+    c->set_err("g4_moe_layer_noalloc: a weight tensor is missing or has the wrong type/size");
+    return G4_E_ARG;
+  }
+  if (T == 0) return 0;
+  const size_t need = moe_scratch_bytes(T, dim, E, K, ff);
+  if (need > (size_t)G4_MOE_NOALLOC_SCRATCH_BYTES) {
+    c->set_err("g4_moe_layer_noalloc: %d tokens need %zu bytes of work memory, more than the fixed %u; "
+               "split the batch or use g4_moe_layer",
+               T, need, (unsigned)G4_MOE_NOALLOC_SCRATCH_BYTES);
+    return G4_E_ARG;
+  }
+  if (int r = c->bind()) return r;
+  uint8_t* base = nullptr;
+  if (int r = noalloc_scratch(c, &base)) return r;
+  cudaStream_t st = (cudaStream_t)stream;
+  // Every work buffer is fully written before it is read, so nothing has to
+  // be cleared between calls.
+  MoeScratch m = carve(base, T, dim, E, K, ff);
+  moe_prep_kernel<<<T, 256, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, (const float*)w->gate_inp_scale->d,
+                                     m.moe_in, m.xr, dim, w->eps);
+  dim3 rg((E + 7) / 8, (T + 7) / 8);
+  moe_router_kernel<8><<<rg, 256, 0, st>>>((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E);
+  moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(m.logits, T, E, K, m.idx, m.prob);
+  moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, T * K, E, m.offsets, m.perm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_noalloc launch");
+  int r = launch_expert_noalloc(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m,
+                                E, K, dim, ff, T, st);
+  if (r == 0)
+    r = launch_expert_noalloc(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K, dim,
+                              ff, T, st);
+  if (r == -1) {
+    c->set_err("g4_moe_layer_noalloc: expert tensor layout not supported by the grouped kernels");
+    return G4_E_ARG;
+  }
+  if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer_noalloc expert launch");
+  moe_combine_kernel<<<T, 256, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
+                                        w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr, out, dim,
+                                        K, w->eps);
+  if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
+  if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : c->cuda_fail(e, "g4_moe_layer_noalloc");
 }

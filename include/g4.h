@@ -143,6 +143,27 @@ int g4_moe_layer(g4_ctx *ctx, const g4_moe_weights *w, const float *x_dev, float
 int g4_moe_layer_host(g4_ctx *ctx, const g4_moe_weights *w, const float *x_host, float *out_host,
                       int n_tokens, int32_t *topk_idx_host, float *topk_prob_host);
 
+/* Allocation-free variant of g4_moe_layer (no counterpart in the reference).
+ * For hosts that cannot let the library allocate device memory while they run:
+ * e.g. a host that hands all free HBM to its own pool at start-up, or a decode
+ * loop that must not stall on the device-wide synchronisation a cudaMalloc or
+ * cudaFree can cause.  Same kernels and results as g4_moe_layer; the work
+ * buffers live in one fixed array of G4_MOE_NOALLOC_SCRATCH_BYTES bytes that
+ * the library image reserves on every GPU that loads it, held until exit.
+ *  - A call needs 4*n_tokens*(2*dim + n_expert + 3*n_used + n_used*(ff + dim))
+ *    bytes (each buffer rounded up to 256 bytes; about 135 KB per token for
+ *    dim 2816, 128 experts, top-8, ff 704, so up to 61 tokens).  Larger
+ *    batches are rejected with G4_E_ARG and a message; split them.
+ *  - The first call on a device resolves the array's device address; make it
+ *    before any stream capture.
+ *  - All calls on a device share the array: calls that can overlap on the GPU
+ *    (different streams, or several contexts on one device) race.  Nothing in
+ *    it needs to start at zero: each call writes every buffer before reading.
+ *  - Never calls cudaMalloc, cudaFree or any allocating library routine. */
+#define G4_MOE_NOALLOC_SCRATCH_BYTES (8u << 20)
+int g4_moe_layer_noalloc(g4_ctx *ctx, const g4_moe_weights *w, const float *x_dev, float *out_dev,
+                         int n_tokens, int32_t *topk_idx_dev, float *topk_prob_dev, void *stream);
+
 /* Router top-k alone on given logits (Llama.kt:273-293 + softmaxInPlace,
  * MutableFloatTensor.kt:54-59): probs_dev/idx_dev [n_tokens, k]. */
 int g4_moe_topk(g4_ctx *ctx, const float *logits_dev, int n_tokens, int n_expert, int k,
