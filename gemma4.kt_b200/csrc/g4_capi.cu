@@ -264,9 +264,11 @@ int g4_matmul(g4_ctx* c, const g4_tensor* w, int64_t off, const float* x, float*
     if (!xal) p.fast = 0;
     itp = c->gemv_plans.emplace(key, p).first;
   }
-  if (launch_gemv(itp->second, (const uint8_t*)w->d, x, y, c->status, st)) {
-    cudaError_t e = cudaGetLastError();
-    return c->cuda_fail(e, "g4_matmul launch");
+  if (int e = launch_gemv(itp->second, (const uint8_t*)w->d, x, y, c->status, st)) {
+    const GemvPlan& p = itp->second;
+    c->set_err("g4_matmul launch (type %d, %dx%d, warps %d, smem %zu, grid %d): %s", p.type, dim0, dim1, p.warps,
+               p.smem, p.grid, cudaGetErrorString((cudaError_t)e));
+    return G4_E_CUDA;
   }
   return 0;
 }

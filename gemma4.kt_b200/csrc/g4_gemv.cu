@@ -37,77 +37,77 @@ struct GemvArgs {
   unsigned* status;  // device error word
 };
 
-// Which (row group, chunk) the i-th stage of this warp holds.
-struct Seq {
-  int g, c;
-};
-
-__device__ __forceinline__ Seq seq_at(const GemvPlan& p, int i, int warp, int W) {
-  if (p.split == 1) {
-    const int gw = blockIdx.x * W + warp, GW = gridDim.x * W;
-    return Seq{gw + (i / p.nchunks) * GW, i % p.nchunks};
-  }
-  return Seq{(int)blockIdx.x, warp + i * W};
-}
-
-__device__ __forceinline__ bool seq_valid(const GemvPlan& p, Seq s) { return s.g < p.ngroups && s.c < p.nchunks; }
-
-template <int FMT, int PR, int RL>
+// LPR lanes share a row: a warp covers 32/LPR rows; lane l owns row slot
+// l % (32/LPR) and, within each chunk, the blocks b with b % LPR == l / (32/LPR).
+template <int FMT, int PR, int LPR>
 __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const GemvPlan& p = a.p;
   constexpr int BS = block_size(FMT), TS = type_size(FMT);
-  constexpr int ROWS = 32 * RL;
+  constexpr int RPW = 32 / LPR;  // rows per warp
   float* xs = reinterpret_cast<float*>(smem + p.xs_off);
-  float* xsum16 = reinterpret_cast<float*>(smem + p.xsum_off);
+  float* xsum = reinterpret_cast<float*>(smem + p.xsum_off);  // per 16 columns, then per 32 columns
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint8_t* ring = smem + p.ring_off;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, W = blockDim.x >> 5;
+  const int rs = lane % RPW, sl = lane / RPW;
   const int NS = p.ns;
-  const size_t stage_bytes = (size_t)ROWS * p.pitch;
+  const size_t stage_bytes = (size_t)RPW * p.pitch;
   uint64_t* mybars = bars + warp * NS;
   uint8_t* myring = ring + (size_t)warp * NS * stage_bytes;
+  const int n16 = p.cols / 16;
+  float* xsum16 = xsum;
+  float* xsum32 = xsum + n16;
 
   if (threadIdx.x < W * NS) mbar_init(&bars[threadIdx.x], 1);
   if (threadIdx.x == 0) fence_barrier_init();
-  // x -> shared memory, plus the sum of every 16 consecutive columns
+  // x -> shared memory, plus the sum of every 16 and every 32 consecutive columns
   for (int i = threadIdx.x * 4; i < p.cols; i += blockDim.x * 4)
     *reinterpret_cast<float4*>(xs + i) = __ldg(reinterpret_cast<const float4*>(a.x + i));
   __syncthreads();
-  for (int k = threadIdx.x; k < p.cols / 16; k += blockDim.x) {
+  for (int k = threadIdx.x; k < n16; k += blockDim.x) {
     float t = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) t += xs[16 * k + i];
     xsum16[k] = t;
   }
   __syncthreads();
+  for (int k = threadIdx.x; k < n16 / 2; k += blockDim.x) xsum32[k] = xsum16[2 * k] + xsum16[2 * k + 1];
+  __syncthreads();
 
   const long long blk0 = p.off / BS;  // first block of the matrix
-  const int bpv = p.bpv;
-
-  // Start of virtual row v, chunk c (bytes from the tensor base) and its length.
-  auto seg = [&](long long v, int c, long long& start, int& len) {
-    const int b = c * p.cb;
-    const int nb = min(p.cb, bpv - b);
-    start = (blk0 + v * bpv + b) * TS;
-    len = nb * TS;
+  const int bpv = p.bpv, cb = p.cb, nchunks = p.nchunks;
+  const long long vrow_bytes = (long long)bpv * TS;
+  const long long chunk_bytes = (long long)cb * TS;
+  // Stage sequence of this warp, advanced incrementally: (group, chunk).
+  // split == 1: groups gw, gw + GW, ... each with chunks 0..nchunks-1;
+  // split  > 1: the CTA's one group, chunks warp, warp + W, ...
+  const int gstep = gridDim.x * W;
+  const int g_first = p.split == 1 ? (int)blockIdx.x * W + warp : (int)blockIdx.x;
+  const int c_first = p.split == 1 ? 0 : warp;
+  const int c_step = p.split == 1 ? 1 : W;
+  auto advance = [&](int& g, int& c) {
+    c += c_step;
+    if (p.split == 1 && c == nchunks) {
+      c = 0;
+      g += gstep;
+    }
   };
-  // All lanes copy their own rows' segments of stage (g, c) into slot `slot`.
-  auto issue = [&](Seq sq, int slot) {
+  auto valid = [&](int g, int c) { return g < p.ngroups && c < nchunks; };
+  // byte offset of this lane's row in group g (only lanes with a row use it)
+  auto row_start = [&](int g) { return (blk0 * TS) + ((long long)g * RPW + rs) * vrow_bytes; };
+  auto row_ok = [&](int g) { return (long long)g * RPW + rs < p.nvrows; };
+
+  // Lanes of sub-slot 0 copy their rows' segments of stage (g, c) into `slot`.
+  auto issue = [&](int g, int c, long long rstart, int slot) {
     uint64_t* bar = &mybars[slot];
-    uint8_t* dst = myring + (size_t)slot * stage_bytes;
     uint32_t mine = 0;
-#pragma unroll
-    for (int j = 0; j < RL; ++j) {
-      const long long v = (long long)sq.g * ROWS + j * 32 + lane;
-      if (v < p.nvrows) {
-        long long start;
-        int len;
-        seg(v, sq.c, start, len);
-        const long long a0 = start & ~15ll, a1 = (start + len + 15) & ~15ll;
-        bulk_g2s(dst + (size_t)(j * 32 + lane) * p.pitch, a.w + a0, (uint32_t)(a1 - a0), bar);
-        mine += (uint32_t)(a1 - a0);
-      }
+    if (sl == 0 && row_ok(g)) {
+      const long long start = rstart + c * chunk_bytes;
+      const long long len = min(chunk_bytes, vrow_bytes - c * chunk_bytes);
+      const long long a0 = start & ~15ll, a1 = (start + len + 15) & ~15ll;
+      bulk_g2s(myring + (size_t)slot * stage_bytes + (size_t)rs * p.pitch, a.w + a0, (uint32_t)(a1 - a0), bar);
+      mine = (uint32_t)(a1 - a0);
     }
     const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
     if (lane == 0) mbar_arrive_expect_tx(bar, total);
@@ -115,22 +115,23 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
 
   bool ok = true;
   int issued = 0, consumed = 0;
-  for (; issued < NS; ++issued) {
-    Seq sq = seq_at(p, issued, warp, W);
-    if (!seq_valid(p, sq)) break;
-    issue(sq, issued);
+  int gi = g_first, ci = c_first;  // issue pointer
+  long long rs_i = row_start(gi);
+  for (; issued < NS && valid(gi, ci); ++issued) {
+    issue(gi, ci, rs_i, issued);
+    const int g0 = gi;
+    advance(gi, ci);
+    if (gi != g0) rs_i = row_start(gi);
   }
 
-  float acc[RL][PR];
+  float acc[PR];
 #pragma unroll
-  for (int j = 0; j < RL; ++j)
-#pragma unroll
-    for (int r = 0; r < PR; ++r) acc[j][r] = 0.f;
+  for (int r = 0; r < PR; ++r) acc[r] = 0.f;
 
-  int cur_g = -1;
-  for (int i = 0;; ++i) {
-    Seq sq = seq_at(p, i, warp, W);
-    if (!seq_valid(p, sq)) break;
+  int g = g_first, c = c_first;  // consume pointer
+  long long rs_c = row_start(g);
+  bool have_row = row_ok(g);
+  for (int i = 0; valid(g, c); ++i) {
     const int slot = i % NS;
     if (!mbar_wait_bounded(&mybars[slot], (i / NS) & 1)) {
       record_error(a.status, ERR_TIMEOUT_FULL);
@@ -138,78 +139,55 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
       consumed = i;
       break;
     }
-    if (p.split == 1 && sq.g != cur_g) {
-      cur_g = sq.g;
-#pragma unroll
-      for (int j = 0; j < RL; ++j)
-#pragma unroll
-        for (int r = 0; r < PR; ++r) acc[j][r] = 0.f;
-    }
-    // ---- compute on this lane's row segments
-    const uint8_t* base[RL];
-#pragma unroll
-    for (int j = 0; j < RL; ++j) {
-      const long long v = (long long)sq.g * ROWS + j * 32 + lane;
-      long long start = 0;
-      int len = 0;
-      if (v < p.nvrows) seg(v, sq.c, start, len);
-      base[j] = myring + (size_t)slot * stage_bytes + (size_t)(j * 32 + lane) * p.pitch + (start & 15);
-    }
-    const int b0 = sq.c * p.cb;
-    const int nb = min(p.cb, bpv - b0);
-    if constexpr (FMT == Q4_K || FMT == Q6_K) {
-      for (int b = 0; b < nb; ++b) {
-        const uint8_t* blk[RL];
-#pragma unroll
-        for (int j = 0; j < RL; ++j) blk[j] = base[j] + b * TS;
-        if constexpr (FMT == Q4_K) block_q4k<RL, PR>(blk, (b0 + b) * BS, p.cols, xs, xsum16, acc);
-        else block_q6k<RL, PR>(blk, (b0 + b) * BS, p.cols, xs, xsum16, acc);
+    // ---- compute on this lane's share of its row segment
+    if (have_row) {
+      const long long start = rs_c + c * chunk_bytes;
+      const int nb = (int)(min(chunk_bytes, vrow_bytes - c * chunk_bytes) / TS);
+      const uint8_t* base = myring + (size_t)slot * stage_bytes + (size_t)rs * p.pitch + (start & 15);
+      const int e0 = c * cb * BS;  // first element of the chunk within the virtual row
+      if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) {
+        for (int b = sl; b < nb; b += LPR) {
+          const uint8_t* blk = base + b * TS;
+          if constexpr (FMT == Q4_K) block_q4k<PR>(blk, e0 + b * BS, p.cols, xs, xsum32, acc);
+          else if constexpr (FMT == Q6_K) block_q6k<PR>(blk, e0 + b * BS, p.cols, xs, xsum16, acc);
+          else block_q8_0(blk, e0 + b * BS, xs, acc[0]);
+        }
+      } else {
+        // BF16 / F32: `blocks` are elements; 16-byte loads of 8 or 4 of them
+        constexpr int EPL = 16 / TS;
+        float2 s2 = f2(0.f, 0.f);
+        for (int e = sl * EPL; e < nb; e += LPR * EPL) {
+          if constexpr (FMT == BF16) unit16_bf16(base + e * TS, e0 + e, xs, s2);
+          else unit16_f32(base + e * TS, e0 + e, xs, s2);
+        }
+        acc[0] += s2.x + s2.y;
       }
-    } else if constexpr (FMT == Q8_0) {
-      for (int b = 0; b < nb; ++b) {
-        const uint8_t* blk[RL];
-#pragma unroll
-        for (int j = 0; j < RL; ++j) blk[j] = base[j] + b * TS;
-        float (&acc1)[RL][1] = *reinterpret_cast<float(*)[RL][1]>(&acc);
-        block_q8_0<RL>(blk, (b0 + b) * BS, xs, acc1);
-      }
-    } else {
-      // BF16 / F32: "blocks" are single elements; 16-byte loads
-      constexpr int EPL = 16 / TS;  // elements per 16-byte load
-      float2 s2[RL];
-#pragma unroll
-      for (int j = 0; j < RL; ++j) s2[j] = f2(0.f, 0.f);
-      for (int e = 0; e < nb; e += EPL) {
-        const uint8_t* pp[RL];
-#pragma unroll
-        for (int j = 0; j < RL; ++j) pp[j] = base[j] + e * TS;
-        if constexpr (FMT == BF16) chunk16_bf16<RL>(pp, b0 + e, xs, s2);
-        else chunk16_f32<RL>(pp, b0 + e, xs, s2);
-      }
-#pragma unroll
-      for (int j = 0; j < RL; ++j) acc[j][0] += s2[j].x + s2[j].y;
     }
-    // ---- refill this slot with stage i + NS (same warp: no other reader)
+    // ---- refill this slot with the stage NS ahead (same warp: no other reader)
     __syncwarp();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    {
-      Seq nx = seq_at(p, i + NS, warp, W);
-      if (seq_valid(p, nx)) {
-        issue(nx, slot);
-        ++issued;
-      }
+    if (valid(gi, ci)) {
+      issue(gi, ci, rs_i, slot);
+      ++issued;
+      const int g0 = gi;
+      advance(gi, ci);
+      if (gi != g0) rs_i = row_start(gi);
     }
-    // ---- row group finished: write results
-    if (p.split == 1) {
-      if (sq.c == p.nchunks - 1) {
+    // ---- row group finished: combine the lanes of each row and write
+    const int gprev = g;
+    advance(g, c);
+    if (p.split == 1 && g != gprev) {
+      const long long v = (long long)gprev * RPW + rs;
 #pragma unroll
-        for (int j = 0; j < RL; ++j) {
-          const long long v = (long long)sq.g * ROWS + j * 32 + lane;
-          if (v < p.nvrows)
+      for (int r = 0; r < PR; ++r) {
+        float t = acc[r];
 #pragma unroll
-            for (int r = 0; r < PR; ++r) a.y[v * PR + r] = acc[j][r];
-        }
+        for (int o = RPW; o < 32; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (sl == 0 && have_row) a.y[v * PR + r] = t;
+        acc[r] = 0.f;
       }
+      rs_c = row_start(g);
+      have_row = row_ok(g);
     }
   }
 
@@ -217,14 +195,17 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
     // CTA = one row group; warps hold partial sums over disjoint chunks.
     float* red = reinterpret_cast<float*>(smem + p.red_off);
 #pragma unroll
-    for (int j = 0; j < RL; ++j)
+    for (int r = 0; r < PR; ++r) {
+      float t = acc[r];
 #pragma unroll
-      for (int r = 0; r < PR; ++r) red[((size_t)warp * ROWS + j * 32 + lane) * PR + r] = acc[j][r];
+      for (int o = RPW; o < 32; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (sl == 0) red[((size_t)warp * RPW + rs) * PR + r] = t;
+    }
     __syncthreads();
-    for (int t = threadIdx.x; t < ROWS * PR; t += blockDim.x) {
-      const long long v = (long long)blockIdx.x * ROWS + t / PR;
+    for (int t = threadIdx.x; t < RPW * PR; t += blockDim.x) {
+      const long long v = (long long)blockIdx.x * RPW + t / PR;
       float sum = 0.f;
-      for (int w = 0; w < W; ++w) sum += red[(size_t)w * ROWS * PR + t];
+      for (int w = 0; w < W; ++w) sum += red[(size_t)w * RPW * PR + t];
       if (v < p.nvrows) a.y[v * PR + (t % PR)] = sum;
     }
   }
@@ -271,27 +252,28 @@ static int gcd_i(int a, int b) {
 using KernelFn = void (*)(const GemvArgs);
 
 template <int FMT>
-static KernelFn pick_kernel(int pr, int rl) {
-  if (pr == 1) return rl == 2 ? gemv_rows_kernel<FMT, 1, 2> : gemv_rows_kernel<FMT, 1, 1>;
+static KernelFn pick_kernel(int pr, int lpr) {
+  if (pr == 1) return lpr == 4 ? gemv_rows_kernel<FMT, 1, 4> : lpr == 2 ? gemv_rows_kernel<FMT, 1, 2>
+                                                                        : gemv_rows_kernel<FMT, 1, 1>;
   if constexpr (FMT == Q4_K || FMT == Q6_K) {
-    if (pr == 2 && rl == 1) return gemv_rows_kernel<FMT, 2, 1>;
-    if (pr == 4 && rl == 1) return gemv_rows_kernel<FMT, 4, 1>;
+    if (pr == 2) return lpr == 2 ? gemv_rows_kernel<FMT, 2, 2> : gemv_rows_kernel<FMT, 2, 1>;
+    if (pr == 4) return lpr == 2 ? gemv_rows_kernel<FMT, 4, 2> : gemv_rows_kernel<FMT, 4, 1>;
   }
   return nullptr;
 }
 
-static KernelFn kernel_for(int type, int pr, int rl) {
+static KernelFn kernel_for(int type, int pr, int lpr) {
   switch (type) {
-    case Q8_0: return pick_kernel<Q8_0>(pr, rl);
-    case Q4_K: return pick_kernel<Q4_K>(pr, rl);
-    case Q6_K: return pick_kernel<Q6_K>(pr, rl);
-    case BF16: return pick_kernel<BF16>(pr, rl);
-    case F32: return pick_kernel<F32>(pr, rl);
+    case Q8_0: return pick_kernel<Q8_0>(pr, lpr);
+    case Q4_K: return pick_kernel<Q4_K>(pr, lpr);
+    case Q6_K: return pick_kernel<Q6_K>(pr, lpr);
+    case BF16: return pick_kernel<BF16>(pr, lpr);
+    case F32: return pick_kernel<F32>(pr, lpr);
     default: return nullptr;
   }
 }
 
-// Overridable for tuning sweeps: G4_GEMV_CHUNK_BYTES, G4_GEMV_WARPS, G4_GEMV_STAGES, G4_GEMV_RL.
+// Overridable for tuning sweeps: G4_GEMV_CHUNK_BYTES, G4_GEMV_WARPS, G4_GEMV_STAGES, G4_GEMV_LPR.
 static int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return v && *v ? atoi(v) : dflt;
@@ -312,7 +294,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.fast = 0;
   const int BS = block_size(type), TS = type_size(type);
   if (TS == 0 || type == F16 || rows <= 0 || cols <= 0) return p;
-  if (cols % 16 != 0 || off % BS != 0) return p;
+  if (cols % 32 != 0 || off % BS != 0) return p;
   if ((type == BF16 || type == F32) && ((off * TS) % 16) != 0) return p;
   int pr = 1;
   if (cols % BS != 0) {
@@ -322,26 +304,29 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   }
   if (rows % pr != 0) return p;
   const int xbytes = ((cols * 4 + 127) / 128) * 128;
-  const int xsbytes = ((cols / 16 * 4 + 127) / 128) * 128;
+  const int xsbytes = (((cols / 16 + cols / 32) * 4 + 127) / 128) * 128;
   if (xbytes > 96 * 1024) return p;
   p.pr = pr;
   p.nvrows = rows / pr;
   p.bpv = (int)((long long)pr * cols / BS);
-  p.rl = env_int("G4_GEMV_RL", 1) == 2 && pr == 1 ? 2 : 1;
-  const int rows_per_group = 32 * p.rl;
+  // defaults from a sweep of 262144 x 1536 on B200 (lanes per row, bytes per copy)
+  const int lpr_default = type == Q4_K ? 2 : 4;
+  p.lpr = env_int("G4_GEMV_LPR", lpr_default);
+  if (p.lpr != 1 && p.lpr != 2 && p.lpr != 4) p.lpr = 1;
+  if (pr > 1 && p.lpr > 2) p.lpr = 2;
+  int rows_per_group = 32 / p.lpr;
   p.ngroups = (p.nvrows + rows_per_group - 1) / rows_per_group;
 
-  // chunk: about `target` bytes of one row per bulk copy, divisor of bpv if possible
-  const int target = env_int("G4_GEMV_CHUNK_BYTES", 288);
-  int cb = std::max(1, std::min(p.bpv, target / TS));
-  if (type == BF16) cb = std::max(8, cb / 8 * 8);
-  if (type == F32) cb = std::max(4, cb / 4 * 4);
+  // chunk: about `target` bytes of one row per bulk copy (copies below ~256 B
+  // cap the copy engine well under HBM speed), at least one block per lane
+  const int target = env_int("G4_GEMV_CHUNK_BYTES", type == Q4_K ? 288 : type == Q6_K ? 840 : 576);
+  const int unit = (type == BF16 ? 8 : type == F32 ? 4 : 1) * p.lpr;  // elements (blocks) per lane step
+  int cb = std::max(unit, std::min(p.bpv, target / TS) / unit * unit);
   const bool small = p.ngroups < 2 * dev.sms;
   if (small) {
     // few row groups: split each row over up to 8 warps of one CTA
-    int want = std::max(1, (p.bpv + 7) / 8);
-    if (type == BF16) want = std::max(8, (want + 7) / 8 * 8);
-    if (type == F32) want = std::max(4, (want + 3) / 4 * 4);
+    int want = std::max(unit, (p.bpv + 7) / 8);
+    want = (want + unit - 1) / unit * unit;
     cb = std::min(cb, want);
   }
   p.cb = cb;
@@ -356,8 +341,8 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
     p.ns = 2;
   } else {
     p.split = 1;
-    p.warps = env_int("G4_GEMV_WARPS", 8);
-    p.ns = env_int("G4_GEMV_STAGES", 3);
+    p.warps = env_int("G4_GEMV_WARPS", 16);
+    p.ns = env_int("G4_GEMV_STAGES", 2);
   }
   for (;;) {
     size_t red = p.split > 1 ? (size_t)p.warps * rows_per_group * pr * 4 : 0;
@@ -365,9 +350,9 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
     if (need <= budget) break;
     if (p.ns > 2) --p.ns;
     else if (p.split == 1 && p.warps > 2) p.warps /= 2;
-    else if (p.split > 1 && p.cb > 1 && type != BF16 && type != F32) {
+    else if (p.split > 1 && p.cb > unit && type != BF16 && type != F32) {
       // narrower chunks, more of them: keeps the CTA's rings within shared memory
-      p.cb = std::max(1, p.cb / 2);
+      p.cb = std::max(unit, p.cb / 2 / unit * unit);
       p.nchunks = (p.bpv + p.cb - 1) / p.cb;
       p.pitch = pitch_for(p.cb * TS + 32);
       stage = (size_t)rows_per_group * p.pitch;
@@ -384,31 +369,37 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.ring_off = p.bar_off + 128 * ((p.warps * p.ns * 8 + 127) / 128);
   p.red_off = (int)(p.ring_off + (size_t)p.warps * p.ns * stage);
   p.smem = (size_t)p.red_off + (p.split > 1 ? (size_t)p.warps * rows_per_group * pr * 4 : 0);
-  KernelFn k = kernel_for(type, pr, p.rl);
+  KernelFn k = kernel_for(type, pr, p.lpr);
   if (!k) return p;
   int occ = 0;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, 32 * p.warps, p.smem) != cudaSuccess || occ < 1) {
+  // The attribute belongs to the kernel, not to this plan: always allow the
+  // device maximum so plans of other shapes stay launchable.
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)budget) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, 32 * p.warps, p.smem) != cudaSuccess || occ < 1) {
     cudaGetLastError();
     return p;
   }
   if (p.split > 1) p.grid = p.ngroups;
   else p.grid = (int)std::min<long long>((p.ngroups + p.warps - 1) / p.warps, (long long)dev.sms * occ);
   p.fast = 1;
+  if (env_int("G4_DEBUG_PLAN", 0))
+    fprintf(stderr, "g4 gemv plan: type %d %dx%d pr %d lpr %d cb %d pitch %d warps %d ns %d split %d grid %d smem %zu occ %d\n",
+            type, rows, cols, pr, p.lpr, p.cb, p.pitch, p.warps, p.ns, p.split, p.grid, p.smem, occ);
   return p;
 }
 
 int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, unsigned* status,
                 cudaStream_t st) {
+  cudaGetLastError();  // launch errors below must not be confused with stale ones
   if (p.fast) {
     GemvArgs a{p, w, x, y, status};
-    KernelFn k = kernel_for(p.type, p.pr, p.rl);
+    KernelFn k = kernel_for(p.type, p.pr, p.lpr);
     k<<<p.grid, 32 * p.warps, p.smem, st>>>(a);
   } else {
     int wpb = 8;
     gemv_generic_kernel<<<(p.rows + wpb - 1) / wpb, 32 * wpb, 0, st>>>(p.type, w, p.off, p.rows, p.cols, x, y);
   }
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return (int)cudaGetLastError();
 }
 
 int launch_dequant(int type, const uint8_t* w, long long off, long long n, float* out, cudaStream_t st) {

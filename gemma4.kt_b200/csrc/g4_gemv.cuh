@@ -16,11 +16,11 @@ struct GemvPlan {
   int cb;            // blocks per chunk (one bulk copy per row and chunk)
   int nchunks;       // chunks per virtual row
   int pitch;         // bytes per row slot in a stage (16 * odd: conflict-free)
-  int rl;            // virtual rows per lane
+  int lpr;           // lanes sharing one row (1, 2 or 4)
   int ns;            // stages per warp
   int warps;         // warps per CTA
   int split;         // 1: persistent, each warp owns whole row groups; >1: CTA per group
-  int ngroups;       // row groups of 32*rl virtual rows
+  int ngroups;       // row groups of 32/lpr virtual rows
   int grid;
   int xs_off, xsum_off, bar_off, ring_off, red_off;  // shared-memory carve-up
   size_t smem;

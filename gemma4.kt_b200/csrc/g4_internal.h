@@ -16,6 +16,7 @@ struct GemvPlan;
 GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols);
 // Launch with a plan from plan_gemv (the caller caches plans: planning queries
 // occupancy and sets kernel attributes, which costs microseconds of host time).
+// Returns the cudaError_t of the launch.
 int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, unsigned* status,
                 cudaStream_t st);
 int launch_dequant(int type, const uint8_t* w, long long off, long long n, float* out, cudaStream_t st);

@@ -596,7 +596,8 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   auto key = std::make_pair(fn, smem);
   auto itc = occ_cache.find(key);
   if (itc == occ_cache.end()) {
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // per-kernel attribute: allow the device maximum, not just this launch's size
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->dev.smem_optin);
     int o = 1;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, 32 * (NCW + 1), smem);
     itc = occ_cache.emplace(key, o < 1 ? 1 : o).first;
@@ -783,7 +784,11 @@ int noalloc_occ(ExpertFn fn, size_t smem, int threads, int* occ) {
       *occ = g_noalloc_occ[i].occ;
       return 0;
     }
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -1;
+  int dev = 0, optin = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return -1;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess) return -1;
   int o = 1;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, threads, smem) != cudaSuccess) return -1;
   if (o < 1) o = 1;
