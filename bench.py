@@ -238,15 +238,52 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize()
     ctx.sync(sp)
 
-    # instrumented pass: CUDA events around every launch (on the launching
-    # stream) give each kernel's average duration for the roofline
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in cases]
-          for _ in range(args.steps)]
-    for s_ in range(args.steps):
-        step(ev[s_])
-    torch.cuda.synchronize()
-    per_case = np.array([np.mean([ev[s_][i][0].elapsed_time(ev[s_][i][1]) for s_ in range(args.steps)])
-                         for i in range(len(cases))])
+    # Per-kernel device time: each case's launch captured 10x in a CUDA graph
+    # and replayed, so host launch gaps do not count (events on the launching
+    # stream).  This feeds the roofline of the dominant kernel.
+    per_case = np.zeros(len(cases))
+    if world == 1:
+        for i, c in enumerate(cases):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                g.capture_begin()
+                for _ in range(10):
+                    rc = L.g4_matmul(ctx.handle, c["w"].handle, 0, C.c_void_p(c["xd"].data_ptr()),
+                                     C.c_void_p(c["yd"].data_ptr()), c["rows"], c["cols"], C.c_void_p(sp))
+                    if rc:
+                        raise RuntimeError(ctx.last_error())
+                g.capture_end()
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 5
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            per_case[i] = e0.elapsed_time(e1) / (10 * reps)
+            del g
+    else:
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in cases]
+              for _ in range(args.steps)]
+        for s_ in range(args.steps):
+            step(ev[s_])
+        torch.cuda.synchronize()
+        per_case = np.array([np.mean([ev[s_][i][0].elapsed_time(ev[s_][i][1]) for s_ in range(args.steps)])
+                             for i in range(len(cases))])
+
+    # The step (all 16 launches) as one CUDA graph at N=1: the GPU sees the same
+    # kernels back to back without Python launch gaps.
+    step_graph = None
+    if world == 1:
+        step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            step_graph.capture_begin()
+            step()
+            step_graph.capture_end()
+        step_graph.replay()
+        torch.cuda.synchronize()
 
     # headline: exactly K steps, barrier + synchronize on both sides
     barrier()
@@ -254,13 +291,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0e.record(stream)
     for _ in range(args.steps):
-        step()
+        if step_graph is not None:
+            step_graph.replay()
+        else:
+            step()
     t1e.record(stream)
     torch.cuda.synchronize()
     barrier()
     clk.__exit__(None, None, None)
     ms = t0e.elapsed_time(t1e) / args.steps
     ctx.sync(sp)
+    del step_graph
     if world > 1:
         import torch.distributed as dist
 
@@ -333,7 +374,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                          "traffic": None},
             "breakdown": breakdown,
             "clocks": clk.summary(),
-            "gpu_launches": len(cases) * args.steps * (2 if world > 1 else 1),
+            "gpu_launches": len(cases) * args.steps * (1 if world == 1 else 2),
+            "timing": "headline: K replays of a CUDA graph of the 16 launches (N=1); breakdown: per-case graphs of 10 launches",
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
@@ -355,20 +397,32 @@ def bench_moe(g4, ctx, torch, dev):
     for T in (1, 16, 256, 4096):
         x = torch.from_numpy(d.tokens(T)).to(dev)
         out = torch.empty((T, d.dim), dtype=torch.float32, device=dev)
-        for _ in range(3):
-            layer.forward(x, out, T)
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                layer.forward(x, out, T, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        # one layer call captured as a CUDA graph (its launches back to back)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            g.capture_begin()
+            layer.forward(x, out, T, stream=stream.cuda_stream)
+            g.capture_end()
+        g.replay()
         torch.cuda.synchronize()
         reps = 20 if T <= 256 else 5
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
+        a.record(stream)
         for _ in range(reps):
-            layer.forward(x, out, T)
-        b.record()
+            g.replay()
+        b.record(stream)
         torch.cuda.synchronize()
         us = a.elapsed_time(b) * 1e3 / reps
+        del g
         res[f"T{T}"] = {"us_per_layer": round(us, 2), "us_per_token": round(us / T, 3)}
     ctx.sync()
     return {"metric": "MoE layer us/token", "config": "hidden 2816, 128 experts top-8, ff 704, Q4_K, seed 2",
+            "timing": "CUDA graph of one g4_moe_layer call, replayed",
             **res}
 
 

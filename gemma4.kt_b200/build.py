@@ -30,7 +30,7 @@ NVCC_FLAGS = ARCH + [
 ]
 
 CU_SOURCES = ["g4_capi.cu", "g4_gemv.cu", "g4_moe.cu"]
-CU_HEADERS = ["g4_common.cuh", "g4_gemv.cuh", "g4_gemv_rows.cuh", "g4_internal.h", "g4_ctx.h", "g4_moe.cuh"]
+CU_HEADERS = ["g4_common.cuh", "g4_gemv.cuh", "g4_gemv_rows.cuh", "g4_internal.h", "g4_ctx.h"]
 
 
 def _run(cmd: list[str]) -> None:

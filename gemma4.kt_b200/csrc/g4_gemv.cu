@@ -61,18 +61,6 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
 
   if (threadIdx.x < W * NS) mbar_init(&bars[threadIdx.x], 1);
   if (threadIdx.x == 0) fence_barrier_init();
-  // x -> shared memory, plus the sum of every 16 and every 32 consecutive columns
-  for (int i = threadIdx.x * 4; i < p.cols; i += blockDim.x * 4)
-    *reinterpret_cast<float4*>(xs + i) = __ldg(reinterpret_cast<const float4*>(a.x + i));
-  __syncthreads();
-  for (int k = threadIdx.x; k < n16; k += blockDim.x) {
-    float t = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) t += xs[16 * k + i];
-    xsum16[k] = t;
-  }
-  __syncthreads();
-  for (int k = threadIdx.x; k < n16 / 2; k += blockDim.x) xsum32[k] = xsum16[2 * k] + xsum16[2 * k + 1];
   __syncthreads();
 
   const long long blk0 = p.off / BS;  // first block of the matrix
@@ -123,6 +111,21 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
     advance(gi, ci);
     if (gi != g0) rs_i = row_start(gi);
   }
+
+  // x -> shared memory while the first weight stages are in flight, plus the
+  // sum of every 16 and every 32 consecutive columns
+  for (int i = threadIdx.x * 4; i < p.cols; i += blockDim.x * 4)
+    *reinterpret_cast<float4*>(xs + i) = __ldg(reinterpret_cast<const float4*>(a.x + i));
+  __syncthreads();
+  for (int k = threadIdx.x; k < n16; k += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t += xs[16 * k + i];
+    xsum16[k] = t;
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < n16 / 2; k += blockDim.x) xsum32[k] = xsum16[2 * k] + xsum16[2 * k + 1];
+  __syncthreads();
 
   float acc[PR];
 #pragma unroll

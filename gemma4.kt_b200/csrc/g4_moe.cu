@@ -19,6 +19,7 @@
 #include "g4.h"
 #include "g4_ctx.h"
 #include "g4_gemv.cuh"
+#include "g4_gemv_rows.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -57,57 +58,131 @@ __device__ __forceinline__ float gelu_ref(float x) {
 
 // ---------------------------------------------------------------- prep
 
-__global__ void moe_prep_kernel(const float* __restrict__ x, const float* __restrict__ pre_norm,
-                                const float* __restrict__ gate_scale, float* __restrict__ moe_in,
-                                float* __restrict__ xr, int dim, float eps) {
+__global__ void __launch_bounds__(512) moe_prep_kernel(const float* __restrict__ x, const float* __restrict__ pre_norm,
+                                                       const float* __restrict__ gate_scale, float* __restrict__ moe_in,
+                                                       float* __restrict__ xr, float* __restrict__ moe_in_s16, int dim,
+                                                       float eps) {
   __shared__ float red[33];
-  const float* xt = x + (size_t)blockIdx.x * dim;
+  const float4* xt = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * dim);
+  const int n4 = dim >> 2;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(xt[i], xt[i], ss);
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    float4 v = xt[i];
+    ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+  }
   ss = block_sum(ss, red);
   // rmsnorm (Llama.kt:27-37): ss/size + eps, 1/sqrt in double
   float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
   float s_norm = (float)(1.0 / sqrt((double)m));
   // router scale (Llama.kt:258-261): (float)(1/sqrt(ss)) / (float)sqrt(dim)
   float s_router = __fdiv_rn(s_norm, (float)sqrt((double)dim));
-  float* mo = moe_in + (size_t)blockIdx.x * dim;
-  float* xo = xr + (size_t)blockIdx.x * dim;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-    float v = xt[i];
-    mo[i] = __fmul_rn(pre_norm[i], __fmul_rn(s_norm, v));
-    xo[i] = __fmul_rn(__fmul_rn(v, s_router), gate_scale[i]);
+  float4* mo = reinterpret_cast<float4*>(moe_in + (size_t)blockIdx.x * dim);
+  float4* xo = reinterpret_cast<float4*>(xr + (size_t)blockIdx.x * dim);
+  const float4* pn = reinterpret_cast<const float4*>(pre_norm);
+  const float4* gs = reinterpret_cast<const float4*>(gate_scale);
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    const float4 v = xt[i], w = pn[i], g = gs[i];
+    mo[i] = make_float4(__fmul_rn(w.x, __fmul_rn(s_norm, v.x)), __fmul_rn(w.y, __fmul_rn(s_norm, v.y)),
+                        __fmul_rn(w.z, __fmul_rn(s_norm, v.z)), __fmul_rn(w.w, __fmul_rn(s_norm, v.w)));
+    xo[i] = make_float4(__fmul_rn(__fmul_rn(v.x, s_router), g.x), __fmul_rn(__fmul_rn(v.y, s_router), g.y),
+                        __fmul_rn(__fmul_rn(v.z, s_router), g.z), __fmul_rn(__fmul_rn(v.w, s_router), g.w));
+  }
+  if (moe_in_s16 == nullptr) return;
+  __syncthreads();
+  const float* mi = moe_in + (size_t)blockIdx.x * dim;
+  for (int k = threadIdx.x; k < dim / 16; k += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t += mi[16 * k + i];
+    moe_in_s16[(size_t)blockIdx.x * (dim / 16) + k] = t;
   }
 }
 
 // ---------------------------------------------------------------- router
-// logits[t][e] = sum_k Wr[e][k] * xr[t][k].  One warp per expert, TT tokens
-// per CTA sharing each weight load.
-template <int TT>
-__global__ void __launch_bounds__(256) moe_router_kernel(const float* __restrict__ wr, const float* __restrict__ xr,
-                                                         float* __restrict__ logits, int T, int dim, int n_expert) {
+// logits[t][e] = sum_k Wr[e][k] * xr[t][k]  (F32 matmul, Llama.kt:269-270).
+// Few tokens: one CTA per (expert, 8 tokens); its 8 warps split K and the
+// partial sums meet in shared memory in a fixed order.
+__global__ void __launch_bounds__(256) moe_router_small_kernel(const float* __restrict__ wr,
+                                                               const float* __restrict__ xr, float* __restrict__ logits,
+                                                               int T, int dim, int n_expert) {
+  __shared__ float part[8][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 8 + warp;
-  const int t0 = blockIdx.y * TT;
-  if (e >= n_expert) return;
-  const float4* w4 = reinterpret_cast<const float4*>(wr + (size_t)e * dim);
-  float acc[TT];
-#pragma unroll
-  for (int j = 0; j < TT; ++j) acc[j] = 0.f;
+  const int e = blockIdx.x, t0 = blockIdx.y * 8;
   const int n4 = dim >> 2;
-  for (int k = lane; k < n4; k += 32) {
-    float4 w = __ldg(w4 + k);
+  const int k0 = (n4 * warp) / 8, k1 = (n4 * (warp + 1)) / 8;
+  const float4* w4 = reinterpret_cast<const float4*>(wr + (size_t)e * dim);
+  float acc[8];
 #pragma unroll
-    for (int j = 0; j < TT; ++j) {
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  for (int k = k0 + lane; k < k1; k += 32) {
+    const float4 w = __ldg(w4 + k);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
       if (t0 + j < T) {
-        float4 v = __ldg(reinterpret_cast<const float4*>(xr + (size_t)(t0 + j) * dim) + k);
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xr + (size_t)(t0 + j) * dim) + k);
         acc[j] = fmaf(w.x, v.x, fmaf(w.y, v.y, fmaf(w.z, v.z, fmaf(w.w, v.w, acc[j]))));
       }
     }
   }
 #pragma unroll
-  for (int j = 0; j < TT; ++j) {
+  for (int j = 0; j < 8; ++j) {
     float v = warp_sum(acc[j]);
-    if (lane == 0 && t0 + j < T) logits[(size_t)(t0 + j) * n_expert + e] = v;
+    if (lane == 0) part[warp][j] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 8 && t0 + threadIdx.x < T) {
+    float v = 0.f;
+    for (int w = 0; w < 8; ++w) v += part[w][threadIdx.x];
+    logits[(size_t)(t0 + threadIdx.x) * n_expert + e] = v;
+  }
+}
+
+// Many tokens: 64 tokens x 64 experts per CTA, K in shared-memory tiles of 32,
+// each thread a 4x4 block of outputs.
+__global__ void __launch_bounds__(256) moe_router_tiled_kernel(const float* __restrict__ wr,
+                                                               const float* __restrict__ xr, float* __restrict__ logits,
+                                                               int T, int dim, int n_expert) {
+  __shared__ float xs[32][64 + 4];
+  __shared__ float ws[32][64 + 4];
+  const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < dim; k0 += 32) {
+    for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+      const int r = i >> 5, k = i & 31;
+      xs[k][r] = (t0 + r < T && k0 + k < dim) ? xr[(size_t)(t0 + r) * dim + k0 + k] : 0.f;
+      ws[k][r] = (e0 + r < n_expert && k0 + k < dim) ? wr[(size_t)(e0 + r) * dim + k0 + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = xs[k][ty * 4 + i];
+        b[i] = ws[k][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + ty * 4 + i, e = e0 + tx * 4 + j;
+      if (t < T && e < n_expert) logits[(size_t)t * n_expert + e] = acc[i][j];
+    }
+}
+
+static void launch_router(const float* wr, const float* xr, float* logits, int T, int dim, int E, cudaStream_t st) {
+  if (T <= 64) {
+    moe_router_small_kernel<<<dim3(E, (T + 7) / 8), 256, 0, st>>>(wr, xr, logits, T, dim, E);
+  } else {
+    moe_router_tiled_kernel<<<dim3((T + 63) / 64, (E + 63) / 64), 256, 0, st>>>(wr, xr, logits, T, dim, E);
   }
 }
 
@@ -244,15 +319,28 @@ __global__ void __launch_bounds__(32 * (NCW + 1)) moe_expert_kernel(const __grid
       mbar_init(&empty[s], NCW);
     }
     fence_barrier_init();
-    int acc = 0;
-    for (int e = 0; e < a.E; ++e) {
-      int n = a.offsets[e + 1] - a.offsets[e];
-      int ch = (n + NB - 1) / NB;
-      s_chunks[e] = ch;
-      s_items[e] = acc;
-      acc += ch * a.tiles_e;
+  }
+  // per-expert chunk counts, then an exclusive scan of chunks * tiles (warp 0)
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+    const int n = a.offsets[e + 1] - a.offsets[e];
+    s_chunks[e] = (n + NB - 1) / NB;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int carry = 0;
+    for (int base = 0; base < a.E; base += 32) {
+      const int e = base + (int)threadIdx.x;
+      const int v = e < a.E ? s_chunks[e] * a.tiles_e : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if ((int)threadIdx.x >= o) incl += u;
+      }
+      if (e < a.E) s_items[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    s_items[a.E] = acc;
+    if (threadIdx.x == 0) s_items[a.E] = carry;
   }
   __syncthreads();
   const int n_items = s_items[a.E];
@@ -430,14 +518,423 @@ __global__ void __launch_bounds__(32 * (NCW + 1)) moe_expert_kernel(const __grid
   }
 }
 
+// ---------------------------------------------------------------- grouped experts, lane-per-row
+// The expert GEMVs in the GEMV kernel's style (csrc/g4_gemv.cu): each warp
+// streams 16 (virtual) rows of one expert through its own bulk-copy ring, two
+// lanes per row, and multiplies every decoded weight into the NB tokens routed
+// to that expert (activations through L1, their per-16-column sums from a
+// table).  Work item = (expert, token chunk of <= NB slots, row group).
+//   GATEUP: lane (rs, half) copies gate row r = 16g+rs (half 0) or up row
+//           ff+r (half 1); both lanes of a row decode alternate blocks of both
+//           rows; epilogue g = gelu(gate) * up -> G[slot][r] and the sum of the
+//           group's 16 G values -> Gs16[slot][g].
+//   DOWN:   lane (rs, half) owns virtual row 16g+rs (pr real rows of the
+//           [dim, ff] expert matrix); D[slot][row].
+struct RowsArgs {
+  const uint8_t* w;
+  const float* act;      // GATEUP: moe_in [T][cols]; DOWN: G [slots][cols]
+  const float* act_s16;  // per-16-column sums of the activation rows
+  float* out;            // GATEUP: G [slots][ff]; DOWN: D [slots][dim]
+  float* out_s16;        // GATEUP: Gs16 [slots][ff/16]
+  const int32_t* offsets;
+  const int32_t* perm;
+  unsigned* status;
+  int E, n_used, ff, dim;
+  int cols;              // K of the product
+  int nvrows;            // GATEUP: ff; DOWN: dim / pr
+  int bpv;               // blocks per virtual row
+  int cb, nchunks, pitch, ns;
+  int ngroups;           // ceil(nvrows / 16)
+  long long expert_elems;
+};
+
+template <int FMT, int PR, int NB>
+__device__ __forceinline__ void blk_nb(const uint8_t* blk, int e0, int cols, const float* const* xr,
+                                       const float* const* xs16, int nbv, float (&acc)[NB][PR]) {
+  constexpr uint32_t C = 0x3F800000u;
+  if constexpr (FMT == Q4_K) {
+    const uint4 h = lds128(blk);
+    const float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
+    const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+    const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int eg = e0 + 64 * g;
+      const int col = PR == 1 ? eg : eg % cols;
+      const int rr = PR == 1 ? 0 : eg / cols;
+      float2 alo[NB], ahi[NB];
+      float xlo[NB], xhi[NB];
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        if (j < nbv) {
+          xlo[j] = __ldg(xs16[j] + col / 16) + __ldg(xs16[j] + col / 16 + 1);
+          xhi[j] = __ldg(xs16[j] + col / 16 + 2) + __ldg(xs16[j] + col / 16 + 3);
+        } else {
+          xlo[j] = xhi[j] = 0.f;
+        }
+        alo[j] = f2(-xlo[j], 0.f);
+        ahi[j] = f2(-xhi[j], 0.f);
+      }
+      const uint4 qa = lds128(blk + 16 + 32 * g), qb = lds128(blk + 32 + 32 * g);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t w = k == 0 ? qa.x : k == 1 ? qa.y : k == 2 ? qa.z : k == 3 ? qa.w
+                         : k == 4 ? qb.x : k == 5 ? qb.y : k == 6 ? qb.z : qb.w;
+        const uint32_t ml = (w & 0x0F0F0F0Fu) | 0x80808080u, mh = w & 0xF0F0F0F0u;
+        const float2 l01 = f2(__uint_as_float(__byte_perm(ml, C, 0x7054u)), __uint_as_float(__byte_perm(ml, C, 0x7154u)));
+        const float2 l23 = f2(__uint_as_float(__byte_perm(ml, C, 0x7254u)), __uint_as_float(__byte_perm(ml, C, 0x7354u)));
+        const float2 h01 = f2(__uint_as_float(__byte_perm(mh, C, 0x7604u)), __uint_as_float(__byte_perm(mh, C, 0x7614u)));
+        const float2 h23 = f2(__uint_as_float(__byte_perm(mh, C, 0x7624u)), __uint_as_float(__byte_perm(mh, C, 0x7634u)));
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          if (j < nbv) {
+            const float4 xl = __ldg(reinterpret_cast<const float4*>(xr[j] + col) + k);
+            const float4 xh = __ldg(reinterpret_cast<const float4*>(xr[j] + col + 32) + k);
+            alo[j] = __ffma2_rn(l01, f2(xl.x, xl.y), alo[j]);
+            alo[j] = __ffma2_rn(l23, f2(xl.z, xl.w), alo[j]);
+            ahi[j] = __ffma2_rn(h01, f2(xh.x, xh.y), ahi[j]);
+            ahi[j] = __ffma2_rn(h23, f2(xh.z, xh.w), ahi[j]);
+          }
+        }
+      }
+      const uint32_t scw = g < 2 ? sc03 : sc47, mnw = g < 2 ? mn03 : mn47;
+      const int b0 = (2 * g) & 3;
+      const float c_lo = 128.f * d * (float)((scw >> (8 * b0)) & 0xFFu);
+      const float c_hi = 2048.f * d * (float)((scw >> (8 * b0 + 8)) & 0xFFu);
+      const float m_lo = dmin * (float)((mnw >> (8 * b0)) & 0xFFu);
+      const float m_hi = dmin * (float)((mnw >> (8 * b0 + 8)) & 0xFFu);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        float v = c_lo * (alo[j].x + alo[j].y);
+        v = fmaf(c_hi, ahi[j].x + ahi[j].y, v);
+        v = fmaf(-m_lo, xlo[j], fmaf(-m_hi, xhi[j], v));
+        add_row<PR>(acc[j], rr, v);
+      }
+    }
+  } else if constexpr (FMT == Q8_0) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+    const uint8_t* b4 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(a & 3u);
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 4 * i);
+    const float d = f16_bits_to_f32((uint16_t)(sh ? (w[0] >> 16) : (w[0] & 0xFFFFu)));
+    const int col = e0;  // Q8_0 rows are whole blocks here (pr == 1)
+    float2 s[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) s[j] = f2(0.f, 0.f);
+    const float2 nb2 = f2(-8388736.0f, -8388736.0f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t m = __funnelshift_rc(w[k], w[k + 1], 16u + 8u * sh) ^ 0x80808080u;
+      const float2 q01 = __fadd2_rn(f2(f_magic23(m, 0), f_magic23(m, 1)), nb2);
+      const float2 q23 = __fadd2_rn(f2(f_magic23(m, 2), f_magic23(m, 3)), nb2);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        if (j < nbv) {
+          const float4 xv = __ldg(reinterpret_cast<const float4*>(xr[j] + col) + k);
+          s[j] = __ffma2_rn(q01, f2(xv.x, xv.y), s[j]);
+          s[j] = __ffma2_rn(q23, f2(xv.z, xv.w), s[j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NB; ++j) acc[j][0] = fmaf(s[j].x + s[j].y, d, acc[j][0]);
+  } else {  // Q6_K
+    const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+    const uint8_t* b4 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = 8u * (uint32_t)(a & 3u);
+    const float d = f16_bits_to_f32((uint16_t)(__funnelshift_r(lds32(b4 + 208), lds32(b4 + 212), sh) & 0xFFFFu));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t qa[8], qb[8], qh[8], w[9];
+#pragma unroll
+      for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 64 * h + 4 * i);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qa[i] = __funnelshift_r(w[i], w[i + 1], sh);
+#pragma unroll
+      for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 64 * h + 32 + 4 * i);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qb[i] = __funnelshift_r(w[i], w[i + 1], sh);
+#pragma unroll
+      for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 128 + 32 * h + 4 * i);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qh[i] = __funnelshift_r(w[i], w[i + 1], sh);
+      const uint32_t s0 = lds32(b4 + 192 + 8 * h), s1 = lds32(b4 + 196 + 8 * h), s2 = lds32(b4 + 200 + 8 * h);
+      const uint32_t scw0 = __funnelshift_r(s0, s1, sh), scw1 = __funnelshift_r(s1, s2, sh);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int ebase = e0 + 128 * h + 16 * c;
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {
+          const int e = ebase + 32 * sub;
+          const int col = PR == 1 ? e : e % cols;
+          const int rr = PR == 1 ? 0 : e / cols;
+          float2 a4[NB];
+          float xsum[NB];
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            xsum[j] = j < nbv ? __ldg(xs16[j] + col / 16) : 0.f;
+            a4[j] = f2(-xsum[j], 0.f);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t la = qa[4 * c + k], lb = qb[4 * c + k], hh = qh[4 * c + k];
+            uint32_t m;
+            if (sub == 0) m = ((la & 0x0F0F0F0Fu) | 0x80808080u) | ((hh << 4) & 0x30303030u);
+            else if (sub == 1) m = ((lb & 0x0F0F0F0Fu) | 0x80808080u) | ((hh << 2) & 0x30303030u);
+            else if (sub == 2) m = (((la >> 4) & 0x0F0F0F0Fu) | 0x80808080u) | (hh & 0x30303030u);
+            else m = (((lb >> 4) & 0x0F0F0F0Fu) | 0x80808080u) | ((hh >> 2) & 0x30303030u);
+            const float2 f01 = f2(__uint_as_float(__byte_perm(m, C, 0x7054u)), __uint_as_float(__byte_perm(m, C, 0x7154u)));
+            const float2 f23 = f2(__uint_as_float(__byte_perm(m, C, 0x7254u)), __uint_as_float(__byte_perm(m, C, 0x7354u)));
+#pragma unroll
+            for (int j = 0; j < NB; ++j) {
+              if (j < nbv) {
+                const float4 xv = __ldg(reinterpret_cast<const float4*>(xr[j] + col) + k);
+                a4[j] = __ffma2_rn(f01, f2(xv.x, xv.y), a4[j]);
+                a4[j] = __ffma2_rn(f23, f2(xv.z, xv.w), a4[j]);
+              }
+            }
+          }
+          const int si = 2 * sub + c;
+          const int8_t sc = (int8_t)((((si >> 2) ? scw1 : scw0) >> (8 * (si & 3))) & 0xFFu);
+          const float ds = d * (float)sc;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) add_row<PR>(acc[j], rr, ds * fmaf(128.f, a4[j].x + a4[j].y, -32.f * xsum[j]));
+        }
+      }
+    }
+  }
+}
+
+template <int FMT, bool GATEUP, int PR, int NB>
+__global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __grid_constant__ RowsArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int BS = block_size(FMT), TS = type_size(FMT);
+  constexpr int RPW = 16, LPR = 2;
+  constexpr int SLOTS = GATEUP ? 2 * RPW : RPW;  // row slots per stage
+  int* s_items = reinterpret_cast<int*>(smem);           // [E+1]
+  int* s_chunks = s_items + (kMaxExperts + 1);           // [E]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 8 * (kMaxExperts + 8));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, W = blockDim.x >> 5;
+  const int NS = a.ns;
+  uint8_t* ring = smem + 8 * (kMaxExperts + 8) + 128 * ((W * NS * 8 + 127) / 128);
+  const size_t stage_bytes = (size_t)SLOTS * a.pitch;
+  uint64_t* mybars = bars + warp * NS;
+  uint8_t* myring = ring + (size_t)warp * NS * stage_bytes;
+  const int rs = lane % RPW, half = lane / RPW;
+
+  if (threadIdx.x < W * NS) mbar_init(&bars[threadIdx.x], 1);
+  if (threadIdx.x == 0) fence_barrier_init();
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+    const int n = a.offsets[e + 1] - a.offsets[e];
+    s_chunks[e] = (n + NB - 1) / NB;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int carry = 0;
+    for (int base = 0; base < a.E; base += 32) {
+      const int e = base + (int)threadIdx.x;
+      const int v = e < a.E ? s_chunks[e] * a.ngroups : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if ((int)threadIdx.x >= o) incl += u;
+      }
+      if (e < a.E) s_items[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (threadIdx.x == 0) s_items[a.E] = carry;
+  }
+  __syncthreads();
+  const int n_items = s_items[a.E];
+
+  struct Item {
+    int e, g, k;
+  };
+  auto locate = [&](int item) {
+    int lo = 0, hi = a.E - 1;  // last e with s_items[e] <= item (never an empty expert)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_items[mid] <= item) lo = mid;
+      else hi = mid - 1;
+    }
+    const int local = item - s_items[lo];
+    const int ch = s_chunks[lo];
+    return Item{lo, local / ch, local % ch};
+  };
+  const long long vrow_bytes = (long long)a.bpv * TS;
+  const long long chunk_bytes = (long long)a.cb * TS;
+  const long long blk_row = (long long)(GATEUP ? 1 : PR) * a.cols / BS;  // blocks per virtual row
+  // first byte of this lane's copied row in item `it` (GATEUP: gate or up row by half)
+  auto row_start = [&](const Item& it, bool& ok) {
+    const int v = it.g * RPW + rs;
+    ok = v < a.nvrows;
+    const long long eb = (long long)it.e * a.expert_elems / BS;  // expert's first block
+    const long long row = GATEUP ? (long long)(half ? a.ff + v : v) : (long long)v;
+    return (eb + row * blk_row) * TS;
+  };
+  auto issue = [&](const Item& it, int c, int slot) {
+    uint64_t* bar = &mybars[slot];
+    uint32_t mine = 0;
+    if (GATEUP || half == 0) {
+      bool ok;
+      const long long rstart = row_start(it, ok);
+      if (ok) {
+        const long long start = rstart + c * chunk_bytes;
+        const long long len = min(chunk_bytes, vrow_bytes - c * chunk_bytes);
+        const long long a0 = start & ~15ll, a1 = (start + len + 15) & ~15ll;
+        const int slot_row = GATEUP ? half * RPW + rs : rs;
+        bulk_g2s(myring + (size_t)slot * stage_bytes + (size_t)slot_row * a.pitch, a.w + a0, (uint32_t)(a1 - a0), bar);
+        mine = (uint32_t)(a1 - a0);
+      }
+    }
+    const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
+    if (lane == 0) mbar_arrive_expect_tx(bar, total);
+  };
+
+  const int gw = blockIdx.x * W + warp, GW = gridDim.x * W;
+  bool okw = true;
+  int issued = 0, consumed = 0;
+  int ii = gw, ci = 0;  // issue pointer (item, chunk)
+  Item iti = ii < n_items ? locate(ii) : Item{0, 0, 0};
+  for (; issued < NS && ii < n_items; ++issued) {
+    issue(iti, ci, issued);
+    if (++ci == a.nchunks) {
+      ci = 0;
+      ii += GW;
+      if (ii < n_items) iti = locate(ii);
+    }
+  }
+
+  float acc[NB][PR], acc2[NB];  // acc2: up-row sums (GATEUP)
+  int item = gw, c = 0;
+  Item it{};
+  const float* xr[NB];
+  const float* xs16[NB];
+  int slots[NB];
+  int nbv = 0;
+  for (int i = 0; item < n_items; ++i) {
+    if (c == 0) {
+      it = locate(item);
+      const int p0 = a.offsets[it.e] + it.k * NB;
+      nbv = min(NB, a.offsets[it.e + 1] - p0);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const int sj = j < nbv ? a.perm[p0 + j] : 0;
+        slots[j] = sj;
+        const int row = GATEUP ? sj / a.n_used : sj;
+        xr[j] = a.act + (size_t)row * a.cols;
+        xs16[j] = a.act_s16 + (size_t)row * (a.cols / 16);
+#pragma unroll
+        for (int r = 0; r < PR; ++r) acc[j][r] = 0.f;
+        acc2[j] = 0.f;
+      }
+    }
+    const int slot = i % NS;
+    if (!mbar_wait_bounded(&mybars[slot], (i / NS) & 1)) {
+      record_error(a.status, ERR_TIMEOUT_FULL);
+      okw = false;
+      consumed = i;
+      break;
+    }
+    {
+      const Item& cur = it;
+      const int v = cur.g * RPW + rs;
+      if (v < a.nvrows) {
+        const long long start_c = (long long)c * chunk_bytes;
+        const int nb = (int)(min(chunk_bytes, vrow_bytes - start_c) / TS);
+        const int e0 = c * a.cb * BS;
+        const uint8_t* sbase = myring + (size_t)slot * stage_bytes;
+        if constexpr (GATEUP) {
+          // both rows' segments: gate in slots [0,16), up in [16,32)
+          const long long eb = (long long)cur.e * a.expert_elems / BS;
+          const long long g_start = (eb + (long long)v * blk_row) * TS + start_c;
+          const long long u_start = (eb + (long long)(a.ff + v) * blk_row) * TS + start_c;
+          const uint8_t* gb = sbase + (size_t)rs * a.pitch + (g_start & 15);
+          const uint8_t* ub = sbase + (size_t)(RPW + rs) * a.pitch + (u_start & 15);
+          for (int b = half; b < nb; b += LPR) {
+            float tmp[NB][1];
+#pragma unroll
+            for (int j = 0; j < NB; ++j) tmp[j][0] = 0.f;
+            blk_nb<FMT, 1, NB>(gb + b * TS, e0 + b * BS, a.cols, xr, xs16, nbv, tmp);
+#pragma unroll
+            for (int j = 0; j < NB; ++j) acc[j][0] += tmp[j][0];
+#pragma unroll
+            for (int j = 0; j < NB; ++j) tmp[j][0] = 0.f;
+            blk_nb<FMT, 1, NB>(ub + b * TS, e0 + b * BS, a.cols, xr, xs16, nbv, tmp);
+#pragma unroll
+            for (int j = 0; j < NB; ++j) acc2[j] += tmp[j][0];
+          }
+        } else {
+          const long long eb = (long long)cur.e * a.expert_elems / BS;
+          const long long r_start = (eb + (long long)v * blk_row) * TS + start_c;
+          const uint8_t* rb = sbase + (size_t)rs * a.pitch + (r_start & 15);
+          for (int b = half; b < nb; b += LPR) blk_nb<FMT, PR, NB>(rb + b * TS, e0 + b * BS, a.cols, xr, xs16, nbv, acc);
+        }
+      }
+    }
+    // refill this slot with the stage NS ahead
+    __syncwarp();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (ii < n_items) {
+      issue(iti, ci, slot);
+      ++issued;
+      if (++ci == a.nchunks) {
+        ci = 0;
+        ii += GW;
+        if (ii < n_items) iti = locate(ii);
+      }
+    }
+    if (++c == a.nchunks) {
+      // item finished: combine the two lanes of each row, write the results
+      const int v = it.g * RPW + rs;
+      const bool ok = v < a.nvrows;
+      if constexpr (GATEUP) {
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          const float hg = acc[j][0] + __shfl_xor_sync(0xffffffffu, acc[j][0], 16);
+          const float hu = acc2[j] + __shfl_xor_sync(0xffffffffu, acc2[j], 16);
+          float gv = 0.f;
+          if (ok && j < nbv) gv = __fmul_rn(gelu_ref(hg), hu);  // Llama.kt:316-322
+          if (half == 0 && ok && j < nbv) a.out[(size_t)slots[j] * a.ff + v] = gv;
+          // per-16-column sum of G for the down product (the group's 16 rows)
+          float t = (half == 0) ? gv : 0.f;
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+          if (lane == 0 && j < nbv) a.out_s16[(size_t)slots[j] * (a.ff / 16) + it.g] = t;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < NB; ++j)
+#pragma unroll
+          for (int r = 0; r < PR; ++r) {
+            const float t = acc[j][r] + __shfl_xor_sync(0xffffffffu, acc[j][r], 16);
+            if (half == 0 && ok && j < nbv) a.out[(size_t)slots[j] * a.dim + (size_t)v * PR + r] = t;
+          }
+      }
+      c = 0;
+      item += GW;
+    }
+  }
+  if (!okw) {
+    for (int q = consumed + 1; q < issued; ++q)
+      if (!mbar_wait_bounded(&mybars[q % NS], (q / NS) & 1)) record_error(a.status, ERR_TIMEOUT_DRAIN);
+  }
+}
+
 // ---------------------------------------------------------------- combine
 // moeOutput = 0; for ki: moeOutput += (prob*downScale) * down  (saxpyInPlace,
 // MutableFloatTensor.kt:61-66: product rounded, then added); then
 // rmsnorm(post_ffw_norm_2) (Llama.kt:340-346) when a weight is given.
-__global__ void moe_combine_kernel(const float* __restrict__ D, const int32_t* __restrict__ idx,
-                                   const float* __restrict__ prob, const float* __restrict__ down_scale,
-                                   const float* __restrict__ post_norm, float* __restrict__ out, int dim, int K,
-                                   float eps) {
+__global__ void __launch_bounds__(512) moe_combine_kernel(const float* __restrict__ D, const int32_t* __restrict__ idx,
+                                                          const float* __restrict__ prob,
+                                                          const float* __restrict__ down_scale,
+                                                          const float* __restrict__ post_norm, float* __restrict__ out,
+                                                          int dim, int K, float eps) {
   __shared__ float red[33];
   __shared__ float fw[kMaxUsed];
   const int t = blockIdx.x;
@@ -446,25 +943,48 @@ __global__ void moe_combine_kernel(const float* __restrict__ D, const int32_t* _
     fw[threadIdx.x] = __fmul_rn(prob[(size_t)t * K + threadIdx.x], down_scale[e]);
   }
   __syncthreads();
-  float* o = out + (size_t)t * dim;
+  float4* o = reinterpret_cast<float4*>(out + (size_t)t * dim);
+  const int n4 = dim >> 2;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-    float acc = 0.f;
-    for (int k = 0; k < K; ++k) acc = __fadd_rn(__fmul_rn(fw[k], D[((size_t)t * K + k) * dim + i]), acc);
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    float4 d[kMaxUsed];
+#pragma unroll
+    for (int k = 0; k < kMaxUsed; ++k)
+      if (k < K) d[k] = __ldg(reinterpret_cast<const float4*>(D + ((size_t)t * K + k) * dim) + i);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < kMaxUsed; ++k) {
+      if (k < K) {
+        acc.x = __fadd_rn(__fmul_rn(fw[k], d[k].x), acc.x);
+        acc.y = __fadd_rn(__fmul_rn(fw[k], d[k].y), acc.y);
+        acc.z = __fadd_rn(__fmul_rn(fw[k], d[k].z), acc.z);
+        acc.w = __fadd_rn(__fmul_rn(fw[k], d[k].w), acc.w);
+      }
+    }
     o[i] = acc;
-    ss = fmaf(acc, acc, ss);
+    ss = fmaf(acc.x, acc.x, fmaf(acc.y, acc.y, fmaf(acc.z, acc.z, fmaf(acc.w, acc.w, ss))));
   }
   if (post_norm == nullptr) return;
   ss = block_sum(ss, red);
-  float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
-  float sn = (float)(1.0 / sqrt((double)m));
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) o[i] = __fmul_rn(post_norm[i], __fmul_rn(sn, o[i]));
+  const float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
+  const float sn = (float)(1.0 / sqrt((double)m));
+  const float4* pn = reinterpret_cast<const float4*>(post_norm);
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    float4 v = o[i];
+    const float4 w = pn[i];
+    v.x = __fmul_rn(w.x, __fmul_rn(sn, v.x));
+    v.y = __fmul_rn(w.y, __fmul_rn(sn, v.y));
+    v.z = __fmul_rn(w.z, __fmul_rn(sn, v.z));
+    v.w = __fmul_rn(w.w, __fmul_rn(sn, v.w));
+    o[i] = v;
+  }
 }
 
 // ---------------------------------------------------------------- host side
 
 struct MoeScratch {
   float *moe_in, *xr, *logits, *prob, *G, *D;
+  float *moe_in_s16, *G_s16;  // per-16-column sums of moe_in rows and of G rows
   int32_t *idx, *offsets, *perm;
 };
 
@@ -478,6 +998,8 @@ static size_t moe_scratch_bytes(int T, int dim, int E, int K, int ff) {
   s += align_up((size_t)(E + 1) * 4, 256);           // offsets
   s += align_up((size_t)T * K * ff * 4, 256);        // G
   s += align_up((size_t)T * K * dim * 4, 256);       // D
+  s += align_up((size_t)T * (dim / 16) * 4, 256);    // moe_in_s16
+  s += align_up((size_t)T * K * (ff / 16) * 4, 256); // G_s16
   return s;
 }
 
@@ -498,6 +1020,8 @@ static MoeScratch carve(uint8_t* base, int T, int dim, int E, int K, int ff) {
   m.offsets = (int32_t*)take((size_t)(E + 1) * 4);
   m.G = (float*)take((size_t)T * K * ff * 4);
   m.D = (float*)take((size_t)T * K * dim * 4);
+  m.moe_in_s16 = (float*)take((size_t)T * (dim / 16) * 4);
+  m.G_s16 = (float*)take((size_t)T * K * (ff / 16) * 4);
   return m;
 }
 
@@ -611,8 +1135,175 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+using RowsFn = void (*)(const RowsArgs);
+
+template <int FMT, bool GU, int PR>
+static RowsFn rows_fn_nb(int nb) {
+  if (nb >= 8) return moe_rows_kernel<FMT, GU, PR, 8>;
+  if (nb >= 4) return moe_rows_kernel<FMT, GU, PR, 4>;
+  if (nb >= 2) return moe_rows_kernel<FMT, GU, PR, 2>;
+  return moe_rows_kernel<FMT, GU, PR, 1>;
+}
+
+static RowsFn rows_fn(int type, bool gu, int pr, int nb) {
+  if (gu) {
+    if (type == Q4_K) return rows_fn_nb<Q4_K, true, 1>(nb);
+    if (type == Q6_K) return rows_fn_nb<Q6_K, true, 1>(nb);
+    if (type == Q8_0) return rows_fn_nb<Q8_0, true, 1>(nb);
+    return nullptr;
+  }
+  if (type == Q8_0) return pr == 1 ? rows_fn_nb<Q8_0, false, 1>(nb) : nullptr;
+  if (type == Q4_K) {
+    if (pr == 1) return rows_fn_nb<Q4_K, false, 1>(nb);
+    if (pr == 2) return rows_fn_nb<Q4_K, false, 2>(nb);
+    if (pr == 4) return rows_fn_nb<Q4_K, false, 4>(std::min(nb, 4));
+  }
+  if (type == Q6_K) {
+    if (pr == 1) return rows_fn_nb<Q6_K, false, 1>(nb);
+    if (pr == 2) return rows_fn_nb<Q6_K, false, 2>(nb);
+    if (pr == 4) return rows_fn_nb<Q6_K, false, 4>(std::min(nb, 4));
+  }
+  return nullptr;
+}
+
+static int rows_pitch(int bytes) {
+  int p = (bytes + 15) / 16;
+  if ((p & 1) == 0) ++p;
+  return 16 * p;
+}
+
+// Kernel set-up (smem attribute + occupancy) cached per kernel; the no-alloc
+// path keeps its own fixed table so it never touches the heap.
+static int rows_occ(RowsFn fn, size_t smem, int threads, int optin, bool noalloc_path);
+
+// Returns 0, -1 when the layout needs the generic expert kernel, -2 on a launch error.
+static int launch_expert_rows(g4_ctx* c, int type, bool gu, const uint8_t* w, const float* act, const float* act_s16,
+                              float* out, float* out_s16, const MoeScratch& m, int E, int K, int dim, int ff, int T,
+                              cudaStream_t st, bool noalloc_path) {
+  if (type != Q4_K && type != Q6_K && type != Q8_0) return -1;
+  const int BS = block_size(type), TS = type_size(type);
+  RowsArgs a{};
+  a.w = w;
+  a.act = act;
+  a.act_s16 = act_s16;
+  a.out = out;
+  a.out_s16 = out_s16;
+  a.offsets = m.offsets;
+  a.perm = m.perm;
+  a.status = c->status;
+  a.E = E;
+  a.n_used = K;
+  a.ff = ff;
+  a.dim = dim;
+  int pr = 1;
+  if (gu) {
+    if (dim % BS || dim % 64 || ff % 16) return -1;
+    a.cols = dim;
+    a.nvrows = ff;
+    a.bpv = dim / BS;
+    a.expert_elems = (long long)2 * ff * dim;
+  } else {
+    if (ff % 64) return -1;
+    if (ff % BS) {
+      if (type == Q8_0) return -1;
+      int g = ff % BS, b = BS;
+      while (b) {
+        int t = g % b;
+        g = b;
+        b = t;
+      }
+      pr = BS / g;
+      if (pr != 2 && pr != 4) return -1;
+    }
+    if (dim % pr) return -1;
+    a.cols = ff;
+    a.nvrows = dim / pr;
+    a.bpv = pr * ff / BS;
+    a.expert_elems = (long long)dim * ff;
+  }
+  if (a.expert_elems % BS) return -1;
+  a.ngroups = (a.nvrows + 15) / 16;
+  // about 288-560 bytes of a row per bulk copy, an even number of blocks (two lanes per row)
+  int cb = type == Q4_K ? 2 : type == Q6_K ? 2 : 8;
+  cb = std::min(cb, (a.bpv + 1) / 2 * 2);
+  a.cb = std::max(2, cb);
+  a.nchunks = (a.bpv + a.cb - 1) / a.cb;
+  a.pitch = rows_pitch(a.cb * TS + 32);
+  const int slots = gu ? 32 : 16;
+  const size_t stage = (size_t)slots * a.pitch;
+  const int optin = (int)c->dev.smem_optin;
+  const size_t head = 8 * (kMaxExperts + 8);
+  const int avg = (T * K + E - 1) / E;
+  // Wide token tiles belong to the tensor-core / generic kernels: here the
+  // activations stream through L1 once per token, which only pays for <= 2.
+  if (avg > 2) return -1;
+  const int nb = avg >= 2 ? 2 : 1;
+  // warps per CTA from the amount of work, so that every SM gets some
+  const long long max_items = (long long)(std::min((long long)T * K, (long long)E) +
+                                          ((long long)T * K + nb - 1) / nb) * a.ngroups;
+  int warps = (int)std::min<long long>(16, std::max<long long>(1, (max_items + c->dev.sms - 1) / c->dev.sms));
+  auto need = [&](int wv, int ns) { return head + 128 * ((wv * ns * 8 + 127) / 128) + (size_t)wv * ns * stage; };
+  // deepest ring (up to 6 stages) that fits; fewer warps per SM leave room for more stages
+  a.ns = 6;
+  while (a.ns > 2 && need(warps, a.ns) > (size_t)optin) --a.ns;
+  while (warps > 1 && need(warps, a.ns) > (size_t)optin) --warps;
+  if (need(warps, a.ns) > (size_t)optin) return -1;
+  const size_t smem = need(warps, a.ns);
+  RowsFn fn = rows_fn(type, gu, pr, nb);
+  if (!fn) return -1;
+  const int occ = rows_occ(fn, smem, 32 * warps, optin, noalloc_path);
+  if (occ < 1) return -2;
+  const int grid = (int)std::max<long long>(1, std::min<long long>((max_items + warps - 1) / warps,
+                                                                   (long long)c->dev.sms * occ));
+  fn<<<grid, 32 * warps, smem, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 static int tensor_ok(const g4_tensor* t, int type, uint64_t n) {
   return t && (type < 0 || t->type == type) && t->n_elems == n;
+}
+
+static int rows_occ_fixed(RowsFn fn, size_t smem, int threads, int optin);
+
+static int rows_occ(RowsFn fn, size_t smem, int threads, int optin, bool noalloc_path) {
+  if (noalloc_path) return rows_occ_fixed(fn, smem, threads, optin);
+  static std::mutex mu;
+  static std::map<std::pair<RowsFn, size_t>, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_pair(fn, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int o = 0;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cache.emplace(key, o);
+  return o;
+}
+
+// fixed table for the no-alloc path (no heap use)
+static int rows_occ_fixed(RowsFn fn, size_t smem, int threads, int optin) {
+  static std::mutex mu;
+  struct E {
+    RowsFn fn;
+    size_t smem;
+    int occ;
+  };
+  static E tab[64];
+  static int n = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < n; ++i)
+    if (tab[i].fn == fn && tab[i].smem == smem) return tab[i].occ;
+  int o = 0;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (n < 64) tab[n++] = E{fn, smem, o};
+  return o;
 }
 
 }  // namespace g4
@@ -669,24 +1360,33 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
   }
   MoeScratch m = carve(base, T, dim, E, K, ff);
   const float* f_scale = (const float*)w->gate_inp_scale->d;
-  moe_prep_kernel<<<T, 256, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, f_scale, m.moe_in, m.xr, dim, w->eps);
-  dim3 rg((E + 7) / 8, (T + 7) / 8);
-  moe_router_kernel<8><<<rg, 256, 0, st>>>((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E);
+  moe_prep_kernel<<<T, 512, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, f_scale, m.moe_in, m.xr, m.moe_in_s16, dim, w->eps);
+  launch_router((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E, st);
   moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(m.logits, T, E, K, m.idx, m.prob);
   moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, T * K, E, m.offsets, m.perm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer launch");
-  int r = launch_expert(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m, E, K,
-                        dim, ff, T, st);
-  if (r == 0)
-    r = launch_expert(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K, dim, ff, T,
-                      st);
+  int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
+                             m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, false);
+  const bool rows_gu = r == 0;
+  if (r == -1)
+    r = launch_expert(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m, E, K,
+                      dim, ff, T, st);
+  if (r == 0) {
+    // the down rows kernel needs G's per-16-column sums, written by the gate_up rows kernel
+    r = rows_gu ? launch_expert_rows(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.G_s16,
+                                     m.D, nullptr, m, E, K, dim, ff, T, st, false)
+                : -1;
+    if (r == -1)
+      r = launch_expert(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K, dim, ff,
+                        T, st);
+  }
   if (r == -1) {
     c->set_err("g4_moe_layer: expert tensor layout not supported by the grouped kernels");
     return G4_E_ARG;
   }
   if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer expert launch");
-  moe_combine_kernel<<<T, 256, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
+  moe_combine_kernel<<<T, 512, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
                                         w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr, out, dim,
                                         K, w->eps);
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
@@ -897,25 +1597,33 @@ extern "C" int g4_moe_layer_noalloc(g4_ctx* c, const g4_moe_weights* w, const fl
   // Every work buffer is fully written before it is read, so nothing has to
   // be cleared between calls.
   MoeScratch m = carve(base, T, dim, E, K, ff);
-  moe_prep_kernel<<<T, 256, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, (const float*)w->gate_inp_scale->d,
-                                     m.moe_in, m.xr, dim, w->eps);
-  dim3 rg((E + 7) / 8, (T + 7) / 8);
-  moe_router_kernel<8><<<rg, 256, 0, st>>>((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E);
+  moe_prep_kernel<<<T, 512, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, (const float*)w->gate_inp_scale->d,
+                                     m.moe_in, m.xr, m.moe_in_s16, dim, w->eps);
+  launch_router((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E, st);
   moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(m.logits, T, E, K, m.idx, m.prob);
   moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, T * K, E, m.offsets, m.perm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_noalloc launch");
-  int r = launch_expert_noalloc(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m,
-                                E, K, dim, ff, T, st);
-  if (r == 0)
-    r = launch_expert_noalloc(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K, dim,
-                              ff, T, st);
+  int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
+                             m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, true);
+  const bool rows_gu = r == 0;
+  if (r == -1)
+    r = launch_expert_noalloc(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m,
+                              E, K, dim, ff, T, st);
+  if (r == 0) {
+    r = rows_gu ? launch_expert_rows(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.G_s16,
+                                     m.D, nullptr, m, E, K, dim, ff, T, st, true)
+                : -1;
+    if (r == -1)
+      r = launch_expert_noalloc(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K,
+                                dim, ff, T, st);
+  }
   if (r == -1) {
     c->set_err("g4_moe_layer_noalloc: expert tensor layout not supported by the grouped kernels");
     return G4_E_ARG;
   }
   if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer_noalloc expert launch");
-  moe_combine_kernel<<<T, 256, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
+  moe_combine_kernel<<<T, 512, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
                                         w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr, out, dim,
                                         K, w->eps);
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
