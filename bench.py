@@ -253,14 +253,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                     if rc:
                         raise RuntimeError(ctx.last_error())
                 g.capture_end()
-            g.replay()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             reps = 5
-            e0.record(stream)
-            for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):  # replay() launches on the current stream
                 g.replay()
-            e1.record(stream)
+                torch.cuda.synchronize()
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
             torch.cuda.synchronize()
             per_case[i] = e0.elapsed_time(e1) / (10 * reps)
             del g
@@ -282,20 +283,22 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             step_graph.capture_begin()
             step()
             step_graph.capture_end()
-        step_graph.replay()
+        with torch.cuda.stream(stream):
+            step_graph.replay()
         torch.cuda.synchronize()
 
     # headline: exactly K steps, barrier + synchronize on both sides
     barrier()
     torch.cuda.synchronize()
     t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0e.record(stream)
-    for _ in range(args.steps):
-        if step_graph is not None:
-            step_graph.replay()
-        else:
-            step()
-    t1e.record(stream)
+    with torch.cuda.stream(stream):  # graph replays launch on the current stream
+        t0e.record(stream)
+        for _ in range(args.steps):
+            if step_graph is not None:
+                step_graph.replay()
+            else:
+                step()
+        t1e.record(stream)
     torch.cuda.synchronize()
     barrier()
     clk.__exit__(None, None, None)
@@ -408,14 +411,15 @@ def bench_moe(g4, ctx, torch, dev):
             g.capture_begin()
             layer.forward(x, out, T, stream=stream.cuda_stream)
             g.capture_end()
-        g.replay()
-        torch.cuda.synchronize()
         reps = 20 if T <= 256 else 5
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
+        with torch.cuda.stream(stream):  # replay() launches on the current stream
             g.replay()
-        b.record(stream)
+            torch.cuda.synchronize()
+            a.record(stream)
+            for _ in range(reps):
+                g.replay()
+            b.record(stream)
         torch.cuda.synchronize()
         us = a.elapsed_time(b) * 1e3 / reps
         del g
@@ -426,6 +430,44 @@ def bench_moe(g4, ctx, torch, dev):
             **res}
 
 
+def profile_mode(args):
+    """Run one GEMV case or the MoE layer a few times with no timing logic, as
+    the target of an ncu capture."""
+    import torch
+
+    import __graft_entry__
+
+    g4 = __graft_entry__.load_package()
+    from gemma4_kt_b200 import synth
+
+    ctx = g4.Context(0)
+    if args.only:
+        name, shape = args.only.split(":")
+        rows, cols = (int(v) for v in shape.split("x"))
+        t = dict(FORMATS)[name]
+        rng = np.random.default_rng(1)
+        raw = synth.quantize(t, synth.normal(rng, rows * cols))
+        x = torch.from_numpy(rng.standard_normal(cols, dtype=np.float32)).cuda()
+        y = torch.empty(rows, device="cuda")
+        w = g4.FloatTensorFactory.create(ctx, t, raw, rows * cols)
+        for _ in range(args.reps):
+            w.matmul(x, y, rows, cols)
+        torch.cuda.synchronize()
+        print(f"ran {name} {rows}x{cols} x{args.reps}")
+    else:
+        d = synth.MoeLayerData(seed=2)
+        layer = g4.MoeLayer.upload(ctx, d)
+        for T in (int(v) for v in args.moe_only.split(",")):
+            x = torch.from_numpy(d.tokens(T)).cuda()
+            out = torch.empty((T, d.dim), device="cuda")
+            for _ in range(args.reps):
+                layer.forward(x, out, T)
+            torch.cuda.synchronize()
+            print(f"ran MoE layer T={T} x{args.reps}")
+    ctx.sync()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -434,7 +476,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--only", default=None,
+                    help="profiling mode: run one sweep case FORMAT:ROWSxCOLS (e.g. Q4_K:262144x1536) --reps times")
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--moe-only", default=None,
+                    help="profiling mode: run the MoE layer --reps times for these token counts (e.g. 1,256)")
     args = ap.parse_args()
+    if args.only or args.moe_only:
+        profile_mode(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(256) moe_router_tiled_kernel(const float* __re
 }
 
 static void launch_router(const float* wr, const float* xr, float* logits, int T, int dim, int E, cudaStream_t st) {
-  if (T <= 64) {
+  if (T <= 512) {
     moe_router_small_kernel<<<dim3(E, (T + 7) / 8), 256, 0, st>>>(wr, xr, logits, T, dim, E);
   } else {
     moe_router_tiled_kernel<<<dim3((T + 63) / 64, (E + 63) / 64), 256, 0, st>>>(wr, xr, logits, T, dim, E);
@@ -545,12 +545,19 @@ struct RowsArgs {
   int bpv;               // blocks per virtual row
   int cb, nchunks, pitch, ns;
   int ngroups;           // ceil(nvrows / 16)
+  int split;             // 1: warps own items; >1: CTA owns an item, its warps split the chunks
+  int xcols;             // activation floats staged per token per stage (GATEUP: the chunk; DOWN: the row)
+  int xs16n;             // per-16 sums staged per token per stage
+  int x_at, xs_at;       // byte offsets of those areas inside a stage
+  int stage_bytes;
   long long expert_elems;
 };
 
+// xr[j] / xs16[j]: token j's activations / per-16-column sums staged in shared
+// memory, holding columns from `xoff` on.
 template <int FMT, int PR, int NB>
 __device__ __forceinline__ void blk_nb(const uint8_t* blk, int e0, int cols, const float* const* xr,
-                                       const float* const* xs16, int nbv, float (&acc)[NB][PR]) {
+                                       const float* const* xs16, int xoff, int nbv, float (&acc)[NB][PR]) {
   constexpr uint32_t C = 0x3F800000u;
   if constexpr (FMT == Q4_K) {
     const uint4 h = lds128(blk);
@@ -569,8 +576,9 @@ __device__ __forceinline__ void blk_nb(const uint8_t* blk, int e0, int cols, con
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
         if (j < nbv) {
-          xlo[j] = __ldg(xs16[j] + col / 16) + __ldg(xs16[j] + col / 16 + 1);
-          xhi[j] = __ldg(xs16[j] + col / 16 + 2) + __ldg(xs16[j] + col / 16 + 3);
+          const float* q = xs16[j] + (col - xoff) / 16;
+          xlo[j] = q[0] + q[1];
+          xhi[j] = q[2] + q[3];
         } else {
           xlo[j] = xhi[j] = 0.f;
         }
@@ -590,8 +598,8 @@ __device__ __forceinline__ void blk_nb(const uint8_t* blk, int e0, int cols, con
 #pragma unroll
         for (int j = 0; j < NB; ++j) {
           if (j < nbv) {
-            const float4 xl = __ldg(reinterpret_cast<const float4*>(xr[j] + col) + k);
-            const float4 xh = __ldg(reinterpret_cast<const float4*>(xr[j] + col + 32) + k);
+            const float4 xl = lds_f4(xr[j] + (col - xoff) + 4 * k);
+            const float4 xh = lds_f4(xr[j] + (col - xoff) + 32 + 4 * k);
             alo[j] = __ffma2_rn(l01, f2(xl.x, xl.y), alo[j]);
             alo[j] = __ffma2_rn(l23, f2(xl.z, xl.w), alo[j]);
             ahi[j] = __ffma2_rn(h01, f2(xh.x, xh.y), ahi[j]);
@@ -634,7 +642,7 @@ __device__ __forceinline__ void blk_nb(const uint8_t* blk, int e0, int cols, con
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
         if (j < nbv) {
-          const float4 xv = __ldg(reinterpret_cast<const float4*>(xr[j] + col) + k);
+          const float4 xv = lds_f4(xr[j] + (col - xoff) + 4 * k);
           s[j] = __ffma2_rn(q01, f2(xv.x, xv.y), s[j]);
           s[j] = __ffma2_rn(q23, f2(xv.z, xv.w), s[j]);
         }
@@ -676,7 +684,7 @@ __device__ __forceinline__ void blk_nb(const uint8_t* blk, int e0, int cols, con
           float xsum[NB];
 #pragma unroll
           for (int j = 0; j < NB; ++j) {
-            xsum[j] = j < nbv ? __ldg(xs16[j] + col / 16) : 0.f;
+            xsum[j] = j < nbv ? xs16[j][(col - xoff) / 16] : 0.f;
             a4[j] = f2(-xsum[j], 0.f);
           }
 #pragma unroll
@@ -692,7 +700,7 @@ __device__ __forceinline__ void blk_nb(const uint8_t* blk, int e0, int cols, con
 #pragma unroll
             for (int j = 0; j < NB; ++j) {
               if (j < nbv) {
-                const float4 xv = __ldg(reinterpret_cast<const float4*>(xr[j] + col) + k);
+                const float4 xv = lds_f4(xr[j] + (col - xoff) + 4 * k);
                 a4[j] = __ffma2_rn(f01, f2(xv.x, xv.y), a4[j]);
                 a4[j] = __ffma2_rn(f23, f2(xv.z, xv.w), a4[j]);
               }
@@ -721,10 +729,11 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, W = blockDim.x >> 5;
   const int NS = a.ns;
   uint8_t* ring = smem + 8 * (kMaxExperts + 8) + 128 * ((W * NS * 8 + 127) / 128);
-  const size_t stage_bytes = (size_t)SLOTS * a.pitch;
+  const size_t stage_bytes = (size_t)a.stage_bytes;
   uint64_t* mybars = bars + warp * NS;
   uint8_t* myring = ring + (size_t)warp * NS * stage_bytes;
   const int rs = lane % RPW, half = lane / RPW;
+  (void)SLOTS;
 
   if (threadIdx.x < W * NS) mbar_init(&bars[threadIdx.x], 1);
   if (threadIdx.x == 0) fence_barrier_init();
@@ -777,9 +786,27 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
     const long long row = GATEUP ? (long long)(half ? a.ff + v : v) : (long long)v;
     return (eb + row * blk_row) * TS;
   };
+  // lane j < NB: slot of token j of the item at the issue pointer (-1: none)
+  int islot = -1;
+  auto item_slot = [&](const Item& it) {
+    const int p0 = a.offsets[it.e] + it.k * NB;
+    const int n = min(NB, a.offsets[it.e + 1] - p0);
+    return lane < n ? a.perm[p0 + lane] : -1;
+  };
   auto issue = [&](const Item& it, int c, int slot) {
     uint64_t* bar = &mybars[slot];
     uint32_t mine = 0;
+    if (lane < NB && islot >= 0) {
+      // this token's activations for the stage (and their per-16 sums)
+      uint8_t* st = myring + (size_t)slot * stage_bytes;
+      const int row = GATEUP ? islot / a.n_used : islot;
+      const int col0 = GATEUP ? c * a.cb * BS : 0;
+      const int ncols = GATEUP ? min(a.cb * BS, a.cols - col0) : a.cols;
+      bulk_g2s(st + a.x_at + (size_t)lane * a.xcols * 4, a.act + (size_t)row * a.cols + col0, (uint32_t)ncols * 4u, bar);
+      const uint32_t sb = (uint32_t)(((ncols / 16) * 4 + 15) & ~15);
+      bulk_g2s(st + a.xs_at + (size_t)lane * a.xs16n * 4, a.act_s16 + (size_t)row * (a.cols / 16) + col0 / 16, sb, bar);
+      mine += (uint32_t)ncols * 4u + sb;
+    }
     if (GATEUP || half == 0) {
       bool ok;
       const long long rstart = row_start(it, ok);
@@ -789,36 +816,58 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
         const long long a0 = start & ~15ll, a1 = (start + len + 15) & ~15ll;
         const int slot_row = GATEUP ? half * RPW + rs : rs;
         bulk_g2s(myring + (size_t)slot * stage_bytes + (size_t)slot_row * a.pitch, a.w + a0, (uint32_t)(a1 - a0), bar);
-        mine = (uint32_t)(a1 - a0);
+        mine += (uint32_t)(a1 - a0);
       }
     }
     const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
     if (lane == 0) mbar_arrive_expect_tx(bar, total);
   };
 
-  const int gw = blockIdx.x * W + warp, GW = gridDim.x * W;
+  // split == 1: warp-owned items gw, gw+GW, ..., each with all its chunks.
+  // split  > 1: item blockIdx.x; warp w takes chunks w, w+W, ...
+  const bool split = a.split > 1;
+  const int gw = split ? (int)blockIdx.x : (int)blockIdx.x * W + warp;
+  const int GW = split ? n_items : (int)gridDim.x * W;  // split: a single item
+  const int c0 = split ? warp : 0, cstep = split ? W : 1;
   bool okw = true;
   int issued = 0, consumed = 0;
-  int ii = gw, ci = 0;  // issue pointer (item, chunk)
+  int ii = gw, ci = c0;  // issue pointer (item, chunk)
+  if (ci >= a.nchunks) ii = n_items;  // split: more warps than chunks
   Item iti = ii < n_items ? locate(ii) : Item{0, 0, 0};
+  if (ii < n_items) islot = item_slot(iti);
   for (; issued < NS && ii < n_items; ++issued) {
     issue(iti, ci, issued);
-    if (++ci == a.nchunks) {
-      ci = 0;
+    ci += cstep;
+    if (ci >= a.nchunks) {
+      ci = c0;
       ii += GW;
-      if (ii < n_items) iti = locate(ii);
+      if (ii < n_items) {
+        iti = locate(ii);
+        islot = item_slot(iti);
+      }
     }
   }
 
   float acc[NB][PR], acc2[NB];  // acc2: up-row sums (GATEUP)
-  int item = gw, c = 0;
+  int item = (c0 < a.nchunks) ? gw : n_items, c = c0;
   Item it{};
-  const float* xr[NB];
-  const float* xs16[NB];
   int slots[NB];
   int nbv = 0;
+  if (split && gw < n_items) {  // a warp without chunks still joins the reduction
+    it = locate(gw);
+    const int p0 = a.offsets[it.e] + it.k * NB;
+    nbv = min(NB, a.offsets[it.e + 1] - p0);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      const int sj = j < nbv ? a.perm[p0 + j] : 0;
+      slots[j] = sj;
+#pragma unroll
+      for (int r = 0; r < PR; ++r) acc[j][r] = 0.f;
+      acc2[j] = 0.f;
+    }
+  }
   for (int i = 0; item < n_items; ++i) {
-    if (c == 0) {
+    if (c == c0 && !split) {
       it = locate(item);
       const int p0 = a.offsets[it.e] + it.k * NB;
       nbv = min(NB, a.offsets[it.e + 1] - p0);
@@ -826,9 +875,6 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
       for (int j = 0; j < NB; ++j) {
         const int sj = j < nbv ? a.perm[p0 + j] : 0;
         slots[j] = sj;
-        const int row = GATEUP ? sj / a.n_used : sj;
-        xr[j] = a.act + (size_t)row * a.cols;
-        xs16[j] = a.act_s16 + (size_t)row * (a.cols / 16);
 #pragma unroll
         for (int r = 0; r < PR; ++r) acc[j][r] = 0.f;
         acc2[j] = 0.f;
@@ -849,6 +895,14 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
         const int nb = (int)(min(chunk_bytes, vrow_bytes - start_c) / TS);
         const int e0 = c * a.cb * BS;
         const uint8_t* sbase = myring + (size_t)slot * stage_bytes;
+        const float* xr[NB];
+        const float* xs16[NB];
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          xr[j] = reinterpret_cast<const float*>(sbase + a.x_at) + (size_t)j * a.xcols;
+          xs16[j] = reinterpret_cast<const float*>(sbase + a.xs_at) + (size_t)j * a.xs16n;
+        }
+        const int xoff = GATEUP ? c * a.cb * BS : 0;
         if constexpr (GATEUP) {
           // both rows' segments: gate in slots [0,16), up in [16,32)
           const long long eb = (long long)cur.e * a.expert_elems / BS;
@@ -860,12 +914,12 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
             float tmp[NB][1];
 #pragma unroll
             for (int j = 0; j < NB; ++j) tmp[j][0] = 0.f;
-            blk_nb<FMT, 1, NB>(gb + b * TS, e0 + b * BS, a.cols, xr, xs16, nbv, tmp);
+            blk_nb<FMT, 1, NB>(gb + b * TS, e0 + b * BS, a.cols, xr, xs16, xoff, nbv, tmp);
 #pragma unroll
             for (int j = 0; j < NB; ++j) acc[j][0] += tmp[j][0];
 #pragma unroll
             for (int j = 0; j < NB; ++j) tmp[j][0] = 0.f;
-            blk_nb<FMT, 1, NB>(ub + b * TS, e0 + b * BS, a.cols, xr, xs16, nbv, tmp);
+            blk_nb<FMT, 1, NB>(ub + b * TS, e0 + b * BS, a.cols, xr, xs16, xoff, nbv, tmp);
 #pragma unroll
             for (int j = 0; j < NB; ++j) acc2[j] += tmp[j][0];
           }
@@ -873,7 +927,7 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
           const long long eb = (long long)cur.e * a.expert_elems / BS;
           const long long r_start = (eb + (long long)v * blk_row) * TS + start_c;
           const uint8_t* rb = sbase + (size_t)rs * a.pitch + (r_start & 15);
-          for (int b = half; b < nb; b += LPR) blk_nb<FMT, PR, NB>(rb + b * TS, e0 + b * BS, a.cols, xr, xs16, nbv, acc);
+          for (int b = half; b < nb; b += LPR) blk_nb<FMT, PR, NB>(rb + b * TS, e0 + b * BS, a.cols, xr, xs16, xoff, nbv, acc);
         }
       }
     }
@@ -883,13 +937,22 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
     if (ii < n_items) {
       issue(iti, ci, slot);
       ++issued;
-      if (++ci == a.nchunks) {
-        ci = 0;
+      ci += cstep;
+      if (ci >= a.nchunks) {
+        ci = c0;
         ii += GW;
-        if (ii < n_items) iti = locate(ii);
+        if (ii < n_items) {
+          iti = locate(ii);
+          islot = item_slot(iti);
+        }
       }
     }
-    if (++c == a.nchunks) {
+    c += cstep;
+    if (split) {
+      if (c >= a.nchunks) break;  // this warp's share of the item is done
+      continue;
+    }
+    if (c >= a.nchunks) {
       // item finished: combine the two lanes of each row, write the results
       const int v = it.g * RPW + rs;
       const bool ok = v < a.nvrows;
@@ -918,6 +981,72 @@ __global__ void __launch_bounds__(NB >= 4 ? 256 : 512) moe_rows_kernel(const __g
       }
       c = 0;
       item += GW;
+    }
+  }
+  if (split && gw < n_items) {
+    // CTA-owned item: warps hold partial sums over disjoint chunks; reduce them
+    // in shared memory in warp order, then finish as the per-warp path does.
+    float* red = reinterpret_cast<float*>(ring);  // the rings are idle now
+    constexpr int PER = GATEUP ? 2 * NB : NB * PR;
+    __syncthreads();  // every warp is done reading its ring
+    {
+      float* mine = red + ((size_t)warp * 32 + lane) * PER;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        if constexpr (GATEUP) {
+          mine[2 * j] = acc[j][0];
+          mine[2 * j + 1] = acc2[j];
+        } else {
+#pragma unroll
+          for (int r = 0; r < PR; ++r) mine[j * PR + r] = acc[j][r];
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        float t0[PR], t1 = 0.f;
+#pragma unroll
+        for (int r = 0; r < PR; ++r) t0[r] = 0.f;
+        for (int w2 = 0; w2 < W; ++w2) {
+          const float* src = red + ((size_t)w2 * 32 + lane) * PER;
+          if constexpr (GATEUP) {
+            t0[0] += src[2 * j];
+            t1 += src[2 * j + 1];
+          } else {
+#pragma unroll
+            for (int r = 0; r < PR; ++r) t0[r] += src[j * PR + r];
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < PR; ++r) acc[j][r] = t0[r];
+        acc2[j] = t1;
+      }
+      const int v = it.g * RPW + rs;
+      const bool ok = v < a.nvrows;
+      if constexpr (GATEUP) {
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          const float hg = acc[j][0] + __shfl_xor_sync(0xffffffffu, acc[j][0], 16);
+          const float hu = acc2[j] + __shfl_xor_sync(0xffffffffu, acc2[j], 16);
+          float gv = 0.f;
+          if (ok && j < nbv) gv = __fmul_rn(gelu_ref(hg), hu);
+          if (half == 0 && ok && j < nbv) a.out[(size_t)slots[j] * a.ff + v] = gv;
+          float t = (half == 0) ? gv : 0.f;
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+          if (lane == 0 && j < nbv) a.out_s16[(size_t)slots[j] * (a.ff / 16) + it.g] = t;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < NB; ++j)
+#pragma unroll
+          for (int r = 0; r < PR; ++r) {
+            const float t = acc[j][r] + __shfl_xor_sync(0xffffffffu, acc[j][r], 16);
+            if (half == 0 && ok && j < nbv) a.out[(size_t)slots[j] * a.dim + (size_t)v * PR + r] = t;
+          }
+      }
     }
   }
   if (!okw) {
@@ -1230,31 +1359,51 @@ static int launch_expert_rows(g4_ctx* c, int type, bool gu, const uint8_t* w, co
   a.nchunks = (a.bpv + a.cb - 1) / a.cb;
   a.pitch = rows_pitch(a.cb * TS + 32);
   const int slots = gu ? 32 : 16;
-  const size_t stage = (size_t)slots * a.pitch;
   const int optin = (int)c->dev.smem_optin;
   const size_t head = 8 * (kMaxExperts + 8);
   const int avg = (T * K + E - 1) / E;
-  // Wide token tiles belong to the tensor-core / generic kernels: here the
-  // activations stream through L1 once per token, which only pays for <= 2.
+  // Wide token tiles belong to the tensor-core / generic kernels: this one
+  // re-reads each token's activations per row, which only pays for <= 2.
   if (avg > 2) return -1;
   const int nb = avg >= 2 ? 2 : 1;
+  // stage = weight row slots, then each token's activations for the stage and
+  // their per-16-column sums
+  a.xcols = gu ? a.cb * BS : a.cols;
+  a.xs16n = ((a.xcols / 16) + 3) / 4 * 4;
+  a.x_at = slots * a.pitch;
+  a.xs_at = a.x_at + nb * a.xcols * 4;
+  a.stage_bytes = (int)align_up((size_t)a.xs_at + (size_t)nb * a.xs16n * 4, 128);
+  const size_t stage = (size_t)a.stage_bytes;
   // warps per CTA from the amount of work, so that every SM gets some
   const long long max_items = (long long)(std::min((long long)T * K, (long long)E) +
                                           ((long long)T * K + nb - 1) / nb) * a.ngroups;
-  int warps = (int)std::min<long long>(16, std::max<long long>(1, (max_items + c->dev.sms - 1) / c->dev.sms));
   auto need = [&](int wv, int ns) { return head + 128 * ((wv * ns * 8 + 127) / 128) + (size_t)wv * ns * stage; };
-  // deepest ring (up to 6 stages) that fits; fewer warps per SM leave room for more stages
-  a.ns = 6;
-  while (a.ns > 2 && need(warps, a.ns) > (size_t)optin) --a.ns;
-  while (warps > 1 && need(warps, a.ns) > (size_t)optin) --warps;
+  int warps;
+  // Few items (small batches): one CTA per item, its warps split the chunks,
+  // so that enough lanes stream weights at once.  Otherwise warps own items.
+  const bool split = max_items < 8LL * c->dev.sms;
+  if (split) {
+    a.split = std::min(a.nchunks, 8);
+    warps = a.split;
+    a.ns = 2;
+    while (a.ns < 4 && a.ns * a.split < a.nchunks && need(warps, a.ns + 1) <= (size_t)optin) ++a.ns;
+  } else {
+    a.split = 1;
+    warps = (int)std::min<long long>(16, std::max<long long>(1, (max_items + c->dev.sms - 1) / c->dev.sms));
+    // deepest ring (up to 6 stages) that fits; fewer warps per SM leave room for more stages
+    a.ns = 6;
+    while (a.ns > 2 && need(warps, a.ns) > (size_t)optin) --a.ns;
+    while (warps > 1 && need(warps, a.ns) > (size_t)optin) --warps;
+  }
   if (need(warps, a.ns) > (size_t)optin) return -1;
   const size_t smem = need(warps, a.ns);
   RowsFn fn = rows_fn(type, gu, pr, nb);
   if (!fn) return -1;
   const int occ = rows_occ(fn, smem, 32 * warps, optin, noalloc_path);
   if (occ < 1) return -2;
-  const int grid = (int)std::max<long long>(1, std::min<long long>((max_items + warps - 1) / warps,
-                                                                   (long long)c->dev.sms * occ));
+  const int grid = split ? (int)max_items
+                         : (int)std::max<long long>(1, std::min<long long>((max_items + warps - 1) / warps,
+                                                                           (long long)c->dev.sms * occ));
   fn<<<grid, 32 * warps, smem, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
