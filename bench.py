@@ -38,6 +38,9 @@ SHAPES = [(1536, 1536), (6144, 1536), (1536, 6144), (262144, 1536)]
 FORMATS = [("Q8_0", 8), ("Q4_K", 12), ("Q6_K", 14), ("BF16", 30)]
 METRIC = "quant GEMV HBM GB/s"
 FALLBACK_HBM = 6650.0
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
+# (profiles/gemv_rows_bf16_262144x1536.md, profiles/gemv_rows_q4k_262144x1536.md)
+MEASURED_TRAFFIC = {"BF16 262144x1536": 810.7e6, "Q4_K 262144x1536": 235.0e6}
 
 
 def log(*a):
@@ -374,7 +377,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "kernel": breakdown[dom]["case"], "achieved": round(achieved, 1),
                          "peak": hbm, "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                         "traffic": None},
+                         "traffic": MEASURED_TRAFFIC.get(breakdown[dom]["case"]) if world == 1 else None,
+                         "algorithmic_bytes": dom_bytes},
             "breakdown": breakdown,
             "clocks": clk.summary(),
             "gpu_launches": len(cases) * args.steps * (1 if world == 1 else 2),

@@ -150,9 +150,10 @@ int g4_moe_layer_host(g4_ctx *ctx, const g4_moe_weights *w, const float *x_host,
  * cudaFree can cause.  Same kernels and results as g4_moe_layer; the work
  * buffers live in one fixed array of G4_MOE_NOALLOC_SCRATCH_BYTES bytes that
  * the library image reserves on every GPU that loads it, held until exit.
- *  - A call needs 4*n_tokens*(2*dim + n_expert + 3*n_used + n_used*(ff + dim))
- *    bytes (each buffer rounded up to 256 bytes; about 135 KB per token for
- *    dim 2816, 128 experts, top-8, ff 704, so up to 61 tokens).  Larger
+ *  - A call needs 4*n_tokens*(2*dim + dim/16 + n_expert + 3*n_used
+ *    + n_used*(ff + ff/16 + dim)) + 4*(n_expert + 1) bytes (each buffer rounded
+ *    up to 256 bytes; about 138 KB per token for dim 2816, 128 experts, top-8,
+ *    ff 704, so up to 60 tokens).  Larger
  *    batches are rejected with G4_E_ARG and a message; split them.
  *  - The first call on a device resolves the array's device address; make it
  *    before any stream capture.
