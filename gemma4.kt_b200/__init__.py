@@ -13,5 +13,6 @@ from .floattensor import (  # noqa: F401
     GGMLType,
     UnsupportedOperation,
     QK_K,
+    row_shard,
 )
 from .moe import MoeLayer, topk  # noqa: F401

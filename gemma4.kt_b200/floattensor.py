@@ -71,6 +71,18 @@ def _stream_ptr(stream) -> int:
     return int(stream)
 
 
+def row_shard(rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Output rows [begin, begin + count) that `rank` of `world` owns when a
+    [rows, cols] tensor is split by output rows (one contiguous slice per GPU,
+    rank order = row order, so an all-gather of the slices is y)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    if rows % world:
+        raise ValueError(f"{rows} rows do not split evenly over {world} GPUs")
+    per = rows // world
+    return rank * per, per
+
+
 class Context:
     """One g4_ctx per CUDA device (per process / host thread)."""
 
@@ -100,6 +112,22 @@ class Context:
     def last_error(self) -> str:
         m = lib().g4_last_error(self.handle)
         return m.decode() if m else ""
+
+    @staticmethod
+    def dist_unique_id() -> bytes:
+        """A fresh NCCL unique id (G4_NCCL_ID_BYTES) for rank 0 to share."""
+        uid = (C.c_ubyte * 128)()
+        rc = lib().g4_dist_unique_id(uid)
+        if rc != 0:
+            raise G4Error(f"g4_dist_unique_id failed ({rc})")
+        return bytes(uid)
+
+    def dist_init(self, rank: int, world: int, uid: bytes) -> None:
+        """Join the NCCL communicator of `world` GPUs (one Context per GPU)."""
+        if len(uid) != 128:
+            raise ValueError("NCCL unique id must be 128 bytes")
+        buf = (C.c_ubyte * 128).from_buffer_copy(uid)
+        check(lib().g4_dist_init(self.handle, rank, world, buf), self.handle, "g4_dist_init")
 
 
 class CudaFloatTensor:
@@ -157,6 +185,18 @@ class CudaFloatTensor:
             rc = lib().g4_matmul_host(self.ctx.handle, self.handle, this_offset, x.ctypes.data_as(C.c_void_p),
                                       out.ctypes.data_as(C.c_void_p), dim0, dim1)
             check(rc, self.ctx.handle, "g4_matmul_host")
+
+    def matmul_sharded(self, that, out, rows: int, cols: int, stream=None) -> None:
+        """matmul of a row-sharded tensor (this holds rows row_shard(rows, world, rank)):
+        computes the local slice of out and all-gathers the full out[rows] on
+        every rank.  that/out are CUDA tensors; out holds all rows."""
+        if not (_is_torch(that) and _is_torch(out) and that.is_cuda and out.is_cuda):
+            raise ValueError("matmul_sharded takes CUDA tensors")
+        if that.numel() < cols or out.numel() < rows:
+            raise ValueError("activation buffers too small")
+        rc = lib().g4_matmul_sharded(self.ctx.handle, self.handle, C.c_void_p(that.data_ptr()),
+                                     C.c_void_p(out.data_ptr()), rows, cols, C.c_void_p(_stream_ptr(stream)))
+        check(rc, self.ctx.handle, "g4_matmul_sharded")
 
     def dequant(self, offset: int, n: int, out=None, stream=None):
         """[get(offset + i) for i < n] (the per-type FloatTensor.get), on the GPU."""

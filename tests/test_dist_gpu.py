@@ -1,0 +1,93 @@
+"""g4_matmul_sharded on 2 GPUs: each rank uploads its output-row slice
+(g4_tensor_upload_rows), computes it and all-gathers y over NCCL; every rank's
+y is compared with the unsharded CPU oracle (the checker) within the GEMV
+tolerance.  Needs two GPUs in one box; skipped otherwise."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import __graft_entry__
+
+g4 = __graft_entry__.load_package()
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3  # relative L2, fp32 outputs
+
+
+def _gpus() -> int:
+    import torch
+
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, cases, q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from gemma4_kt_b200 import synth
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    # gloo only carries the 128-byte NCCL id; the data path is the library's own NCCL communicator
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        torch.cuda.set_device(rank)
+        ctx = g4.Context(rank)
+        obj = [g4.Context.dist_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.dist_init(rank, world, obj[0])
+        res = []
+        for t, rows, cols, seed in cases:
+            raw, x = synth.gemv_case(t, rows, cols, seed=seed)
+            begin, per = g4.row_shard(rows, world, rank)
+            w = g4.FloatTensorFactory.create_rows(ctx, t, raw, cols, begin, per)
+            xd = torch.from_numpy(x).cuda()
+            yd = torch.full((rows,), float("nan"), device="cuda")
+            w.matmul_sharded(xd, yd, rows, cols)
+            torch.cuda.synchronize()
+            res.append(yd.cpu().numpy())
+            w.free()
+        q.put((rank, res))
+        dist.barrier()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_matmul_sharded_two_gpus():
+    import multiprocessing as mp
+
+    from gemma4_kt_b200 import synth
+    from oracle import oracle
+
+    T = g4.GGMLType
+    cases = [(T.Q4_K, 4096, 1536, 1), (T.Q8_0, 2048, 2048, 0), (T.Q6_K, 1536, 1536, 1), (T.BF16, 6144, 1536, 1)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, cases, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for i, (t, rows, cols, seed) in enumerate(cases):
+        raw, x = synth.gemv_case(t, rows, cols, seed=seed)
+        ref = oracle.matmul(int(t), raw, x, rows, cols)
+        for r in range(2):
+            y = got[r][i]
+            err = np.linalg.norm(y - ref) / np.linalg.norm(ref)
+            assert err < TOL, (t.name, r, err)
