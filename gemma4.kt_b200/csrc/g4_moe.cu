@@ -20,6 +20,7 @@
 #include "g4_ctx.h"
 #include "g4_gemv.cuh"
 #include "g4_gemv_rows.cuh"
+#include "g4_moe_tc.h"
 
 #include <algorithm>
 #include <cmath>
@@ -1501,7 +1502,11 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
   }
   if (int r = c->bind()) return r;
   cudaStream_t st = (cudaStream_t)stream;
-  size_t need = moe_scratch_bytes(T, dim, E, K, ff);
+  const size_t base_need = moe_scratch_bytes(T, dim, E, K, ff);
+  // wide batches: grouped expert products on the tensor cores (g4_moe_tc.cu)
+  const bool use_tc = moe_tc_supported(w->gate_up_exps->type, w->down_exps->type, dim, ff, E) &&
+                      moe_tc_wanted(T, K, E);
+  size_t need = base_need + (use_tc ? moe_tc_scratch_bytes(T, dim, E, K, ff) : 0);
   uint8_t* base = (uint8_t*)c->scratch(need);
   if (!base) {
     c->set_err("g4_moe_layer: cannot allocate %zu bytes of scratch", need);
@@ -1515,26 +1520,35 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
   moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, T * K, E, m.offsets, m.perm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer launch");
-  int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
-                             m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, false);
-  const bool rows_gu = r == 0;
-  if (r == -1)
-    r = launch_expert(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m, E, K,
-                      dim, ff, T, st);
-  if (r == 0) {
-    // the down rows kernel needs G's per-16-column sums, written by the gate_up rows kernel
-    r = rows_gu ? launch_expert_rows(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.G_s16,
-                                     m.D, nullptr, m, E, K, dim, ff, T, st, false)
-                : -1;
+  bool done = false;
+  if (use_tc) {
+    e = launch_moe_tc(c, (const uint8_t*)w->gate_up_exps->d, (const uint8_t*)w->down_exps->d, m.moe_in, m.offsets,
+                      m.perm, m.D, base + base_need, T, dim, E, K, ff, st);
+    if (e != cudaSuccess && e != cudaErrorNotSupported) return c->cuda_fail(e, "g4_moe_layer tensor-core launch");
+    done = e == cudaSuccess;  // cudaErrorNotSupported: the driver cannot encode tensor maps; CUDA-core kernels follow
+  }
+  if (!done) {
+    int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
+                               m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, false);
+    const bool rows_gu = r == 0;
     if (r == -1)
-      r = launch_expert(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K, dim, ff,
-                        T, st);
+      r = launch_expert(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m, E, K,
+                        dim, ff, T, st);
+    if (r == 0) {
+      // the down rows kernel needs G's per-16-column sums, written by the gate_up rows kernel
+      r = rows_gu ? launch_expert_rows(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.G_s16,
+                                       m.D, nullptr, m, E, K, dim, ff, T, st, false)
+                  : -1;
+      if (r == -1)
+        r = launch_expert(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.D, m, E, K, dim, ff,
+                          T, st);
+    }
+    if (r == -1) {
+      c->set_err("g4_moe_layer: expert tensor layout not supported by the grouped kernels");
+      return G4_E_ARG;
+    }
+    if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer expert launch");
   }
-  if (r == -1) {
-    c->set_err("g4_moe_layer: expert tensor layout not supported by the grouped kernels");
-    return G4_E_ARG;
-  }
-  if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer expert launch");
   moe_combine_kernel<<<T, 512, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
                                         w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr, out, dim,
                                         K, w->eps);

@@ -1,0 +1,638 @@
+// g4_moe_tc.cu -- the grouped expert products of the MoE block on the
+// 5th-generation tensor cores (tcgen05), for token batches wide enough that
+// the experts' weight tiles are reused across many tokens.
+//
+// The arithmetic is the expert block of Llama.forward (Llama.kt:297-337):
+//   gate_up = W_gu[e] · moeInput   (rows 0..ff-1 gate, ff..2ff-1 up; Llama.kt:305-313)
+//   g       = gelu(gate) * up      (Llama.kt:316-322)
+//   down    = W_d[e] · g           (Llama.kt:325-332)
+// for every routed slot, grouped by expert.  The weights stay in their GGUF
+// Q4_K blocks in HBM and are dequantized inside the kernel (q*d*sc - dmin*m
+// evaluated in fp32, Q4_KFloatTensor.kt:23-55, then rounded once to fp16);
+// activations enter the tensor cores as fp16; products accumulate in fp32
+// in tensor memory.  The result differs from the fp32 reference by the fp16
+// rounding of weights and activations (about 3e-4 relative L2 per product).
+//
+// One persistent CTA per SM, warp-specialised:
+//   warp 0        allocates tensor memory; lane 0 issues tcgen05.mma
+//                 (M = 128 weight rows, N = tokens, K = 16) into one of two
+//                 accumulators, so the epilogue of one tile overlaps the
+//                 main loop of the next;
+//   warp 1        lane 0 loads token tiles [N x 64] fp16 with TMA (128-byte
+//                 swizzle) from the expert-sorted activation matrix;
+//   warps 2..9    dequantize the 128 x 64 weight tile of each stage into
+//                 shared memory in the same swizzled K-major layout;
+//   warps 10..13  read the accumulator (tcgen05.ld) and write the outputs:
+//                 gelu(gate)*up as fp16 rows of G (gate_up), or fp32 rows of
+//                 D by slot (down).
+// Every wait is bounded (kWaitLimitNs) and reports through the status word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "g4_common.cuh"
+#include "g4_moe_tc.h"
+
+namespace g4 {
+namespace {
+
+constexpr int kTileM = 128;                                 // weight rows per tile (MMA M)
+constexpr int kKB = 64;                                     // K per pipeline stage: one 128-byte fp16 row
+constexpr int kMmaK = 16;                                   // K of one kind::f16 MMA
+constexpr int kProdWarps = 8;                               // dequantizing warps
+constexpr int kEpiWarps = 4;                                // epilogue warps (one per TMEM lane quarter)
+constexpr int kThreads = 32 * (2 + kProdWarps + kEpiWarps);  // 448
+constexpr int kMaxStages = 8;
+constexpr int kNumBoxes = 5;                                // token-tile heights 16, 32, 64, 128, 256
+constexpr int kATile = kTileM * kKB * 2;                    // 16 KB of fp16
+constexpr int kBarBytes = 512;
+constexpr int kMaxExpertsTc = 256;
+
+struct TcArgs {
+  const uint8_t* w;        // expert weights, Q4_K block stream
+  long long expert_elems;  // elements of one expert's matrix
+  int cols;                // K of the product
+  int ff;                  // gate_up: rows of each half
+  int out_ld;              // row length of the output (ff for G, dim for D)
+  int n_row_tiles;         // tiles of 128 rows per expert (pairs of 64 gate/up rows for gate_up)
+  int nkb;                 // cols / 64
+  int stages;
+  int b_stage_bytes;       // token-tile cap * 128
+  int acc_cols;            // tensor-memory columns per accumulator (= token-tile cap)
+  uint32_t tmem_cols;      // allocated columns (2 accumulators)
+  const int4* tiles;       // {expert, first sorted position, tokens, box index}
+  const int32_t* n_tiles;
+  const int32_t* perm;     // sorted position -> slot
+  __half* g16;             // gate_up output [sorted position][ff]
+  float* D;                // down output [slot][dim]
+  unsigned* status;
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Arrive on bar once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (start >> 4 | LBO 16 B | SBO 1024 B | version 1 | SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
+  const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+  return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor of kind::f16: fp32 accumulate, fp16 A and B, both K-major, M = 128.
+__device__ __forceinline__ uint32_t idesc_f16(uint32_t n) {
+  return (1u << 4) | ((n >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 consecutive accumulator columns of this warp's 32 lanes (one row per
+// lane), waited for inside the same statement.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Bounded wait that also gives up as soon as another role of the CTA has
+// given up (abort flag in shared memory).  On its own timeout it raises the
+// flag and records `bit` in the status word.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* status,
+                                        unsigned bit) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        record_error(status, bit);
+        return false;
+      }
+    }
+  }
+}
+// Short bounded wait used only while draining after an abort.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - t0 > 50000000ull) break;
+}
+
+__device__ __forceinline__ float gelu_f(float x) {
+  // Llama.kt:23-25 (evaluated in float: the result is rounded to fp16 next)
+  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
+// Byte k (0..11) of the 12 scale bytes held in three words.
+__device__ __forceinline__ uint32_t scale_byte(uint32_t s0, uint32_t s1, uint32_t s2, int k) {
+  const uint32_t w = k < 4 ? s0 : k < 8 ? s1 : s2;
+  return (w >> (8 * (k & 3))) & 0xFFu;
+}
+
+// Four fp16 weights from one word of Q4_K codes: the low (mask 0x000F000F) or
+// high (mask 0x00F000F0) nibbles of bytes 0..3, each mapped to 1024 + code
+// (or 1024 + 16*code) as an fp16 bit pattern, widened to fp32 exactly, then
+// w = code*scale - min in fp32 (mult and c carry the 1024 offset and the 1/16
+// of the high nibble), rounded once to fp16.  Returns K positions 0,1 | 2,3.
+__device__ __forceinline__ uint2 q4_word_to_f16(uint32_t x, uint32_t mask, float2 mult, float2 c) {
+  const uint32_t a02 = (x & mask) | 0x64006400u;         // bytes 0 and 2
+  const uint32_t a13 = ((x >> 8) & mask) | 0x64006400u;  // bytes 1 and 3
+  const float2 f02 = __half22float2(*reinterpret_cast<const __half2*>(&a02));
+  const float2 f13 = __half22float2(*reinterpret_cast<const __half2*>(&a13));
+  const float2 w02 = __ffma2_rn(f02, mult, c);
+  const float2 w13 = __ffma2_rn(f13, mult, c);
+  const __half2 h01 = __floats2half2_rn(w02.x, w13.x);
+  const __half2 h23 = __floats2half2_rn(w02.y, w13.y);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+}
+
+// ---------------------------------------------------------------- kernels
+// Token tiles per expert: at most `cap` tokens each, balanced, heights rounded
+// up to 16 (the MMA's N granule).  One CTA of 256 threads (E <= 256).
+__global__ void __launch_bounds__(256) moe_tc_tiles_kernel(const int32_t* __restrict__ offsets, int E, int cap,
+                                                           int4* __restrict__ tiles, int32_t* __restrict__ n_tiles) {
+  __shared__ int cnt[kMaxExpertsTc];
+  const int e = threadIdx.x;
+  int ne = 0, nt = 0, tn = 0;
+  if (e < E) {
+    ne = offsets[e + 1] - offsets[e];
+    if (ne > 0) {
+      const int nt0 = (ne + cap - 1) / cap;
+      tn = (((ne + nt0 - 1) / nt0) + 15) & ~15;
+      nt = (ne + tn - 1) / tn;
+    }
+  }
+  cnt[e] = nt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int i = 0; i < (int)blockDim.x; ++i) {
+      const int v = cnt[i];
+      cnt[i] = acc;
+      acc += v;
+    }
+    *n_tiles = acc;
+  }
+  __syncthreads();
+  const int base = cnt[e];
+  for (int i = 0; i < nt; ++i) {
+    const int start = i * tn, n = min(tn, ne - start), N = (n + 15) & ~15;
+    const int box = N <= 16 ? 0 : N <= 32 ? 1 : N <= 64 ? 2 : N <= 128 ? 3 : 4;
+    tiles[base + i] = make_int4(e, offsets[e] + start, n, box);
+  }
+}
+
+// x16[p][:] = fp16(moe_in[token of slot perm[p]][:]), one warp per sorted position.
+__global__ void __launch_bounds__(256) moe_tc_gather_kernel(const float* __restrict__ moe_in,
+                                                            const int32_t* __restrict__ perm,
+                                                            __half* __restrict__ x16, int n_pos, int dim, int K) {
+  const int p = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (p >= n_pos) return;
+  const int tok = perm[p] / K;
+  const float4* src = reinterpret_cast<const float4*>(moe_in + (size_t)tok * dim);
+  uint2* dst = reinterpret_cast<uint2*>(x16 + (size_t)p * dim);
+  for (int i = lane; i < dim / 4; i += 32) {
+    const float4 v = __ldg(src + i);
+    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    dst[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  }
+}
+
+template <bool GATEUP>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_tc_kernel(const __grid_constant__ TcArgs a, const __grid_constant__ CUtensorMap m0,
+                  const __grid_constant__ CUtensorMap m1, const __grid_constant__ CUtensorMap m2,
+                  const __grid_constant__ CUtensorMap m3, const __grid_constant__ CUtensorMap m4) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  uint8_t* a_st = sm;                                   // S x [128 rows x 128 B]
+  uint8_t* b_st = sm + (size_t)S * kATile;              // S x [cap rows x 128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_st + (size_t)S * a.b_stage_bytes);
+  uint64_t* full_a = bars;                              // producers -> MMA  (count 8)
+  uint64_t* full_b = bars + kMaxStages;                 // TMA -> MMA        (count 1 + bytes)
+  uint64_t* empty = bars + 2 * kMaxStages;              // MMA -> producers  (tcgen05.commit)
+  uint64_t* tfull = bars + 3 * kMaxStages;              // MMA -> epilogue   [2]
+  uint64_t* tempty = tfull + 2;                         // epilogue -> MMA   [2] (count 4)
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_a[s], kProdWarps);
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, a.tmem_cols);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int R = a.n_row_tiles, nkb = a.nkb;
+  const int n_items = *a.n_tiles * R;
+
+  if (warp == 0) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, acc = 0, aph = 0;
+      bool issued = false, ok = true;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        const int4 tl = a.tiles[item / R];
+        const uint32_t idesc = idesc_f16((uint32_t)((tl.z + 15) & ~15));
+        if (!tc_wait(&tempty[acc], aph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * (uint32_t)a.acc_cols;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!tc_wait(&full_a[s], ph, abort_flag, a.status, ERR_TIMEOUT_FULL) ||
+              !tc_wait(&full_b[s], ph, abort_flag, a.status, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(a_st + (size_t)s * kATile);
+          const uint64_t bd = sw128_desc(b_st + (size_t)s * a.b_stage_bytes);
+#pragma unroll
+          for (int kk = 0; kk < kKB / kMmaK; ++kk)  // +32 bytes of K per step, inside the swizzle row
+            tc_mma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+          issued = true;
+          tc_commit(&empty[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        acc ^= 1u;
+        if (acc == 0) aph ^= 1u;
+      }
+      if (!ok && issued) {  // let every issued MMA finish before tensor memory is released
+        tc_commit(drain);
+        drain_wait(drain, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ TMA producer (token tiles)
+    if (lane == 0) {
+      int s = 0, n_issued = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        const int4 tl = a.tiles[item / R];
+        const CUtensorMap* map = tl.w == 0 ? &m0 : tl.w == 1 ? &m1 : tl.w == 2 ? &m2 : tl.w == 3 ? &m3 : &m4;
+        const uint32_t bytes = (16u << tl.w) * 128u;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!tc_wait(&empty[s], ph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_b[s], bytes);
+          tma_load_2d(b_st + (size_t)s * a.b_stage_bytes, map, kb * kKB, tl.y, &full_b[s]);
+          ++n_issued;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {  // wait for this thread's copies still in flight (the last S at most)
+        int ss = s;
+        uint32_t pp = ph;
+        for (int i = 0; i < S && i < n_issued; ++i) {
+          if (--ss < 0) {
+            ss = S - 1;
+            pp ^= 1u;
+          }
+          drain_wait(&full_b[ss], pp);
+        }
+      }
+    }
+  } else if (warp < 2 + kProdWarps) {
+    // ------------------------------------------------ dequantizing producers
+    // Thread pt: A-tile row t = pt / 2, half h = pt % 2 (h = 0: low nibbles ->
+    // K 0..31 of the stage, chunks 0..3; h = 1: high nibbles -> K 32..63,
+    // chunks 4..7).  Chunk c of row t sits at (t/8)*1024 + (t%8)*128 +
+    // ((c ^ t%8) * 16): the 128-byte swizzle the MMA descriptors name.
+    const int pt = threadIdx.x - 64, t = pt >> 1, h = pt & 1;
+    const uint32_t mask = h ? 0x00F000F0u : 0x000F000Fu;
+    const uint32_t row_off = (uint32_t)(t >> 3) * 1024u + (uint32_t)(t & 7) * 128u;
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+      const int4 tl = a.tiles[item / R];
+      const int rt = item % R;
+      const long long wr = GATEUP ? (long long)((t & 1) ? a.ff : 0) + 64ll * rt + (t >> 1)
+                                  : (long long)kTileM * rt + t;
+      const long long e0 = (long long)tl.x * a.expert_elems + wr * a.cols;
+      // one 64-element group of a super-block per stage: header + 32 code bytes
+      auto blk_of = [&](int kb) { return a.w + (size_t)((e0 + (long long)kb * kKB) >> 8) * 144; };
+      auto grp_of = [&](int kb) { return (int)(((e0 + (long long)kb * kKB) >> 6) & 3); };
+      const uint8_t* b0 = blk_of(0);
+      int g0 = grp_of(0);
+      uint4 hd = __ldg(reinterpret_cast<const uint4*>(b0));
+      uint4 q0 = __ldg(reinterpret_cast<const uint4*>(b0 + 16 + 32 * g0));
+      uint4 q1 = __ldg(reinterpret_cast<const uint4*>(b0 + 32 + 32 * g0));
+      for (int kb = 0; kb < nkb; ++kb) {
+        const uint4 chd = hd, cq0 = q0, cq1 = q1;
+        const int g = g0;
+        if (kb + 1 < nkb) {  // prefetch the next stage's bytes
+          const uint8_t* bn = blk_of(kb + 1);
+          g0 = grp_of(kb + 1);
+          hd = __ldg(reinterpret_cast<const uint4*>(bn));
+          q0 = __ldg(reinterpret_cast<const uint4*>(bn + 16 + 32 * g0));
+          q1 = __ldg(reinterpret_cast<const uint4*>(bn + 32 + 32 * g0));
+        }
+        // getScaleMinK4 (Q4_KFloatTensor.kt:70-84) for sub-block j = 2g + h
+        const int j = 2 * g + h;
+        uint32_t sc, mn;
+        if (j < 4) {
+          sc = scale_byte(chd.y, chd.z, chd.w, j) & 63u;
+          mn = scale_byte(chd.y, chd.z, chd.w, j + 4) & 63u;
+        } else {
+          const uint32_t bj4 = scale_byte(chd.y, chd.z, chd.w, j + 4);
+          sc = (bj4 & 0xFu) | ((scale_byte(chd.y, chd.z, chd.w, j - 4) >> 6) << 4);
+          mn = (bj4 >> 4) | ((scale_byte(chd.y, chd.z, chd.w, j) >> 6) << 4);
+        }
+        const float d = f16_bits_to_f32((uint16_t)(chd.x & 0xFFFFu));
+        const float dmin = f16_bits_to_f32((uint16_t)(chd.x >> 16));
+        const float sf = d * (float)sc;     // exact: 11-bit by 6-bit product
+        const float mf = dmin * (float)mn;  // exact
+        const float mult = h ? sf * 0.0625f : sf;
+        const float cc = -fmaf(1024.f, mult, mf);
+        const float2 m2 = make_float2(mult, mult), c2 = make_float2(cc, cc);
+        uint4 ch[4];
+        const uint32_t qw[8] = {cq0.x, cq0.y, cq0.z, cq0.w, cq1.x, cq1.y, cq1.z, cq1.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint2 lo = q4_word_to_f16(qw[2 * i], mask, m2, c2);
+          const uint2 hi = q4_word_to_f16(qw[2 * i + 1], mask, m2, c2);
+          ch[i] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        // every lane waits; the verdict is made warp-uniform so the warp never splits
+        if (!__all_sync(0xffffffffu, tc_wait(&empty[s], ph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY))) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = a_st + (size_t)s * kATile + row_off;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t c = (uint32_t)(i + 4 * h);
+          *reinterpret_cast<uint4*>(dst + ((c ^ (uint32_t)(t & 7)) << 4)) = ch[i];
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue
+    const int q = warp & 3;  // tensor-memory lane quarter this warp may access
+    uint32_t acc = 0, aph = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const int4 tl = a.tiles[item / R];
+      const int rt = item % R, n = tl.z, p0 = tl.y;
+      if (!__all_sync(0xffffffffu, tc_wait(&tfull[acc], aph, abort_flag, a.status, ERR_TIMEOUT_FULL))) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + ((uint32_t)(32 * q) << 16) + acc * (uint32_t)a.acc_cols;
+      for (int c0 = 0; c0 < n; c0 += 32) {
+        float v[32];
+        tmem_ld32(tb + (uint32_t)c0, v);
+        if (GATEUP) {
+          // lanes 2i / 2i+1 hold gate / up row of pair 16q + i
+          const int col = 64 * rt + 16 * q + (lane >> 1);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const float u = __shfl_xor_sync(0xffffffffu, v[jj], 1);
+            if (!(lane & 1) && c0 + jj < n)
+              a.g16[(size_t)(p0 + c0 + jj) * a.out_ld + col] = __float2half_rn(gelu_f(v[jj]) * u);
+          }
+        } else {
+          const int my_slot = (c0 + lane < n) ? a.perm[p0 + c0 + lane] : 0;
+          const int row = kTileM * rt + 32 * q + lane;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int sl = __shfl_sync(0xffffffffu, my_slot, jj);
+            if (c0 + jj < n) a.D[(size_t)sl * a.out_ld + row] = v[jj];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1u;
+      if (acc == 0) aph ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// [rows][cols] fp16, row-major; box = 64 columns x box_rows rows, 128-byte swizzle.
+bool make_map(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+              uint32_t box_rows) {
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kKB, box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+struct TcWork {
+  __half *x16, *g16;
+  int4* tiles;
+  int32_t* n_tiles;
+};
+
+TcWork carve_tc(void* base, int T, int dim, int E, int K, int ff) {
+  TcWork w;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  const size_t n_pos = (size_t)T * K;
+  w.x16 = reinterpret_cast<__half*>(p);
+  p += al256(n_pos * dim * 2);
+  w.g16 = reinterpret_cast<__half*>(p);
+  p += al256(n_pos * ff * 2);
+  w.tiles = reinterpret_cast<int4*>(p);
+  p += al256((n_pos / 16 + E + 1) * sizeof(int4));
+  w.n_tiles = reinterpret_cast<int32_t*>(p);
+  return w;
+}
+
+int token_cap(int T, int K, int E) {
+  const long long avg = (long long)T * K / E;
+  return avg >= 128 ? 256 : avg >= 48 ? 128 : avg >= 12 ? 64 : 32;
+}
+
+}  // namespace
+
+size_t moe_tc_scratch_bytes(int T, int dim, int E, int K, int ff) {
+  const size_t n_pos = (size_t)T * K;
+  return al256(n_pos * dim * 2) + al256(n_pos * ff * 2) + al256((n_pos / 16 + E + 1) * sizeof(int4)) + 256;
+}
+
+bool moe_tc_supported(int gate_up_type, int down_type, int dim, int ff, int E) {
+  return gate_up_type == Q4_K && down_type == Q4_K && dim % kTileM == 0 && ff % kKB == 0 && dim % 256 == 0 &&
+         E <= kMaxExpertsTc;
+}
+
+bool moe_tc_wanted(int T, int K, int E) {
+  const char* env = std::getenv("G4_MOE_TC");
+  if (env && env[0] == '0') return false;
+  if (env && env[0] == '1') return true;
+  return (long long)T * K >= 4ll * E;  // four or more tokens per expert on average
+}
+
+cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* down_w, const float* moe_in,
+                          const int32_t* offsets, const int32_t* perm, float* D, void* work, int T, int dim, int E,
+                          int K, int ff, cudaStream_t st) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const int n_pos = T * K;
+  TcWork w = carve_tc(work, T, dim, E, K, ff);
+  const int cap = token_cap(T, K, E);
+
+  moe_tc_tiles_kernel<<<1, kMaxExpertsTc, 0, st>>>(offsets, E, cap, w.tiles, w.n_tiles);
+  moe_tc_gather_kernel<<<(n_pos + 7) / 8, 256, 0, st>>>(moe_in, perm, w.x16, n_pos, dim, K);
+
+  CUtensorMap mx[kNumBoxes], mg[kNumBoxes];
+  for (int b = 0; b < kNumBoxes; ++b) {
+    if (!make_map(enc, &mx[b], w.x16, (uint64_t)n_pos, (uint64_t)dim, 16u << b) ||
+        !make_map(enc, &mg[b], w.g16, (uint64_t)n_pos, (uint64_t)ff, 16u << b))
+      return cudaErrorInvalidValue;
+  }
+  const int b_stage = cap * 128;
+  const size_t optin = c->dev.smem_optin;
+  int stages = (int)((optin - 1024 - kBarBytes) / (size_t)(kATile + b_stage));
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2) return cudaErrorInvalidConfiguration;
+  const size_t smem = 1024 + (size_t)stages * (kATile + b_stage) + kBarBytes;
+
+  TcArgs ga{};
+  ga.w = gate_up_w;
+  ga.expert_elems = 2ll * ff * dim;
+  ga.cols = dim;
+  ga.ff = ff;
+  ga.out_ld = ff;
+  ga.n_row_tiles = ff / 64;
+  ga.nkb = dim / kKB;
+  ga.stages = stages;
+  ga.b_stage_bytes = b_stage;
+  ga.acc_cols = cap;
+  ga.tmem_cols = 2u * (uint32_t)cap;
+  ga.tiles = w.tiles;
+  ga.n_tiles = w.n_tiles;
+  ga.perm = perm;
+  ga.g16 = w.g16;
+  ga.D = nullptr;
+  ga.status = c->status;
+
+  TcArgs da = ga;
+  da.w = down_w;
+  da.expert_elems = (long long)dim * ff;
+  da.cols = ff;
+  da.out_ld = dim;
+  da.n_row_tiles = dim / kTileM;
+  da.nkb = ff / kKB;
+  da.g16 = nullptr;
+  da.D = D;
+
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(moe_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+          cudaSuccess ||
+      (e = cudaFuncSetAttribute(moe_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+          cudaSuccess)
+    return e;
+  const int grid = c->dev.sms;
+  moe_tc_kernel<true><<<grid, kThreads, smem, st>>>(ga, mx[0], mx[1], mx[2], mx[3], mx[4]);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  moe_tc_kernel<false><<<grid, kThreads, smem, st>>>(da, mg[0], mg[1], mg[2], mg[3], mg[4]);
+  return cudaGetLastError();
+}
+
+}  // namespace g4
