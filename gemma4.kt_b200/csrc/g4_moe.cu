@@ -138,53 +138,116 @@ __global__ void __launch_bounds__(256) moe_router_small_kernel(const float* __re
   }
 }
 
-// Many tokens: 64 tokens x 64 experts per CTA, K in shared-memory tiles of 32,
-// each thread a 4x4 block of outputs.
-__global__ void __launch_bounds__(256) moe_router_tiled_kernel(const float* __restrict__ wr,
-                                                               const float* __restrict__ xr, float* __restrict__ logits,
-                                                               int T, int dim, int n_expert) {
-  __shared__ float xs[32][64 + 4];
-  __shared__ float ws[32][64 + 4];
-  const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < dim; k0 += 32) {
-    for (int i = threadIdx.x; i < 64 * 32; i += 256) {
-      const int r = i >> 5, k = i & 31;
-      xs[k][r] = (t0 + r < T && k0 + k < dim) ? xr[(size_t)(t0 + r) * dim + k0 + k] : 0.f;
-      ws[k][r] = (e0 + r < n_expert && k0 + k < dim) ? wr[(size_t)(e0 + r) * dim + k0 + k] : 0.f;
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a[i] = xs[k][ty * 4 + i];
-        b[i] = ws[k][tx * 4 + i];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
+// Many tokens: register-tiled fp32 GEMM.  A CTA (128 threads) computes 64
+// tokens x 128 experts over one K range of a split-K partition; thread
+// (ty, tx) = (tid / 16, tid % 16) holds tokens {4ty..4ty+3, 32+4ty..} x
+// experts {4tx..4tx+3, 64+4tx..}, so every shared-memory read is a
+// conflict-free 16-byte vector (64 FMAs per 4 reads).  K advances in tiles
+// of 32 staged through registers (coalesced global loads, transposed into
+// k-major shared rows).  Partial sums go to part[split][T][E]; the top-k
+// kernel adds the splits in order.
+constexpr int kRtM = 64, kRtN = 128, kRtK = 32, kRtMaxSplit = 32;
+__global__ void __launch_bounds__(128) moe_router_gemm_kernel(const float* __restrict__ wr,
+                                                              const float* __restrict__ xr, float* __restrict__ part,
+                                                              int T, int dim, int E, int nsplit) {
+  __shared__ __align__(16) float xs[kRtK][kRtM + 4];
+  __shared__ __align__(16) float ws[kRtK][kRtN + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int t0 = blockIdx.x * kRtM, e0 = blockIdx.z * kRtN, split = blockIdx.y;
+  const int nk = (dim + kRtK - 1) / kRtK;
+  const int kt0 = (int)((long long)nk * split / nsplit), kt1 = (int)((long long)nk * (split + 1) / nsplit);
+  // loads: float4 number i = tid + 128j; row i / 8, columns 4*(i % 8) of the k tile
+  float4 xv[4], wv[8];
+  auto load = [&](int kt) {
+    const int kb = kt * kRtK + 4 * (tid & 7);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int t = t0 + ty * 4 + i, e = e0 + tx * 4 + j;
-      if (t < T && e < n_expert) logits[(size_t)t * n_expert + e] = acc[i][j];
+      const int r = t0 + ((tid + 128 * j) >> 3);
+      xv[j] = (r < T && kb < dim) ? __ldg(reinterpret_cast<const float4*>(xr + (size_t)r * dim + kb))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + ((tid + 128 * j) >> 3);
+      wv[j] = (e < E && kb < dim) ? __ldg(reinterpret_cast<const float4*>(wr + (size_t)e * dim + kb))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto store = [&]() {
+    const int k = 4 * (tid & 7);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = (tid + 128 * j) >> 3;
+      xs[k][r] = xv[j].x;
+      xs[k + 1][r] = xv[j].y;
+      xs[k + 2][r] = xv[j].z;
+      xs[k + 3][r] = xv[j].w;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = (tid + 128 * j) >> 3;
+      ws[k][e] = wv[j].x;
+      ws[k + 1][e] = wv[j].y;
+      ws[k + 2][e] = wv[j].z;
+      ws[k + 3][e] = wv[j].w;
+    }
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  if (kt0 < kt1) load(kt0);
+  for (int kt = kt0; kt < kt1; ++kt) {
+    __syncthreads();  // the previous tile's reads are done
+    store();
+    __syncthreads();
+    if (kt + 1 < kt1) load(kt + 1);
+#pragma unroll 4
+    for (int k = 0; k < kRtK; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&xs[k][4 * ty]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&xs[k][32 + 4 * ty]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&ws[k][4 * tx]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&ws[k][64 + 4 * tx]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+  }
+  float* out = part + (size_t)split * T * E;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t = t0 + (i < 4 ? 4 * ty + i : 32 + 4 * ty + i - 4);
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + (j < 4 ? 4 * tx + j : 64 + 4 * tx + j - 4);
+      if (e < E) out[(size_t)t * E + e] = acc[i][j];
+    }
+  }
 }
 
-static void launch_router(const float* wr, const float* xr, float* logits, int T, int dim, int E, cudaStream_t st) {
-  if (T <= 512) {
+// Router logits for T tokens.  Returns the number of K splits written to
+// `part` ([nsplit][T][E]; the caller sums them in order), or 0 when the
+// logits went straight to `logits`.  part needs nsplit*T*E floats, at most
+// kRtMaxSplit*T*E.
+static int launch_router(const float* wr, const float* xr, float* logits, float* part, int T, int dim, int E,
+                         int sms, cudaStream_t st) {
+  if (T < 32) {
     moe_router_small_kernel<<<dim3(E, (T + 7) / 8), 256, 0, st>>>(wr, xr, logits, T, dim, E);
-  } else {
-    moe_router_tiled_kernel<<<dim3((T + 63) / 64, (E + 63) / 64), 256, 0, st>>>(wr, xr, logits, T, dim, E);
+    return 0;
   }
+  const int tiles = ((T + kRtM - 1) / kRtM) * ((E + kRtN - 1) / kRtN);
+  const int nk = (dim + kRtK - 1) / kRtK;
+  int nsplit = (2 * sms + tiles - 1) / tiles;
+  nsplit = nsplit < 1 ? 1 : nsplit > kRtMaxSplit ? kRtMaxSplit : nsplit;
+  if (nsplit > nk) nsplit = nk;
+  moe_router_gemm_kernel<<<dim3((T + kRtM - 1) / kRtM, nsplit, (E + kRtN - 1) / kRtN), 128, 0, st>>>(
+      wr, xr, part, T, dim, E, nsplit);
+  return nsplit;
 }
 
 // ---------------------------------------------------------------- softmax + top-k
@@ -192,19 +255,25 @@ static void launch_router(const float* wr, const float* xr, float* logits, int T
 // exp((v-max) in double) -> float, sequential float sum, divide.  Top-k as
 // Llama.kt:280-293: strict '>' over ascending index, so ties go to the lowest
 // index; the selected entry is masked to -inf.
-__global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, int K,
+// `logits` holds nsplit >= 1 partial logit matrices [nsplit][T][E] (split-K
+// router) that are added in split order first.
+__global__ void moe_topk_kernel(const float* __restrict__ logits, int nsplit, int T, int E, int K,
                                 int32_t* __restrict__ idx_out, float* __restrict__ prob_out) {
   __shared__ float probs[8][kMaxExperts];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
-  const float* lg = logits + (size_t)t * E;
   float* p = probs[warp];
   float mx = -INFINITY;
-  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+  for (int e = lane; e < E; e += 32) {
+    float v = logits[(size_t)t * E + e];
+    for (int sp = 1; sp < nsplit; ++sp) v = __fadd_rn(v, logits[((size_t)sp * T + t) * E + e]);
+    p[e] = v;
+    mx = fmaxf(mx, v);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  for (int e = lane; e < E; e += 32) p[e] = (float)exp((double)__fsub_rn(lg[e], mx));
+  for (int e = lane; e < E; e += 32) p[e] = (float)exp((double)__fsub_rn(p[e], mx));
   __syncwarp();
   float sum = 0.f;
   if (lane == 0)
@@ -269,6 +338,71 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t* __rest
     int pos = off[e] + atomicAdd(&cur[e], 1);
     perm[pos] = s;
   }
+}
+
+// Wide batches: the same result from three kernels over chunks of slots.
+// Within an expert the slots come in no fixed order; nothing downstream
+// depends on it (every slot's products are independent of its neighbours).
+constexpr int kPermChunk = 2048;
+__global__ void __launch_bounds__(256) moe_perm_count_kernel(const int32_t* __restrict__ idx, int n_slots, int E,
+                                                             int32_t* __restrict__ cnt) {
+  __shared__ int h[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  const int s0 = blockIdx.x * kPermChunk, s1 = min(n_slots, s0 + kPermChunk);
+  for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) atomicAdd(&h[idx[s]], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[(size_t)blockIdx.x * E + e] = h[e];
+}
+// One CTA of kMaxExperts threads: offsets[e] (offsets[E] = n_slots) and, in
+// place of the chunk counts, each chunk's first position for each expert.
+__global__ void __launch_bounds__(kMaxExperts) moe_perm_scan_kernel(int32_t* __restrict__ cnt, int nb, int E,
+                                                                    int32_t* __restrict__ offsets) {
+  __shared__ int tot[kMaxExperts + 1];
+  const int e = threadIdx.x;
+  int sum = 0;
+  if (e < E)
+    for (int b = 0; b < nb; ++b) sum += cnt[(size_t)b * E + e];
+  tot[e] = sum;
+  __syncthreads();
+  if (e == 0) {
+    int a = 0;
+    for (int i = 0; i < E; ++i) {
+      const int v = tot[i];
+      tot[i] = a;
+      a += v;
+    }
+    tot[E] = a;
+    offsets[E] = a;
+  }
+  __syncthreads();
+  if (e < E) {
+    int run = tot[e];
+    offsets[e] = run;
+    for (int b = 0; b < nb; ++b) {
+      const int c = cnt[(size_t)b * E + e];
+      cnt[(size_t)b * E + e] = run;
+      run += c;
+    }
+  }
+}
+__global__ void __launch_bounds__(256) moe_perm_place_kernel(const int32_t* __restrict__ idx, int n_slots, int E,
+                                                             const int32_t* __restrict__ base,
+                                                             int32_t* __restrict__ perm) {
+  __shared__ int cur[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cur[e] = base[(size_t)blockIdx.x * E + e];
+  __syncthreads();
+  const int s0 = blockIdx.x * kPermChunk, s1 = min(n_slots, s0 + kPermChunk);
+  for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) perm[atomicAdd(&cur[idx[s]], 1)] = s;
+}
+
+// Threads for a one-row-per-CTA kernel over n4 float4 columns: about 512,
+// with every thread doing the same number of columns.
+static int row_threads(int n4) {
+  const int iters = (n4 + 511) / 512;
+  int t = (n4 + iters - 1) / iters;
+  t = (t + 31) / 32 * 32;
+  return t < 32 ? 32 : t;
 }
 
 // ---------------------------------------------------------------- grouped experts
@@ -1110,6 +1244,76 @@ __global__ void __launch_bounds__(512) moe_combine_kernel(const float* __restric
   }
 }
 
+// Same arithmetic with the combined row held in registers between the sum and
+// the post-norm (one write of the output instead of write + re-read +
+// write): thread i owns float4 columns i, i + blockDim, ... (IT of them).
+template <int IT>
+__global__ void __launch_bounds__(512) moe_combine_reg_kernel(const float* __restrict__ D,
+                                                              const int32_t* __restrict__ idx,
+                                                              const float* __restrict__ prob,
+                                                              const float* __restrict__ down_scale,
+                                                              const float* __restrict__ post_norm,
+                                                              float* __restrict__ out, int dim, int K, float eps) {
+  __shared__ float red[33];
+  __shared__ float fw[kMaxUsed];
+  const int t = blockIdx.x;
+  if (threadIdx.x < K) {
+    const int e = idx[(size_t)t * K + threadIdx.x];
+    fw[threadIdx.x] = __fmul_rn(prob[(size_t)t * K + threadIdx.x], down_scale[e]);
+  }
+  __syncthreads();
+  const int n4 = dim >> 2;
+  float4 acc[IT];
+  float ss = 0.f;
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    acc[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < n4) {
+      for (int k0 = 0; k0 < K; k0 += 8) {  // eight rows in flight, summed in k order
+        float4 d[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k0 + k < K) d[k] = __ldg(reinterpret_cast<const float4*>(D + ((size_t)t * K + k0 + k) * dim) + i);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k0 + k < K) {
+            const float f = fw[k0 + k];
+            acc[it].x = __fadd_rn(__fmul_rn(f, d[k].x), acc[it].x);
+            acc[it].y = __fadd_rn(__fmul_rn(f, d[k].y), acc[it].y);
+            acc[it].z = __fadd_rn(__fmul_rn(f, d[k].z), acc[it].z);
+            acc[it].w = __fadd_rn(__fmul_rn(f, d[k].w), acc[it].w);
+          }
+        }
+      }
+      ss = fmaf(acc[it].x, acc[it].x, fmaf(acc[it].y, acc[it].y, fmaf(acc[it].z, acc[it].z,
+                                                                      fmaf(acc[it].w, acc[it].w, ss))));
+    }
+  }
+  float4* o = reinterpret_cast<float4*>(out + (size_t)t * dim);
+  float sn = 1.f;
+  if (post_norm != nullptr) {
+    ss = block_sum(ss, red);
+    const float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
+    sn = (float)(1.0 / sqrt((double)m));
+  }
+  const float4* pn = reinterpret_cast<const float4*>(post_norm);
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int i = threadIdx.x + it * blockDim.x;
+    if (i >= n4) continue;
+    float4 v = acc[it];
+    if (post_norm != nullptr) {
+      const float4 w = pn[i];
+      v.x = __fmul_rn(w.x, __fmul_rn(sn, v.x));
+      v.y = __fmul_rn(w.y, __fmul_rn(sn, v.y));
+      v.z = __fmul_rn(w.z, __fmul_rn(sn, v.z));
+      v.w = __fmul_rn(w.w, __fmul_rn(sn, v.w));
+    }
+    o[i] = v;
+  }
+}
+
 // ---------------------------------------------------------------- host side
 
 struct MoeScratch {
@@ -1153,6 +1357,52 @@ static MoeScratch carve(uint8_t* base, int T, int dim, int E, int K, int ff) {
   m.moe_in_s16 = (float*)take((size_t)T * (dim / 16) * 4);
   m.G_s16 = (float*)take((size_t)T * K * (ff / 16) * 4);
   return m;
+}
+
+// Front of the layer, shared by every entry point: norms (prep), router
+// logits, softmax + top-k, and the slot permutation.  The router's split-K
+// partials and the permutation's chunk counts use the D buffer, which the
+// expert products only write later.
+static cudaError_t launch_front(g4_ctx* c, const g4_moe_weights* w, const float* x, const MoeScratch& m, int T,
+                                bool want_s16, cudaStream_t st) {
+  const int dim = w->dim, E = w->n_expert, K = w->n_used;
+  moe_prep_kernel<<<T, row_threads(dim / 4), 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d,
+                                                      (const float*)w->gate_inp_scale->d, m.moe_in, m.xr,
+                                                      want_s16 ? m.moe_in_s16 : nullptr, dim, w->eps);
+  // D holds T*K*dim floats; the split-K router may use up to kRtMaxSplit*T*E of them
+  int nsplit = 0;
+  if ((long long)kRtMaxSplit * E <= (long long)K * dim)
+    nsplit = launch_router((const float*)w->gate_inp->d, m.xr, m.logits, m.D, T, dim, E, c->dev.sms, st);
+  else
+    moe_router_small_kernel<<<dim3(E, (T + 7) / 8), 256, 0, st>>>((const float*)w->gate_inp->d, m.xr, m.logits, T,
+                                                                  dim, E);
+  moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(nsplit ? m.D : m.logits, nsplit ? nsplit : 1, T, E, K, m.idx,
+                                               m.prob);
+  const int n_slots = T * K;
+  if (n_slots <= 2 * kPermChunk) {
+    moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, n_slots, E, m.offsets, m.perm);
+  } else {
+    const int nb = (n_slots + kPermChunk - 1) / kPermChunk;
+    int32_t* cnt = reinterpret_cast<int32_t*>(m.D);  // nb*E ints, far below T*K*dim
+    moe_perm_count_kernel<<<nb, 256, 0, st>>>(m.idx, n_slots, E, cnt);
+    moe_perm_scan_kernel<<<1, kMaxExperts, 0, st>>>(cnt, nb, E, m.offsets);
+    moe_perm_place_kernel<<<nb, 256, 0, st>>>(m.idx, n_slots, E, cnt, m.perm);
+  }
+  return cudaGetLastError();
+}
+
+static void launch_combine(const g4_moe_weights* w, const MoeScratch& m, float* out, int T, cudaStream_t st) {
+  const int n4 = w->dim / 4, threads = row_threads(n4), iters = (n4 + threads - 1) / threads;
+  const float* ds = (const float*)w->down_exps_scale->d;
+  const float* pn = w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr;
+  switch (iters) {
+    case 1: moe_combine_reg_kernel<1><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
+    case 2: moe_combine_reg_kernel<2><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
+    case 3: moe_combine_reg_kernel<3><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
+    case 4: moe_combine_reg_kernel<4><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
+    default:
+      moe_combine_kernel<<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps);
+  }
 }
 
 using ExpertFn = void (*)(const ExpertArgs);
@@ -1469,7 +1719,7 @@ extern "C" int g4_moe_topk(g4_ctx* c, const float* logits, int T, int E, int K, 
   }
   if (T == 0) return 0;
   if (int r = c->bind()) return r;
-  moe_topk_kernel<<<(T + 7) / 8, 256, 0, (cudaStream_t)stream>>>(logits, T, E, K, idx, prob);
+  moe_topk_kernel<<<(T + 7) / 8, 256, 0, (cudaStream_t)stream>>>(logits, 1, T, E, K, idx, prob);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : c->cuda_fail(e, "g4_moe_topk");
 }
@@ -1513,19 +1763,14 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
     return G4_E_NOMEM;
   }
   MoeScratch m = carve(base, T, dim, E, K, ff);
-  const float* f_scale = (const float*)w->gate_inp_scale->d;
-  moe_prep_kernel<<<T, 512, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, f_scale, m.moe_in, m.xr, m.moe_in_s16, dim, w->eps);
-  launch_router((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E, st);
-  moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(m.logits, T, E, K, m.idx, m.prob);
-  moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, T * K, E, m.offsets, m.perm);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_front(c, w, x, m, T, !use_tc, st);
   if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer launch");
   bool done = false;
   if (use_tc) {
     e = launch_moe_tc(c, (const uint8_t*)w->gate_up_exps->d, (const uint8_t*)w->down_exps->d, m.moe_in, m.offsets,
                       m.perm, m.D, base + base_need, T, dim, E, K, ff, st);
-    if (e != cudaSuccess && e != cudaErrorNotSupported) return c->cuda_fail(e, "g4_moe_layer tensor-core launch");
-    done = e == cudaSuccess;  // cudaErrorNotSupported: the driver cannot encode tensor maps; CUDA-core kernels follow
+    if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer tensor-core launch");
+    done = true;
   }
   if (!done) {
     int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
@@ -1549,9 +1794,7 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
     }
     if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer expert launch");
   }
-  moe_combine_kernel<<<T, 512, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
-                                        w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr, out, dim,
-                                        K, w->eps);
+  launch_combine(w, m, out, T, st);
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   e = cudaGetLastError();
@@ -1760,12 +2003,7 @@ extern "C" int g4_moe_layer_noalloc(g4_ctx* c, const g4_moe_weights* w, const fl
   // Every work buffer is fully written before it is read, so nothing has to
   // be cleared between calls.
   MoeScratch m = carve(base, T, dim, E, K, ff);
-  moe_prep_kernel<<<T, 512, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d, (const float*)w->gate_inp_scale->d,
-                                     m.moe_in, m.xr, m.moe_in_s16, dim, w->eps);
-  launch_router((const float*)w->gate_inp->d, m.xr, m.logits, T, dim, E, st);
-  moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(m.logits, T, E, K, m.idx, m.prob);
-  moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, T * K, E, m.offsets, m.perm);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_front(c, w, x, m, T, true, st);
   if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_noalloc launch");
   int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
                              m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, true);
@@ -1786,9 +2024,7 @@ extern "C" int g4_moe_layer_noalloc(g4_ctx* c, const g4_moe_weights* w, const fl
     return G4_E_ARG;
   }
   if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer_noalloc expert launch");
-  moe_combine_kernel<<<T, 512, 0, st>>>(m.D, m.idx, m.prob, (const float*)w->down_exps_scale->d,
-                                        w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr, out, dim,
-                                        K, w->eps);
+  launch_combine(w, m, out, T, st);
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   e = cudaGetLastError();

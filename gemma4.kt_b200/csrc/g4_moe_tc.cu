@@ -7,11 +7,18 @@
 //   g       = gelu(gate) * up      (Llama.kt:316-322)
 //   down    = W_d[e] · g           (Llama.kt:325-332)
 // for every routed slot, grouped by expert.  The weights stay in their GGUF
-// Q4_K blocks in HBM and are dequantized inside the kernel (q*d*sc - dmin*m
-// evaluated in fp32, Q4_KFloatTensor.kt:23-55, then rounded once to fp16);
-// activations enter the tensor cores as fp16; products accumulate in fp32
-// in tensor memory.  The result differs from the fp32 reference by the fp16
-// rounding of weights and activations (about 3e-4 relative L2 per product).
+// Q4_K blocks in HBM and are dequantized inside the kernel to fp16
+// (w = q*d*sc - dmin*m, Q4_KFloatTensor.kt:23-55, in packed fp16 arithmetic
+// with the scale and min split into fp16 high and low parts, so the result is
+// within about one fp16 rounding of the exact weight); activations enter the
+// tensor cores as fp16; products accumulate in fp32 in tensor memory.  The
+// result differs from the fp32 reference by the fp16 roundings of weights and
+// activations (about 3.5e-4 relative L2 per product).
+//
+// K order inside every aligned group of four columns is (0, 2, 1, 3) in the
+// fp16 operands on both sides (weights as dequantized, activations as the
+// gather and gate_up epilogue write them): the products are unchanged and
+// the dequantizer needs no re-packing.
 //
 // One persistent CTA per SM, warp-specialised:
 //   warp 0        allocates tensor memory; lane 0 issues tcgen05.mma
@@ -50,6 +57,10 @@ constexpr int kMaxStages = 8;
 constexpr int kNumBoxes = 5;                                // token-tile heights 16, 32, 64, 128, 256
 constexpr int kATile = kTileM * kKB * 2;                    // 16 KB of fp16
 constexpr int kBarBytes = 512;
+constexpr int kRawDepth = 4;                                // group steps of raw weight bytes in flight
+constexpr int kRawRow = 48;                                 // header 16 + codes 32 per row and stage
+constexpr int kRawSlot = kTileM * kRawRow;                  // 6 KB
+constexpr int kRawBytes = 2 * kRawDepth * kRawSlot;         // two producer groups: 48 KB
 constexpr int kMaxExpertsTc = 256;
 
 struct TcArgs {
@@ -114,6 +125,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 16-byte global -> shared copy through L2 only (cp.async, completion per thread by commit groups).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // 32 consecutive accumulator columns of this warp's 32 lanes (one row per
 // lane), waited for inside the same statement.
@@ -133,6 +153,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// try_wait that lets the hardware suspend the thread until the phase
+// completes (or at most kSuspendNs), instead of spinning.
+constexpr uint32_t kSuspendNs = 100000;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait that also gives up as soon as another role of the CTA has
 // given up (abort flag in shared memory).  On its own timeout it raises the
 // flag and records `bit` in the status word.
@@ -141,8 +176,8 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u) {
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    if ((it & 7u) == 7u) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         *abort_flag = 1;
@@ -160,8 +195,11 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 }
 
 __device__ __forceinline__ float gelu_f(float x) {
-  // Llama.kt:23-25 (evaluated in float: the result is rounded to fp16 next)
-  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+  // Llama.kt:23-25: 0.5x(1 + tanh(u)), u = sqrt(2/pi)(x + 0.044715x^3), written
+  // as x * sigmoid(2u) = x / (1 + e^(-2u)); evaluated in float with the fast
+  // exponential and division (relative error ~1e-6): the result is rounded to fp16 next.
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return __fdividef(x, 1.f + __expf(-2.f * u));
 }
 
 // Byte k (0..11) of the 12 scale bytes held in three words.
@@ -170,21 +208,48 @@ __device__ __forceinline__ uint32_t scale_byte(uint32_t s0, uint32_t s1, uint32_
   return (w >> (8 * (k & 3))) & 0xFFu;
 }
 
-// Four fp16 weights from one word of Q4_K codes: the low (mask 0x000F000F) or
-// high (mask 0x00F000F0) nibbles of bytes 0..3, each mapped to 1024 + code
-// (or 1024 + 16*code) as an fp16 bit pattern, widened to fp32 exactly, then
-// w = code*scale - min in fp32 (mult and c carry the 1024 offset and the 1/16
-// of the high nibble), rounded once to fp16.  Returns K positions 0,1 | 2,3.
-__device__ __forceinline__ uint2 q4_word_to_f16(uint32_t x, uint32_t mask, float2 mult, float2 c) {
+// Position of logical K column k in the fp16 operands (bits 0 and 1 swapped).
+__device__ __forceinline__ int kperm(int k) { return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1); }
+
+// Constants of one 32-weight sub-block for the fp16 dequantizer.  A code c
+// arrives as v = 1024 + c*step (an fp16 bit pattern: step 1 for low nibbles,
+// 16 for high ones) and w = c*s - m (s already divided by step) becomes
+//   t = v*s_hi - c_hi,  u = v*s_lo - c_lo,  w = t + u
+// with s_hi = fp16(s), s_lo = fp16(s - s_hi), c_hi = fp16(1024*s_hi + m) and
+// c_lo = fp16(1024*s_lo + r), r the rounding residual of c_hi: t and u carry
+// the whole of q*s - m between them, and each fp16 operation rounds once.
+struct SubConst {
+  __half2 s_hi, c_hi, s_lo, c_lo;  // c_* negated
+};
+__device__ __forceinline__ SubConst sub_const(float s, float m) {
+  const __half shi = __float2half_rn(s);
+  const float fshi = __half2float(shi);
+  const __half slo = __float2half_rn(s - fshi);
+  const float big = fmaf(1024.f, fshi, m);
+  const __half chi = __float2half_rn(big);
+  const float r = big - __half2float(chi);
+  const __half clo = __float2half_rn(fmaf(1024.f, __half2float(slo), r));
+  SubConst k;
+  k.s_hi = __halves2half2(shi, shi);
+  k.s_lo = __halves2half2(slo, slo);
+  k.c_hi = __halves2half2(__hneg(chi), __hneg(chi));
+  k.c_lo = __halves2half2(__hneg(clo), __hneg(clo));
+  return k;
+}
+__device__ __forceinline__ uint32_t deq2(uint32_t v, const SubConst& k) {
+  const __half2 hv = *reinterpret_cast<const __half2*>(&v);
+  const __half2 t = __hfma2(hv, k.s_hi, k.c_hi);
+  const __half2 u = __hfma2(hv, k.s_lo, k.c_lo);
+  const __half2 w = __hadd2(t, u);
+  return *reinterpret_cast<const uint32_t*>(&w);
+}
+// Four fp16 weights from one word of Q4_K codes (bytes b0..b3 = K 0..3 of a
+// group of four): the low (mask 0x000F000F) or high (mask 0x00F000F0)
+// nibbles as 1024 + code*step, in stored K order (0, 2, 1, 3).
+__device__ __forceinline__ uint2 q4_word_to_f16(uint32_t x, uint32_t mask, const SubConst& k) {
   const uint32_t a02 = (x & mask) | 0x64006400u;         // bytes 0 and 2
   const uint32_t a13 = ((x >> 8) & mask) | 0x64006400u;  // bytes 1 and 3
-  const float2 f02 = __half22float2(*reinterpret_cast<const __half2*>(&a02));
-  const float2 f13 = __half22float2(*reinterpret_cast<const __half2*>(&a13));
-  const float2 w02 = __ffma2_rn(f02, mult, c);
-  const float2 w13 = __ffma2_rn(f13, mult, c);
-  const __half2 h01 = __floats2half2_rn(w02.x, w13.x);
-  const __half2 h23 = __floats2half2_rn(w02.y, w13.y);
-  return make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+  return make_uint2(deq2(a02, k), deq2(a13, k));
 }
 
 // ---------------------------------------------------------------- kernels
@@ -223,7 +288,7 @@ __global__ void __launch_bounds__(256) moe_tc_tiles_kernel(const int32_t* __rest
   }
 }
 
-// x16[p][:] = fp16(moe_in[token of slot perm[p]][:]), one warp per sorted position.
+// x16[p][:] = fp16(moe_in[token of slot perm[p]][:]) in stored K order, one warp per sorted position.
 __global__ void __launch_bounds__(256) moe_tc_gather_kernel(const float* __restrict__ moe_in,
                                                             const int32_t* __restrict__ perm,
                                                             __half* __restrict__ x16, int n_pos, int dim, int K) {
@@ -233,8 +298,8 @@ __global__ void __launch_bounds__(256) moe_tc_gather_kernel(const float* __restr
   const float4* src = reinterpret_cast<const float4*>(moe_in + (size_t)tok * dim);
   uint2* dst = reinterpret_cast<uint2*>(x16 + (size_t)p * dim);
   for (int i = lane; i < dim / 4; i += 32) {
-    const float4 v = __ldg(src + i);
-    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    const float4 v = __ldg(src + i);  // K 4i..4i+3 stored in the order (0, 2, 1, 3)
+    const __half2 a = __floats2half2_rn(v.x, v.z), b = __floats2half2_rn(v.y, v.w);
     dst[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
   }
 }
@@ -249,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int S = a.stages;
   uint8_t* a_st = sm;                                   // S x [128 rows x 128 B]
   uint8_t* b_st = sm + (size_t)S * kATile;              // S x [cap rows x 128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_st + (size_t)S * a.b_stage_bytes);
+  uint8_t* raw = b_st + (size_t)S * a.b_stage_bytes;   // kRawDepth x [128 rows x 48 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + kRawBytes);
   uint64_t* full_a = bars;                              // producers -> MMA  (count 8)
   uint64_t* full_b = bars + kMaxStages;                 // TMA -> MMA        (count 1 + bytes)
   uint64_t* empty = bars + 2 * kMaxStages;              // MMA -> producers  (tcgen05.commit)
@@ -262,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full_a[s], kProdWarps);
+      mbar_init(&full_a[s], kProdWarps / 2);  // the four warps of the group that fills the stage
       mbar_init(&full_b[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -367,86 +433,127 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 2 + kProdWarps) {
     // ------------------------------------------------ dequantizing producers
-    // Thread pt: A-tile row t = pt / 2, half h = pt % 2 (h = 0: low nibbles ->
-    // K 0..31 of the stage, chunks 0..3; h = 1: high nibbles -> K 32..63,
-    // chunks 4..7).  Chunk c of row t sits at (t/8)*1024 + (t%8)*128 +
-    // ((c ^ t%8) * 16): the 128-byte swizzle the MMA descriptors name.
-    const int pt = threadIdx.x - 64, t = pt >> 1, h = pt & 1;
-    const uint32_t mask = h ? 0x00F000F0u : 0x000F000Fu;
+    // Two groups of four warps take alternate k-blocks of the CTA's sequence
+    // (item, kb), so two stages are dequantized at once.  In a group, thread t
+    // owns A-tile row t: the stage's 64 weights = low nibbles of its 32 code
+    // bytes (K 0..31, chunks 0..3) and high nibbles (K 32..63, chunks 4..7).
+    // Chunk c of row t sits at (t/8)*1024 + (t%8)*128 + ((c ^ t%8) * 16): the
+    // 128-byte swizzle the MMA descriptors name.  Raw bytes travel kRawDepth
+    // group steps ahead through the thread's own slots of a cp.async ring:
+    // per stage 48 bytes = super-block header (d, dmin, scales) + 32 code bytes.
+    const int grp = (warp - 2) / 4;
+    const int t = threadIdx.x - 64 - 128 * grp;
     const uint32_t row_off = (uint32_t)(t >> 3) * 1024u + (uint32_t)(t & 7) * 128u;
-    int s = 0;
-    uint32_t ph = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+    uint8_t* my_raw = raw + (size_t)grp * kRawDepth * kRawSlot + (size_t)t * kRawRow;
+    auto row_e0 = [&](int item) {
       const int4 tl = a.tiles[item / R];
       const int rt = item % R;
       const long long wr = GATEUP ? (long long)((t & 1) ? a.ff : 0) + 64ll * rt + (t >> 1)
                                   : (long long)kTileM * rt + t;
-      const long long e0 = (long long)tl.x * a.expert_elems + wr * a.cols;
-      // one 64-element group of a super-block per stage: header + 32 code bytes
-      auto blk_of = [&](int kb) { return a.w + (size_t)((e0 + (long long)kb * kKB) >> 8) * 144; };
-      auto grp_of = [&](int kb) { return (int)(((e0 + (long long)kb * kKB) >> 6) & 3); };
-      const uint8_t* b0 = blk_of(0);
-      int g0 = grp_of(0);
-      uint4 hd = __ldg(reinterpret_cast<const uint4*>(b0));
-      uint4 q0 = __ldg(reinterpret_cast<const uint4*>(b0 + 16 + 32 * g0));
-      uint4 q1 = __ldg(reinterpret_cast<const uint4*>(b0 + 32 + 32 * g0));
-      for (int kb = 0; kb < nkb; ++kb) {
-        const uint4 chd = hd, cq0 = q0, cq1 = q1;
-        const int g = g0;
-        if (kb + 1 < nkb) {  // prefetch the next stage's bytes
-          const uint8_t* bn = blk_of(kb + 1);
-          g0 = grp_of(kb + 1);
-          hd = __ldg(reinterpret_cast<const uint4*>(bn));
-          q0 = __ldg(reinterpret_cast<const uint4*>(bn + 16 + 32 * g0));
-          q1 = __ldg(reinterpret_cast<const uint4*>(bn + 32 + 32 * g0));
-        }
-        // getScaleMinK4 (Q4_KFloatTensor.kt:70-84) for sub-block j = 2g + h
-        const int j = 2 * g + h;
+      return (long long)tl.x * a.expert_elems + wr * a.cols;
+    };
+    // A cursor over the sequence: k-block kb of item `item` = group g of the
+    // super-block at blk.  step() moves it one k-block on.
+    struct Cursor {
+      int item, kb, g;
+      const uint8_t* blk;
+    };
+    auto start = [&](Cursor& c, int item) {
+      c.item = item;
+      c.kb = 0;
+      c.g = 0;
+      c.blk = a.w;
+      if (item < n_items) {
+        const long long e0 = row_e0(item);
+        c.blk = a.w + (size_t)(e0 >> 8) * 144;
+        c.g = (int)((e0 >> 6) & 3);
+      }
+    };
+    auto step = [&](Cursor& c) {
+      if (++c.g == 4) {
+        c.g = 0;
+        c.blk += 144;
+      }
+      if (++c.kb == nkb) start(c, c.item + gridDim.x);
+    };
+    Cursor fc, cc;  // fetch and compute cursors, both at this group's first k-block
+    start(fc, blockIdx.x);
+    if (grp) step(fc);
+    cc = fc;
+    int f_slot = 0;
+    auto fetch = [&]() {  // copies for the fetch cursor (if any are left); always one commit group
+      if (fc.item < n_items) {
+        uint8_t* dst = my_raw + (size_t)f_slot * (kRawSlot);
+        cp_async16(dst, fc.blk);
+        cp_async16(dst + 16, fc.blk + 16 + 32 * fc.g);
+        cp_async16(dst + 32, fc.blk + 32 + 32 * fc.g);
+        step(fc);
+        if (fc.item < n_items) step(fc);
+      }
+      cp_async_commit();
+      if (++f_slot == kRawDepth) f_slot = 0;
+    };
+#pragma unroll 1
+    for (int i = 0; i < kRawDepth - 1; ++i) fetch();
+    int s = grp, c_slot = 0;  // stage of k-block number grp, then every second one
+    uint32_t ph = 0;
+    while (cc.item < n_items) {
+      fetch();
+      cp_async_wait<kRawDepth - 1>();  // this thread's bytes for the compute cursor have landed
+      const uint8_t* src = my_raw + (size_t)c_slot * kRawSlot;
+      const uint4 hd = *reinterpret_cast<const uint4*>(src);
+      const uint4 q0 = *reinterpret_cast<const uint4*>(src + 16);
+      const uint4 q1 = *reinterpret_cast<const uint4*>(src + 32);
+      if (++c_slot == kRawDepth) c_slot = 0;
+      // getScaleMinK4 (Q4_KFloatTensor.kt:70-84) for sub-blocks 2g (low nibbles) and 2g+1 (high)
+      const int g = cc.g;
+      SubConst kc[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int j = 2 * g + hh;
         uint32_t sc, mn;
         if (j < 4) {
-          sc = scale_byte(chd.y, chd.z, chd.w, j) & 63u;
-          mn = scale_byte(chd.y, chd.z, chd.w, j + 4) & 63u;
+          sc = scale_byte(hd.y, hd.z, hd.w, j) & 63u;
+          mn = scale_byte(hd.y, hd.z, hd.w, j + 4) & 63u;
         } else {
-          const uint32_t bj4 = scale_byte(chd.y, chd.z, chd.w, j + 4);
-          sc = (bj4 & 0xFu) | ((scale_byte(chd.y, chd.z, chd.w, j - 4) >> 6) << 4);
-          mn = (bj4 >> 4) | ((scale_byte(chd.y, chd.z, chd.w, j) >> 6) << 4);
+          const uint32_t bj4 = scale_byte(hd.y, hd.z, hd.w, j + 4);
+          sc = (bj4 & 0xFu) | ((scale_byte(hd.y, hd.z, hd.w, j - 4) >> 6) << 4);
+          mn = (bj4 >> 4) | ((scale_byte(hd.y, hd.z, hd.w, j) >> 6) << 4);
         }
-        const float d = f16_bits_to_f32((uint16_t)(chd.x & 0xFFFFu));
-        const float dmin = f16_bits_to_f32((uint16_t)(chd.x >> 16));
+        const float d = f16_bits_to_f32((uint16_t)(hd.x & 0xFFFFu));
+        const float dmin = f16_bits_to_f32((uint16_t)(hd.x >> 16));
         const float sf = d * (float)sc;     // exact: 11-bit by 6-bit product
         const float mf = dmin * (float)mn;  // exact
-        const float mult = h ? sf * 0.0625f : sf;
-        const float cc = -fmaf(1024.f, mult, mf);
-        const float2 m2 = make_float2(mult, mult), c2 = make_float2(cc, cc);
-        uint4 ch[4];
-        const uint32_t qw[8] = {cq0.x, cq0.y, cq0.z, cq0.w, cq1.x, cq1.y, cq1.z, cq1.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint2 lo = q4_word_to_f16(qw[2 * i], mask, m2, c2);
-          const uint2 hi = q4_word_to_f16(qw[2 * i + 1], mask, m2, c2);
-          ch[i] = make_uint4(lo.x, lo.y, hi.x, hi.y);
-        }
-        // every lane waits; the verdict is made warp-uniform so the warp never splits
-        if (!__all_sync(0xffffffffu, tc_wait(&empty[s], ph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY))) {
-          ok = false;
-          break;
-        }
-        uint8_t* dst = a_st + (size_t)s * kATile + row_off;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t c = (uint32_t)(i + 4 * h);
-          *reinterpret_cast<uint4*>(dst + ((c ^ (uint32_t)(t & 7)) << 4)) = ch[i];
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full_a[s]);
-        if (++s == S) {
-          s = 0;
-          ph ^= 1u;
-        }
+        kc[hh] = sub_const(hh ? sf * 0.0625f : sf, mf);
       }
+      const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      uint4 ch[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint2 la = q4_word_to_f16(qw[2 * i], 0x000F000Fu, kc[0]);
+        const uint2 lb = q4_word_to_f16(qw[2 * i + 1], 0x000F000Fu, kc[0]);
+        const uint2 ha = q4_word_to_f16(qw[2 * i], 0x00F000F0u, kc[1]);
+        const uint2 hb = q4_word_to_f16(qw[2 * i + 1], 0x00F000F0u, kc[1]);
+        ch[i] = make_uint4(la.x, la.y, lb.x, lb.y);
+        ch[4 + i] = make_uint4(ha.x, ha.y, hb.x, hb.y);
+      }
+      // every lane waits; the verdict is made warp-uniform so the warp never splits
+      if (!__all_sync(0xffffffffu, tc_wait(&empty[s], ph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY))) break;
+      uint8_t* dst = a_st + (size_t)s * kATile + row_off;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + (((uint32_t)c ^ (uint32_t)(t & 7)) << 4)) = ch[c];
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_a[s]);
+      s += 2;  // this group's next k-block is two on
+      if (s >= S) {
+        s -= S;
+        ph ^= 1u;
+      }
+      step(cc);
+      if (cc.item < n_items) step(cc);
     }
+    cp_async_wait<0>();  // no copy of this thread outlives the role (after an abort too)
   } else {
     // ------------------------------------------------ epilogue
     const int q = warp & 3;  // tensor-memory lane quarter this warp may access
@@ -461,13 +568,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
         tmem_ld32(tb + (uint32_t)c0, v);
         if (GATEUP) {
-          // lanes 2i / 2i+1 hold gate / up row of pair 16q + i
-          const int col = 64 * rt + 16 * q + (lane >> 1);
+          // Lanes 2i / 2i+1 hold the gate / up row of pair 16q + i.  Per two
+          // token columns the even lane finishes column jj, the odd lane
+          // column jj + 1, each after one exchange.
+          const int col = kperm(64 * rt + 16 * q + (lane >> 1));  // stored K order of the down product
+          const bool odd = lane & 1;
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const float u = __shfl_xor_sync(0xffffffffu, v[jj], 1);
-            if (!(lane & 1) && c0 + jj < n)
-              a.g16[(size_t)(p0 + c0 + jj) * a.out_ld + col] = __float2half_rn(gelu_f(v[jj]) * u);
+          for (int jj = 0; jj < 32; jj += 2) {
+            const float recv = __shfl_xor_sync(0xffffffffu, odd ? v[jj] : v[jj + 1], 1);
+            const float gate = odd ? recv : v[jj];
+            const float up = odd ? v[jj + 1] : recv;
+            const int tok = c0 + jj + (odd ? 1 : 0);
+            if (tok < n) a.g16[(size_t)(p0 + tok) * a.out_ld + col] = __float2half_rn(gelu_f(gate) * up);
           }
         } else {
           const int my_slot = (c0 + lane < n) ? a.perm[p0 + c0 + lane] : 0;
@@ -558,7 +670,7 @@ size_t moe_tc_scratch_bytes(int T, int dim, int E, int K, int ff) {
 
 bool moe_tc_supported(int gate_up_type, int down_type, int dim, int ff, int E) {
   return gate_up_type == Q4_K && down_type == Q4_K && dim % kTileM == 0 && ff % kKB == 0 && dim % 256 == 0 &&
-         E <= kMaxExpertsTc;
+         E <= kMaxExpertsTc && encode_fn() != nullptr;
 }
 
 bool moe_tc_wanted(int T, int K, int E) {
@@ -588,10 +700,10 @@ cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* do
   }
   const int b_stage = cap * 128;
   const size_t optin = c->dev.smem_optin;
-  int stages = (int)((optin - 1024 - kBarBytes) / (size_t)(kATile + b_stage));
+  int stages = (int)((optin - 1024 - kBarBytes - kRawBytes) / (size_t)(kATile + b_stage));
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return cudaErrorInvalidConfiguration;
-  const size_t smem = 1024 + (size_t)stages * (kATile + b_stage) + kBarBytes;
+  const size_t smem = 1024 + (size_t)stages * (kATile + b_stage) + kRawBytes + kBarBytes;
 
   TcArgs ga{};
   ga.w = gate_up_w;

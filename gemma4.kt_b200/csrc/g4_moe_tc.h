@@ -13,7 +13,8 @@ namespace g4 {
 size_t moe_tc_scratch_bytes(int T, int dim, int E, int K, int ff);
 
 // True when the weight types and the geometry are ones the tensor-core path
-// handles (Q4_K experts, dim % 256 == 0, ff % 64 == 0, at most 256 experts).
+// handles (Q4_K experts, dim % 256 == 0, ff % 64 == 0, at most 256 experts)
+// and the driver can encode TMA tensor maps.
 bool moe_tc_supported(int gate_up_type, int down_type, int dim, int ff, int E);
 
 // True when g4_moe_layer should take the tensor-core path for T tokens
@@ -24,8 +25,7 @@ bool moe_tc_wanted(int T, int K, int E);
 //   moe_in [T][dim] fp32, offsets [E+1] / perm [T*K] from the permutation step,
 //   D [T*K][dim] fp32 indexed by slot = token*K + k (what the combine reads).
 // work points at moe_tc_scratch_bytes(...) bytes.  Returns a cudaError_t
-// (cudaSuccess on success); cudaErrorNotSupported when the driver cannot
-// encode tensor maps.
+// (cudaSuccess on success).  Call only when moe_tc_supported(...) is true.
 cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* down_w, const float* moe_in,
                           const int32_t* offsets, const int32_t* perm, float* D, void* work, int T, int dim, int E,
                           int K, int ff, cudaStream_t st);
