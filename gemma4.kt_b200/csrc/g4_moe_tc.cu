@@ -37,6 +37,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -50,17 +51,16 @@ namespace {
 constexpr int kTileM = 128;                                 // weight rows per tile (MMA M)
 constexpr int kKB = 64;                                     // K per pipeline stage: one 128-byte fp16 row
 constexpr int kMmaK = 16;                                   // K of one kind::f16 MMA
-constexpr int kProdWarps = 8;                               // dequantizing warps
 constexpr int kEpiWarps = 4;                                // epilogue warps (one per TMEM lane quarter)
-constexpr int kThreads = 32 * (2 + kProdWarps + kEpiWarps);  // 448
+// NG producer groups of four dequantizing warps each
+__host__ __device__ constexpr int tc_threads(int ng) { return 32 * (2 + 4 * ng + kEpiWarps); }
 constexpr int kMaxStages = 8;
 constexpr int kNumBoxes = 5;                                // token-tile heights 16, 32, 64, 128, 256
 constexpr int kATile = kTileM * kKB * 2;                    // 16 KB of fp16
 constexpr int kBarBytes = 512;
-constexpr int kRawDepth = 4;                                // group steps of raw weight bytes in flight
-constexpr int kRawRow = 48;                                 // header 16 + codes 32 per row and stage
-constexpr int kRawSlot = kTileM * kRawRow;                  // 6 KB
-constexpr int kRawBytes = 2 * kRawDepth * kRawSlot;         // two producer groups: 48 KB
+constexpr int kRawDepth = 4;                                // 64-column blocks of raw weights in flight per group
+constexpr int kRawRow = 48;                                 // header 16 + codes 32 per row and 64 columns
+__host__ __device__ constexpr int tc_raw_bytes(int ng) { return ng * kRawDepth * kTileM * kRawRow; }  // 24 KB a group
 constexpr int kMaxExpertsTc = 256;
 
 struct TcArgs {
@@ -74,7 +74,9 @@ struct TcArgs {
   int stages;
   int b_stage_bytes;       // token-tile cap * 128
   int acc_cols;            // tensor-memory columns per accumulator (= token-tile cap)
-  uint32_t tmem_cols;      // allocated columns (2 accumulators)
+  uint32_t tmem_cols;      // allocated columns
+  uint32_t tmem_a_col;     // first column of the weight stages when A lives in tensor memory
+  int pipe_bytes;          // shared memory of one pipeline (1024-byte multiple)
   const int4* tiles;       // {expert, first sorted position, tokens, box index}
   const int32_t* n_tiles;
   const int32_t* perm;     // sorted position -> slot
@@ -107,6 +109,28 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Same with the A operand (128 rows x 16 K, two fp16 per 32-bit column, row m
+// in lane m) read from tensor memory.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 consecutive tensor-memory columns of this warp's 32 lanes (one row per lane).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (start >> 4 | LBO 16 B | SBO 1024 B | version 1 | SWIZZLE_128B).
 __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
@@ -304,32 +328,52 @@ __global__ void __launch_bounds__(256) moe_tc_gather_kernel(const float* __restr
   }
 }
 
-template <bool GATEUP>
-__global__ void __launch_bounds__(kThreads, 1)
+// One pipeline stage covers KSUB sub-tiles of 64 K columns (the last stage of
+// an item may hold fewer): per sub-tile a 128-row x 64 weight tile and a
+// token tile of up to cap rows x 64, each in the 128-byte-swizzled K-major
+// layout.  Larger stages mean fewer barrier handshakes per K, which paces
+// the pipeline when token tiles are narrow.
+// TMEM_A: the dequantized weight tile of each stage goes to tensor memory
+// (tcgen05.st, 32 columns per 64-column sub-tile) and the MMA reads it from
+// there; shared memory then carries only the token tiles.  Chosen for token
+// tiles of at most 128 rows, where fetching A from shared memory (4 KB per
+// MMA) would cost more than the MMA itself.
+// P independent pipelines share the CTA (each with its own issuing thread,
+// token-tile loader, producers, epilogue warps, stage ring, barriers and
+// 512/P tensor-memory columns) and split its items: a single thread issues
+// one tcgen05.mma per ~120 cycles whatever the tile width, so narrow token
+// tiles need several issuers to keep the tensor core fed.
+template <bool GATEUP, int KSUB, bool TMEM_A, int NG, int P>
+__global__ void __launch_bounds__(P * tc_threads(NG), 1)
     moe_tc_kernel(const __grid_constant__ TcArgs a, const __grid_constant__ CUtensorMap m0,
                   const __grid_constant__ CUtensorMap m1, const __grid_constant__ CUtensorMap m2,
                   const __grid_constant__ CUtensorMap m3, const __grid_constant__ CUtensorMap m4) {
+  constexpr int kDepth = kRawDepth / KSUB;           // raw stages in flight per producer group
+  constexpr int kRowRaw = KSUB * kRawRow;            // raw bytes per row and stage
+  constexpr int kSlot = kTileM * kRowRaw;            // one raw stage of one group
+  constexpr int kWpp = 2 + 4 * NG + kEpiWarps;       // warps per pipeline
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int S = a.stages;
-  uint8_t* a_st = sm;                                   // S x [128 rows x 128 B]
-  uint8_t* b_st = sm + (size_t)S * kATile;              // S x [cap rows x 128 B]
-  uint8_t* raw = b_st + (size_t)S * a.b_stage_bytes;   // kRawDepth x [128 rows x 48 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + kRawBytes);
-  uint64_t* full_a = bars;                              // producers -> MMA  (count 8)
-  uint64_t* full_b = bars + kMaxStages;                 // TMA -> MMA        (count 1 + bytes)
-  uint64_t* empty = bars + 2 * kMaxStages;              // MMA -> producers  (tcgen05.commit)
-  uint64_t* tfull = bars + 3 * kMaxStages;              // MMA -> epilogue   [2]
+  const int gwarp = threadIdx.x >> 5;                // CTA warp (its % 4 is its tensor-memory lane quarter)
+  const int pp = gwarp / kWpp;                       // this thread's pipeline
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023)) +
+                (size_t)pp * a.pipe_bytes;
+  const int S = a.stages, bsub = a.b_stage_bytes;
+  uint8_t* a_st = sm;                                   // [S][KSUB] x [128 rows x 128 B] (unless TMEM_A)
+  uint8_t* b_st = sm + (TMEM_A ? 0 : (size_t)S * KSUB * kATile);  // [S][KSUB] x [cap rows x 128 B]
+  uint8_t* raw = b_st + (size_t)S * KSUB * bsub;        // [NG groups][kDepth] x [128 rows x kRowRaw]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + tc_raw_bytes(NG));
+  uint64_t* full = bars;                                // producers (4 warps) + TMA bytes -> MMA
+  uint64_t* empty = bars + kMaxStages;                  // MMA -> producers and TMA (tcgen05.commit)
+  uint64_t* tfull = bars + 2 * kMaxStages;              // MMA -> epilogue   [2]
   uint64_t* tempty = tfull + 2;                         // epilogue -> MMA   [2] (count 4)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
+  const int warp = gwarp - pp * kWpp, lane = threadIdx.x & 31;  // warp within the pipeline
+  if (warp == 0 && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full_a[s], kProdWarps / 2);  // the four warps of the group that fills the stage
-      mbar_init(&full_b[s], 1);
+      mbar_init(&full[s], 4 + 1);  // the four warps of the group that fills it + the TMA thread
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -340,16 +384,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0) {
+  // pipeline 0's first warp allocates all 512 columns; pipeline p uses columns [p*512/P, (p+1)*512/P)
+  uint32_t* tmem_slot0 = reinterpret_cast<uint32_t*>(
+      reinterpret_cast<uint8_t*>(tmem_slot) - (size_t)pp * a.pipe_bytes);
+  if (gwarp == 0) {
     __syncwarp();
-    tmem_alloc(tmem_slot, a.tmem_cols);
+    tmem_alloc(tmem_slot0, a.tmem_cols);
     tc_fence_before();
   }
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const int R = a.n_row_tiles, nkb = a.nkb;
+  const uint32_t tmem_base = *tmem_slot0 + (uint32_t)pp * (512u / P);
+  const int R = a.n_row_tiles, nkb = a.nkb;          // nkb: 64-column blocks per item
+  const int nst = (nkb + KSUB - 1) / KSUB;           // stages per item
   const int n_items = *a.n_tiles * R;
+  auto nsub_of = [&](int st) { return min(KSUB, nkb - st * KSUB); };
 
   if (warp == 0) {
     // ------------------------------------------------ MMA issuer
@@ -357,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0, acc = 0, aph = 0;
       bool issued = false, ok = true;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+      for (int item = blockIdx.x + pp * gridDim.x; ok && item < n_items; item += P * gridDim.x) {
         const int4 tl = a.tiles[item / R];
         const uint32_t idesc = idesc_f16((uint32_t)((tl.z + 15) & ~15));
         if (!tc_wait(&tempty[acc], aph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY)) {
@@ -366,18 +415,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * (uint32_t)a.acc_cols;
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!tc_wait(&full_a[s], ph, abort_flag, a.status, ERR_TIMEOUT_FULL) ||
-              !tc_wait(&full_b[s], ph, abort_flag, a.status, ERR_TIMEOUT_FULL)) {
+        for (int st = 0; st < nst; ++st) {
+          if (!tc_wait(&full[s], ph, abort_flag, a.status, ERR_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sw128_desc(a_st + (size_t)s * kATile);
-          const uint64_t bd = sw128_desc(b_st + (size_t)s * a.b_stage_bytes);
+          const int nsub = nsub_of(st);
 #pragma unroll
-          for (int kk = 0; kk < kKB / kMmaK; ++kk)  // +32 bytes of K per step, inside the swizzle row
-            tc_mma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+          for (int sub = 0; sub < KSUB; ++sub) {
+            if (sub < nsub) {
+              const uint64_t bd = sw128_desc(b_st + (size_t)(s * KSUB + sub) * bsub);
+              if (TMEM_A) {
+                const uint32_t at = tmem_base + a.tmem_a_col + (uint32_t)(s * KSUB + sub) * 32u;
+#pragma unroll
+                for (int kk = 0; kk < kKB / kMmaK; ++kk)  // 16 K = 8 columns of A, 32 bytes of B
+                  tc_mma_f16_ts(d_tmem, at + 8u * kk, bd + 2 * kk, idesc, (st | sub | kk) != 0);
+              } else {
+                const uint64_t ad = sw128_desc(a_st + (size_t)(s * KSUB + sub) * kATile);
+#pragma unroll
+                for (int kk = 0; kk < kKB / kMmaK; ++kk)  // +32 bytes of K per step, inside the swizzle row
+                  tc_mma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (st | sub | kk) != 0);
+              }
+            }
+          }
           issued = true;
           tc_commit(&empty[s]);
           if (++s == S) {
@@ -401,17 +462,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0, n_issued = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+      for (int item = blockIdx.x + pp * gridDim.x; ok && item < n_items; item += P * gridDim.x) {
         const int4 tl = a.tiles[item / R];
         const CUtensorMap* map = tl.w == 0 ? &m0 : tl.w == 1 ? &m1 : tl.w == 2 ? &m2 : tl.w == 3 ? &m3 : &m4;
-        const uint32_t bytes = (16u << tl.w) * 128u;
-        for (int kb = 0; kb < nkb; ++kb) {
+        const uint32_t box_bytes = (16u << tl.w) * 128u;
+        for (int st = 0; st < nst; ++st) {
           if (!tc_wait(&empty[s], ph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_b[s], bytes);
-          tma_load_2d(b_st + (size_t)s * a.b_stage_bytes, map, kb * kKB, tl.y, &full_b[s]);
+          const int nsub = nsub_of(st);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)nsub * box_bytes);
+          for (int sub = 0; sub < nsub; ++sub)
+            tma_load_2d(b_st + (size_t)(s * KSUB + sub) * bsub, map, (st * KSUB + sub) * kKB, tl.y, &full[s]);
           ++n_issued;
           if (++s == S) {
             s = 0;
@@ -419,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!ok) {  // wait for this thread's copies still in flight (the last S at most)
+      if (!ok) {  // let this thread's copies still in flight (the last S stages at most) land
         int ss = s;
         uint32_t pp = ph;
         for (int i = 0; i < S && i < n_issued; ++i) {
@@ -427,24 +490,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             ss = S - 1;
             pp ^= 1u;
           }
-          drain_wait(&full_b[ss], pp);
+          drain_wait(&full[ss], pp);
         }
       }
     }
-  } else if (warp < 2 + kProdWarps) {
+  } else if (warp < 2 + 4 * NG) {
     // ------------------------------------------------ dequantizing producers
-    // Two groups of four warps take alternate k-blocks of the CTA's sequence
-    // (item, kb), so two stages are dequantized at once.  In a group, thread t
-    // owns A-tile row t: the stage's 64 weights = low nibbles of its 32 code
-    // bytes (K 0..31, chunks 0..3) and high nibbles (K 32..63, chunks 4..7).
-    // Chunk c of row t sits at (t/8)*1024 + (t%8)*128 + ((c ^ t%8) * 16): the
-    // 128-byte swizzle the MMA descriptors name.  Raw bytes travel kRawDepth
-    // group steps ahead through the thread's own slots of a cp.async ring:
-    // per stage 48 bytes = super-block header (d, dmin, scales) + 32 code bytes.
+    // NG groups of four warps take every NG-th stage of the CTA's sequence
+    // (item, stage), so NG stages are dequantized at once.  In a group,
+    // thread t owns A-tile row t: per 64-column sub-tile, the low nibbles of
+    // its 32 code bytes (K 0..31, chunks 0..3) and the high nibbles (K 32..63,
+    // chunks 4..7).  Chunk c of row t sits at (t/8)*1024 + (t%8)*128 +
+    // ((c ^ t%8) * 16): the 128-byte swizzle the MMA descriptors name.  Raw
+    // bytes travel kDepth group steps ahead through the thread's own slots of
+    // a cp.async ring: per sub-tile 48 bytes = super-block header (d, dmin,
+    // scales) + 32 code bytes.
     const int grp = (warp - 2) / 4;
-    const int t = threadIdx.x - 64 - 128 * grp;
+    // with A in tensor memory a warp may only write its own lane quarter (warp % 4)
+    const int t = TMEM_A ? 32 * (gwarp & 3) + lane : 32 * (warp - 2 - 4 * grp) + lane;
     const uint32_t row_off = (uint32_t)(t >> 3) * 1024u + (uint32_t)(t & 7) * 128u;
-    uint8_t* my_raw = raw + (size_t)grp * kRawDepth * kRawSlot + (size_t)t * kRawRow;
+    uint8_t* my_raw = raw + (size_t)grp * kDepth * kSlot + (size_t)t * kRowRaw;
     auto row_e0 = [&](int item) {
       const int4 tl = a.tiles[item / R];
       const int rt = item % R;
@@ -452,15 +517,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   : (long long)kTileM * rt + t;
       return (long long)tl.x * a.expert_elems + wr * a.cols;
     };
-    // A cursor over the sequence: k-block kb of item `item` = group g of the
-    // super-block at blk.  step() moves it one k-block on.
+    // A cursor at the start of stage st of item `item`: its first 64-column
+    // block is group g of the super-block at blk.
     struct Cursor {
-      int item, kb, g;
+      int item, st, g;
       const uint8_t* blk;
     };
     auto start = [&](Cursor& c, int item) {
       c.item = item;
-      c.kb = 0;
+      c.st = 0;
       c.g = 0;
       c.blk = a.w;
       if (item < n_items) {
@@ -469,96 +534,133 @@ __global__ void __launch_bounds__(kThreads, 1)
         c.g = (int)((e0 >> 6) & 3);
       }
     };
-    auto step = [&](Cursor& c) {
-      if (++c.g == 4) {
-        c.g = 0;
-        c.blk += 144;
-      }
-      if (++c.kb == nkb) start(c, c.item + gridDim.x);
+    auto step = [&](Cursor& c) {  // on to the next stage of the sequence
+      const int n = nsub_of(c.st);
+      c.g += n;
+      c.blk += 144 * (c.g >> 2);
+      c.g &= 3;
+      if (++c.st == nst) start(c, c.item + P * gridDim.x);
     };
-    Cursor fc, cc;  // fetch and compute cursors, both at this group's first k-block
-    start(fc, blockIdx.x);
-    if (grp) step(fc);
+    Cursor fc, cc;  // fetch and compute cursors, both at this group's first stage
+    start(fc, blockIdx.x + pp * gridDim.x);
+    for (int i = 0; i < grp && fc.item < n_items; ++i) step(fc);
     cc = fc;
     int f_slot = 0;
     auto fetch = [&]() {  // copies for the fetch cursor (if any are left); always one commit group
       if (fc.item < n_items) {
-        uint8_t* dst = my_raw + (size_t)f_slot * (kRawSlot);
-        cp_async16(dst, fc.blk);
-        cp_async16(dst + 16, fc.blk + 16 + 32 * fc.g);
-        cp_async16(dst + 32, fc.blk + 32 + 32 * fc.g);
-        step(fc);
-        if (fc.item < n_items) step(fc);
+        const int n = nsub_of(fc.st);
+        const uint8_t* blk = fc.blk;
+        int g = fc.g;
+        uint8_t* dst = my_raw + (size_t)f_slot * kSlot;
+#pragma unroll
+        for (int sub = 0; sub < KSUB; ++sub) {
+          if (sub < n) {
+            cp_async16(dst + sub * kRawRow, blk);
+            cp_async16(dst + sub * kRawRow + 16, blk + 16 + 32 * g);
+            cp_async16(dst + sub * kRawRow + 32, blk + 32 + 32 * g);
+            if (++g == 4) {
+              g = 0;
+              blk += 144;
+            }
+          }
+        }
+        for (int i = 0; i < NG && fc.item < n_items; ++i) step(fc);
       }
       cp_async_commit();
-      if (++f_slot == kRawDepth) f_slot = 0;
+      if (++f_slot == kDepth) f_slot = 0;
     };
 #pragma unroll 1
-    for (int i = 0; i < kRawDepth - 1; ++i) fetch();
-    int s = grp, c_slot = 0;  // stage of k-block number grp, then every second one
+    for (int i = 0; i < kDepth - 1; ++i) fetch();
+    int s = grp, c_slot = 0;  // ring stage of this group's first stage, then every NG-th one
     uint32_t ph = 0;
     while (cc.item < n_items) {
       fetch();
-      cp_async_wait<kRawDepth - 1>();  // this thread's bytes for the compute cursor have landed
-      const uint8_t* src = my_raw + (size_t)c_slot * kRawSlot;
-      const uint4 hd = *reinterpret_cast<const uint4*>(src);
-      const uint4 q0 = *reinterpret_cast<const uint4*>(src + 16);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(src + 32);
-      if (++c_slot == kRawDepth) c_slot = 0;
-      // getScaleMinK4 (Q4_KFloatTensor.kt:70-84) for sub-blocks 2g (low nibbles) and 2g+1 (high)
-      const int g = cc.g;
-      SubConst kc[2];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int j = 2 * g + hh;
-        uint32_t sc, mn;
-        if (j < 4) {
-          sc = scale_byte(hd.y, hd.z, hd.w, j) & 63u;
-          mn = scale_byte(hd.y, hd.z, hd.w, j + 4) & 63u;
-        } else {
-          const uint32_t bj4 = scale_byte(hd.y, hd.z, hd.w, j + 4);
-          sc = (bj4 & 0xFu) | ((scale_byte(hd.y, hd.z, hd.w, j - 4) >> 6) << 4);
-          mn = (bj4 >> 4) | ((scale_byte(hd.y, hd.z, hd.w, j) >> 6) << 4);
-        }
-        const float d = f16_bits_to_f32((uint16_t)(hd.x & 0xFFFFu));
-        const float dmin = f16_bits_to_f32((uint16_t)(hd.x >> 16));
-        const float sf = d * (float)sc;     // exact: 11-bit by 6-bit product
-        const float mf = dmin * (float)mn;  // exact
-        kc[hh] = sub_const(hh ? sf * 0.0625f : sf, mf);
-      }
-      const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-      uint4 ch[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint2 la = q4_word_to_f16(qw[2 * i], 0x000F000Fu, kc[0]);
-        const uint2 lb = q4_word_to_f16(qw[2 * i + 1], 0x000F000Fu, kc[0]);
-        const uint2 ha = q4_word_to_f16(qw[2 * i], 0x00F000F0u, kc[1]);
-        const uint2 hb = q4_word_to_f16(qw[2 * i + 1], 0x00F000F0u, kc[1]);
-        ch[i] = make_uint4(la.x, la.y, lb.x, lb.y);
-        ch[4 + i] = make_uint4(ha.x, ha.y, hb.x, hb.y);
-      }
+      cp_async_wait<kDepth - 1>();  // this thread's bytes for the compute cursor have landed
+      const int n = nsub_of(cc.st);
       // every lane waits; the verdict is made warp-uniform so the warp never splits
       if (!__all_sync(0xffffffffu, tc_wait(&empty[s], ph ^ 1u, abort_flag, a.status, ERR_TIMEOUT_EMPTY))) break;
-      uint8_t* dst = a_st + (size_t)s * kATile + row_off;
+      int g = cc.g;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + (((uint32_t)c ^ (uint32_t)(t & 7)) << 4)) = ch[c];
-      fence_async_smem();
+      for (int sub = 0; sub < KSUB; ++sub) {
+        if (sub < n) {
+          const uint8_t* src = my_raw + (size_t)c_slot * kSlot + sub * kRawRow;
+          const uint4 hd = *reinterpret_cast<const uint4*>(src);
+          const uint4 q0 = *reinterpret_cast<const uint4*>(src + 16);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(src + 32);
+          // getScaleMinK4 (Q4_KFloatTensor.kt:70-84) for sub-blocks 2g (low nibbles) and 2g+1 (high)
+          SubConst kc[2];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int j = 2 * g + hh;
+            uint32_t sc, mn;
+            if (j < 4) {
+              sc = scale_byte(hd.y, hd.z, hd.w, j) & 63u;
+              mn = scale_byte(hd.y, hd.z, hd.w, j + 4) & 63u;
+            } else {
+              const uint32_t bj4 = scale_byte(hd.y, hd.z, hd.w, j + 4);
+              sc = (bj4 & 0xFu) | ((scale_byte(hd.y, hd.z, hd.w, j - 4) >> 6) << 4);
+              mn = (bj4 >> 4) | ((scale_byte(hd.y, hd.z, hd.w, j) >> 6) << 4);
+            }
+            const float d = f16_bits_to_f32((uint16_t)(hd.x & 0xFFFFu));
+            const float dmin = f16_bits_to_f32((uint16_t)(hd.x >> 16));
+            const float sf = d * (float)sc;     // exact: 11-bit by 6-bit product
+            const float mf = dmin * (float)mn;  // exact
+            kc[hh] = sub_const(hh ? sf * 0.0625f : sf, mf);
+          }
+          const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          if (TMEM_A) {
+            // word i of the row (stored K positions 2i, 2i+1) goes to column i of the sub-tile
+            uint32_t r[32];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint2 la = q4_word_to_f16(qw[2 * i], 0x000F000Fu, kc[0]);
+              const uint2 lb = q4_word_to_f16(qw[2 * i + 1], 0x000F000Fu, kc[0]);
+              const uint2 ha = q4_word_to_f16(qw[2 * i], 0x00F000F0u, kc[1]);
+              const uint2 hb = q4_word_to_f16(qw[2 * i + 1], 0x00F000F0u, kc[1]);
+              r[4 * i] = la.x, r[4 * i + 1] = la.y, r[4 * i + 2] = lb.x, r[4 * i + 3] = lb.y;
+              r[16 + 4 * i] = ha.x, r[16 + 4 * i + 1] = ha.y, r[16 + 4 * i + 2] = hb.x, r[16 + 4 * i + 3] = hb.y;
+            }
+            tmem_st32(tmem_base + ((uint32_t)(32 * (gwarp & 3)) << 16) + a.tmem_a_col + (uint32_t)(s * KSUB + sub) * 32u,
+                      r);
+          } else {
+            uint8_t* dst = a_st + (size_t)(s * KSUB + sub) * kATile + row_off;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint2 la = q4_word_to_f16(qw[2 * i], 0x000F000Fu, kc[0]);
+              const uint2 lb = q4_word_to_f16(qw[2 * i + 1], 0x000F000Fu, kc[0]);
+              const uint2 ha = q4_word_to_f16(qw[2 * i], 0x00F000F0u, kc[1]);
+              const uint2 hb = q4_word_to_f16(qw[2 * i + 1], 0x00F000F0u, kc[1]);
+              *reinterpret_cast<uint4*>(dst + (((uint32_t)i ^ (uint32_t)(t & 7)) << 4)) =
+                  make_uint4(la.x, la.y, lb.x, lb.y);
+              *reinterpret_cast<uint4*>(dst + (((uint32_t)(4 + i) ^ (uint32_t)(t & 7)) << 4)) =
+                  make_uint4(ha.x, ha.y, hb.x, hb.y);
+            }
+          }
+          g = (g + 1) & 3;
+        }
+      }
+      if (++c_slot == kDepth) c_slot = 0;
+      if (TMEM_A) {
+        tmem_st_wait();  // the rows are in tensor memory before the MMA thread hears of them
+        tc_fence_before();
+      } else {
+        fence_async_smem();
+      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[s]);
-      s += 2;  // this group's next k-block is two on
+      if (lane == 0) mbar_arrive(&full[s]);
+      s += NG;  // this group's next stage is NG on (S >= NG)
       if (s >= S) {
         s -= S;
         ph ^= 1u;
       }
-      step(cc);
-      if (cc.item < n_items) step(cc);
+      for (int i = 0; i < NG && cc.item < n_items; ++i) step(cc);
     }
     cp_async_wait<0>();  // no copy of this thread outlives the role (after an abort too)
   } else {
     // ------------------------------------------------ epilogue
-    const int q = warp & 3;  // tensor-memory lane quarter this warp may access
+    const int q = gwarp & 3;  // tensor-memory lane quarter this warp may access
     uint32_t acc = 0, aph = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    for (int item = blockIdx.x + pp * gridDim.x; item < n_items; item += P * gridDim.x) {
       const int4 tl = a.tiles[item / R];
       const int rt = item % R, n = tl.z, p0 = tl.y;
       if (!__all_sync(0xffffffffu, tc_wait(&tfull[acc], aph, abort_flag, a.status, ERR_TIMEOUT_FULL))) break;
@@ -600,10 +702,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
-  if (warp == 0) {
+  if (gwarp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, a.tmem_cols);
+    tmem_dealloc(*tmem_slot0, a.tmem_cols);
   }
 }
 
@@ -677,7 +779,7 @@ bool moe_tc_wanted(int T, int K, int E) {
   const char* env = std::getenv("G4_MOE_TC");
   if (env && env[0] == '0') return false;
   if (env && env[0] == '1') return true;
-  return (long long)T * K >= 4ll * E;  // four or more tokens per expert on average
+  return 4ll * T * K >= (long long)E;  // a quarter of a token per expert on average, or more
 }
 
 cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* down_w, const float* moe_in,
@@ -698,12 +800,29 @@ cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* do
         !make_map(enc, &mg[b], w.g16, (uint64_t)n_pos, (uint64_t)ff, 16u << b))
       return cudaErrorInvalidValue;
   }
-  const int b_stage = cap * 128;
+  const int bsub = cap * 128;  // one 64-column token sub-tile
+  // Narrow token tiles: two pipelines (two MMA issuers), one producer group
+  // each, weights in tensor memory.  128-token tiles: one pipeline, weights in
+  // tensor memory next to the 256 accumulator columns.  256-token tiles: the
+  // accumulators fill tensor memory, weights go through shared memory.
+  const int P = cap <= 64 ? 2 : 1;
+  const int ng = cap <= 64 ? 1 : 2;
+  const int ksub = 1;
+  const bool tmem_a = cap <= 128;
   const size_t optin = c->dev.smem_optin;
-  int stages = (int)((optin - 1024 - kBarBytes - kRawBytes) / (size_t)(kATile + b_stage));
+  const size_t a_bytes = tmem_a ? 0 : (size_t)kATile;
+  const size_t raw_bytes = (size_t)tc_raw_bytes(ng);
+  const size_t stage_bytes = (size_t)ksub * (a_bytes + bsub);
+  const size_t pipe_budget = (optin - 1024) / P;
+  if (pipe_budget < raw_bytes + kBarBytes + 2 * stage_bytes) return cudaErrorInvalidConfiguration;
+  int stages = (int)((pipe_budget - raw_bytes - kBarBytes) / stage_bytes);
+  if (tmem_a) stages = std::min(stages, (512 / P - 2 * cap) / (32 * ksub));
   if (stages > kMaxStages) stages = kMaxStages;
-  if (stages < 2) return cudaErrorInvalidConfiguration;
-  const size_t smem = 1024 + (size_t)stages * (kATile + b_stage) + kRawBytes + kBarBytes;
+  if (stages < ng || stages < 2) return cudaErrorInvalidConfiguration;  // every group needs a stage of its own
+  const size_t pipe_bytes = (stages * stage_bytes + raw_bytes + kBarBytes + 1023) / 1024 * 1024;
+  // at least 120 KB, so that one CTA per SM holds all 512 tensor-memory columns
+  const size_t smem = std::max<size_t>(1024 + P * pipe_bytes, 120 * 1024);
+  if (smem > optin) return cudaErrorInvalidConfiguration;
 
   TcArgs ga{};
   ga.w = gate_up_w;
@@ -714,9 +833,11 @@ cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* do
   ga.n_row_tiles = ff / 64;
   ga.nkb = dim / kKB;
   ga.stages = stages;
-  ga.b_stage_bytes = b_stage;
+  ga.b_stage_bytes = bsub;
   ga.acc_cols = cap;
-  ga.tmem_cols = 2u * (uint32_t)cap;
+  ga.tmem_cols = 512;
+  ga.tmem_a_col = 2u * (uint32_t)cap;
+  ga.pipe_bytes = (int)pipe_bytes;
   ga.tiles = w.tiles;
   ga.n_tiles = w.n_tiles;
   ga.perm = perm;
@@ -734,16 +855,20 @@ cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* do
   da.g16 = nullptr;
   da.D = D;
 
+  using Kern = void (*)(TcArgs, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap);
+  const Kern kg = P == 2 ? moe_tc_kernel<true, 1, true, 1, 2> : tmem_a ? moe_tc_kernel<true, 1, true, 2, 1>
+                                                                       : moe_tc_kernel<true, 1, false, 2, 1>;
+  const Kern kd = P == 2 ? moe_tc_kernel<false, 1, true, 1, 2> : tmem_a ? moe_tc_kernel<false, 1, true, 2, 1>
+                                                                        : moe_tc_kernel<false, 1, false, 2, 1>;
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(moe_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
-          cudaSuccess ||
-      (e = cudaFuncSetAttribute(moe_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
-          cudaSuccess)
+  if ((e = cudaFuncSetAttribute(kg, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
     return e;
   const int grid = c->dev.sms;
-  moe_tc_kernel<true><<<grid, kThreads, smem, st>>>(ga, mx[0], mx[1], mx[2], mx[3], mx[4]);
+  const int threads = P * tc_threads(ng);
+  kg<<<grid, threads, smem, st>>>(ga, mx[0], mx[1], mx[2], mx[3], mx[4]);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  moe_tc_kernel<false><<<grid, kThreads, smem, st>>>(da, mg[0], mg[1], mg[2], mg[3], mg[4]);
+  kd<<<grid, threads, smem, st>>>(da, mg[0], mg[1], mg[2], mg[3], mg[4]);
   return cudaGetLastError();
 }
 
