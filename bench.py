@@ -37,6 +37,7 @@ sys.path.insert(0, str(ROOT))
 SHAPES = [(1536, 1536), (6144, 1536), (1536, 6144), (262144, 1536)]
 FORMATS = [("Q8_0", 8), ("Q4_K", 12), ("Q6_K", 14), ("BF16", 30)]
 METRIC = "quant GEMV HBM GB/s"
+FALLBACK_TFLOPS = 1590.0
 FALLBACK_HBM = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
 # (profiles/gemv_rows_bf16_262144x1536.md, profiles/gemv_rows_q4k_262144x1536.md)
@@ -391,6 +392,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     moe = None
     if world == 1 and rank == 0 and not args.no_moe:
         moe = bench_moe(g4, ctx, torch, dev)
+    elif world > 1 and not args.no_moe:
+        moe = bench_moe_ep(g4, ctx, torch, dev, rank, world)
 
     if rank == 0:
         line = {
@@ -426,15 +429,24 @@ def bench_moe(g4, ctx, torch, dev):
 
     d = synth.MoeLayerData(seed=2)
     layer = g4.MoeLayer.upload(ctx, d)
+    hbm, _ = peaks()
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tensor_peak = float(pk.get("bf16_tflops", FALLBACK_TFLOPS))
+    # Q4_K bytes of one expert (gate_up 2ff x dim + down dim x ff) and its multiply-adds per slot
+    expert_w = 2 * d.ff * d.dim + d.dim * d.ff
+    expert_bytes = expert_w * 144 // 256
     res = {}
     for T in (1, 16, 256, 4096):
         x = torch.from_numpy(d.tokens(T)).to(dev)
         out = torch.empty((T, d.dim), dtype=torch.float32, device=dev)
+        idx = torch.empty((T, d.n_used), dtype=torch.int32, device=dev)
         stream = torch.cuda.Stream(dev)
         with torch.cuda.stream(stream):
-            for _ in range(3):
+            layer.forward(x, out, T, topk_idx=idx, stream=stream.cuda_stream)
+            for _ in range(2):
                 layer.forward(x, out, T, stream=stream.cuda_stream)
         torch.cuda.synchronize()
+        n_unique = int(torch.unique(idx).numel())
         # one layer call captured as a CUDA graph (its launches back to back)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
@@ -453,10 +465,62 @@ def bench_moe(g4, ctx, torch, dev):
         torch.cuda.synchronize()
         us = a.elapsed_time(b) * 1e3 / reps
         del g
-        res[f"T{T}"] = {"us_per_layer": round(us, 2), "us_per_token": round(us / T, 3)}
+        # algorithmic bytes: weights of the experts routed to + router weights + activations in and out
+        nbytes = n_unique * expert_bytes + d.dim * d.n_expert * 4 + 2 * T * d.dim * 4
+        flops = 2.0 * T * d.n_used * expert_w + 2.0 * T * d.dim * d.n_expert
+        gbs = nbytes / (us * 1e-6) / 1e9
+        tfs = flops / (us * 1e-6) / 1e12
+        res[f"T{T}"] = {"us_per_layer": round(us, 2), "us_per_token": round(us / T, 3),
+                        "experts_touched": n_unique, "GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                        "TFLOPs": round(tfs, 2), "tensor_frac": round(tfs / tensor_peak, 4),
+                        "path": "tcgen05 grouped GEMM" if 4 * T * d.n_used >= d.n_expert else "CUDA-core rows"}
     ctx.sync()
     return {"metric": "MoE layer us/token", "config": "hidden 2816, 128 experts top-8, ff 704, Q4_K, seed 2",
             "timing": "CUDA graph of one g4_moe_layer call, replayed",
+            "roofline": "hbm_frac = (touched experts' Q4_K bytes + router + activations) / time / measured HBM; "
+                        "tensor_frac = 2*T*8*5947392 flops / time / measured bf16 dense peak",
+            **res}
+
+
+def bench_moe_ep(g4, ctx, torch, dev, rank: int, world: int):
+    """MoE layer (config 3) expert-parallel over `world` GPUs: every rank holds
+    128/world experts and T/world of the T tokens of a layer call; device time
+    of one g4_moe_layer_ep call (CUDA events, max over ranks)."""
+    import torch.distributed as dist
+
+    from gemma4_kt_b200 import synth
+
+    d = synth.MoeLayerData(seed=2)
+    layer = g4.MoeLayer.upload_shard(ctx, d, rank, world)
+    stream = torch.cuda.Stream(dev)
+    res = {}
+    for T_total in (256, 4096):
+        T = T_total // world
+        x = torch.from_numpy(d.tokens(T_total)[rank * T:(rank + 1) * T].copy()).to(dev)
+        out = torch.empty((T, d.dim), dtype=torch.float32, device=dev)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                layer.forward_ep(x, out, T, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        reps = 10
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for _ in range(reps):
+                layer.forward_ep(x, out, T, stream=stream.cuda_stream)
+            b.record(stream)
+        torch.cuda.synchronize()
+        tt = torch.tensor([a.elapsed_time(b) * 1e3 / reps], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        us = float(tt.item())
+        res[f"T{T_total}"] = {"us_per_layer": round(us, 2), "us_per_token": round(us / T_total, 3),
+                              "tokens_per_rank": T}
+    ctx.sync()
+    return {"metric": "MoE layer us/token", "config": "hidden 2816, 128 experts top-8, ff 704, Q4_K, seed 2",
+            "parallelism": f"expert-parallel x{world} ({128 // world} experts per GPU), NCCL send/recv dispatch "
+                           "and return",
+            "timing": "CUDA events around 10 g4_moe_layer_ep calls (one host count exchange each), max over ranks",
             **res}
 
 

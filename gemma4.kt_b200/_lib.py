@@ -43,6 +43,7 @@ SIGNATURES = {
     "g4_moe_layer_host": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "g4_moe_topk": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp, _vp]),
     "g4_moe_layer_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
+    "g4_moe_layer_ep": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "g4_dist_unique_id": (_i, [_vp]),
     "g4_dist_init": (_i, [_vp, _i, _i, _vp]),
     "g4_dist_rank": (_i, [_vp]),

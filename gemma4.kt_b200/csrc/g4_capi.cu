@@ -82,6 +82,24 @@ void* g4_ctx::io(size_t bytes) {
   return io_ptr;
 }
 
+void* g4_ctx::ep(size_t bytes) {
+  if (bytes <= ep_bytes) return ep_ptr;
+  if (ep_ptr) {
+    cudaDeviceSynchronize();
+    cudaFree(ep_ptr);
+  }
+  ep_ptr = nullptr;
+  ep_bytes = 0;
+  const size_t want = bytes + bytes / 4 + (1u << 20);
+  if (cudaMalloc(&ep_ptr, want) != cudaSuccess) {
+    cudaGetLastError();
+    ep_ptr = nullptr;
+    return nullptr;
+  }
+  ep_bytes = want;
+  return ep_ptr;
+}
+
 int g4_ctx::check_status(cudaStream_t st) {
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_fail(e, "kernel execution");
@@ -149,6 +167,7 @@ int g4_destroy(g4_ctx* c) {
   if (c->scratch_ptr) cudaFree(c->scratch_ptr);
   if (c->pinned_ptr) cudaFreeHost(c->pinned_ptr);
   if (c->io_ptr) cudaFree(c->io_ptr);
+  if (c->ep_ptr) cudaFree(c->ep_ptr);
   if (c->status) cudaFree(c->status);
   delete c;
   return 0;
@@ -433,3 +452,36 @@ void g4_dist_teardown(g4_ctx* c) {
 }
 
 bool g4_nccl_send_recv_available() { return g_nccl.loaded; }
+
+int g4_nccl_allgather_i32(g4_ctx* c, const int32_t* send, int32_t* recv, size_t count, cudaStream_t st) {
+  if (!c->comm) {
+    c->set_err("expert-parallel layer: g4_dist_init not called");
+    return G4_E_DIST;
+  }
+  const ncclResult_t r = g_nccl.allGather(send, recv, count, ncclInt32, (ncclComm_t)c->comm, st);
+  if (r != ncclSuccess) {
+    c->set_err("ncclAllGather: %s", g_nccl.errStr(r));
+    return G4_E_DIST;
+  }
+  return 0;
+}
+
+int g4_nccl_alltoallv(g4_ctx* c, const void* send, const size_t* soff, const size_t* slen, void* recv,
+                      const size_t* roff, const size_t* rlen, cudaStream_t st) {
+  if (!c->comm) {
+    c->set_err("expert-parallel layer: g4_dist_init not called");
+    return G4_E_DIST;
+  }
+  ncclComm_t comm = (ncclComm_t)c->comm;
+  ncclResult_t r = g_nccl.groupStart();
+  for (int p = 0; r == ncclSuccess && p < c->world; ++p) {
+    if (slen[p]) r = g_nccl.send((const uint8_t*)send + soff[p], slen[p], ncclUint8, p, comm, st);
+    if (r == ncclSuccess && rlen[p]) r = g_nccl.recv((uint8_t*)recv + roff[p], rlen[p], ncclUint8, p, comm, st);
+  }
+  const ncclResult_t r2 = g_nccl.groupEnd();
+  if (r != ncclSuccess || r2 != ncclSuccess) {
+    c->set_err("NCCL send/recv group: %s", g_nccl.errStr(r != ncclSuccess ? r : r2));
+    return G4_E_DIST;
+  }
+  return 0;
+}

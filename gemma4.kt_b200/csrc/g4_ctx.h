@@ -18,6 +18,8 @@ struct g4_ctx {
   size_t pinned_bytes = 0;
   void* io_ptr = nullptr;      // device staging for the *_host entry points
   size_t io_bytes = 0;
+  void* ep_ptr = nullptr;      // receive-side buffers of the expert-parallel MoE layer
+  size_t ep_bytes = 0;
   void* comm = nullptr;        // ncclComm_t when g4_dist_init has run
   int rank = 0;
   int world = 1;
@@ -31,6 +33,7 @@ struct g4_ctx {
   void* scratch(size_t bytes);
   void* pinned(size_t bytes);
   void* io(size_t bytes);
+  void* ep(size_t bytes);
   int check_status(cudaStream_t st);
 };
 
@@ -43,3 +46,12 @@ struct g4_tensor {
 };
 
 void g4_dist_teardown(g4_ctx* c);
+
+// Collectives of the expert-parallel MoE layer, over the context's NCCL
+// communicator (g4_dist_init).  Return 0 or a G4_E_* code with the message set.
+//   allgather: recv[r*count + i] = send_of_rank_r[i]
+//   alltoallv: to every peer p, send[soff[p], soff[p]+slen[p]) bytes; from every
+//              peer p, receive rlen[p] bytes at recv + roff[p] (one NCCL group)
+int g4_nccl_allgather_i32(g4_ctx* c, const int32_t* send, int32_t* recv, size_t count, cudaStream_t st);
+int g4_nccl_alltoallv(g4_ctx* c, const void* send, const size_t* soff, const size_t* slen, void* recv,
+                      const size_t* roff, const size_t* rlen, cudaStream_t st);

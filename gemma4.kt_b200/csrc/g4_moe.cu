@@ -26,6 +26,7 @@
 #include <cmath>
 #include <map>
 #include <mutex>
+#include <vector>
 
 namespace g4 {
 
@@ -1359,6 +1360,20 @@ static MoeScratch carve(uint8_t* base, int T, int dim, int E, int K, int ff) {
   return m;
 }
 
+// offsets[e] / perm for n_slots slots routed by idx[] to E buckets.  `work`
+// holds ceil(n_slots / kPermChunk) * E ints (used when n_slots is large).
+static void launch_permute(const int32_t* idx, int n_slots, int E, int32_t* offsets, int32_t* perm, int32_t* work,
+                           cudaStream_t st) {
+  if (n_slots <= 2 * kPermChunk) {
+    moe_permute_kernel<<<1, 1024, 0, st>>>(idx, n_slots, E, offsets, perm);
+  } else {
+    const int nb = (n_slots + kPermChunk - 1) / kPermChunk;
+    moe_perm_count_kernel<<<nb, 256, 0, st>>>(idx, n_slots, E, work);
+    moe_perm_scan_kernel<<<1, kMaxExperts, 0, st>>>(work, nb, E, offsets);
+    moe_perm_place_kernel<<<nb, 256, 0, st>>>(idx, n_slots, E, work, perm);
+  }
+}
+
 // Front of the layer, shared by every entry point: norms (prep), router
 // logits, softmax + top-k, and the slot permutation.  The router's split-K
 // partials and the permutation's chunk counts use the D buffer, which the
@@ -1378,16 +1393,7 @@ static cudaError_t launch_front(g4_ctx* c, const g4_moe_weights* w, const float*
                                                                   dim, E);
   moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(nsplit ? m.D : m.logits, nsplit ? nsplit : 1, T, E, K, m.idx,
                                                m.prob);
-  const int n_slots = T * K;
-  if (n_slots <= 2 * kPermChunk) {
-    moe_permute_kernel<<<1, 1024, 0, st>>>(m.idx, n_slots, E, m.offsets, m.perm);
-  } else {
-    const int nb = (n_slots + kPermChunk - 1) / kPermChunk;
-    int32_t* cnt = reinterpret_cast<int32_t*>(m.D);  // nb*E ints, far below T*K*dim
-    moe_perm_count_kernel<<<nb, 256, 0, st>>>(m.idx, n_slots, E, cnt);
-    moe_perm_scan_kernel<<<1, kMaxExperts, 0, st>>>(cnt, nb, E, m.offsets);
-    moe_perm_place_kernel<<<nb, 256, 0, st>>>(m.idx, n_slots, E, cnt, m.perm);
-  }
+  launch_permute(m.idx, T * K, E, m.offsets, m.perm, reinterpret_cast<int32_t*>(m.D), st);
   return cudaGetLastError();
 }
 
@@ -1833,6 +1839,204 @@ extern "C" int g4_moe_layer_host(g4_ctx* c, const g4_moe_weights* w, const float
   if (idx_h) cudaMemcpyAsync(idx_h, id, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st);
   if (prob_h) cudaMemcpyAsync(prob_h, pd, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st);
   return c->check_status(st);
+}
+
+// ============================================================================
+// Expert-parallel MoE layer (one process per GPU, NCCL).
+//
+// Rank r holds experts [r*El, (r+1)*El) of the layer (El = n_expert / world)
+// and the replicated router, scales and norms, and owns its own tokens.  A
+// call routes the rank's tokens, sends every routed slot's moe_in row to the
+// rank that owns its expert, runs the grouped expert products over what it
+// received, sends the products back and combines them on the owner in the
+// reference's selection order: the same arithmetic as g4_moe_layer.
+// ============================================================================
+
+// dest[s] = owning rank of slot s's expert
+__global__ void moe_ep_dest_kernel(const int32_t* __restrict__ idx, int n, int e_local, int32_t* __restrict__ dest) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s < n) dest[s] = idx[s] / e_local;
+}
+// send order p (slots grouped by destination): row p = moe_in of the slot's
+// token, eid[p] = the expert's index at the destination.  One warp per row.
+__global__ void __launch_bounds__(256) moe_ep_pack_kernel(const float* __restrict__ moe_in,
+                                                          const int32_t* __restrict__ idx,
+                                                          const int32_t* __restrict__ perm, int n, int dim, int K,
+                                                          int e_local, float* __restrict__ rows,
+                                                          int32_t* __restrict__ eid) {
+  const int p = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (p >= n) return;
+  const int slot = perm[p];
+  const float4* src = reinterpret_cast<const float4*>(moe_in + (size_t)(slot / K) * dim);
+  float4* dst = reinterpret_cast<float4*>(rows + (size_t)p * dim);
+  for (int i = lane; i < dim / 4; i += 32) dst[i] = __ldg(src + i);
+  if (lane == 0) eid[p] = idx[slot] % e_local;
+}
+// D[slot of send position p] = back[p]
+__global__ void __launch_bounds__(256) moe_ep_unpack_kernel(const float* __restrict__ back,
+                                                            const int32_t* __restrict__ perm, int n, int dim,
+                                                            float* __restrict__ D) {
+  const int p = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (p >= n) return;
+  const float4* src = reinterpret_cast<const float4*>(back + (size_t)p * dim);
+  float4* dst = reinterpret_cast<float4*>(D + (size_t)perm[p] * dim);
+  for (int i = lane; i < dim / 4; i += 32) dst[i] = src[i];
+}
+
+extern "C" int g4_moe_layer_ep(g4_ctx* c, const g4_moe_weights* w, const float* x, float* out, int T,
+                               int32_t* topk_idx, float* topk_prob, void* stream) {
+  if (!c) return G4_E_ARG;
+  if (!w || (T > 0 && (!x || !out)) || T < 0) {
+    c->set_err("g4_moe_layer_ep: bad argument");
+    return G4_E_ARG;
+  }
+  const int world = c->world, rank = c->rank;
+  const int dim = w->dim, E = w->n_expert, K = w->n_used, ff = w->expert_ff;
+  if (dim <= 0 || E < 1 || E > kMaxExperts || K < 1 || K > E || K > kMaxUsed || ff <= 0 || dim % 4 ||
+      E % world) {
+    c->set_err("g4_moe_layer_ep: unsupported geometry dim=%d experts=%d used=%d ff=%d world=%d", dim, E, K, ff,
+               world);
+    return G4_E_ARG;
+  }
+  const int El = E / world;
+  if (!tensor_ok(w->gate_inp, G4_TYPE_F32, (uint64_t)dim * E) ||
+      !tensor_ok(w->gate_inp_scale, G4_TYPE_F32, dim) || !tensor_ok(w->down_exps_scale, G4_TYPE_F32, E) ||
+      !tensor_ok(w->pre_ffw_norm_2, G4_TYPE_F32, dim) ||
+      (w->post_ffw_norm_2 && !tensor_ok(w->post_ffw_norm_2, G4_TYPE_F32, dim)) ||
+      !tensor_ok(w->gate_up_exps, -1, (uint64_t)dim * 2 * ff * El) ||
+      !tensor_ok(w->down_exps, -1, (uint64_t)ff * dim * El)) {
+    c->set_err("g4_moe_layer_ep: a weight tensor is missing or has the wrong type/size "
+               "(expert tensors hold this rank's %d experts)", El);
+    return G4_E_ARG;
+  }
+  if (!moe_tc_supported(w->gate_up_exps->type, w->down_exps->type, dim, ff, El)) {
+    c->set_err("g4_moe_layer_ep: expert layout not supported (Q4_K experts, dim %% 256 == 0, ff %% 64 == 0)");
+    return G4_E_TYPE;
+  }
+  if ((long long)T * K * world > (1 << 24)) {
+    c->set_err("g4_moe_layer_ep: too many tokens (%d)", T);
+    return G4_E_ARG;
+  }
+  if (world > 1 && !c->comm) {
+    c->set_err("g4_moe_layer_ep: g4_dist_init not called");
+    return G4_E_DIST;
+  }
+  if (int r = c->bind()) return r;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int n_slots = T * K;
+
+  // ---- send side: this rank's tokens (scratch arena)
+  const size_t base_need = moe_scratch_bytes(T > 0 ? T : 1, dim, E, K, ff);
+  const size_t ns_al = align_up((size_t)(n_slots > 0 ? n_slots : 1) * 4, 256);
+  const size_t rows_al = align_up((size_t)(n_slots > 0 ? n_slots : 1) * dim * 4, 256);
+  const size_t cnt_al = align_up((size_t)world * (world + 1) * 4, 256);
+  const size_t need = base_need + 3 * ns_al + align_up((size_t)(world + 1) * 4, 256) + 2 * rows_al + cnt_al;
+  uint8_t* base = (uint8_t*)c->scratch(need);
+  if (!base) {
+    c->set_err("g4_moe_layer_ep: cannot allocate %zu bytes of scratch", need);
+    return G4_E_NOMEM;
+  }
+  MoeScratch m = carve(base, T > 0 ? T : 1, dim, E, K, ff);
+  uint8_t* q = base + base_need;
+  int32_t* dest = (int32_t*)q;                 q += ns_al;
+  int32_t* perm_d = (int32_t*)q;               q += ns_al;
+  int32_t* send_eid = (int32_t*)q;             q += ns_al;
+  int32_t* off_d = (int32_t*)q;                q += align_up((size_t)(world + 1) * 4, 256);
+  float* send_rows = (float*)q;                q += rows_al;
+  float* back_rows = (float*)q;                q += rows_al;
+  int32_t* off_all = (int32_t*)q;
+
+  cudaError_t e = cudaSuccess;
+  if (T > 0) {
+    e = launch_front(c, w, x, m, T, false, st);
+    if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_ep launch");
+    moe_ep_dest_kernel<<<(n_slots + 255) / 256, 256, 0, st>>>(m.idx, n_slots, El, dest);
+    launch_permute(dest, n_slots, world, off_d, perm_d, reinterpret_cast<int32_t*>(m.G), st);
+    moe_ep_pack_kernel<<<(n_slots + 7) / 8, 256, 0, st>>>(m.moe_in, m.idx, perm_d, n_slots, dim, K, El, send_rows,
+                                                           send_eid);
+  } else {
+    e = cudaMemsetAsync(off_d, 0, (size_t)(world + 1) * 4, st);
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_ep dispatch");
+
+  // ---- every rank's send offsets, so each rank knows what it receives from whom
+  if (int r = g4_nccl_allgather_i32(c, off_d, off_all, (size_t)world + 1, st)) return r;
+  int32_t* h_off = (int32_t*)c->pinned((size_t)world * (world + 1) * 4);
+  if (!h_off) {
+    c->set_err("g4_moe_layer_ep: cannot allocate pinned memory");
+    return G4_E_NOMEM;
+  }
+  e = cudaMemcpyAsync(h_off, off_all, (size_t)world * (world + 1) * 4, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_ep count exchange");
+  std::vector<size_t> s_off(world), s_len(world), r_off(world), r_len(world);
+  size_t R = 0;
+  for (int p = 0; p < world; ++p) {
+    const int32_t* mine = h_off + (size_t)rank * (world + 1);
+    const int32_t* theirs = h_off + (size_t)p * (world + 1);
+    s_off[p] = (size_t)mine[p];
+    s_len[p] = (size_t)(mine[p + 1] - mine[p]);
+    r_off[p] = R;
+    r_len[p] = (size_t)(theirs[rank + 1] - theirs[rank]);
+    R += r_len[p];
+  }
+
+  // ---- receive side (ep arena, sized now that the counts are known)
+  const int Ri = (int)(R > 0 ? R : 1);
+  const size_t rr_al = align_up((size_t)Ri * dim * 4, 256), ri_al = align_up((size_t)Ri * 4, 256);
+  const size_t tc_need = moe_tc_scratch_bytes(Ri, dim, El, 1, ff);
+  const size_t ep_need = 2 * rr_al + 2 * ri_al + align_up((size_t)(El + 1) * 4, 256) +
+                         align_up((size_t)((Ri + kPermChunk - 1) / kPermChunk) * El * 4, 256) + tc_need;
+  uint8_t* eb = (uint8_t*)c->ep(ep_need);
+  if (!eb) {
+    c->set_err("g4_moe_layer_ep: cannot allocate %zu bytes for received rows", ep_need);
+    return G4_E_NOMEM;
+  }
+  float* recv_rows = (float*)eb;               eb += rr_al;
+  float* recv_out = (float*)eb;                eb += rr_al;
+  int32_t* recv_eid = (int32_t*)eb;            eb += ri_al;
+  int32_t* perm_l = (int32_t*)eb;              eb += ri_al;
+  int32_t* off_l = (int32_t*)eb;               eb += align_up((size_t)(El + 1) * 4, 256);
+  int32_t* perm_work = (int32_t*)eb;           eb += align_up((size_t)((Ri + kPermChunk - 1) / kPermChunk) * El * 4, 256);
+  void* tc_work = eb;
+
+  // ---- dispatch: rows and their local expert ids
+  {
+    std::vector<size_t> so(world), sl(world), ro(world), rl(world);
+    const size_t rb = (size_t)dim * 4;
+    for (int p = 0; p < world; ++p) so[p] = s_off[p] * rb, sl[p] = s_len[p] * rb, ro[p] = r_off[p] * rb,
+                                    rl[p] = r_len[p] * rb;
+    if (int r = g4_nccl_alltoallv(c, send_rows, so.data(), sl.data(), recv_rows, ro.data(), rl.data(), st)) return r;
+    for (int p = 0; p < world; ++p) so[p] = s_off[p] * 4, sl[p] = s_len[p] * 4, ro[p] = r_off[p] * 4, rl[p] = r_len[p] * 4;
+    if (int r = g4_nccl_alltoallv(c, send_eid, so.data(), sl.data(), recv_eid, ro.data(), rl.data(), st)) return r;
+  }
+
+  // ---- this rank's experts over the received rows (each row one slot)
+  if (R > 0) {
+    launch_permute(recv_eid, (int)R, El, off_l, perm_l, perm_work, st);
+    e = cudaGetLastError();
+    if (e == cudaSuccess)
+      e = launch_moe_tc(c, (const uint8_t*)w->gate_up_exps->d, (const uint8_t*)w->down_exps->d, recv_rows, off_l,
+                        perm_l, recv_out, tc_work, (int)R, dim, El, 1, ff, st);
+    if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_ep expert launch");
+  }
+
+  // ---- products back to the ranks that own the tokens, in their send order
+  {
+    std::vector<size_t> so(world), sl(world), ro(world), rl(world);
+    const size_t rb = (size_t)dim * 4;
+    for (int p = 0; p < world; ++p) so[p] = r_off[p] * rb, sl[p] = r_len[p] * rb, ro[p] = s_off[p] * rb,
+                                    rl[p] = s_len[p] * rb;
+    if (int r = g4_nccl_alltoallv(c, recv_out, so.data(), sl.data(), back_rows, ro.data(), rl.data(), st)) return r;
+  }
+  if (T == 0) return 0;
+  moe_ep_unpack_kernel<<<(n_slots + 7) / 8, 256, 0, st>>>(back_rows, perm_d, n_slots, dim, m.D);
+  launch_combine(w, m, out, T, st);
+  if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
+  if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : c->cuda_fail(e, "g4_moe_layer_ep");
 }
 
 // ============================================================================

@@ -45,6 +45,50 @@ class MoeLayer:
             post_ffw_norm_2=up(ctx, f32, data.post_norm, data.dim) if post_norm else None,
         )
 
+    @staticmethod
+    def expert_shard(n_expert: int, world: int, rank: int) -> tuple[int, int]:
+        """Experts [begin, begin + count) that `rank` of `world` holds in the
+        expert-parallel layer (contiguous, equal shares)."""
+        if world < 1 or not 0 <= rank < world:
+            raise ValueError(f"bad rank {rank} of world {world}")
+        if n_expert % world:
+            raise ValueError(f"{n_expert} experts do not split evenly over {world} GPUs")
+        per = n_expert // world
+        return rank * per, per
+
+    @staticmethod
+    def upload_shard(ctx: Context, data, rank: int, world: int, post_norm: bool = True) -> "MoeLayer":
+        """Upload the expert-parallel share of rank `rank`: its experts' slices
+        of ffn_gate_up_exps / ffn_down_exps (whole experts are contiguous in the
+        GGUF block stream), everything else replicated."""
+        e0, ne = MoeLayer.expert_shard(data.n_expert, world, rank)
+        t = GGMLType(int(data.expert_type))
+        gu_n, dn_n = 2 * data.ff * data.dim, data.dim * data.ff  # elements per expert
+        gu_b, dn_b = t.byte_size_for(gu_n), t.byte_size_for(dn_n)
+        raw_gu = np.frombuffer(data.gate_up, np.uint8) if not isinstance(data.gate_up, np.ndarray) else data.gate_up.view(np.uint8).reshape(-1)
+        raw_dn = np.frombuffer(data.down, np.uint8) if not isinstance(data.down, np.ndarray) else data.down.view(np.uint8).reshape(-1)
+        f32 = GGMLType.F32
+        up = FloatTensorFactory.create
+        return MoeLayer(
+            ctx, dim=data.dim, n_expert=data.n_expert, n_used=data.n_used, expert_ff=data.ff, eps=data.eps,
+            gate_inp=up(ctx, f32, data.gate_inp, data.n_expert * data.dim),
+            gate_inp_scale=up(ctx, f32, data.gate_inp_scale, data.dim),
+            gate_up_exps=up(ctx, t, raw_gu[e0 * gu_b:(e0 + ne) * gu_b], ne * gu_n),
+            down_exps=up(ctx, t, raw_dn[e0 * dn_b:(e0 + ne) * dn_b], ne * dn_n),
+            down_exps_scale=up(ctx, f32, data.down_scale, data.n_expert),
+            pre_ffw_norm_2=up(ctx, f32, data.pre_norm, data.dim),
+            post_ffw_norm_2=up(ctx, f32, data.post_norm, data.dim) if post_norm else None,
+        )
+
+    def forward_ep(self, x, out, n_tokens: int, topk_idx=None, topk_prob=None, stream=None) -> None:
+        """Expert-parallel forward (g4_moe_layer_ep) of this rank's n_tokens
+        tokens; every rank of the communicator must call it at the same time.
+        x, out: torch CUDA tensors [n_tokens, dim] (may be empty)."""
+        p = lambda t: C.c_void_p(t.data_ptr()) if t is not None and t.numel() else None
+        rc = lib().g4_moe_layer_ep(self.ctx.handle, C.byref(self.w), p(x), p(out), n_tokens, p(topk_idx),
+                                   p(topk_prob), C.c_void_p(_stream_ptr(stream)))
+        check(rc, self.ctx.handle, "g4_moe_layer_ep")
+
     def forward(self, x, out, n_tokens: int, topk_idx=None, topk_prob=None, stream=None) -> None:
         """x, out: [n_tokens, dim]; topk_idx (int32) / topk_prob: [n_tokens, n_used] or None.
         torch CUDA tensors run asynchronously on `stream`; numpy arrays synchronously."""

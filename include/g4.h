@@ -165,6 +165,20 @@ int g4_moe_layer_host(g4_ctx *ctx, const g4_moe_weights *w, const float *x_host,
 int g4_moe_layer_noalloc(g4_ctx *ctx, const g4_moe_weights *w, const float *x_dev, float *out_dev,
                          int n_tokens, int32_t *topk_idx_dev, float *topk_prob_dev, void *stream);
 
+/* Expert-parallel variant of g4_moe_layer for one process per GPU (no
+ * counterpart in the reference, which runs in one process).  After
+ * g4_dist_init, rank r of world W holds experts [r*E/W, (r+1)*E/W): its
+ * gate_up_exps / down_exps tensors contain only those experts, in the same
+ * per-expert layout; gate_inp, gate_inp_scale, down_exps_scale (all E) and
+ * the norms are replicated.  Every rank calls this with its own n_tokens
+ * tokens (0 allowed) at the same time: each routed slot's row travels to the
+ * rank owning its expert (NCCL send/recv), the products come back and are
+ * combined on the owning rank exactly as g4_moe_layer combines them.
+ * topk_* report global expert ids.  Synchronises the stream once (the row
+ * counts are exchanged through the host).  Q4_K experts only. */
+int g4_moe_layer_ep(g4_ctx *ctx, const g4_moe_weights *w_local, const float *x_dev, float *out_dev,
+                    int n_tokens, int32_t *topk_idx_dev, float *topk_prob_dev, void *stream);
+
 /* Router top-k alone on given logits (Llama.kt:273-293 + softmaxInPlace,
  * MutableFloatTensor.kt:54-59): probs_dev/idx_dev [n_tokens, k]. */
 int g4_moe_topk(g4_ctx *ctx, const float *logits_dev, int n_tokens, int n_expert, int k,

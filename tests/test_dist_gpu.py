@@ -91,3 +91,69 @@ def test_matmul_sharded_two_gpus():
             y = got[r][i]
             err = np.linalg.norm(y - ref) / np.linalg.norm(ref)
             assert err < TOL, (t.name, r, err)
+
+
+def _ep_rank_main(rank, world, port, q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from gemma4_kt_b200 import synth
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        torch.cuda.set_device(rank)
+        ctx = g4.Context(rank)
+        obj = [g4.Context.dist_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.dist_init(rank, world, obj[0])
+        d = synth.MoeLayerData(seed=2, n_expert=32)
+        full = g4.MoeLayer.upload(ctx, d)
+        ep = g4.MoeLayer.upload_shard(ctx, d, rank, world)
+        res = []
+        for t_per_rank in ((48, 48), (40, 0)):  # the second call leaves rank 1 without tokens
+            T = t_per_rank[rank]
+            x_all = d.tokens(sum(t_per_rank))
+            x = torch.from_numpy(x_all[sum(t_per_rank[:rank]):sum(t_per_rank[:rank]) + T].copy()).cuda()
+            out = torch.empty((T, d.dim), device="cuda")
+            idx = torch.empty((T, d.n_used), dtype=torch.int32, device="cuda")
+            ep.forward_ep(x, out, T, topk_idx=idx)
+            torch.cuda.synchronize()
+            ref = torch.empty((T, d.dim), device="cuda")
+            ridx = torch.empty((T, d.n_used), dtype=torch.int32, device="cuda")
+            if T:
+                full.forward(x, ref, T, topk_idx=ridx)
+            torch.cuda.synchronize()
+            res.append((out.cpu().numpy(), ref.cpu().numpy(), idx.cpu().numpy(), ridx.cpu().numpy()))
+        q.put((rank, res))
+        dist.barrier()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_moe_expert_parallel_two_gpus():
+    """g4_moe_layer_ep over 2 GPUs (16 of 32 experts each) equals the
+    single-GPU layer on the same tokens (same routing, outputs within 1e-3)."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        for out, ref, idx, ridx in got[r]:
+            assert np.array_equal(idx, ridx)
+            for t in range(out.shape[0]):
+                err = np.linalg.norm(out[t] - ref[t]) / np.linalg.norm(ref[t])
+                assert err < TOL, (r, t, err)
