@@ -115,7 +115,9 @@ int g4_ctx::check_status(cudaStream_t st) {
 }
 
 static bool supported_type(int t) {
-  return t == G4_TYPE_F32 || t == G4_TYPE_Q8_0 || t == G4_TYPE_Q4_K || t == G4_TYPE_Q6_K || t == G4_TYPE_BF16;
+  return t == G4_TYPE_F32 || t == G4_TYPE_F16 || t == G4_TYPE_Q4_0 || t == G4_TYPE_Q4_1 || t == G4_TYPE_Q5_1 ||
+         t == G4_TYPE_Q8_0 || t == G4_TYPE_Q4_K || t == G4_TYPE_Q5_K || t == G4_TYPE_Q6_K || t == G4_TYPE_BF16 ||
+         t == G4_TYPE_MXFP4;
 }
 
 extern "C" {

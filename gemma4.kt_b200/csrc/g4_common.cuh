@@ -10,18 +10,22 @@
 namespace g4 {
 
 // GGML type ids (GGMLType.kt:16-46)
-enum GgmlType : int { F32 = 0, F16 = 1, Q8_0 = 8, Q4_K = 12, Q6_K = 14, BF16 = 30 };
+enum GgmlType : int {
+  F32 = 0, F16 = 1, Q4_0 = 2, Q4_1 = 3, Q5_1 = 7, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, BF16 = 30, MXFP4 = 39
+};
 
 // Error bits written to the context's device status word.
 enum DevErr : unsigned { ERR_TIMEOUT_FULL = 1u, ERR_TIMEOUT_EMPTY = 2u, ERR_TIMEOUT_DRAIN = 4u,
                          ERR_BAD_ARG = 8u };
 
 __host__ __device__ constexpr int block_size(int t) {
-  return t == Q8_0 ? 32 : (t == Q4_K || t == Q6_K) ? 256 : 1;
+  return (t == Q8_0 || t == Q4_0 || t == Q4_1 || t == Q5_1 || t == MXFP4) ? 32
+         : (t == Q4_K || t == Q5_K || t == Q6_K)                          ? 256
+                                                                          : 1;
 }
 __host__ __device__ constexpr int type_size(int t) {
-  return t == F32 ? 4 : t == F16 ? 2 : t == BF16 ? 2 : t == Q8_0 ? 34 : t == Q4_K ? 144
-                                                                                   : t == Q6_K ? 210 : 0;
+  return t == F32 ? 4 : t == F16 ? 2 : t == BF16 ? 2 : t == Q8_0 ? 34 : t == Q4_K ? 144 : t == Q6_K ? 210
+       : t == Q4_0 ? 18 : t == Q4_1 ? 20 : t == Q5_1 ? 24 : t == Q5_K ? 176 : t == MXFP4 ? 17 : 0;
 }
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.  Far

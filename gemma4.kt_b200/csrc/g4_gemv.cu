@@ -296,7 +296,10 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.off = off;
   p.fast = 0;
   const int BS = block_size(type), TS = type_size(type);
-  if (TS == 0 || type == F16 || rows <= 0 || cols <= 0) return p;
+  // the lane-per-row kernel decodes F32, BF16, Q8_0, Q4_K and Q6_K; the other formats take the
+  // generic kernel (one warp per row, element decoder)
+  const bool fast_type = type == F32 || type == BF16 || type == Q8_0 || type == Q4_K || type == Q6_K;
+  if (TS == 0 || !fast_type || rows <= 0 || cols <= 0) return p;
   if (cols % 32 != 0 || off % BS != 0) return p;
   if ((type == BF16 || type == F32) && ((off * TS) % 16) != 0) return p;
   int pr = 1;

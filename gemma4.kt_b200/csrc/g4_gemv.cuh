@@ -86,6 +86,63 @@ __device__ __forceinline__ float get_elem(int type, const uint8_t* base, long lo
       float d = f16_bits_to_f32((uint16_t)(blk[208] | (blk[209] << 8)));
       return __fmul_rn(__fmul_rn(d, (float)sc), (float)q6);
     }
+    case Q4_0: {  // Q4_0FloatTensor.kt:20-38: (q - 8) * scale
+      const uint8_t* blk = base + (idx >> 5) * 18;
+      const int w = (int)(idx & 31);
+      const int q = w < 16 ? (blk[2 + w] & 0xF) : (blk[2 + w - 16] >> 4);
+      return __fmul_rn((float)(q - 8), f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8))));
+    }
+    case Q4_1: {  // Q4_1FloatTensor.kt:22-41: delta * quant + min (two roundings)
+      const uint8_t* blk = base + (idx >> 5) * 20;
+      const int w = (int)(idx & 31);
+      const int q = w < 16 ? (blk[4 + w] & 0xF) : (blk[4 + w - 16] >> 4);
+      const float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+      const float m = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+      return __fadd_rn(__fmul_rn(d, (float)q), m);
+    }
+    case Q5_1: {  // Q5_1FloatTensor.kt:20-51: q * d + m, fifth bit from the 32-bit qh
+      const uint8_t* blk = base + (idx >> 5) * 24;
+      const int w = (int)(idx & 31);
+      const uint32_t qh = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) | ((uint32_t)blk[6] << 16) |
+                          ((uint32_t)blk[7] << 24);
+      const int nib = w < 16 ? (blk[8 + w] & 0xF) : (blk[8 + w - 16] >> 4);
+      const int xh = w < 16 ? (int)((qh >> w) << 4) & 0x10 : (int)(qh >> (w - 16 + 12)) & 0x10;
+      const float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+      const float m = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+      return __fadd_rn(__fmul_rn((float)(nib | xh), d), m);
+    }
+    case Q5_K: {  // Q5_KFloatTensor.kt:23-50: d * sc * quant - dmin * m
+      const uint8_t* blk = base + (idx >> 8) * 176;
+      const int w = (int)(idx & 255);
+      const float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+      const float dmin = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+      const uint8_t* s = blk + 4;
+      const int group = w >> 6, ig = w & 63, hi = ig >= 32, l = ig & 31;
+      const int sub = group * 2 + hi;
+      int sc, m;
+      if (sub < 4) {
+        sc = s[sub] & 63;
+        m = s[sub + 4] & 63;
+      } else {
+        sc = (s[sub + 4] & 0xF) | (((s[sub - 4] >> 6) & 3) << 4);
+        m = (s[sub + 4] >> 4) | (((s[sub] >> 6) & 3) << 4);
+      }
+      const uint8_t b = blk[48 + group * 32 + l];
+      const int nib = hi ? (b >> 4) : (b & 0xF);
+      const int hbit = (blk[16 + l] >> (2 * group + hi)) & 1;
+      const float t = __fmul_rn(__fmul_rn(d, (float)sc), (float)(nib | (hbit << 4)));
+      return __fsub_rn(t, __fmul_rn(dmin, (float)m));
+    }
+    case MXFP4: {  // MXFP4FloatTensor.kt:22-36,49,209-216: E2M1 value * 2^(e8m0 - 128)
+      const uint8_t* blk = base + (idx >> 5) * 17;
+      const int w = (int)(idx & 31);
+      const int e = blk[0];
+      const float dd = __uint_as_float(e < 2 ? (0x00200000u << e) : ((uint32_t)(e - 1) << 23));
+      const int packed = blk[1 + (w & 15)];
+      const int nib = w < 16 ? (packed & 0xF) : (packed >> 4);
+      const int mag = (nib & 7) < 4 ? (nib & 7) : (nib & 7) == 4 ? 4 : (nib & 7) == 5 ? 6 : (nib & 7) == 6 ? 8 : 12;
+      return __fmul_rn((float)((nib & 8) ? -mag : mag), dd);
+    }
     default: return __int_as_float(0x7fc00000);
   }
 }

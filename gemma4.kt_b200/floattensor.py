@@ -28,21 +28,31 @@ class UnsupportedOperation(G4Error):
 
 
 class GGMLType(IntEnum):
-    """GGML tensor types of the hot path, GGMLType.kt:16-46."""
+    """GGML tensor types FloatTensorFactory.create accepts (FloatTensorFactory.kt:7-23,
+    GGMLType.kt:16-55)."""
 
     F32 = 0
+    F16 = 1
+    Q4_0 = 2
+    Q4_1 = 3
+    Q5_1 = 7
     Q8_0 = 8
     Q4_K = 12
+    Q5_K = 13
     Q6_K = 14
     BF16 = 30
+    MXFP4 = 39
 
     @property
     def block_size(self) -> int:
-        return {GGMLType.Q8_0: 32, GGMLType.Q4_K: QK_K, GGMLType.Q6_K: QK_K}.get(self, 1)
+        return {GGMLType.Q4_0: 32, GGMLType.Q4_1: 32, GGMLType.Q5_1: 32, GGMLType.Q8_0: 32, GGMLType.MXFP4: 32,
+                GGMLType.Q4_K: QK_K, GGMLType.Q5_K: QK_K, GGMLType.Q6_K: QK_K}.get(self, 1)
 
     @property
     def type_size(self) -> int:
-        return {GGMLType.F32: 4, GGMLType.BF16: 2, GGMLType.Q8_0: 34, GGMLType.Q4_K: 144, GGMLType.Q6_K: 210}[self]
+        return {GGMLType.F32: 4, GGMLType.F16: 2, GGMLType.BF16: 2, GGMLType.Q4_0: 18, GGMLType.Q4_1: 20,
+                GGMLType.Q5_1: 24, GGMLType.Q8_0: 34, GGMLType.Q4_K: 144, GGMLType.Q5_K: 176, GGMLType.Q6_K: 210,
+                GGMLType.MXFP4: 17}[self]
 
     def byte_size_for(self, n_elems: int) -> int:
         """GGMLType.byteSizeFor (GGMLType.kt:58-62)."""

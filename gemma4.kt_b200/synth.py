@@ -82,3 +82,31 @@ class MoeLayerData:
         """Residual-stream hidden states ~ N(0, 1), [n_tokens, dim]."""
         rng = np.random.default_rng(seed + 1000)
         return rng.standard_normal((n_tokens, self.dim), dtype=np.float32)
+
+
+def random_blocks(ggml_type, n_elems: int, rng: np.random.Generator) -> np.ndarray:
+    """Valid block streams for the formats without a quantizer here (F16, Q4_0,
+    Q4_1, Q5_1, Q5_K, MXFP4): random code bytes, fp16 scale fields ~ N(0, 0.01)
+    (Q4_1/Q5_1 minima and Q5_K mins included), MXFP4 exponents 2^-12..2^-4.
+    Weights of roughly the magnitude of the quantized N(0, 0.02) ones."""
+    from .floattensor import GGMLType
+
+    t = GGMLType(int(ggml_type))
+    nb = n_elems // t.block_size
+    if nb * t.block_size != n_elems:
+        raise ValueError("n_elems is not a whole number of blocks")
+    f16 = lambda n: (rng.standard_normal(n) * 0.01).astype(np.float16).view(np.uint8).reshape(n, 2)
+    if t == GGMLType.F16:
+        return (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint8)
+    raw = rng.integers(0, 256, size=(nb, t.type_size), dtype=np.uint8)
+    fields = {GGMLType.Q4_0: [0], GGMLType.Q4_1: [0, 2], GGMLType.Q5_1: [0, 2], GGMLType.Q5_K: [0, 2]}
+    if t == GGMLType.MXFP4:
+        raw[:, 0] = rng.integers(116, 125, size=nb)
+    elif t in fields:
+        for off in fields[t]:
+            raw[:, off:off + 2] = f16(nb)
+        if t == GGMLType.Q4_0:  # |d|/8 per step, as a symmetric 4-bit quantizer would
+            raw[:, 0:2] = (rng.standard_normal(nb) * 0.004).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    else:
+        raise ValueError(f"no random block generator for {t.name}")
+    return raw.reshape(-1)

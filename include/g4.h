@@ -40,10 +40,16 @@ extern "C" {
 
 /* GGML type ids accepted by g4_tensor_upload (GGMLType.kt:16-46) */
 #define G4_TYPE_F32 0
+#define G4_TYPE_F16 1
+#define G4_TYPE_Q4_0 2
+#define G4_TYPE_Q4_1 3
+#define G4_TYPE_Q5_1 7
 #define G4_TYPE_Q8_0 8
 #define G4_TYPE_Q4_K 12
+#define G4_TYPE_Q5_K 13
 #define G4_TYPE_Q6_K 14
 #define G4_TYPE_BF16 30
+#define G4_TYPE_MXFP4 39
 
 typedef struct g4_ctx g4_ctx;
 typedef struct g4_tensor g4_tensor;

@@ -19,8 +19,13 @@
 
 int o_block_size(int type) {
   switch (type) {
-    case O_Q8_0: return 32;
-    case O_Q4_K: return QK_K;
+    case O_Q4_0:
+    case O_Q4_1:
+    case O_Q5_1:
+    case O_Q8_0:
+    case O_MXFP4: return 32;  /* QK_MXFP4, GGMLType.kt:6 */
+    case O_Q4_K:
+    case O_Q5_K:
     case O_Q6_K: return QK_K;
     default: return 1;
   }
@@ -31,9 +36,14 @@ int o_type_size(int type) {
     case O_F32: return 4;
     case O_F16: return 2;
     case O_BF16: return 2;
+    case O_Q4_0: return 18;   /* GGMLType.kt:18 */
+    case O_Q4_1: return 20;   /* GGMLType.kt:19 */
+    case O_Q5_1: return 24;   /* GGMLType.kt:23 */
     case O_Q8_0: return 34;   /* GGMLType.kt:24 */
     case O_Q4_K: return 144;  /* GGMLType.kt:28 */
+    case O_Q5_K: return 176;  /* GGMLType.kt:29 */
     case O_Q6_K: return 210;  /* GGMLType.kt:30 */
+    case O_MXFP4: return 17;  /* GGMLType.kt:55 */
     default: return 0;
   }
 }
@@ -119,6 +129,60 @@ float o_get(int type, const uint8_t *base, int64_t index) {
       t = t * (float)q;
       float u = dmin * (float)m;
       return t - u;
+    }
+    case O_Q4_0: { /* Q4_0FloatTensor.kt:20-38: (q - 8) * scale */
+      const uint8_t *blk = base + (index / 32) * 18;
+      int w = (int)(index % 32);
+      int q = w < 16 ? (blk[2 + w] & 0x0F) : ((blk[2 + w - 16] >> 4) & 0x0F);
+      return (float)(q - 8) * rd_f16(blk);
+    }
+    case O_Q4_1: { /* Q4_1FloatTensor.kt:22-41: delta * quant + min, two roundings */
+      const uint8_t *blk = base + (index / 32) * 20;
+      int w = (int)(index % 32);
+      int q = w < 16 ? (blk[4 + w] & 0x0F) : ((blk[4 + w - 16] >> 4) & 0x0F);
+      float t = rd_f16(blk) * (float)q;
+      return t + rd_f16(blk + 2);
+    }
+    case O_Q5_1: { /* Q5_1FloatTensor.kt:20-51: q * d + m, fifth bit from the 32-bit qh */
+      const uint8_t *blk = base + (index / 32) * 24;
+      int w = (int)(index % 32);
+      uint32_t qh = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) | ((uint32_t)blk[6] << 16) | ((uint32_t)blk[7] << 24);
+      int nib, xh;
+      if (w < 16) {
+        nib = blk[8 + w] & 0x0F;
+        xh = (int)((qh >> w) << 4) & 0x10;
+      } else {
+        nib = (blk[8 + w - 16] >> 4) & 0x0F;
+        xh = (int)(qh >> (w - 16 + 12)) & 0x10;
+      }
+      float t = (float)(nib | xh) * rd_f16(blk);
+      return t + rd_f16(blk + 2);
+    }
+    case O_Q5_K: { /* Q5_KFloatTensor.kt:23-50: d * sc * quant - dmin * m, quant = nibble | qh bit << 4 */
+      const uint8_t *blk = base + (index / QK_K) * 176;
+      int within = (int)(index % QK_K);
+      float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+      int group = within / 64, in_group = within % 64, high = in_group >= 32, l = high ? in_group - 32 : in_group;
+      int sub = group * 2 + high;
+      int sc = scale_min_k4(sub, blk + 4, 0), m = scale_min_k4(sub, blk + 4, 1);
+      uint8_t qb = blk[48 + group * 32 + l];
+      int nib = high ? ((qb >> 4) & 0xF) : (qb & 0xF);
+      int hbit = (blk[16 + l] >> (2 * group + high)) & 1;
+      float t = d * (float)sc;
+      t = t * (float)(nib | (hbit << 4));
+      float u = dmin * (float)m;
+      return t - u;
+    }
+    case O_MXFP4: { /* MXFP4FloatTensor.kt:22-36,49,209-216: E2M1 value * 2^(e8m0 - 128) */
+      static const int vals[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+      const uint8_t *blk = base + (index / 32) * 17;
+      int w = (int)(index % 32);
+      int e = blk[0];
+      uint32_t bits = e < 2 ? (0x00200000u << e) : ((uint32_t)(e - 1) << 23);
+      float dd = bits_to_f32(bits);
+      int packed = blk[1 + (w & 0x0F)];
+      int nib = w < 16 ? (packed & 0x0F) : ((packed >> 4) & 0x0F);
+      return (float)vals[nib] * dd;
     }
     case O_Q6_K: { /* Q6_KFloatTensor.kt:26-73 */
       int64_t b = index / QK_K;

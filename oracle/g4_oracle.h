@@ -32,10 +32,15 @@ extern "C" {
 enum {
   O_F32 = 0,
   O_F16 = 1,
+  O_Q4_0 = 2,
+  O_Q4_1 = 3,
+  O_Q5_1 = 7,
   O_Q8_0 = 8,
   O_Q4_K = 12,
+  O_Q5_K = 13,
   O_Q6_K = 14,
-  O_BF16 = 30
+  O_BF16 = 30,
+  O_MXFP4 = 39
 };
 
 int o_block_size(int type);  /* elements per block, GGMLType.kt:12-56 */

@@ -28,6 +28,12 @@ def golden():
 
 
 @pytest.fixture(scope="session")
+def golden_more():
+    """F16, Q4_0, Q4_1, Q5_1, Q5_K, MXFP4 (tests/golden/make_golden.py, main_more)."""
+    return dict(np.load(GOLDEN.with_name("blocks_more.npz")))
+
+
+@pytest.fixture(scope="session")
 def g4():
     import gemma4_kt_b200
 

@@ -56,8 +56,10 @@ def test_ggml_type_geometry(g4):
     assert T.Q4_K.byte_size_for(1536 * 262144) == 226_492_416
     with pytest.raises(ValueError):
         T.Q8_0.byte_size_for(33)
+    assert [(t.block_size, t.type_size) for t in (T.F16, T.Q4_0, T.Q4_1, T.Q5_1, T.Q5_K, T.MXFP4)] == [
+        (1, 2), (32, 18), (32, 20), (32, 24), (256, 176), (32, 17)]  # GGMLType.kt:17-55
     with pytest.raises(g4.UnsupportedOperation):
-        T.from_id(13)  # Q5_K: not on the hot path
+        T.from_id(10)  # Q2_K: FloatTensorFactory.create has no tensor class for it
 
 
 def test_q8_0_quantizer_matches_ggml(golden):

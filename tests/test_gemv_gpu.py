@@ -169,8 +169,48 @@ def test_errors(g4, ctx):
     with pytest.raises(g4.G4Error):
         w.matmul(x, y, 4, 64)  # 256 elements > 128
     with pytest.raises(g4.UnsupportedOperation):
-        g4.FloatTensorFactory.create(ctx, 13, raw, 128)
+        g4.FloatTensorFactory.create(ctx, 10, raw, 128)  # Q2_K: no tensor class in FloatTensorFactory.create
     with pytest.raises(ValueError):
         g4.FloatTensorFactory.create(ctx, 8, raw, 100)  # not whole blocks
     w.matmul(x, y, 0, 64)  # dim0 = 0 is a no-op
     ctx.sync()
+
+
+# ---------------------------------------------------------------- the other formats the reference loads
+MORE = {"F16": 1, "Q4_0": 2, "Q4_1": 3, "Q5_1": 7, "Q5_K": 13, "MXFP4": 39}
+
+
+@pytest.mark.parametrize("name", list(MORE))
+@pytest.mark.parametrize("kind", ["", "edge_"])
+def test_more_formats_dequant_bit_exact(g4, ctx, golden_more, name, kind):
+    """g4_dequant of F16/Q4_0/Q4_1/Q5_1/Q5_K/MXFP4 blocks equals gguf-py's decode bit for bit."""
+    raw, vals = golden_more[f"{name}_{kind}raw"], golden_more[f"{name}_{kind}vals"]
+    w = g4.FloatTensorFactory.create(ctx, MORE[name], raw, vals.size)
+    got = w.dequant(0, vals.size).cpu().numpy()
+    assert bits_equal(got, vals)
+    if vals.size > 40:
+        assert bits_equal(w.dequant(37, vals.size - 37).cpu().numpy(), vals[37:])
+
+
+@pytest.mark.parametrize("name", list(MORE))
+def test_more_formats_gemv_fixture(g4, ctx, golden_more, name):
+    rows, cols = (int(v) for v in golden_more[f"gemv_{name}_shape"])
+    y, _ = run_gemv(g4, ctx, MORE[name], golden_more[f"gemv_{name}_raw"], golden_more[f"gemv_{name}_x"], rows,
+                    cols)
+    assert rel_l2(y, golden_more[f"gemv_{name}_y"]) < TOL
+
+
+@pytest.mark.parametrize("name", list(MORE))
+def test_more_formats_gemv_vs_oracle(g4, ctx, name):
+    """1024 x 1536 random blocks, whole matrix and a row window at an element offset."""
+    from gemma4_kt_b200 import synth
+
+    rng = np.random.default_rng(11)
+    rows, cols = 1024, 1536
+    raw = synth.random_blocks(MORE[name], rows * cols, rng)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y, _ = run_gemv(g4, ctx, MORE[name], raw, x, rows, cols)
+    assert rel_l2(y, oracle.matmul(MORE[name], raw, x, rows, cols)) < TOL
+    off = 100 * cols
+    y2, _ = run_gemv(g4, ctx, MORE[name], raw, x, 300, cols, off=off)
+    assert rel_l2(y2, oracle.matmul(MORE[name], raw, x, 300, cols, this_offset=off)) < TOL

@@ -90,3 +90,24 @@ def test_gelu_and_rmsnorm():
         xd = float(np.float32(v))
         ref = 0.5 * xd * (1 + np.tanh(np.sqrt(2 / np.pi) * (xd + 0.044715 * xd ** 3)))
         assert same_bits([oracle.gelu(v)], [np.float32(ref)])
+
+
+# ---------------------------------------------------------------- the other formats the reference loads
+MORE_IDS = {"F16": 1, "Q4_0": 2, "Q4_1": 3, "Q5_1": 7, "Q5_K": 13, "MXFP4": 39}
+
+
+@pytest.mark.parametrize("name", list(MORE_IDS))
+@pytest.mark.parametrize("kind", ["", "edge_"])
+def test_more_formats_dequant_match_gguf_py(golden_more, name, kind):
+    """Q4_0/Q4_1/Q5_1/Q5_K/F16/MXFP4FloatTensor.get restated in the oracle, bit for bit."""
+    raw, vals = golden_more[f"{name}_{kind}raw"], golden_more[f"{name}_{kind}vals"]
+    got = oracle.dequant(MORE_IDS[name], raw, 0, vals.size)
+    assert same_bits(got, vals)
+
+
+@pytest.mark.parametrize("name", list(MORE_IDS))
+def test_more_formats_gemv_fixture(golden_more, name):
+    rows, cols = golden_more[f"gemv_{name}_shape"]
+    raw, x, y = golden_more[f"gemv_{name}_raw"], golden_more[f"gemv_{name}_x"], golden_more[f"gemv_{name}_y"]
+    got = oracle.matmul(MORE_IDS[name], raw, x, int(rows), int(cols))
+    assert rel_l2(got, y) < 1e-5
