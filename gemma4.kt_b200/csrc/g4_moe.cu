@@ -258,20 +258,11 @@ static int launch_router(const float* wr, const float* xr, float* logits, float*
 // index; the selected entry is masked to -inf.
 // `logits` holds nsplit >= 1 partial logit matrices [nsplit][T][E] (split-K
 // router) that are added in split order first.
-__global__ void moe_topk_kernel(const float* __restrict__ logits, int nsplit, int T, int E, int K,
-                                int32_t* __restrict__ idx_out, float* __restrict__ prob_out) {
-  __shared__ float probs[8][kMaxExperts];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= T) return;
-  float* p = probs[warp];
-  float mx = -INFINITY;
-  for (int e = lane; e < E; e += 32) {
-    float v = logits[(size_t)t * E + e];
-    for (int sp = 1; sp < nsplit; ++sp) v = __fadd_rn(v, logits[((size_t)sp * T + t) * E + e]);
-    p[e] = v;
-    mx = fmaxf(mx, v);
-  }
+// Softmax and top-k of one token by one warp; p (E floats of shared memory)
+// holds the token's logits on entry and the token's mx is their maximum.
+__device__ __forceinline__ void topk_warp(float* p, float mx, int E, int K, int t, int32_t* __restrict__ idx_out,
+                                          float* __restrict__ prob_out) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   for (int e = lane; e < E; e += 32) p[e] = (float)exp((double)__fsub_rn(p[e], mx));
@@ -311,12 +302,30 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, int nsplit, in
   }
 }
 
+__global__ void moe_topk_kernel(const float* __restrict__ logits, int nsplit, int T, int E, int K,
+                                int32_t* __restrict__ idx_out, float* __restrict__ prob_out) {
+  __shared__ float probs[8][kMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  float* p = probs[warp];
+  float mx = -INFINITY;
+  for (int e = lane; e < E; e += 32) {
+    float v = logits[(size_t)t * E + e];
+    for (int sp = 1; sp < nsplit; ++sp) v = __fadd_rn(v, logits[((size_t)sp * T + t) * E + e]);
+    p[e] = v;
+    mx = fmaxf(mx, v);
+  }
+  topk_warp(p, mx, E, K, t, idx_out, prob_out);
+}
+
 // ---------------------------------------------------------------- permutation
 // Single CTA: counts per expert, exclusive offsets (offsets[E] = T*K), and
 // perm[offsets[e] + j] = slot for the j-th slot routed to e.
-__global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t* __restrict__ idx, int n_slots, int E,
-                                                           int32_t* __restrict__ offsets, int32_t* __restrict__ perm) {
-  __shared__ int cnt[kMaxExperts], off[kMaxExperts + 1], cur[kMaxExperts];
+// Block-wide body of the permutation (shared arrays passed in).
+__device__ __forceinline__ void permute_block(const int32_t* __restrict__ idx, int n_slots, int E,
+                                              int32_t* __restrict__ offsets, int32_t* __restrict__ perm, int* cnt,
+                                              int* off, int* cur) {
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     cnt[e] = 0;
     cur[e] = 0;
@@ -339,6 +348,118 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t* __rest
     int pos = off[e] + atomicAdd(&cur[e], 1);
     perm[pos] = s;
   }
+}
+
+__global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t* __restrict__ idx, int n_slots, int E,
+                                                           int32_t* __restrict__ offsets, int32_t* __restrict__ perm) {
+  __shared__ int cnt[kMaxExperts], off[kMaxExperts + 1], cur[kMaxExperts];
+  permute_block(idx, n_slots, E, offsets, perm, cnt, off, cur);
+}
+
+// Small batches (T <= 8): prep, router, softmax/top-k and permutation in one
+// launch.  CTA e computes expert e's logit for every token (8 warps split K,
+// their partial sums meet in shared memory in a fixed order) and moe_in for
+// the 16-column groups j = e, e + E, ... of every token (with the groups'
+// sums).  The last CTA to finish (an atomic ticket taken after a memory
+// fence; *ticket is 0 on entry) runs softmax/top-k and the permutation.
+// Same arithmetic as moe_prep_kernel + the router + moe_topk_kernel +
+// moe_permute_kernel.
+__global__ void __launch_bounds__(256) moe_front_small_kernel(
+    const float* __restrict__ x, const float* __restrict__ pre_norm, const float* __restrict__ gate_scale,
+    const float* __restrict__ wr, float* __restrict__ moe_in, float* __restrict__ moe_in_s16,
+    float* __restrict__ logits, int32_t* __restrict__ idx, float* __restrict__ prob, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ perm, unsigned* __restrict__ ticket, int T, int dim, int E, int K, float eps) {
+  __shared__ float s_norm[8], s_router[8];
+  __shared__ float part[8][8];
+  __shared__ float probs[8][kMaxExperts];
+  __shared__ int cnt[kMaxExperts], off[kMaxExperts + 1], cur[kMaxExperts];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, e = blockIdx.x;
+  const int n4 = dim >> 2;
+  // per-token scales (rmsnorm, Llama.kt:27-37; router scale, Llama.kt:258-261), warp t for token t
+  if (warp < T) {
+    const float4* xt = reinterpret_cast<const float4*>(x + (size_t)warp * dim);
+    float ss = 0.f;
+    for (int i = lane; i < n4; i += 32) {
+      const float4 v = xt[i];
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) {
+      const float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
+      const float sn = (float)(1.0 / sqrt((double)m));
+      s_norm[warp] = sn;
+      s_router[warp] = __fdiv_rn(sn, (float)sqrt((double)dim));
+    }
+  }
+  __syncthreads();
+  // moe_in and its per-16 sums for this CTA's column groups
+  for (int item = threadIdx.x; item < T * (dim / 16); item += blockDim.x) {
+    const int t = item / (dim / 16), jj = item % (dim / 16);
+    if (jj % gridDim.x != (unsigned)e) continue;
+    const float* xr_ = x + (size_t)t * dim + 16 * jj;
+    float* mo = moe_in + (size_t)t * dim + 16 * jj;
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float v = __fmul_rn(pre_norm[16 * jj + i], __fmul_rn(s_norm[t], xr_[i]));
+      mo[i] = v;
+      acc += v;
+    }
+    moe_in_s16[(size_t)t * (dim / 16) + jj] = acc;
+  }
+  // router logit of expert e (F32 matmul, Llama.kt:269-270) on xr = (x * s) * gate_scale
+  const int k0 = (n4 * warp) / 8, k1 = (n4 * (warp + 1)) / 8;
+  const float4* w4 = reinterpret_cast<const float4*>(wr + (size_t)e * dim);
+  const float4* g4 = reinterpret_cast<const float4*>(gate_scale);
+  float acc[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+  for (int k = k0 + lane; k < k1; k += 32) {
+    const float4 w = __ldg(w4 + k), g = __ldg(g4 + k);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (t < T) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x + (size_t)t * dim) + k);
+        const float sr = s_router[t];
+        acc[t] = fmaf(w.x, __fmul_rn(__fmul_rn(v.x, sr), g.x),
+                      fmaf(w.y, __fmul_rn(__fmul_rn(v.y, sr), g.y),
+                           fmaf(w.z, __fmul_rn(__fmul_rn(v.z, sr), g.z),
+                                fmaf(w.w, __fmul_rn(__fmul_rn(v.w, sr), g.w), acc[t]))));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float v = warp_sum(acc[t]);
+    if (lane == 0) part[warp][t] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < T) {
+    float v = 0.f;
+    for (int w = 0; w < 8; ++w) v += part[w][threadIdx.x];
+    logits[(size_t)threadIdx.x * E + e] = v;
+  }
+  // the last CTA to get here routes every token
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (warp < T) {
+    float* p = probs[warp];
+    float mx = -INFINITY;
+    for (int ee = lane; ee < E; ee += 32) {
+      const float v = __ldcg(logits + (size_t)warp * E + ee);
+      p[ee] = v;
+      mx = fmaxf(mx, v);
+    }
+    topk_warp(p, mx, E, K, warp, idx, prob);
+  }
+  __syncthreads();
+  __threadfence_block();
+  permute_block(idx, T * K, E, offsets, perm, cnt, off, cur);
 }
 
 // Wide batches: the same result from three kernels over chunks of slots.
@@ -1381,6 +1502,17 @@ static void launch_permute(const int32_t* idx, int n_slots, int E, int32_t* offs
 static cudaError_t launch_front(g4_ctx* c, const g4_moe_weights* w, const float* x, const MoeScratch& m, int T,
                                 bool want_s16, cudaStream_t st) {
   const int dim = w->dim, E = w->n_expert, K = w->n_used;
+  if (T <= 8 && dim % 16 == 0) {
+    // one launch; its ticket borrows G_s16, which only the expert products write later
+    unsigned* ticket = reinterpret_cast<unsigned*>(m.G_s16);
+    cudaError_t e = cudaMemsetAsync(ticket, 0, sizeof(unsigned), st);
+    if (e != cudaSuccess) return e;
+    moe_front_small_kernel<<<E, 256, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d,
+                                             (const float*)w->gate_inp_scale->d, (const float*)w->gate_inp->d,
+                                             m.moe_in, m.moe_in_s16, m.logits, m.idx, m.prob, m.offsets, m.perm,
+                                             ticket, T, dim, E, K, w->eps);
+    return cudaGetLastError();
+  }
   moe_prep_kernel<<<T, row_threads(dim / 4), 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d,
                                                       (const float*)w->gate_inp_scale->d, m.moe_in, m.xr,
                                                       want_s16 ? m.moe_in_s16 : nullptr, dim, w->eps);
