@@ -435,6 +435,8 @@ def bench_moe(g4, ctx, torch, dev):
     # Q4_K bytes of one expert (gate_up 2ff x dim + down dim x ff) and its multiply-adds per slot
     expert_w = 2 * d.ff * d.dim + d.dim * d.ff
     expert_bytes = expert_w * 144 // 256
+    flush = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    flush_out = torch.empty((), dtype=torch.float32, device=dev)
     res = {}
     for T in (1, 16, 256, 4096):
         x = torch.from_numpy(d.tokens(T)).to(dev)
@@ -454,16 +456,19 @@ def bench_moe(g4, ctx, torch, dev):
             layer.forward(x, out, T, stream=stream.cuda_stream)
             g.capture_end()
         reps = 20 if T <= 256 else 5
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # each timed replay starts with a cold L2: a 256 MB read (twice the
+        # L2, clean lines: nothing to write back) runs before it, outside its
+        # event pair
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
         with torch.cuda.stream(stream):  # replay() launches on the current stream
             g.replay()
-            torch.cuda.synchronize()
-            a.record(stream)
-            for _ in range(reps):
+            for a, b in ev:
+                torch.sum(flush, 0, out=flush_out)
+                a.record(stream)
                 g.replay()
-            b.record(stream)
+                b.record(stream)
         torch.cuda.synchronize()
-        us = a.elapsed_time(b) * 1e3 / reps
+        us = sum(a.elapsed_time(b) for a, b in ev) * 1e3 / reps
         del g
         # algorithmic bytes: weights of the experts routed to + router weights + activations in and out
         nbytes = n_unique * expert_bytes + d.dim * d.n_expert * 4 + 2 * T * d.dim * 4
@@ -473,10 +478,12 @@ def bench_moe(g4, ctx, torch, dev):
         res[f"T{T}"] = {"us_per_layer": round(us, 2), "us_per_token": round(us / T, 3),
                         "experts_touched": n_unique, "GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
                         "TFLOPs": round(tfs, 2), "tensor_frac": round(tfs / tensor_peak, 4),
-                        "path": "tcgen05 grouped GEMM" if 4 * T * d.n_used >= d.n_expert else "CUDA-core rows"}
+                        "path": "tcgen05 grouped GEMM" if 4 * T * d.n_used >= d.n_expert
+                        else "one-wave decode kernels" if T <= 2 else "CUDA-core rows"}
     ctx.sync()
     return {"metric": "MoE layer us/token", "config": "hidden 2816, 128 experts top-8, ff 704, Q4_K, seed 2",
-            "timing": "CUDA graph of one g4_moe_layer call, replayed",
+            "timing": "CUDA graph of one g4_moe_layer call, replayed; L2 flushed (256 MB read) before each "
+                      "timed replay, outside its event pair",
             "roofline": "hbm_frac = (touched experts' Q4_K bytes + router + activations) / time / measured HBM; "
                         "tensor_frac = 2*T*8*5947392 flops / time / measured bf16 dense peak",
             **res}

@@ -151,12 +151,12 @@ int g4_init(int device, g4_ctx** out) {
   c->dev.device = device;
   c->dev.sms = prop.multiProcessorCount;
   c->dev.smem_optin = prop.sharedMemPerBlockOptin;
-  if ((e = cudaMalloc(&c->status, sizeof(unsigned))) != cudaSuccess) {
+  if ((e = cudaMalloc(&c->status, kStatusWords * sizeof(unsigned))) != cudaSuccess) {
     snprintf(g_init_err, sizeof g_init_err, "g4_init: %s", cudaGetErrorString(e));
     delete c;
     return G4_E_NOMEM;
   }
-  cudaMemset(c->status, 0, sizeof(unsigned));
+  cudaMemset(c->status, 0, kStatusWords * sizeof(unsigned));
   *out = c;
   return 0;
 }

@@ -92,6 +92,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Programmatic dependent launch: wait for the grids this one depends on
+// (no-op when launched without the attribute), and let the next grid launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void record_error(unsigned* status, unsigned bits) {
   if (status) atomicOr(status, bits);
 }

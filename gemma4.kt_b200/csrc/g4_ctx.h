@@ -9,9 +9,14 @@
 #include <map>
 #include <tuple>
 
+constexpr int kStatusWords = 16;  // device words behind g4_ctx::status
+
 struct g4_ctx {
   g4::DeviceInfo dev{};
-  unsigned* status = nullptr;  // device error word written by kernels (bounded waits)
+  // device words: [0] error flags written by kernels (bounded waits), [1] the
+  // MoE front kernel's completion ticket (its last CTA resets it to 0)
+  unsigned* status = nullptr;
+  unsigned* ticket() const { return status + 1; }
   void* scratch_ptr = nullptr; // growable device arena (host-buffer staging, MoE work buffers)
   size_t scratch_bytes = 0;
   void* pinned_ptr = nullptr;  // growable pinned host staging

@@ -125,6 +125,10 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
   }
   __syncthreads();
   for (int k = threadIdx.x; k < n16 / 2; k += blockDim.x) xsum32[k] = xsum16[2 * k] + xsum16[2 * k + 1];
+  // quantized formats: int16 activations per 32 columns for the dp2a decoders
+  int16_t* xq = reinterpret_cast<int16_t*>(smem + p.xq_off);
+  float* xsc32 = xsum32 + n16 / 2;
+  if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) quantize_x16(xs, p.cols, xq, xsc32);
   __syncthreads();
 
   float acc[PR];
@@ -151,9 +155,9 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
       if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) {
         for (int b = sl; b < nb; b += LPR) {
           const uint8_t* blk = base + b * TS;
-          if constexpr (FMT == Q4_K) block_q4k<PR>(blk, e0 + b * BS, p.cols, xs, xsum32, acc);
-          else if constexpr (FMT == Q6_K) block_q6k<PR>(blk, e0 + b * BS, p.cols, xs, xsum16, acc);
-          else block_q8_0(blk, e0 + b * BS, xs, acc[0]);
+          if constexpr (FMT == Q4_K) block_q4k_i16<PR>(blk, e0 + b * BS, p.cols, xq, xsc32, xsum32, acc);
+          else if constexpr (FMT == Q6_K) block_q6k_i16<PR>(blk, e0 + b * BS, p.cols, xq, xsc32, xsum16, acc);
+          else block_q8_0_i16(blk, e0 + b * BS, xq, xsc32, acc[0]);
         }
       } else {
         // BF16 / F32: `blocks` are elements; 16-byte loads of 8 or 4 of them
@@ -310,13 +314,15 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   }
   if (rows % pr != 0) return p;
   const int xbytes = ((cols * 4 + 127) / 128) * 128;
-  const int xsbytes = (((cols / 16 + cols / 32) * 4 + 127) / 128) * 128;
+  // per-16 and per-32 column sums, per-32 int16 scales; int16 activations
+  const int xsbytes = (((cols / 16 + 2 * (cols / 32)) * 4 + 127) / 128) * 128;
+  const int xqbytes = (((cols + 8 * ((cols + 255) / 256)) * 2 + 127) / 128) * 128;
   if (xbytes > 96 * 1024) return p;
   p.pr = pr;
   p.nvrows = rows / pr;
   p.bpv = (int)((long long)pr * cols / BS);
   // defaults from a sweep of 262144 x 1536 on B200 (lanes per row, bytes per copy)
-  const int lpr_default = type == Q4_K ? 2 : 4;
+  const int lpr_default = (type == Q4_K || type == Q6_K) ? 2 : 4;
   p.lpr = env_int("G4_GEMV_LPR", lpr_default);
   if (p.lpr != 1 && p.lpr != 2 && p.lpr != 4) p.lpr = 1;
   if (pr > 1 && p.lpr > 2) p.lpr = 2;
@@ -325,7 +331,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
 
   // chunk: about `target` bytes of one row per bulk copy (copies below ~256 B
   // cap the copy engine well under HBM speed), at least one block per lane
-  const int target = env_int("G4_GEMV_CHUNK_BYTES", type == Q4_K ? 288 : type == Q6_K ? 840 : 576);
+  const int target = env_int("G4_GEMV_CHUNK_BYTES", type == Q4_K ? 288 : type == Q6_K ? 420 : 576);
   const int unit = (type == BF16 ? 8 : type == F32 ? 4 : 1) * p.lpr;  // elements (blocks) per lane step
   int cb = std::max(unit, std::min(p.bpv, target / TS) / unit * unit);
   const bool small = p.ngroups < 2 * dev.sms;
@@ -340,7 +346,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.pitch = pitch_for(cb * TS + 32);
   size_t stage = (size_t)rows_per_group * p.pitch;
   const size_t budget = dev.smem_optin > 0 ? dev.smem_optin : 227 * 1024;
-  const size_t fixed = (size_t)xbytes + xsbytes + 256;
+  const size_t fixed = (size_t)xbytes + xsbytes + xqbytes + 256;
   if (small) {
     p.split = std::min(p.nchunks, 8);
     p.warps = p.split;
@@ -371,7 +377,8 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   }
   p.xs_off = 0;
   p.xsum_off = xbytes;
-  p.bar_off = xbytes + xsbytes;
+  p.xq_off = xbytes + xsbytes;
+  p.bar_off = p.xq_off + xqbytes;
   p.ring_off = p.bar_off + 128 * ((p.warps * p.ns * 8 + 127) / 128);
   p.red_off = (int)(p.ring_off + (size_t)p.warps * p.ns * stage);
   p.smem = (size_t)p.red_off + (p.split > 1 ? (size_t)p.warps * rows_per_group * pr * 4 : 0);

@@ -22,7 +22,7 @@ struct GemvPlan {
   int split;         // 1: persistent, each warp owns whole row groups; >1: CTA per group
   int ngroups;       // row groups of 32/lpr virtual rows
   int grid;
-  int xs_off, xsum_off, bar_off, ring_off, red_off;  // shared-memory carve-up
+  int xs_off, xsum_off, xq_off, bar_off, ring_off, red_off;  // shared-memory carve-up
   size_t smem;
   int fast;          // 1: streaming kernel; 0: generic fallback
 };

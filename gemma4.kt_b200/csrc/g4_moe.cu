@@ -24,6 +24,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <vector>
@@ -333,13 +334,21 @@ __device__ __forceinline__ void permute_block(const int32_t* __restrict__ idx, i
   __syncthreads();
   for (int s = threadIdx.x; s < n_slots; s += blockDim.x) atomicAdd(&cnt[idx[s]], 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int a = 0;
-    for (int e = 0; e < E; ++e) {
-      off[e] = a;
-      a += cnt[e];
+  if (threadIdx.x < 32) {  // exclusive scan of the counts, 32 experts at a time
+    int carry = 0;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + (int)threadIdx.x;
+      const int v = e < E ? cnt[e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if ((int)threadIdx.x >= o) incl += u;
+      }
+      if (e < E) off[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    off[E] = a;
+    if (threadIdx.x == 0) off[E] = carry;
   }
   __syncthreads();
   for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off[e];
@@ -357,13 +366,14 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t* __rest
 }
 
 // Small batches (T <= 8): prep, router, softmax/top-k and permutation in one
-// launch.  CTA e computes expert e's logit for every token (8 warps split K,
-// their partial sums meet in shared memory in a fixed order) and moe_in for
-// the 16-column groups j = e, e + E, ... of every token (with the groups'
-// sums).  The last CTA to finish (an atomic ticket taken after a memory
-// fence; *ticket is 0 on entry) runs softmax/top-k and the permutation.
-// Same arithmetic as moe_prep_kernel + the router + moe_topk_kernel +
-// moe_permute_kernel.
+// launch.  CTA e computes expert e's logit for every token: each thread holds
+// its share of router row e and of the gate scale in registers (float4 columns
+// tid, tid + 256, ...), so the sums of squares and the logits need a single
+// round trip to memory.  The CTA also writes moe_in and its per-16 sums for
+// the 16-column groups jj = e (mod E).  The last CTA to finish (ticket
+// counter) runs softmax/top-k per token and the permutation, and puts the
+// ticket back to 0 for the next call.
+constexpr int kFrontMaxF4 = 4;  // float4 columns per thread: dim <= 4096
 __global__ void __launch_bounds__(256) moe_front_small_kernel(
     const float* __restrict__ x, const float* __restrict__ pre_norm, const float* __restrict__ gate_scale,
     const float* __restrict__ wr, float* __restrict__ moe_in, float* __restrict__ moe_in_s16,
@@ -374,58 +384,35 @@ __global__ void __launch_bounds__(256) moe_front_small_kernel(
   __shared__ float probs[8][kMaxExperts];
   __shared__ int cnt[kMaxExperts], off[kMaxExperts + 1], cur[kMaxExperts];
   __shared__ int is_last;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, e = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, e = blockIdx.x;
   const int n4 = dim >> 2;
-  // per-token scales (rmsnorm, Llama.kt:27-37; router scale, Llama.kt:258-261), warp t for token t
-  if (warp < T) {
-    const float4* xt = reinterpret_cast<const float4*>(x + (size_t)warp * dim);
-    float ss = 0.f;
-    for (int i = lane; i < n4; i += 32) {
-      const float4 v = xt[i];
-      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) {
-      const float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
-      const float sn = (float)(1.0 / sqrt((double)m));
-      s_norm[warp] = sn;
-      s_router[warp] = __fdiv_rn(sn, (float)sqrt((double)dim));
-    }
-  }
-  __syncthreads();
-  // moe_in and its per-16 sums for this CTA's column groups
-  for (int item = threadIdx.x; item < T * (dim / 16); item += blockDim.x) {
-    const int t = item / (dim / 16), jj = item % (dim / 16);
-    if (jj % gridDim.x != (unsigned)e) continue;
-    const float* xr_ = x + (size_t)t * dim + 16 * jj;
-    float* mo = moe_in + (size_t)t * dim + 16 * jj;
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float v = __fmul_rn(pre_norm[16 * jj + i], __fmul_rn(s_norm[t], xr_[i]));
-      mo[i] = v;
-      acc += v;
-    }
-    moe_in_s16[(size_t)t * (dim / 16) + jj] = acc;
-  }
-  // router logit of expert e (F32 matmul, Llama.kt:269-270) on xr = (x * s) * gate_scale
-  const int k0 = (n4 * warp) / 8, k1 = (n4 * (warp + 1)) / 8;
   const float4* w4 = reinterpret_cast<const float4*>(wr + (size_t)e * dim);
   const float4* g4 = reinterpret_cast<const float4*>(gate_scale);
+  float4 wv[kFrontMaxF4], gv[kFrontMaxF4];
+#pragma unroll
+  for (int i = 0; i < kFrontMaxF4; ++i) {
+    const int k = tid + 256 * i;
+    if (k < n4) {
+      wv[i] = __ldg(w4 + k);
+      gv[i] = __ldg(g4 + k);
+    }
+  }
+  grid_dep_launch();
+  grid_dep_wait();  // x comes from the previous grid
+  // per-token sums of squares (rmsnorm, Llama.kt:27-37)
   float acc[8];
 #pragma unroll
   for (int t = 0; t < 8; ++t) acc[t] = 0.f;
-  for (int k = k0 + lane; k < k1; k += 32) {
-    const float4 w = __ldg(w4 + k), g = __ldg(g4 + k);
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      if (t < T) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(x + (size_t)t * dim) + k);
-        const float sr = s_router[t];
-        acc[t] = fmaf(w.x, __fmul_rn(__fmul_rn(v.x, sr), g.x),
-                      fmaf(w.y, __fmul_rn(__fmul_rn(v.y, sr), g.y),
-                           fmaf(w.z, __fmul_rn(__fmul_rn(v.z, sr), g.z),
-                                fmaf(w.w, __fmul_rn(__fmul_rn(v.w, sr), g.w), acc[t]))));
+  for (int i = 0; i < kFrontMaxF4; ++i) {
+    const int k = tid + 256 * i;
+    if (k < n4) {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        if (t < T) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(x + (size_t)t * dim) + k);
+          acc[t] = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, acc[t]))));
+        }
       }
     }
   }
@@ -435,17 +422,69 @@ __global__ void __launch_bounds__(256) moe_front_small_kernel(
     if (lane == 0) part[warp][t] = v;
   }
   __syncthreads();
-  if (threadIdx.x < T) {
+  if (tid < T) {
+    float ss = 0.f;
+    for (int w = 0; w < 8; ++w) ss += part[w][tid];
+    const float m = __fadd_rn(__fdiv_rn(ss, (float)dim), eps);
+    const float sn = (float)(1.0 / sqrt((double)m));
+    s_norm[tid] = sn;
+    s_router[tid] = __fdiv_rn(sn, (float)sqrt((double)dim));  // router scale, Llama.kt:258-261
+  }
+  __syncthreads();
+  // router logit of expert e (F32 matmul, Llama.kt:269-270) on xr = (x * s) * gate_scale
+#pragma unroll
+  for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+#pragma unroll
+  for (int i = 0; i < kFrontMaxF4; ++i) {
+    const int k = tid + 256 * i;
+    if (k < n4) {
+      const float4 w = wv[i], g = gv[i];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        if (t < T) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(x + (size_t)t * dim) + k);
+          const float sr = s_router[t];
+          acc[t] = fmaf(w.x, __fmul_rn(__fmul_rn(v.x, sr), g.x),
+                        fmaf(w.y, __fmul_rn(__fmul_rn(v.y, sr), g.y),
+                             fmaf(w.z, __fmul_rn(__fmul_rn(v.z, sr), g.z),
+                                  fmaf(w.w, __fmul_rn(__fmul_rn(v.w, sr), g.w), acc[t]))));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float v = warp_sum(acc[t]);
+    if (lane == 0) part[warp][t] = v;  // every thread read part before the last barrier
+  }
+  // moe_in and its per-16 sums for this CTA's column groups
+  for (int item = tid; item < T * (dim / 16); item += blockDim.x) {
+    const int t = item / (dim / 16), jj = item % (dim / 16);
+    if (jj % gridDim.x != (unsigned)e) continue;
+    const float* xr_ = x + (size_t)t * dim + 16 * jj;
+    float* mo = moe_in + (size_t)t * dim + 16 * jj;
+    float s16 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float v = __fmul_rn(pre_norm[16 * jj + i], __fmul_rn(s_norm[t], xr_[i]));
+      mo[i] = v;
+      s16 += v;
+    }
+    moe_in_s16[(size_t)t * (dim / 16) + jj] = s16;
+  }
+  __syncthreads();
+  if (tid < T) {
     float v = 0.f;
-    for (int w = 0; w < 8; ++w) v += part[w][threadIdx.x];
-    logits[(size_t)threadIdx.x * E + e] = v;
+    for (int w = 0; w < 8; ++w) v += part[w][tid];
+    logits[(size_t)tid * E + e] = v;
   }
   // the last CTA to get here routes every token
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  if (tid == 0) is_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
   __syncthreads();
   if (!is_last) return;
+  if (tid == 0) *ticket = 0u;  // every CTA has counted
   __threadfence();
   if (warp < T) {
     float* p = probs[warp];
@@ -1324,6 +1363,8 @@ __global__ void __launch_bounds__(512) moe_combine_kernel(const float* __restric
   __shared__ float red[33];
   __shared__ float fw[kMaxUsed];
   const int t = blockIdx.x;
+  grid_dep_wait();
+  grid_dep_launch();
   if (threadIdx.x < K) {
     int e = idx[(size_t)t * K + threadIdx.x];
     fw[threadIdx.x] = __fmul_rn(prob[(size_t)t * K + threadIdx.x], down_scale[e]);
@@ -1379,6 +1420,8 @@ __global__ void __launch_bounds__(512) moe_combine_reg_kernel(const float* __res
   __shared__ float red[33];
   __shared__ float fw[kMaxUsed];
   const int t = blockIdx.x;
+  grid_dep_wait();
+  grid_dep_launch();
   if (threadIdx.x < K) {
     const int e = idx[(size_t)t * K + threadIdx.x];
     fw[threadIdx.x] = __fmul_rn(prob[(size_t)t * K + threadIdx.x], down_scale[e]);
@@ -1495,6 +1538,31 @@ static void launch_permute(const int32_t* idx, int n_slots, int E, int32_t* offs
   }
 }
 
+// G4_PDL=0 launches the decode chain without programmatic dependent launch
+static bool pdl_enabled() {
+  const char* v = getenv("G4_PDL");
+  return !(v && v[0] == '0');
+}
+
+// Launch with programmatic stream serialization: the grid may start while the
+// previous grid in the stream is still running; the kernel's grid_dep_wait()
+// orders it after that grid (kernels without the wait must not use this).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Front of the layer, shared by every entry point: norms (prep), router
 // logits, softmax + top-k, and the slot permutation.  The router's split-K
 // partials and the permutation's chunk counts use the D buffer, which the
@@ -1502,16 +1570,11 @@ static void launch_permute(const int32_t* idx, int n_slots, int E, int32_t* offs
 static cudaError_t launch_front(g4_ctx* c, const g4_moe_weights* w, const float* x, const MoeScratch& m, int T,
                                 bool want_s16, cudaStream_t st) {
   const int dim = w->dim, E = w->n_expert, K = w->n_used;
-  if (T <= 8 && dim % 16 == 0) {
-    // one launch; its ticket borrows G_s16, which only the expert products write later
-    unsigned* ticket = reinterpret_cast<unsigned*>(m.G_s16);
-    cudaError_t e = cudaMemsetAsync(ticket, 0, sizeof(unsigned), st);
-    if (e != cudaSuccess) return e;
-    moe_front_small_kernel<<<E, 256, 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d,
-                                             (const float*)w->gate_inp_scale->d, (const float*)w->gate_inp->d,
-                                             m.moe_in, m.moe_in_s16, m.logits, m.idx, m.prob, m.offsets, m.perm,
-                                             ticket, T, dim, E, K, w->eps);
-    return cudaGetLastError();
+  if (T <= 8 && dim % 16 == 0 && dim <= 4 * 256 * kFrontMaxF4) {
+    // one launch; its completion ticket is a context word that the last CTA resets
+    return launch_pdl(moe_front_small_kernel, E, 256, 0, st, x, (const float*)w->pre_ffw_norm_2->d,
+                      (const float*)w->gate_inp_scale->d, (const float*)w->gate_inp->d, m.moe_in, m.moe_in_s16,
+                      m.logits, m.idx, m.prob, m.offsets, m.perm, c->ticket(), T, dim, E, K, w->eps);
   }
   moe_prep_kernel<<<T, row_threads(dim / 4), 0, st>>>(x, (const float*)w->pre_ffw_norm_2->d,
                                                       (const float*)w->gate_inp_scale->d, m.moe_in, m.xr,
@@ -1529,17 +1592,21 @@ static cudaError_t launch_front(g4_ctx* c, const g4_moe_weights* w, const float*
   return cudaGetLastError();
 }
 
-static void launch_combine(const g4_moe_weights* w, const MoeScratch& m, float* out, int T, cudaStream_t st) {
+static cudaError_t launch_combine(const g4_moe_weights* w, const MoeScratch& m, float* out, int T, cudaStream_t st) {
   const int n4 = w->dim / 4, threads = row_threads(n4), iters = (n4 + threads - 1) / threads;
   const float* ds = (const float*)w->down_exps_scale->d;
   const float* pn = w->post_ffw_norm_2 ? (const float*)w->post_ffw_norm_2->d : nullptr;
+  const float* D = m.D;
+  const int32_t* idx = m.idx;
+  const float* prob = m.prob;
+  const int dim = w->dim, K = w->n_used;
+  const float eps = w->eps;
   switch (iters) {
-    case 1: moe_combine_reg_kernel<1><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
-    case 2: moe_combine_reg_kernel<2><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
-    case 3: moe_combine_reg_kernel<3><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
-    case 4: moe_combine_reg_kernel<4><<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps); break;
-    default:
-      moe_combine_kernel<<<T, threads, 0, st>>>(m.D, m.idx, m.prob, ds, pn, out, w->dim, w->n_used, w->eps);
+    case 1: return launch_pdl(moe_combine_reg_kernel<1>, T, threads, 0, st, D, idx, prob, ds, pn, out, dim, K, eps);
+    case 2: return launch_pdl(moe_combine_reg_kernel<2>, T, threads, 0, st, D, idx, prob, ds, pn, out, dim, K, eps);
+    case 3: return launch_pdl(moe_combine_reg_kernel<3>, T, threads, 0, st, D, idx, prob, ds, pn, out, dim, K, eps);
+    case 4: return launch_pdl(moe_combine_reg_kernel<4>, T, threads, 0, st, D, idx, prob, ds, pn, out, dim, K, eps);
+    default: return launch_pdl(moe_combine_kernel, T, threads, 0, st, D, idx, prob, ds, pn, out, dim, K, eps);
   }
 }
 
@@ -1653,6 +1720,289 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// ---------------------------------------------------------------- decode batches
+// T <= 2 tokens (at most 2K routed slots): the expert products as one wave of
+// CTAs, one per SM.  The work is the list of units (expert e, token chunk of up
+// to NB = T slots, row v) in expert-major order with v fastest, so a CTA's
+// contiguous share of it is a few contiguous byte ranges of weights.  The CTA
+// streams its share through a ring of NS stages (one bulk copy per physical
+// row, issued as far ahead as the ring allows) and all its warps decode a
+// stage together: task (block b, physical row r) in block-major order, so the
+// lanes of a warp read the same activation columns (shared-memory broadcasts)
+// and distinct rows' blocks.  Per-task partial sums go to shared memory; each
+// unit then adds its blocks in block order (fixed order: deterministic).
+//   GATEUP: physical rows of a unit = gate row v and up row ff+v of expert e;
+//           G[slot][v] = gelu(gate) * up (Llama.kt:316-322).
+//   DOWN:   one virtual row (PR real rows of the [dim, ff] matrix) per unit;
+//           D[slot][v*PR + r].  The per-16-column sums of the staged G rows
+//           are made here.
+constexpr int kDecHeadInts = kMaxExperts + 4;  // s_units, s_off
+constexpr int kDecMaxSlots = 2 * kMaxUsed;      // T <= 2
+constexpr int kDecHeadBytes = 4 * (2 * kDecHeadInts + kDecMaxSlots);
+
+struct DecArgs {
+  const uint8_t* w;
+  const float* act;      // GATEUP: moe_in [T][cols]; DOWN: G [T*K][cols]
+  const float* act_s16;  // GATEUP: moe_in_s16 [T][cols/16]; DOWN: unused
+  float* out;            // GATEUP: G [slots][ff]; DOWN: D [slots][dim]
+  const int32_t* offsets;
+  const int32_t* perm;
+  unsigned* status;
+  int E, n_used, ff, dim;
+  int cols, nvrows, bpv;
+  int act_rows;          // activation rows staged (GATEUP: T; DOWN: T*K)
+  int rs, ns, pitch;     // units per stage, ring stages, bytes per physical row slot
+  int stage_bytes;
+  int tab_at, red_at, act_at, s16_at, ring_at;  // shared-memory layout (bytes)
+  int red_stride;        // floats of one of the two partial-sum buffers
+  int n_slots;           // T * n_used
+  long long expert_elems;
+  // GATEUP only: the down product's weights, prefetched into L2 for the down
+  // kernel's CTA with the same index (nullptr: none)
+  const uint8_t* pf_w;
+  int pf_nvrows, pf_grid;
+  long long pf_row_bytes, pf_expert_bytes;
+};
+
+struct DecUnit {
+  int v, nbv;
+  int arow[2];  // activation row of each token (GATEUP: its token; DOWN: its slot)
+  int slot[2];  // output row (slot)
+  int off[2];   // offset of each physical row's first byte in its ring row
+};
+
+template <int FMT, bool GATEUP, int PR, int NB>
+__global__ void __launch_bounds__(512, 1) moe_dec_kernel(const __grid_constant__ DecArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int BS = block_size(FMT), TS = type_size(FMT);
+  constexpr int PHYS = GATEUP ? 2 : 1;
+  int* s_units = reinterpret_cast<int*>(smem);  // [E+1] first unit of each expert
+  int* s_off = s_units + kDecHeadInts;           // [E+1] copy of offsets
+  int* s_perm = s_off + kDecHeadInts;            // [n_slots] copy of perm
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecHeadBytes);  // [ns] stages, [1] activations
+  DecUnit* tab = reinterpret_cast<DecUnit*>(smem + a.tab_at);          // [2 ns][rs]
+  float* red = reinterpret_cast<float*>(smem + a.red_at);              // [2][red_stride]
+  float* s_act = reinterpret_cast<float*>(smem + a.act_at);            // [act_rows][cols]
+  float* s_s16 = reinterpret_cast<float*>(smem + a.s16_at);            // [act_rows][cols/16]
+  uint8_t* ring = smem + a.ring_at;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  const int NS = a.ns, RS = a.rs, c16 = a.cols / 16;
+  uint64_t* act_bar = bars + NS;
+
+  if (tid <= NS) mbar_init(&bars[tid], 1);
+  if (tid == 0) fence_barrier_init();
+  // GATEUP waits for the front (offsets, perm, moe_in) and only then lets the
+  // down grid launch, so the down grid may read offsets/perm and fetch its
+  // weights before its own wait, which guards only G.
+  if (GATEUP) {
+    grid_dep_wait();
+    grid_dep_launch();
+  }
+  // offsets and perm into shared memory (one round trip for all threads)
+  for (int i = tid; i <= a.E; i += nthr) s_off[i] = a.offsets[i];
+  for (int i = tid; i < a.n_slots; i += nthr) s_perm[i] = a.perm[i];
+  __syncthreads();
+  if (warp == 0) {  // units per expert: ceil(n_e / NB) token chunks x nvrows rows
+    int carry = 0;
+    for (int base = 0; base < a.E; base += 32) {
+      const int e = base + lane;
+      const int v = e < a.E ? (s_off[e + 1] - s_off[e] + NB - 1) / NB * a.nvrows : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (e < a.E) s_units[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_units[a.E] = carry;
+  }
+  __syncthreads();
+  const int U = s_units[a.E];
+  const int u0 = (int)((long long)U * blockIdx.x / gridDim.x);
+  const int u1 = (int)((long long)U * (blockIdx.x + 1) / gridDim.x);
+  const int nst = (u1 - u0 + RS - 1) / RS;
+  if (nst == 0) {
+    if (!GATEUP) {
+      grid_dep_wait();
+      grid_dep_launch();
+    }
+    return;
+  }
+
+  // stage s of this CTA: ring slot s % NS, unit table s % (2 NS) (the epilogue
+  // of stage s still reads its table while stage s + NS is being issued)
+  auto issue = [&](int s) {
+    const int slot = s % NS;
+    DecUnit* tb = tab + (size_t)(s % (2 * NS)) * RS;
+    uint8_t* sbase = ring + (size_t)slot * a.stage_bytes;
+    const int us = u0 + s * RS, nu = min(RS, u1 - us);
+    uint32_t mine = 0;
+    for (int i = lane; i < nu; i += 32) {
+      const int u = us + i;
+      int lo = 0, hi = a.E - 1;  // last expert whose first unit is <= u (never an empty one)
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_units[mid] <= u) lo = mid;
+        else hi = mid - 1;
+      }
+      const int e = lo, local = u - s_units[e];
+      const int k = local / a.nvrows, v = local - k * a.nvrows;
+      const int p0 = s_off[e] + k * NB;
+      DecUnit d;
+      d.v = v;
+      d.nbv = min(NB, s_off[e + 1] - p0);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int sl = (j < NB && j < d.nbv) ? s_perm[p0 + j] : s_perm[p0];
+        d.slot[j] = sl;
+        d.arow[j] = GATEUP ? sl / a.n_used : sl;
+      }
+      const long long eb = (long long)e * a.expert_elems / BS;  // expert's first block
+#pragma unroll
+      for (int ph = 0; ph < PHYS; ++ph) {
+        const long long row = GATEUP ? (ph ? (long long)a.ff + v : (long long)v) : (long long)v;
+        const long long start = (eb + row * a.bpv) * TS;
+        const long long a0 = start & ~15ll, a1 = (start + (long long)a.bpv * TS + 15) & ~15ll;
+        d.off[ph] = (int)(start & 15);
+        bulk_g2s(sbase + (size_t)(ph * nu + i) * a.pitch, a.w + a0, (uint32_t)(a1 - a0), &bars[slot]);
+        mine += (uint32_t)(a1 - a0);
+      }
+      if (PHYS == 1) d.off[1] = 0;
+      tb[i] = d;
+    }
+    const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      mbar_arrive_expect_tx(&bars[slot], total);
+    }
+  };
+
+  if (warp == 0)
+    for (int s = 0; s < NS && s < nst; ++s) issue(s);
+  if (!GATEUP) {  // G is the previous grid's output
+    grid_dep_wait();
+    grid_dep_launch();
+  }
+  if (tid == 32) {  // activations, once (warp 1)
+    const uint32_t ab = (uint32_t)a.act_rows * (uint32_t)a.cols * 4u;
+    const uint32_t sb = GATEUP ? (uint32_t)a.act_rows * (uint32_t)c16 * 4u : 0u;
+    mbar_arrive_expect_tx(act_bar, ab + sb);
+    bulk_g2s(s_act, a.act, ab, act_bar);
+    if (GATEUP) bulk_g2s(s_s16, a.act_s16, sb, act_bar);
+  }
+  if (GATEUP && a.pf_w && tid == 64 && (int)blockIdx.x < a.pf_grid) {
+    // L2 prefetch of the down rows that down CTA blockIdx.x will read.  With
+    // NB = T every routed expert has one token chunk, so down unit u is row
+    // u % pf_nvrows of the (u / pf_nvrows)-th routed expert.
+    const int Ud = U / a.nvrows * a.pf_nvrows;
+    const int d0 = (int)((long long)Ud * blockIdx.x / a.pf_grid);
+    const int d1 = (int)((long long)Ud * (blockIdx.x + 1) / a.pf_grid);
+    for (int r = d0 / a.pf_nvrows; d0 < d1 && r <= (d1 - 1) / a.pf_nvrows; ++r) {
+      int lo = 0, hi = a.E - 1;  // the expert whose units start at r * nvrows
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_units[mid] <= r * a.nvrows) lo = mid;
+        else hi = mid - 1;
+      }
+      const int v0 = max(d0, r * a.pf_nvrows) - r * a.pf_nvrows;
+      const int v1 = min(d1, (r + 1) * a.pf_nvrows) - r * a.pf_nvrows;
+      const long long b0 = (long long)lo * a.pf_expert_bytes + v0 * a.pf_row_bytes;
+      const long long b1 = (long long)lo * a.pf_expert_bytes + v1 * a.pf_row_bytes;
+      const long long p0 = b0 & ~15ll, p1 = (b1 + 15) & ~15ll;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.pf_w + p0), "r"((uint32_t)(p1 - p0))
+                   : "memory");
+    }
+  }
+
+  bool ok = mbar_wait_bounded(act_bar, 0);
+  if (!GATEUP && ok) {
+    for (int i = tid; i < a.act_rows * c16; i += nthr) {
+      const float* q = s_act + (size_t)(i / c16) * a.cols + 16 * (i % c16);
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) t += q[k];
+      s_s16[i] = t;
+    }
+  }
+  int s = 0;
+  if (!__syncthreads_and(ok)) {
+    if (tid == 0) record_error(a.status, ERR_TIMEOUT_FULL);
+  } else {
+    for (; s < nst; ++s) {
+      const int slot = s % NS;
+      const DecUnit* tb = tab + (size_t)(s % (2 * NS)) * RS;
+      const int us = u0 + s * RS, nu = min(RS, u1 - us);
+      const int prow = PHYS * nu, ntask = prow * a.bpv;
+      float* rb = red + (size_t)(s & 1) * a.red_stride;
+      const uint8_t* sbase = ring + (size_t)slot * a.stage_bytes;
+      const bool okw = mbar_wait_bounded(&bars[slot], (s / NS) & 1);
+      if (okw) {
+        for (int t = tid; t < ntask; t += nthr) {
+          const int b = t / prow, r = t - b * prow;
+          const int ph = (PHYS == 2 && r >= nu) ? 1 : 0;
+          const DecUnit& d = tb[r - ph * nu];
+          const float* xr[NB];
+          const float* xs16[NB];
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            xr[j] = s_act + (size_t)d.arow[j] * a.cols;
+            xs16[j] = s_s16 + (size_t)d.arow[j] * c16;
+          }
+          float acc[NB][PR];
+#pragma unroll
+          for (int j = 0; j < NB; ++j)
+#pragma unroll
+            for (int q = 0; q < PR; ++q) acc[j][q] = 0.f;
+          blk_nb<FMT, PR, NB>(sbase + (size_t)r * a.pitch + d.off[ph] + (size_t)b * TS, b * BS, a.cols, xr, xs16, 0,
+                              d.nbv, acc);
+          float* o = rb + (size_t)t * (NB * PR);
+#pragma unroll
+          for (int j = 0; j < NB; ++j)
+#pragma unroll
+            for (int q = 0; q < PR; ++q) o[j * PR + q] = acc[j][q];
+        }
+      }
+      // the ring slot is read: order those reads before the bulk copies that refill it
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (__syncthreads_or(!okw)) {
+        if (tid == 0) record_error(a.status, ERR_TIMEOUT_FULL);
+        break;
+      }
+      if (warp == 0 && s + NS < nst) issue(s + NS);
+      // unit results: blocks added in block order (the last threads, away from the issuing warp)
+      for (int q = nthr - 1 - tid; q < nu * NB; q += nthr) {
+        const int i = q / NB, j = q - (q / NB) * NB;
+        const DecUnit& d = tb[i];
+        if (j >= d.nbv) continue;
+        if constexpr (GATEUP) {
+          float g = 0.f, up = 0.f;
+          for (int b = 0; b < a.bpv; ++b) {
+            g += rb[((size_t)b * prow + i) * NB + j];
+            up += rb[((size_t)b * prow + nu + i) * NB + j];
+          }
+          a.out[(size_t)d.slot[j] * a.ff + d.v] = __fmul_rn(gelu_ref(g), up);
+        } else {
+#pragma unroll
+          for (int q2 = 0; q2 < PR; ++q2) {
+            float sum = 0.f;
+            for (int b = 0; b < a.bpv; ++b) sum += rb[((size_t)b * prow + i) * (NB * PR) + j * PR + q2];
+            a.out[(size_t)d.slot[j] * a.dim + (size_t)d.v * PR + q2] = sum;
+          }
+        }
+      }
+    }
+  }
+  if (s < nst && warp == 0) {
+    // stopped early: wait (bounded) for the copies still in flight before the CTA exits
+    const int issued = min(nst, s + NS);
+    for (int q = s; q < issued; ++q)
+      if (!mbar_wait_bounded(&bars[q % NS], (q / NS) & 1)) record_error(a.status, ERR_TIMEOUT_DRAIN);
+  }
+}
+
 using RowsFn = void (*)(const RowsArgs);
 
 template <int FMT, bool GU, int PR>
@@ -1764,8 +2114,10 @@ static int launch_expert_rows(g4_ctx* c, int type, bool gu, const uint8_t* w, co
   a.stage_bytes = (int)align_up((size_t)a.xs_at + (size_t)nb * a.xs16n * 4, 128);
   const size_t stage = (size_t)a.stage_bytes;
   // warps per CTA from the amount of work, so that every SM gets some
-  const long long max_items = (long long)(std::min((long long)T * K, (long long)E) +
-                                          ((long long)T * K + nb - 1) / nb) * a.ngroups;
+  // Upper bound on items: sum over experts of ceil(n_e / nb) token chunks is
+  // at most (T*K + (nb - 1) * experts used) / nb, times the row groups.
+  const long long tk = (long long)T * K;
+  const long long max_items = ((tk + (long long)(nb - 1) * std::min(tk, (long long)E) + nb - 1) / nb) * a.ngroups;
   auto need = [&](int wv, int ns) { return head + 128 * ((wv * ns * 8 + 127) / 128) + (size_t)wv * ns * stage; };
   int warps;
   // Few items (small batches): one CTA per item, its warps split the chunks,
@@ -1774,7 +2126,9 @@ static int launch_expert_rows(g4_ctx* c, int type, bool gu, const uint8_t* w, co
   if (split) {
     a.split = std::min(a.nchunks, 8);
     warps = a.split;
-    a.ns = 2;
+    // as many stages as a warp has chunks (up to 4): no idle ring slots, so
+    // that more CTAs fit on an SM
+    a.ns = 1;
     while (a.ns < 4 && a.ns * a.split < a.nchunks && need(warps, a.ns + 1) <= (size_t)optin) ++a.ns;
   } else {
     a.split = 1;
@@ -1795,6 +2149,182 @@ static int launch_expert_rows(g4_ctx* c, int type, bool gu, const uint8_t* w, co
                                                                            (long long)c->dev.sms * occ));
   fn<<<grid, 32 * warps, smem, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// ---------------------------------------------------------------- decode launch
+using DecFn = void (*)(const DecArgs);
+
+template <int FMT, bool GU, int PR>
+static DecFn dec_fn_nb(int nb) {
+  return nb == 2 ? moe_dec_kernel<FMT, GU, PR, 2> : moe_dec_kernel<FMT, GU, PR, 1>;
+}
+
+static DecFn dec_fn(int type, bool gu, int pr, int nb) {
+  if (type == Q4_K) {
+    if (gu) return dec_fn_nb<Q4_K, true, 1>(nb);
+    return pr == 1 ? dec_fn_nb<Q4_K, false, 1>(nb) : pr == 2 ? dec_fn_nb<Q4_K, false, 2>(nb)
+                                                             : dec_fn_nb<Q4_K, false, 4>(nb);
+  }
+  if (type == Q6_K) {
+    if (gu) return dec_fn_nb<Q6_K, true, 1>(nb);
+    return pr == 1 ? dec_fn_nb<Q6_K, false, 1>(nb) : pr == 2 ? dec_fn_nb<Q6_K, false, 2>(nb)
+                                                             : dec_fn_nb<Q6_K, false, 4>(nb);
+  }
+  if (type == Q8_0 && pr == 1) return gu ? dec_fn_nb<Q8_0, true, 1>(nb) : dec_fn_nb<Q8_0, false, 1>(nb);
+  return nullptr;
+}
+
+// Geometry and shared-memory layout of one decode product; false when the
+// decode kernels do not handle it (the caller then takes the other kernels).
+static bool dec_plan(const g4_ctx* c, int type, bool gu, int E, int K, int dim, int ff, int T, int per_sm,
+                     DecArgs& a, int& grid, int& threads, size_t& smem, int& pr) {
+  if (type != Q4_K && type != Q6_K && type != Q8_0) return false;
+  if (T < 1 || T > 2 || E > kMaxExperts || K > kMaxUsed) return false;
+  const int BS = block_size(type), TS = type_size(type);
+  a = DecArgs{};
+  a.E = E;
+  a.n_used = K;
+  a.ff = ff;
+  a.dim = dim;
+  a.n_slots = T * K;
+  pr = 1;
+  if (gu) {
+    if (dim % BS || dim % 64) return false;
+    a.cols = dim;
+    a.nvrows = ff;
+    a.bpv = dim / BS;
+    a.expert_elems = 2LL * ff * dim;
+    a.act_rows = T;
+  } else {
+    if (ff % 64) return false;
+    if (ff % BS) {
+      if (type == Q8_0) return false;
+      int g = ff % BS, b = BS;
+      while (b) {
+        const int t = g % b;
+        g = b;
+        b = t;
+      }
+      pr = BS / g;
+      if (pr != 2 && pr != 4) return false;
+    }
+    if (dim % pr) return false;
+    a.cols = ff;
+    a.nvrows = dim / pr;
+    a.bpv = pr * ff / BS;
+    a.expert_elems = (long long)dim * ff;
+    a.act_rows = T * K;
+  }
+  if (a.expert_elems % BS) return false;
+  const int PHYS = gu ? 2 : 1, NB = T;
+  a.pitch = rows_pitch(a.bpv * TS + 32);
+  // NB = T covers every expert's slots in one chunk (a token picks an expert once)
+  const long long units_max = std::min((long long)T * K, (long long)E) * a.nvrows;
+  // per_sm CTAs of 512 / per_sm threads on each SM: their stages interleave
+  threads = 512 / per_sm;
+  grid = (int)std::min<long long>((long long)c->dev.sms * per_sm, units_max);
+  const long long share = (units_max + grid - 1) / grid;
+  // about one block per thread per stage (four for 32-weight blocks), at most
+  // 96 KB of rows per SM and stage
+  int rs = std::max(1, (BS == 32 ? 4 : 1) * threads / (PHYS * a.bpv));
+  rs = std::min(rs, std::max(1, 96 * 1024 / per_sm / (PHYS * a.pitch)));
+  rs = (int)std::max<long long>(1, std::min<long long>(rs, share));
+  int ns = (int)std::min<long long>(4, (share + rs - 1) / rs);
+  auto layout = [&](int rs_, int ns_) {
+    size_t o = kDecHeadBytes + 8 * (size_t)(ns_ + 1);
+    o = align_up(o, 16);
+    a.tab_at = (int)o;
+    o += (size_t)2 * ns_ * rs_ * sizeof(DecUnit);
+    o = align_up(o, 16);
+    a.red_at = (int)o;
+    a.red_stride = rs_ * PHYS * a.bpv * NB * pr;
+    o += (size_t)2 * a.red_stride * 4;
+    o = align_up(o, 128);
+    a.act_at = (int)o;
+    o += (size_t)a.act_rows * a.cols * 4;
+    o = align_up(o, 16);
+    a.s16_at = (int)o;
+    o += (size_t)a.act_rows * (a.cols / 16) * 4;
+    o = align_up(o, 128);
+    a.ring_at = (int)o;
+    a.stage_bytes = (int)align_up((size_t)rs_ * PHYS * a.pitch, 128);
+    return o + (size_t)ns_ * a.stage_bytes;
+  };
+  // the SM's shared memory (the opt-in limit plus the 1 KB each CTA reserves) split over per_sm CTAs
+  const size_t optin = std::min<size_t>(c->dev.smem_optin, (c->dev.smem_optin + 1024) / per_sm - 1024);
+  smem = layout(rs, ns);
+  while (smem > optin && ns > 2) smem = layout(rs, --ns);
+  while (smem > optin && rs > 1) smem = layout(--rs, ns);
+  if (smem > optin) return false;
+  a.rs = rs;
+  a.ns = ns;
+  return true;
+}
+
+// CTAs per SM of the decode kernels (512 / this many threads each)
+constexpr int kDecCtasPerSm = 4;
+
+// Fixed table of decode kernels whose shared-memory limit was raised (no heap use).
+static bool dec_prepare(DecFn fn, int optin) {
+  static std::mutex mu;
+  static DecFn done[32];
+  static int n = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < n; ++i)
+    if (done[i] == fn) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (n < 32) done[n++] = fn;
+  return true;
+}
+
+// G4_MOE_DEC=0 turns the decode kernels off (read at every call)
+static bool dec_enabled() {
+  const char* v = getenv("G4_MOE_DEC");
+  return !(v && v[0] == '0');
+}
+
+// Both expert products of a decode batch (T <= 2) on the decode kernels.
+// Returns 0 when launched, -1 when they do not apply (nothing launched), -2 on
+// a launch error.
+static int launch_dec_pair(g4_ctx* c, const g4_moe_weights* w, const MoeScratch& m, int E, int K, int dim, int ff,
+                           int T, cudaStream_t st) {
+  if (!dec_enabled() || T > 2) return -1;
+  DecArgs ga, da;
+  int gg = 0, dg = 0, gt = 0, dt_ = 0, gpr = 1, dpr = 1;
+  size_t gs = 0, ds = 0;
+  const int per_sm = kDecCtasPerSm;
+  if (!dec_plan(c, w->gate_up_exps->type, true, E, K, dim, ff, T, per_sm, ga, gg, gt, gs, gpr) ||
+      !dec_plan(c, w->down_exps->type, false, E, K, dim, ff, T, per_sm, da, dg, dt_, ds, dpr))
+    return -1;
+  const DecFn gf = dec_fn(w->gate_up_exps->type, true, 1, T), df = dec_fn(w->down_exps->type, false, dpr, T);
+  if (!gf || !df) return -1;
+  const int optin = (int)c->dev.smem_optin;
+  if (!dec_prepare(gf, optin) || !dec_prepare(df, optin)) return -1;
+  ga.w = (const uint8_t*)w->gate_up_exps->d;
+  ga.act = m.moe_in;
+  ga.act_s16 = m.moe_in_s16;
+  ga.out = m.G;
+  da.w = (const uint8_t*)w->down_exps->d;
+  da.act = m.G;
+  da.act_s16 = nullptr;
+  da.out = m.D;
+  for (DecArgs* a : {&ga, &da}) {
+    a->offsets = m.offsets;
+    a->perm = m.perm;
+    a->status = c->status;
+  }
+  const int dt = w->down_exps->type;
+  ga.pf_w = da.w;
+  ga.pf_nvrows = da.nvrows;
+  ga.pf_grid = dg;
+  ga.pf_row_bytes = (long long)da.bpv * type_size(dt);
+  ga.pf_expert_bytes = da.expert_elems / block_size(dt) * type_size(dt);
+  if (launch_pdl(gf, gg, gt, gs, st, ga) != cudaSuccess) return -2;
+  if (launch_pdl(df, dg, dt_, ds, st, da) != cudaSuccess) return -2;
+  return 0;
 }
 
 static int tensor_ok(const g4_tensor* t, int type, uint64_t n) {
@@ -1911,6 +2441,11 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
     done = true;
   }
   if (!done) {
+    const int rd = launch_dec_pair(c, w, m, E, K, dim, ff, T, st);
+    if (rd == -2) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer decode launch");
+    done = rd == 0;
+  }
+  if (!done) {
     int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
                                m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, false);
     const bool rows_gu = r == 0;
@@ -1932,7 +2467,7 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
     }
     if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer expert launch");
   }
-  launch_combine(w, m, out, T, st);
+  if (cudaError_t ce = launch_combine(w, m, out, T, st)) return c->cuda_fail(ce, "g4_moe_layer combine launch");
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   e = cudaGetLastError();
@@ -2164,7 +2699,7 @@ extern "C" int g4_moe_layer_ep(g4_ctx* c, const g4_moe_weights* w, const float* 
   }
   if (T == 0) return 0;
   moe_ep_unpack_kernel<<<(n_slots + 7) / 8, 256, 0, st>>>(back_rows, perm_d, n_slots, dim, m.D);
-  launch_combine(w, m, out, T, st);
+  if (cudaError_t ce = launch_combine(w, m, out, T, st)) return c->cuda_fail(ce, "g4_moe_layer_ep combine launch");
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   e = cudaGetLastError();
@@ -2341,13 +2876,16 @@ extern "C" int g4_moe_layer_noalloc(g4_ctx* c, const g4_moe_weights* w, const fl
   MoeScratch m = carve(base, T, dim, E, K, ff);
   cudaError_t e = launch_front(c, w, x, m, T, true, st);
   if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_noalloc launch");
-  int r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
-                             m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, true);
-  const bool rows_gu = r == 0;
+  int r = launch_dec_pair(c, w, m, E, K, dim, ff, T, st);
+  const bool dec = r == 0;
+  if (r == -1)
+    r = launch_expert_rows(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in,
+                           m.moe_in_s16, m.G, m.G_s16, m, E, K, dim, ff, T, st, true);
+  const bool rows_gu = !dec && r == 0;
   if (r == -1)
     r = launch_expert_noalloc(c, w->gate_up_exps->type, true, (const uint8_t*)w->gate_up_exps->d, m.moe_in, m.G, m,
                               E, K, dim, ff, T, st);
-  if (r == 0) {
+  if (r == 0 && !dec) {
     r = rows_gu ? launch_expert_rows(c, w->down_exps->type, false, (const uint8_t*)w->down_exps->d, m.G, m.G_s16,
                                      m.D, nullptr, m, E, K, dim, ff, T, st, true)
                 : -1;
@@ -2360,7 +2898,7 @@ extern "C" int g4_moe_layer_noalloc(g4_ctx* c, const g4_moe_weights* w, const fl
     return G4_E_ARG;
   }
   if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer_noalloc expert launch");
-  launch_combine(w, m, out, T, st);
+  if (cudaError_t ce = launch_combine(w, m, out, T, st)) return c->cuda_fail(ce, "g4_moe_layer_noalloc combine launch");
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   e = cudaGetLastError();

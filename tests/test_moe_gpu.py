@@ -131,3 +131,57 @@ def test_moe_bad_weights_rejected(g4, ctx, moe32):
     out = torch.zeros((1, 2816), device="cuda")
     with pytest.raises(g4.G4Error):
         layer.forward(x, out, 1)
+
+
+@pytest.mark.parametrize("etype", [12, 14, 8])
+@pytest.mark.parametrize("n_tokens", [1, 2])
+def test_moe_decode_batches(g4, ctx, etype, n_tokens):
+    """T <= 2 runs on the one-wave decode kernels; every token vs the oracle."""
+    from gemma4_kt_b200 import synth
+
+    d = synth.MoeLayerData(seed=7 + n_tokens, n_expert=16, expert_type=etype)
+    check_layer(g4, ctx, d, n_tokens)
+
+
+@pytest.mark.parametrize("n_tokens", [1, 2])
+def test_moe_decode_full_geometry(g4, ctx, n_tokens):
+    """The benchmark layer at decode sizes (down rows of 704 Q4_K weights: 4 rows per 11 blocks)."""
+    from gemma4_kt_b200 import synth
+
+    d = synth.MoeLayerData(seed=3)
+    check_layer(g4, ctx, d, n_tokens)
+    check_layer(g4, ctx, d, n_tokens, post_norm=False)
+
+
+def test_moe_decode_matches_rows_path(g4, ctx, moe32, monkeypatch):
+    """Decode kernels against the rows kernels (G4_MOE_DEC=0) on the same tokens."""
+    import torch
+
+    layer = g4.MoeLayer.upload(ctx, moe32)
+    for T in (1, 2):
+        x = torch.from_numpy(moe32.tokens(T)).cuda()
+        outs = []
+        for mode in ("1", "0"):
+            monkeypatch.setenv("G4_MOE_DEC", mode)
+            out = torch.empty((T, moe32.dim), dtype=torch.float32, device="cuda")
+            layer.forward(x, out, T)
+            ctx.sync()
+            outs.append(out.cpu().numpy())
+        for t in range(T):
+            assert rel_l2(outs[0][t], outs[1][t]) < 1e-4
+
+
+def test_moe_pdl_off_matches(g4, ctx, moe32, monkeypatch):
+    """The decode chain launched without programmatic dependent launch (G4_PDL=0) gives the same bits."""
+    import torch
+
+    layer = g4.MoeLayer.upload(ctx, moe32)
+    x = torch.from_numpy(moe32.tokens(2)).cuda()
+    outs = []
+    for mode in ("1", "0", "1"):
+        monkeypatch.setenv("G4_PDL", mode)
+        out = torch.empty((2, moe32.dim), dtype=torch.float32, device="cuda")
+        layer.forward(x, out, 2)
+        ctx.sync()
+        outs.append(out.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
