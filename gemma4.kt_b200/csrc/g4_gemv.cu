@@ -112,23 +112,50 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
     if (gi != g0) rs_i = row_start(gi);
   }
 
-  // x -> shared memory while the first weight stages are in flight, plus the
-  // sum of every 16 and every 32 consecutive columns
-  for (int i = threadIdx.x * 4; i < p.cols; i += blockDim.x * 4)
-    *reinterpret_cast<float4*>(xs + i) = __ldg(reinterpret_cast<const float4*>(a.x + i));
-  __syncthreads();
-  for (int k = threadIdx.x; k < n16; k += blockDim.x) {
-    float t = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) t += xs[16 * k + i];
-    xsum16[k] = t;
-  }
-  __syncthreads();
-  for (int k = threadIdx.x; k < n16 / 2; k += blockDim.x) xsum32[k] = xsum16[2 * k] + xsum16[2 * k + 1];
-  // quantized formats: int16 activations per 32 columns for the dp2a decoders
+  // x -> shared memory while the first weight stages are in flight, in one
+  // pass: thread t takes float4 columns t, t + blockDim, ...; for the quantized
+  // formats 4 lanes form a 16-column sum, 8 lanes (one 32-column block) the
+  // 32-column sum and the block's int16 values (quantize_x16's rule)
   int16_t* xq = reinterpret_cast<int16_t*>(smem + p.xq_off);
   float* xsc32 = xsum32 + n16 / 2;
-  if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) quantize_x16(xs, p.cols, xq, xsc32);
+  {
+    const int n4 = p.cols / 4;  // a multiple of 8 (cols % 32 == 0)
+    for (int i0 = 0; i0 < n4; i0 += blockDim.x) {
+      const int i = i0 + (int)threadIdx.x;
+      const bool act = i < n4;
+      const float4 v = act ? __ldg(reinterpret_cast<const float4*>(a.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) {
+        float s16 = (v.x + v.y) + (v.z + v.w);
+        s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
+        s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
+        const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 4);
+        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        // smallest power of two sc with m / sc <= 32760 (1 for an all-zero block)
+        const uint32_t t = __float_as_uint(m * (1.0f / 32760.0f));
+        uint32_t e = t & 0x7F800000u;
+        if (t & 0x007FFFFFu) e += 0x00800000u;
+        const bool nz = m > 0.f && e != 0u;
+        const float inv = nz ? __uint_as_float(0x7F000000u - e) : 1.0f;
+        if (act) {
+          const uint32_t q01 = (uint32_t)(uint16_t)__float2int_rn(v.x * inv) |
+                               ((uint32_t)(uint16_t)__float2int_rn(v.y * inv) << 16);
+          const uint32_t q23 = (uint32_t)(uint16_t)__float2int_rn(v.z * inv) |
+                               ((uint32_t)(uint16_t)__float2int_rn(v.w * inv) << 16);
+          *reinterpret_cast<uint2*>(xq + xq_at(4 * i)) = make_uint2(q01, q23);
+          if ((i & 3) == 0) xsum16[i >> 2] = s16;
+          if ((i & 7) == 0) {
+            xsum32[i >> 3] = s32;
+            xsc32[i >> 3] = nz ? __uint_as_float(e) : 1.0f;
+          }
+        }
+      } else {
+        if (act) *reinterpret_cast<float4*>(xs + 4 * i) = v;
+      }
+    }
+  }
   __syncthreads();
 
   float acc[PR];

@@ -1720,6 +1720,65 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// Q4_K for NB tokens on int16 activations (quantize_x16 layout: xq[j] is token
+// j's padded int16 row, xsc[j] its per-32-column scales, xs16[j] its fp32
+// per-16-column sums), the dp2a form of blk_nb's Q4_K branch.
+template <int PR, int NB>
+__device__ __forceinline__ void blk_q4k_nb_i16(const uint8_t* blk, int e0, int cols, const int16_t* const* xq,
+                                               const float* const* xsc, const float* const* xs16, int nbv,
+                                               float (&acc)[NB][PR]) {
+  const uint4 h = lds128(blk);
+  const float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
+  const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+  const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
+  const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+  const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int eg = e0 + 64 * g;
+    const int col = PR == 1 ? eg : eg % cols;
+    const int rr = PR == 1 ? 0 : eg / cols;
+    const int xo = xq_at(col);
+    const uint4 qa = lds128(blk + 16 + 32 * g), qb = lds128(blk + 32 + 32 * g);
+    int alo[NB], ahi[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) alo[j] = ahi[j] = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t w = k == 0 ? qa.x : k == 1 ? qa.y : k == 2 ? qa.z : k == 3 ? qa.w
+                       : k == 4 ? qb.x : k == 5 ? qb.y : k == 6 ? qb.z : qb.w;
+      const uint32_t lo = w & 0x0F0F0F0Fu, hi = w & 0xF0F0F0F0u;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        if (j < nbv) {
+          const uint2 xl = *reinterpret_cast<const uint2*>(xq[j] + xo + 4 * k);
+          const uint2 xh = *reinterpret_cast<const uint2*>(xq[j] + xo + 32 + 4 * k);
+          alo[j] = dp2a_lo_su(xl.x, lo, alo[j]);
+          alo[j] = dp2a_hi_su(xl.y, lo, alo[j]);
+          ahi[j] = dp2a_lo_su(xh.x, hi, ahi[j]);
+          ahi[j] = dp2a_hi_su(xh.y, hi, ahi[j]);
+        }
+      }
+    }
+    const uint32_t scw = g < 2 ? sc03 : sc47, mnw = g < 2 ? mn03 : mn47;
+    const int b0 = (2 * g) & 3;
+    const float dsl = d * small_u2f((scw >> (8 * b0)) & 0xFFu), dsh = d * small_u2f((scw >> (8 * b0 + 8)) & 0xFFu);
+    const float mn_lo = small_u2f((mnw >> (8 * b0)) & 0xFFu), mn_hi = small_u2f((mnw >> (8 * b0 + 8)) & 0xFFu);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      if (j < nbv) {
+        const float* q = xs16[j] + col / 16;
+        const float xlo = q[0] + q[1], xhi = q[2] + q[3];
+        const float s_lo = xsc[j][col / 32], s_hi = xsc[j][col / 32 + 1] * 0.0625f;
+        float v = dsl * (s_lo * (float)alo[j]);
+        v = fmaf(dsh, s_hi * (float)ahi[j], v);
+        v = fmaf(-dmin, fmaf(mn_lo, xlo, mn_hi * xhi), v);
+        add_row<PR>(acc[j], rr, v);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- decode batches
 // T <= 2 tokens (at most 2K routed slots): the expert products as one wave of
 // CTAs, one per SM.  The work is the list of units (expert e, token chunk of up
@@ -1754,6 +1813,7 @@ struct DecArgs {
   int rs, ns, pitch;     // units per stage, ring stages, bytes per physical row slot
   int stage_bytes;
   int tab_at, red_at, act_at, s16_at, ring_at;  // shared-memory layout (bytes)
+  int xq_at_, xsc_at, xq_stride;                // Q4_K: int16 activations (padded rows), per-32 scales
   int red_stride;        // floats of one of the two partial-sum buffers
   int n_slots;           // T * n_used
   long long expert_elems;
@@ -1784,6 +1844,8 @@ __global__ void __launch_bounds__(512, 1) moe_dec_kernel(const __grid_constant__
   float* red = reinterpret_cast<float*>(smem + a.red_at);              // [2][red_stride]
   float* s_act = reinterpret_cast<float*>(smem + a.act_at);            // [act_rows][cols]
   float* s_s16 = reinterpret_cast<float*>(smem + a.s16_at);            // [act_rows][cols/16]
+  int16_t* s_xq = reinterpret_cast<int16_t*>(smem + a.xq_at_);         // Q4_K: [act_rows][xq_stride]
+  float* s_xsc = reinterpret_cast<float*>(smem + a.xsc_at);            // Q4_K: [act_rows][cols/32]
   uint8_t* ring = smem + a.ring_at;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
   const int NS = a.ns, RS = a.rs, c16 = a.cols / 16;
@@ -1928,6 +1990,24 @@ __global__ void __launch_bounds__(512, 1) moe_dec_kernel(const __grid_constant__
     }
   }
   int s = 0;
+  if (FMT == Q4_K && ok) {
+    // int16 activations per 32 columns (see quantize_x16), one warp per block
+    const int c32 = a.cols / 32, W = nthr >> 5;
+    for (int bk = warp; bk < a.act_rows * c32; bk += W) {
+      const int r = bk / c32, b = bk - r * c32;
+      const float v = s_act[(size_t)r * a.cols + 32 * b + lane];
+      float m = fabsf(v);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const uint32_t t = __float_as_uint(m * (1.0f / 32760.0f));
+      uint32_t e = t & 0x7F800000u;
+      if (t & 0x007FFFFFu) e += 0x00800000u;
+      const bool nz = m > 0.f && e != 0u;
+      const float inv = nz ? __uint_as_float(0x7F000000u - e) : 1.0f;
+      s_xq[(size_t)r * a.xq_stride + xq_at(32 * b + lane)] = (int16_t)__float2int_rn(v * inv);
+      if (lane == 0) s_xsc[(size_t)r * c32 + b] = nz ? __uint_as_float(e) : 1.0f;
+    }
+  }
   if (!__syncthreads_and(ok)) {
     if (tid == 0) record_error(a.status, ERR_TIMEOUT_FULL);
   } else {
@@ -1956,8 +2036,19 @@ __global__ void __launch_bounds__(512, 1) moe_dec_kernel(const __grid_constant__
           for (int j = 0; j < NB; ++j)
 #pragma unroll
             for (int q = 0; q < PR; ++q) acc[j][q] = 0.f;
-          blk_nb<FMT, PR, NB>(sbase + (size_t)r * a.pitch + d.off[ph] + (size_t)b * TS, b * BS, a.cols, xr, xs16, 0,
-                              d.nbv, acc);
+          const uint8_t* blk = sbase + (size_t)r * a.pitch + d.off[ph] + (size_t)b * TS;
+          if constexpr (FMT == Q4_K) {
+            const int16_t* xq[NB];
+            const float* xsc[NB];
+#pragma unroll
+            for (int j = 0; j < NB; ++j) {
+              xq[j] = s_xq + (size_t)d.arow[j] * a.xq_stride;
+              xsc[j] = s_xsc + (size_t)d.arow[j] * (a.cols / 32);
+            }
+            blk_q4k_nb_i16<PR, NB>(blk, b * BS, a.cols, xq, xsc, xs16, d.nbv, acc);
+          } else {
+            blk_nb<FMT, PR, NB>(blk, b * BS, a.cols, xr, xs16, 0, d.nbv, acc);
+          }
           float* o = rb + (size_t)t * (NB * PR);
 #pragma unroll
           for (int j = 0; j < NB; ++j)
@@ -2218,6 +2309,7 @@ static bool dec_plan(const g4_ctx* c, int type, bool gu, int E, int K, int dim, 
   if (a.expert_elems % BS) return false;
   const int PHYS = gu ? 2 : 1, NB = T;
   a.pitch = rows_pitch(a.bpv * TS + 32);
+  a.xq_stride = (a.cols + 8 * ((a.cols + 255) / 256) + 3) / 4 * 4;  // padded int16 row, 8-byte multiple
   // NB = T covers every expert's slots in one chunk (a token picks an expert once)
   const long long units_max = std::min((long long)T * K, (long long)E) * a.nvrows;
   // per_sm CTAs of 512 / per_sm threads on each SM: their stages interleave
@@ -2245,6 +2337,12 @@ static bool dec_plan(const g4_ctx* c, int type, bool gu, int E, int K, int dim, 
     o = align_up(o, 16);
     a.s16_at = (int)o;
     o += (size_t)a.act_rows * (a.cols / 16) * 4;
+    o = align_up(o, 16);
+    a.xq_at_ = (int)o;
+    o += type == Q4_K ? (size_t)a.act_rows * a.xq_stride * 2 : 0;
+    o = align_up(o, 16);
+    a.xsc_at = (int)o;
+    o += type == Q4_K ? (size_t)a.act_rows * (a.cols / 32) * 4 : 0;
     o = align_up(o, 128);
     a.ring_at = (int)o;
     a.stage_bytes = (int)align_up((size_t)rs_ * PHYS * a.pitch, 128);
@@ -2262,7 +2360,7 @@ static bool dec_plan(const g4_ctx* c, int type, bool gu, int E, int K, int dim, 
 }
 
 // CTAs per SM of the decode kernels (512 / this many threads each)
-constexpr int kDecCtasPerSm = 4;
+constexpr int kDecCtasPerSm = 1;
 
 // Fixed table of decode kernels whose shared-memory limit was raised (no heap use).
 static bool dec_prepare(DecFn fn, int optin) {
@@ -2280,18 +2378,22 @@ static bool dec_prepare(DecFn fn, int optin) {
   return true;
 }
 
-// G4_MOE_DEC=0 turns the decode kernels off (read at every call)
-static bool dec_enabled() {
+// Largest batch the decode kernels take: 1 by default (at T = 2 the rows
+// kernels are faster on B200); G4_MOE_DEC=0 turns them off and G4_MOE_DEC=1
+// uses them up to T = 2 (read at every call).
+static int dec_max_tokens() {
   const char* v = getenv("G4_MOE_DEC");
-  return !(v && v[0] == '0');
+  if (v && v[0] == '0') return 0;
+  if (v && v[0] == '1') return 2;
+  return 1;
 }
 
-// Both expert products of a decode batch (T <= 2) on the decode kernels.
+// Both expert products of a decode batch (T <= dec_max_tokens()) on the decode kernels.
 // Returns 0 when launched, -1 when they do not apply (nothing launched), -2 on
 // a launch error.
 static int launch_dec_pair(g4_ctx* c, const g4_moe_weights* w, const MoeScratch& m, int E, int K, int dim, int ff,
                            int T, cudaStream_t st) {
-  if (!dec_enabled() || T > 2) return -1;
+  if (T > dec_max_tokens()) return -1;
   DecArgs ga, da;
   int gg = 0, dg = 0, gt = 0, dt_ = 0, gpr = 1, dpr = 1;
   size_t gs = 0, ds = 0;

@@ -135,19 +135,21 @@ def test_moe_bad_weights_rejected(g4, ctx, moe32):
 
 @pytest.mark.parametrize("etype", [12, 14, 8])
 @pytest.mark.parametrize("n_tokens", [1, 2])
-def test_moe_decode_batches(g4, ctx, etype, n_tokens):
-    """T <= 2 runs on the one-wave decode kernels; every token vs the oracle."""
+def test_moe_decode_batches(g4, ctx, etype, n_tokens, monkeypatch):
+    """T <= 2 on the one-wave decode kernels (forced up to T = 2); every token vs the oracle."""
     from gemma4_kt_b200 import synth
 
+    monkeypatch.setenv("G4_MOE_DEC", "1")
     d = synth.MoeLayerData(seed=7 + n_tokens, n_expert=16, expert_type=etype)
     check_layer(g4, ctx, d, n_tokens)
 
 
 @pytest.mark.parametrize("n_tokens", [1, 2])
-def test_moe_decode_full_geometry(g4, ctx, n_tokens):
+def test_moe_decode_full_geometry(g4, ctx, n_tokens, monkeypatch):
     """The benchmark layer at decode sizes (down rows of 704 Q4_K weights: 4 rows per 11 blocks)."""
     from gemma4_kt_b200 import synth
 
+    monkeypatch.setenv("G4_MOE_DEC", "1")
     d = synth.MoeLayerData(seed=3)
     check_layer(g4, ctx, d, n_tokens)
     check_layer(g4, ctx, d, n_tokens, post_norm=False)
@@ -178,6 +180,7 @@ def test_moe_pdl_off_matches(g4, ctx, moe32, monkeypatch):
     layer = g4.MoeLayer.upload(ctx, moe32)
     x = torch.from_numpy(moe32.tokens(2)).cuda()
     outs = []
+    monkeypatch.setenv("G4_MOE_DEC", "1")
     for mode in ("1", "0", "1"):
         monkeypatch.setenv("G4_PDL", mode)
         out = torch.empty((2, moe32.dim), dtype=torch.float32, device="cuda")
