@@ -340,7 +340,9 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
     if (pr != 2 && pr != 4) return p;
   }
   if (rows % pr != 0) return p;
-  const int xbytes = ((cols * 4 + 127) / 128) * 128;
+  // fp32 x in shared memory only for BF16 / F32; the quantized formats read the int16 form
+  const bool quantized = type == Q8_0 || type == Q4_K || type == Q6_K;
+  const int xbytes = quantized ? 0 : ((cols * 4 + 127) / 128) * 128;
   // per-16 and per-32 column sums, per-32 int16 scales; int16 activations
   const int xsbytes = (((cols / 16 + 2 * (cols / 32)) * 4 + 127) / 128) * 128;
   const int xqbytes = (((cols + 8 * ((cols + 255) / 256)) * 2 + 127) / 128) * 128;
@@ -380,15 +382,17 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
     p.ns = 2;
   } else {
     p.split = 1;
-    p.warps = env_int("G4_GEMV_WARPS", 16);
-    p.ns = env_int("G4_GEMV_STAGES", 2);
+    // enough CTAs to cover every SM: a warp streams one row group at a time, so
+    // fewer than 16 groups per SM means fewer warps per CTA, not fewer CTAs
+    p.warps = env_int("G4_GEMV_WARPS", std::max(1, std::min(16, p.ngroups / dev.sms)));
+    p.ns = env_int("G4_GEMV_STAGES", p.warps >= 16 ? 2 : 4);  // deeper rings when few warps share the SM
   }
   for (;;) {
     size_t red = p.split > 1 ? (size_t)p.warps * rows_per_group * pr * 4 : 0;
     size_t need = fixed + red + (size_t)p.warps * p.ns * stage;
     if (need <= budget) break;
     if (p.ns > 2) --p.ns;
-    else if (p.split == 1 && p.warps > 2) p.warps /= 2;
+    else if (p.split == 1 && p.warps > 2) --p.warps;
     else if (p.split > 1 && p.cb > unit && type != BF16 && type != F32) {
       // narrower chunks, more of them: keeps the CTA's rings within shared memory
       p.cb = std::max(unit, p.cb / 2 / unit * unit);

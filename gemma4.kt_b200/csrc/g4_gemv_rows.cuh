@@ -385,8 +385,10 @@ __device__ __forceinline__ void block_q6k_i16(const uint8_t* blk, int e0, int co
         const int rr = PR == 1 ? 0 : e / cols;
         // sc index 8h + 2*sub + c (Q6_KFloatTensor.kt:70)
         const int si = 2 * sub + c;
-        const int8_t sc = (int8_t)((((si >> 2) ? scw1 : scw0) >> (8 * (si & 3))) & 0xFFu);
-        const float v = (d * (float)sc) * fmaf(xsc32[col / 32], (float)a4[sub], -32.f * xsum16[col / 16]);
+        // int8 scale as float without I2F: (sc + 128) as an unsigned byte, minus 128
+        const uint32_t scb = ((((si >> 2) ? scw1 : scw0) >> (8 * (si & 3))) & 0xFFu) ^ 0x80u;
+        const float scf = small_u2f(scb) - 128.f;
+        const float v = (d * scf) * fmaf(xsc32[col / 32], (float)a4[sub], -32.f * xsum16[col / 16]);
         add_row<PR>(acc, rr, v);
       }
     }
