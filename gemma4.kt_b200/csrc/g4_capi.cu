@@ -101,11 +101,20 @@ void* g4_ctx::ep(size_t bytes) {
 }
 
 int g4_ctx::check_status(cudaStream_t st) {
-  cudaError_t e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) return cuda_fail(e, "kernel execution");
   unsigned h = 0;
-  e = cudaMemcpy(&h, status, sizeof h, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "status read");
+  if (status_host) {
+    // the status word rides the stream into pinned memory: one synchronisation
+    cudaError_t e = cudaMemcpyAsync(status_host, status, sizeof h, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return cuda_fail(e, "status read");
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel execution");
+    h = *status_host;
+  } else {
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel execution");
+    e = cudaMemcpy(&h, status, sizeof h, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "status read");
+  }
   if (h) {
     cudaMemset(status, 0, sizeof(unsigned));
     set_err("device status 0x%x (a bounded wait expired inside a kernel)", h);
@@ -157,6 +166,10 @@ int g4_init(int device, g4_ctx** out) {
     return G4_E_NOMEM;
   }
   cudaMemset(c->status, 0, kStatusWords * sizeof(unsigned));
+  if (cudaMallocHost(&c->status_host, sizeof(unsigned)) != cudaSuccess) {
+    cudaGetLastError();
+    c->status_host = nullptr;  // check_status falls back to a blocking copy
+  }
   *out = c;
   return 0;
 }
@@ -171,6 +184,7 @@ int g4_destroy(g4_ctx* c) {
   if (c->io_ptr) cudaFree(c->io_ptr);
   if (c->ep_ptr) cudaFree(c->ep_ptr);
   if (c->status) cudaFree(c->status);
+  if (c->status_host) cudaFreeHost(c->status_host);
   delete c;
   return 0;
 }

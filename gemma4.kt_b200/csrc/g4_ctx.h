@@ -17,6 +17,7 @@ struct g4_ctx {
   // MoE front kernel's completion ticket (its last CTA resets it to 0)
   unsigned* status = nullptr;
   unsigned* ticket() const { return status + 1; }
+  unsigned* status_host = nullptr;  // pinned copy target of status[0] (one synchronisation per check)
   void* scratch_ptr = nullptr; // growable device arena (host-buffer staging, MoE work buffers)
   size_t scratch_bytes = 0;
   void* pinned_ptr = nullptr;  // growable pinned host staging
