@@ -5,15 +5,17 @@
 // (FloatTensor.kt:18-29) and the per-type vectorDot it fans out to.
 //
 // Design (HBM-bound, CUDA cores):
-//  * Persistent CTAs (grid = #SMs x resident CTAs).  Warp 0 is a producer: one
-//    lane streams contiguous row tiles of the raw block stream into a ring of
-//    shared-memory stages with cp.async.bulk (TMA bulk copies, no multicast),
-//    signalling an mbarrier per stage.  The weights keep their on-disk layout;
-//    unaligned block strides (34 B, 210 B) are handled by copying the
-//    16-byte-aligned superset of each tile and decoding at a byte offset.
-//  * The other warps are consumers.  Each owns `rw` virtual rows of a tile and
-//    walks 16-weight units across them; the 16 activations of a unit are loaded
-//    once from shared memory and reused for every row (cuts smem traffic).
+//  * Persistent CTAs, sized so that every SM gets one.  Each warp owns row
+//    groups of 32/LPR virtual rows (LPR lanes share a row) and streams their
+//    segments through its own ring of shared-memory stages: one cp.async.bulk
+//    (no multicast) per row segment, one mbarrier per stage.  The weights keep
+//    their on-disk layout; unaligned block strides (34 B, 210 B) are handled by
+//    copying the 16-byte-aligned superset of each segment and decoding at a
+//    byte offset.  Few row groups: one CTA per group, its warps split the row.
+//  * Quantized formats: the CTA's prologue turns x, in one pass, into int16 per
+//    32-column block (power-of-two scales) plus fp32 column sums, and the block
+//    decoders multiply the stored codes as bytes with dp2a (g4_gemv_rows.cuh).
+//    BF16 / F32 read fp32 x with packed fma.
 //  * Rows whose length is not a multiple of the block size (e.g. 704-wide Q4_K
 //    expert down rows) are grouped into virtual rows of `pr` real rows, after
 //    which the block pattern repeats; accumulators are kept per real row.

@@ -1,31 +1,22 @@
-// g4_gemv_rows.cuh -- per-block dot products for the lane-per-row GEMV.
+// g4_gemv_rows.cuh -- per-block dot products for the lane-per-row GEMV and
+// the MoE expert kernels.
 //
 // Each lane owns one row (or a share of its blocks when several lanes split a
 // row) and walks its row segment in shared memory block by block; the
 // activations are read as broadcasts.  The arithmetic restates the reference vectorDots
 // (Q8_0FloatTensor.kt:39-142, Q4_KFloatTensor.kt:86-207,
 // Q6_KFloatTensor.kt:111-250, BF16FloatTensor.kt:35-74,
-// F32FloatTensor.kt:37-66) in fp32 with a different summation order; results
-// agree within rounding, not bitwise.
+// F32FloatTensor.kt:37-66) with a different summation order; results agree
+// within rounding, not bitwise.
 //
-// Integer -> float without the quarter-rate I2F pipe: a 4-bit or 6-bit code q
-// placed in mantissa bits 16..21 under exponent 127 is the float 1 + q/128
-// (one PRMT builds it from a byte that already holds 0x80|q).  Then
-// sum_i q_i x_i = 128 * (sum_i f_i x_i - sum_i x_i), with sum_i x_i taken from a
-// per-16/32-column table computed once per CTA.  The offset stays within ~8x
-// (q/128) or ~128x (q/2048) of the code term, so the cancellation costs a few
-// ulp of the partial sums: relative errors of 1e-6 and 1e-4 at worst, inside
-// the 1e-3 tolerance.
-// Int8 codes use the exact 2^23 + b form plus one packed subtraction.
+// The quantized formats multiply on the integer pipe (int16 activations, dp2a
+// on the stored codes, below).  BF16 / F32 use packed fp32 fma.  f_magic23
+// (int -> float without the quarter-rate I2F: byte b under exponent 150 is
+// 2^23 + b) serves the MoE kernels' float decoders.
 #pragma once
 #include "g4_common.cuh"
 
 namespace g4 {
-
-__device__ __forceinline__ float f_one_plus(uint32_t m, uint32_t byte) {
-  // byte 2 <- m.byte[byte] (0x80 | q), byte 3 <- 0x3F: 1 + q/128
-  return __uint_as_float(__byte_perm(m, 0x3F000000u, 0x7044u | (byte << 8)));
-}
 
 __device__ __forceinline__ float f_magic23(uint32_t m, uint32_t byte) {
   // byte 0 <- m.byte[byte], byte 3 <- 0x4B: 2^23 + b
@@ -46,165 +37,6 @@ __device__ __forceinline__ void add_row(float (&acc)[PR], int r, float v) {
   } else {
 #pragma unroll
     for (int k = 0; k < PR; ++k) acc[k] += (k == r) ? v : 0.f;
-  }
-}
-
-// ---------------------------------------------------------------- Q4_K
-// [fp16 d][fp16 dmin][scales 12][qs 128]; group g (64 weights) = low nibbles
-// of qs[32g..32g+31] (sub-block 2g) then their high nibbles (sub-block 2g+1).
-// Blocks are 144 = 9*16 bytes, so every block start is 16-byte aligned.
-// Low nibbles become 1 + q/128 (byte 2 of the float), high nibbles 1 + q/2048
-// (byte 1; one masking op for four codes instead of a shift and a mask).  The
-// accumulators start at -sum(x), so they end at sum(q x)/128 and
-// sum(q x)/2048; both are then scaled by d*sc (Q4_KFloatTensor.kt:117-147).
-template <int PR>
-__device__ __forceinline__ void block_q4k(const uint8_t* blk, int e0, int cols, const float* xs,
-                                          const float* xsum32, float (&acc)[PR]) {
-  const uint4 h = lds128(blk);
-  const float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
-  const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
-  const float dlo = 128.f * d, dhi = 2048.f * d;
-  // getScaleMinK4 (Q4_KFloatTensor.kt:70-84) for all 8 sub-blocks, byte-parallel
-  const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
-  const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-  const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-  const uint32_t C = 0x3F800000u;
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    const int eg = e0 + 64 * g;
-    const int col = PR == 1 ? eg : eg % cols;
-    const int rr = PR == 1 ? 0 : eg / cols;
-    const float* xp = xs + col;
-    const float xs_lo = xsum32[col / 32], xs_hi = xsum32[col / 32 + 1];
-    float2 alo = f2(-xs_lo, 0.f), ahi = f2(-xs_hi, 0.f);
-    const uint4 qa = lds128(blk + 16 + 32 * g), qb = lds128(blk + 32 + 32 * g);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float4 xl = lds_f4(xp + 4 * k);
-      const float4 xh = lds_f4(xp + 32 + 4 * k);
-      const uint32_t w = k == 0 ? qa.x : k == 1 ? qa.y : k == 2 ? qa.z : k == 3 ? qa.w
-                       : k == 4 ? qb.x : k == 5 ? qb.y : k == 6 ? qb.z : qb.w;
-      const uint32_t ml = (w & 0x0F0F0F0Fu) | 0x80808080u;
-      const uint32_t mh = w & 0xF0F0F0F0u;
-      alo = __ffma2_rn(f2(__uint_as_float(__byte_perm(ml, C, 0x7054u)), __uint_as_float(__byte_perm(ml, C, 0x7154u))),
-                       f2(xl.x, xl.y), alo);
-      alo = __ffma2_rn(f2(__uint_as_float(__byte_perm(ml, C, 0x7254u)), __uint_as_float(__byte_perm(ml, C, 0x7354u))),
-                       f2(xl.z, xl.w), alo);
-      ahi = __ffma2_rn(f2(__uint_as_float(__byte_perm(mh, C, 0x7604u)), __uint_as_float(__byte_perm(mh, C, 0x7614u))),
-                       f2(xh.x, xh.y), ahi);
-      ahi = __ffma2_rn(f2(__uint_as_float(__byte_perm(mh, C, 0x7624u)), __uint_as_float(__byte_perm(mh, C, 0x7634u))),
-                       f2(xh.z, xh.w), ahi);
-    }
-    const uint32_t scw = g < 2 ? sc03 : sc47, mnw = g < 2 ? mn03 : mn47;
-    const int b0 = (2 * g) & 3;
-    const float sc_lo = (float)((scw >> (8 * b0)) & 0xFFu), sc_hi = (float)((scw >> (8 * b0 + 8)) & 0xFFu);
-    const float mn_lo = (float)((mnw >> (8 * b0)) & 0xFFu), mn_hi = (float)((mnw >> (8 * b0 + 8)) & 0xFFu);
-    // sum_i (d*sc*q_i - dmin*m) x_i over both sub-blocks of the group
-    float v = (dlo * sc_lo) * (alo.x + alo.y);
-    v = fmaf(dhi * sc_hi, ahi.x + ahi.y, v);
-    v = fmaf(-dmin, fmaf(mn_lo, xs_lo, mn_hi * xs_hi), v);
-    add_row<PR>(acc, rr, v);
-  }
-}
-
-// ---------------------------------------------------------------- Q8_0
-// [fp16 d][int8 q x32]: 34 bytes, so a block starts on a 2-byte boundary.
-// Codes become 2^23 + (q+128) exactly; one packed subtraction restores q.
-__device__ __forceinline__ void block_q8_0(const uint8_t* blk, int col, const float* xs, float& acc) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
-  const uint8_t* b4 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
-  const uint32_t sh = (uint32_t)(a & 3u);  // 0 or 2
-  uint32_t w[9];
-#pragma unroll
-  for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 4 * i);
-  const float d = f16_bits_to_f32((uint16_t)(sh ? (w[0] >> 16) : (w[0] & 0xFFFFu)));
-  float2 s = f2(0.f, 0.f);
-  const float2 nb = f2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    // quants start at byte 2 + sh of b4: a 16- or 32-bit clamped funnel shift
-    const uint32_t m = __funnelshift_rc(w[k], w[k + 1], 16u + 8u * sh) ^ 0x80808080u;
-    const float4 xv = lds_f4(xs + col + 4 * k);
-    const float2 q01 = __fadd2_rn(f2(f_magic23(m, 0), f_magic23(m, 1)), nb);
-    const float2 q23 = __fadd2_rn(f2(f_magic23(m, 2), f_magic23(m, 3)), nb);
-    s = __ffma2_rn(q01, f2(xv.x, xv.y), s);
-    s = __ffma2_rn(q23, f2(xv.z, xv.w), s);
-  }
-  acc = fmaf(s.x + s.y, d, acc);  // fma(sum, d, acc) as Q8_0FloatTensor.kt:77
-}
-
-// ---------------------------------------------------------------- Q6_K
-// [ql 128][qh 64][int8 sc 16][fp16 d]: 210 bytes, 2-byte aligned starts.
-// Half h (128 weights): for 16-byte column c and word k, qlA = ql[64h+16c+4k..],
-// qlB = ql[64h+32+16c+4k..], qh = qh[32h+16c+4k..] give the codes of weights
-// 128h + 32*sub + 16c + 4k + (0..3), sub = 0..3 (Q6_KFloatTensor.kt:163-178).
-template <int PR>
-__device__ __forceinline__ void block_q6k(const uint8_t* blk, int e0, int cols, const float* xs,
-                                          const float* xsum16, float (&acc)[PR]) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
-  const uint8_t* b4 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
-  const uint32_t sh = 8u * (uint32_t)(a & 3u);  // 0 or 16 bits
-  const float d = f16_bits_to_f32((uint16_t)(__funnelshift_r(lds32(b4 + 208), lds32(b4 + 212), sh) & 0xFFFFu));
-  const uint32_t C = 0x3F800000u;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t qa[8], qb[8], qh[8], w[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 64 * h + 4 * i);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qa[i] = __funnelshift_r(w[i], w[i + 1], sh);
-#pragma unroll
-    for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 64 * h + 32 + 4 * i);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qb[i] = __funnelshift_r(w[i], w[i + 1], sh);
-#pragma unroll
-    for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 128 + 32 * h + 4 * i);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qh[i] = __funnelshift_r(w[i], w[i + 1], sh);
-    const uint32_t s0 = lds32(b4 + 192 + 8 * h), s1 = lds32(b4 + 196 + 8 * h), s2 = lds32(b4 + 200 + 8 * h);
-    const uint32_t scw0 = __funnelshift_r(s0, s1, sh);  // sc[8h + 0..3]
-    const uint32_t scw1 = __funnelshift_r(s1, s2, sh);  // sc[8h + 4..7]
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int ebase = e0 + 128 * h + 16 * c;
-      float2 a4[4];
-      float xsum[4];
-#pragma unroll
-      for (int sub = 0; sub < 4; ++sub) {
-        const int e = ebase + 32 * sub;
-        xsum[sub] = xsum16[(PR == 1 ? e : e % cols) / 16];
-        a4[sub] = f2(-xsum[sub], 0.f);  // ends at sum(q6 x)/128
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t la = qa[4 * c + k], lb = qb[4 * c + k], hh = qh[4 * c + k];
-        uint32_t m[4];
-        m[0] = ((la & 0x0F0F0F0Fu) | 0x80808080u) | ((hh << 4) & 0x30303030u);
-        m[1] = ((lb & 0x0F0F0F0Fu) | 0x80808080u) | ((hh << 2) & 0x30303030u);
-        m[2] = (((la >> 4) & 0x0F0F0F0Fu) | 0x80808080u) | (hh & 0x30303030u);
-        m[3] = (((lb >> 4) & 0x0F0F0F0Fu) | 0x80808080u) | ((hh >> 2) & 0x30303030u);
-#pragma unroll
-        for (int sub = 0; sub < 4; ++sub) {
-          const int e = ebase + 32 * sub + 4 * k;
-          const float4 xv = lds_f4(xs + (PR == 1 ? e : e % cols));
-          a4[sub] = __ffma2_rn(f2(__uint_as_float(__byte_perm(m[sub], C, 0x7054u)),
-                                  __uint_as_float(__byte_perm(m[sub], C, 0x7154u))), f2(xv.x, xv.y), a4[sub]);
-          a4[sub] = __ffma2_rn(f2(__uint_as_float(__byte_perm(m[sub], C, 0x7254u)),
-                                  __uint_as_float(__byte_perm(m[sub], C, 0x7354u))), f2(xv.z, xv.w), a4[sub]);
-        }
-      }
-#pragma unroll
-      for (int sub = 0; sub < 4; ++sub) {
-        const int e = ebase + 32 * sub;
-        const int rr = PR == 1 ? 0 : e / cols;
-        // sc index 8h + 2*sub + c (Q6_KFloatTensor.kt:70)
-        const int si = 2 * sub + c;
-        const int8_t sc = (int8_t)((((si >> 2) ? scw1 : scw0) >> (8 * (si & 3))) & 0xFFu);
-        // sum (q6 - 32) x = 128 * sum(q6 x)/128 - 32 * sum x
-        const float v = (d * (float)sc) * fmaf(128.f, a4[sub].x + a4[sub].y, -32.f * xsum[sub]);
-        add_row<PR>(acc, rr, v);
-      }
-    }
   }
 }
 
