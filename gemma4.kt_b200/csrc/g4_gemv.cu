@@ -167,9 +167,14 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
   int g = g_first, c = c_first;  // consume pointer
   long long rs_c = row_start(g);
   bool have_row = row_ok(g);
+  int slot = 0;
+  uint32_t phase = 0;  // slot = i % NS and phase = (i / NS) & 1, kept incrementally
   for (int i = 0; valid(g, c); ++i) {
-    const int slot = i % NS;
-    if (!mbar_wait_bounded(&mybars[slot], (i / NS) & 1)) {
+    if (i > 0 && ++slot == NS) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    if (!mbar_wait_bounded(&mybars[slot], phase)) {
       record_error(a.status, ERR_TIMEOUT_FULL);
       ok = false;
       consumed = i;
@@ -178,7 +183,7 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
     // ---- compute on this lane's share of its row segment
     if (have_row) {
       const long long start = rs_c + c * chunk_bytes;
-      const int nb = (int)(min(chunk_bytes, vrow_bytes - c * chunk_bytes) / TS);
+      const int nb = min(cb, bpv - c * cb);  // blocks (elements for BF16 / F32) in this chunk
       const uint8_t* base = myring + (size_t)slot * stage_bytes + (size_t)rs * p.pitch + (start & 15);
       const int e0 = c * cb * BS;  // first element of the chunk within the virtual row
       if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) {
