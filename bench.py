@@ -110,6 +110,9 @@ class ClockSampler:
 
 
 def make_cases(seed: int = 1):
+    import __graft_entry__
+
+    __graft_entry__.load_package()  # registers the package (its directory name holds a dot); no GPU library
     from gemma4_kt_b200 import synth
 
     cases = []
