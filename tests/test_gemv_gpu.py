@@ -214,3 +214,21 @@ def test_more_formats_gemv_vs_oracle(g4, ctx, name):
     off = 100 * cols
     y2, _ = run_gemv(g4, ctx, MORE[name], raw, x, 300, cols, off=off)
     assert rel_l2(y2, oracle.matmul(MORE[name], raw, x, 300, cols, this_offset=off)) < TOL
+
+
+@pytest.mark.parametrize("name", ["Q8_0", "Q4_K", "Q6_K"])
+def test_int16_activation_precision(g4, ctx, name):
+    """The quantized formats multiply int16 activations (per 32 columns, power-of-two
+    scales).  With an outlier inside a block, an all-zero block and a block of tiny
+    values the rounding stays near 6e-5 relative L2 (numpy restatement of the rule);
+    the bound leaves a 4x margin and is 4x tighter than the general tolerance."""
+    from gemma4_kt_b200 import synth
+
+    rows, cols = 2048, 1536
+    raw, x = synth.gemv_case(T[name], rows, cols, seed=6)
+    x = x.copy()
+    x[5], x[700] = 40.0, -25.0  # outliers set their blocks' scales
+    x[64:96] = 0.0  # all-zero block
+    x[256:288] *= 1e-20  # tiny values: their own small scale
+    y, _ = run_gemv(g4, ctx, T[name], raw, x, rows, cols)
+    assert rel_l2(y, oracle.matmul(T[name], raw, x, rows, cols)) < 2.5e-4
