@@ -1,5 +1,5 @@
 // g4_common.cuh -- sm_100a building blocks shared by the gemma4.kt B200 kernels:
-// mbarrier + cp.async.bulk (TMA, non-tensor, no multicast) staging, bounded
+// mbarrier + cp.async.bulk (TMA, non-tensor, one CTA) staging, bounded
 // waits that report a timeout instead of hanging, and GGML block constants.
 #pragma once
 
@@ -82,7 +82,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// 1-D bulk copy global -> shared (cp.async.bulk, no multicast).  dst, src and
+// 1-D bulk copy global -> shared (cp.async.bulk into this CTA).  dst, src and
 // bytes must all be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -8,7 +8,7 @@
 //  * Persistent CTAs, sized so that every SM gets one.  Each warp owns row
 //    groups of 32/LPR virtual rows (LPR lanes share a row) and streams their
 //    segments through its own ring of shared-memory stages: one cp.async.bulk
-//    (no multicast) per row segment, one mbarrier per stage.  The weights keep
+//    (into this CTA only) per row segment, one mbarrier per stage.  The weights keep
 //    their on-disk layout; unaligned block strides (34 B, 210 B) are handled by
 //    copying the 16-byte-aligned superset of each segment and decoding at a
 //    byte offset.  Few row groups: one CTA per group, its warps split the row.
