@@ -37,10 +37,15 @@ sys.path.insert(0, str(ROOT))
 SHAPES = [(1536, 1536), (6144, 1536), (1536, 6144), (262144, 1536)]
 FORMATS = [("Q8_0", 8), ("Q4_K", 12), ("Q6_K", 14), ("BF16", 30)]
 METRIC = "quant GEMV HBM GB/s"
+# Arithmetic of the sweep's kernels: Q8_0 / Q4_K / Q6_K multiply the stored
+# integer codes by int16 activations (x rounded per 32 columns to a power-of-two
+# scale) into exact int32 sums, scaled and accumulated in fp32; BF16 widens the
+# weights to fp32 and uses fp32 fma.
+DTYPE = "i16 activations x int codes -> i32, f32 accumulate (Q8_0/Q4_K/Q6_K); f32 fma on widened bf16 (BF16)"
 FALLBACK_TFLOPS = 1590.0
 FALLBACK_HBM = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
-# (profiles/gemv_rows_bf16_262144x1536.md, profiles/gemv_rows_q4k_262144x1536.md)
+# dram__bytes_read.sum + dram__bytes_write.sum per launch, from one ncu capture
+# of each kernel (one launch, --clock-control none) of this build
 MEASURED_TRAFFIC = {"BF16 262144x1536": 810.7e6, "Q4_K 262144x1536": 235.0e6}
 
 
@@ -402,7 +407,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (u8/bf16 weight blocks)", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
             "config": {"workload": "C2 quantized GEMV sweep: 4 shapes x {Q8_0,Q4_K,Q6_K,BF16}, batch 1, seed 1",
                        "shapes": [f"{r}x{c}" for r, c in SHAPES], "bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2 (1.9 GB streamed per step)",

@@ -46,6 +46,8 @@ SIGNATURES = {
     "g4_moe_layer_ep": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "g4_dist_unique_id": (_i, [_vp]),
     "g4_dist_init": (_i, [_vp, _i, _i, _vp]),
+    "g4_dist_init_timeout": (_i, [_vp, _i, _i, _vp, _i]),
+    "g4_dist_abort": (_i, [_vp]),
     "g4_dist_rank": (_i, [_vp]),
     "g4_dist_world": (_i, [_vp]),
     "g4_matmul_sharded": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),

@@ -7,8 +7,12 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <time.h>
+#include <unistd.h>
+
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -170,6 +174,11 @@ int g4_init(int device, g4_ctx** out) {
     cudaGetLastError();
     c->status_host = nullptr;  // check_status falls back to a blocking copy
   }
+  // Bring the allocation-free MoE entry point's fixed array into being now,
+  // while the device still has room: under lazy module loading it would
+  // otherwise appear at its first use, after a host may have reserved the
+  // remaining HBM.  A failure here is reported by that entry point later.
+  noalloc_prepare_device(device);
   *out = c;
   return 0;
 }
@@ -355,7 +364,9 @@ int g4_sync(g4_ctx* c, void* stream) {
 struct NcclApi {
   bool loaded = false;
   ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*commInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
@@ -382,7 +393,9 @@ static bool load_nccl(char* err, size_t n) {
     return false;                                             \
   }
   G4_SYM(getUniqueId, "ncclGetUniqueId")
-  G4_SYM(commInitRank, "ncclCommInitRank")
+  G4_SYM(commInitRankConfig, "ncclCommInitRankConfig")
+  G4_SYM(commGetAsyncError, "ncclCommGetAsyncError")
+  G4_SYM(commAbort, "ncclCommAbort")
   G4_SYM(commDestroy, "ncclCommDestroy")
   G4_SYM(allGather, "ncclAllGather")
   G4_SYM(send, "ncclSend")
@@ -409,26 +422,90 @@ int g4_dist_unique_id(void* id_out) {
   return 0;
 }
 
-int g4_dist_init(g4_ctx* c, int rank, int world, const void* id) {
+static long long now_ms() {
+  struct timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (long long)ts.tv_sec * 1000 + ts.tv_nsec / 1000000;
+}
+
+// Default bound on g4_dist_init: G4_DIST_TIMEOUT_MS, else 120 s.
+static int default_dist_timeout_ms() {
+  const char* v = getenv("G4_DIST_TIMEOUT_MS");
+  const int t = v && *v ? atoi(v) : 0;
+  return t > 0 ? t : 120000;
+}
+
+// The communicator is non-blocking: a call may return ncclInProgress while
+// NCCL finishes it in the background.  Poll its state until it settles or the
+// deadline passes; on expiry (or any error) abort the communicator so no rank
+// is left waiting on it, and report G4_E_DIST.
+static int nccl_settle(g4_ctx* c, ncclComm_t comm, ncclResult_t r, long long deadline_ms, const char* what) {
+  while (r == ncclInProgress) {
+    if (now_ms() > deadline_ms) {
+      g_nccl.commAbort(comm);
+      if (c->comm == (void*)comm) {
+        c->comm = nullptr;
+        c->rank = 0;
+        c->world = 1;
+      }
+      c->set_err("%s: timed out (a peer rank did not answer); communicator aborted", what);
+      return G4_E_DIST;
+    }
+    usleep(200);
+    if (g_nccl.commGetAsyncError(comm, &r) != ncclSuccess) r = ncclSystemError;
+  }
+  if (r != ncclSuccess) {
+    g_nccl.commAbort(comm);
+    if (c->comm == (void*)comm) {
+      c->comm = nullptr;
+      c->rank = 0;
+      c->world = 1;
+    }
+    c->set_err("%s: %s; communicator aborted", what, g_nccl.errStr(r));
+    return G4_E_DIST;
+  }
+  return 0;
+}
+
+int g4_dist_init_timeout(g4_ctx* c, int rank, int world, const void* id, int timeout_ms) {
   if (!c) return G4_E_ARG;
-  if (!id || world < 1 || rank < 0 || rank >= world) {
-    c->set_err("g4_dist_init: bad rank %d / world %d", rank, world);
+  if (!id || world < 1 || rank < 0 || rank >= world || timeout_ms <= 0) {
+    c->set_err("g4_dist_init: bad rank %d / world %d / timeout %d ms", rank, world, timeout_ms);
     return G4_E_ARG;
   }
   if (!load_nccl(c->err, sizeof c->err)) return G4_E_DIST;
   if (int r = c->bind()) return r;
   g4_dist_teardown(c);
+  c->dist_timeout_ms = timeout_ms;
   ncclUniqueId uid;
   memcpy(&uid, id, sizeof uid);
   ncclComm_t comm = nullptr;
-  ncclResult_t r = g_nccl.commInitRank(&comm, world, uid, rank);
-  if (r != ncclSuccess) {
-    c->set_err("ncclCommInitRank: %s", g_nccl.errStr(r));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  const long long deadline = now_ms() + timeout_ms;
+  ncclResult_t r = g_nccl.commInitRankConfig(&comm, world, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    if (comm) g_nccl.commAbort(comm);
+    c->set_err("ncclCommInitRankConfig: %s", g_nccl.errStr(r));
     return G4_E_DIST;
   }
+  if (int e = nccl_settle(c, comm, r, deadline, "ncclCommInitRankConfig")) return e;
   c->comm = comm;
   c->rank = rank;
   c->world = world;
+  return 0;
+}
+
+int g4_dist_init(g4_ctx* c, int rank, int world, const void* id) {
+  return g4_dist_init_timeout(c, rank, world, id, default_dist_timeout_ms());
+}
+
+int g4_dist_abort(g4_ctx* c) {
+  if (!c) return G4_E_ARG;
+  if (c->comm && g_nccl.loaded) g_nccl.commAbort((ncclComm_t)c->comm);
+  c->comm = nullptr;
+  c->rank = 0;
+  c->world = 1;
   return 0;
 }
 
@@ -451,11 +528,7 @@ int g4_matmul_sharded(g4_ctx* c, const g4_tensor* w, const float* x, float* y, i
   int r = g4_matmul(c, w, 0, x, my, local, cols, stream);
   if (r || world == 1) return r;
   ncclResult_t nr = g_nccl.allGather(my, y, (size_t)local, ncclFloat32, (ncclComm_t)c->comm, (cudaStream_t)stream);
-  if (nr != ncclSuccess) {
-    c->set_err("ncclAllGather: %s", g_nccl.errStr(nr));
-    return G4_E_DIST;
-  }
-  return 0;
+  return nccl_settle(c, (ncclComm_t)c->comm, nr, now_ms() + c->dist_timeout_ms, "ncclAllGather");
 }
 
 }  // extern "C"
@@ -475,11 +548,7 @@ int g4_nccl_allgather_i32(g4_ctx* c, const int32_t* send, int32_t* recv, size_t 
     return G4_E_DIST;
   }
   const ncclResult_t r = g_nccl.allGather(send, recv, count, ncclInt32, (ncclComm_t)c->comm, st);
-  if (r != ncclSuccess) {
-    c->set_err("ncclAllGather: %s", g_nccl.errStr(r));
-    return G4_E_DIST;
-  }
-  return 0;
+  return nccl_settle(c, (ncclComm_t)c->comm, r, now_ms() + c->dist_timeout_ms, "ncclAllGather");
 }
 
 int g4_nccl_alltoallv(g4_ctx* c, const void* send, const size_t* soff, const size_t* slen, void* recv,
@@ -495,9 +564,38 @@ int g4_nccl_alltoallv(g4_ctx* c, const void* send, const size_t* soff, const siz
     if (r == ncclSuccess && rlen[p]) r = g_nccl.recv((uint8_t*)recv + roff[p], rlen[p], ncclUint8, p, comm, st);
   }
   const ncclResult_t r2 = g_nccl.groupEnd();
-  if (r != ncclSuccess || r2 != ncclSuccess) {
-    c->set_err("NCCL send/recv group: %s", g_nccl.errStr(r != ncclSuccess ? r : r2));
+  if (r != ncclSuccess && r != ncclInProgress) {
+    c->set_err("NCCL send/recv group: %s", g_nccl.errStr(r));
     return G4_E_DIST;
   }
-  return 0;
+  return nccl_settle(c, comm, r2, now_ms() + c->dist_timeout_ms, "NCCL send/recv group");
+}
+
+// Wait for the work queued on `st` (collectives included) with the context's
+// distributed timeout: polls the stream and the communicator's asynchronous
+// error instead of blocking in cudaStreamSynchronize, so a peer that stopped
+// answering ends in G4_E_DIST (communicator aborted) rather than a hung host.
+int g4_dist_stream_wait(g4_ctx* c, cudaStream_t st) {
+  const long long deadline = now_ms() + c->dist_timeout_ms;
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) return 0;
+    if (q != cudaErrorNotReady) return c->cuda_fail(q, "stream wait");
+    if (c->comm) {
+      ncclResult_t ar = ncclSuccess;
+      if (g_nccl.commGetAsyncError((ncclComm_t)c->comm, &ar) != ncclSuccess) ar = ncclSystemError;
+      if (ar != ncclSuccess && ar != ncclInProgress)
+        return nccl_settle(c, (ncclComm_t)c->comm, ar, deadline, "collective");
+    }
+    if (now_ms() > deadline) {
+      if (c->comm) g_nccl.commAbort((ncclComm_t)c->comm);
+      c->comm = nullptr;
+      c->rank = 0;
+      c->world = 1;
+      c->set_err("collective did not complete within %d ms (a peer rank stopped answering); communicator aborted",
+                 c->dist_timeout_ms);
+      return G4_E_DIST;
+    }
+    usleep(50);
+  }
 }

@@ -29,6 +29,7 @@ struct g4_ctx {
   void* comm = nullptr;        // ncclComm_t when g4_dist_init has run
   int rank = 0;
   int world = 1;
+  int dist_timeout_ms = 120000;  // bound on waits for peer ranks (g4_dist_init_timeout)
   char err[512] = {0};
   // launch plans, keyed by (type, offset, rows, cols, x 16B-aligned)
   std::map<std::tuple<int, long long, int, int, int>, g4::GemvPlan> gemv_plans;
@@ -61,3 +62,6 @@ void g4_dist_teardown(g4_ctx* c);
 int g4_nccl_allgather_i32(g4_ctx* c, const int32_t* send, int32_t* recv, size_t count, cudaStream_t st);
 int g4_nccl_alltoallv(g4_ctx* c, const void* send, const size_t* soff, const size_t* slen, void* recv,
                       const size_t* roff, const size_t* rlen, cudaStream_t st);
+// Wait for the stream's work within the context's distributed timeout (polls
+// the stream and the communicator's error state; aborts it on expiry).
+int g4_dist_stream_wait(g4_ctx* c, cudaStream_t st);

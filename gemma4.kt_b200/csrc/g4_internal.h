@@ -20,5 +20,8 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
 int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, unsigned* status,
                 cudaStream_t st);
 int launch_dequant(int type, const uint8_t* w, long long off, long long n, float* out, cudaStream_t st);
+// Resolve the fixed work array of g4_moe_layer_noalloc on `device` (which must
+// be current); returns a cudaError_t (0 on success).
+int noalloc_prepare_device(int device);
 
 }  // namespace g4

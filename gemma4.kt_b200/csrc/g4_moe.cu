@@ -1700,18 +1700,25 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   ExpertFn fn = select_expert(type, gu, a.pr, nb);
   if (!fn) return -1;
   size_t smem = 64 + 4 * (2 * kMaxExperts + 8) + 128 + (size_t)a.nstages * a.stage_bytes;
-  // kernel attributes and occupancy are queried once per (kernel, smem)
-  static std::map<std::pair<ExpertFn, size_t>, int> occ_cache;
-  auto key = std::make_pair(fn, smem);
-  auto itc = occ_cache.find(key);
-  if (itc == occ_cache.end()) {
-    // per-kernel attribute: allow the device maximum, not just this launch's size
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->dev.smem_optin);
-    int o = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, 32 * (NCW + 1), smem);
-    itc = occ_cache.emplace(key, o < 1 ? 1 : o).first;
+  // kernel attributes and occupancy are queried once per (device, kernel, smem):
+  // the shared-memory attribute is a per-device setting of the kernel
+  static std::mutex occ_mu;
+  static std::map<std::tuple<int, ExpertFn, size_t>, int> occ_cache;
+  int occ = 1;
+  {
+    std::lock_guard<std::mutex> lk(occ_mu);
+    auto key = std::make_tuple(c->dev.device, fn, smem);
+    auto itc = occ_cache.find(key);
+    if (itc == occ_cache.end()) {
+      // per-kernel attribute: allow the device maximum, not just this launch's size
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->dev.smem_optin);
+      int o = 1;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, 32 * (NCW + 1), smem);
+      cudaGetLastError();
+      itc = occ_cache.emplace(key, o < 1 ? 1 : o).first;
+    }
+    occ = itc->second;
   }
-  int occ = itc->second;
   // Upper bound on items: every slot in its own chunk.
   long long max_items = (long long)std::min(T * K, E * ((T * K + nb - 1) / nb + 1)) * a.tiles_e;
   int grid = (int)std::min<long long>(max_items, (long long)c->dev.sms * occ);
@@ -2362,19 +2369,24 @@ static bool dec_plan(const g4_ctx* c, int type, bool gu, int E, int K, int dim, 
 // CTAs per SM of the decode kernels (512 / this many threads each)
 constexpr int kDecCtasPerSm = 1;
 
-// Fixed table of decode kernels whose shared-memory limit was raised (no heap use).
-static bool dec_prepare(DecFn fn, int optin) {
+// Fixed table of (device, decode kernel) pairs whose shared-memory limit was
+// raised (no heap use; the attribute is set per device).
+static bool dec_prepare(DecFn fn, int optin, int device) {
   static std::mutex mu;
-  static DecFn done[32];
+  struct Done {
+    DecFn fn;
+    int device;
+  };
+  static Done done[64];
   static int n = 0;
   std::lock_guard<std::mutex> lk(mu);
   for (int i = 0; i < n; ++i)
-    if (done[i] == fn) return true;
+    if (done[i].fn == fn && done[i].device == device) return true;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
-  if (n < 32) done[n++] = fn;
+  if (n < 64) done[n++] = Done{fn, device};
   return true;
 }
 
@@ -2404,7 +2416,7 @@ static int launch_dec_pair(g4_ctx* c, const g4_moe_weights* w, const MoeScratch&
   const DecFn gf = dec_fn(w->gate_up_exps->type, true, 1, T), df = dec_fn(w->down_exps->type, false, dpr, T);
   if (!gf || !df) return -1;
   const int optin = (int)c->dev.smem_optin;
-  if (!dec_prepare(gf, optin) || !dec_prepare(df, optin)) return -1;
+  if (!dec_prepare(gf, optin, c->dev.device) || !dec_prepare(df, optin, c->dev.device)) return -1;
   ga.w = (const uint8_t*)w->gate_up_exps->d;
   ga.act = m.moe_in;
   ga.act_s16 = m.moe_in_s16;
@@ -2435,12 +2447,19 @@ static int tensor_ok(const g4_tensor* t, int type, uint64_t n) {
 
 static int rows_occ_fixed(RowsFn fn, size_t smem, int threads, int optin);
 
+// Kernel set-up per (device, kernel, smem): the shared-memory attribute is a
+// per-device setting, so a process using several devices sets it on each.
 static int rows_occ(RowsFn fn, size_t smem, int threads, int optin, bool noalloc_path) {
   if (noalloc_path) return rows_occ_fixed(fn, smem, threads, optin);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
   static std::mutex mu;
-  static std::map<std::pair<RowsFn, size_t>, int> cache;
+  static std::map<std::tuple<int, RowsFn, size_t>, int> cache;
   std::lock_guard<std::mutex> lk(mu);
-  auto key = std::make_pair(fn, smem);
+  auto key = std::make_tuple(device, fn, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   int o = 0;
@@ -2453,26 +2472,32 @@ static int rows_occ(RowsFn fn, size_t smem, int threads, int optin, bool noalloc
   return o;
 }
 
-// fixed table for the no-alloc path (no heap use)
+// fixed table for the no-alloc path (no heap use), keyed by device as well
 static int rows_occ_fixed(RowsFn fn, size_t smem, int threads, int optin) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
   static std::mutex mu;
   struct E {
     RowsFn fn;
     size_t smem;
+    int device;
     int occ;
   };
-  static E tab[64];
+  static E tab[128];
   static int n = 0;
   std::lock_guard<std::mutex> lk(mu);
   for (int i = 0; i < n; ++i)
-    if (tab[i].fn == fn && tab[i].smem == smem) return tab[i].occ;
+    if (tab[i].fn == fn && tab[i].smem == smem && tab[i].device == device) return tab[i].occ;
   int o = 0;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, threads, smem) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
-  if (n < 64) tab[n++] = E{fn, smem, o};
+  if (n < 128) tab[n++] = E{fn, smem, device, o};
   return o;
 }
 
@@ -2737,8 +2762,9 @@ extern "C" int g4_moe_layer_ep(g4_ctx* c, const g4_moe_weights* w, const float* 
     return G4_E_NOMEM;
   }
   e = cudaMemcpyAsync(h_off, off_all, (size_t)world * (world + 1) * 4, cudaMemcpyDeviceToHost, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return c->cuda_fail(e, "g4_moe_layer_ep count exchange");
+  // bounded wait: a peer that stopped answering ends in G4_E_DIST, not a hung host
+  if (int r = g4_dist_stream_wait(c, st)) return r;
   std::vector<size_t> s_off(world), s_len(world), r_off(world), r_len(world);
   size_t R = 0;
   for (int p = 0; p < world; ++p) {
@@ -2831,14 +2857,16 @@ void* g_noalloc_ptr[kNoallocMaxDevices];  // device address of the array, per de
 struct FixedOcc {
   ExpertFn fn;
   size_t smem;
+  int device;
   int occ;
 };
-FixedOcc g_noalloc_occ[64];  // kernel set-up done by the no-alloc path (fixed table, no heap)
+FixedOcc g_noalloc_occ[128];  // kernel set-up done by the no-alloc path per device (fixed table, no heap)
 int g_noalloc_occ_n = 0;
 
-// Device address of the scratch array on the current device.  The first call
-// per device resolves it (cudaGetSymbolAddress); the symbol's host-side name is
-// only a stand-in and must never be passed to a kernel.
+// Device address of the scratch array on the current device.  It is resolved
+// (cudaGetSymbolAddress) once per device, normally by g4_init through
+// noalloc_prepare_device; the symbol's host-side name is only a stand-in and
+// must never be passed to a kernel.
 int noalloc_scratch(g4_ctx* c, uint8_t** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   const int d = c->dev.device;
@@ -2855,23 +2883,44 @@ int noalloc_scratch(g4_ctx* c, uint8_t** out) {
   *out = static_cast<uint8_t*>(g_noalloc_ptr[d]);
   return 0;
 }
+}  // namespace
+
+// Resolve the no-alloc array on `device` (current).  Under lazy module
+// loading (CUDA's default) the array only comes into being when this
+// translation unit's module is loaded on the device; resolving its address
+// loads the module, so g4_init calls this before the host can hand the free
+// HBM to a pool of its own.  Returns the cudaError_t of the lookup.
+int noalloc_prepare_device(int device) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (device < 0 || device >= kNoallocMaxDevices) return (int)cudaErrorInvalidDevice;
+  if (g_noalloc_ptr[device]) return 0;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();
+    return (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+  }
+  g_noalloc_ptr[device] = p;
+  return 0;
+}
+
+namespace {
 
 int noalloc_occ(ExpertFn fn, size_t smem, int threads, int* occ) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  int dev = 0, optin = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   for (int i = 0; i < g_noalloc_occ_n; ++i)
-    if (g_noalloc_occ[i].fn == fn && g_noalloc_occ[i].smem == smem) {
+    if (g_noalloc_occ[i].fn == fn && g_noalloc_occ[i].smem == smem && g_noalloc_occ[i].device == dev) {
       *occ = g_noalloc_occ[i].occ;
       return 0;
     }
-  int dev = 0, optin = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-    return -1;
+  if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return -1;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess) return -1;
   int o = 1;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, threads, smem) != cudaSuccess) return -1;
   if (o < 1) o = 1;
-  if (g_noalloc_occ_n < 64) g_noalloc_occ[g_noalloc_occ_n++] = FixedOcc{fn, smem, o};
+  if (g_noalloc_occ_n < 128) g_noalloc_occ[g_noalloc_occ_n++] = FixedOcc{fn, smem, dev, o};
   *occ = o;
   return 0;
 }

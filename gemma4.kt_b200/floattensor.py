@@ -132,12 +132,22 @@ class Context:
             raise G4Error(f"g4_dist_unique_id failed ({rc})")
         return bytes(uid)
 
-    def dist_init(self, rank: int, world: int, uid: bytes) -> None:
-        """Join the NCCL communicator of `world` GPUs (one Context per GPU)."""
+    def dist_init(self, rank: int, world: int, uid: bytes, timeout_ms: int | None = None) -> None:
+        """Join the NCCL communicator of `world` GPUs (one Context per GPU).
+        Waits on peers are bounded by timeout_ms (default: G4_DIST_TIMEOUT_MS
+        or 120 s); on expiry the communicator is aborted and G4Error raised."""
         if len(uid) != 128:
             raise ValueError("NCCL unique id must be 128 bytes")
         buf = (C.c_ubyte * 128).from_buffer_copy(uid)
-        check(lib().g4_dist_init(self.handle, rank, world, buf), self.handle, "g4_dist_init")
+        if timeout_ms is None:
+            rc = lib().g4_dist_init(self.handle, rank, world, buf)
+        else:
+            rc = lib().g4_dist_init_timeout(self.handle, rank, world, buf, int(timeout_ms))
+        check(rc, self.handle, "g4_dist_init")
+
+    def dist_abort(self) -> None:
+        """Abort this context's communicator (single-GPU calls keep working)."""
+        check(lib().g4_dist_abort(self.handle), self.handle, "g4_dist_abort")
 
 
 class CudaFloatTensor:

@@ -2,9 +2,9 @@
  * g4.h -- C ABI of libg4b200: B200 (sm_100a) kernels for gemma4.kt's two hot
  * paths, the quantized matrix-vector product and the mixture-of-experts layer.
  *
- * The Kotlin host binds these with java.lang.foreign (FFM) downcalls; see
- * INTEGRATION.md.  Every reference interface below is cited by its file:line
- * under lib/src/main/kotlin/io/github/lbenedetto/internal/.
+ * The Kotlin host binds these with java.lang.foreign (FFM) downcalls.  Every
+ * reference interface below is cited by its file:line under
+ * lib/src/main/kotlin/io/github/lbenedetto/internal/.
  *
  * Conventions
  *  - Every entry point returns 0 on success and a negative G4_E* code on
@@ -155,14 +155,17 @@ int g4_moe_layer_host(g4_ctx *ctx, const g4_moe_weights *w, const float *x_host,
  * loop that must not stall on the device-wide synchronisation a cudaMalloc or
  * cudaFree can cause.  Same kernels and results as g4_moe_layer; the work
  * buffers live in one fixed array of G4_MOE_NOALLOC_SCRATCH_BYTES bytes that
- * the library image reserves on every GPU that loads it, held until exit.
+ * the library image reserves on every GPU it is used on, held until exit.
  *  - A call needs 4*n_tokens*(2*dim + dim/16 + n_expert + 3*n_used
  *    + n_used*(ff + ff/16 + dim)) + 4*(n_expert + 1) bytes (each buffer rounded
  *    up to 256 bytes; about 138 KB per token for dim 2816, 128 experts, top-8,
  *    ff 704, so up to 60 tokens).  Larger
  *    batches are rejected with G4_E_ARG and a message; split them.
- *  - The first call on a device resolves the array's device address; make it
- *    before any stream capture.
+ *  - g4_init creates the array on its device and resolves its address (under
+ *    CUDA's lazy module loading it would otherwise only appear at first use):
+ *    create the context before the host reserves the free HBM for its own
+ *    pool.  If that failed, the first call on the device retries it; make
+ *    that call before any stream capture.
  *  - All calls on a device share the array: calls that can overlap on the GPU
  *    (different streams, or several contexts on one device) race.  Nothing in
  *    it needs to start at zero: each call writes every buffer before reading.
@@ -194,7 +197,17 @@ int g4_moe_topk(g4_ctx *ctx, const float *logits_dev, int n_tokens, int n_expert
  * No reference counterpart: the reference is single-process (no distributed code). */
 #define G4_NCCL_ID_BYTES 128
 int g4_dist_unique_id(void *id_out /* G4_NCCL_ID_BYTES */);
+/* Join the communicator of `world` ranks.  The communicator is created
+ * non-blocking and every wait on peers is bounded: if the other ranks do not
+ * all join within timeout_ms, or a later collective of this context does not
+ * complete within it, the communicator is aborted and the call returns
+ * G4_E_DIST (the context is then single-rank again).  g4_dist_init uses the
+ * G4_DIST_TIMEOUT_MS environment variable, else 120 s. */
+int g4_dist_init_timeout(g4_ctx *ctx, int rank, int world, const void *id, int timeout_ms);
 int g4_dist_init(g4_ctx *ctx, int rank, int world, const void *id /* G4_NCCL_ID_BYTES */);
+/* Abort the context's communicator (for a host watchdog that gave up on a
+ * peer); the context stays usable for single-GPU calls. */
+int g4_dist_abort(g4_ctx *ctx);
 int g4_dist_rank(const g4_ctx *ctx);
 int g4_dist_world(const g4_ctx *ctx);
 

@@ -157,3 +157,63 @@ def test_moe_expert_parallel_two_gpus():
             for t in range(out.shape[0]):
                 err = np.linalg.norm(out[t] - ref[t]) / np.linalg.norm(ref[t])
                 assert err < TOL, (r, t, err)
+
+
+def _lonely_rank_main(q):
+    """Rank 0 of a 2-rank communicator whose peer never joins."""
+    import time
+
+    import torch
+
+    from gemma4_kt_b200 import synth
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(0)
+    ctx = g4.Context(0)
+    uid = g4.Context.dist_unique_id()
+    t0 = time.monotonic()
+    msg = ""
+    try:
+        ctx.dist_init(0, 2, uid, timeout_ms=3000)
+        joined = True
+    except g4.G4Error as e:
+        joined, msg = False, str(e)
+    waited = time.monotonic() - t0
+    # the context is single-GPU again and still computes
+    raw, x = synth.gemv_case(g4.GGMLType.Q8_0, 256, 2048, seed=0)
+    w = g4.FloatTensorFactory.create(ctx, g4.GGMLType.Q8_0, raw, 256 * 2048)
+    y = np.zeros(256, dtype=np.float32)
+    w.matmul(x, y, 256, 2048)
+    q.put((joined, msg, waited, y, raw, x))
+    w.free()
+    ctx.close()
+
+
+def test_dist_init_gives_up_when_a_peer_never_joins():
+    """A rank whose peer never joins gets G4_E_DIST after the timeout (the
+    communicator is created non-blocking and aborted on expiry) instead of
+    hanging; the context keeps working on one GPU.  The failure is made on
+    the host (no second rank is started); runs in a child process that is
+    killed if it ever hangs."""
+    if _gpus() < 1:
+        pytest.skip("no CUDA device")
+    import multiprocessing as mp
+
+    from oracle import oracle
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely_rank_main, args=(q,))
+    p.start()
+    try:
+        joined, msg, waited, y, raw, x = q.get(timeout=180)
+    finally:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert p.exitcode == 0
+    assert not joined
+    assert "timed out" in msg and "G4_E_DIST" in msg, msg
+    assert 2.5 < waited < 60, waited
+    ref = oracle.matmul(int(g4.GGMLType.Q8_0), raw, x, 256, 2048)
+    assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < TOL
