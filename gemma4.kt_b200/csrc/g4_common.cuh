@@ -148,4 +148,35 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Sum over the CTA, the same fixed order in every CTA; red holds >= 33 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < nw ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// Llama.gelu (Llama.kt:23-25): double precision, rounded to float.
+__device__ __forceinline__ float gelu_ref(float x) {
+  double xd = (double)x;
+  double inner = 0.7978845608028654 * (xd + 0.044715 * (xd * xd * xd));
+  return (float)(0.5 * xd * (1.0 + tanh(inner)));
+}
+
+// rmsnorm's scale (Llama.kt:28-31): ss / size + eps in float, 1/sqrt in double.
+__device__ __forceinline__ float rms_scale(float ss, int size, float eps) {
+  ss = __fdiv_rn(ss, (float)size);
+  ss = __fadd_rn(ss, eps);
+  return (float)(1.0 / sqrt((double)ss));
+}
+
 }  // namespace g4

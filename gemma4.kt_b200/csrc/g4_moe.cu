@@ -36,29 +36,6 @@ constexpr int kMaxUsed = 16;
 
 // ---------------------------------------------------------------- helpers
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  v = warp_sum(v);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float t = 0.f;
-  if (threadIdx.x < 32) {
-    t = threadIdx.x < nw ? red[threadIdx.x] : 0.f;
-    t = warp_sum(t);
-    if (threadIdx.x == 0) red[32] = t;
-  }
-  __syncthreads();
-  return red[32];
-}
-
-// Llama.gelu (Llama.kt:23-25): double precision, rounded to float.
-__device__ __forceinline__ float gelu_ref(float x) {
-  double xd = (double)x;
-  double inner = 0.7978845608028654 * (xd + 0.044715 * (xd * xd * xd));
-  return (float)(0.5 * xd * (1.0 + tanh(inner)));
-}
-
 // ---------------------------------------------------------------- prep
 
 __global__ void __launch_bounds__(512) moe_prep_kernel(const float* __restrict__ x, const float* __restrict__ pre_norm,
@@ -1480,6 +1457,16 @@ __global__ void __launch_bounds__(512) moe_combine_reg_kernel(const float* __res
 }
 
 // ---------------------------------------------------------------- host side
+// The CUDA error of the last failed expert-kernel launch on this thread (a
+// launcher reads cudaGetLastError(), which clears it; callers report this).
+static thread_local cudaError_t t_launch_err = cudaSuccess;
+static int launch_status() {
+  t_launch_err = cudaGetLastError();
+  return t_launch_err == cudaSuccess ? 0 : -2;
+}
+static cudaError_t last_launch_err() {
+  return t_launch_err != cudaSuccess ? t_launch_err : cudaErrorLaunchFailure;
+}
 
 struct MoeScratch {
   float *moe_in, *xr, *logits, *prob, *G, *D;
@@ -1693,13 +1680,17 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
     a.expert_elems = (long long)dim * ff;
   }
   if (a.expert_elems % BS) return -1;
+  // up to 4 stages, as many as fit in shared memory (wide BF16 / F32 rows take 2)
+  const size_t fixed_smem = 64 + 4 * (2 * kMaxExperts + 8) + 128;
   a.nstages = 4;
+  while (a.nstages > 2 && fixed_smem + (size_t)a.nstages * a.stage_bytes > c->dev.smem_optin) --a.nstages;
+  if (fixed_smem + (size_t)a.nstages * a.stage_bytes > c->dev.smem_optin) return -1;
   // Token chunk: enough slots per expert on average -> wider chunks.
   int avg = (T * K + E - 1) / E;
   int nb = avg >= 8 ? 8 : avg >= 4 ? 4 : avg >= 2 ? 2 : 1;
   ExpertFn fn = select_expert(type, gu, a.pr, nb);
   if (!fn) return -1;
-  size_t smem = 64 + 4 * (2 * kMaxExperts + 8) + 128 + (size_t)a.nstages * a.stage_bytes;
+  size_t smem = fixed_smem + (size_t)a.nstages * a.stage_bytes;
   // kernel attributes and occupancy are queried once per (device, kernel, smem):
   // the shared-memory attribute is a per-device setting of the kernel
   static std::mutex occ_mu;
@@ -1724,7 +1715,7 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   int grid = (int)std::min<long long>(max_items, (long long)c->dev.sms * occ);
   if (grid < 1) grid = 1;
   fn<<<grid, 32 * (NCW + 1), smem, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  return launch_status();
 }
 
 // Q4_K for NB tokens on int16 activations (quantize_x16 layout: xq[j] is token
@@ -2241,12 +2232,15 @@ static int launch_expert_rows(g4_ctx* c, int type, bool gu, const uint8_t* w, co
   RowsFn fn = rows_fn(type, gu, pr, nb);
   if (!fn) return -1;
   const int occ = rows_occ(fn, smem, 32 * warps, optin, noalloc_path);
-  if (occ < 1) return -2;
+  if (occ < 1) {
+    t_launch_err = cudaErrorInvalidConfiguration;
+    return -2;
+  }
   const int grid = split ? (int)max_items
                          : (int)std::max<long long>(1, std::min<long long>((max_items + warps - 1) / warps,
                                                                            (long long)c->dev.sms * occ));
   fn<<<grid, 32 * warps, smem, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  return launch_status();
 }
 
 // ---------------------------------------------------------------- decode launch
@@ -2569,7 +2563,7 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
   }
   if (!done) {
     const int rd = launch_dec_pair(c, w, m, E, K, dim, ff, T, st);
-    if (rd == -2) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer decode launch");
+    if (rd == -2) return c->cuda_fail(last_launch_err(), "g4_moe_layer decode launch");
     done = rd == 0;
   }
   if (!done) {
@@ -2592,7 +2586,7 @@ extern "C" int g4_moe_layer(g4_ctx* c, const g4_moe_weights* w, const float* x, 
       c->set_err("g4_moe_layer: expert tensor layout not supported by the grouped kernels");
       return G4_E_ARG;
     }
-    if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer expert launch");
+    if (r) return c->cuda_fail(last_launch_err(), "g4_moe_layer expert launch");
   }
   if (cudaError_t ce = launch_combine(w, m, out, T, st)) return c->cuda_fail(ce, "g4_moe_layer combine launch");
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
@@ -2971,19 +2965,25 @@ int launch_expert_noalloc(g4_ctx* c, int type, bool gu, const uint8_t* w, const 
     a.expert_elems = (long long)dim * ff;
   }
   if (a.expert_elems % BS) return -1;
+  const size_t fixed_smem = 64 + 4 * (2 * kMaxExperts + 8) + 128;
   a.nstages = 4;
+  while (a.nstages > 2 && fixed_smem + (size_t)a.nstages * a.stage_bytes > c->dev.smem_optin) --a.nstages;
+  if (fixed_smem + (size_t)a.nstages * a.stage_bytes > c->dev.smem_optin) return -1;
   int avg = (T * K + E - 1) / E;
   int nb = avg >= 8 ? 8 : avg >= 4 ? 4 : avg >= 2 ? 2 : 1;
   ExpertFn fn = select_expert(type, gu, a.pr, nb);
   if (!fn) return -1;
-  size_t smem = 64 + 4 * (2 * kMaxExperts + 8) + 128 + (size_t)a.nstages * a.stage_bytes;
+  size_t smem = fixed_smem + (size_t)a.nstages * a.stage_bytes;
   int occ = 1;
-  if (noalloc_occ(fn, smem, 32 * (NCW + 1), &occ)) return -2;
+  if (noalloc_occ(fn, smem, 32 * (NCW + 1), &occ)) {
+    t_launch_err = cudaErrorInvalidConfiguration;
+    return -2;
+  }
   long long max_items = (long long)std::min(T * K, E * ((T * K + nb - 1) / nb + 1)) * a.tiles_e;
   int grid = (int)std::min<long long>(max_items, (long long)c->dev.sms * occ);
   if (grid < 1) grid = 1;
   fn<<<grid, 32 * (NCW + 1), smem, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  return launch_status();
 }
 }  // namespace
 
@@ -3048,7 +3048,7 @@ extern "C" int g4_moe_layer_noalloc(g4_ctx* c, const g4_moe_weights* w, const fl
     c->set_err("g4_moe_layer_noalloc: expert tensor layout not supported by the grouped kernels");
     return G4_E_ARG;
   }
-  if (r) return c->cuda_fail(cudaGetLastError(), "g4_moe_layer_noalloc expert launch");
+  if (r) return c->cuda_fail(last_launch_err(), "g4_moe_layer_noalloc expert launch");
   if (cudaError_t ce = launch_combine(w, m, out, T, st)) return c->cuda_fail(ce, "g4_moe_layer_noalloc combine launch");
   if (topk_idx) cudaMemcpyAsync(topk_idx, m.idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
   if (topk_prob) cudaMemcpyAsync(topk_prob, m.prob, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st);
