@@ -37,11 +37,88 @@ struct GemvArgs {
   const float* x;    // cols floats, 16B aligned
   float* y;          // rows floats
   unsigned* status;  // device error word
+  GemvFuse f;        // fused prologue / epilogue (IN_PLAIN / OUT_PLAIN: none)
 };
+
+// ---------------------------------------------------------------- fused prologue
+// The activation vector of a decoder GEMV, computed by every CTA into xs
+// (shared memory, n floats) from the kernel's inputs; CTA 0 also stores the
+// new residual stream xn to f.x_out.  The arithmetic follows the reference's
+// rounding order per element (Llama.kt:27-37 rmsnorm: w * (s * x);
+// MutableFloatTensor.addInPlace / mapInPlace); sums of squares use a fixed
+// tree instead of the sequential float sum.
+__device__ void fused_prologue(const GemvFuse& f, const float* __restrict__ x, float* xs, float* red, int n) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const bool store = f.x_out != nullptr && blockIdx.x == 0;
+  float ss = 0.f;
+  if (f.in_mode == IN_NORM) {
+    for (int i = tid; i < n; i += nt) {
+      const float v = x[i];
+      xs[i] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  } else if (f.in_mode == IN_EMBED_NORM) {
+    // Llama.kt:112-113: x = tokenEmbeddingTable.get(token * dim + i) * sqrt(dim)
+    const int s = *f.step;
+    int tok = f.in_tok[s];
+    if (tok < 0) tok = *f.next_tok;
+    const long long base = (long long)tok * n;
+    for (int i = tid; i < n; i += nt) {
+      const float v = __fmul_rn(get_elem(f.emb_type, f.emb, base + i), f.sqrt_dim);
+      xs[i] = v;
+      if (store) f.x_out[i] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  } else {
+    // IN_RESID_NORM / IN_MOE_MERGE: xn = (x + branch) * scale
+    float s_r = 0.f;
+    if (f.r) {
+      float sr = 0.f;
+      for (int i = tid; i < n; i += nt) sr = __fadd_rn(sr, __fmul_rn(f.r[i], f.r[i]));
+      s_r = rms_scale(block_sum(sr, red), n, f.eps);
+    }
+    float s_m = 0.f;
+    if (f.in_mode == IN_MOE_MERGE) {
+      // xb = rmsnorm(shared, post_ffw_norm_1) + moeOutput (Llama.kt:237-243, 349)
+      float st = 0.f;
+      for (int i = tid; i < n; i += nt) {
+        const float t = __fadd_rn(__fmul_rn(f.w_r[i], __fmul_rn(s_r, f.r[i])), f.m[i]);
+        xs[i] = t;
+        st = __fadd_rn(st, __fmul_rn(t, t));
+      }
+      s_m = rms_scale(block_sum(st, red), n, f.eps);
+    }
+    for (int i = tid; i < n; i += nt) {
+      float v = x[i];
+      if (f.in_mode == IN_MOE_MERGE) v = __fadd_rn(v, __fmul_rn(f.w_m[i], __fmul_rn(s_m, xs[i])));
+      else if (f.r) v = __fadd_rn(v, __fmul_rn(f.w_r[i], __fmul_rn(s_r, f.r[i])));
+      if (f.scale != 1.f) v = __fmul_rn(v, f.scale);  // Llama.kt:393-397
+      xs[i] = v;
+      if (store) f.x_out[i] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  }
+  const float sx = rms_scale(block_sum(ss, red), n, f.eps);
+  for (int i = tid; i < n; i += nt) xs[i] = __fmul_rn(f.w_in[i], __fmul_rn(sx, xs[i]));
+  __syncthreads();
+}
+
+// Order-preserving key of an output for the argmax: larger value first, and
+// among equal values the lower row (FloatTensor.argmax keeps the first maximum).
+__device__ __forceinline__ unsigned long long argmax_key(float v, long long row) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
+}
+
+__device__ __forceinline__ float softcap_ref(float v, float cap) {
+  // Llama.kt:403-406: cap * tanh((v / cap).toDouble()).toFloat()
+  return cap > 0.f ? __fmul_rn(cap, (float)tanh((double)__fdiv_rn(v, cap))) : v;
+}
 
 // LPR lanes share a row: a warp covers 32/LPR rows; lane l owns row slot
 // l % (32/LPR) and, within each chunk, the blocks b with b % LPR == l / (32/LPR).
-template <int FMT, int PR, int LPR>
+template <int FMT, int PR, int LPR, bool X2>
 __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const GemvPlan& p = a.p;
@@ -113,19 +190,34 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
     advance(gi, ci);
     if (gi != g0) rs_i = row_start(gi);
   }
+  // Weights are never written by preceding kernels: the first stages are in
+  // flight before this waits for them (programmatic dependent launch; both
+  // are no-ops for a plain launch).  Dependents launch only after the wait,
+  // so everything two kernels back has completed when they start.
+  grid_dep_wait();
+  grid_dep_launch();
+  float* misc = reinterpret_cast<float*>(smem + p.misc_off);
+  const float* src = a.x;
+  if (a.f.in_mode != IN_PLAIN) {
+    fused_prologue(a.f, a.x, xs, misc, p.cols);
+    src = xs;
+  }
 
   // x -> shared memory while the first weight stages are in flight, in one
   // pass: thread t takes float4 columns t, t + blockDim, ...; for the quantized
   // formats 4 lanes form a 16-column sum, 8 lanes (one 32-column block) the
   // 32-column sum and the block's int16 values (quantize_x16's rule)
   int16_t* xq = reinterpret_cast<int16_t*>(smem + p.xq_off);
+  int16_t* xql = X2 ? reinterpret_cast<int16_t*>(smem + p.xq2_off) : nullptr;  // remainders (two-part form)
   float* xsc32 = xsum32 + n16 / 2;
   {
     const int n4 = p.cols / 4;  // a multiple of 8 (cols % 32 == 0)
     for (int i0 = 0; i0 < n4; i0 += blockDim.x) {
       const int i = i0 + (int)threadIdx.x;
       const bool act = i < n4;
-      const float4 v = act ? __ldg(reinterpret_cast<const float4*>(a.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 v = !act ? make_float4(0.f, 0.f, 0.f, 0.f)
+                       : src == a.x ? __ldg(reinterpret_cast<const float4*>(a.x) + i)
+                                    : reinterpret_cast<const float4*>(src)[i];
       if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) {
         float s16 = (v.x + v.y) + (v.z + v.w);
         s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
@@ -142,11 +234,20 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
         const bool nz = m > 0.f && e != 0u;
         const float inv = nz ? __uint_as_float(0x7F000000u - e) : 1.0f;
         if (act) {
-          const uint32_t q01 = (uint32_t)(uint16_t)__float2int_rn(v.x * inv) |
-                               ((uint32_t)(uint16_t)__float2int_rn(v.y * inv) << 16);
-          const uint32_t q23 = (uint32_t)(uint16_t)__float2int_rn(v.z * inv) |
-                               ((uint32_t)(uint16_t)__float2int_rn(v.w * inv) << 16);
+          const float s0 = v.x * inv, s1 = v.y * inv, s2 = v.z * inv, s3 = v.w * inv;  // exact (power of two)
+          const int i0 = __float2int_rn(s0), i1 = __float2int_rn(s1), i2 = __float2int_rn(s2), i3 = __float2int_rn(s3);
+          const uint32_t q01 = (uint32_t)(uint16_t)i0 | ((uint32_t)(uint16_t)i1 << 16);
+          const uint32_t q23 = (uint32_t)(uint16_t)i2 | ((uint32_t)(uint16_t)i3 << 16);
           *reinterpret_cast<uint2*>(xq + xq_at(4 * i)) = make_uint2(q01, q23);
+          if constexpr (X2) {
+            // remainder s - rint(s) in [-0.5, 0.5] (exact), in units of 1/65536
+            auto lo16 = [](float sv, int iv) {
+              const int r = __float2int_rn((sv - (float)iv) * 65536.0f);
+              return (uint32_t)(uint16_t)max(-32767, min(32767, r));
+            };
+            *reinterpret_cast<uint2*>(xql + xq_at(4 * i)) =
+                make_uint2(lo16(s0, i0) | (lo16(s1, i1) << 16), lo16(s2, i2) | (lo16(s3, i3) << 16));
+          }
           if ((i & 3) == 0) xsum16[i >> 2] = s16;
           if ((i & 7) == 0) {
             xsum32[i >> 3] = s32;
@@ -154,7 +255,7 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
           }
         }
       } else {
-        if (act) *reinterpret_cast<float4*>(xs + 4 * i) = v;
+        if (act && src != xs) *reinterpret_cast<float4*>(xs + 4 * i) = v;
       }
     }
   }
@@ -163,6 +264,8 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
   float acc[PR];
 #pragma unroll
   for (int r = 0; r < PR; ++r) acc[r] = 0.f;
+  const int out_mode = a.f.out_mode;
+  unsigned long long best = 0ull;  // OUT_SOFTCAP_ARGMAX: this lane's best key
 
   int g = g_first, c = c_first;  // consume pointer
   long long rs_c = row_start(g);
@@ -189,9 +292,9 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
       if constexpr (FMT == Q4_K || FMT == Q6_K || FMT == Q8_0) {
         for (int b = sl; b < nb; b += LPR) {
           const uint8_t* blk = base + b * TS;
-          if constexpr (FMT == Q4_K) block_q4k_i16<PR>(blk, e0 + b * BS, p.cols, xq, xsc32, xsum32, acc);
-          else if constexpr (FMT == Q6_K) block_q6k_i16<PR>(blk, e0 + b * BS, p.cols, xq, xsc32, xsum16, acc);
-          else block_q8_0_i16(blk, e0 + b * BS, xq, xsc32, acc[0]);
+          if constexpr (FMT == Q4_K) block_q4k_i16<PR, X2>(blk, e0 + b * BS, p.cols, xq, xsc32, xsum32, acc, xql);
+          else if constexpr (FMT == Q6_K) block_q6k_i16<PR, X2>(blk, e0 + b * BS, p.cols, xq, xsc32, xsum16, acc, xql);
+          else block_q8_0_i16<X2>(blk, e0 + b * BS, xq, xsc32, acc[0], xql);
         }
       } else {
         // BF16 / F32: `blocks` are elements; 16-byte loads of 8 or 4 of them
@@ -224,7 +327,20 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
         float t = acc[r];
 #pragma unroll
         for (int o = RPW; o < 32; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (sl == 0 && have_row) a.y[v * PR + r] = t;
+        if (out_mode == OUT_PLAIN) {
+          if (sl == 0 && have_row) a.y[v * PR + r] = t;
+        } else if (out_mode == OUT_GELU_PAIR) {
+          // rows 2i (gate) and 2i + 1 (up) sit in lanes rs, rs ^ 1 (PR == 1)
+          const float u = __shfl_xor_sync(0xffffffffu, t, 1);
+          if (sl == 0 && have_row && (v & 1) == 0) a.y[v >> 1] = __fmul_rn(gelu_ref(t), u);
+        } else {
+          const float capped = softcap_ref(t, a.f.softcap);
+          if (sl == 0 && have_row) {
+            a.y[v] = capped;
+            const unsigned long long k = argmax_key(capped, v);
+            best = k > best ? k : best;
+          }
+        }
         acc[r] = 0.f;
       }
       rs_c = row_start(g);
@@ -243,11 +359,45 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
       if (sl == 0) red[((size_t)warp * RPW + rs) * PR + r] = t;
     }
     __syncthreads();
-    for (int t = threadIdx.x; t < RPW * PR; t += blockDim.x) {
-      const long long v = (long long)blockIdx.x * RPW + t / PR;
+    if (out_mode == OUT_PLAIN) {
+      for (int t = threadIdx.x; t < RPW * PR; t += blockDim.x) {
+        const long long v = (long long)blockIdx.x * RPW + t / PR;
+        float sum = 0.f;
+        for (int w = 0; w < W; ++w) sum += red[(size_t)w * RPW * PR + t];
+        if (v < p.nvrows) a.y[v * PR + (t % PR)] = sum;
+      }
+    } else if (warp == 0) {
+      // fused epilogues (PR == 1): row t of the group in lane t
+      const int t = lane;
+      const long long v = (long long)blockIdx.x * RPW + t;
       float sum = 0.f;
-      for (int w = 0; w < W; ++w) sum += red[(size_t)w * RPW * PR + t];
-      if (v < p.nvrows) a.y[v * PR + (t % PR)] = sum;
+      if (t < RPW)
+        for (int w = 0; w < W; ++w) sum += red[(size_t)w * RPW + t];
+      if (out_mode == OUT_GELU_PAIR) {
+        const float u = __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (t < RPW && v < p.nvrows && (v & 1) == 0) a.y[v >> 1] = __fmul_rn(gelu_ref(sum), u);
+      } else if (t < RPW && v < p.nvrows) {
+        const float capped = softcap_ref(sum, a.f.softcap);
+        a.y[v] = capped;
+        best = argmax_key(capped, v);
+      }
+    }
+  }
+  if (out_mode == OUT_SOFTCAP_ARGMAX) {
+    // CTA maximum, one atomic per CTA
+    unsigned long long* kb = reinterpret_cast<unsigned long long*>(misc + 64);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+      best = k > best ? k : best;
+    }
+    __syncthreads();
+    if (lane == 0) kb[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < W; ++w) b = kb[w] > b ? kb[w] : b;
+      atomicMax(a.f.argmax, b);
     }
   }
   // Never leave the CTA with bulk copies still landing in its shared memory
@@ -293,23 +443,30 @@ static int gcd_i(int a, int b) {
 using KernelFn = void (*)(const GemvArgs);
 
 template <int FMT>
-static KernelFn pick_kernel(int pr, int lpr) {
-  if (pr == 1) return lpr == 4 ? gemv_rows_kernel<FMT, 1, 4> : lpr == 2 ? gemv_rows_kernel<FMT, 1, 2>
-                                                                        : gemv_rows_kernel<FMT, 1, 1>;
+static KernelFn pick_kernel(int pr, int lpr, bool x2) {
+  if (x2) {
+    // two-part activations: the decoder's row-aligned projections only
+    if constexpr (FMT == Q8_0 || FMT == Q4_K || FMT == Q6_K)
+      if (pr == 1) return lpr == 4 ? gemv_rows_kernel<FMT, 1, 4, true> : lpr == 2 ? gemv_rows_kernel<FMT, 1, 2, true>
+                                                                                  : gemv_rows_kernel<FMT, 1, 1, true>;
+    return nullptr;
+  }
+  if (pr == 1) return lpr == 4 ? gemv_rows_kernel<FMT, 1, 4, false> : lpr == 2 ? gemv_rows_kernel<FMT, 1, 2, false>
+                                                                               : gemv_rows_kernel<FMT, 1, 1, false>;
   if constexpr (FMT == Q4_K || FMT == Q6_K) {
-    if (pr == 2) return lpr == 2 ? gemv_rows_kernel<FMT, 2, 2> : gemv_rows_kernel<FMT, 2, 1>;
-    if (pr == 4) return lpr == 2 ? gemv_rows_kernel<FMT, 4, 2> : gemv_rows_kernel<FMT, 4, 1>;
+    if (pr == 2) return lpr == 2 ? gemv_rows_kernel<FMT, 2, 2, false> : gemv_rows_kernel<FMT, 2, 1, false>;
+    if (pr == 4) return lpr == 2 ? gemv_rows_kernel<FMT, 4, 2, false> : gemv_rows_kernel<FMT, 4, 1, false>;
   }
   return nullptr;
 }
 
-static KernelFn kernel_for(int type, int pr, int lpr) {
+static KernelFn kernel_for(int type, int pr, int lpr, bool x2 = false) {
   switch (type) {
-    case Q8_0: return pick_kernel<Q8_0>(pr, lpr);
-    case Q4_K: return pick_kernel<Q4_K>(pr, lpr);
-    case Q6_K: return pick_kernel<Q6_K>(pr, lpr);
-    case BF16: return pick_kernel<BF16>(pr, lpr);
-    case F32: return pick_kernel<F32>(pr, lpr);
+    case Q8_0: return pick_kernel<Q8_0>(pr, lpr, x2);
+    case Q4_K: return pick_kernel<Q4_K>(pr, lpr, x2);
+    case Q6_K: return pick_kernel<Q6_K>(pr, lpr, x2);
+    case BF16: return pick_kernel<BF16>(pr, lpr, false);
+    case F32: return pick_kernel<F32>(pr, lpr, false);
     default: return nullptr;
   }
 }
@@ -326,13 +483,16 @@ static int pitch_for(int bytes) {
   return 16 * p;
 }
 
-GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols) {
+GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols, bool fused,
+                   size_t max_smem, bool exact_x) {
   GemvPlan p{};
   p.type = type;
   p.rows = rows;
   p.cols = cols;
   p.off = off;
   p.fast = 0;
+  p.fused = fused ? 1 : 0;
+  p.x2 = exact_x && (type == Q8_0 || type == Q4_K || type == Q6_K) ? 1 : 0;
   const int BS = block_size(type), TS = type_size(type);
   // the lane-per-row kernel decodes F32, BF16, Q8_0, Q4_K and Q6_K; the other formats take the
   // generic kernel (one warp per row, element decoder)
@@ -349,10 +509,13 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   if (rows % pr != 0) return p;
   // fp32 x in shared memory only for BF16 / F32; the quantized formats read the int16 form
   const bool quantized = type == Q8_0 || type == Q4_K || type == Q6_K;
-  const int xbytes = quantized ? 0 : ((cols * 4 + 127) / 128) * 128;
+  // a fused prologue stages the fp32 activation in shared memory for every format
+  const int xbytes = quantized && !fused ? 0 : ((cols * 4 + 127) / 128) * 128;
+  constexpr int kMiscBytes = 512;  // block reductions and the argmax epilogue
   // per-16 and per-32 column sums, per-32 int16 scales; int16 activations
   const int xsbytes = (((cols / 16 + 2 * (cols / 32)) * 4 + 127) / 128) * 128;
-  const int xqbytes = (((cols + 8 * ((cols + 255) / 256)) * 2 + 127) / 128) * 128;
+  const int xq1 = (((cols + 8 * ((cols + 255) / 256)) * 2 + 127) / 128) * 128;
+  const int xqbytes = xq1 * (p.x2 ? 2 : 1);  // two-part form: the remainders follow the first part
   if (xbytes > 96 * 1024) return p;
   p.pr = pr;
   p.nvrows = rows / pr;
@@ -381,8 +544,9 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.nchunks = (p.bpv + cb - 1) / cb;
   p.pitch = pitch_for(cb * TS + 32);
   size_t stage = (size_t)rows_per_group * p.pitch;
-  const size_t budget = dev.smem_optin > 0 ? dev.smem_optin : 227 * 1024;
-  const size_t fixed = (size_t)xbytes + xsbytes + xqbytes + 256;
+  const size_t optin = dev.smem_optin > 0 ? dev.smem_optin : 227 * 1024;
+  const size_t budget = max_smem > 0 ? std::min(max_smem, optin) : optin;
+  const size_t fixed = (size_t)xbytes + xsbytes + xqbytes + kMiscBytes + 256;
   if (small) {
     p.split = std::min(p.nchunks, 8);
     p.warps = p.split;
@@ -416,16 +580,18 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.xs_off = 0;
   p.xsum_off = xbytes;
   p.xq_off = xbytes + xsbytes;
-  p.bar_off = p.xq_off + xqbytes;
+  p.xq2_off = p.xq_off + xq1;
+  p.misc_off = p.xq_off + xqbytes;
+  p.bar_off = p.misc_off + kMiscBytes;
   p.ring_off = p.bar_off + 128 * ((p.warps * p.ns * 8 + 127) / 128);
   p.red_off = (int)(p.ring_off + (size_t)p.warps * p.ns * stage);
   p.smem = (size_t)p.red_off + (p.split > 1 ? (size_t)p.warps * rows_per_group * pr * 4 : 0);
-  KernelFn k = kernel_for(type, pr, p.lpr);
+  KernelFn k = kernel_for(type, pr, p.lpr, p.x2 != 0);
   if (!k) return p;
   int occ = 0;
   // The attribute belongs to the kernel, not to this plan: always allow the
   // device maximum so plans of other shapes stay launchable.
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)budget) != cudaSuccess ||
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)optin) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, 32 * p.warps, p.smem) != cudaSuccess || occ < 1) {
     cudaGetLastError();
     return p;
@@ -439,12 +605,32 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   return p;
 }
 
+int launch_gemv_fused(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvFuse& f,
+                      unsigned* status, cudaStream_t st, bool pdl) {
+  cudaGetLastError();
+  if (!p.fast || (f.in_mode != IN_PLAIN && !p.fused) || (f.out_mode != OUT_PLAIN && p.pr != 1))
+    return (int)cudaErrorInvalidValue;
+  GemvArgs a{p, w, x, y, status, f};
+  KernelFn k = kernel_for(p.type, p.pr, p.lpr, p.x2 != 0);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(32 * p.warps);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return (int)cudaLaunchKernelEx(&cfg, k, a);
+}
+
 int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, unsigned* status,
                 cudaStream_t st) {
   cudaGetLastError();  // launch errors below must not be confused with stale ones
   if (p.fast) {
-    GemvArgs a{p, w, x, y, status};
-    KernelFn k = kernel_for(p.type, p.pr, p.lpr);
+    GemvArgs a{p, w, x, y, status, GemvFuse{}};
+    KernelFn k = kernel_for(p.type, p.pr, p.lpr, p.x2 != 0);
     k<<<p.grid, 32 * p.warps, p.smem, st>>>(a);
   } else {
     int wpb = 8;

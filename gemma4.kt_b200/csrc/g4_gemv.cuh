@@ -22,9 +22,47 @@ struct GemvPlan {
   int split;         // 1: persistent, each warp owns whole row groups; >1: CTA per group
   int ngroups;       // row groups of 32/lpr virtual rows
   int grid;
-  int xs_off, xsum_off, xq_off, bar_off, ring_off, red_off;  // shared-memory carve-up
+  int xs_off, xsum_off, xq_off, xq2_off, bar_off, misc_off, ring_off, red_off;  // shared-memory carve-up
   size_t smem;
   int fast;          // 1: streaming kernel; 0: generic fallback
+  int fused;         // planned for a fused prologue (fp32 activation staged in shared memory)
+  int x2;            // two-part int16 activations (fp32-level products) for the quantized formats
+};
+
+// Fused prologue / epilogue of the decoder's GEMV launches (GemvFuse.in_mode /
+// out_mode).  The prologue turns the kernel's inputs into the activation
+// vector before it is quantized; the epilogue post-processes each output row.
+enum FuseIn : int {
+  IN_PLAIN = 0,       // act = x
+  IN_NORM = 1,        // act = rmsnorm(x, w_in)                                   Llama.kt:27-37
+  IN_RESID_NORM = 2,  // xn = (x + rmsnorm(r, w_r)) * scale [r optional]; act = rmsnorm(xn, w_in)
+  IN_EMBED_NORM = 3,  // xn = emb.get(tok * dim + i) * sqrt(dim); act = rmsnorm(xn, w_in)  Llama.kt:112-113
+  IN_MOE_MERGE = 4,   // xn = (x + rmsnorm(rmsnorm(r, w_r) + m, w_m)) * scale; act = rmsnorm(xn, w_in)  Llama.kt:349-353
+};
+enum FuseOut : int {
+  OUT_PLAIN = 0,           // y[row] = dot
+  OUT_GELU_PAIR = 1,       // rows (2i, 2i+1) = (gate_i, up_i): y[i] = gelu(gate_i) * up_i   Llama.kt:357-360
+  OUT_SOFTCAP_ARGMAX = 2,  // y[row] = cap * tanh(dot / cap) (cap > 0); argmax key (first maximum)  Llama.kt:403-406
+};
+
+struct GemvFuse {
+  int in_mode = IN_PLAIN, out_mode = OUT_PLAIN;
+  float eps = 1e-6f;
+  float scale = 1.f;          // layer output scale (IN_RESID_NORM / IN_MOE_MERGE)
+  float sqrt_dim = 1.f;       // IN_EMBED_NORM
+  float softcap = 0.f;        // OUT_SOFTCAP_ARGMAX
+  const float* w_in = nullptr;
+  const float* r = nullptr;   // residual-branch output to normalise and add
+  const float* w_r = nullptr;
+  const float* m = nullptr;   // IN_MOE_MERGE: the expert half's output
+  const float* w_m = nullptr;
+  float* x_out = nullptr;     // CTA 0 stores xn (the new residual stream) here; must not alias x
+  const uint8_t* emb = nullptr;  // IN_EMBED_NORM: embedding table (GGUF blocks)
+  int emb_type = 0;
+  const int* step = nullptr;     // IN_EMBED_NORM: token = in_tok[*step] >= 0 ? in_tok[*step] : *next_tok
+  const int* in_tok = nullptr;
+  const int* next_tok = nullptr;
+  unsigned long long* argmax = nullptr;  // OUT_SOFTCAP_ARGMAX: atomicMax of (ordered value << 32 | ~row)
 };
 
 // Magic-number int->float: 2^23 + b as float bits, then subtract 2^23 (+bias).

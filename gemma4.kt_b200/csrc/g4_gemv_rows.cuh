@@ -95,11 +95,20 @@ __device__ __forceinline__ void quantize_x16(const float* xs, int cols, int16_t*
   }
 }
 
+// Two-part activations (X2): x = s_b * (xq + xql / 65536), the second int16
+// holding the rounding remainder of the first, so the products carry about
+// 31 bits of each activation (fp32-level dot products) at twice the dp2a
+// work.  The whole-model decoder uses this form: its attention (scale 1.0 on
+// RMS-normalised q and k) turns activation errors of a few 1e-5 into
+// visibly different attention weights.
+constexpr float kLoScale = 1.0f / 65536.0f;
+
 // Q4_K on int16 activations.  Low nibbles are the bytes w & 0x0F, high nibbles
 // stay in place as 16 * q (w & 0xF0): one mask per four codes each.
-template <int PR>
+template <int PR, bool X2 = false>
 __device__ __forceinline__ void block_q4k_i16(const uint8_t* blk, int e0, int cols, const int16_t* xq,
-                                              const float* xsc32, const float* xsum32, float (&acc)[PR]) {
+                                              const float* xsc32, const float* xsum32, float (&acc)[PR],
+                                              const int16_t* xql = nullptr) {
   const uint4 h = lds128(blk);
   const float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
   const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
@@ -114,7 +123,7 @@ __device__ __forceinline__ void block_q4k_i16(const uint8_t* blk, int e0, int co
     const int rr = PR == 1 ? 0 : eg / cols;
     const int16_t* xp = xq + xq_at(col);  // the 64 columns of a group share one 256-column span
     const uint4 qa = lds128(blk + 16 + 32 * g), qb = lds128(blk + 32 + 32 * g);
-    int alo = 0, ahi = 0;
+    int alo = 0, ahi = 0, alo2 = 0, ahi2 = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const uint2 xl = *reinterpret_cast<const uint2*>(xp + 4 * k);
@@ -126,7 +135,18 @@ __device__ __forceinline__ void block_q4k_i16(const uint8_t* blk, int e0, int co
       alo = dp2a_hi_su(xl.y, lo, alo);
       ahi = dp2a_lo_su(xh.x, hi, ahi);
       ahi = dp2a_hi_su(xh.y, hi, ahi);
+      if constexpr (X2) {
+        const int16_t* xpl = xql + xq_at(col);
+        const uint2 yl = *reinterpret_cast<const uint2*>(xpl + 4 * k);
+        const uint2 yh = *reinterpret_cast<const uint2*>(xpl + 32 + 4 * k);
+        alo2 = dp2a_lo_su(yl.x, lo, alo2);
+        alo2 = dp2a_hi_su(yl.y, lo, alo2);
+        ahi2 = dp2a_lo_su(yh.x, hi, ahi2);
+        ahi2 = dp2a_hi_su(yh.y, hi, ahi2);
+      }
     }
+    const float flo = X2 ? fmaf((float)alo2, kLoScale, (float)alo) : (float)alo;
+    const float fhi = X2 ? fmaf((float)ahi2, kLoScale, (float)ahi) : (float)ahi;
     const uint32_t scw = g < 2 ? sc03 : sc47, mnw = g < 2 ? mn03 : mn47;
     const int b0 = (2 * g) & 3;
     const float sc_lo = small_u2f((scw >> (8 * b0)) & 0xFFu), sc_hi = small_u2f((scw >> (8 * b0 + 8)) & 0xFFu);
@@ -134,16 +154,17 @@ __device__ __forceinline__ void block_q4k_i16(const uint8_t* blk, int e0, int co
     const float s_lo = xsc32[col / 32], s_hi = xsc32[col / 32 + 1] * 0.0625f;
     const float xs_lo = xsum32[col / 32], xs_hi = xsum32[col / 32 + 1];
     // sum_i (d*sc*q_i - dmin*m) x_i over both sub-blocks of the group
-    float v = (d * sc_lo) * (s_lo * (float)alo);
-    v = fmaf(d * sc_hi, s_hi * (float)ahi, v);
+    float v = (d * sc_lo) * (s_lo * flo);
+    v = fmaf(d * sc_hi, s_hi * fhi, v);
     v = fmaf(-dmin, fmaf(mn_lo, xs_lo, mn_hi * xs_hi), v);
     add_row<PR>(acc, rr, v);
   }
 }
 
 // Q8_0 on int16 activations: the int8 codes are dp2a's signed bytes as stored.
+template <bool X2 = false>
 __device__ __forceinline__ void block_q8_0_i16(const uint8_t* blk, int col, const int16_t* xq, const float* xsc32,
-                                               float& acc) {
+                                               float& acc, const int16_t* xql = nullptr) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
   const uint8_t* b4 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
   const uint32_t sh = (uint32_t)(a & 3u);  // 0 or 2
@@ -151,7 +172,7 @@ __device__ __forceinline__ void block_q8_0_i16(const uint8_t* blk, int col, cons
 #pragma unroll
   for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 4 * i);
   const float d = f16_bits_to_f32((uint16_t)(sh ? (w[0] >> 16) : (w[0] & 0xFFFFu)));
-  int s = 0;
+  int s = 0, s2 = 0;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     // quants start at byte 2 + sh of b4: a 16- or 32-bit clamped funnel shift
@@ -159,15 +180,22 @@ __device__ __forceinline__ void block_q8_0_i16(const uint8_t* blk, int col, cons
     const uint2 xv = *reinterpret_cast<const uint2*>(xq + xq_at(col) + 4 * k);
     s = dp2a_lo_ss(xv.x, m, s);
     s = dp2a_hi_ss(xv.y, m, s);
+    if constexpr (X2) {
+      const uint2 yv = *reinterpret_cast<const uint2*>(xql + xq_at(col) + 4 * k);
+      s2 = dp2a_lo_ss(yv.x, m, s2);
+      s2 = dp2a_hi_ss(yv.y, m, s2);
+    }
   }
-  acc = fmaf((float)s * xsc32[col / 32], d, acc);  // fma(sum, d, acc) as Q8_0FloatTensor.kt:77
+  const float fs = X2 ? fmaf((float)s2, kLoScale, (float)s) : (float)s;
+  acc = fmaf(fs * xsc32[col / 32], d, acc);  // fma(sum, d, acc) as Q8_0FloatTensor.kt:77
 }
 
 // Q6_K on int16 activations: the 6-bit codes as bytes 0..63; sum (q - 32) x =
 // s_b * sum(q xq) - 32 * sum x per 16-weight group.
-template <int PR>
+template <int PR, bool X2 = false>
 __device__ __forceinline__ void block_q6k_i16(const uint8_t* blk, int e0, int cols, const int16_t* xq,
-                                              const float* xsc32, const float* xsum16, float (&acc)[PR]) {
+                                              const float* xsc32, const float* xsum16, float (&acc)[PR],
+                                              const int16_t* xql = nullptr) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
   const uint8_t* b4 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
   const uint32_t sh = 8u * (uint32_t)(a & 3u);  // 0 or 16 bits
@@ -193,7 +221,7 @@ __device__ __forceinline__ void block_q6k_i16(const uint8_t* blk, int e0, int co
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const int ebase = e0 + 128 * h + 16 * c;
-      int a4[4] = {0, 0, 0, 0};
+      int a4[4] = {0, 0, 0, 0}, b4[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t la = qa[4 * c + k], lb = qb[4 * c + k], hh = qh[4 * c + k];
@@ -208,6 +236,11 @@ __device__ __forceinline__ void block_q6k_i16(const uint8_t* blk, int e0, int co
           const uint2 xv = *reinterpret_cast<const uint2*>(xq + xq_at(PR == 1 ? e : e % cols));
           a4[sub] = dp2a_lo_su(xv.x, m[sub], a4[sub]);
           a4[sub] = dp2a_hi_su(xv.y, m[sub], a4[sub]);
+          if constexpr (X2) {
+            const uint2 yv = *reinterpret_cast<const uint2*>(xql + xq_at(PR == 1 ? e : e % cols));
+            b4[sub] = dp2a_lo_su(yv.x, m[sub], b4[sub]);
+            b4[sub] = dp2a_hi_su(yv.y, m[sub], b4[sub]);
+          }
         }
       }
 #pragma unroll
@@ -220,7 +253,8 @@ __device__ __forceinline__ void block_q6k_i16(const uint8_t* blk, int e0, int co
         // int8 scale as float without I2F: (sc + 128) as an unsigned byte, minus 128
         const uint32_t scb = ((((si >> 2) ? scw1 : scw0) >> (8 * (si & 3))) & 0xFFu) ^ 0x80u;
         const float scf = small_u2f(scb) - 128.f;
-        const float v = (d * scf) * fmaf(xsc32[col / 32], (float)a4[sub], -32.f * xsum16[col / 16]);
+        const float qx = X2 ? fmaf((float)b4[sub], kLoScale, (float)a4[sub]) : (float)a4[sub];
+        const float v = (d * scf) * fmaf(xsc32[col / 32], qx, -32.f * xsum16[col / 16]);
         add_row<PR>(acc, rr, v);
       }
     }

@@ -12,13 +12,24 @@ struct DeviceInfo {
 };
 
 struct GemvPlan;
+struct GemvFuse;
 
-GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols);
+// fused: reserve shared memory for a fused prologue (launch_gemv_fused).
+// max_smem > 0 caps the plan's shared memory (room for a second CTA per SM).
+// exact_x: two-part int16 activations for Q8_0 / Q4_K / Q6_K (rows of whole
+// blocks only), products at fp32 precision instead of ~3e-5.
+GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols, bool fused = false,
+                   size_t max_smem = 0, bool exact_x = false);
 // Launch with a plan from plan_gemv (the caller caches plans: planning queries
 // occupancy and sets kernel attributes, which costs microseconds of host time).
 // Returns the cudaError_t of the launch.
 int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, unsigned* status,
                 cudaStream_t st);
+// Same with a fused prologue / epilogue; pdl launches with programmatic
+// stream serialization (weights stream in before the previous kernel ends).
+// Needs a plan made with fused = true for a fused prologue, and the fast kernel.
+int launch_gemv_fused(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvFuse& f,
+                      unsigned* status, cudaStream_t st, bool pdl);
 int launch_dequant(int type, const uint8_t* w, long long off, long long n, float* out, cudaStream_t st);
 // Resolve the fixed work array of g4_moe_layer_noalloc on `device` (which must
 // be current); returns a cudaError_t (0 on success).
