@@ -16,3 +16,4 @@ from .floattensor import (  # noqa: F401
     row_shard,
 )
 from .moe import MoeLayer, topk  # noqa: F401
+from .model import DecoderModel, DecoderState, ModelConfig, TensorSource  # noqa: F401

@@ -110,3 +110,204 @@ def random_blocks(ggml_type, n_elems: int, rng: np.random.Generator) -> np.ndarr
     else:
         raise ValueError(f"no random block generator for {t.name}")
     return raw.reshape(-1)
+
+
+# ---------------------------------------------------------------------- whole models
+from dataclasses import dataclass, field  # noqa: E402
+
+
+@dataclass
+class DecoderSpec:
+    """Geometry of a synthetic Gemma-4-style decoder (the metadata keys of
+    ModelLoader.kt:46-116 and the tensor set of ModelLoader.kt:154-261).
+
+    Layer l uses sliding-window attention unless (l + 1) % swa_period == 0
+    (swa_period 0: every layer full attention); the pattern is written as
+    gemma4.attention.sliding_window_pattern.  The last shared_kv_layers layers
+    reuse the KV cache of an earlier layer (LlamaConfiguration.kvSourceLayer).
+    Layers listed in no_v_layers have no attn_v tensor (V = K, Llama.kt:176-181).
+    n_expert > 0 makes every layer a MoE layer: shared dense FFN of width ff
+    plus n_expert experts of width expert_ff (top n_expert_used)."""
+
+    name: str
+    n_layers: int
+    dim: int
+    n_heads: int
+    n_kv_heads: int
+    head_size: int
+    ff: int
+    vocab: int
+    ctx_len: int = 4096
+    wtype: int = GGMLType.Q8_0
+    emb_type: int = GGMLType.Q8_0
+    head_size_swa: int = 0          # 0: same as head_size
+    sliding_window: int = 512
+    swa_period: int = 5
+    shared_kv_layers: int = 0
+    no_v_layers: tuple = ()
+    softcap: float = 30.0
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+    rope_theta_swa: float = 1e4
+    tied_output: bool = True
+    n_expert: int = 0
+    n_expert_used: int = 0
+    expert_ff: int = 0
+    expert_type: int = GGMLType.Q4_K
+    layer_scale: bool = True
+    extra: dict = field(default_factory=dict)
+
+    def hs(self, layer: int) -> int:
+        return (self.head_size_swa or self.head_size) if self.is_swa(layer) else self.head_size
+
+    def is_swa(self, layer: int) -> bool:
+        return self.swa_period > 0 and (layer + 1) % self.swa_period != 0
+
+
+# The benchmark's configurations 4 and 5 (dense and MoE decoders).
+C4_DENSE = DecoderSpec("C4 dense decoder", n_layers=35, dim=1536, n_heads=8, n_kv_heads=1, head_size=256, ff=6144,
+                       vocab=262144)
+C5_MOE = DecoderSpec("C5 MoE decoder", n_layers=30, dim=2816, n_heads=16, n_kv_heads=8, head_size=256, ff=2112,
+                     vocab=262144, n_expert=128, n_expert_used=8, expert_ff=704)
+
+# special tokens the reference tokenizer and chat format look up
+# (GemmaTokenizer.kt:18-28, GemmaChatFormat.kt:6-13, Llama.kt:18)
+SPECIAL_TOKENS = ["<pad>", "<eos>", "<bos>", "<unk>", "<mask>", "<|turn>", "<turn|>"]
+N_SPECIAL = len(SPECIAL_TOKENS) + 256  # specials, then the 256 byte tokens <0x00>..<0xFF>
+
+
+def vocabulary(n: int):
+    """Token strings, scores and types of a synthetic vocabulary of n tokens."""
+    tokens = list(SPECIAL_TOKENS) + [f"<0x{b:02X}>" for b in range(256)]
+    tokens += [f"▁t{i}" for i in range(n - len(tokens))]
+    scores = np.zeros(n, dtype=np.float32)
+    scores[N_SPECIAL:] = -np.arange(n - N_SPECIAL, dtype=np.float32)
+    types = np.ones(n, dtype=np.int32)
+    types[:len(SPECIAL_TOKENS)] = 3  # control
+    types[len(SPECIAL_TOKENS):N_SPECIAL] = 6  # byte
+    return tokens, scores, types
+
+
+class SynthDecoder:
+    """Seeded random-init weights of a DecoderSpec, in GGUF form: `metadata`
+    (gguf.Typed values) and `tensors` [(name, dims, GGMLType, block bytes)].
+    Matrices are N(0, 0.02) quantized by the build's quantizers; norm weights
+    N(1, 0.1); layer output scales U(0.5, 1); rope_freqs U(1, 2); router
+    F32 N(0, 0.02); router input scales N(1, 0.1); expert output scales
+    U(0.5, 1.5).  Every tensor draws from its own stream
+    default_rng([seed, index]), so tensors can be made in any order."""
+
+    def __init__(self, spec: DecoderSpec, seed: int, threads: int | None = None):
+        from . import gguf as G
+
+        self.spec, self.seed = spec, seed
+        s = spec
+        self._i = 0
+        self.tensors = []
+        self.threads = threads
+        tokens, scores, types = vocabulary(s.vocab)
+        A, VT = G.arr, G.ValueType
+        self.metadata = {
+            "general.architecture": "gemma4",
+            "general.name": f"synthetic {s.name} seed {seed}",
+            "general.alignment": G.u32(32),
+            "gemma4.context_length": G.u32(s.ctx_len),
+            "gemma4.embedding_length": G.u32(s.dim),
+            "gemma4.block_count": G.u32(s.n_layers),
+            "gemma4.feed_forward_length": G.u32(s.ff),
+            "gemma4.attention.head_count": G.u32(s.n_heads),
+            "gemma4.attention.head_count_kv": G.u32(s.n_kv_heads),
+            "gemma4.attention.key_length": G.u32(s.head_size),
+            "gemma4.attention.value_length": G.u32(s.head_size),
+            "gemma4.attention.key_length_swa": G.u32(s.head_size_swa or s.head_size),
+            "gemma4.attention.value_length_swa": G.u32(s.head_size_swa or s.head_size),
+            "gemma4.attention.sliding_window": G.u32(s.sliding_window),
+            "gemma4.attention.sliding_window_pattern": A(VT.BOOL, [s.is_swa(l) for l in range(s.n_layers)]),
+            "gemma4.attention.shared_kv_layers": G.u32(s.shared_kv_layers),
+            "gemma4.attention.layer_norm_rms_epsilon": G.f32(s.eps),
+            "gemma4.rope.freq_base": G.f32(s.rope_theta),
+            "gemma4.rope.freq_base_swa": G.f32(s.rope_theta_swa),
+            "gemma4.final_logit_softcapping": G.f32(s.softcap),
+            "tokenizer.ggml.model": "gemma4",
+            "tokenizer.ggml.tokens": A(VT.STRING, tokens),
+            "tokenizer.ggml.scores": A(VT.FLOAT32, scores),
+            "tokenizer.ggml.token_type": A(VT.INT32, types),
+            "tokenizer.ggml.bos_token_id": G.u32(2),
+            "tokenizer.ggml.eos_token_id": G.u32(1),
+        }
+        if s.n_expert:
+            self.metadata.update({
+                "gemma4.expert_count": G.u32(s.n_expert),
+                "gemma4.expert_used_count": G.u32(s.n_expert_used),
+                "gemma4.expert_feed_forward_length": G.u32(s.expert_ff),
+            })
+        self.metadata.update(s.extra)
+        d = s.dim
+        self._mat("token_embd.weight", s.emb_type, d, s.vocab)
+        if not s.tied_output:
+            self._mat("output.weight", s.wtype, d, s.vocab)
+        self._f32("output_norm.weight", self._rng().normal(1.0, 0.1, d))
+        self._f32("rope_freqs.weight", self._rng().uniform(1.0, 2.0, s.head_size // 2))
+        for l in range(s.n_layers):
+            hs = s.hs(l)
+            p = f"blk.{l}."
+            self._f32(p + "attn_norm.weight", self._rng().normal(1.0, 0.1, d))
+            self._mat(p + "attn_q.weight", s.wtype, d, s.n_heads * hs)
+            self._mat(p + "attn_k.weight", s.wtype, d, s.n_kv_heads * hs)
+            if l not in s.no_v_layers:
+                self._mat(p + "attn_v.weight", s.wtype, d, s.n_kv_heads * hs)
+            self._mat(p + "attn_output.weight", s.wtype, s.n_heads * hs, d)
+            self._f32(p + "attn_q_norm.weight", self._rng().normal(1.0, 0.1, hs))
+            self._f32(p + "attn_k_norm.weight", self._rng().normal(1.0, 0.1, hs))
+            self._f32(p + "post_attention_norm.weight", self._rng().normal(1.0, 0.1, d))
+            self._f32(p + "ffn_norm.weight", self._rng().normal(1.0, 0.1, d))
+            self._mat(p + "ffn_gate.weight", s.wtype, d, s.ff)
+            self._mat(p + "ffn_up.weight", s.wtype, d, s.ff)
+            self._mat(p + "ffn_down.weight", s.wtype, s.ff, d)
+            self._f32(p + "post_ffw_norm.weight", self._rng().normal(1.0, 0.1, d))
+            if s.layer_scale:
+                self._f32(p + "layer_output_scale.weight", self._rng().uniform(0.5, 1.0, 1))
+            if s.n_expert:
+                E, eff = s.n_expert, s.expert_ff
+                self._f32(p + "post_ffw_norm_1.weight", self._rng().normal(1.0, 0.1, d))
+                self._f32(p + "pre_ffw_norm_2.weight", self._rng().normal(1.0, 0.1, d))
+                self._f32(p + "post_ffw_norm_2.weight", self._rng().normal(1.0, 0.1, d))
+                self._mat(p + "ffn_gate_inp.weight", GGMLType.F32, d, E)
+                self._f32(p + "ffn_gate_inp.scale", self._rng().normal(1.0, 0.1, d))
+                self._mat(p + "ffn_gate_up_exps.weight", s.expert_type, d, 2 * eff, E)
+                self._mat(p + "ffn_down_exps.weight", s.expert_type, eff, d, E)
+                self._f32(p + "ffn_down_exps.scale", self._rng().uniform(0.5, 1.5, E))
+
+    def _rng(self):
+        r = np.random.default_rng([self.seed, self._i])
+        self._i += 1
+        return r
+
+    def _f32(self, name, values):
+        a = np.asarray(values, dtype=np.float32).reshape(-1)
+        self.tensors.append((name, (a.size,), GGMLType.F32, a.view(np.uint8)))
+
+    def _mat(self, name, t, *dims):
+        n = 1
+        for x in dims:
+            n *= x
+        rng = self._rng()
+        w = normal(rng, n)
+        raw = w.view(np.uint8) if int(t) == GGMLType.F32 else quantize(t, w, self.threads)
+        self.tensors.append((name, tuple(dims), GGMLType(int(t)), raw))
+
+    def tensor(self, name: str) -> np.ndarray:
+        for n, _, _, raw in self.tensors:
+            if n == name:
+                return raw
+        raise KeyError(name)
+
+    def write(self, path) -> None:
+        from .gguf import write_gguf
+
+        write_gguf(path, self.metadata, self.tensors)
+
+    def prompt(self, n: int, seed: int | None = None) -> np.ndarray:
+        """n uniform random token ids outside the special and byte tokens."""
+        rng = np.random.default_rng([self.seed if seed is None else seed, 999983])
+        return rng.integers(N_SPECIAL, self.spec.vocab, size=n, dtype=np.int64).astype(np.int32)

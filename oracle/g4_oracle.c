@@ -513,3 +513,275 @@ void o_moe_token(const o_moe_weights *w, const float *x, float *out, int32_t *to
   free(gate_up);
   free(down);
 }
+
+/* ====================================================================== */
+/* Whole-model forward, Llama.kt:105-408                                   */
+/* ====================================================================== */
+
+/* RotaryPositionEmbeddings.kt:8-27 (freq_factors == NULL) and :29-53 */
+void o_rope_table(int ctx_len, int head_size, double theta, const float *freq_factors, float *cr, float *ci) {
+  int half = head_size / 2;
+  int64_t n = 0;
+  for (int pos = 0; pos < ctx_len; pos++) {
+    for (int i = 0; i < half; i++) {
+      float value;
+      if (freq_factors) {
+        float base = (float)(1.0 / pow(theta, (2.0 * i) / head_size));
+        value = (float)pos * base;
+        value = value / freq_factors[i];
+      } else {
+        /* i0 = 2*i walks the head in steps of 2: theta^(i0 / headSize) */
+        float freq = (float)(1.0 / pow(theta, (double)(2 * i) / (double)head_size));
+        value = (float)pos * freq;
+      }
+      cr[n] = (float)cos((double)value);
+      ci[n] = (float)sin((double)value);
+      n++;
+    }
+  }
+}
+
+struct o_state {
+  float *x, *xb, *xbk, *xb2, *hb, *hb2, *q, *k, *v, *att, *logits;
+  float *moe_out;
+  float **key_cache, **value_cache; /* [n_layer_kv_from_start][ctx * kvDim] */
+  int n_kv_layers;
+  float *cr_full, *ci_full, *cr_swa, *ci_swa;
+};
+
+static int head_size_of(const o_model *m, int l) { return m->is_swa[l] ? m->head_size_swa : m->head_size_full; }
+static int kv_dim_of(const o_model *m, int l) { return m->n_kv_heads[l] * head_size_of(m, l); }
+
+o_state *o_state_new(const o_model *m) {
+  o_state *s = (o_state *)calloc(1, sizeof(o_state));
+  int max_q = m->n_heads * (m->head_size_full > m->head_size_swa ? m->head_size_full : m->head_size_swa);
+  int max_kv = 0, max_ff = 0;
+  for (int l = 0; l < m->n_layers; l++) {
+    if (kv_dim_of(m, l) > max_kv) max_kv = kv_dim_of(m, l);
+    if (m->ff[l] > max_ff) max_ff = m->ff[l];
+  }
+  s->x = (float *)calloc(m->dim, 4);
+  s->xb = (float *)calloc(m->dim, 4);
+  s->xbk = (float *)calloc(max_q, 4);
+  s->xb2 = (float *)calloc(m->dim, 4);
+  s->hb = (float *)calloc(max_ff > 0 ? max_ff : 1, 4);
+  s->hb2 = (float *)calloc(max_ff > 0 ? max_ff : 1, 4);
+  s->q = (float *)calloc(max_q, 4);
+  s->k = (float *)calloc(max_kv, 4);
+  s->v = (float *)calloc(max_kv, 4);
+  s->att = (float *)calloc((size_t)m->n_heads * m->ctx_len, 4);
+  s->logits = (float *)calloc(m->vocab, 4);
+  s->moe_out = (float *)calloc(m->dim, 4);
+  int nkv = m->n_layer_kv_from_start;
+  s->n_kv_layers = nkv;
+  s->key_cache = (float **)calloc(nkv, sizeof(float *));
+  s->value_cache = (float **)calloc(nkv, sizeof(float *));
+  for (int l = 0; l < nkv; l++) {
+    s->key_cache[l] = (float *)calloc((size_t)m->ctx_len * kv_dim_of(m, l), 4);
+    s->value_cache[l] = (float *)calloc((size_t)m->ctx_len * kv_dim_of(m, l), 4);
+  }
+  size_t hf = (size_t)m->ctx_len * (m->head_size_full / 2), hs = (size_t)m->ctx_len * (m->head_size_swa / 2);
+  s->cr_full = (float *)malloc(hf * 4);
+  s->ci_full = (float *)malloc(hf * 4);
+  s->cr_swa = (float *)malloc(hs * 4);
+  s->ci_swa = (float *)malloc(hs * 4);
+  /* ModelLoader.loadWeights (ModelLoader.kt:154-166) */
+  o_rope_table(m->ctx_len, m->head_size_swa, (double)m->rope_theta_swa, NULL, s->cr_swa, s->ci_swa);
+  o_rope_table(m->ctx_len, m->head_size_full, (double)m->rope_theta, m->rope_freqs, s->cr_full, s->ci_full);
+  return s;
+}
+
+void o_state_free(o_state *s) {
+  if (!s) return;
+  free(s->x); free(s->xb); free(s->xbk); free(s->xb2); free(s->hb); free(s->hb2);
+  free(s->q); free(s->k); free(s->v); free(s->att); free(s->logits); free(s->moe_out);
+  free(s->cr_full); free(s->ci_full); free(s->cr_swa); free(s->ci_swa);
+  for (int l = 0; l < s->n_kv_layers; l++) {
+    free(s->key_cache[l]);
+    free(s->value_cache[l]);
+  }
+  free(s->key_cache);
+  free(s->value_cache);
+  free(s);
+}
+
+/* Llama.kt:39-59: rmsnorm with offsets: out = (weight * ss) * x, left to right */
+static void rmsnorm_off(float *out, const float *x, const float *w, int size, float eps) {
+  float ss = 0.0f;
+  for (int i = 0; i < size; i++) {
+    float sq = x[i] * x[i];
+    ss = ss + sq;
+  }
+  ss = ss / (float)size;
+  ss = ss + eps;
+  ss = (float)(1.0 / sqrt((double)ss));
+  for (int i = 0; i < size; i++) {
+    float t = w[i] * ss;
+    out[i] = t * x[i];
+  }
+}
+
+/* Llama.kt:62-81: bare RMS norm */
+static void rmsnorm_noweight(float *out, const float *x, int size, float eps) {
+  float ss = 0.0f;
+  for (int i = 0; i < size; i++) {
+    float sq = x[i] * x[i];
+    ss = ss + sq;
+  }
+  ss = ss / (float)size;
+  ss = ss + eps;
+  ss = (float)(1.0 / sqrt((double)ss));
+  for (int i = 0; i < size; i++) out[i] = ss * x[i];
+}
+
+/* Llama.kt:83-103 (NeoX pairs ic, ic + halfHead) */
+static void rope(float *v, int h, int head_size, const float *fr, const float *fi, int position) {
+  int half = head_size / 2, po = h * head_size;
+  for (int ic = 0; ic < half; ic++) {
+    float fcr = fr[(size_t)position * half + ic], fci = fi[(size_t)position * half + ic];
+    float v0 = v[po + ic], v1 = v[po + ic + half];
+    float a = v0 * fcr, b = v1 * fci;
+    float c = v0 * fci, d = v1 * fcr;
+    v[po + ic] = a - b;
+    v[po + ic + half] = c + d;
+  }
+}
+
+/* llama.VectorBitSize=0 runs every dot product through scalarDot
+ * (FloatTensorHelpers.kt:9-21, USE_VECTOR_API false); o_set_vector_api(0)
+ * selects that mode for the whole-model forward. */
+static int g_vector_api = 1;
+void o_set_vector_api(int on) { g_vector_api = on != 0; }
+
+/* ArrayFloatTensor.dot (ArrayFloatTensor.kt:48-87): 16-lane fma, reduceLanes,
+ * scalar tail; scalarDot when the Vector API is off */
+static float array_dot(const float *a, const float *b, int size) {
+  if (!g_vector_api) {
+    float r = 0.0f;
+    for (int i = 0; i < size; i++) {
+      float p = a[i] * b[i];
+      r = r + p;
+    }
+    return r;
+  }
+  float acc[LANES] = {0};
+  int upper = size / LANES * LANES;
+  for (int i = 0; i < upper; i += LANES)
+    for (int l = 0; l < LANES; l++) acc[l] = fmaf(a[i + l], b[i + l], acc[l]);
+  float r = reduce_lanes(acc);
+  for (int i = upper; i < size; i++) {
+    float p = a[i] * b[i];
+    r = r + p;
+  }
+  return r;
+}
+
+static void mm(const o_tensor *t, const float *x, float *out, int dim0, int dim1, int nthreads) {
+  o_matmul(t->type, t->data, 0, x, out, dim0, dim1, nthreads, g_vector_api);
+}
+
+int o_argmax(const float *v, int n) {
+  int best = 0;
+  float bv = v[0];
+  for (int i = 0; i < n; i++)
+    if (v[i] > bv) {
+      bv = v[i];
+      best = i;
+    }
+  return best;
+}
+
+const float *o_forward(const o_model *m, o_state *s, int token, int position, int nthreads) {
+  const int dim = m->dim;
+  const float sqrt_dim = (float)sqrt((double)dim);
+  /* Llama.kt:112-113 */
+  for (int i = 0; i < dim; i++) s->x[i] = o_get(m->tok_embd.type, m->tok_embd.data, (int64_t)token * dim + i);
+  for (int i = 0; i < dim; i++) s->x[i] = s->x[i] * sqrt_dim;
+
+  for (int l = 0; l < m->n_layers; l++) {
+    const o_layer *L = &m->layers[l];
+    const int swa = m->is_swa[l];
+    const int hs = head_size_of(m, l);
+    const int qdim = m->n_heads * hs, kvdim = kv_dim_of(m, l), hidden = m->ff[l];
+    const float *fr = swa ? s->cr_swa : s->cr_full, *fi = swa ? s->ci_swa : s->ci_full;
+    /* Llama.kt:155-161 */
+    o_rmsnorm(s->xb, s->x, L->attn_norm, dim, m->eps);
+    mm(&L->wq, s->xb, s->q, qdim, dim, nthreads);
+    for (int h = 0; h < m->n_heads; h++) rmsnorm_off(s->q + h * hs, s->q + h * hs, L->attn_q_norm, hs, m->eps);
+    for (int h = 0; h < m->n_heads; h++) rope(s->q, h, hs, fr, fi, position);
+    /* Llama.kt:170-196 */
+    const int kv_layer = l < m->n_layer_kv_from_start ? l : m->n_layer_kv_from_start - (swa ? 2 : 1);
+    const int nkv = m->n_kv_heads[l], kv_mul = m->n_heads / nkv;
+    if (l < m->n_layer_kv_from_start) {
+      mm(&L->wk, s->xb, s->k, kvdim, dim, nthreads);
+      if (L->wv.data) mm(&L->wv, s->xb, s->v, kvdim, dim, nthreads);
+      else memcpy(s->v, s->k, sizeof(float) * kvdim);
+      for (int h = 0; h < nkv; h++) {
+        rmsnorm_off(s->k + h * hs, s->k + h * hs, L->attn_k_norm, hs, m->eps);
+        rmsnorm_noweight(s->v + h * hs, s->v + h * hs, hs, m->eps);
+      }
+      for (int h = 0; h < nkv; h++) rope(s->k, h, hs, fr, fi, position);
+      memcpy(s->key_cache[kv_layer] + (size_t)position * kvdim, s->k, sizeof(float) * kvdim);
+      memcpy(s->value_cache[kv_layer] + (size_t)position * kvdim, s->v, sizeof(float) * kvdim);
+    }
+    /* Llama.kt:198-218 */
+    const int att_start = swa ? (position - m->sliding_window + 1 > 0 ? position - m->sliding_window + 1 : 0) : 0;
+    const float *kc = s->key_cache[kv_layer], *vc = s->value_cache[kv_layer];
+    for (int h = 0; h < m->n_heads; h++) {
+      float *att = s->att + (size_t)h * m->ctx_len;
+      for (int t = att_start; t <= position; t++)
+        att[t] = array_dot(s->q + h * hs, kc + (size_t)t * kvdim + (h / kv_mul) * hs, hs);
+      o_softmax(att + att_start, position - att_start + 1);
+      float *xo = s->xbk + h * hs;
+      for (int i = 0; i < hs; i++) xo[i] = 0.0f;
+      for (int t = att_start; t <= position; t++) {
+        const float *vv = vc + (size_t)t * kvdim + (h / kv_mul) * hs;
+        float a = att[t];
+        for (int i = 0; i < hs; i++) {
+          float p = a * vv[i];
+          xo[i] = p + xo[i];
+        }
+      }
+    }
+    /* Llama.kt:221-223 */
+    mm(&L->wo, s->xbk, s->xb2, dim, qdim, nthreads);
+    o_rmsnorm(s->xb2, s->xb2, L->post_attention_norm, dim, m->eps);
+    for (int i = 0; i < dim; i++) s->x[i] = s->x[i] + s->xb2[i];
+    /* Llama.kt:226-364 */
+    o_rmsnorm(s->xb, s->x, L->ffn_norm, dim, m->eps);
+    mm(&L->w1, s->xb, s->hb, hidden, dim, nthreads);
+    mm(&L->w3, s->xb, s->hb2, hidden, dim, nthreads);
+    for (int i = 0; i < hidden; i++) s->hb[i] = o_gelu(s->hb[i]);
+    for (int i = 0; i < hidden; i++) s->hb[i] = s->hb[i] * s->hb2[i];
+    mm(&L->w2, s->hb, s->xb, dim, hidden, nthreads);
+    if (m->n_expert > 0) {
+      o_rmsnorm(s->xb, s->xb, L->post_ffw_norm_1, dim, m->eps);
+      o_moe_weights mw = {dim, m->n_expert, m->n_expert_used, m->expert_ff, m->eps,
+                          L->gate_up_exps.type, L->down_exps.type, L->gate_inp.data, L->gate_inp_scale,
+                          L->gate_up_exps.data, L->down_exps.data, L->down_exps_scale, L->pre_ffw_norm_2,
+                          L->post_ffw_norm_2};
+      int32_t idx[64];
+      float prob[64];
+      o_moe_token(&mw, s->x, s->moe_out, idx, prob, NULL, nthreads);
+      for (int i = 0; i < dim; i++) s->xb[i] = s->xb[i] + s->moe_out[i];
+    }
+    o_rmsnorm(s->xb, s->xb, L->post_ffw_norm, dim, m->eps);
+    for (int i = 0; i < dim; i++) s->x[i] = s->x[i] + s->xb[i];
+    /* Llama.kt:393-397 */
+    const float sc = m->layer_scale[l];
+    if (sc != 1.0f)
+      for (int i = 0; i < dim; i++) s->x[i] = s->x[i] * sc;
+  }
+  /* Llama.kt:401-406 */
+  o_rmsnorm(s->x, s->x, m->output_norm, dim, m->eps);
+  const o_tensor *wcls = m->output.data ? &m->output : &m->tok_embd;
+  mm(wcls, s->x, s->logits, m->vocab, dim, nthreads);
+  if (m->logit_softcap > 0) {
+    const float cap = m->logit_softcap;
+    for (int i = 0; i < m->vocab; i++) {
+      float t = s->logits[i] / cap;
+      s->logits[i] = cap * (float)tanh((double)t);
+    }
+  }
+  return s->logits;
+}

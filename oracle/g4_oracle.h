@@ -103,6 +103,61 @@ void o_moe_token(const o_moe_weights *w, const float *x, float *out, int32_t *to
 /* Router stage only (Llama.kt:257-270): logits[n_expert] before softmax */
 void o_moe_router_logits(const o_moe_weights *w, const float *x, float *logits);
 
+/* ---------------- whole-model forward (Llama.kt:105-408) ----------------
+ * One token at one position through every layer, exactly as Llama.forward:
+ * embedding x sqrt(dim), per layer attention (RMSNorm, Q/K/V projections,
+ * per-head Q/K norms and bare V norm, NeoX RoPE from the precomputed tables,
+ * GQA attention with scale 1.0 over [attStart, position], shared KV for the
+ * layers past n_layer_kv_from_start), output projection, post-attention
+ * norm + residual, then the dense GELU FFN or the MoE block (shared MLP +
+ * experts + merge), layer output scale; final norm, logits, softcapping.
+ * Per-layer embeddings (Llama.kt:115-143,366-391) are not restated: the
+ * synthetic models of the benchmark have none. */
+typedef struct {
+  int type;             /* GGML type id */
+  const uint8_t *data;  /* block stream */
+} o_tensor;
+
+typedef struct {
+  const float *attn_norm, *attn_q_norm, *attn_k_norm, *post_attention_norm, *ffn_norm, *post_ffw_norm;
+  o_tensor wq, wk, wv, wo; /* wv.data == NULL: V = K (Llama.kt:176-181) */
+  o_tensor w1, w2, w3;     /* ffn_gate, ffn_down, ffn_up */
+  /* MoE layers only (Llama.kt:226-353) */
+  const float *post_ffw_norm_1, *pre_ffw_norm_2, *post_ffw_norm_2, *gate_inp_scale, *down_exps_scale;
+  o_tensor gate_inp, gate_up_exps, down_exps;
+} o_layer;
+
+typedef struct {
+  int dim, n_layers, n_heads, vocab, ctx_len;
+  int head_size_full, head_size_swa, sliding_window, n_layer_kv_from_start;
+  float eps, rope_theta, rope_theta_swa, logit_softcap;
+  int n_expert, n_expert_used, expert_ff; /* n_expert == 0: dense model */
+  const int *n_kv_heads;     /* [n_layers] */
+  const int *ff;             /* [n_layers] feed_forward_length */
+  const uint8_t *is_swa;     /* [n_layers] */
+  const float *layer_scale;  /* [n_layers] */
+  const float *rope_freqs;   /* [head_size_full/2] rope_freqs.weight */
+  o_tensor tok_embd, output; /* output.data == NULL: tied to tok_embd */
+  const float *output_norm;
+  const o_layer *layers;
+} o_model;
+
+typedef struct o_state o_state;
+
+/* RotaryPositionEmbeddings.precomputeFreqsCis (RotaryPositionEmbeddings.kt:8-27)
+ * and precomputeFreqsCisFromFreqs (:29-53): cr/ci [ctx * head/2]. */
+void o_rope_table(int ctx_len, int head_size, double theta, const float *freq_factors, float *cr, float *ci);
+
+o_state *o_state_new(const o_model *m);
+void o_state_free(o_state *s);
+/* Llama.forward(model, state, token, position); returns state.logits (vocab floats). */
+const float *o_forward(const o_model *m, o_state *s, int token, int position, int nthreads);
+/* FloatTensor.argmax (FloatTensor.kt:120-133): first index of the maximum. */
+int o_argmax(const float *v, int n);
+/* 1 (default): the Vector API dot products (512-bit branch); 0: scalarDot
+ * everywhere, the reference's llama.VectorBitSize=0 mode. */
+void o_set_vector_api(int on);
+
 #ifdef __cplusplus
 }
 #endif

@@ -142,3 +142,159 @@ class MoeOracle:
         out = np.empty(self.e, dtype=np.float32)
         lib().o_moe_router_logits(C.byref(self.w), _p(x), _p(out))
         return out
+
+
+# ---------------------------------------------------------------------- whole model
+class OTensor(C.Structure):
+    _fields_ = [("type", C.c_int), ("data", C.c_void_p)]
+
+
+class OLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("attn_norm", "attn_q_norm", "attn_k_norm", "post_attention_norm",
+                                          "ffn_norm", "post_ffw_norm")] + \
+               [(n, OTensor) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3")] + \
+               [(n, C.c_void_p) for n in ("post_ffw_norm_1", "pre_ffw_norm_2", "post_ffw_norm_2", "gate_inp_scale",
+                                          "down_exps_scale")] + \
+               [(n, OTensor) for n in ("gate_inp", "gate_up_exps", "down_exps")]
+
+
+class OModel(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("dim", "n_layers", "n_heads", "vocab", "ctx_len", "head_size_full",
+                                       "head_size_swa", "sliding_window", "n_layer_kv_from_start")] + \
+               [(n, C.c_float) for n in ("eps", "rope_theta", "rope_theta_swa", "logit_softcap")] + \
+               [(n, C.c_int) for n in ("n_expert", "n_expert_used", "expert_ff")] + \
+               [(n, C.c_void_p) for n in ("n_kv_heads", "ff", "is_swa", "layer_scale", "rope_freqs")] + \
+               [("tok_embd", OTensor), ("output", OTensor), ("output_norm", C.c_void_p),
+                ("layers", C.POINTER(OLayer))]
+
+
+def _model_lib():
+    L = lib()
+    if not getattr(L, "_model_sigs", False):
+        L.o_state_new.restype = C.c_void_p
+        L.o_state_new.argtypes = [C.POINTER(OModel)]
+        L.o_state_free.restype = None
+        L.o_state_free.argtypes = [C.c_void_p]
+        L.o_forward.restype = C.POINTER(C.c_float)
+        L.o_forward.argtypes = [C.POINTER(OModel), C.c_void_p, C.c_int, C.c_int, C.c_int]
+        L.o_argmax.restype = C.c_int
+        L.o_argmax.argtypes = [C.c_void_p, C.c_int]
+        L.o_set_vector_api.restype = None
+        L.o_set_vector_api.argtypes = [C.c_int]
+        L.o_rope_table.restype = None
+        L.o_rope_table.argtypes = [C.c_int, C.c_int, C.c_double, C.c_void_p, C.c_void_p, C.c_void_p]
+        L._model_sigs = True
+    return L
+
+
+def set_vector_api(on: bool) -> None:
+    """Whole-model forward: Vector-API dot products (True, default) or the
+    reference's scalarDot mode (llama.VectorBitSize=0)."""
+    _model_lib().o_set_vector_api(1 if on else 0)
+
+
+class ModelOracle:
+    """Llama.forward restated on the CPU over a model's raw tensors
+    (src: gemma4_kt_b200.model.TensorSource).  One state (KV cache) per
+    instance; call step() with positions 0, 1, 2, ... like generateTokens."""
+
+    def __init__(self, src, context_length: int = -1, threads: int | None = None):
+        from gemma4_kt_b200.model import layer_scales  # host mirror of the loader's scale lookup
+
+        cfg = src.config(context_length)
+        self.cfg = cfg
+        self.threads = threads or os.cpu_count() or 1
+        keep = self._keep = []
+
+        def ptr(a):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a)
+            keep.append(a)
+            return a.ctypes.data
+
+        def ten(name):
+            if not src.has(name):
+                return OTensor(0, None)
+            return OTensor(int(src.type(name)), ptr(np.asarray(src.raw(name)).view(np.uint8)))
+
+        def f32(name):
+            v = src.f32(name)
+            return ptr(v) if v is not None else None
+
+        L = cfg.n_layers
+        layers = (OLayer * L)()
+        for i in range(L):
+            p = f"blk.{i}."
+            ly = layers[i]
+            ly.attn_norm, ly.attn_q_norm = f32(p + "attn_norm.weight"), f32(p + "attn_q_norm.weight")
+            ly.attn_k_norm = f32(p + "attn_k_norm.weight")
+            ly.post_attention_norm, ly.ffn_norm = f32(p + "post_attention_norm.weight"), f32(p + "ffn_norm.weight")
+            ly.post_ffw_norm = f32(p + "post_ffw_norm.weight")
+            ly.wq, ly.wk, ly.wv = ten(p + "attn_q.weight"), ten(p + "attn_k.weight"), ten(p + "attn_v.weight")
+            ly.wo = ten(p + "attn_output.weight")
+            ly.w1, ly.w2, ly.w3 = ten(p + "ffn_gate.weight"), ten(p + "ffn_down.weight"), ten(p + "ffn_up.weight")
+            if cfg.n_expert:
+                ly.post_ffw_norm_1 = f32(p + "post_ffw_norm_1.weight")
+                ly.pre_ffw_norm_2 = f32(p + "pre_ffw_norm_2.weight")
+                ly.post_ffw_norm_2 = f32(p + "post_ffw_norm_2.weight")
+                ly.gate_inp_scale = f32(p + "ffn_gate_inp.scale")
+                ly.down_exps_scale = f32(p + "ffn_down_exps.scale")
+                ly.gate_inp = ten(p + "ffn_gate_inp.weight")
+                ly.gate_up_exps, ly.down_exps = ten(p + "ffn_gate_up_exps.weight"), ten(p + "ffn_down_exps.weight")
+        keep.append(layers)
+        m = OModel()
+        m.dim, m.n_layers, m.n_heads, m.vocab, m.ctx_len = cfg.dim, L, cfg.n_heads, cfg.vocab, cfg.ctx_len
+        m.head_size_full, m.head_size_swa, m.sliding_window = cfg.head_size_full, cfg.head_size_swa, cfg.sliding_window
+        m.n_layer_kv_from_start = cfg.n_layer_kv_from_start
+        m.eps, m.rope_theta, m.rope_theta_swa = cfg.eps, cfg.rope_theta, cfg.rope_theta_swa
+        m.logit_softcap = cfg.logit_softcap
+        m.n_expert, m.n_expert_used, m.expert_ff = cfg.n_expert, cfg.n_expert_used, cfg.expert_ff
+        m.n_kv_heads = ptr(np.array(cfg.n_kv_heads, np.int32))
+        m.ff = ptr(np.array(cfg.ff, np.int32))
+        m.is_swa = ptr(np.array(cfg.is_swa, np.uint8))
+        m.layer_scale = ptr(layer_scales(cfg, src.f32))
+        m.rope_freqs = f32("rope_freqs.weight")
+        m.tok_embd = ten("token_embd.weight")
+        m.output = ten("output.weight")
+        m.output_norm = f32("output_norm.weight")
+        m.layers = layers
+        self.m = m
+        self.state = _model_lib().o_state_new(C.byref(m))
+
+    def close(self):
+        if self.state:
+            _model_lib().o_state_free(self.state)
+            self.state = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def step(self, token: int, position: int) -> np.ndarray:
+        """Llama.forward: logits (a copy) for `token` at `position`."""
+        p = _model_lib().o_forward(C.byref(self.m), self.state, int(token), int(position), self.threads)
+        return np.ctypeslib.as_array(p, shape=(self.cfg.vocab,)).copy()
+
+    def greedy(self, prompt, n_generate: int, bos: int = 2, collect_logits: bool = False):
+        """Llama.generateTokens with the ARGMAX sampler, stop tokens ignored:
+        BOS at position 0, prompt[i] at position i + 1, then n_generate greedy
+        tokens.  Returns the generated ids (and every position's logits)."""
+        token, out, logits = bos, [], []
+        pos = 0
+        for t in list(prompt):
+            lg = self.step(token, pos)
+            if collect_logits:
+                logits.append(lg)
+            token = int(t)
+            pos += 1
+        for _ in range(n_generate):
+            lg = self.step(token, pos)
+            if collect_logits:
+                logits.append(lg)
+            token = int(np.argmax(lg))  # first maximum, as FloatTensor.argmax
+            out.append(token)
+            pos += 1
+        return (np.array(out, np.int32), logits) if collect_logits else np.array(out, np.int32)
