@@ -51,6 +51,18 @@ SIGNATURES = {
     "g4_dist_rank": (_i, [_vp]),
     "g4_dist_world": (_i, [_vp]),
     "g4_matmul_sharded": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "g4_model_create": (_i, [_vp, _vp, C.POINTER(_vp)]),
+    "g4_model_set_tensor": (_i, [_vp, C.c_char_p, _i, _vp, _u64, _u64]),
+    "g4_model_finalize": (_i, [_vp]),
+    "g4_model_free": (_i, [_vp]),
+    "g4_state_create": (_i, [_vp, C.POINTER(_vp)]),
+    "g4_state_free": (_i, [_vp]),
+    "g4_decode_step": (_i, [_vp, _i, _i, _vp, _vp]),
+    "g4_decode_greedy": (_i, [_vp, _vp, _i, _i, _i, _vp]),
+    "g4_decode_stage": (_i, [_vp, _vp, _vp, _i]),
+    "g4_decode_enqueue": (_i, [_vp, _i]),
+    "g4_decode_read_tokens": (_i, [_vp, _i, _i, _vp]),
+    "g4_state_stream": (_vp, [_vp]),
 }
 
 
@@ -75,6 +87,16 @@ class MoeWeightsStruct(C.Structure):
         ("pre_ffw_norm_2", C.c_void_p),
         ("post_ffw_norm_2", C.c_void_p),
     ]
+
+
+class ModelConfigStruct(C.Structure):
+    """g4_model_config (include/g4.h)."""
+
+    _fields_ = [(n, C.c_int) for n in ("dim", "n_layers", "n_heads", "vocab", "ctx_len", "head_size_full",
+                                       "head_size_swa", "sliding_window", "n_layer_kv_from_start")] + \
+               [(n, C.c_float) for n in ("eps", "rope_theta", "rope_theta_swa", "logit_softcap")] + \
+               [(n, C.c_int) for n in ("n_expert", "n_expert_used", "expert_ff")] + \
+               [("n_kv_heads", C.c_void_p), ("ff", C.c_void_p), ("is_swa", C.c_void_p)]
 
 
 _lib = None

@@ -1,0 +1,1085 @@
+// g4_decode.cu -- GPU-resident Llama.forward (Llama.kt:105-408) and the greedy
+// decode loop of Llama.generateTokens (Llama.kt:413-477), on sm_100a.
+//
+// One decode step (one token at one position) is one CUDA graph of, per layer:
+//
+//   qkv GEMV     prologue: previous layer's residual + post-FFN norm + layer
+//                scale (or the embedding x sqrt(dim) at layer 0), then
+//                rmsnorm(attn_norm); rows q | k | v of one fused tensor
+//   attention    per (KV head, position chunk) CTA: Q/K norms, NeoX RoPE, K/V
+//                into the cache, scores (scale 1.0), softmax partials, V sum;
+//                the last CTA of each KV head (ticket) combines the chunks
+//   wo GEMV      plain
+//   gate/up GEMV prologue: residual + post-attention norm, rmsnorm(ffn_norm);
+//                rows interleaved gate_i, up_i; epilogue gelu(gate) * up
+//   down GEMV    plain (the shared MLP of a MoE layer)
+//   [MoE layers: the expert half (g4_moe.cu kernels) on the residual stream;
+//    the next layer's qkv prologue merges shared + expert outputs]
+//
+// then the logits GEMV (final residual, output_norm, softcapping, argmax as
+// an atomicMax key) and a one-thread sampling kernel that records the argmax
+// and feeds it to the next step.  Every kernel after the first is launched
+// with programmatic stream serialization: a GEMV streams its first weight
+// stages before waiting for its predecessor.  The step index, the input token
+// and the position live in device memory, so a greedy generation of N tokens
+// is N graph launches with no host round trip.  The GEMVs use two-part int16
+// activations (fp32-level products): with attention scale 1.0 on normalised
+// q and k, activation errors of a few 1e-5 visibly move the attention weights.
+#include "g4.h"
+#include "g4_ctx.h"
+#include "g4_gemv.cuh"
+#include "g4_internal.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+#include <vector>
+
+namespace g4 {
+
+constexpr int kAttnChunks = 32;  // position chunks (CTAs) per KV head
+constexpr int kAttnThreads = 256;
+constexpr int kTicketStride = 64;  // ticket words per layer (KV heads <= 64)
+
+struct AttnArgs {
+  const float* qkv;        // raw projections: q [n_heads*hs] | k [n_kv*hs] | v [n_kv*hs]
+  int hs, n_kv, kv_mul, qdim, kvdim;
+  int k_off, v_off;        // offsets of k and v in qkv (v_off == k_off when V = K)
+  const float* q_norm;     // [hs]
+  const float* k_norm;     // [hs]
+  float eps;
+  const float* cr;         // rope tables [ctx][hs/2] of this layer's attention type
+  const float* ci;
+  float* kc;               // KV cache of the layer's KV source layer [ctx][kvdim]
+  float* vc;
+  int write_kv;            // the layer has its own KV (Llama.kt:174)
+  int window;              // sliding window (0: full attention)
+  const int* step;
+  const int* in_pos;
+  float* part;             // [n_kv][kAttnChunks][kv_mul][hs + 2]
+  unsigned* ticket;        // [n_kv]
+  float* out;              // [qdim]
+  int max_chunk;           // capacity of a score row (positions per chunk at the full context)
+};
+
+// Llama.kt:39-59 per-head rmsnorm, (w * ss) * x left to right (w == nullptr:
+// the bare norm of Llama.kt:62-81); one warp per head vector in shared memory.
+__device__ __forceinline__ void head_rmsnorm(float* v, const float* w, int hs, float eps, int lane) {
+  float ss = 0.f;
+  for (int i = lane; i < hs; i += 32) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+  const float s = rms_scale(warp_sum(ss), hs, eps);
+  __syncwarp();
+  for (int i = lane; i < hs; i += 32) v[i] = w ? __fmul_rn(__fmul_rn(w[i], s), v[i]) : __fmul_rn(s, v[i]);
+  __syncwarp();
+}
+
+// Llama.kt:83-103: pairs (ic, ic + hs/2)
+__device__ __forceinline__ void head_rope(float* v, const float* fr, const float* fi, int hs, int lane) {
+  const int half = hs / 2;
+  for (int ic = lane; ic < half; ic += 32) {
+    const float fcr = fr[ic], fci = fi[ic];
+    const float v0 = v[ic], v1 = v[ic + half];
+    v[ic] = __fsub_rn(__fmul_rn(v0, fcr), __fmul_rn(v1, fci));
+    v[ic + half] = __fadd_rn(__fmul_rn(v0, fci), __fmul_rn(v1, fcr));
+  }
+  __syncwarp();
+}
+
+// Attention of one layer (Llama.kt:157-218) for the KV-head group g and the
+// position chunk c of this CTA.  KVM = query heads per KV head.
+template <int KVM>
+__global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int hs = a.hs;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, NW = kAttnThreads / 32;
+  const int pos = a.in_pos[*a.step];
+  const int start = a.window > 0 ? max(0, pos - a.window + 1) : 0;
+  const int len = pos - start + 1;
+  int ch = (len + kAttnChunks - 1) / kAttnChunks;
+  ch = max(8, (ch + 7) / 8 * 8);
+  const int nch = (len + ch - 1) / ch;
+  const int g = blockIdx.x / kAttnChunks, c = blockIdx.x % kAttnChunks;
+  if (c >= nch) return;
+  const int t0 = start + c * ch, t1 = min(t0 + ch, pos + 1);
+  const int scs = max(a.max_chunk, kAttnChunks);
+  float* qs = sm;                 // [KVM][hs]
+  float* kp = qs + KVM * hs;      // [hs] k at pos
+  float* vp = kp + hs;            // [hs] v at pos
+  float* sc = vp + hs;            // [KVM][max_chunk] scores, then exp; later [KVM][kAttnChunks] chunk weights
+  float* st = sc + KVM * scs;     // [KVM] max, [KVM] sum, flag, pad, [KVM] denominators
+  const float* fr = a.cr + (size_t)pos * (hs / 2);
+  const float* fi = a.ci + (size_t)pos * (hs / 2);
+
+  // q of the group's heads: per-head norm and RoPE (Llama.kt:158-168)
+  for (int i = tid; i < KVM * hs; i += kAttnThreads) qs[i] = a.qkv[(size_t)g * KVM * hs + i];
+  const bool own_pos = t1 == pos + 1 && a.write_kv;  // this CTA computes and stores the new K/V row
+  if (own_pos)
+    for (int i = tid; i < hs; i += kAttnThreads) {
+      kp[i] = a.qkv[a.k_off + (size_t)g * hs + i];
+      vp[i] = a.qkv[a.v_off + (size_t)g * hs + i];
+    }
+  __syncthreads();
+  for (int h = warp; h < KVM; h += NW) {
+    head_rmsnorm(qs + h * hs, a.q_norm, hs, a.eps, lane);
+    head_rope(qs + h * hs, fr, fi, hs, lane);
+  }
+  if (own_pos) {
+    // K: learned norm then RoPE; V: bare norm (Llama.kt:183-195)
+    if (warp == NW - 1) {
+      head_rmsnorm(kp, a.k_norm, hs, a.eps, lane);
+      head_rope(kp, fr, fi, hs, lane);
+    } else if (warp == NW - 2) {
+      head_rmsnorm(vp, nullptr, hs, a.eps, lane);
+    }
+  }
+  __syncthreads();
+  if (own_pos)
+    for (int i = tid; i < hs; i += kAttnThreads) {
+      a.kc[(size_t)pos * a.kvdim + (size_t)g * hs + i] = kp[i];
+      a.vc[(size_t)pos * a.kvdim + (size_t)g * hs + i] = vp[i];
+    }
+
+  // scores q_h . k_t (Llama.kt:204-208)
+  const int n = t1 - t0;
+  for (int j = warp; j < n; j += NW) {
+    const int t = t0 + j;
+    const float* kt = (own_pos && t == pos) ? kp : a.kc + (size_t)t * a.kvdim + (size_t)g * hs;
+    float acc[KVM];
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) acc[h] = 0.f;
+    for (int i = lane; i < hs; i += 32) {
+      const float kv = kt[i];
+#pragma unroll
+      for (int h = 0; h < KVM; ++h) acc[h] = fmaf(qs[h * hs + i], kv, acc[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) {
+      const float s = warp_sum(acc[h]);
+      if (lane == 0) sc[h * a.max_chunk + j] = s;
+    }
+  }
+  __syncthreads();
+  // chunk softmax statistics: exp((s - m) as double), as softmaxInPlace (MutableFloatTensor.kt:54-59)
+  for (int h = warp; h < KVM; h += NW) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * a.max_chunk + j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float e = (float)exp((double)__fsub_rn(sc[h * a.max_chunk + j], m));
+      sc[h * a.max_chunk + j] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      st[h] = m;
+      st[KVM + h] = l;
+    }
+  }
+  __syncthreads();
+  // partial V sums (Llama.kt:211-217)
+  float* part = a.part + ((size_t)g * kAttnChunks + c) * KVM * (hs + 2);
+  for (int d = tid; d < hs; d += kAttnThreads) {
+    float acc[KVM];
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) acc[h] = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const int t = t0 + j;
+      const float vv = (own_pos && t == pos) ? vp[d] : a.vc[(size_t)t * a.kvdim + (size_t)g * hs + d];
+#pragma unroll
+      for (int h = 0; h < KVM; ++h) acc[h] = fmaf(sc[h * a.max_chunk + j], vv, acc[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < KVM; ++h) part[(size_t)h * (hs + 2) + 2 + d] = acc[h];
+  }
+  if (tid < KVM) {
+    part[(size_t)tid * (hs + 2)] = st[tid];
+    part[(size_t)tid * (hs + 2) + 1] = st[KVM + tid];
+  }
+  // the last CTA of the group combines the chunks (threadfence reduction)
+  __threadfence();
+  __syncthreads();
+  int* flag = reinterpret_cast<int*>(st + 2 * KVM);
+  if (tid == 0) flag[0] = atomicAdd(&a.ticket[g], 1u) == (unsigned)(nch - 1);
+  __syncthreads();
+  if (!flag[0]) return;
+  __threadfence();
+  const float* pg = a.part + (size_t)g * kAttnChunks * KVM * (hs + 2);
+  float* wt = sc;  // [KVM][kAttnChunks] chunk weights exp(m_c - M)
+  for (int i = tid; i < KVM * nch; i += kAttnThreads) {
+    const int h = i / nch, cc = i % nch;
+    float M = -INFINITY;
+    for (int k = 0; k < nch; ++k) M = fmaxf(M, __ldcg(pg + ((size_t)k * KVM + h) * (hs + 2)));
+    wt[h * kAttnChunks + cc] = (float)exp((double)__fsub_rn(__ldcg(pg + ((size_t)cc * KVM + h) * (hs + 2)), M));
+  }
+  __syncthreads();
+  float* den = st + 2 * KVM + 4;
+  if (tid < KVM) {
+    float dsum = 0.f;
+    for (int k = 0; k < nch; ++k)
+      dsum = fmaf(wt[tid * kAttnChunks + k], __ldcg(pg + ((size_t)k * KVM + tid) * (hs + 2) + 1), dsum);
+    den[tid] = dsum;
+  }
+  __syncthreads();
+  for (int i = tid; i < KVM * hs; i += kAttnThreads) {
+    const int h = i / hs, d = i % hs;
+    float num = 0.f;
+    for (int k = 0; k < nch; ++k)
+      num = fmaf(wt[h * kAttnChunks + k], __ldcg(pg + ((size_t)k * KVM + h) * (hs + 2) + 2 + d), num);
+    a.out[(size_t)(g * KVM + h) * hs + d] = __fdiv_rn(num, den[h]);
+  }
+  if (tid == 0) a.ticket[g] = 0u;
+}
+
+// Greedy sampling (Sampler.ARGMAX, FloatTensor.argmax): the logits GEMV left
+// the maximum's key; record the token, feed it to the next step, reset.
+__global__ void dec_sample_kernel(int* ctl, int* out_tok, unsigned long long* argmax) {
+  grid_dep_wait();
+  if (threadIdx.x == 0) {
+    const int s = ctl[0];
+    const unsigned long long k = *argmax;
+    const int tok = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    out_tok[s] = tok;
+    ctl[1] = tok;
+    ctl[0] = s + 1;
+    *argmax = 0ull;
+  }
+}
+
+}  // namespace g4
+
+using namespace g4;
+
+// ---------------------------------------------------------------- host side
+namespace {
+
+struct LayerDev {
+  int hs = 0, qdim = 0, kvdim = 0, n_kv = 0, ff = 0, has_v = 0, swa = 0, kv_src = 0;
+  float scale = 1.f;
+  g4_tensor* qkv = nullptr;      // rows q | k | v
+  g4_tensor* wo = nullptr;
+  g4_tensor* gate_up = nullptr;  // rows interleaved gate_i, up_i
+  g4_tensor* down = nullptr;
+  const float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn_norm = nullptr;
+  const float *ffn_norm = nullptr, *post_ffw_norm = nullptr, *post_ffw_norm_1 = nullptr;
+  g4_moe_weights moe{};
+  GemvPlan p_qkv{}, p_wo{}, p_gu{}, p_down{};
+};
+
+const char* kLayerNames[] = {
+    "attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight",
+    "attn_q_norm.weight", "attn_k_norm.weight", "post_attention_norm.weight", "ffn_norm.weight",
+    "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight", "post_ffw_norm.weight", "layer_output_scale.weight",
+    "post_ffw_norm_1.weight", "pre_ffw_norm_2.weight", "post_ffw_norm_2.weight", "ffn_gate_inp.weight",
+    "ffn_gate_inp.scale", "ffn_gate_up_exps.weight", "ffn_down_exps.weight", "ffn_down_exps.scale"};
+
+}  // namespace
+
+struct g4_model {
+  g4_ctx* ctx = nullptr;
+  g4_model_config cfg{};
+  std::vector<int> n_kv, ff;
+  std::vector<unsigned char> is_swa;
+  std::map<std::string, g4_tensor*> t;  // uploaded tensors by GGUF name
+  std::vector<float> layer_scale;
+  std::vector<float> rope_freqs;
+  std::vector<LayerDev> L;
+  const g4_tensor* wcls = nullptr;
+  GemvPlan p_logits{};
+  float *cr_full = nullptr, *ci_full = nullptr, *cr_swa = nullptr, *ci_swa = nullptr;
+  bool finalized = false;
+  int max_q = 0, max_kv = 0, max_ff = 0, max_hs = 0, max_kvm = 0;
+
+  const g4_tensor* get(const std::string& n) const {
+    auto it = t.find(n);
+    return it == t.end() ? nullptr : it->second;
+  }
+  const float* f32(const std::string& n) const {
+    const g4_tensor* x = get(n);
+    return x ? static_cast<const float*>(x->d) : nullptr;
+  }
+};
+
+struct g4_state {
+  g4_model* m = nullptr;
+  cudaStream_t st = nullptr;
+  float* buf = nullptr;  // one allocation for the activations and the KV cache
+  float *x[2] = {nullptr, nullptr}, *qkv = nullptr, *xbk = nullptr, *xb2 = nullptr, *hb = nullptr, *sh = nullptr;
+  float *moe_out = nullptr, *logits = nullptr, *part = nullptr;
+  std::vector<float*> kc, vc;
+  uint8_t* small = nullptr;     // argmax key, tickets, step control
+  unsigned* tickets = nullptr;
+  unsigned long long* argmax = nullptr;
+  int* ctl = nullptr;     // [0] step, [1] next token, then in_tok[ctx], in_pos[ctx], out_tok[ctx]
+  int* h_ctl = nullptr;   // pinned staging of the same layout
+  cudaGraphExec_t graph = nullptr;
+  int* in_tok() const { return ctl + 4; }
+  int* in_pos() const { return ctl + 4 + m->cfg.ctx_len; }
+  int* out_tok() const { return ctl + 4 + 2 * m->cfg.ctx_len; }
+};
+
+static int tensor_ok_n(const g4_tensor* t, int type, uint64_t n) {
+  return t && (type < 0 || t->type == type) && t->n_elems == n;
+}
+
+extern "C" {
+
+int g4_model_create(g4_ctx* c, const g4_model_config* cfg, g4_model** out) {
+  if (!c) return G4_E_ARG;
+  if (!cfg || !out || !cfg->n_kv_heads || !cfg->ff || !cfg->is_swa) {
+    c->set_err("g4_model_create: NULL argument");
+    return G4_E_ARG;
+  }
+  const g4_model_config& k = *cfg;
+  if (k.dim <= 0 || k.dim % 32 || k.n_layers <= 0 || k.n_heads <= 0 || k.vocab <= 0 || k.ctx_len <= 0 ||
+      k.head_size_full <= 0 || k.head_size_swa <= 0 || k.head_size_full % 2 || k.head_size_swa % 2 ||
+      k.n_layer_kv_from_start < 1 || k.n_layer_kv_from_start > k.n_layers || k.dim > 16384) {
+    c->set_err("g4_model_create: unsupported configuration");
+    return G4_E_ARG;
+  }
+  g4_model* m = new (std::nothrow) g4_model();
+  if (!m) return G4_E_NOMEM;
+  m->ctx = c;
+  m->cfg = k;
+  m->n_kv.assign(k.n_kv_heads, k.n_kv_heads + k.n_layers);
+  m->ff.assign(k.ff, k.ff + k.n_layers);
+  m->is_swa.assign(k.is_swa, k.is_swa + k.n_layers);
+  m->cfg.n_kv_heads = m->n_kv.data();
+  m->cfg.ff = m->ff.data();
+  m->cfg.is_swa = m->is_swa.data();
+  m->layer_scale.assign(k.n_layers, 1.f);
+  for (int l = 0; l < k.n_layers; ++l) {
+    const int hs = m->is_swa[l] ? k.head_size_swa : k.head_size_full;
+    if (m->n_kv[l] <= 0 || m->n_kv[l] > kTicketStride || k.n_heads % m->n_kv[l] || m->ff[l] <= 0) {
+      delete m;
+      c->set_err("g4_model_create: layer %d: bad KV head count (1..%d dividing the heads) or FFN width", l,
+                 kTicketStride);
+      return G4_E_ARG;
+    }
+    const int kvm = k.n_heads / m->n_kv[l];
+    if (kvm != 1 && kvm != 2 && kvm != 4 && kvm != 8 && kvm != 16) {
+      delete m;
+      c->set_err("g4_model_create: %d query heads per KV head is not supported", kvm);
+      return G4_E_ARG;
+    }
+    m->max_q = std::max(m->max_q, k.n_heads * hs);
+    m->max_kv = std::max(m->max_kv, m->n_kv[l] * hs);
+    m->max_ff = std::max(m->max_ff, m->ff[l]);
+    m->max_hs = std::max(m->max_hs, hs);
+    m->max_kvm = std::max(m->max_kvm, kvm);
+  }
+  *out = m;
+  return 0;
+}
+
+int g4_model_set_tensor(g4_model* m, const char* name, int ggml_type, const void* host, uint64_t nbytes,
+                        uint64_t n_elems) {
+  if (!m) return G4_E_ARG;
+  g4_ctx* c = m->ctx;
+  if (!name || !host) {
+    c->set_err("g4_model_set_tensor: NULL argument");
+    return G4_E_ARG;
+  }
+  if (m->finalized) {
+    c->set_err("g4_model_set_tensor: the model is already finalized");
+    return G4_E_ARG;
+  }
+  const std::string n(name);
+  bool known = n == "token_embd.weight" || n == "output.weight" || n == "output_norm.weight" ||
+               n == "rope_freqs.weight";
+  if (!known && n.rfind("blk.", 0) == 0) {
+    const size_t dot = n.find('.', 4);
+    if (dot != std::string::npos) {
+      const std::string suffix = n.substr(dot + 1);
+      for (const char* s : kLayerNames) known = known || suffix == s;
+      const int l = atoi(n.substr(4, dot - 4).c_str());
+      known = known && l >= 0 && l < m->cfg.n_layers;
+    }
+  }
+  if (!known) {
+    // per-layer embeddings (Llama.kt:115-143,366-391) and anything else the
+    // decoder does not compute
+    c->set_err("g4_model_set_tensor: tensor %s is not used by this decoder", name);
+    return G4_E_TYPE;
+  }
+  static const std::string kScale = "layer_output_scale.weight";
+  if (n.size() > kScale.size() && n.compare(n.size() - kScale.size(), kScale.size(), kScale) == 0) {
+    if (ggml_type != G4_TYPE_F32 || n_elems < 1) {
+      c->set_err("g4_model_set_tensor: %s must be F32", name);
+      return G4_E_TYPE;
+    }
+    const int l = atoi(n.c_str() + 4);
+    memcpy(&m->layer_scale[l], host, 4);  // ModelLoader.kt:179-188
+    return 0;
+  }
+  if (n == "rope_freqs.weight") {
+    if (ggml_type != G4_TYPE_F32 || n_elems != (uint64_t)m->cfg.head_size_full / 2) {
+      c->set_err("g4_model_set_tensor: rope_freqs.weight must be F32[%d]", m->cfg.head_size_full / 2);
+      return G4_E_ARG;
+    }
+    m->rope_freqs.assign((const float*)host, (const float*)host + n_elems);
+    return 0;
+  }
+  auto it = m->t.find(n);
+  if (it != m->t.end()) {
+    g4_tensor_free(it->second);
+    m->t.erase(it);
+  }
+  g4_tensor* t = nullptr;
+  if (int r = g4_tensor_upload(c, ggml_type, host, nbytes, n_elems, &t)) return r;
+  m->t[n] = t;
+  return 0;
+}
+
+}  // extern "C"
+
+// RotaryPositionEmbeddings.kt:8-53 (ff == nullptr: precomputeFreqsCis)
+static void rope_table(int ctx, int hs, double theta, const float* ff, std::vector<float>& cr,
+                       std::vector<float>& ci) {
+  const int half = hs / 2;
+  cr.resize((size_t)ctx * half);
+  ci.resize((size_t)ctx * half);
+  size_t n = 0;
+  for (int pos = 0; pos < ctx; ++pos)
+    for (int i = 0; i < half; ++i) {
+      float value;
+      if (ff) {
+        const float base = (float)(1.0 / pow(theta, (2.0 * i) / hs));
+        value = (float)pos * base;
+        value = value / ff[i];
+      } else {
+        const float freq = (float)(1.0 / pow(theta, (double)(2 * i) / (double)hs));
+        value = (float)pos * freq;
+      }
+      cr[n] = (float)cos((double)value);
+      ci[n] = (float)sin((double)value);
+      ++n;
+    }
+}
+
+static int upload_f32(g4_ctx* c, const std::vector<float>& v, float** out) {
+  if (cudaMalloc(out, v.size() * 4 + 256) != cudaSuccess) {
+    cudaGetLastError();
+    *out = nullptr;
+    c->set_err("decoder: cannot allocate %zu bytes", v.size() * 4);
+    return G4_E_NOMEM;
+  }
+  if (cudaError_t e = cudaMemcpy(*out, v.data(), v.size() * 4, cudaMemcpyHostToDevice))
+    return c->cuda_fail(e, "decoder upload");
+  return 0;
+}
+
+// A device tensor holding the rows of several same-type tensors: rows of
+// `parts` one after the other (interleave false), or row i of every part in
+// turn (interleave true: gate_0, up_0, gate_1, up_1, ...).
+static int fuse_rows(g4_ctx* c, const std::vector<const g4_tensor*>& parts, int cols, bool interleave,
+                     g4_tensor** out) {
+  const int type = parts[0]->type;
+  const uint64_t BS = block_size(type), TS = type_size(type);
+  if (cols % BS) {
+    c->set_err("decoder: rows of %d elements do not hold whole %llu-element blocks", cols, (unsigned long long)BS);
+    return G4_E_TYPE;
+  }
+  const size_t row_bytes = (size_t)cols / BS * TS;
+  uint64_t n = 0, bytes = 0;
+  for (const g4_tensor* p : parts) {
+    if (p->type != type) {
+      c->set_err("decoder: fused projections need one GGML type (got %d and %d)", type, p->type);
+      return G4_E_TYPE;
+    }
+    n += p->n_elems;
+    bytes += p->nbytes;
+  }
+  g4_tensor* t = new (std::nothrow) g4_tensor();
+  if (!t) return G4_E_NOMEM;
+  const size_t alloc = (bytes + 255) / 256 * 256 + 256;
+  if (cudaMalloc(&t->d, alloc) != cudaSuccess) {
+    cudaGetLastError();
+    delete t;
+    c->set_err("decoder: cannot allocate %zu bytes", alloc);
+    return G4_E_NOMEM;
+  }
+  cudaMemset(t->d, 0, alloc);
+  uint8_t* dst = (uint8_t*)t->d;
+  cudaError_t e = cudaSuccess;
+  if (!interleave) {
+    size_t o = 0;
+    for (const g4_tensor* p : parts) {
+      e = cudaMemcpy(dst + o, p->d, p->nbytes, cudaMemcpyDeviceToDevice);
+      o += p->nbytes;
+      if (e) break;
+    }
+  } else {
+    const size_t k = parts.size();
+    for (size_t i = 0; i < k && !e; ++i)
+      e = cudaMemcpy2D(dst + i * row_bytes, k * row_bytes, parts[i]->d, row_bytes, row_bytes,
+                       parts[i]->nbytes / row_bytes, cudaMemcpyDeviceToDevice);
+  }
+  if (e) {
+    cudaFree(t->d);
+    delete t;
+    return c->cuda_fail(e, "decoder: fusing projections");
+  }
+  t->ctx = c;
+  t->type = type;
+  t->nbytes = bytes;
+  t->n_elems = n;
+  *out = t;
+  return 0;
+}
+
+static void drop(g4_model* m, const std::string& n) {
+  auto it = m->t.find(n);
+  if (it != m->t.end()) {
+    g4_tensor_free(it->second);
+    m->t.erase(it);
+  }
+}
+
+extern "C" int g4_model_finalize(g4_model* m) {
+  if (!m) return G4_E_ARG;
+  g4_ctx* c = m->ctx;
+  if (m->finalized) return 0;
+  if (int r = c->bind()) return r;
+  const g4_model_config& k = m->cfg;
+  const int dim = k.dim;
+  auto need = [&](const std::string& n, int type, uint64_t elems) -> bool {
+    if (!tensor_ok_n(m->get(n), type, elems)) {
+      c->set_err("g4_model_finalize: tensor %s missing or of the wrong type/size (%llu elements expected)", n.c_str(),
+                 (unsigned long long)elems);
+      return false;
+    }
+    return true;
+  };
+  if (!need("token_embd.weight", -1, (uint64_t)dim * k.vocab) || !need("output_norm.weight", G4_TYPE_F32, dim))
+    return G4_E_ARG;
+  m->wcls = m->get("output.weight") ? m->get("output.weight") : m->get("token_embd.weight");
+  if (m->wcls->n_elems != (uint64_t)dim * k.vocab) {
+    c->set_err("g4_model_finalize: output.weight has the wrong size");
+    return G4_E_ARG;
+  }
+  if ((int)m->rope_freqs.size() != k.head_size_full / 2) {
+    c->set_err("g4_model_finalize: rope_freqs.weight missing (ModelLoader.kt:156)");
+    return G4_E_ARG;
+  }
+  m->L.resize(k.n_layers);
+  for (int l = 0; l < k.n_layers; ++l) {
+    LayerDev& L = m->L[l];
+    const std::string p = "blk." + std::to_string(l) + ".";
+    L.swa = m->is_swa[l] != 0;
+    L.hs = L.swa ? k.head_size_swa : k.head_size_full;
+    L.n_kv = m->n_kv[l];
+    L.qdim = k.n_heads * L.hs;
+    L.kvdim = L.n_kv * L.hs;
+    L.ff = m->ff[l];
+    L.kv_src = l < k.n_layer_kv_from_start ? l : k.n_layer_kv_from_start - (L.swa ? 2 : 1);  // kvSourceLayer
+    if (L.kv_src < 0) {
+      c->set_err("g4_model_finalize: layer %d has no KV source layer", l);
+      return G4_E_ARG;
+    }
+    L.scale = m->layer_scale[l];
+    const bool own_kv = l < k.n_layer_kv_from_start;
+    if (!need(p + "attn_norm.weight", G4_TYPE_F32, dim) || !need(p + "attn_q_norm.weight", G4_TYPE_F32, L.hs) ||
+        !need(p + "post_attention_norm.weight", G4_TYPE_F32, dim) || !need(p + "ffn_norm.weight", G4_TYPE_F32, dim) ||
+        !need(p + "post_ffw_norm.weight", G4_TYPE_F32, dim) ||
+        !need(p + "attn_q.weight", -1, (uint64_t)dim * L.qdim) ||
+        !need(p + "attn_output.weight", -1, (uint64_t)dim * L.qdim) ||
+        !need(p + "ffn_gate.weight", -1, (uint64_t)dim * L.ff) ||
+        !need(p + "ffn_up.weight", -1, (uint64_t)dim * L.ff) || !need(p + "ffn_down.weight", -1, (uint64_t)dim * L.ff))
+      return G4_E_ARG;
+    if (own_kv && (!need(p + "attn_k.weight", -1, (uint64_t)dim * L.kvdim) ||
+                   !need(p + "attn_k_norm.weight", G4_TYPE_F32, L.hs)))
+      return G4_E_ARG;
+    L.has_v = m->get(p + "attn_v.weight") != nullptr;
+    if (own_kv && L.has_v && !need(p + "attn_v.weight", -1, (uint64_t)dim * L.kvdim)) return G4_E_ARG;
+    if (k.n_expert > 0) {
+      const int E = k.n_expert, eff = k.expert_ff;
+      if (!need(p + "post_ffw_norm_1.weight", G4_TYPE_F32, dim) ||
+          !need(p + "pre_ffw_norm_2.weight", G4_TYPE_F32, dim) ||
+          !need(p + "post_ffw_norm_2.weight", G4_TYPE_F32, dim) ||
+          !need(p + "ffn_gate_inp.weight", G4_TYPE_F32, (uint64_t)dim * E) ||
+          !need(p + "ffn_gate_inp.scale", G4_TYPE_F32, dim) || !need(p + "ffn_down_exps.scale", G4_TYPE_F32, E) ||
+          !need(p + "ffn_gate_up_exps.weight", -1, (uint64_t)dim * 2 * eff * E) ||
+          !need(p + "ffn_down_exps.weight", -1, (uint64_t)eff * dim * E))
+        return G4_E_ARG;
+      L.moe = g4_moe_weights{dim, E, k.n_expert_used, eff, k.eps, m->get(p + "ffn_gate_inp.weight"),
+                             m->get(p + "ffn_gate_inp.scale"), m->get(p + "ffn_gate_up_exps.weight"),
+                             m->get(p + "ffn_down_exps.weight"), m->get(p + "ffn_down_exps.scale"),
+                             m->get(p + "pre_ffw_norm_2.weight"), m->get(p + "post_ffw_norm_2.weight")};
+      L.post_ffw_norm_1 = m->f32(p + "post_ffw_norm_1.weight");
+    }
+    // fused projections: q | k | v and interleaved gate / up
+    std::vector<const g4_tensor*> qkv = {m->get(p + "attn_q.weight")};
+    if (own_kv) {
+      qkv.push_back(m->get(p + "attn_k.weight"));
+      if (L.has_v) qkv.push_back(m->get(p + "attn_v.weight"));
+    }
+    if (int r = fuse_rows(c, qkv, dim, false, &L.qkv)) return r;
+    if (int r = fuse_rows(c, {m->get(p + "ffn_gate.weight"), m->get(p + "ffn_up.weight")}, dim, true, &L.gate_up))
+      return r;
+    drop(m, p + "attn_q.weight");
+    drop(m, p + "attn_k.weight");
+    drop(m, p + "attn_v.weight");
+    drop(m, p + "ffn_gate.weight");
+    drop(m, p + "ffn_up.weight");
+    L.wo = m->t[p + "attn_output.weight"];
+    L.down = m->t[p + "ffn_down.weight"];
+    L.attn_norm = m->f32(p + "attn_norm.weight");
+    L.q_norm = m->f32(p + "attn_q_norm.weight");
+    L.k_norm = m->f32(p + "attn_k_norm.weight");
+    L.post_attn_norm = m->f32(p + "post_attention_norm.weight");
+    L.ffn_norm = m->f32(p + "ffn_norm.weight");
+    L.post_ffw_norm = m->f32(p + "post_ffw_norm.weight");
+    const int qkv_rows = (int)(L.qkv->n_elems / dim);
+    // two-part activations everywhere: fp32-level products (plan_gemv exact_x)
+    L.p_qkv = plan_gemv(c->dev, L.qkv->type, 0, qkv_rows, dim, true, 0, true);
+    L.p_wo = plan_gemv(c->dev, L.wo->type, 0, dim, L.qdim, false, 0, true);
+    L.p_gu = plan_gemv(c->dev, L.gate_up->type, 0, 2 * L.ff, dim, true, 0, true);
+    L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, false, 0, true);
+    if (!L.p_qkv.fast || !L.p_gu.fast || !L.p_wo.fast || !L.p_down.fast) {
+      c->set_err("g4_model_finalize: layer %d: the projections need a streaming-kernel format "
+                 "(Q8_0 / Q4_K / Q6_K / BF16 / F32, rows of whole blocks)", l);
+      return G4_E_TYPE;
+    }
+  }
+  m->p_logits = plan_gemv(c->dev, m->wcls->type, 0, k.vocab, dim, true, 0, true);
+  if (!m->p_logits.fast || m->p_logits.pr != 1) {
+    c->set_err("g4_model_finalize: the output projection needs a streaming-kernel format");
+    return G4_E_TYPE;
+  }
+  // ModelLoader.loadWeights (ModelLoader.kt:154-166): SWA tables from theta_swa, full from rope_freqs
+  std::vector<float> cr, ci;
+  rope_table(k.ctx_len, k.head_size_swa, (double)k.rope_theta_swa, nullptr, cr, ci);
+  if (int r = upload_f32(c, cr, &m->cr_swa)) return r;
+  if (int r = upload_f32(c, ci, &m->ci_swa)) return r;
+  rope_table(k.ctx_len, k.head_size_full, (double)k.rope_theta, m->rope_freqs.data(), cr, ci);
+  if (int r = upload_f32(c, cr, &m->cr_full)) return r;
+  if (int r = upload_f32(c, ci, &m->ci_full)) return r;
+  m->finalized = true;
+  return 0;
+}
+
+extern "C" int g4_model_free(g4_model* m) {
+  if (!m) return G4_E_ARG;
+  cudaSetDevice(m->ctx->dev.device);
+  for (auto& kv : m->t) g4_tensor_free(kv.second);
+  for (LayerDev& L : m->L) {
+    if (L.qkv) g4_tensor_free(L.qkv);
+    if (L.gate_up) g4_tensor_free(L.gate_up);
+  }
+  for (float* p : {m->cr_full, m->ci_full, m->cr_swa, m->ci_swa})
+    if (p) cudaFree(p);
+  delete m;
+  return 0;
+}
+
+extern "C" int g4_state_free(g4_state* s);
+
+extern "C" int g4_state_create(g4_model* m, g4_state** out) {
+  if (!m) return G4_E_ARG;
+  g4_ctx* c = m->ctx;
+  if (!out || !m->finalized) {
+    c->set_err("g4_state_create: %s", out ? "finalize the model first" : "NULL argument");
+    return G4_E_ARG;
+  }
+  if (int r = c->bind()) return r;
+  const g4_model_config& k = m->cfg;
+  g4_state* s = new (std::nothrow) g4_state();
+  if (!s) return G4_E_NOMEM;
+  s->m = m;
+  auto al = [](size_t n) { return (n + 63) / 64 * 64; };  // floats, 256-byte multiples
+  const size_t dim = k.dim;
+  size_t off = 0;
+  const size_t o_x0 = off; off += al(dim);
+  const size_t o_x1 = off; off += al(dim);
+  const size_t o_qkv = off; off += al(m->max_q + 2 * m->max_kv);
+  const size_t o_xbk = off; off += al(m->max_q);
+  const size_t o_xb2 = off; off += al(dim);
+  const size_t o_hb = off; off += al(m->max_ff);
+  const size_t o_sh = off; off += al(dim);
+  const size_t o_moe = off; off += al(dim);
+  const size_t o_log = off; off += al(k.vocab);
+  const size_t o_part = off; off += al((size_t)k.n_heads * kAttnChunks * (m->max_hs + 2));
+  std::vector<size_t> o_kc, o_vc;
+  for (int l = 0; l < k.n_layer_kv_from_start; ++l) {
+    const int hs = m->is_swa[l] ? k.head_size_swa : k.head_size_full;
+    const size_t n = al((size_t)k.ctx_len * m->n_kv[l] * hs);
+    o_kc.push_back(off);
+    off += n;
+    o_vc.push_back(off);
+    off += n;
+  }
+  if (cudaMalloc(&s->buf, off * 4) != cudaSuccess) {
+    cudaGetLastError();
+    delete s;
+    c->set_err("g4_state_create: cannot allocate %zu bytes of activations and KV cache", off * 4);
+    return G4_E_NOMEM;
+  }
+  cudaMemset(s->buf, 0, off * 4);
+  s->x[0] = s->buf + o_x0;
+  s->x[1] = s->buf + o_x1;
+  s->qkv = s->buf + o_qkv;
+  s->xbk = s->buf + o_xbk;
+  s->xb2 = s->buf + o_xb2;
+  s->hb = s->buf + o_hb;
+  s->sh = s->buf + o_sh;
+  s->moe_out = s->buf + o_moe;
+  s->logits = s->buf + o_log;
+  s->part = s->buf + o_part;
+  for (int l = 0; l < k.n_layer_kv_from_start; ++l) {
+    s->kc.push_back(s->buf + o_kc[l]);
+    s->vc.push_back(s->buf + o_vc[l]);
+  }
+  const size_t ctl_ints = 4 + 3 * (size_t)k.ctx_len;
+  const size_t tick_bytes = (size_t)k.n_layers * kTicketStride * 4;
+  const size_t small = 256 + tick_bytes + ctl_ints * 4;
+  if (cudaMalloc(&s->small, small) != cudaSuccess || cudaMallocHost(&s->h_ctl, ctl_ints * 4) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    g4_state_free(s);
+    c->set_err("g4_state_create: cannot allocate control buffers");
+    return G4_E_NOMEM;
+  }
+  cudaMemset(s->small, 0, small);
+  s->argmax = reinterpret_cast<unsigned long long*>(s->small);
+  s->tickets = reinterpret_cast<unsigned*>(s->small + 256);
+  s->ctl = reinterpret_cast<int*>(s->small + 256 + tick_bytes);
+  // The MoE layers take their work buffers from the context's arena: size it
+  // (and set the kernels up) now, outside any stream capture.
+  if (k.n_expert > 0) {
+    int r = g4_moe_layer(c, &m->L[0].moe, s->x[0], s->moe_out, 1, nullptr, nullptr, s->st);
+    if (!r) r = c->check_status(s->st);
+    if (r) {
+      g4_state_free(s);
+      return r;
+    }
+  }
+  if (cudaError_t e = cudaStreamSynchronize(s->st)) {
+    g4_state_free(s);
+    return c->cuda_fail(e, "g4_state_create");
+  }
+  *out = s;
+  return 0;
+}
+
+extern "C" int g4_state_free(g4_state* s) {
+  if (!s) return G4_E_ARG;
+  cudaSetDevice(s->m->ctx->dev.device);
+  if (s->st) cudaStreamSynchronize(s->st);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  if (s->small) cudaFree(s->small);
+  if (s->h_ctl) cudaFreeHost(s->h_ctl);
+  if (s->buf) cudaFree(s->buf);
+  if (s->st) cudaStreamDestroy(s->st);
+  delete s;
+  return 0;
+}
+
+using AttnFn = void (*)(const AttnArgs);
+static AttnFn attn_fn(int kvm) {
+  switch (kvm) {
+    case 1: return dec_attention_kernel<1>;
+    case 2: return dec_attention_kernel<2>;
+    case 4: return dec_attention_kernel<4>;
+    case 8: return dec_attention_kernel<8>;
+    default: return dec_attention_kernel<16>;
+  }
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl_k(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t st,
+                                Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Enqueue one decode step on s->st (captured into the graph).
+static int enqueue_step(g4_state* s) {
+  g4_model* m = s->m;
+  g4_ctx* c = m->ctx;
+  const g4_model_config& k = m->cfg;
+  const int dim = k.dim;
+  cudaStream_t st = s->st;
+  int cur = 0;
+  const int* step = s->ctl;
+  const float* branch = nullptr;     // output of the previous residual branch (FFN)
+  const float* branch_w = nullptr;   // its post-norm weight
+  float branch_scale = 1.f;          // layer output scale of the previous layer
+  const float* moe_prev = nullptr;   // previous layer's expert output (MoE merge)
+  const float* moe_w = nullptr;
+  const int max_chunk = std::max(8, ((k.ctx_len + kAttnChunks - 1) / kAttnChunks + 7) / 8 * 8);
+  for (int l = 0; l < k.n_layers; ++l) {
+    const LayerDev& L = m->L[l];
+    // ---- q | k | v, prologue: previous layer's residual (or embedding) + rmsnorm(attn_norm)
+    GemvFuse f;
+    f.eps = k.eps;
+    f.w_in = L.attn_norm;
+    f.x_out = s->x[cur ^ 1];
+    if (l == 0) {
+      f.in_mode = IN_EMBED_NORM;
+      const g4_tensor* emb = m->get("token_embd.weight");
+      f.emb = (const uint8_t*)emb->d;
+      f.emb_type = emb->type;
+      f.sqrt_dim = (float)sqrt((double)dim);
+      f.step = step;
+      f.in_tok = s->in_tok();
+      f.next_tok = s->ctl + 1;
+    } else if (moe_prev) {
+      f.in_mode = IN_MOE_MERGE;
+      f.r = branch;
+      f.w_r = branch_w;
+      f.m = moe_prev;
+      f.w_m = moe_w;
+      f.scale = branch_scale;
+    } else {
+      f.in_mode = IN_RESID_NORM;
+      f.r = branch;
+      f.w_r = branch_w;
+      f.scale = branch_scale;
+    }
+    int e = launch_gemv_fused(L.p_qkv, (const uint8_t*)L.qkv->d, s->x[cur], s->qkv, f, c->status, st, l > 0);
+    if (e) return c->cuda_fail((cudaError_t)e, "decode: qkv projection");
+    cur ^= 1;
+    // ---- attention
+    AttnArgs aa{};
+    aa.qkv = s->qkv;
+    aa.hs = L.hs;
+    aa.n_kv = L.n_kv;
+    aa.kv_mul = k.n_heads / L.n_kv;
+    aa.qdim = L.qdim;
+    aa.kvdim = L.kvdim;
+    const bool own = l < k.n_layer_kv_from_start;
+    aa.k_off = L.qdim;
+    aa.v_off = L.has_v ? L.qdim + L.kvdim : L.qdim;
+    aa.q_norm = L.q_norm;
+    aa.k_norm = L.k_norm;
+    aa.eps = k.eps;
+    aa.cr = L.swa ? m->cr_swa : m->cr_full;
+    aa.ci = L.swa ? m->ci_swa : m->ci_full;
+    aa.kc = s->kc[L.kv_src];
+    aa.vc = s->vc[L.kv_src];
+    aa.write_kv = own ? 1 : 0;
+    aa.window = L.swa ? k.sliding_window : 0;
+    aa.step = step;
+    aa.in_pos = s->in_pos();
+    aa.part = s->part;
+    aa.ticket = s->tickets + (size_t)l * kTicketStride;
+    aa.out = s->xbk;
+    aa.max_chunk = max_chunk;
+    const size_t asmem =
+        ((size_t)aa.kv_mul * L.hs + 2 * L.hs + (size_t)aa.kv_mul * std::max(max_chunk, kAttnChunks) +
+         4 * aa.kv_mul + 8) * 4;
+    AttnFn af = attn_fn(aa.kv_mul);
+    if (asmem > 48 * 1024 && cudaFuncSetAttribute(af, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem))
+      return c->cuda_fail(cudaGetLastError(), "decode: attention set-up");
+    cudaError_t ce = launch_pdl_k(af, L.n_kv * kAttnChunks, kAttnThreads, asmem, st, aa);
+    if (ce) return c->cuda_fail(ce, "decode: attention");
+    // ---- output projection
+    e = launch_gemv_fused(L.p_wo, (const uint8_t*)L.wo->d, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);
+    if (e) return c->cuda_fail((cudaError_t)e, "decode: output projection");
+    // ---- gate / up, prologue: x += rmsnorm(xb2, post_attention_norm); rmsnorm(x, ffn_norm)
+    GemvFuse g;
+    g.in_mode = IN_RESID_NORM;
+    g.out_mode = OUT_GELU_PAIR;
+    g.eps = k.eps;
+    g.r = s->xb2;
+    g.w_r = L.post_attn_norm;
+    g.w_in = L.ffn_norm;
+    g.x_out = s->x[cur ^ 1];
+    e = launch_gemv_fused(L.p_gu, (const uint8_t*)L.gate_up->d, s->x[cur], s->hb, g, c->status, st, true);
+    if (e) return c->cuda_fail((cudaError_t)e, "decode: gate/up projection");
+    cur ^= 1;
+    e = launch_gemv_fused(L.p_down, (const uint8_t*)L.down->d, s->hb, s->sh, GemvFuse{}, c->status, st, true);
+    if (e) return c->cuda_fail((cudaError_t)e, "decode: down projection");
+    branch = s->sh;
+    branch_scale = L.scale;
+    if (k.n_expert > 0) {
+      // expert half on the residual stream after attention (Llama.kt:247-346)
+      if (int r = g4_moe_layer(c, &L.moe, s->x[cur], s->moe_out, 1, nullptr, nullptr, st)) return r;
+      branch_w = L.post_ffw_norm_1;
+      moe_prev = s->moe_out;
+      moe_w = L.post_ffw_norm;
+    } else {
+      branch_w = L.post_ffw_norm;
+      moe_prev = nullptr;
+    }
+  }
+  // ---- logits: last residual, rmsnorm(output_norm), projection, softcap, argmax
+  GemvFuse f;
+  f.in_mode = moe_prev ? IN_MOE_MERGE : IN_RESID_NORM;
+  f.out_mode = OUT_SOFTCAP_ARGMAX;
+  f.eps = k.eps;
+  f.r = branch;
+  f.w_r = branch_w;
+  f.m = moe_prev;
+  f.w_m = moe_w;
+  f.scale = branch_scale;
+  f.w_in = m->f32("output_norm.weight");
+  f.softcap = k.logit_softcap;
+  f.argmax = s->argmax;
+  int e = launch_gemv_fused(m->p_logits, (const uint8_t*)m->wcls->d, s->x[cur], s->logits, f, c->status, st, true);
+  if (e) return c->cuda_fail((cudaError_t)e, "decode: logits");
+  cudaError_t ce = launch_pdl_k(dec_sample_kernel, 1, 32, 0, st, s->ctl, s->out_tok(), s->argmax);
+  if (ce) return c->cuda_fail(ce, "decode: sampling");
+  return 0;
+}
+
+static int build_graph(g4_state* s) {
+  g4_ctx* c = s->m->ctx;
+  if (s->graph) return 0;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal);
+  if (e) return c->cuda_fail(e, "decode: begin capture");
+  const int r = enqueue_step(s);
+  e = cudaStreamEndCapture(s->st, &g);
+  if (r) {
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    return r;
+  }
+  if (e) return c->cuda_fail(e, "decode: end capture");
+  e = cudaGraphInstantiate(&s->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e) {
+    s->graph = nullptr;
+    return c->cuda_fail(e, "decode: graph instantiation");
+  }
+  return 0;
+}
+
+// Stage steps [0, n) (input token or -1, position, in h_ctl) and reset the step counter.
+static int stage_steps(g4_state* s, int n) {
+  g4_ctx* c = s->m->ctx;
+  const int ctx = s->m->cfg.ctx_len;
+  s->h_ctl[0] = 0;
+  s->h_ctl[1] = 0;
+  cudaError_t e = cudaMemcpyAsync(s->ctl, s->h_ctl, 8, cudaMemcpyHostToDevice, s->st);
+  if (!e) e = cudaMemcpyAsync(s->in_tok(), s->h_ctl + 4, (size_t)n * 4, cudaMemcpyHostToDevice, s->st);
+  if (!e) e = cudaMemcpyAsync(s->in_pos(), s->h_ctl + 4 + ctx, (size_t)n * 4, cudaMemcpyHostToDevice, s->st);
+  return e ? c->cuda_fail(e, "decode: staging") : 0;
+}
+
+extern "C" {
+
+int g4_decode_step(g4_state* s, int token, int position, float* logits_host, int* next_token_host) {
+  if (!s) return G4_E_ARG;
+  g4_model* m = s->m;
+  g4_ctx* c = m->ctx;
+  if (token < 0 || token >= m->cfg.vocab || position < 0 || position >= m->cfg.ctx_len) {
+    c->set_err("g4_decode_step: token %d / position %d out of range (vocab %d, context %d)", token, position,
+               m->cfg.vocab, m->cfg.ctx_len);
+    return G4_E_ARG;
+  }
+  if (int r = c->bind()) return r;
+  if (int r = build_graph(s)) return r;
+  if (cudaError_t e = cudaStreamSynchronize(s->st)) return c->cuda_fail(e, "g4_decode_step");
+  s->h_ctl[4] = token;
+  s->h_ctl[4 + m->cfg.ctx_len] = position;
+  if (int r = stage_steps(s, 1)) return r;
+  cudaError_t e = cudaGraphLaunch(s->graph, s->st);
+  if (e) return c->cuda_fail(e, "g4_decode_step: graph launch");
+  if (logits_host) e = cudaMemcpyAsync(logits_host, s->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s->st);
+  if (!e && next_token_host) e = cudaMemcpyAsync(next_token_host, s->out_tok(), 4, cudaMemcpyDeviceToHost, s->st);
+  if (e) return c->cuda_fail(e, "g4_decode_step: read back");
+  return c->check_status(s->st);
+}
+
+int g4_decode_greedy(g4_state* s, const int* tokens, int n_tokens, int start_position, int n_generate,
+                     int* out_tokens) {
+  if (!s) return G4_E_ARG;
+  g4_model* m = s->m;
+  g4_ctx* c = m->ctx;
+  const int ctx = m->cfg.ctx_len;
+  if (!tokens || n_tokens < 1 || n_generate < 0 || (n_generate > 0 && !out_tokens) || start_position < 0 ||
+      (long long)start_position + n_tokens + std::max(n_generate, 1) - 1 > ctx) {
+    c->set_err("g4_decode_greedy: bad arguments (%d tokens from position %d, %d to generate, context %d)", n_tokens,
+               start_position, n_generate, ctx);
+    return G4_E_ARG;
+  }
+  for (int i = 0; i < n_tokens; ++i)
+    if (tokens[i] < 0 || tokens[i] >= m->cfg.vocab) {
+      c->set_err("g4_decode_greedy: token %d out of range", tokens[i]);
+      return G4_E_ARG;
+    }
+  if (int r = c->bind()) return r;
+  if (int r = build_graph(s)) return r;
+  if (cudaError_t e = cudaStreamSynchronize(s->st)) return c->cuda_fail(e, "g4_decode_greedy");
+  const int steps = n_tokens + std::max(n_generate, 1) - 1;
+  for (int i = 0; i < steps; ++i) {
+    s->h_ctl[4 + i] = i < n_tokens ? tokens[i] : -1;
+    s->h_ctl[4 + ctx + i] = start_position + i;
+  }
+  if (int r = stage_steps(s, steps)) return r;
+  for (int i = 0; i < steps; ++i)
+    if (cudaError_t e = cudaGraphLaunch(s->graph, s->st)) return c->cuda_fail(e, "g4_decode_greedy: graph launch");
+  if (n_generate > 0) {
+    cudaError_t e = cudaMemcpyAsync(out_tokens, s->out_tok() + (n_tokens - 1), (size_t)n_generate * 4,
+                                    cudaMemcpyDeviceToHost, s->st);
+    if (e) return c->cuda_fail(e, "g4_decode_greedy: read back");
+  }
+  return c->check_status(s->st);
+}
+
+int g4_decode_stage(g4_state* s, const int* tokens, const int* positions, int n_steps) {
+  if (!s) return G4_E_ARG;
+  g4_ctx* c = s->m->ctx;
+  const int ctx = s->m->cfg.ctx_len;
+  if (!tokens || !positions || n_steps < 1 || n_steps > ctx) {
+    c->set_err("g4_decode_stage: bad arguments (%d steps, context %d)", n_steps, ctx);
+    return G4_E_ARG;
+  }
+  if (int r = c->bind()) return r;
+  if (cudaError_t e = cudaStreamSynchronize(s->st)) return c->cuda_fail(e, "g4_decode_stage");
+  for (int i = 0; i < n_steps; ++i) {
+    if (positions[i] < 0 || positions[i] >= ctx || tokens[i] >= s->m->cfg.vocab || (i == 0 && tokens[i] < 0)) {
+      c->set_err("g4_decode_stage: step %d: token %d / position %d out of range", i, tokens[i], positions[i]);
+      return G4_E_ARG;
+    }
+    s->h_ctl[4 + i] = tokens[i];
+    s->h_ctl[4 + ctx + i] = positions[i];
+  }
+  return stage_steps(s, n_steps);
+}
+
+int g4_decode_enqueue(g4_state* s, int n_steps) {
+  if (!s || n_steps < 0) return G4_E_ARG;
+  g4_ctx* c = s->m->ctx;
+  if (int r = c->bind()) return r;
+  if (int r = build_graph(s)) return r;
+  for (int i = 0; i < n_steps; ++i)
+    if (cudaError_t e = cudaGraphLaunch(s->graph, s->st)) return c->cuda_fail(e, "g4_decode_enqueue");
+  return 0;
+}
+
+int g4_decode_read_tokens(g4_state* s, int first_step, int n, int* out) {
+  if (!s) return G4_E_ARG;
+  g4_ctx* c = s->m->ctx;
+  if (!out || first_step < 0 || n < 0 || first_step + n > s->m->cfg.ctx_len) {
+    c->set_err("g4_decode_read_tokens: bad arguments");
+    return G4_E_ARG;
+  }
+  cudaError_t e = cudaMemcpyAsync(out, s->out_tok() + first_step, (size_t)n * 4, cudaMemcpyDeviceToHost, s->st);
+  if (e) return c->cuda_fail(e, "g4_decode_read_tokens");
+  return c->check_status(s->st);
+}
+
+void* g4_state_stream(g4_state* s) { return s ? (void*)s->st : nullptr; }
+
+}  // extern "C"

@@ -188,6 +188,83 @@ int g4_moe_layer_noalloc(g4_ctx *ctx, const g4_moe_weights *w, const float *x_de
 int g4_moe_layer_ep(g4_ctx *ctx, const g4_moe_weights *w_local, const float *x_dev, float *out_dev,
                     int n_tokens, int32_t *topk_idx_dev, float *topk_prob_dev, void *stream);
 
+/* ---------------- whole-model decode (Llama.kt:105-477) ----------------
+ * A GPU-resident Llama.forward: the residual stream, the KV cache and the
+ * greedy sampler stay in HBM; one decode step is one CUDA graph.
+ *
+ * Model configuration, as LlamaConfiguration (LlamaConfiguration.kt:3-55) is
+ * derived by ModelLoader.loadModel (ModelLoader.kt:39-139).  The arrays are
+ * copied by g4_model_create.  Per-layer embeddings (embedding_length_per_layer
+ * > 0, Llama.kt:115-143,366-391) are not supported. */
+typedef struct {
+  int dim;                   /* gemma4.embedding_length */
+  int n_layers;              /* gemma4.block_count */
+  int n_heads;               /* gemma4.attention.head_count */
+  int vocab;                 /* size of tokenizer.ggml.tokens */
+  int ctx_len;               /* context length (KV cache positions) */
+  int head_size_full;        /* gemma4.attention.key_length */
+  int head_size_swa;         /* gemma4.attention.key_length_swa */
+  int sliding_window;        /* gemma4.attention.sliding_window */
+  int n_layer_kv_from_start; /* block_count - gemma4.attention.shared_kv_layers */
+  float eps;                 /* gemma4.attention.layer_norm_rms_epsilon */
+  float rope_theta;          /* gemma4.rope.freq_base */
+  float rope_theta_swa;      /* gemma4.rope.freq_base_swa */
+  float logit_softcap;       /* gemma4.final_logit_softcapping (0: none) */
+  int n_expert;              /* gemma4.expert_count (0: dense model) */
+  int n_expert_used;         /* gemma4.expert_used_count */
+  int expert_ff;             /* gemma4.expert_feed_forward_length */
+  const int *n_kv_heads;     /* [n_layers] KV heads (attn_k rows / head size) */
+  const int *ff;             /* [n_layers] gemma4.feed_forward_length */
+  const unsigned char *is_swa; /* [n_layers] gemma4.attention.sliding_window_pattern */
+} g4_model_config;
+
+typedef struct g4_model g4_model;
+typedef struct g4_state g4_state;
+
+/* Replaces ModelLoader.loadWeights (ModelLoader.kt:154-261) for the decoder:
+ * create, hand over every tensor by its GGUF name (raw blocks, no dequant:
+ * token_embd, output (optional: tied), output_norm, rope_freqs and the blk.N.*
+ * tensors of ModelLoader.kt:179-248), then finalize.  Finalize fuses q|k|v
+ * and gate/up of each layer into one tensor each (same GGML type required,
+ * rows of whole blocks) and builds the RoPE tables (RotaryPositionEmbeddings.kt).
+ * set_tensor copies the data; the host buffer may be released afterwards.
+ * Unknown tensors (per-layer embeddings) are rejected with G4_E_TYPE. */
+int g4_model_create(g4_ctx *ctx, const g4_model_config *cfg, g4_model **out);
+int g4_model_set_tensor(g4_model *model, const char *gguf_name, int ggml_type, const void *host_blocks,
+                        uint64_t nbytes, uint64_t n_elems);
+int g4_model_finalize(g4_model *model);
+int g4_model_free(g4_model *model);
+
+/* LlamaState (LlamaState.kt:38-77) on the device: activations, fp32 KV cache
+ * [ctx_len][kv_dim] per KV layer, step control.  One per sequence; not
+ * thread-safe.  Its work runs on a stream of its own. */
+int g4_state_create(g4_model *model, g4_state **out);
+int g4_state_free(g4_state *state);
+
+/* Llama.forward(model, state, token, position) (Llama.kt:105-408): one step.
+ * logits_host (vocab floats, after softcapping) and next_token_host (the
+ * argmax, FloatTensor.argmax: first maximum) may be NULL.  Synchronous. */
+int g4_decode_step(g4_state *state, int token, int position, float *logits_host, int *next_token_host);
+
+/* Llama.generateTokens with the ARGMAX sampler (Llama.kt:413-458), stop tokens
+ * not checked: tokens[i] is fed at position start_position + i (tokens[0] is
+ * normally <bos>), then n_generate greedy tokens, each fed back on the device
+ * (n_tokens + n_generate - 1 steps, no host round trip between them).
+ * out_tokens[n_generate] receives the generated ids.  Synchronous. */
+int g4_decode_greedy(g4_state *state, const int *tokens, int n_tokens, int start_position, int n_generate,
+                     int *out_tokens);
+
+/* Building blocks of g4_decode_greedy for callers that time or pipeline the
+ * steps: stage the inputs of steps [0, n_steps) (token, or -1 for the previous
+ * step's argmax; position) and reset the step counter; enqueue n_steps steps
+ * on the state's stream (asynchronous); read the argmax of steps
+ * [first_step, first_step + n) (synchronous). */
+int g4_decode_stage(g4_state *state, const int *tokens, const int *positions, int n_steps);
+int g4_decode_enqueue(g4_state *state, int n_steps);
+int g4_decode_read_tokens(g4_state *state, int first_step, int n, int *out);
+/* The state's cudaStream_t. */
+void *g4_state_stream(g4_state *state);
+
 /* Router top-k alone on given logits (Llama.kt:273-293 + softmaxInPlace,
  * MutableFloatTensor.kt:54-59): probs_dev/idx_dev [n_tokens, k]. */
 int g4_moe_topk(g4_ctx *ctx, const float *logits_dev, int n_tokens, int n_expert, int k,
