@@ -402,6 +402,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         moe = bench_moe(g4, ctx, torch, dev)
     elif world > 1 and not args.no_moe:
         moe = bench_moe_ep(g4, ctx, torch, dev, rank, world)
+    decode = None
+    if world == 1 and rank == 0 and not args.no_decode:
+        decode = bench_decode(g4, ctx, torch, dev, with_cpu=not args.no_cpu)
 
     if rank == 0:
         line = {
@@ -425,10 +428,121 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         }
         if moe:
             line["moe"] = moe
+        if decode:
+            line["decode"] = decode
         print(json.dumps(line), flush=True)
     for cc in cases:
         cc["w"].free()
     ctx.close()
+
+
+def decode_bytes_per_token(cfg, src, position: int) -> int:
+    """Algorithmic HBM bytes of one decode step at `position`: every weight
+    tensor once in its block size (the tied embedding once more as the output
+    projection, one embedding row for the lookup), the KV cache rows the
+    attention reads and the row it writes."""
+    from gemma4_kt_b200.floattensor import GGMLType
+
+    total = 0
+    for name, (dims, t) in src.infos.items():
+        n = int(np.prod(dims))
+        b = GGMLType(int(t)).byte_size_for(n)
+        if name == "token_embd.weight":
+            total += b // cfg.vocab  # the looked-up row
+            if not src.has("output.weight"):
+                total += b  # tied output projection
+        elif name.startswith("rope_freqs") or name.endswith("layer_output_scale.weight"):
+            continue
+        else:
+            total += b
+    for l in range(cfg.n_layers):
+        kvdim = cfg.n_kv_heads[l] * cfg.head_size(l)
+        start = max(0, position - cfg.sliding_window + 1) if cfg.is_swa[l] else 0
+        total += (position - start + 1) * kvdim * 4 * 2  # K and V rows read
+        if l < cfg.n_layer_kv_from_start:
+            total += kvdim * 4 * 2  # this position's K and V written
+    return total
+
+
+def bench_decode(g4, ctx, torch, dev, with_cpu: bool = True):
+    """Configuration 4 (dense decoder, seed 3): greedy decode of 256 tokens
+    after <bos> + 128 random prompt ids, one CUDA graph per step, every step
+    on the device (the argmax is fed back without a host round trip)."""
+    from gemma4_kt_b200 import synth
+
+    t0 = time.time()
+    m = synth.SynthDecoder(synth.C4_DENSE, seed=3)
+    src = g4.TensorSource.from_synth(m)
+    model = g4.DecoderModel(ctx, src)
+    cfg = model.cfg
+    prompt = m.prompt(128)
+    build_s = time.time() - t0
+    n_prompt, n_gen = 128, 256
+    toks = np.concatenate([[2], prompt]).astype(np.int32)
+    steps = n_prompt + n_gen  # positions 0..383: 128 prompt steps, then 256 generating steps
+    tin = np.full(steps, -1, np.int32)
+    tin[:n_prompt + 1] = toks
+    pos = np.arange(steps, dtype=np.int32)
+    st = model.new_state()
+    stream = torch.cuda.ExternalStream(st.stream, device=dev)
+    for _ in range(3):  # warm-up: full greedy runs (graph built, weights touched)
+        st.stage(tin, pos)
+        st.enqueue(steps)
+    torch.cuda.synchronize()
+    # timed: prompt phase (steps 0..127) and generation (steps 128..383), events on the state's stream
+    st.stage(tin, pos)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(stream)
+    st.enqueue(n_prompt)
+    e1.record(stream)
+    st.enqueue(n_gen)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    prompt_ms, gen_ms = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    generated = st.read_tokens(n_prompt, n_gen)
+    hbm, hbm_kind = peaks()
+    bytes_gen = sum(decode_bytes_per_token(cfg, src, p) for p in range(n_prompt, steps))
+    achieved = bytes_gen / (gen_ms * 1e-3) / 1e9
+    # end to end through the public host API: prompt ids in, generated ids out (g4_decode_greedy)
+    t1 = time.perf_counter()
+    out = st.generate(toks, n_gen)
+    e2e_s = time.perf_counter() - t1
+    res = {
+        "metric": "decode tok/s",
+        "config": "C4 dense decoder: 35 layers, hidden 1536, 8 q heads / 1 kv head x 256, FFN 6144, vocab 262144 "
+                  "tied, Q8_0, seed 3; <bos> + 128 random prompt ids, 256 greedy tokens, context 4096, fp32 KV cache",
+        "generation_tok_s": round(n_gen / (gen_ms * 1e-3), 2), "prompt_tok_s": round(n_prompt / (prompt_ms * 1e-3), 2),
+        "ms_per_token": round(gen_ms / n_gen, 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "peak_kind": hbm_kind,
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4), "bytes_per_token": round(bytes_gen / n_gen),
+                     "ceiling_tok_s": round(hbm * 1e9 / (bytes_gen / n_gen), 1)},
+        "e2e": {"value": round((n_prompt + n_gen) / e2e_s, 2), "unit": "tok/s (prompt and generated positions)",
+                "h2d_bytes_per_step": int(toks.nbytes), "d2h_bytes_per_step": int(n_gen * 4),
+                "note": "one g4_decode_greedy call: 129 prompt ids in from host memory, 256 generated ids out"},
+        "stream_matches_e2e": bool(np.array_equal(out, generated)),
+        "gpu_launches_per_token": cfg.n_layers * 5 + 2,
+        "timing": "CUDA events on the state's stream around 128 prompt steps and 256 generating steps "
+                  "(graph launches, no host synchronisation between steps); weights 1.7 GB >> L2",
+        "model_build_s": round(build_s, 1),
+    }
+    if with_cpu:
+        from oracle import oracle
+
+        orc = oracle.ModelOracle(src)
+        n_cpu = 8
+        tc = time.perf_counter()
+        tok = 2
+        for p in range(n_cpu):
+            lg = orc.step(tok, p)
+            tok = int(toks[p + 1]) if p + 1 < len(toks) else int(np.argmax(lg))
+        cpu_s = (time.perf_counter() - tc) / n_cpu
+        res["cpu_baseline"] = {"value": round(1.0 / cpu_s, 3), "unit": "tok/s", "cores": os.cpu_count() or 1,
+                               "kind": "port", "sample": f"{n_cpu} forward steps (positions 0-{n_cpu - 1}) of the "
+                                                         "same model through the oracle's Llama.forward restatement"}
+        orc.close()
+    st.free()
+    model.free()
+    return res
 
 
 def bench_moe(g4, ctx, torch, dev):
@@ -585,6 +699,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode-only", action="store_true", help="time only the C4 decoder (prints its object)")
     ap.add_argument("--only", default=None,
                     help="profiling mode: run one sweep case FORMAT:ROWSxCOLS (e.g. Q4_K:262144x1536) --reps times")
     ap.add_argument("--reps", type=int, default=3)
@@ -593,6 +709,16 @@ def main():
     args = ap.parse_args()
     if args.only or args.moe_only:
         profile_mode(args)
+        return
+    if args.decode_only:
+        import torch
+
+        import __graft_entry__
+
+        g4 = __graft_entry__.load_package()
+        ctx = g4.Context(0)
+        print(json.dumps(bench_decode(g4, ctx, torch, torch.device("cuda", 0), with_cpu=not args.no_cpu)), flush=True)
+        ctx.close()
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

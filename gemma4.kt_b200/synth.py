@@ -155,6 +155,7 @@ class DecoderSpec:
     expert_ff: int = 0
     expert_type: int = GGMLType.Q4_K
     layer_scale: bool = True
+    qk_temperature: bool = True     # q/k norm weights scaled by head_size^-1/4 (see SynthDecoder)
     extra: dict = field(default_factory=dict)
 
     def hs(self, layer: int) -> int:
@@ -195,7 +196,16 @@ class SynthDecoder:
     N(1, 0.1); layer output scales U(0.5, 1); rope_freqs U(1, 2); router
     F32 N(0, 0.02); router input scales N(1, 0.1); expert output scales
     U(0.5, 1.5).  Every tensor draws from its own stream
-    default_rng([seed, index]), so tensors can be made in any order."""
+    default_rng([seed, index]), so tensors can be made in any order.
+
+    The attention of the reference has scale 1.0 (Llama.kt:198): the learned
+    q/k norm weights set the temperature.  With weights near 1, scores of
+    RMS-normalised q and k have a spread of about sqrt(head_size) (16 at 256)
+    and the model is chaotic: the reference's own Vector-API and scalarDot
+    modes (llama.VectorBitSize) stop agreeing within a few positions.  So
+    by default (qk_temperature) the q and k norm weights are
+    head_size^-1/4 * N(1, 0.1): scores of unit spread, the usual
+    1/sqrt(head_size) temperature folded into the two norms."""
 
     def __init__(self, spec: DecoderSpec, seed: int, threads: int | None = None):
         from . import gguf as G
@@ -257,8 +267,9 @@ class SynthDecoder:
             if l not in s.no_v_layers:
                 self._mat(p + "attn_v.weight", s.wtype, d, s.n_kv_heads * hs)
             self._mat(p + "attn_output.weight", s.wtype, s.n_heads * hs, d)
-            self._f32(p + "attn_q_norm.weight", self._rng().normal(1.0, 0.1, hs))
-            self._f32(p + "attn_k_norm.weight", self._rng().normal(1.0, 0.1, hs))
+            qk = float(hs) ** -0.25 if s.qk_temperature else 1.0
+            self._f32(p + "attn_q_norm.weight", qk * self._rng().normal(1.0, 0.1, hs))
+            self._f32(p + "attn_k_norm.weight", qk * self._rng().normal(1.0, 0.1, hs))
             self._f32(p + "post_attention_norm.weight", self._rng().normal(1.0, 0.1, d))
             self._f32(p + "ffn_norm.weight", self._rng().normal(1.0, 0.1, d))
             self._mat(p + "ffn_gate.weight", s.wtype, d, s.ff)
