@@ -664,7 +664,19 @@ def profile_mode(args):
     from gemma4_kt_b200 import synth
 
     ctx = g4.Context(0)
-    if args.only:
+    if args.decode_steps:
+        m = synth.SynthDecoder(synth.C4_DENSE, seed=3)
+        model = g4.DecoderModel(ctx, g4.TensorSource.from_synth(m))
+        st = model.new_state()
+        n = args.decode_steps
+        toks = np.concatenate([[2], m.prompt(n - 1)]).astype(np.int32)
+        st.stage(toks, np.arange(n, dtype=np.int32) + 120)
+        st.enqueue(n)
+        torch.cuda.synchronize()
+        print(f"ran {n} C4 decode steps (positions 120..{119 + n})")
+        st.free()
+        model.free()
+    elif args.only:
         name, shape = args.only.split(":")
         rows, cols = (int(v) for v in shape.split("x"))
         t = dict(FORMATS)[name]
@@ -700,6 +712,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=0,
+                    help="profiling mode: run this many C4 decode steps (graph launches) and exit")
     ap.add_argument("--decode-only", action="store_true", help="time only the C4 decoder (prints its object)")
     ap.add_argument("--only", default=None,
                     help="profiling mode: run one sweep case FORMAT:ROWSxCOLS (e.g. Q4_K:262144x1536) --reps times")
@@ -707,7 +721,7 @@ def main():
     ap.add_argument("--moe-only", default=None,
                     help="profiling mode: run the MoE layer --reps times for these token counts (e.g. 1,256)")
     args = ap.parse_args()
-    if args.only or args.moe_only:
+    if args.only or args.moe_only or args.decode_steps:
         profile_mode(args)
         return
     if args.decode_only:
