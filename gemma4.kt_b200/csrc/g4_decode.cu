@@ -6,7 +6,8 @@
 //   qkv GEMV     prologue: previous layer's residual + post-FFN norm + layer
 //                scale (or the embedding x sqrt(dim) at layer 0), then
 //                rmsnorm(attn_norm); rows q | k | v of one fused tensor
-//   attention    per (KV head, position chunk) CTA: Q/K norms, NeoX RoPE, K/V
+//   attention    per (KV head, position chunk) CTA: the chunk's K/V rows bulk-
+//                copied to shared memory, Q/K norms, NeoX RoPE, the new K/V row
 //                into the cache, scores (scale 1.0), softmax partials, V sum;
 //                the last CTA of each KV head (ticket) combines the chunks
 //   wo GEMV      plain
@@ -42,9 +43,10 @@
 
 namespace g4 {
 
-constexpr int kAttnChunks = 32;  // position chunks (CTAs) per KV head
+constexpr int kAttnMaxChunks = 128;  // position chunks (CTAs) per KV head
 constexpr int kAttnThreads = 256;
-constexpr int kTicketStride = 64;  // ticket words per layer (KV heads <= 64)
+constexpr int kTicketStride = 64;    // ticket words per layer (KV heads <= 64)
+constexpr size_t kAttnTileBudget = 160 * 1024;  // shared memory for a chunk's K and V rows
 
 struct AttnArgs {
   const float* qkv;        // raw projections: q [n_heads*hs] | k [n_kv*hs] | v [n_kv*hs]
@@ -61,11 +63,19 @@ struct AttnArgs {
   int window;              // sliding window (0: full attention)
   const int* step;
   const int* in_pos;
-  float* part;             // [n_kv][kAttnChunks][kv_mul][hs + 2]
+  float* part;             // [n_kv][kAttnMaxChunks][kv_mul][hs + 2]
   unsigned* ticket;        // [n_kv]
   float* out;              // [qdim]
-  int max_chunk;           // capacity of a score row (positions per chunk at the full context)
+  int ch_max;              // positions per chunk that fit the shared-memory tiles (multiple of 16)
+  unsigned* status;
 };
+
+// Positions per chunk: about len / 8 (so the combine reads few partials),
+// a multiple of 16, at most ch_max; len <= kAttnMaxChunks * ch_max.
+__host__ __device__ __forceinline__ int attn_chunk(int len, int ch_max) {
+  int ch = ((len + 7) / 8 + 15) / 16 * 16;
+  return ch < 16 ? 16 : ch > ch_max ? ch_max : ch;
+}
 
 // Llama.kt:39-59 per-head rmsnorm, (w * ss) * x left to right (w == nullptr:
 // the bare norm of Llama.kt:62-81); one warp per head vector in shared memory.
@@ -91,46 +101,74 @@ __device__ __forceinline__ void head_rope(float* v, const float* fr, const float
 }
 
 // Attention of one layer (Llama.kt:157-218) for the KV-head group g and the
-// position chunk c of this CTA.  KVM = query heads per KV head.
+// position chunk c of this CTA.  KVM = query heads per KV head.  The chunk's
+// K and V rows of earlier positions are final before the step starts, so
+// their bulk copies into shared memory are issued before waiting for the
+// q/k/v projection; everything after reads them from shared memory.
 template <int KVM>
 __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __grid_constant__ AttnArgs a) {
-  extern __shared__ __align__(16) float sm[];
-  grid_dep_wait();
-  grid_dep_launch();
+  extern __shared__ __align__(128) uint8_t smraw[];
   const int hs = a.hs;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, NW = kAttnThreads / 32;
+  // the step's position is staged by the host before the step's first kernel
   const int pos = a.in_pos[*a.step];
   const int start = a.window > 0 ? max(0, pos - a.window + 1) : 0;
   const int len = pos - start + 1;
-  int ch = (len + kAttnChunks - 1) / kAttnChunks;
-  ch = max(8, (ch + 7) / 8 * 8);
+  const int ch = attn_chunk(len, a.ch_max);
   const int nch = (len + ch - 1) / ch;
-  const int g = blockIdx.x / kAttnChunks, c = blockIdx.x % kAttnChunks;
+  const int g = blockIdx.x / kAttnMaxChunks, c = blockIdx.x % kAttnMaxChunks;
   if (c >= nch) return;
-  const int t0 = start + c * ch, t1 = min(t0 + ch, pos + 1);
-  const int scs = max(a.max_chunk, kAttnChunks);
-  float* qs = sm;                 // [KVM][hs]
-  float* kp = qs + KVM * hs;      // [hs] k at pos
-  float* vp = kp + hs;            // [hs] v at pos
-  float* sc = vp + hs;            // [KVM][max_chunk] scores, then exp; later [KVM][kAttnChunks] chunk weights
-  float* st = sc + KVM * scs;     // [KVM] max, [KVM] sum, flag, pad, [KVM] denominators
+  const int t0 = start + c * ch, t1 = min(t0 + ch, pos + 1), n = t1 - t0;
+  float* kt = reinterpret_cast<float*>(smraw);        // [ch_max][hs]
+  float* vt = kt + (size_t)a.ch_max * hs;             // [ch_max][hs]
+  float* qs = vt + (size_t)a.ch_max * hs;             // [KVM][hs]
+  float* sc = qs + KVM * hs;                          // [KVM][ch_max] scores, then exp
+  float* wt = sc + KVM * a.ch_max;                    // [KVM][kAttnMaxChunks] chunk weights
+  float* st = wt + KVM * kAttnMaxChunks;              // [KVM] max, [KVM] sum, [KVM] denominators, flag
+  uint64_t* bar = reinterpret_cast<uint64_t*>(st + 4 * KVM);
+  int* flag = reinterpret_cast<int*>(st + 3 * KVM);
+
+  // rows t < pos of the chunk: bulk copies before the wait
+  const int n_pre = max(0, min(t1, pos) - t0);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t row_bytes = (uint32_t)hs * 4u;
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)n_pre * row_bytes * 2u);
+    __syncwarp();
+    for (int j = lane; j < n_pre; j += 32) {
+      const size_t src = (size_t)(t0 + j) * a.kvdim + (size_t)g * hs;
+      bulk_g2s(kt + (size_t)j * hs, a.kc + src, row_bytes, bar);
+      bulk_g2s(vt + (size_t)j * hs, a.vc + src, row_bytes, bar);
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
   const float* fr = a.cr + (size_t)pos * (hs / 2);
   const float* fi = a.ci + (size_t)pos * (hs / 2);
-
-  // q of the group's heads: per-head norm and RoPE (Llama.kt:158-168)
+  const bool has_pos = t1 == pos + 1;
+  float* kp = kt + (size_t)(pos - t0) * hs;  // the row of this position (when has_pos)
+  float* vp = vt + (size_t)(pos - t0) * hs;
+  // q of the group's heads (Llama.kt:158-168) and, in the chunk holding the
+  // position, its K/V row: computed (Llama.kt:174-195) or, for a layer that
+  // shares an earlier layer's cache, read from it
   for (int i = tid; i < KVM * hs; i += kAttnThreads) qs[i] = a.qkv[(size_t)g * KVM * hs + i];
-  const bool own_pos = t1 == pos + 1 && a.write_kv;  // this CTA computes and stores the new K/V row
-  if (own_pos)
+  if (has_pos) {
+    const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
-      kp[i] = a.qkv[a.k_off + (size_t)g * hs + i];
-      vp[i] = a.qkv[a.v_off + (size_t)g * hs + i];
+      kp[i] = a.write_kv ? a.qkv[a.k_off + (size_t)g * hs + i] : a.kc[row + i];
+      vp[i] = a.write_kv ? a.qkv[a.v_off + (size_t)g * hs + i] : a.vc[row + i];
     }
+  }
   __syncthreads();
   for (int h = warp; h < KVM; h += NW) {
     head_rmsnorm(qs + h * hs, a.q_norm, hs, a.eps, lane);
     head_rope(qs + h * hs, fr, fi, hs, lane);
   }
-  if (own_pos) {
+  if (has_pos && a.write_kv) {
     // K: learned norm then RoPE; V: bare norm (Llama.kt:183-195)
     if (warp == NW - 1) {
       head_rmsnorm(kp, a.k_norm, hs, a.eps, lane);
@@ -140,42 +178,48 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
     }
   }
   __syncthreads();
-  if (own_pos)
+  if (has_pos && a.write_kv) {
+    const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
-      a.kc[(size_t)pos * a.kvdim + (size_t)g * hs + i] = kp[i];
-      a.vc[(size_t)pos * a.kvdim + (size_t)g * hs + i] = vp[i];
+      a.kc[row + i] = kp[i];
+      a.vc[row + i] = vp[i];
     }
+  }
+  if (!mbar_wait_bounded(bar, 0)) {
+    record_error(a.status, ERR_TIMEOUT_FULL);
+    // give the copies still in flight one more bounded wait before the CTA leaves
+    if (!mbar_wait_bounded(bar, 0)) record_error(a.status, ERR_TIMEOUT_DRAIN);
+    return;
+  }
 
   // scores q_h . k_t (Llama.kt:204-208)
-  const int n = t1 - t0;
   for (int j = warp; j < n; j += NW) {
-    const int t = t0 + j;
-    const float* kt = (own_pos && t == pos) ? kp : a.kc + (size_t)t * a.kvdim + (size_t)g * hs;
+    const float* kr = kt + (size_t)j * hs;
     float acc[KVM];
 #pragma unroll
     for (int h = 0; h < KVM; ++h) acc[h] = 0.f;
     for (int i = lane; i < hs; i += 32) {
-      const float kv = kt[i];
+      const float kv = kr[i];
 #pragma unroll
       for (int h = 0; h < KVM; ++h) acc[h] = fmaf(qs[h * hs + i], kv, acc[h]);
     }
 #pragma unroll
     for (int h = 0; h < KVM; ++h) {
       const float s = warp_sum(acc[h]);
-      if (lane == 0) sc[h * a.max_chunk + j] = s;
+      if (lane == 0) sc[h * a.ch_max + j] = s;
     }
   }
   __syncthreads();
   // chunk softmax statistics: exp((s - m) as double), as softmaxInPlace (MutableFloatTensor.kt:54-59)
   for (int h = warp; h < KVM; h += NW) {
     float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * a.max_chunk + j]);
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * a.ch_max + j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
     for (int j = lane; j < n; j += 32) {
-      const float e = (float)exp((double)__fsub_rn(sc[h * a.max_chunk + j], m));
-      sc[h * a.max_chunk + j] = e;
+      const float e = (float)exp((double)__fsub_rn(sc[h * a.ch_max + j], m));
+      sc[h * a.ch_max + j] = e;
       l += e;
     }
     l = warp_sum(l);
@@ -186,16 +230,15 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   }
   __syncthreads();
   // partial V sums (Llama.kt:211-217)
-  float* part = a.part + ((size_t)g * kAttnChunks + c) * KVM * (hs + 2);
+  float* part = a.part + ((size_t)g * kAttnMaxChunks + c) * KVM * (hs + 2);
   for (int d = tid; d < hs; d += kAttnThreads) {
     float acc[KVM];
 #pragma unroll
     for (int h = 0; h < KVM; ++h) acc[h] = 0.f;
     for (int j = 0; j < n; ++j) {
-      const int t = t0 + j;
-      const float vv = (own_pos && t == pos) ? vp[d] : a.vc[(size_t)t * a.kvdim + (size_t)g * hs + d];
+      const float vv = vt[(size_t)j * hs + d];
 #pragma unroll
-      for (int h = 0; h < KVM; ++h) acc[h] = fmaf(sc[h * a.max_chunk + j], vv, acc[h]);
+      for (int h = 0; h < KVM; ++h) acc[h] = fmaf(sc[h * a.ch_max + j], vv, acc[h]);
     }
 #pragma unroll
     for (int h = 0; h < KVM; ++h) part[(size_t)h * (hs + 2) + 2 + d] = acc[h];
@@ -207,34 +250,42 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   // the last CTA of the group combines the chunks (threadfence reduction)
   __threadfence();
   __syncthreads();
-  int* flag = reinterpret_cast<int*>(st + 2 * KVM);
   if (tid == 0) flag[0] = atomicAdd(&a.ticket[g], 1u) == (unsigned)(nch - 1);
   __syncthreads();
   if (!flag[0]) return;
   __threadfence();
-  const float* pg = a.part + (size_t)g * kAttnChunks * KVM * (hs + 2);
-  float* wt = sc;  // [KVM][kAttnChunks] chunk weights exp(m_c - M)
-  for (int i = tid; i < KVM * nch; i += kAttnThreads) {
-    const int h = i / nch, cc = i % nch;
+  const float* pg = a.part + (size_t)g * kAttnMaxChunks * KVM * (hs + 2);
+  float* den = st + 2 * KVM;
+  for (int h = warp; h < KVM; h += NW) {
+    // lanes over chunks: M = max m_c, w_c = exp(m_c - M), den = sum w_c l_c
     float M = -INFINITY;
-    for (int k = 0; k < nch; ++k) M = fmaxf(M, __ldcg(pg + ((size_t)k * KVM + h) * (hs + 2)));
-    wt[h * kAttnChunks + cc] = (float)exp((double)__fsub_rn(__ldcg(pg + ((size_t)cc * KVM + h) * (hs + 2)), M));
-  }
-  __syncthreads();
-  float* den = st + 2 * KVM + 4;
-  if (tid < KVM) {
+    for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(pg + ((size_t)k * KVM + h) * (hs + 2)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float dsum = 0.f;
-    for (int k = 0; k < nch; ++k)
-      dsum = fmaf(wt[tid * kAttnChunks + k], __ldcg(pg + ((size_t)k * KVM + tid) * (hs + 2) + 1), dsum);
-    den[tid] = dsum;
+    for (int k = lane; k < nch; k += 32) {
+      const float* pk = pg + ((size_t)k * KVM + h) * (hs + 2);
+      const float w = (float)exp((double)__fsub_rn(__ldcg(pk), M));
+      wt[h * kAttnMaxChunks + k] = w;
+      dsum = fmaf(w, __ldcg(pk + 1), dsum);
+    }
+    dsum = warp_sum(dsum);
+    if (lane == 0) den[h] = dsum;
   }
   __syncthreads();
   for (int i = tid; i < KVM * hs; i += kAttnThreads) {
     const int h = i / hs, d = i % hs;
-    float num = 0.f;
-    for (int k = 0; k < nch; ++k)
-      num = fmaf(wt[h * kAttnChunks + k], __ldcg(pg + ((size_t)k * KVM + h) * (hs + 2) + 2 + d), num);
-    a.out[(size_t)(g * KVM + h) * hs + d] = __fdiv_rn(num, den[h]);
+    const float* ph = pg + (size_t)h * (hs + 2) + 2 + d;
+    const size_t stride = (size_t)KVM * (hs + 2);
+    float num0 = 0.f, num1 = 0.f;
+    int k = 0;
+    for (; k + 1 < nch; k += 2) {
+      const float x0 = __ldcg(ph + (size_t)k * stride), x1 = __ldcg(ph + (size_t)(k + 1) * stride);
+      num0 = fmaf(wt[h * kAttnMaxChunks + k], x0, num0);
+      num1 = fmaf(wt[h * kAttnMaxChunks + k + 1], x1, num1);
+    }
+    if (k < nch) num0 = fmaf(wt[h * kAttnMaxChunks + k], __ldcg(ph + (size_t)k * stride), num0);
+    a.out[(size_t)(g * KVM + h) * hs + d] = __fdiv_rn(num0 + num1, den[h]);
   }
   if (tid == 0) a.ticket[g] = 0u;
 }
@@ -368,6 +419,13 @@ int g4_model_create(g4_ctx* c, const g4_model_config* cfg, g4_model** out) {
     if (kvm != 1 && kvm != 2 && kvm != 4 && kvm != 8 && kvm != 16) {
       delete m;
       c->set_err("g4_model_create: %d query heads per KV head is not supported", kvm);
+      return G4_E_ARG;
+    }
+    const int chm = (int)std::min<size_t>(256, kAttnTileBudget / ((size_t)hs * 8) / 16 * 16);
+    if (chm < 16 || k.ctx_len > kAttnMaxChunks * chm) {
+      delete m;
+      c->set_err("g4_model_create: context %d too long for head size %d (at most %d positions)", k.ctx_len, hs,
+                 kAttnMaxChunks * chm);
       return G4_E_ARG;
     }
     m->max_q = std::max(m->max_q, k.n_heads * hs);
@@ -640,10 +698,10 @@ extern "C" int g4_model_finalize(g4_model* m) {
     L.post_ffw_norm = m->f32(p + "post_ffw_norm.weight");
     const int qkv_rows = (int)(L.qkv->n_elems / dim);
     // two-part activations everywhere: fp32-level products (plan_gemv exact_x)
-    L.p_qkv = plan_gemv(c->dev, L.qkv->type, 0, qkv_rows, dim, true, 0, true);
-    L.p_wo = plan_gemv(c->dev, L.wo->type, 0, dim, L.qdim, false, 0, true);
-    L.p_gu = plan_gemv(c->dev, L.gate_up->type, 0, 2 * L.ff, dim, true, 0, true);
-    L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, false, 0, true);
+    L.p_qkv = plan_gemv(c->dev, L.qkv->type, 0, qkv_rows, dim, true, 0, true, true);
+    L.p_wo = plan_gemv(c->dev, L.wo->type, 0, dim, L.qdim, false, 0, true, true);
+    L.p_gu = plan_gemv(c->dev, L.gate_up->type, 0, 2 * L.ff, dim, true, 0, true, true);
+    L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, false, 0, true, true);
     if (!L.p_qkv.fast || !L.p_gu.fast || !L.p_wo.fast || !L.p_down.fast) {
       c->set_err("g4_model_finalize: layer %d: the projections need a streaming-kernel format "
                  "(Q8_0 / Q4_K / Q6_K / BF16 / F32, rows of whole blocks)", l);
@@ -707,7 +765,7 @@ extern "C" int g4_state_create(g4_model* m, g4_state** out) {
   const size_t o_sh = off; off += al(dim);
   const size_t o_moe = off; off += al(dim);
   const size_t o_log = off; off += al(k.vocab);
-  const size_t o_part = off; off += al((size_t)k.n_heads * kAttnChunks * (m->max_hs + 2));
+  const size_t o_part = off; off += al((size_t)k.n_heads * kAttnMaxChunks * (m->max_hs + 2));
   std::vector<size_t> o_kc, o_vc;
   for (int l = 0; l < k.n_layer_kv_from_start; ++l) {
     const int hs = m->is_swa[l] ? k.head_size_swa : k.head_size_full;
@@ -783,6 +841,13 @@ extern "C" int g4_state_free(g4_state* s) {
   return 0;
 }
 
+// Positions per attention chunk that fit kAttnTileBudget (K and V rows), a multiple of 16.
+static int attn_ch_max(int hs) { return (int)std::min<size_t>(256, kAttnTileBudget / ((size_t)hs * 8) / 16 * 16); }
+static size_t attn_smem(int hs, int kvm) {
+  const size_t ch = (size_t)attn_ch_max(hs);
+  return (2 * ch * hs + (size_t)kvm * hs + (size_t)kvm * ch + (size_t)kvm * kAttnMaxChunks + 4 * kvm + 8) * 4;
+}
+
 using AttnFn = void (*)(const AttnArgs);
 static AttnFn attn_fn(int kvm) {
   switch (kvm) {
@@ -824,7 +889,6 @@ static int enqueue_step(g4_state* s) {
   float branch_scale = 1.f;          // layer output scale of the previous layer
   const float* moe_prev = nullptr;   // previous layer's expert output (MoE merge)
   const float* moe_w = nullptr;
-  const int max_chunk = std::max(8, ((k.ctx_len + kAttnChunks - 1) / kAttnChunks + 7) / 8 * 8);
   for (int l = 0; l < k.n_layers; ++l) {
     const LayerDev& L = m->L[l];
     // ---- q | k | v, prologue: previous layer's residual (or embedding) + rmsnorm(attn_norm)
@@ -882,14 +946,13 @@ static int enqueue_step(g4_state* s) {
     aa.part = s->part;
     aa.ticket = s->tickets + (size_t)l * kTicketStride;
     aa.out = s->xbk;
-    aa.max_chunk = max_chunk;
-    const size_t asmem =
-        ((size_t)aa.kv_mul * L.hs + 2 * L.hs + (size_t)aa.kv_mul * std::max(max_chunk, kAttnChunks) +
-         4 * aa.kv_mul + 8) * 4;
+    aa.ch_max = attn_ch_max(L.hs);
+    aa.status = c->status;
+    const size_t asmem = attn_smem(L.hs, aa.kv_mul);
     AttnFn af = attn_fn(aa.kv_mul);
     if (asmem > 48 * 1024 && cudaFuncSetAttribute(af, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem))
       return c->cuda_fail(cudaGetLastError(), "decode: attention set-up");
-    cudaError_t ce = launch_pdl_k(af, L.n_kv * kAttnChunks, kAttnThreads, asmem, st, aa);
+    cudaError_t ce = launch_pdl_k(af, L.n_kv * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
     if (ce) return c->cuda_fail(ce, "decode: attention");
     // ---- output projection
     e = launch_gemv_fused(L.p_wo, (const uint8_t*)L.wo->d, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);

@@ -484,7 +484,7 @@ static int pitch_for(int bytes) {
 }
 
 GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols, bool fused,
-                   size_t max_smem, bool exact_x) {
+                   size_t max_smem, bool exact_x, bool latency) {
   GemvPlan p{};
   p.type = type;
   p.rows = rows;
@@ -533,7 +533,10 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   const int target = env_int("G4_GEMV_CHUNK_BYTES", type == Q4_K ? 288 : type == Q6_K ? 420 : 576);
   const int unit = (type == BF16 ? 8 : type == F32 ? 4 : 1) * p.lpr;  // elements (blocks) per lane step
   int cb = std::max(unit, std::min(p.bpv, target / TS) / unit * unit);
-  const bool small = p.ngroups < 2 * dev.sms;
+  // latency: decode-size matrices take the split form up to 16 row groups per
+  // SM, so that every row is shared by several warps (a persistent warp would
+  // walk its rows' blocks one after the other)
+  const bool small = p.ngroups < 2 * dev.sms || (latency && p.ngroups <= 16 * dev.sms);
   if (small) {
     // few row groups: split each row over up to 8 warps of one CTA
     int want = std::max(unit, (p.bpv + 7) / 8);
