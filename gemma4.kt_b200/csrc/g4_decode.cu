@@ -8,9 +8,8 @@
 //                rmsnorm(attn_norm); rows q | k | v of one fused tensor
 //   attention    per (KV head, position chunk) CTA: the chunk's K/V rows bulk-
 //                copied to shared memory, Q/K norms, NeoX RoPE, the new K/V row
-//                into the cache, scores (scale 1.0), softmax partials, V sum;
-//                the last CTA of each KV head (ticket) combines the chunks
-//   wo GEMV      plain
+//                into the cache, scores (scale 1.0), softmax partials and V sums
+//   wo GEMV      prologue: the chunks combined into the attention output
 //   gate/up GEMV prologue: residual + post-attention norm, rmsnorm(ffn_norm);
 //                rows interleaved gate_i, up_i; epilogue gelu(gate) * up
 //   down GEMV    plain (the shared MLP of a MoE layer)
@@ -43,9 +42,8 @@
 
 namespace g4 {
 
-constexpr int kAttnMaxChunks = 128;  // position chunks (CTAs) per KV head
 constexpr int kAttnThreads = 256;
-constexpr int kTicketStride = 64;    // ticket words per layer (KV heads <= 64)
+constexpr int kMaxKvHeads = 64;      // KV heads per layer
 constexpr size_t kAttnTileBudget = 160 * 1024;  // shared memory for a chunk's K and V rows
 
 struct AttnArgs {
@@ -64,18 +62,9 @@ struct AttnArgs {
   const int* step;
   const int* in_pos;
   float* part;             // [n_kv][kAttnMaxChunks][kv_mul][hs + 2]
-  unsigned* ticket;        // [n_kv]
-  float* out;              // [qdim]
   int ch_max;              // positions per chunk that fit the shared-memory tiles (multiple of 16)
   unsigned* status;
 };
-
-// Positions per chunk: about len / 8 (so the combine reads few partials),
-// a multiple of 16, at most ch_max; len <= kAttnMaxChunks * ch_max.
-__host__ __device__ __forceinline__ int attn_chunk(int len, int ch_max) {
-  int ch = ((len + 7) / 8 + 15) / 16 * 16;
-  return ch < 16 ? 16 : ch > ch_max ? ch_max : ch;
-}
 
 // Llama.kt:39-59 per-head rmsnorm, (w * ss) * x left to right (w == nullptr:
 // the bare norm of Llama.kt:62-81); one warp per head vector in shared memory.
@@ -104,7 +93,9 @@ __device__ __forceinline__ void head_rope(float* v, const float* fr, const float
 // position chunk c of this CTA.  KVM = query heads per KV head.  The chunk's
 // K and V rows of earlier positions are final before the step starts, so
 // their bulk copies into shared memory are issued before waiting for the
-// q/k/v projection; everything after reads them from shared memory.
+// q/k/v projection; everything after reads them from shared memory.  The
+// chunk's softmax partials go to `part`; the output projection's prologue
+// combines them (IN_ATTN_COMBINE).
 template <int KVM>
 __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smraw[];
@@ -123,10 +114,8 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   float* vt = kt + (size_t)a.ch_max * hs;             // [ch_max][hs]
   float* qs = vt + (size_t)a.ch_max * hs;             // [KVM][hs]
   float* sc = qs + KVM * hs;                          // [KVM][ch_max] scores, then exp
-  float* wt = sc + KVM * a.ch_max;                    // [KVM][kAttnMaxChunks] chunk weights
-  float* st = wt + KVM * kAttnMaxChunks;              // [KVM] max, [KVM] sum, [KVM] denominators, flag
-  uint64_t* bar = reinterpret_cast<uint64_t*>(st + 4 * KVM);
-  int* flag = reinterpret_cast<int*>(st + 3 * KVM);
+  float* st = sc + KVM * a.ch_max;                    // [KVM] max, [KVM] sum
+  uint64_t* bar = reinterpret_cast<uint64_t*>(st + 2 * KVM);
 
   // rows t < pos of the chunk: bulk copies before the wait
   const int n_pre = max(0, min(t1, pos) - t0);
@@ -247,47 +236,6 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
     part[(size_t)tid * (hs + 2)] = st[tid];
     part[(size_t)tid * (hs + 2) + 1] = st[KVM + tid];
   }
-  // the last CTA of the group combines the chunks (threadfence reduction)
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) flag[0] = atomicAdd(&a.ticket[g], 1u) == (unsigned)(nch - 1);
-  __syncthreads();
-  if (!flag[0]) return;
-  __threadfence();
-  const float* pg = a.part + (size_t)g * kAttnMaxChunks * KVM * (hs + 2);
-  float* den = st + 2 * KVM;
-  for (int h = warp; h < KVM; h += NW) {
-    // lanes over chunks: M = max m_c, w_c = exp(m_c - M), den = sum w_c l_c
-    float M = -INFINITY;
-    for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(pg + ((size_t)k * KVM + h) * (hs + 2)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float dsum = 0.f;
-    for (int k = lane; k < nch; k += 32) {
-      const float* pk = pg + ((size_t)k * KVM + h) * (hs + 2);
-      const float w = (float)exp((double)__fsub_rn(__ldcg(pk), M));
-      wt[h * kAttnMaxChunks + k] = w;
-      dsum = fmaf(w, __ldcg(pk + 1), dsum);
-    }
-    dsum = warp_sum(dsum);
-    if (lane == 0) den[h] = dsum;
-  }
-  __syncthreads();
-  for (int i = tid; i < KVM * hs; i += kAttnThreads) {
-    const int h = i / hs, d = i % hs;
-    const float* ph = pg + (size_t)h * (hs + 2) + 2 + d;
-    const size_t stride = (size_t)KVM * (hs + 2);
-    float num0 = 0.f, num1 = 0.f;
-    int k = 0;
-    for (; k + 1 < nch; k += 2) {
-      const float x0 = __ldcg(ph + (size_t)k * stride), x1 = __ldcg(ph + (size_t)(k + 1) * stride);
-      num0 = fmaf(wt[h * kAttnMaxChunks + k], x0, num0);
-      num1 = fmaf(wt[h * kAttnMaxChunks + k + 1], x1, num1);
-    }
-    if (k < nch) num0 = fmaf(wt[h * kAttnMaxChunks + k], __ldcg(ph + (size_t)k * stride), num0);
-    a.out[(size_t)(g * KVM + h) * hs + d] = __fdiv_rn(num0 + num1, den[h]);
-  }
-  if (tid == 0) a.ticket[g] = 0u;
 }
 
 // Greedy sampling (Sampler.ARGMAX, FloatTensor.argmax): the logits GEMV left
@@ -366,8 +314,7 @@ struct g4_state {
   float *x[2] = {nullptr, nullptr}, *qkv = nullptr, *xbk = nullptr, *xb2 = nullptr, *hb = nullptr, *sh = nullptr;
   float *moe_out = nullptr, *logits = nullptr, *part = nullptr;
   std::vector<float*> kc, vc;
-  uint8_t* small = nullptr;     // argmax key, tickets, step control
-  unsigned* tickets = nullptr;
+  uint8_t* small = nullptr;     // argmax key, step control
   unsigned long long* argmax = nullptr;
   int* ctl = nullptr;     // [0] step, [1] next token, then in_tok[ctx], in_pos[ctx], out_tok[ctx]
   int* h_ctl = nullptr;   // pinned staging of the same layout
@@ -409,10 +356,10 @@ int g4_model_create(g4_ctx* c, const g4_model_config* cfg, g4_model** out) {
   m->layer_scale.assign(k.n_layers, 1.f);
   for (int l = 0; l < k.n_layers; ++l) {
     const int hs = m->is_swa[l] ? k.head_size_swa : k.head_size_full;
-    if (m->n_kv[l] <= 0 || m->n_kv[l] > kTicketStride || k.n_heads % m->n_kv[l] || m->ff[l] <= 0) {
+    if (m->n_kv[l] <= 0 || m->n_kv[l] > kMaxKvHeads || k.n_heads % m->n_kv[l] || m->ff[l] <= 0) {
       delete m;
       c->set_err("g4_model_create: layer %d: bad KV head count (1..%d dividing the heads) or FFN width", l,
-                 kTicketStride);
+                 kMaxKvHeads);
       return G4_E_ARG;
     }
     const int kvm = k.n_heads / m->n_kv[l];
@@ -698,17 +645,30 @@ extern "C" int g4_model_finalize(g4_model* m) {
     L.post_ffw_norm = m->f32(p + "post_ffw_norm.weight");
     const int qkv_rows = (int)(L.qkv->n_elems / dim);
     // two-part activations everywhere: fp32-level products (plan_gemv exact_x)
-    L.p_qkv = plan_gemv(c->dev, L.qkv->type, 0, qkv_rows, dim, true, 0, true, true);
-    L.p_wo = plan_gemv(c->dev, L.wo->type, 0, dim, L.qdim, false, 0, true, true);
-    L.p_gu = plan_gemv(c->dev, L.gate_up->type, 0, 2 * L.ff, dim, true, 0, true, true);
-    L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, false, 0, true, true);
+    GemvOpts o;
+    o.exact_x = true;
+    o.latency = true;
+    o.fused = true;
+    L.p_qkv = plan_gemv(c->dev, L.qkv->type, 0, qkv_rows, dim, o);
+    GemvOpts oc = o;  // the attention combine needs its chunk weights in shared memory
+    oc.fused_extra = (k.n_heads * (kAttnMaxChunks + 1)) * 4;
+    L.p_wo = plan_gemv(c->dev, L.wo->type, 0, dim, L.qdim, oc);
+    GemvOpts op = o;
+    op.pair_rows = true;
+    L.p_gu = plan_gemv(c->dev, L.gate_up->type, 0, 2 * L.ff, dim, op);
+    GemvOpts od = o;
+    od.fused = false;
+    L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, od);
     if (!L.p_qkv.fast || !L.p_gu.fast || !L.p_wo.fast || !L.p_down.fast) {
       c->set_err("g4_model_finalize: layer %d: the projections need a streaming-kernel format "
                  "(Q8_0 / Q4_K / Q6_K / BF16 / F32, rows of whole blocks)", l);
       return G4_E_TYPE;
     }
   }
-  m->p_logits = plan_gemv(c->dev, m->wcls->type, 0, k.vocab, dim, true, 0, true);
+  GemvOpts ol;
+  ol.fused = true;
+  ol.exact_x = true;
+  m->p_logits = plan_gemv(c->dev, m->wcls->type, 0, k.vocab, dim, ol);
   if (!m->p_logits.fast || m->p_logits.pr != 1) {
     c->set_err("g4_model_finalize: the output projection needs a streaming-kernel format");
     return G4_E_TYPE;
@@ -797,8 +757,7 @@ extern "C" int g4_state_create(g4_model* m, g4_state** out) {
     s->vc.push_back(s->buf + o_vc[l]);
   }
   const size_t ctl_ints = 4 + 3 * (size_t)k.ctx_len;
-  const size_t tick_bytes = (size_t)k.n_layers * kTicketStride * 4;
-  const size_t small = 256 + tick_bytes + ctl_ints * 4;
+  const size_t small = 256 + ctl_ints * 4;
   if (cudaMalloc(&s->small, small) != cudaSuccess || cudaMallocHost(&s->h_ctl, ctl_ints * 4) != cudaSuccess ||
       cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
     cudaGetLastError();
@@ -808,8 +767,7 @@ extern "C" int g4_state_create(g4_model* m, g4_state** out) {
   }
   cudaMemset(s->small, 0, small);
   s->argmax = reinterpret_cast<unsigned long long*>(s->small);
-  s->tickets = reinterpret_cast<unsigned*>(s->small + 256);
-  s->ctl = reinterpret_cast<int*>(s->small + 256 + tick_bytes);
+  s->ctl = reinterpret_cast<int*>(s->small + 256);
   // The MoE layers take their work buffers from the context's arena: size it
   // (and set the kernels up) now, outside any stream capture.
   if (k.n_expert > 0) {
@@ -845,7 +803,7 @@ extern "C" int g4_state_free(g4_state* s) {
 static int attn_ch_max(int hs) { return (int)std::min<size_t>(256, kAttnTileBudget / ((size_t)hs * 8) / 16 * 16); }
 static size_t attn_smem(int hs, int kvm) {
   const size_t ch = (size_t)attn_ch_max(hs);
-  return (2 * ch * hs + (size_t)kvm * hs + (size_t)kvm * ch + (size_t)kvm * kAttnMaxChunks + 4 * kvm + 8) * 4;
+  return (2 * ch * hs + (size_t)kvm * hs + (size_t)kvm * ch + 2 * kvm + 4) * 4;
 }
 
 using AttnFn = void (*)(const AttnArgs);
@@ -944,8 +902,6 @@ static int enqueue_step(g4_state* s) {
     aa.step = step;
     aa.in_pos = s->in_pos();
     aa.part = s->part;
-    aa.ticket = s->tickets + (size_t)l * kTicketStride;
-    aa.out = s->xbk;
     aa.ch_max = attn_ch_max(L.hs);
     aa.status = c->status;
     const size_t asmem = attn_smem(L.hs, aa.kv_mul);
@@ -954,8 +910,17 @@ static int enqueue_step(g4_state* s) {
       return c->cuda_fail(cudaGetLastError(), "decode: attention set-up");
     cudaError_t ce = launch_pdl_k(af, L.n_kv * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
     if (ce) return c->cuda_fail(ce, "decode: attention");
-    // ---- output projection
-    e = launch_gemv_fused(L.p_wo, (const uint8_t*)L.wo->d, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);
+    // ---- output projection, prologue: the attention output from the chunk partials
+    GemvFuse fc;
+    fc.in_mode = IN_ATTN_COMBINE;
+    fc.part = s->part;
+    fc.step = step;
+    fc.in_pos = s->in_pos();
+    fc.hs = L.hs;
+    fc.kv_mul = aa.kv_mul;
+    fc.window = aa.window;
+    fc.ch_max = aa.ch_max;
+    e = launch_gemv_fused(L.p_wo, (const uint8_t*)L.wo->d, s->xbk, s->xb2, fc, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: output projection");
     // ---- gate / up, prologue: x += rmsnorm(xb2, post_attention_norm); rmsnorm(x, ffn_norm)
     GemvFuse g;

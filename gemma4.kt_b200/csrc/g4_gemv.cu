@@ -47,9 +47,55 @@ struct GemvArgs {
 // rounding order per element (Llama.kt:27-37 rmsnorm: w * (s * x);
 // MutableFloatTensor.addInPlace / mapInPlace); sums of squares use a fixed
 // tree instead of the sequential float sum.
-__device__ void fused_prologue(const GemvFuse& f, const float* __restrict__ x, float* xs, float* red, int n) {
+__device__ void fused_prologue(const GemvFuse& f, const float* __restrict__ x, float* xs, float* red, int n,
+                               float* extra) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const bool store = f.x_out != nullptr && blockIdx.x == 0;
+  if (f.in_mode == IN_ATTN_COMBINE) {
+    // Llama.kt:201-218 from the attention kernel's chunk partials (max m_c,
+    // sum l_c of exp(s - m_c), acc_c = sum exp(s - m_c) v): per head
+    // out = sum_c w_c acc_c / sum_c w_c l_c with w_c = exp(m_c - max m)
+    const int pos = f.in_pos[*f.step];
+    const int start = f.window > 0 ? max(0, pos - f.window + 1) : 0;
+    const int len = pos - start + 1;
+    const int nch = (len + attn_chunk(len, f.ch_max) - 1) / attn_chunk(len, f.ch_max);
+    const int hs = f.hs, kvm = f.kv_mul, n_heads = n / hs;
+    const size_t hstride = (size_t)hs + 2, cstride = (size_t)kvm * hstride;
+    float* wt = extra;                           // [n_heads][kAttnMaxChunks]
+    float* den = extra + n_heads * kAttnMaxChunks;  // [n_heads]
+    const int warp = tid >> 5, lane = tid & 31, W = nt >> 5;
+    for (int h = warp; h < n_heads; h += W) {
+      const float* ph = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride;
+      float M = -INFINITY;
+      for (int k = lane; k < nch; k += 32) M = fmaxf(M, ph[(size_t)k * cstride]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float dsum = 0.f;
+      for (int k = lane; k < nch; k += 32) {
+        const float w = (float)exp((double)__fsub_rn(ph[(size_t)k * cstride], M));
+        wt[h * kAttnMaxChunks + k] = w;
+        dsum = fmaf(w, ph[(size_t)k * cstride + 1], dsum);
+      }
+      dsum = warp_sum(dsum);
+      if (lane == 0) den[h] = dsum;
+    }
+    __syncthreads();
+    for (int i = tid; i < n; i += nt) {
+      const int h = i / hs, d = i % hs;
+      const float* ph = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride + 2 + d;
+      const float* w = wt + h * kAttnMaxChunks;
+      float a0 = 0.f, a1 = 0.f;
+      int k = 0;
+      for (; k + 1 < nch; k += 2) {
+        a0 = fmaf(w[k], ph[(size_t)k * cstride], a0);
+        a1 = fmaf(w[k + 1], ph[(size_t)(k + 1) * cstride], a1);
+      }
+      if (k < nch) a0 = fmaf(w[k], ph[(size_t)k * cstride], a0);
+      xs[i] = __fdiv_rn(a0 + a1, den[h]);
+    }
+    __syncthreads();
+    return;
+  }
   float ss = 0.f;
   if (f.in_mode == IN_NORM) {
     for (int i = tid; i < n; i += nt) {
@@ -199,7 +245,7 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
   float* misc = reinterpret_cast<float*>(smem + p.misc_off);
   const float* src = a.x;
   if (a.f.in_mode != IN_PLAIN) {
-    fused_prologue(a.f, a.x, xs, misc, p.cols);
+    fused_prologue(a.f, a.x, xs, misc, p.cols, reinterpret_cast<float*>(smem + p.extra_off));
     src = xs;
   }
 
@@ -447,12 +493,16 @@ static KernelFn pick_kernel(int pr, int lpr, bool x2) {
   if (x2) {
     // two-part activations: the decoder's row-aligned projections only
     if constexpr (FMT == Q8_0 || FMT == Q4_K || FMT == Q6_K)
-      if (pr == 1) return lpr == 4 ? gemv_rows_kernel<FMT, 1, 4, true> : lpr == 2 ? gemv_rows_kernel<FMT, 1, 2, true>
-                                                                                  : gemv_rows_kernel<FMT, 1, 1, true>;
+      if (pr == 1)
+        return lpr == 32 ? gemv_rows_kernel<FMT, 1, 32, true> : lpr == 16 ? gemv_rows_kernel<FMT, 1, 16, true>
+             : lpr == 4  ? gemv_rows_kernel<FMT, 1, 4, true>  : lpr == 2  ? gemv_rows_kernel<FMT, 1, 2, true>
+                                                                          : gemv_rows_kernel<FMT, 1, 1, true>;
     return nullptr;
   }
-  if (pr == 1) return lpr == 4 ? gemv_rows_kernel<FMT, 1, 4, false> : lpr == 2 ? gemv_rows_kernel<FMT, 1, 2, false>
-                                                                               : gemv_rows_kernel<FMT, 1, 1, false>;
+  if (pr == 1)
+    return lpr == 32 ? gemv_rows_kernel<FMT, 1, 32, false> : lpr == 16 ? gemv_rows_kernel<FMT, 1, 16, false>
+         : lpr == 4  ? gemv_rows_kernel<FMT, 1, 4, false>  : lpr == 2  ? gemv_rows_kernel<FMT, 1, 2, false>
+                                                                       : gemv_rows_kernel<FMT, 1, 1, false>;
   if constexpr (FMT == Q4_K || FMT == Q6_K) {
     if (pr == 2) return lpr == 2 ? gemv_rows_kernel<FMT, 2, 2, false> : gemv_rows_kernel<FMT, 2, 1, false>;
     if (pr == 4) return lpr == 2 ? gemv_rows_kernel<FMT, 4, 2, false> : gemv_rows_kernel<FMT, 4, 1, false>;
@@ -483,8 +533,13 @@ static int pitch_for(int bytes) {
   return 16 * p;
 }
 
-GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols, bool fused,
-                   size_t max_smem, bool exact_x, bool latency) {
+GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols) {
+  return plan_gemv(dev, type, off, rows, cols, GemvOpts{});
+}
+
+GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols, const GemvOpts& o) {
+  const bool fused = o.fused, exact_x = o.exact_x, latency = o.latency;
+  const size_t max_smem = o.max_smem;
   GemvPlan p{};
   p.type = type;
   p.rows = rows;
@@ -511,6 +566,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   const bool quantized = type == Q8_0 || type == Q4_K || type == Q6_K;
   // a fused prologue stages the fp32 activation in shared memory for every format
   const int xbytes = quantized && !fused ? 0 : ((cols * 4 + 127) / 128) * 128;
+  const int extra = fused ? (o.fused_extra + 127) / 128 * 128 : 0;
   constexpr int kMiscBytes = 512;  // block reductions and the argmax epilogue
   // per-16 and per-32 column sums, per-32 int16 scales; int16 activations
   const int xsbytes = (((cols / 16 + 2 * (cols / 32)) * 4 + 127) / 128) * 128;
@@ -525,6 +581,9 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.lpr = env_int("G4_GEMV_LPR", lpr_default);
   if (p.lpr != 1 && p.lpr != 2 && p.lpr != 4) p.lpr = 1;
   if (pr > 1 && p.lpr > 2) p.lpr = 2;
+  // decode-size matrices: a warp per row (half a warp when rows are paired),
+  // so that a row's blocks are decoded side by side, not one after another
+  if (latency && pr == 1) p.lpr = o.pair_rows ? 16 : 32;
   int rows_per_group = 32 / p.lpr;
   p.ngroups = (p.nvrows + rows_per_group - 1) / rows_per_group;
 
@@ -533,10 +592,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   const int target = env_int("G4_GEMV_CHUNK_BYTES", type == Q4_K ? 288 : type == Q6_K ? 420 : 576);
   const int unit = (type == BF16 ? 8 : type == F32 ? 4 : 1) * p.lpr;  // elements (blocks) per lane step
   int cb = std::max(unit, std::min(p.bpv, target / TS) / unit * unit);
-  // latency: decode-size matrices take the split form up to 16 row groups per
-  // SM, so that every row is shared by several warps (a persistent warp would
-  // walk its rows' blocks one after the other)
-  const bool small = p.ngroups < 2 * dev.sms || (latency && p.ngroups <= 16 * dev.sms);
+  const bool small = latency ? p.ngroups < dev.sms : p.ngroups < 2 * dev.sms;
   if (small) {
     // few row groups: split each row over up to 8 warps of one CTA
     int want = std::max(unit, (p.bpv + 7) / 8);
@@ -549,7 +605,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   size_t stage = (size_t)rows_per_group * p.pitch;
   const size_t optin = dev.smem_optin > 0 ? dev.smem_optin : 227 * 1024;
   const size_t budget = max_smem > 0 ? std::min(max_smem, optin) : optin;
-  const size_t fixed = (size_t)xbytes + xsbytes + xqbytes + kMiscBytes + 256;
+  const size_t fixed = (size_t)xbytes + extra + xsbytes + xqbytes + kMiscBytes + 256;
   if (small) {
     p.split = std::min(p.nchunks, 8);
     p.warps = p.split;
@@ -558,7 +614,8 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
     p.split = 1;
     // enough CTAs to cover every SM: a warp streams one row group at a time, so
     // fewer than 16 groups per SM means fewer warps per CTA, not fewer CTAs
-    p.warps = env_int("G4_GEMV_WARPS", std::max(1, std::min(16, p.ngroups / dev.sms)));
+    p.warps = env_int("G4_GEMV_WARPS", std::max(1, std::min(16, latency ? (p.ngroups + dev.sms - 1) / dev.sms
+                                                                           : p.ngroups / dev.sms)));
     p.ns = env_int("G4_GEMV_STAGES", p.warps >= 16 ? 2 : 4);  // deeper rings when few warps share the SM
   }
   for (;;) {
@@ -581,8 +638,9 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
     }
   }
   p.xs_off = 0;
-  p.xsum_off = xbytes;
-  p.xq_off = xbytes + xsbytes;
+  p.extra_off = xbytes;
+  p.xsum_off = xbytes + extra;
+  p.xq_off = xbytes + extra + xsbytes;
   p.xq2_off = p.xq_off + xq1;
   p.misc_off = p.xq_off + xqbytes;
   p.bar_off = p.misc_off + kMiscBytes;

@@ -27,7 +27,27 @@ struct GemvPlan {
   int fast;          // 1: streaming kernel; 0: generic fallback
   int fused;         // planned for a fused prologue (fp32 activation staged in shared memory)
   int x2;            // two-part int16 activations (fp32-level products) for the quantized formats
+  int extra_off;     // fused prologue work space (GemvOpts::fused_extra bytes)
 };
+
+// Options of plan_gemv.
+struct GemvOpts {
+  bool fused = false;     // room for a fused prologue (fp32 activation in shared memory)
+  int fused_extra = 0;    // further shared memory for the prologue (IN_ATTN_COMBINE weights)
+  size_t max_smem = 0;    // cap on the plan's shared memory (0: the device maximum)
+  bool exact_x = false;   // two-part int16 activations (Q8_0 / Q4_K / Q6_K, rows of whole blocks)
+  bool latency = false;   // decode-size matrix: persistent CTAs with a warp (or half) per row
+  bool pair_rows = false; // the epilogue pairs rows 2i, 2i + 1 (needs two rows per warp)
+};
+
+// Position chunks of the decoder's attention (shared by the attention kernel
+// and the combine prologue): at most kAttnMaxChunks per KV head, about len / 8
+// positions each, a multiple of 16, at most ch_max (the shared-memory tile).
+constexpr int kAttnMaxChunks = 128;
+__host__ __device__ __forceinline__ int attn_chunk(int len, int ch_max) {
+  int ch = ((len + 7) / 8 + 15) / 16 * 16;
+  return ch < 16 ? 16 : ch > ch_max ? ch_max : ch;
+}
 
 // Fused prologue / epilogue of the decoder's GEMV launches (GemvFuse.in_mode /
 // out_mode).  The prologue turns the kernel's inputs into the activation
@@ -38,6 +58,7 @@ enum FuseIn : int {
   IN_RESID_NORM = 2,  // xn = (x + rmsnorm(r, w_r)) * scale [r optional]; act = rmsnorm(xn, w_in)
   IN_EMBED_NORM = 3,  // xn = emb.get(tok * dim + i) * sqrt(dim); act = rmsnorm(xn, w_in)  Llama.kt:112-113
   IN_MOE_MERGE = 4,   // xn = (x + rmsnorm(rmsnorm(r, w_r) + m, w_m)) * scale; act = rmsnorm(xn, w_in)  Llama.kt:349-353
+  IN_ATTN_COMBINE = 5,  // act = attention output from the per-chunk softmax partials   Llama.kt:201-218
 };
 enum FuseOut : int {
   OUT_PLAIN = 0,           // y[row] = dot
@@ -63,6 +84,10 @@ struct GemvFuse {
   const int* in_tok = nullptr;
   const int* next_tok = nullptr;
   unsigned long long* argmax = nullptr;  // OUT_SOFTCAP_ARGMAX: atomicMax of (ordered value << 32 | ~row)
+  // IN_ATTN_COMBINE: partials [n_kv][kAttnMaxChunks][kv_mul][hs + 2] = (max, sum, acc[hs]) per head
+  const float* part = nullptr;
+  const int* in_pos = nullptr;  // with step: the position, for the chunk geometry
+  int hs = 0, kv_mul = 1, window = 0, ch_max = 16;
 };
 
 // Magic-number int->float: 2^23 + b as float bits, then subtract 2^23 (+bias).

@@ -14,13 +14,11 @@ struct DeviceInfo {
 struct GemvPlan;
 struct GemvFuse;
 
-// fused: reserve shared memory for a fused prologue (launch_gemv_fused).
-// max_smem > 0 caps the plan's shared memory (room for a second CTA per SM).
-// exact_x: two-part int16 activations for Q8_0 / Q4_K / Q6_K (rows of whole
-// blocks only), products at fp32 precision instead of ~3e-5.
-// latency: favour many warps per row (the split form) for decode-size matrices.
-GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols, bool fused = false,
-                   size_t max_smem = 0, bool exact_x = false, bool latency = false);
+struct GemvOpts;
+// Launch plan of y = W . x (options: GemvOpts in g4_gemv.cuh; exact_x gives
+// products at fp32 precision instead of ~3e-5, latency favours a warp per row).
+GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols);
+GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int cols, const GemvOpts& o);
 // Launch with a plan from plan_gemv (the caller caches plans: planning queries
 // occupancy and sets kernel attributes, which costs microseconds of host time).
 // Returns the cudaError_t of the launch.
