@@ -270,8 +270,16 @@ struct LayerDev {
   const float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn_norm = nullptr;
   const float *ffn_norm = nullptr, *post_ffw_norm = nullptr, *post_ffw_norm_1 = nullptr;
   g4_moe_weights moe{};
-  GemvPlan p_qkv{}, p_wo{}, p_gu{}, p_down{};
+  GemvPlan p_qkv{}, p_wo{}, p_gu{}, p_down{};        // general GEMV plans (BF16 / F32 and other layouts)
+  DecGemvPlan d_qkv{}, d_wo{}, d_gu{}, d_down{};     // decoder GEMV (Q8_0 / Q4_K / Q6_K), used when fast
 };
+
+// One of a layer's projections: the decoder GEMV when it applies, else the general one.
+static int launch_proj(const DecGemvPlan& d, const GemvPlan& g, const g4_tensor* w, const float* x, float* y,
+                       const GemvFuse& f, unsigned* status, cudaStream_t st, bool pdl) {
+  if (d.fast) return launch_gemv_dec(d, (const uint8_t*)w->d, x, y, f, status, st, pdl);
+  return launch_gemv_fused(g, (const uint8_t*)w->d, x, y, f, status, st, pdl);
+}
 
 const char* kLayerNames[] = {
     "attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight",
@@ -659,7 +667,13 @@ extern "C" int g4_model_finalize(g4_model* m) {
     GemvOpts od = o;
     od.fused = false;
     L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, od);
-    if (!L.p_qkv.fast || !L.p_gu.fast || !L.p_wo.fast || !L.p_down.fast) {
+    const int comb_extra = (k.n_heads * (kAttnMaxChunks + 1)) * 4;
+    L.d_qkv = plan_gemv_dec(c->dev, L.qkv->type, qkv_rows, dim, false, 0);
+    L.d_wo = plan_gemv_dec(c->dev, L.wo->type, dim, L.qdim, false, comb_extra);
+    L.d_gu = plan_gemv_dec(c->dev, L.gate_up->type, 2 * L.ff, dim, true, 0);
+    L.d_down = plan_gemv_dec(c->dev, L.down->type, dim, L.ff, false, 0);
+    if ((!L.p_qkv.fast && !L.d_qkv.fast) || (!L.p_gu.fast && !L.d_gu.fast) || (!L.p_wo.fast && !L.d_wo.fast) ||
+        (!L.p_down.fast && !L.d_down.fast)) {
       c->set_err("g4_model_finalize: layer %d: the projections need a streaming-kernel format "
                  "(Q8_0 / Q4_K / Q6_K / BF16 / F32, rows of whole blocks)", l);
       return G4_E_TYPE;
@@ -876,7 +890,7 @@ static int enqueue_step(g4_state* s) {
       f.w_r = branch_w;
       f.scale = branch_scale;
     }
-    int e = launch_gemv_fused(L.p_qkv, (const uint8_t*)L.qkv->d, s->x[cur], s->qkv, f, c->status, st, l > 0);
+    int e = launch_proj(L.d_qkv, L.p_qkv, L.qkv, s->x[cur], s->qkv, f, c->status, st, l > 0);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: qkv projection");
     cur ^= 1;
     // ---- attention
@@ -920,7 +934,7 @@ static int enqueue_step(g4_state* s) {
     fc.kv_mul = aa.kv_mul;
     fc.window = aa.window;
     fc.ch_max = aa.ch_max;
-    e = launch_gemv_fused(L.p_wo, (const uint8_t*)L.wo->d, s->xbk, s->xb2, fc, c->status, st, true);
+    e = launch_proj(L.d_wo, L.p_wo, L.wo, s->xbk, s->xb2, fc, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: output projection");
     // ---- gate / up, prologue: x += rmsnorm(xb2, post_attention_norm); rmsnorm(x, ffn_norm)
     GemvFuse g;
@@ -931,10 +945,10 @@ static int enqueue_step(g4_state* s) {
     g.w_r = L.post_attn_norm;
     g.w_in = L.ffn_norm;
     g.x_out = s->x[cur ^ 1];
-    e = launch_gemv_fused(L.p_gu, (const uint8_t*)L.gate_up->d, s->x[cur], s->hb, g, c->status, st, true);
+    e = launch_proj(L.d_gu, L.p_gu, L.gate_up, s->x[cur], s->hb, g, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: gate/up projection");
     cur ^= 1;
-    e = launch_gemv_fused(L.p_down, (const uint8_t*)L.down->d, s->hb, s->sh, GemvFuse{}, c->status, st, true);
+    e = launch_proj(L.d_down, L.p_down, L.down, s->hb, s->sh, GemvFuse{}, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: down projection");
     branch = s->sh;
     branch_scale = L.scale;

@@ -1,0 +1,220 @@
+// g4_fuse.cuh -- the fused prologues and epilogues of the decoder's GEMV
+// launches (GemvFuse, g4_gemv.cuh): the activation vector computed from the
+// kernel's inputs (norms, residual, embedding, MoE merge, attention combine)
+// and the row post-processing (GELU pairs, softcap + argmax).
+#pragma once
+#include "g4_gemv.cuh"
+
+namespace g4 {
+
+// ---------------------------------------------------------------- fused prologue
+// The activation vector of a decoder GEMV, computed by every CTA into xs
+// (shared memory, n floats) from the kernel's inputs; CTA 0 also stores the
+// new residual stream xn to f.x_out.  The arithmetic follows the reference's
+// rounding order per element (Llama.kt:27-37 rmsnorm: w * (s * x);
+// MutableFloatTensor.addInPlace / mapInPlace); sums of squares use a fixed
+// tree instead of the sequential float sum.
+static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict__ x, float* xs, float* red, int n,
+                               float* extra) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const bool store = f.x_out != nullptr && blockIdx.x == 0;
+  if (f.in_mode == IN_ATTN_COMBINE) {
+    // Llama.kt:201-218 from the attention kernel's chunk partials (max m_c,
+    // sum l_c of exp(s - m_c), acc_c = sum exp(s - m_c) v): per head
+    // out = sum_c w_c acc_c / sum_c w_c l_c with w_c = exp(m_c - max m)
+    const int pos = f.in_pos[*f.step];
+    const int start = f.window > 0 ? max(0, pos - f.window + 1) : 0;
+    const int len = pos - start + 1;
+    const int nch = (len + attn_chunk(len, f.ch_max) - 1) / attn_chunk(len, f.ch_max);
+    const int hs = f.hs, kvm = f.kv_mul, n_heads = n / hs;
+    const size_t hstride = (size_t)hs + 2, cstride = (size_t)kvm * hstride;
+    float* wt = extra;                           // [n_heads][kAttnMaxChunks]
+    float* den = extra + n_heads * kAttnMaxChunks;  // [n_heads]
+    const int warp = tid >> 5, lane = tid & 31, W = nt >> 5;
+    for (int h = warp; h < n_heads; h += W) {
+      const float* ph = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride;
+      float M = -INFINITY;
+      for (int k = lane; k < nch; k += 32) M = fmaxf(M, ph[(size_t)k * cstride]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float dsum = 0.f;
+      for (int k = lane; k < nch; k += 32) {
+        const float w = (float)exp((double)__fsub_rn(ph[(size_t)k * cstride], M));
+        wt[h * kAttnMaxChunks + k] = w;
+        dsum = fmaf(w, ph[(size_t)k * cstride + 1], dsum);
+      }
+      dsum = warp_sum(dsum);
+      if (lane == 0) den[h] = dsum;
+    }
+    __syncthreads();
+    constexpr int kOut = 8;  // outputs per thread per round: their loads are issued together
+    for (int i0 = tid; i0 < n; i0 += kOut * nt) {
+      float num[kOut];
+      const float* ph[kOut];
+      const float* w[kOut];
+#pragma unroll
+      for (int q = 0; q < kOut; ++q) {
+        const int i = min(i0 + q * nt, n - 1);
+        const int h = i / hs, d = i % hs;
+        ph[q] = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride + 2 + d;
+        w[q] = wt + h * kAttnMaxChunks;
+        num[q] = 0.f;
+      }
+      for (int k = 0; k < nch; ++k) {
+        float v[kOut];
+#pragma unroll
+        for (int q = 0; q < kOut; ++q) v[q] = __ldcg(ph[q] + (size_t)k * cstride);
+#pragma unroll
+        for (int q = 0; q < kOut; ++q) num[q] = fmaf(w[q][k], v[q], num[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < kOut; ++q) {
+        const int i = i0 + q * nt;
+        if (i < n) xs[i] = __fdiv_rn(num[q], den[i / hs]);
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  constexpr int kMaxE = 8;  // elements per thread held in registers by the one-round path
+  if (n <= kMaxE * nt) {
+    // every input this thread needs, loaded in one round, then the passes in registers
+    const bool merge = f.in_mode == IN_MOE_MERGE, embed = f.in_mode == IN_EMBED_NORM;
+    const bool resid = f.in_mode == IN_RESID_NORM || merge;
+    float xv[kMaxE], rv[kMaxE], wr[kMaxE], mv[kMaxE], wm[kMaxE], wi[kMaxE];
+    long long ebase = 0;
+    if (embed) {
+      const int s = *f.step;
+      int tok = f.in_tok[s];
+      if (tok < 0) tok = *f.next_tok;
+      ebase = (long long)tok * n;
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxE; ++k) {
+      const int i = tid + k * nt;
+      const bool in = i < n;
+      xv[k] = rv[k] = wr[k] = mv[k] = wm[k] = wi[k] = 0.f;
+      if (in) {
+        wi[k] = f.w_in[i];
+        if (embed) xv[k] = get_elem(f.emb_type, f.emb, ebase + i);
+        else xv[k] = x[i];
+        if (resid && f.r) {
+          rv[k] = f.r[i];
+          wr[k] = f.w_r[i];
+        }
+        if (merge) {
+          mv[k] = f.m[i];
+          wm[k] = f.w_m[i];
+        }
+      }
+    }
+    float s_r = 0.f;
+    if (resid && f.r) {
+      float sr = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxE; ++k) sr = __fadd_rn(sr, __fmul_rn(rv[k], rv[k]));
+      s_r = rms_scale(block_sum(sr, red), n, f.eps);
+    }
+    float ss = 0.f;
+    if (merge) {
+      // xb = rmsnorm(shared, post_ffw_norm_1) + moeOutput (Llama.kt:237-243, 349)
+      float st = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxE; ++k) {
+        mv[k] = __fadd_rn(__fmul_rn(wr[k], __fmul_rn(s_r, rv[k])), mv[k]);
+        st = __fadd_rn(st, __fmul_rn(mv[k], mv[k]));
+      }
+      const float s_m = rms_scale(block_sum(st, red), n, f.eps);
+#pragma unroll
+      for (int k = 0; k < kMaxE; ++k) xv[k] = __fadd_rn(xv[k], __fmul_rn(wm[k], __fmul_rn(s_m, mv[k])));
+    } else if (resid && f.r) {
+#pragma unroll
+      for (int k = 0; k < kMaxE; ++k) xv[k] = __fadd_rn(xv[k], __fmul_rn(wr[k], __fmul_rn(s_r, rv[k])));
+    } else if (embed) {
+#pragma unroll
+      for (int k = 0; k < kMaxE; ++k) xv[k] = __fmul_rn(xv[k], f.sqrt_dim);  // Llama.kt:113
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxE; ++k) {
+      if (resid && f.scale != 1.f) xv[k] = __fmul_rn(xv[k], f.scale);  // Llama.kt:393-397
+      ss = __fadd_rn(ss, __fmul_rn(xv[k], xv[k]));
+    }
+    const float sx = rms_scale(block_sum(ss, red), n, f.eps);
+#pragma unroll
+    for (int k = 0; k < kMaxE; ++k) {
+      const int i = tid + k * nt;
+      if (i < n) {
+        if (store) f.x_out[i] = xv[k];
+        xs[i] = __fmul_rn(wi[k], __fmul_rn(sx, xv[k]));
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  float ss = 0.f;
+  if (f.in_mode == IN_NORM) {
+    for (int i = tid; i < n; i += nt) {
+      const float v = x[i];
+      xs[i] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  } else if (f.in_mode == IN_EMBED_NORM) {
+    // Llama.kt:112-113: x = tokenEmbeddingTable.get(token * dim + i) * sqrt(dim)
+    const int s = *f.step;
+    int tok = f.in_tok[s];
+    if (tok < 0) tok = *f.next_tok;
+    const long long base = (long long)tok * n;
+    for (int i = tid; i < n; i += nt) {
+      const float v = __fmul_rn(get_elem(f.emb_type, f.emb, base + i), f.sqrt_dim);
+      xs[i] = v;
+      if (store) f.x_out[i] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  } else {
+    // IN_RESID_NORM / IN_MOE_MERGE: xn = (x + branch) * scale
+    float s_r = 0.f;
+    if (f.r) {
+      float sr = 0.f;
+      for (int i = tid; i < n; i += nt) sr = __fadd_rn(sr, __fmul_rn(f.r[i], f.r[i]));
+      s_r = rms_scale(block_sum(sr, red), n, f.eps);
+    }
+    float s_m = 0.f;
+    if (f.in_mode == IN_MOE_MERGE) {
+      // xb = rmsnorm(shared, post_ffw_norm_1) + moeOutput (Llama.kt:237-243, 349)
+      float st = 0.f;
+      for (int i = tid; i < n; i += nt) {
+        const float t = __fadd_rn(__fmul_rn(f.w_r[i], __fmul_rn(s_r, f.r[i])), f.m[i]);
+        xs[i] = t;
+        st = __fadd_rn(st, __fmul_rn(t, t));
+      }
+      s_m = rms_scale(block_sum(st, red), n, f.eps);
+    }
+    for (int i = tid; i < n; i += nt) {
+      float v = x[i];
+      if (f.in_mode == IN_MOE_MERGE) v = __fadd_rn(v, __fmul_rn(f.w_m[i], __fmul_rn(s_m, xs[i])));
+      else if (f.r) v = __fadd_rn(v, __fmul_rn(f.w_r[i], __fmul_rn(s_r, f.r[i])));
+      if (f.scale != 1.f) v = __fmul_rn(v, f.scale);  // Llama.kt:393-397
+      xs[i] = v;
+      if (store) f.x_out[i] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  }
+  const float sx = rms_scale(block_sum(ss, red), n, f.eps);
+  for (int i = tid; i < n; i += nt) xs[i] = __fmul_rn(f.w_in[i], __fmul_rn(sx, xs[i]));
+  __syncthreads();
+}
+
+// Order-preserving key of an output for the argmax: larger value first, and
+// among equal values the lower row (FloatTensor.argmax keeps the first maximum).
+static __device__ __forceinline__ unsigned long long argmax_key(float v, long long row) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
+}
+
+static __device__ __forceinline__ float softcap_ref(float v, float cap) {
+  // Llama.kt:403-406: cap * tanh((v / cap).toDouble()).toFloat()
+  return cap > 0.f ? __fmul_rn(cap, (float)tanh((double)__fdiv_rn(v, cap))) : v;
+}
+
+}  // namespace g4

@@ -23,6 +23,7 @@
 //    deterministic.
 #include "g4_gemv.cuh"
 #include "g4_gemv_rows.cuh"
+#include "g4_fuse.cuh"
 #include "g4_internal.h"
 
 #include <algorithm>
@@ -39,128 +40,6 @@ struct GemvArgs {
   unsigned* status;  // device error word
   GemvFuse f;        // fused prologue / epilogue (IN_PLAIN / OUT_PLAIN: none)
 };
-
-// ---------------------------------------------------------------- fused prologue
-// The activation vector of a decoder GEMV, computed by every CTA into xs
-// (shared memory, n floats) from the kernel's inputs; CTA 0 also stores the
-// new residual stream xn to f.x_out.  The arithmetic follows the reference's
-// rounding order per element (Llama.kt:27-37 rmsnorm: w * (s * x);
-// MutableFloatTensor.addInPlace / mapInPlace); sums of squares use a fixed
-// tree instead of the sequential float sum.
-__device__ void fused_prologue(const GemvFuse& f, const float* __restrict__ x, float* xs, float* red, int n,
-                               float* extra) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const bool store = f.x_out != nullptr && blockIdx.x == 0;
-  if (f.in_mode == IN_ATTN_COMBINE) {
-    // Llama.kt:201-218 from the attention kernel's chunk partials (max m_c,
-    // sum l_c of exp(s - m_c), acc_c = sum exp(s - m_c) v): per head
-    // out = sum_c w_c acc_c / sum_c w_c l_c with w_c = exp(m_c - max m)
-    const int pos = f.in_pos[*f.step];
-    const int start = f.window > 0 ? max(0, pos - f.window + 1) : 0;
-    const int len = pos - start + 1;
-    const int nch = (len + attn_chunk(len, f.ch_max) - 1) / attn_chunk(len, f.ch_max);
-    const int hs = f.hs, kvm = f.kv_mul, n_heads = n / hs;
-    const size_t hstride = (size_t)hs + 2, cstride = (size_t)kvm * hstride;
-    float* wt = extra;                           // [n_heads][kAttnMaxChunks]
-    float* den = extra + n_heads * kAttnMaxChunks;  // [n_heads]
-    const int warp = tid >> 5, lane = tid & 31, W = nt >> 5;
-    for (int h = warp; h < n_heads; h += W) {
-      const float* ph = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride;
-      float M = -INFINITY;
-      for (int k = lane; k < nch; k += 32) M = fmaxf(M, ph[(size_t)k * cstride]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      float dsum = 0.f;
-      for (int k = lane; k < nch; k += 32) {
-        const float w = (float)exp((double)__fsub_rn(ph[(size_t)k * cstride], M));
-        wt[h * kAttnMaxChunks + k] = w;
-        dsum = fmaf(w, ph[(size_t)k * cstride + 1], dsum);
-      }
-      dsum = warp_sum(dsum);
-      if (lane == 0) den[h] = dsum;
-    }
-    __syncthreads();
-    for (int i = tid; i < n; i += nt) {
-      const int h = i / hs, d = i % hs;
-      const float* ph = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride + 2 + d;
-      const float* w = wt + h * kAttnMaxChunks;
-      float a0 = 0.f, a1 = 0.f;
-      int k = 0;
-      for (; k + 1 < nch; k += 2) {
-        a0 = fmaf(w[k], ph[(size_t)k * cstride], a0);
-        a1 = fmaf(w[k + 1], ph[(size_t)(k + 1) * cstride], a1);
-      }
-      if (k < nch) a0 = fmaf(w[k], ph[(size_t)k * cstride], a0);
-      xs[i] = __fdiv_rn(a0 + a1, den[h]);
-    }
-    __syncthreads();
-    return;
-  }
-  float ss = 0.f;
-  if (f.in_mode == IN_NORM) {
-    for (int i = tid; i < n; i += nt) {
-      const float v = x[i];
-      xs[i] = v;
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
-    }
-  } else if (f.in_mode == IN_EMBED_NORM) {
-    // Llama.kt:112-113: x = tokenEmbeddingTable.get(token * dim + i) * sqrt(dim)
-    const int s = *f.step;
-    int tok = f.in_tok[s];
-    if (tok < 0) tok = *f.next_tok;
-    const long long base = (long long)tok * n;
-    for (int i = tid; i < n; i += nt) {
-      const float v = __fmul_rn(get_elem(f.emb_type, f.emb, base + i), f.sqrt_dim);
-      xs[i] = v;
-      if (store) f.x_out[i] = v;
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
-    }
-  } else {
-    // IN_RESID_NORM / IN_MOE_MERGE: xn = (x + branch) * scale
-    float s_r = 0.f;
-    if (f.r) {
-      float sr = 0.f;
-      for (int i = tid; i < n; i += nt) sr = __fadd_rn(sr, __fmul_rn(f.r[i], f.r[i]));
-      s_r = rms_scale(block_sum(sr, red), n, f.eps);
-    }
-    float s_m = 0.f;
-    if (f.in_mode == IN_MOE_MERGE) {
-      // xb = rmsnorm(shared, post_ffw_norm_1) + moeOutput (Llama.kt:237-243, 349)
-      float st = 0.f;
-      for (int i = tid; i < n; i += nt) {
-        const float t = __fadd_rn(__fmul_rn(f.w_r[i], __fmul_rn(s_r, f.r[i])), f.m[i]);
-        xs[i] = t;
-        st = __fadd_rn(st, __fmul_rn(t, t));
-      }
-      s_m = rms_scale(block_sum(st, red), n, f.eps);
-    }
-    for (int i = tid; i < n; i += nt) {
-      float v = x[i];
-      if (f.in_mode == IN_MOE_MERGE) v = __fadd_rn(v, __fmul_rn(f.w_m[i], __fmul_rn(s_m, xs[i])));
-      else if (f.r) v = __fadd_rn(v, __fmul_rn(f.w_r[i], __fmul_rn(s_r, f.r[i])));
-      if (f.scale != 1.f) v = __fmul_rn(v, f.scale);  // Llama.kt:393-397
-      xs[i] = v;
-      if (store) f.x_out[i] = v;
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
-    }
-  }
-  const float sx = rms_scale(block_sum(ss, red), n, f.eps);
-  for (int i = tid; i < n; i += nt) xs[i] = __fmul_rn(f.w_in[i], __fmul_rn(sx, xs[i]));
-  __syncthreads();
-}
-
-// Order-preserving key of an output for the argmax: larger value first, and
-// among equal values the lower row (FloatTensor.argmax keeps the first maximum).
-__device__ __forceinline__ unsigned long long argmax_key(float v, long long row) {
-  uint32_t u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
-}
-
-__device__ __forceinline__ float softcap_ref(float v, float cap) {
-  // Llama.kt:403-406: cap * tanh((v / cap).toDouble()).toFloat()
-  return cap > 0.f ? __fmul_rn(cap, (float)tanh((double)__fdiv_rn(v, cap))) : v;
-}
 
 // LPR lanes share a row: a warp covers 32/LPR rows; lane l owns row slot
 // l % (32/LPR) and, within each chunk, the blocks b with b % LPR == l / (32/LPR).

@@ -30,6 +30,23 @@ struct GemvPlan {
   int extra_off;     // fused prologue work space (GemvOpts::fused_extra bytes)
 };
 
+// Plan of the decoder's GEMV (gemv_dec_kernel): a warp per row (or per pair
+// of rows gate_i, up_i), rows copied into shared memory with 16-byte
+// cp.async, the next row in flight while the current one is decoded;
+// Q8_0 / Q4_K / Q6_K with two-part activations.
+struct DecGemvPlan {
+  int type, rows, cols;
+  int pair;          // 1: units of two rows (2i, 2i + 1) -> one output each
+  int row_bytes;     // bytes of one row (whole blocks)
+  int nchunk16;      // 16-byte chunks covering the aligned superset of a row
+  int nslot;         // shared-memory slots per warp (2: double-buffered units)
+  int warps, grid;
+  int xs_off, extra_off, xsum_off, xq_off, xq2_off, misc_off, stage_off;
+  int stage_bytes;   // per warp
+  size_t smem;
+  int fast;
+};
+
 // Options of plan_gemv.
 struct GemvOpts {
   bool fused = false;     // room for a fused prologue (fp32 activation in shared memory)

@@ -24,6 +24,12 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
 // Returns the cudaError_t of the launch.
 int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, unsigned* status,
                 cudaStream_t st);
+struct DecGemvPlan;
+// The decoder's GEMV (g4_gemv_dec.cu): Q8_0 / Q4_K / Q6_K rows of whole blocks;
+// fast == 0 when it does not apply.  fused_extra: prologue work space.
+DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, bool pair, int fused_extra);
+int launch_gemv_dec(const DecGemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvFuse& f,
+                    unsigned* status, cudaStream_t st, bool pdl);
 // Same with a fused prologue / epilogue; pdl launches with programmatic
 // stream serialization (weights stream in before the previous kernel ends).
 // Needs a plan made with fused = true for a fused prologue, and the fast kernel.
