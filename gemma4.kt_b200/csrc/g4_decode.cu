@@ -301,6 +301,7 @@ struct g4_model {
   std::vector<LayerDev> L;
   const g4_tensor* wcls = nullptr;
   GemvPlan p_logits{};
+  DecGemvPlan d_logits{};  // the decoder GEMV when the format has one
   float *cr_full = nullptr, *ci_full = nullptr, *cr_swa = nullptr, *ci_swa = nullptr;
   bool finalized = false;
   int max_q = 0, max_kv = 0, max_ff = 0, max_hs = 0, max_kvm = 0;
@@ -668,10 +669,10 @@ extern "C" int g4_model_finalize(g4_model* m) {
     od.fused = false;
     L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, od);
     const int comb_extra = (k.n_heads * (kAttnMaxChunks + 1)) * 4;
-    L.d_qkv = plan_gemv_dec(c->dev, L.qkv->type, qkv_rows, dim, false, 0);
-    L.d_wo = plan_gemv_dec(c->dev, L.wo->type, dim, L.qdim, false, comb_extra);
-    L.d_gu = plan_gemv_dec(c->dev, L.gate_up->type, 2 * L.ff, dim, true, 0);
-    L.d_down = plan_gemv_dec(c->dev, L.down->type, dim, L.ff, false, 0);
+    L.d_qkv = plan_gemv_dec(c->dev, L.qkv->type, qkv_rows, dim, false, true, 0);
+    L.d_wo = plan_gemv_dec(c->dev, L.wo->type, dim, L.qdim, false, true, comb_extra);
+    L.d_gu = plan_gemv_dec(c->dev, L.gate_up->type, 2 * L.ff, dim, true, true, 0);
+    L.d_down = plan_gemv_dec(c->dev, L.down->type, dim, L.ff, false, false, 0);
     if ((!L.p_qkv.fast && !L.d_qkv.fast) || (!L.p_gu.fast && !L.d_gu.fast) || (!L.p_wo.fast && !L.d_wo.fast) ||
         (!L.p_down.fast && !L.d_down.fast)) {
       c->set_err("g4_model_finalize: layer %d: the projections need a streaming-kernel format "
@@ -683,7 +684,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
   ol.fused = true;
   ol.exact_x = true;
   m->p_logits = plan_gemv(c->dev, m->wcls->type, 0, k.vocab, dim, ol);
-  if (!m->p_logits.fast || m->p_logits.pr != 1) {
+  m->d_logits = plan_gemv_dec(c->dev, m->wcls->type, k.vocab, dim, false, true, 0);
+  if (!m->d_logits.fast && (!m->p_logits.fast || m->p_logits.pr != 1)) {
     c->set_err("g4_model_finalize: the output projection needs a streaming-kernel format");
     return G4_E_TYPE;
   }
@@ -976,7 +978,7 @@ static int enqueue_step(g4_state* s) {
   f.w_in = m->f32("output_norm.weight");
   f.softcap = k.logit_softcap;
   f.argmax = s->argmax;
-  int e = launch_gemv_fused(m->p_logits, (const uint8_t*)m->wcls->d, s->x[cur], s->logits, f, c->status, st, true);
+  int e = launch_proj(m->d_logits, m->p_logits, m->wcls, s->x[cur], s->logits, f, c->status, st, true);
   if (e) return c->cuda_fail((cudaError_t)e, "decode: logits");
   cudaError_t ce = launch_pdl_k(dec_sample_kernel, 1, 32, 0, st, s->ctl, s->out_tok(), s->argmax);
   if (ce) return c->cuda_fail(ce, "decode: sampling");

@@ -14,8 +14,33 @@ namespace g4 {
 // rounding order per element (Llama.kt:27-37 rmsnorm: w * (s * x);
 // MutableFloatTensor.addInPlace / mapInPlace); sums of squares use a fixed
 // tree instead of the sequential float sum.
+constexpr int kPrologueMaxE = 8;  // elements per thread held in registers by the one-round path
+
+// The constant inputs of the one-round path (norm weights), loaded by each
+// thread for its elements i = tid + k * blockDim.x.  They never change, so a
+// kernel loads them before waiting for its predecessor.
+struct PrologueConst {
+  float wi[kPrologueMaxE], wr[kPrologueMaxE], wm[kPrologueMaxE];
+  bool loaded;
+};
+static __device__ __forceinline__ void prologue_const(const GemvFuse& f, int n, PrologueConst& c) {
+  c.loaded = f.in_mode != IN_PLAIN && f.in_mode != IN_ATTN_COMBINE && n <= kPrologueMaxE * (int)blockDim.x;
+  if (!c.loaded) return;
+  const bool merge = f.in_mode == IN_MOE_MERGE, resid = f.in_mode == IN_RESID_NORM || merge;
+#pragma unroll
+  for (int k = 0; k < kPrologueMaxE; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    c.wi[k] = c.wr[k] = c.wm[k] = 0.f;
+    if (i < n) {
+      c.wi[k] = __ldg(f.w_in + i);
+      if (resid && f.r) c.wr[k] = __ldg(f.w_r + i);
+      if (merge) c.wm[k] = __ldg(f.w_m + i);
+    }
+  }
+}
+
 static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict__ x, float* xs, float* red, int n,
-                               float* extra) {
+                               float* extra, const PrologueConst* pc = nullptr) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const bool store = f.x_out != nullptr && blockIdx.x == 0;
   if (f.in_mode == IN_ATTN_COMBINE) {
@@ -33,21 +58,34 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
     const int warp = tid >> 5, lane = tid & 31, W = nt >> 5;
     for (int h = warp; h < n_heads; h += W) {
       const float* ph = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride;
+      float mc[kAttnMaxChunks / 32], lc[kAttnMaxChunks / 32];
+#pragma unroll
+      for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
+        const int k = lane + 32 * j;
+        mc[j] = k < nch ? __ldcg(ph + (size_t)k * cstride) : -INFINITY;
+        lc[j] = k < nch ? __ldcg(ph + (size_t)k * cstride + 1) : 0.f;
+      }
       float M = -INFINITY;
-      for (int k = lane; k < nch; k += 32) M = fmaxf(M, ph[(size_t)k * cstride]);
+#pragma unroll
+      for (int j = 0; j < kAttnMaxChunks / 32; ++j) M = fmaxf(M, mc[j]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
       float dsum = 0.f;
-      for (int k = lane; k < nch; k += 32) {
-        const float w = (float)exp((double)__fsub_rn(ph[(size_t)k * cstride], M));
-        wt[h * kAttnMaxChunks + k] = w;
-        dsum = fmaf(w, ph[(size_t)k * cstride + 1], dsum);
+#pragma unroll
+      for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
+        const int k = lane + 32 * j;
+        if (k < nch) {
+          const float w = (float)exp((double)__fsub_rn(mc[j], M));
+          wt[h * kAttnMaxChunks + k] = w;
+          dsum = fmaf(w, lc[j], dsum);
+        }
       }
       dsum = warp_sum(dsum);
       if (lane == 0) den[h] = dsum;
     }
     __syncthreads();
-    constexpr int kOut = 8;  // outputs per thread per round: their loads are issued together
+    constexpr int kOut = 4;  // outputs per thread per round
+    constexpr int kCh = 4;   // chunks whose loads are issued together
     for (int i0 = tid; i0 < n; i0 += kOut * nt) {
       float num[kOut];
       const float* ph[kOut];
@@ -60,12 +98,17 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
         w[q] = wt + h * kAttnMaxChunks;
         num[q] = 0.f;
       }
-      for (int k = 0; k < nch; ++k) {
-        float v[kOut];
+      for (int k0 = 0; k0 < nch; k0 += kCh) {
+        float v[kOut][kCh];
 #pragma unroll
-        for (int q = 0; q < kOut; ++q) v[q] = __ldcg(ph[q] + (size_t)k * cstride);
+        for (int q = 0; q < kOut; ++q)
 #pragma unroll
-        for (int q = 0; q < kOut; ++q) num[q] = fmaf(w[q][k], v[q], num[q]);
+          for (int j = 0; j < kCh; ++j) v[q][j] = k0 + j < nch ? __ldcg(ph[q] + (size_t)(k0 + j) * cstride) : 0.f;
+#pragma unroll
+        for (int q = 0; q < kOut; ++q)
+#pragma unroll
+          for (int j = 0; j < kCh; ++j)
+            if (k0 + j < nch) num[q] = fmaf(w[q][k0 + j], v[q][j], num[q]);
       }
 #pragma unroll
       for (int q = 0; q < kOut; ++q) {
@@ -76,7 +119,7 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
     __syncthreads();
     return;
   }
-  constexpr int kMaxE = 8;  // elements per thread held in registers by the one-round path
+  constexpr int kMaxE = kPrologueMaxE;
   if (n <= kMaxE * nt) {
     // every input this thread needs, loaded in one round, then the passes in registers
     const bool merge = f.in_mode == IN_MOE_MERGE, embed = f.in_mode == IN_EMBED_NORM;
@@ -94,18 +137,21 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
       const int i = tid + k * nt;
       const bool in = i < n;
       xv[k] = rv[k] = wr[k] = mv[k] = wm[k] = wi[k] = 0.f;
+      if (pc && pc->loaded) {
+        wi[k] = pc->wi[k];
+        wr[k] = pc->wr[k];
+        wm[k] = pc->wm[k];
+      }
       if (in) {
-        wi[k] = f.w_in[i];
+        if (!(pc && pc->loaded)) {
+          wi[k] = f.w_in[i];
+          if (resid && f.r) wr[k] = f.w_r[i];
+          if (merge) wm[k] = f.w_m[i];
+        }
         if (embed) xv[k] = get_elem(f.emb_type, f.emb, ebase + i);
         else xv[k] = x[i];
-        if (resid && f.r) {
-          rv[k] = f.r[i];
-          wr[k] = f.w_r[i];
-        }
-        if (merge) {
-          mv[k] = f.m[i];
-          wm[k] = f.w_m[i];
-        }
+        if (resid && f.r) rv[k] = f.r[i];
+        if (merge) mv[k] = f.m[i];
       }
     }
     float s_r = 0.f;

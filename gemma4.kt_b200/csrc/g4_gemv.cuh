@@ -30,19 +30,24 @@ struct GemvPlan {
   int extra_off;     // fused prologue work space (GemvOpts::fused_extra bytes)
 };
 
-// Plan of the decoder's GEMV (gemv_dec_kernel): a warp per row (or per pair
-// of rows gate_i, up_i), rows copied into shared memory with 16-byte
-// cp.async, the next row in flight while the current one is decoded;
-// Q8_0 / Q4_K / Q6_K with two-part activations.
+// Plan of the decoder's GEMV (gemv_dec_kernel): CTAs of kDecWarps warps, each
+// CTA taking row groups of 8 rows in turn, its warps splitting a group's
+// blocks (K) between them; a warp's 8 rows are decoded by 4 lanes each, so
+// the 8 lanes at one column read the activations once (shared-memory
+// broadcast).  Row segments are copied with 16-byte cp.async into per-warp
+// slots, the next group's in flight while this one is decoded.  Q8_0 / Q4_K /
+// Q6_K rows of whole blocks, two-part activations.
+constexpr int kDecWarps = 8;
 struct DecGemvPlan {
   int type, rows, cols;
-  int pair;          // 1: units of two rows (2i, 2i + 1) -> one output each
+  int pair;          // 1: rows (2i, 2i + 1) -> one output each (gelu(gate) * up)
   int row_bytes;     // bytes of one row (whole blocks)
-  int nchunk16;      // 16-byte chunks covering the aligned superset of a row
-  int nslot;         // shared-memory slots per warp (2: double-buffered units)
-  int warps, grid;
-  int xs_off, extra_off, xsum_off, xq_off, xq2_off, misc_off, stage_off;
-  int stage_bytes;   // per warp
+  int bpr, bps;      // blocks per row, per warp (K split)
+  int seg_cap;       // bytes of a row-segment slot (16-byte multiple)
+  int ngroups;       // row groups of 8
+  int grid;
+  int xs_off, extra_off, xsum_off, xq_off, xq2_off, misc_off, red_off, stage_off;
+  int stage_bytes;   // per warp: 2 slots x 8 rows x seg_cap
   size_t smem;
   int fast;
 };

@@ -1,17 +1,23 @@
 // g4_gemv_dec.cu -- the decoder's matrix-vector products (Llama.forward's
-// projections at batch 1: q|k|v, o, gate/up, down), on sm_100a.
+// projections at batch 1: q|k|v, o, gate/up, down, the output projection),
+// on sm_100a.
 //
 // A decode step runs dozens of small GEMVs (2-20 MB each) back to back, so
-// what matters is the time to first byte and how many rows progress at once,
-// not the streaming rate of a long kernel.  Design:
-//  * one CTA of 16 warps per SM; a warp owns a row (or the pair gate_i, up_i)
-//    at a time and its 32 lanes decode the row's blocks side by side;
-//  * a row (the 16-byte-aligned superset of its bytes) is copied by the
-//    warp's lanes with 16-byte cp.async into the warp's slot in shared
-//    memory and decoded there by the block decoders of g4_gemv_rows.cuh;
-//    the warp's next row streams into a second slot while this one is
-//    decoded, and the first row is requested before the kernel waits for
+// what matters is the time to the first bytes and how many bytes are in
+// flight per SM, not the streaming rate of a long kernel.  Design:
+//  * CTAs of 8 warps take row groups of 8 rows in turn (persistent, 2-3 CTAs
+//    per SM); the 8 warps split a group's blocks (K) into 8 segments;
+//  * in a warp, 4 lanes share a row and the 8 rows of the group sit side by
+//    side, so the 8 lanes at one column read the activations once (a
+//    shared-memory broadcast) and each lane decodes whole units (a Q8_0
+//    block, a 64-column group of a Q4_K block, half a Q6_K block);
+//  * each warp copies its 8 row segments (16-byte aligned supersets) with
+//    16-byte cp.async into its own slots, NS - 1 groups ahead of the one it
+//    decodes; the first NS groups are requested before the kernel waits for
 //    its predecessor (programmatic dependent launch: weights never change);
+//  * the 8 warps' partial sums meet in shared memory (one barrier per group)
+//    and warp 0 finishes the rows in a fixed order: plain, gelu(gate) * up on
+//    interleaved rows, or the soft cap with the argmax key;
 //  * the activation vector comes from the fused prologue (g4_fuse.cuh), once
 //    per CTA, and is held as two-part int16 (fp32-level products).
 #include "g4_fuse.cuh"
@@ -42,19 +48,139 @@ __device__ __forceinline__ void cp_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// NSLOT shared-memory slots per warp (2: the next unit streams in while this
-// one is decoded; 1 for long rows, which come one per warp).
-template <int FMT, int NSLOT, bool PAIR>
-__global__ void __launch_bounds__(512, 1) gemv_dec_kernel(const __grid_constant__ DecGemvArgs a) {
+// Units a block is decoded in (one lane each).
+template <int FMT>
+struct DecUnits {
+  static constexpr int kPerBlock = FMT == Q4_K ? 4 : FMT == Q6_K ? 2 : 1;
+};
+
+// Q4_K, 64-column group g of a block (Q4_KFloatTensor.kt:86-207): the same
+// arithmetic as block_q4k_i16 for one group.
+__device__ __forceinline__ float q4k_group_x2(const uint8_t* blk, int g, int e0, const int16_t* xq,
+                                              const int16_t* xql, const float* xsc32, const float* xsum32) {
+  const uint4 h = lds128(blk);
+  const float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
+  const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+  const uint32_t scw = g < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
+  const uint32_t mnw = g < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+  const int col = e0 + 64 * g;
+  const int16_t* xp = xq + xq_at(col);
+  const int16_t* xpl = xql + xq_at(col);
+  const uint4 qa = lds128(blk + 16 + 32 * g), qb = lds128(blk + 32 + 32 * g);
+  int alo = 0, ahi = 0, alo2 = 0, ahi2 = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint2 xl = *reinterpret_cast<const uint2*>(xp + 4 * k);
+    const uint2 xh = *reinterpret_cast<const uint2*>(xp + 32 + 4 * k);
+    const uint2 yl = *reinterpret_cast<const uint2*>(xpl + 4 * k);
+    const uint2 yh = *reinterpret_cast<const uint2*>(xpl + 32 + 4 * k);
+    const uint32_t w = k == 0 ? qa.x : k == 1 ? qa.y : k == 2 ? qa.z : k == 3 ? qa.w
+                     : k == 4 ? qb.x : k == 5 ? qb.y : k == 6 ? qb.z : qb.w;
+    const uint32_t lo = w & 0x0F0F0F0Fu, hi = w & 0xF0F0F0F0u;
+    alo = dp2a_lo_su(xl.x, lo, alo);
+    alo = dp2a_hi_su(xl.y, lo, alo);
+    ahi = dp2a_lo_su(xh.x, hi, ahi);
+    ahi = dp2a_hi_su(xh.y, hi, ahi);
+    alo2 = dp2a_lo_su(yl.x, lo, alo2);
+    alo2 = dp2a_hi_su(yl.y, lo, alo2);
+    ahi2 = dp2a_lo_su(yh.x, hi, ahi2);
+    ahi2 = dp2a_hi_su(yh.y, hi, ahi2);
+  }
+  const float flo = fmaf((float)alo2, kLoScale, (float)alo);
+  const float fhi = fmaf((float)ahi2, kLoScale, (float)ahi);
+  const int b0 = (2 * g) & 3;
+  const float sc_lo = small_u2f((scw >> (8 * b0)) & 0xFFu), sc_hi = small_u2f((scw >> (8 * b0 + 8)) & 0xFFu);
+  const float mn_lo = small_u2f((mnw >> (8 * b0)) & 0xFFu), mn_hi = small_u2f((mnw >> (8 * b0 + 8)) & 0xFFu);
+  const float s_lo = xsc32[col / 32], s_hi = xsc32[col / 32 + 1] * 0.0625f;
+  const float xs_lo = xsum32[col / 32], xs_hi = xsum32[col / 32 + 1];
+  float v = (d * sc_lo) * (s_lo * flo);
+  v = fmaf(d * sc_hi, s_hi * fhi, v);
+  return fmaf(-dmin, fmaf(mn_lo, xs_lo, mn_hi * xs_hi), v);
+}
+
+// Q6_K, 128-column half h of a block (Q6_KFloatTensor.kt:111-250): the same
+// arithmetic as block_q6k_i16 for one half.
+__device__ __forceinline__ float q6k_half_x2(const uint8_t* blk, int h, int e0, const int16_t* xq,
+                                             const int16_t* xql, const float* xsc32, const float* xsum16) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+  const uint8_t* b4 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = 8u * (uint32_t)(a & 3u);
+  const float d = f16_bits_to_f32((uint16_t)(__funnelshift_r(lds32(b4 + 208), lds32(b4 + 212), sh) & 0xFFFFu));
+  uint32_t qa[8], qb[8], qh[8], w[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 64 * h + 4 * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) qa[i] = __funnelshift_r(w[i], w[i + 1], sh);
+#pragma unroll
+  for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 64 * h + 32 + 4 * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) qb[i] = __funnelshift_r(w[i], w[i + 1], sh);
+#pragma unroll
+  for (int i = 0; i < 9; ++i) w[i] = lds32(b4 + 128 + 32 * h + 4 * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) qh[i] = __funnelshift_r(w[i], w[i + 1], sh);
+  const uint32_t s0 = lds32(b4 + 192 + 8 * h), s1 = lds32(b4 + 196 + 8 * h), s2 = lds32(b4 + 200 + 8 * h);
+  const uint32_t scw0 = __funnelshift_r(s0, s1, sh), scw1 = __funnelshift_r(s1, s2, sh);
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int ebase = e0 + 128 * h + 16 * c;
+    int a4[4] = {0, 0, 0, 0}, b4s[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t la = qa[4 * c + k], lb = qb[4 * c + k], hh = qh[4 * c + k];
+      uint32_t m[4];
+      m[0] = (la & 0x0F0F0F0Fu) | ((hh << 4) & 0x30303030u);
+      m[1] = (lb & 0x0F0F0F0Fu) | ((hh << 2) & 0x30303030u);
+      m[2] = ((la >> 4) & 0x0F0F0F0Fu) | (hh & 0x30303030u);
+      m[3] = ((lb >> 4) & 0x0F0F0F0Fu) | ((hh >> 2) & 0x30303030u);
+#pragma unroll
+      for (int sub = 0; sub < 4; ++sub) {
+        const int e = ebase + 32 * sub + 4 * k;
+        const uint2 xv = *reinterpret_cast<const uint2*>(xq + xq_at(e));
+        const uint2 yv = *reinterpret_cast<const uint2*>(xql + xq_at(e));
+        a4[sub] = dp2a_lo_su(xv.x, m[sub], a4[sub]);
+        a4[sub] = dp2a_hi_su(xv.y, m[sub], a4[sub]);
+        b4s[sub] = dp2a_lo_su(yv.x, m[sub], b4s[sub]);
+        b4s[sub] = dp2a_hi_su(yv.y, m[sub], b4s[sub]);
+      }
+    }
+#pragma unroll
+    for (int sub = 0; sub < 4; ++sub) {
+      const int col = ebase + 32 * sub;
+      const int si = 2 * sub + c;  // sc index 8h + 2*sub + c (Q6_KFloatTensor.kt:70)
+      const uint32_t scb = ((((si >> 2) ? scw1 : scw0) >> (8 * (si & 3))) & 0xFFu) ^ 0x80u;
+      const float scf = small_u2f(scb) - 128.f;
+      const float qx = fmaf((float)b4s[sub], kLoScale, (float)a4[sub]);
+      acc += (d * scf) * fmaf(xsc32[col / 32], qx, -32.f * xsum16[col / 16]);
+    }
+  }
+  return acc;
+}
+
+template <int FMT>
+__device__ __forceinline__ float dec_unit(const uint8_t* blk, int sub, int e0, const int16_t* xq, const int16_t* xql,
+                                          const float* xsc32, const float* xsum16, const float* xsum32) {
+  if constexpr (FMT == Q4_K) return q4k_group_x2(blk, sub, e0, xq, xql, xsc32, xsum32);
+  else if constexpr (FMT == Q6_K) return q6k_half_x2(blk, sub, e0, xq, xql, xsc32, xsum16);
+  else {
+    float acc = 0.f;
+    block_q8_0_i16<true>(blk, e0, xq, xsc32, acc, xql);
+    return acc;
+  }
+}
+
+// NS slots per warp: groups it + 1 .. it + NS - 1 stream in while group it is decoded.
+template <int FMT, int NS>
+__global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __grid_constant__ DecGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecGemvPlan& p = a.p;
-  constexpr int BS = block_size(FMT), TS = type_size(FMT);
-  constexpr int RPU = PAIR ? 2 : 1;  // rows per unit
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, W = blockDim.x >> 5;
-  const int GW = gridDim.x * W;
-  const int nunits = p.rows / RPU, nblk = p.cols / BS;
-  const int row_cap = p.nchunk16 * 16;  // bytes of a row slot
-  uint8_t* slots = smem + p.stage_off + (size_t)warp * p.stage_bytes;  // NSLOT x RPU rows
+  constexpr int BS = block_size(FMT), TS = type_size(FMT), UPB = DecUnits<FMT>::kPerBlock;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rs = lane & 7, sl = lane >> 3;  // row of the group, lane of the row
+  const int b0 = warp * p.bps, b1 = min(p.bpr, b0 + p.bps);  // this warp's blocks of each row
+  const int seg_len = b1 > b0 ? (b1 - b0) * TS : 0;
+  uint8_t* slots = smem + p.stage_off + (size_t)warp * p.stage_bytes;  // NS x 8 rows x seg_cap
   float* xs = reinterpret_cast<float*>(smem + p.xs_off);
   float* xsum16 = reinterpret_cast<float*>(smem + p.xsum_off);
   float* xsum32 = xsum16 + p.cols / 16;
@@ -62,27 +188,33 @@ __global__ void __launch_bounds__(512, 1) gemv_dec_kernel(const __grid_constant_
   int16_t* xq = reinterpret_cast<int16_t*>(smem + p.xq_off);
   int16_t* xql = reinterpret_cast<int16_t*>(smem + p.xq2_off);
   float* misc = reinterpret_cast<float*>(smem + p.misc_off);
+  float* red = reinterpret_cast<float*>(smem + p.red_off);  // [2][8 warps][8 rows]
 
-  // the aligned superset of unit u's rows -> slot `slot` (one commit group)
-  auto issue = [&](int u, int slot) {
-#pragma unroll
-    for (int r = 0; r < RPU; ++r) {
-      const long long start = (long long)(u * RPU + r) * p.row_bytes;
-      const uint8_t* src = a.w + (start & ~15ll);
-      uint8_t* dst = slots + ((size_t)slot * RPU + r) * row_cap;
-      for (int c = lane; c < p.nchunk16; c += 32) cp16(dst + (size_t)c * 16, src + (size_t)c * 16);
+  // lane (rs, sl) copies chunks sl, sl + 4, ... of row rs's segment of group g
+  auto issue = [&](int g, int slot) {
+    const int row = g * 8 + rs;
+    if (g < p.ngroups && row < p.rows && seg_len > 0) {
+      const long long start = (long long)row * p.row_bytes + (long long)b0 * TS;
+      const long long a0 = start & ~15ll;
+      const int nch = (int)((start + seg_len - a0 + 15) >> 4);
+      const uint8_t* src = a.w + a0;
+      uint8_t* dst = slots + ((size_t)slot * 8 + rs) * p.seg_cap;
+      for (int c = sl; c < nch; c += 4) cp16(dst + (size_t)c * 16, src + (size_t)c * 16);
     }
-    cp_commit();
+    cp_commit();  // one commit group per group, empty or not
   };
-  int u = blockIdx.x * W + warp;
-  if (u < nunits) issue(u, 0);  // weights only: before the dependency wait
+  PrologueConst pc;
+  prologue_const(a.f, p.cols, pc);  // constant inputs: before the dependency wait
+  const int g0 = blockIdx.x, G = gridDim.x;
+#pragma unroll
+  for (int k = 0; k < NS; ++k) issue(g0 + k * G, k);  // weights only: before the dependency wait
   grid_dep_wait();
   grid_dep_launch();
 
   // activation: fused prologue (or x itself), then two-part int16 per 32 columns
   const float* src = a.x;
   if (a.f.in_mode != IN_PLAIN) {
-    fused_prologue(a.f, a.x, xs, misc, p.cols, reinterpret_cast<float*>(smem + p.extra_off));
+    fused_prologue(a.f, a.x, xs, misc, p.cols, reinterpret_cast<float*>(smem + p.extra_off), &pc);
     src = xs;
   }
   {
@@ -91,7 +223,7 @@ __global__ void __launch_bounds__(512, 1) gemv_dec_kernel(const __grid_constant_
       const int i = i0 + (int)threadIdx.x;
       const bool act = i < n4;
       const float4 v = !act ? make_float4(0.f, 0.f, 0.f, 0.f)
-                       : src == a.x ? __ldg(reinterpret_cast<const float4*>(a.x) + i)
+                       : src == a.x ? __ldcg(reinterpret_cast<const float4*>(a.x) + i)
                                     : reinterpret_cast<const float4*>(src)[i];
       float s16 = (v.x + v.y) + (v.z + v.w);
       s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
@@ -130,76 +262,83 @@ __global__ void __launch_bounds__(512, 1) gemv_dec_kernel(const __grid_constant_
   __syncthreads();
 
   const int out_mode = a.f.out_mode;
+  const int nunits = (b1 - b0) * UPB;
   unsigned long long best = 0ull;
-  for (int it = 0; u < nunits; u += GW, ++it) {
-    const int cur = NSLOT == 2 ? (it & 1) : 0;
-    if (NSLOT == 2 && u + GW < nunits) {
-      issue(u + GW, cur ^ 1);  // the next unit streams in during this decode
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
+  for (int g = g0, it = 0; g < p.ngroups; g += G, ++it) {
+    const int slot = it % NS;
+    cp_wait<NS - 1>();  // this warp's copies of group it have landed
     __syncwarp();
-    float s[RPU];
+    float acc = 0.f;
+    const int row = g * 8 + rs;
+    if (row < p.rows) {
+      const long long start = (long long)row * p.row_bytes + (long long)b0 * TS;
+      const uint8_t* seg = slots + ((size_t)slot * 8 + rs) * p.seg_cap + (start & 15);
+      for (int u = sl; u < nunits; u += 4) {
+        const int bl = u / UPB, sub = u % UPB;
+        acc += dec_unit<FMT>(seg + (size_t)bl * TS, sub, (b0 + bl) * BS, xq, xql, xsc32, xsum16, xsum32);
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 8);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+    float* rb = red + (it & 1) * 64;
+    if (lane < 8) rb[warp * 8 + lane] = acc;
+    __syncwarp();
+    issue(g + NS * G, slot);  // this warp is done with the slot
+    __syncthreads();
+    if (warp == 0) {
+      float s = 0.f;
+      if (lane < 8) {
 #pragma unroll
-    for (int r = 0; r < RPU; ++r) {
-      const long long start = (long long)(u * RPU + r) * p.row_bytes;
-      const uint8_t* rowp = slots + ((size_t)cur * RPU + r) * row_cap + (start & 15);
-      float acc[1] = {0.f};
-      for (int b = lane; b < nblk; b += 32) {
-        const uint8_t* blk = rowp + (size_t)b * TS;
-        if constexpr (FMT == Q4_K) block_q4k_i16<1, true>(blk, b * BS, p.cols, xq, xsc32, xsum32, acc, xql);
-        else if constexpr (FMT == Q6_K) block_q6k_i16<1, true>(blk, b * BS, p.cols, xq, xsc32, xsum16, acc, xql);
-        else block_q8_0_i16<true>(blk, b * BS, xq, xsc32, acc[0], xql);
+        for (int w = 0; w < kDecWarps; ++w) s += rb[w * 8 + lane];
       }
-      s[r] = warp_sum(acc[0]);
-    }
-    if (lane == 0) {
+      const int r = g * 8 + lane;
+      const bool ok = lane < 8 && r < p.rows;
       if (out_mode == OUT_GELU_PAIR) {
-        a.y[u] = __fmul_rn(gelu_ref(s[0]), s[RPU - 1]);
+        const float up = __shfl_xor_sync(0xffffffffu, s, 1);
+        if (ok && !(lane & 1)) a.y[r >> 1] = __fmul_rn(gelu_ref(s), up);
       } else if (out_mode == OUT_SOFTCAP_ARGMAX) {
-        const float c = softcap_ref(s[0], a.f.softcap);
-        a.y[u] = c;
-        const unsigned long long k = argmax_key(c, u);
-        best = k > best ? k : best;
-      } else {
-        a.y[u] = s[0];
+        if (ok) {
+          const float c = softcap_ref(s, a.f.softcap);
+          a.y[r] = c;
+          const unsigned long long k = argmax_key(c, r);
+          best = k > best ? k : best;
+        }
+      } else if (ok) {
+        a.y[r] = s;
       }
     }
-    __syncwarp();  // the slot is rewritten by a later unit
-    if (NSLOT == 1 && u + GW < nunits) issue(u + GW, 0);
   }
-  if (out_mode == OUT_SOFTCAP_ARGMAX) {
-    unsigned long long* kb = reinterpret_cast<unsigned long long*>(misc + 64);
-    __syncthreads();
-    if (lane == 0) kb[warp] = best;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      unsigned long long b = 0ull;
-      for (int w = 0; w < W; ++w) b = kb[w] > b ? kb[w] : b;
-      atomicMax(a.f.argmax, b);
+  cp_wait<0>();
+  if (out_mode == OUT_SOFTCAP_ARGMAX && warp == 0) {
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+      best = v > best ? v : best;
     }
+    if (lane == 0 && best) atomicMax(a.f.argmax, best);
   }
 }
 
 using DecFnG = void (*)(const DecGemvArgs);
 
 template <int FMT>
-static DecFnG dec_fn_slots(int nslot, bool pair) {
-  if (pair) return nslot == 2 ? gemv_dec_kernel<FMT, 2, true> : gemv_dec_kernel<FMT, 1, true>;
-  return nslot == 2 ? gemv_dec_kernel<FMT, 2, false> : gemv_dec_kernel<FMT, 1, false>;
+static DecFnG dec_fn_ns(int ns) {
+  return ns >= 3 ? gemv_dec_kernel<FMT, 3> : ns == 2 ? gemv_dec_kernel<FMT, 2> : gemv_dec_kernel<FMT, 1>;
 }
 
-static DecFnG dec_gemv_fn(int type, int nslot, bool pair) {
+static DecFnG dec_gemv_fn(int type, int ns) {
   switch (type) {
-    case Q8_0: return dec_fn_slots<Q8_0>(nslot, pair);
-    case Q4_K: return dec_fn_slots<Q4_K>(nslot, pair);
-    case Q6_K: return dec_fn_slots<Q6_K>(nslot, pair);
+    case Q8_0: return dec_fn_ns<Q8_0>(ns);
+    case Q4_K: return dec_fn_ns<Q4_K>(ns);
+    case Q6_K: return dec_fn_ns<Q6_K>(ns);
     default: return nullptr;
   }
 }
 
-DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, bool pair, int fused_extra) {
+static int dec_ns(const DecGemvPlan& p) { return (p.stage_bytes / (8 * std::max(p.seg_cap, 16))); }
+
+DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, bool pair, bool fused,
+                          int fused_extra) {
   DecGemvPlan p{};
   p.type = type;
   p.rows = rows;
@@ -209,41 +348,71 @@ DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, b
   const int BS = block_size(type), TS = type_size(type);
   if (rows <= 0 || cols <= 0 || cols % BS || cols % 32 || (pair && rows % 2)) return p;
   p.row_bytes = cols / BS * TS;
-  p.nchunk16 = (p.row_bytes + 15) / 16 + 1;
-  p.warps = 16;
-  const int unit_bytes = (pair ? 2 : 1) * p.nchunk16 * 16;
-  p.nslot = unit_bytes <= 4608 ? 2 : 1;  // double-buffer units of up to 4.5 KB
-  p.stage_bytes = p.nslot * unit_bytes;
+  p.bpr = cols / BS;
+  p.bps = (p.bpr + kDecWarps - 1) / kDecWarps;
+  // 16-byte chunks of the aligned superset, rounded to an odd count: the
+  // 8 row slots then start in 8 different bank quads
+  int nch = (15 + p.bps * TS + 15) / 16;
+  if (!(nch & 1)) ++nch;
+  p.seg_cap = nch * 16;
+  p.ngroups = (rows + 7) / 8;
   auto al = [](size_t v) { return (int)((v + 127) / 128 * 128); };
   p.xs_off = 0;
-  p.extra_off = al((size_t)cols * 4);
+  p.extra_off = fused ? al((size_t)cols * 4) : 0;
   p.xsum_off = p.extra_off + al((size_t)std::max(fused_extra, 0));
   p.xq_off = p.xsum_off + al((size_t)(cols / 16 + 2 * (cols / 32)) * 4);
   const int xq1 = al((size_t)(cols + 8 * ((cols + 255) / 256)) * 2);
   p.xq2_off = p.xq_off + xq1;
   p.misc_off = p.xq2_off + xq1;
-  p.stage_off = p.misc_off + 512;
-  p.smem = (size_t)p.stage_off + (size_t)p.warps * p.stage_bytes;
-  if (p.smem > dev.smem_optin) return p;
-  DecFnG fn = dec_gemv_fn(type, p.nslot, pair);
-  if (!fn || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dev.smem_optin)) {
-    cudaGetLastError();
-    return p;
+  p.red_off = p.misc_off + 512;
+  p.stage_off = p.red_off + 512;
+  // slots per warp: as many groups in flight as a CTA will take (at most 3),
+  // fewer when that costs a CTA per SM
+  const int slot_bytes = 8 * p.seg_cap;
+  DecGemvPlan best{};
+  long long best_score = -1;
+  for (int ns = 1; ns <= 3; ++ns) {
+    DecGemvPlan q = p;
+    q.stage_bytes = ns * slot_bytes;
+    q.smem = (size_t)q.stage_off + (size_t)kDecWarps * q.stage_bytes;
+    if (q.smem > dev.smem_optin) break;
+    DecFnG fn = dec_gemv_fn(type, ns);
+    // the attribute is per kernel and device, shared by every plan: the device maximum
+    if (!fn || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dev.smem_optin)) {
+      cudaGetLastError();
+      break;
+    }
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kDecWarps * 32, q.smem) != cudaSuccess || occ < 1) {
+      cudaGetLastError();
+      break;
+    }
+    occ = std::min(occ, 3);
+    const int slots_total = occ * dev.sms;
+    const int gpc = (q.ngroups + slots_total - 1) / slots_total;  // groups per CTA
+    q.grid = (q.ngroups + gpc - 1) / gpc;
+    q.fast = 1;
+    // bytes in flight per SM while a CTA decodes, ties to fewer slots
+    const long long score = (long long)occ * std::min(ns, gpc) * 1000 - ns;
+    if (score > best_score) {
+      best_score = score;
+      best = q;
+    }
+    if (gpc <= ns) break;  // more slots than groups per CTA buy nothing
   }
-  const int units = rows / (pair ? 2 : 1);
-  p.grid = std::min(dev.sms, (units + p.warps - 1) / p.warps);
-  p.fast = 1;
-  return p;
+  if (!best.fast) return p;
+  return best;
 }
 
 int launch_gemv_dec(const DecGemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvFuse& f,
                     unsigned* status, cudaStream_t st, bool pdl) {
   cudaGetLastError();
-  if (!p.fast || (f.out_mode == OUT_GELU_PAIR) != (p.pair != 0)) return (int)cudaErrorInvalidValue;
+  if (!p.fast || (f.out_mode == OUT_GELU_PAIR) != (p.pair != 0) || (f.in_mode != IN_PLAIN && p.extra_off == 0))
+    return (int)cudaErrorInvalidValue;
   DecGemvArgs a{p, w, x, y, status, f};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
-  cfg.blockDim = dim3(32 * p.warps);
+  cfg.blockDim = dim3(32 * kDecWarps);
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -251,7 +420,7 @@ int launch_gemv_dec(const DecGemvPlan& p, const uint8_t* w, const float* x, floa
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return (int)cudaLaunchKernelEx(&cfg, dec_gemv_fn(p.type, p.nslot, p.pair != 0), a);
+  return (int)cudaLaunchKernelEx(&cfg, dec_gemv_fn(p.type, dec_ns(p)), a);
 }
 
 }  // namespace g4
