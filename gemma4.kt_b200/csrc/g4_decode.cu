@@ -35,6 +35,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <map>
 #include <new>
 #include <string>
@@ -46,9 +47,18 @@ constexpr int kAttnThreads = 256;
 constexpr int kMaxKvHeads = 64;      // KV heads per layer
 constexpr size_t kAttnTileBudget = 160 * 1024;  // shared memory for a chunk's K and V rows
 
+// Position chunks of the decoder's attention: at most kAttnMaxChunks per
+// query head, about len / 8 positions each, a multiple of 16, at most ch_max
+// (the shared-memory tile).
+constexpr int kAttnMaxChunks = 128;
+__host__ __device__ __forceinline__ int attn_chunk(int len, int ch_max) {
+  int ch = ((len + 7) / 8 + 15) / 16 * 16;
+  return ch < 16 ? 16 : ch > ch_max ? ch_max : ch;
+}
+
 struct AttnArgs {
   const float* qkv;        // raw projections: q [n_heads*hs] | k [n_kv*hs] | v [n_kv*hs]
-  int hs, n_kv, kv_mul, qdim, kvdim;
+  int hs, kv_mul, kvdim;
   int k_off, v_off;        // offsets of k and v in qkv (v_off == k_off when V = K)
   const float* q_norm;     // [hs]
   const float* k_norm;     // [hs]
@@ -61,7 +71,9 @@ struct AttnArgs {
   int window;              // sliding window (0: full attention)
   const int* step;
   const int* in_pos;
-  float* part;             // [n_kv][kAttnMaxChunks][kv_mul][hs + 2]
+  float* part;             // [n_heads][kAttnMaxChunks][hs + 2]: (max, sum, acc[hs]) per chunk
+  unsigned* tickets;       // [n_heads] chunks finished; the last one combines and resets it
+  float* out;              // [n_heads * hs] attention output
   int ch_max;              // positions per chunk that fit the shared-memory tiles (multiple of 16)
   unsigned* status;
 };
@@ -89,17 +101,15 @@ __device__ __forceinline__ void head_rope(float* v, const float* fr, const float
   __syncwarp();
 }
 
-// Attention of one layer (Llama.kt:157-218) for the KV-head group g and the
-// position chunk c of this CTA.  KVM = query heads per KV head.  The chunk's
-// K and V rows of earlier positions are final before the step starts, so
-// their bulk copies into shared memory are issued before waiting for the
-// q/k/v projection; everything after reads them from shared memory.  The
-// chunk's softmax partials go to `part`; the output projection's prologue
-// combines them (IN_ATTN_COMBINE).
-template <int KVM>
+// Attention of one layer (Llama.kt:157-218) for query head hq and position
+// chunk c of this CTA.  The chunk's K and V rows of earlier positions are
+// final before the step starts, so their bulk copies into shared memory (and
+// the RoPE row of the position) are issued before waiting for the q/k/v
+// projection.  Each chunk leaves (max, sum, acc) partials; the last chunk of
+// the head to finish (a ticket counter) combines them into the head's output.
 __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smraw[];
-  const int hs = a.hs;
+  const int hs = a.hs, half = hs / 2;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, NW = kAttnThreads / 32;
   // the step's position is staged by the host before the step's first kernel
   const int pos = a.in_pos[*a.step];
@@ -107,15 +117,19 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   const int len = pos - start + 1;
   const int ch = attn_chunk(len, a.ch_max);
   const int nch = (len + ch - 1) / ch;
-  const int g = blockIdx.x / kAttnMaxChunks, c = blockIdx.x % kAttnMaxChunks;
+  const int hq = blockIdx.x / kAttnMaxChunks, c = blockIdx.x % kAttnMaxChunks;
+  const int g = hq / a.kv_mul;
   if (c >= nch) return;
   const int t0 = start + c * ch, t1 = min(t0 + ch, pos + 1), n = t1 - t0;
   float* kt = reinterpret_cast<float*>(smraw);        // [ch_max][hs]
   float* vt = kt + (size_t)a.ch_max * hs;             // [ch_max][hs]
-  float* qs = vt + (size_t)a.ch_max * hs;             // [KVM][hs]
-  float* sc = qs + KVM * hs;                          // [KVM][ch_max] scores, then exp
-  float* st = sc + KVM * a.ch_max;                    // [KVM] max, [KVM] sum
-  uint64_t* bar = reinterpret_cast<uint64_t*>(st + 2 * KVM);
+  float* qs = vt + (size_t)a.ch_max * hs;             // [hs]
+  float* fr = qs + hs;                                // [hs/2] RoPE row of pos
+  float* fi = fr + half;
+  float* sc = fi + half;                              // [ch_max] scores, then exp
+  float* wc = sc + a.ch_max;                          // [kAttnMaxChunks] combine weights
+  float* st = wc + kAttnMaxChunks;                    // max, sum, denominator, last flag
+  uint64_t* bar = reinterpret_cast<uint64_t*>(st + 4);
 
   // rows t < pos of the chunk: bulk copies before the wait
   const int n_pre = max(0, min(t1, pos) - t0);
@@ -134,17 +148,19 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
       bulk_g2s(vt + (size_t)j * hs, a.vc + src, row_bytes, bar);
     }
   }
+  const bool has_pos = t1 == pos + 1;
+  for (int i = tid; i < half; i += kAttnThreads) {
+    fr[i] = a.cr[(size_t)pos * half + i];
+    fi[i] = a.ci[(size_t)pos * half + i];
+  }
   grid_dep_wait();
   grid_dep_launch();
-  const float* fr = a.cr + (size_t)pos * (hs / 2);
-  const float* fi = a.ci + (size_t)pos * (hs / 2);
-  const bool has_pos = t1 == pos + 1;
   float* kp = kt + (size_t)(pos - t0) * hs;  // the row of this position (when has_pos)
   float* vp = vt + (size_t)(pos - t0) * hs;
-  // q of the group's heads (Llama.kt:158-168) and, in the chunk holding the
-  // position, its K/V row: computed (Llama.kt:174-195) or, for a layer that
-  // shares an earlier layer's cache, read from it
-  for (int i = tid; i < KVM * hs; i += kAttnThreads) qs[i] = a.qkv[(size_t)g * KVM * hs + i];
+  // q of the head (Llama.kt:158-168) and, in the chunk holding the position,
+  // its K/V row: computed (Llama.kt:174-195) or, for a layer that shares an
+  // earlier layer's cache, read from it
+  for (int i = tid; i < hs; i += kAttnThreads) qs[i] = a.qkv[(size_t)hq * hs + i];
   if (has_pos) {
     const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
@@ -153,21 +169,20 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
     }
   }
   __syncthreads();
-  for (int h = warp; h < KVM; h += NW) {
-    head_rmsnorm(qs + h * hs, a.q_norm, hs, a.eps, lane);
-    head_rope(qs + h * hs, fr, fi, hs, lane);
-  }
-  if (has_pos && a.write_kv) {
+  if (warp == 0) {
+    head_rmsnorm(qs, a.q_norm, hs, a.eps, lane);
+    head_rope(qs, fr, fi, hs, lane);
+  } else if (has_pos && a.write_kv) {
     // K: learned norm then RoPE; V: bare norm (Llama.kt:183-195)
-    if (warp == NW - 1) {
+    if (warp == 1) {
       head_rmsnorm(kp, a.k_norm, hs, a.eps, lane);
       head_rope(kp, fr, fi, hs, lane);
-    } else if (warp == NW - 2) {
+    } else if (warp == 2) {
       head_rmsnorm(vp, nullptr, hs, a.eps, lane);
     }
   }
   __syncthreads();
-  if (has_pos && a.write_kv) {
+  if (has_pos && a.write_kv && hq % a.kv_mul == 0) {
     const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
       a.kc[row + i] = kp[i];
@@ -181,61 +196,98 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
     return;
   }
 
-  // scores q_h . k_t (Llama.kt:204-208)
+  // scores q . k_t (Llama.kt:204-208)
   for (int j = warp; j < n; j += NW) {
     const float* kr = kt + (size_t)j * hs;
-    float acc[KVM];
-#pragma unroll
-    for (int h = 0; h < KVM; ++h) acc[h] = 0.f;
-    for (int i = lane; i < hs; i += 32) {
-      const float kv = kr[i];
-#pragma unroll
-      for (int h = 0; h < KVM; ++h) acc[h] = fmaf(qs[h * hs + i], kv, acc[h]);
-    }
-#pragma unroll
-    for (int h = 0; h < KVM; ++h) {
-      const float s = warp_sum(acc[h]);
-      if (lane == 0) sc[h * a.ch_max + j] = s;
-    }
+    float acc = 0.f;
+    for (int i = lane; i < hs; i += 32) acc = fmaf(qs[i], kr[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) sc[j] = acc;
   }
   __syncthreads();
   // chunk softmax statistics: exp((s - m) as double), as softmaxInPlace (MutableFloatTensor.kt:54-59)
-  for (int h = warp; h < KVM; h += NW) {
+  if (warp == 0) {
     float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * a.ch_max + j]);
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
     for (int j = lane; j < n; j += 32) {
-      const float e = (float)exp((double)__fsub_rn(sc[h * a.ch_max + j], m));
-      sc[h * a.ch_max + j] = e;
+      const float e = (float)exp((double)__fsub_rn(sc[j], m));
+      sc[j] = e;
       l += e;
     }
     l = warp_sum(l);
     if (lane == 0) {
-      st[h] = m;
-      st[KVM + h] = l;
+      st[0] = m;
+      st[1] = l;
     }
   }
   __syncthreads();
   // partial V sums (Llama.kt:211-217)
-  float* part = a.part + ((size_t)g * kAttnMaxChunks + c) * KVM * (hs + 2);
+  float* part = a.part + ((size_t)hq * kAttnMaxChunks + c) * (hs + 2);
   for (int d = tid; d < hs; d += kAttnThreads) {
-    float acc[KVM];
+    float acc = 0.f;
+    for (int j = 0; j < n; ++j) acc = fmaf(sc[j], vt[(size_t)j * hs + d], acc);
+    part[2 + d] = acc;
+  }
+  if (tid == 0) {
+    part[0] = st[0];
+    part[1] = st[1];
+  }
+  // the head's last chunk to finish combines the partials (release: fence, then the ticket)
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned done = atomicAdd(a.tickets + hq, 1u);
+    st[3] = done + 1 == (unsigned)nch ? 1.f : 0.f;
+  }
+  __syncthreads();
+  if (st[3] == 0.f) return;
+  __threadfence();  // acquire: the other chunks' partials are visible
+  const float* ph = a.part + (size_t)hq * kAttnMaxChunks * (hs + 2);
+  // out = sum_c w_c acc_c / sum_c w_c l_c, w_c = exp(m_c - max m) (Llama.kt:201-218 over the chunks)
+  if (warp == 0) {
+    float mc[kAttnMaxChunks / 32], lc[kAttnMaxChunks / 32];
 #pragma unroll
-    for (int h = 0; h < KVM; ++h) acc[h] = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const float vv = vt[(size_t)j * hs + d];
-#pragma unroll
-      for (int h = 0; h < KVM; ++h) acc[h] = fmaf(sc[h * a.ch_max + j], vv, acc[h]);
+    for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
+      const int k = lane + 32 * j;
+      mc[j] = k < nch ? __ldcg(ph + (size_t)k * (hs + 2)) : -INFINITY;
+      lc[j] = k < nch ? __ldcg(ph + (size_t)k * (hs + 2) + 1) : 0.f;
     }
+    float M = -INFINITY;
 #pragma unroll
-    for (int h = 0; h < KVM; ++h) part[(size_t)h * (hs + 2) + 2 + d] = acc[h];
+    for (int j = 0; j < kAttnMaxChunks / 32; ++j) M = fmaxf(M, mc[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float dsum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
+      const int k = lane + 32 * j;
+      if (k < nch) {
+        const float w = (float)exp((double)__fsub_rn(mc[j], M));
+        wc[k] = w;
+        dsum = fmaf(w, lc[j], dsum);
+      }
+    }
+    dsum = warp_sum(dsum);
+    if (lane == 0) st[2] = dsum;
   }
-  if (tid < KVM) {
-    part[(size_t)tid * (hs + 2)] = st[tid];
-    part[(size_t)tid * (hs + 2) + 1] = st[KVM + tid];
+  __syncthreads();
+  constexpr int kCh = 8;  // chunk loads issued together
+  for (int d = tid; d < hs; d += kAttnThreads) {
+    float num = 0.f;
+    for (int k0 = 0; k0 < nch; k0 += kCh) {
+      float v[kCh];
+#pragma unroll
+      for (int j = 0; j < kCh; ++j) v[j] = k0 + j < nch ? __ldcg(ph + (size_t)(k0 + j) * (hs + 2) + 2 + d) : 0.f;
+#pragma unroll
+      for (int j = 0; j < kCh; ++j)
+        if (k0 + j < nch) num = fmaf(wc[k0 + j], v[j], num);
+    }
+    a.out[(size_t)hq * hs + d] = __fdiv_rn(num, st[2]);
   }
+  if (tid == 0) a.tickets[hq] = 0u;  // every chunk has arrived: ready for the next launch
 }
 
 // Greedy sampling (Sampler.ARGMAX, FloatTensor.argmax): the logits GEMV left
@@ -301,10 +353,9 @@ struct g4_model {
   std::vector<LayerDev> L;
   const g4_tensor* wcls = nullptr;
   GemvPlan p_logits{};
-  DecGemvPlan d_logits{};  // the decoder GEMV when the format has one
   float *cr_full = nullptr, *ci_full = nullptr, *cr_swa = nullptr, *ci_swa = nullptr;
   bool finalized = false;
-  int max_q = 0, max_kv = 0, max_ff = 0, max_hs = 0, max_kvm = 0;
+  int max_q = 0, max_kv = 0, max_ff = 0, max_hs = 0;
 
   const g4_tensor* get(const std::string& n) const {
     auto it = t.find(n);
@@ -326,6 +377,7 @@ struct g4_state {
   uint8_t* small = nullptr;     // argmax key, step control
   unsigned long long* argmax = nullptr;
   int* ctl = nullptr;     // [0] step, [1] next token, then in_tok[ctx], in_pos[ctx], out_tok[ctx]
+  unsigned* tickets = nullptr;  // attention: chunks finished per query head (zero between launches)
   int* h_ctl = nullptr;   // pinned staging of the same layout
   cudaGraphExec_t graph = nullptr;
   int* in_tok() const { return ctl + 4; }
@@ -371,12 +423,6 @@ int g4_model_create(g4_ctx* c, const g4_model_config* cfg, g4_model** out) {
                  kMaxKvHeads);
       return G4_E_ARG;
     }
-    const int kvm = k.n_heads / m->n_kv[l];
-    if (kvm != 1 && kvm != 2 && kvm != 4 && kvm != 8 && kvm != 16) {
-      delete m;
-      c->set_err("g4_model_create: %d query heads per KV head is not supported", kvm);
-      return G4_E_ARG;
-    }
     const int chm = (int)std::min<size_t>(256, kAttnTileBudget / ((size_t)hs * 8) / 16 * 16);
     if (chm < 16 || k.ctx_len > kAttnMaxChunks * chm) {
       delete m;
@@ -388,7 +434,6 @@ int g4_model_create(g4_ctx* c, const g4_model_config* cfg, g4_model** out) {
     m->max_kv = std::max(m->max_kv, m->n_kv[l] * hs);
     m->max_ff = std::max(m->max_ff, m->ff[l]);
     m->max_hs = std::max(m->max_hs, hs);
-    m->max_kvm = std::max(m->max_kvm, kvm);
   }
   *out = m;
   return 0;
@@ -659,8 +704,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
     o.latency = true;
     o.fused = true;
     L.p_qkv = plan_gemv(c->dev, L.qkv->type, 0, qkv_rows, dim, o);
-    GemvOpts oc = o;  // the attention combine needs its chunk weights in shared memory
-    oc.fused_extra = (k.n_heads * (kAttnMaxChunks + 1)) * 4;
+    GemvOpts oc = o;  // the attention output is final: no prologue
+    oc.fused = false;
     L.p_wo = plan_gemv(c->dev, L.wo->type, 0, dim, L.qdim, oc);
     GemvOpts op = o;
     op.pair_rows = true;
@@ -668,11 +713,10 @@ extern "C" int g4_model_finalize(g4_model* m) {
     GemvOpts od = o;
     od.fused = false;
     L.p_down = plan_gemv(c->dev, L.down->type, 0, dim, L.ff, od);
-    const int comb_extra = (k.n_heads * (kAttnMaxChunks + 1)) * 4;
-    L.d_qkv = plan_gemv_dec(c->dev, L.qkv->type, qkv_rows, dim, false, true, 0);
-    L.d_wo = plan_gemv_dec(c->dev, L.wo->type, dim, L.qdim, false, true, comb_extra);
-    L.d_gu = plan_gemv_dec(c->dev, L.gate_up->type, 2 * L.ff, dim, true, true, 0);
-    L.d_down = plan_gemv_dec(c->dev, L.down->type, dim, L.ff, false, false, 0);
+    L.d_qkv = plan_gemv_dec(c->dev, L.qkv->type, qkv_rows, dim, false, true);
+    L.d_wo = plan_gemv_dec(c->dev, L.wo->type, dim, L.qdim, false, false);
+    L.d_gu = plan_gemv_dec(c->dev, L.gate_up->type, 2 * L.ff, dim, true, true);
+    L.d_down = plan_gemv_dec(c->dev, L.down->type, dim, L.ff, false, false);
     if ((!L.p_qkv.fast && !L.d_qkv.fast) || (!L.p_gu.fast && !L.d_gu.fast) || (!L.p_wo.fast && !L.d_wo.fast) ||
         (!L.p_down.fast && !L.d_down.fast)) {
       c->set_err("g4_model_finalize: layer %d: the projections need a streaming-kernel format "
@@ -684,8 +728,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
   ol.fused = true;
   ol.exact_x = true;
   m->p_logits = plan_gemv(c->dev, m->wcls->type, 0, k.vocab, dim, ol);
-  m->d_logits = plan_gemv_dec(c->dev, m->wcls->type, k.vocab, dim, false, true, 0);
-  if (!m->d_logits.fast && (!m->p_logits.fast || m->p_logits.pr != 1)) {
+  if (!m->p_logits.fast || m->p_logits.pr != 1) {
     c->set_err("g4_model_finalize: the output projection needs a streaming-kernel format");
     return G4_E_TYPE;
   }
@@ -773,7 +816,8 @@ extern "C" int g4_state_create(g4_model* m, g4_state** out) {
     s->vc.push_back(s->buf + o_vc[l]);
   }
   const size_t ctl_ints = 4 + 3 * (size_t)k.ctx_len;
-  const size_t small = 256 + ctl_ints * 4;
+  const size_t tickets_off = 256 + (ctl_ints * 4 + 255) / 256 * 256;
+  const size_t small = tickets_off + (size_t)k.n_heads * 4;
   if (cudaMalloc(&s->small, small) != cudaSuccess || cudaMallocHost(&s->h_ctl, ctl_ints * 4) != cudaSuccess ||
       cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
     cudaGetLastError();
@@ -784,6 +828,7 @@ extern "C" int g4_state_create(g4_model* m, g4_state** out) {
   cudaMemset(s->small, 0, small);
   s->argmax = reinterpret_cast<unsigned long long*>(s->small);
   s->ctl = reinterpret_cast<int*>(s->small + 256);
+  s->tickets = reinterpret_cast<unsigned*>(s->small + tickets_off);
   // The MoE layers take their work buffers from the context's arena: size it
   // (and set the kernels up) now, outside any stream capture.
   if (k.n_expert > 0) {
@@ -817,20 +862,10 @@ extern "C" int g4_state_free(g4_state* s) {
 
 // Positions per attention chunk that fit kAttnTileBudget (K and V rows), a multiple of 16.
 static int attn_ch_max(int hs) { return (int)std::min<size_t>(256, kAttnTileBudget / ((size_t)hs * 8) / 16 * 16); }
-static size_t attn_smem(int hs, int kvm) {
+// K and V tiles, q, the RoPE row, scores, combine weights, 4 statistics, the mbarrier
+static size_t attn_smem(int hs) {
   const size_t ch = (size_t)attn_ch_max(hs);
-  return (2 * ch * hs + (size_t)kvm * hs + (size_t)kvm * ch + 2 * kvm + 4) * 4;
-}
-
-using AttnFn = void (*)(const AttnArgs);
-static AttnFn attn_fn(int kvm) {
-  switch (kvm) {
-    case 1: return dec_attention_kernel<1>;
-    case 2: return dec_attention_kernel<2>;
-    case 4: return dec_attention_kernel<4>;
-    case 8: return dec_attention_kernel<8>;
-    default: return dec_attention_kernel<16>;
-  }
+  return ((2 * ch * hs + 2 * (size_t)hs + ch + kAttnMaxChunks + 4) * 4 + 7) / 8 * 8 + 8;
 }
 
 template <typename... KArgs, typename... Args>
@@ -847,6 +882,16 @@ static cudaError_t launch_pdl_k(void (*kern)(KArgs...), int grid, int block, siz
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+static void set_prefetch(GemvFuse& f, std::initializer_list<const g4_tensor*> ts) {
+  int k = 0;
+  for (const g4_tensor* t : ts)
+    if (t && k < GemvFuse::kPrefetch) {
+      f.pf[k] = (const uint8_t*)t->d;
+      f.pf_bytes[k] = (long long)t->nbytes;
+      ++k;
+    }
 }
 
 // Enqueue one decode step on s->st (captured into the graph).
@@ -892,6 +937,8 @@ static int enqueue_step(g4_state* s) {
       f.w_r = branch_w;
       f.scale = branch_scale;
     }
+    // this layer's remaining projections stream into L2 during q|k|v and the attention
+    set_prefetch(f, {L.wo, L.gate_up, L.down});
     int e = launch_proj(L.d_qkv, L.p_qkv, L.qkv, s->x[cur], s->qkv, f, c->status, st, l > 0);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: qkv projection");
     cur ^= 1;
@@ -899,9 +946,7 @@ static int enqueue_step(g4_state* s) {
     AttnArgs aa{};
     aa.qkv = s->qkv;
     aa.hs = L.hs;
-    aa.n_kv = L.n_kv;
     aa.kv_mul = k.n_heads / L.n_kv;
-    aa.qdim = L.qdim;
     aa.kvdim = L.kvdim;
     const bool own = l < k.n_layer_kv_from_start;
     aa.k_off = L.qdim;
@@ -918,25 +963,18 @@ static int enqueue_step(g4_state* s) {
     aa.step = step;
     aa.in_pos = s->in_pos();
     aa.part = s->part;
+    aa.tickets = s->tickets;
+    aa.out = s->xbk;
     aa.ch_max = attn_ch_max(L.hs);
     aa.status = c->status;
-    const size_t asmem = attn_smem(L.hs, aa.kv_mul);
-    AttnFn af = attn_fn(aa.kv_mul);
-    if (asmem > 48 * 1024 && cudaFuncSetAttribute(af, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem))
+    const size_t asmem = attn_smem(L.hs);
+    if (asmem > 48 * 1024 &&
+        cudaFuncSetAttribute(dec_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem))
       return c->cuda_fail(cudaGetLastError(), "decode: attention set-up");
-    cudaError_t ce = launch_pdl_k(af, L.n_kv * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
+    cudaError_t ce = launch_pdl_k(dec_attention_kernel, k.n_heads * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
     if (ce) return c->cuda_fail(ce, "decode: attention");
-    // ---- output projection, prologue: the attention output from the chunk partials
-    GemvFuse fc;
-    fc.in_mode = IN_ATTN_COMBINE;
-    fc.part = s->part;
-    fc.step = step;
-    fc.in_pos = s->in_pos();
-    fc.hs = L.hs;
-    fc.kv_mul = aa.kv_mul;
-    fc.window = aa.window;
-    fc.ch_max = aa.ch_max;
-    e = launch_proj(L.d_wo, L.p_wo, L.wo, s->xbk, s->xb2, fc, c->status, st, true);
+    // ---- output projection of the attention output
+    e = launch_proj(L.d_wo, L.p_wo, L.wo, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: output projection");
     // ---- gate / up, prologue: x += rmsnorm(xb2, post_attention_norm); rmsnorm(x, ffn_norm)
     GemvFuse g;
@@ -947,6 +985,7 @@ static int enqueue_step(g4_state* s) {
     g.w_r = L.post_attn_norm;
     g.w_in = L.ffn_norm;
     g.x_out = s->x[cur ^ 1];
+    if (l + 1 < k.n_layers) set_prefetch(g, {m->L[l + 1].qkv});  // the next layer's first projection
     e = launch_proj(L.d_gu, L.p_gu, L.gate_up, s->x[cur], s->hb, g, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: gate/up projection");
     cur ^= 1;
@@ -978,7 +1017,8 @@ static int enqueue_step(g4_state* s) {
   f.w_in = m->f32("output_norm.weight");
   f.softcap = k.logit_softcap;
   f.argmax = s->argmax;
-  int e = launch_proj(m->d_logits, m->p_logits, m->wcls, s->x[cur], s->logits, f, c->status, st, true);
+  set_prefetch(f, {m->L[0].qkv});  // the next step's first projection
+  int e = launch_gemv_fused(m->p_logits, (const uint8_t*)m->wcls->d, s->x[cur], s->logits, f, c->status, st, true);
   if (e) return c->cuda_fail((cudaError_t)e, "decode: logits");
   cudaError_t ce = launch_pdl_k(dec_sample_kernel, 1, 32, 0, st, s->ctl, s->out_tok(), s->argmax);
   if (ce) return c->cuda_fail(ce, "decode: sampling");

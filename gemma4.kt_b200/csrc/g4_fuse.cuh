@@ -1,6 +1,6 @@
 // g4_fuse.cuh -- the fused prologues and epilogues of the decoder's GEMV
 // launches (GemvFuse, g4_gemv.cuh): the activation vector computed from the
-// kernel's inputs (norms, residual, embedding, MoE merge, attention combine)
+// kernel's inputs (norms, residual, embedding, MoE merge)
 // and the row post-processing (GELU pairs, softcap + argmax).
 #pragma once
 #include "g4_gemv.cuh"
@@ -23,10 +23,13 @@ struct PrologueConst {
   float wi[kPrologueMaxE], wr[kPrologueMaxE], wm[kPrologueMaxE];
   bool loaded;
 };
+// IN: the kernel's prologue mode when fixed at compile time (-1: f.in_mode).
+template <int IN = -1>
 static __device__ __forceinline__ void prologue_const(const GemvFuse& f, int n, PrologueConst& c) {
-  c.loaded = f.in_mode != IN_PLAIN && f.in_mode != IN_ATTN_COMBINE && n <= kPrologueMaxE * (int)blockDim.x;
+  const int mode = IN >= 0 ? IN : f.in_mode;
+  c.loaded = mode != IN_PLAIN && n <= kPrologueMaxE * (int)blockDim.x;
   if (!c.loaded) return;
-  const bool merge = f.in_mode == IN_MOE_MERGE, resid = f.in_mode == IN_RESID_NORM || merge;
+  const bool merge = mode == IN_MOE_MERGE, resid = mode == IN_RESID_NORM || merge;
 #pragma unroll
   for (int k = 0; k < kPrologueMaxE; ++k) {
     const int i = threadIdx.x + k * blockDim.x;
@@ -39,91 +42,17 @@ static __device__ __forceinline__ void prologue_const(const GemvFuse& f, int n, 
   }
 }
 
+template <int IN = -1>
 static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict__ x, float* xs, float* red, int n,
-                               float* extra, const PrologueConst* pc = nullptr) {
+                                      const PrologueConst* pc = nullptr) {
+  const int mode = IN >= 0 ? IN : f.in_mode;
   const int tid = threadIdx.x, nt = blockDim.x;
   const bool store = f.x_out != nullptr && blockIdx.x == 0;
-  if (f.in_mode == IN_ATTN_COMBINE) {
-    // Llama.kt:201-218 from the attention kernel's chunk partials (max m_c,
-    // sum l_c of exp(s - m_c), acc_c = sum exp(s - m_c) v): per head
-    // out = sum_c w_c acc_c / sum_c w_c l_c with w_c = exp(m_c - max m)
-    const int pos = f.in_pos[*f.step];
-    const int start = f.window > 0 ? max(0, pos - f.window + 1) : 0;
-    const int len = pos - start + 1;
-    const int nch = (len + attn_chunk(len, f.ch_max) - 1) / attn_chunk(len, f.ch_max);
-    const int hs = f.hs, kvm = f.kv_mul, n_heads = n / hs;
-    const size_t hstride = (size_t)hs + 2, cstride = (size_t)kvm * hstride;
-    float* wt = extra;                           // [n_heads][kAttnMaxChunks]
-    float* den = extra + n_heads * kAttnMaxChunks;  // [n_heads]
-    const int warp = tid >> 5, lane = tid & 31, W = nt >> 5;
-    for (int h = warp; h < n_heads; h += W) {
-      const float* ph = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride;
-      float mc[kAttnMaxChunks / 32], lc[kAttnMaxChunks / 32];
-#pragma unroll
-      for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
-        const int k = lane + 32 * j;
-        mc[j] = k < nch ? __ldcg(ph + (size_t)k * cstride) : -INFINITY;
-        lc[j] = k < nch ? __ldcg(ph + (size_t)k * cstride + 1) : 0.f;
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < kAttnMaxChunks / 32; ++j) M = fmaxf(M, mc[j]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      float dsum = 0.f;
-#pragma unroll
-      for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
-        const int k = lane + 32 * j;
-        if (k < nch) {
-          const float w = (float)exp((double)__fsub_rn(mc[j], M));
-          wt[h * kAttnMaxChunks + k] = w;
-          dsum = fmaf(w, lc[j], dsum);
-        }
-      }
-      dsum = warp_sum(dsum);
-      if (lane == 0) den[h] = dsum;
-    }
-    __syncthreads();
-    constexpr int kOut = 4;  // outputs per thread per round
-    constexpr int kCh = 4;   // chunks whose loads are issued together
-    for (int i0 = tid; i0 < n; i0 += kOut * nt) {
-      float num[kOut];
-      const float* ph[kOut];
-      const float* w[kOut];
-#pragma unroll
-      for (int q = 0; q < kOut; ++q) {
-        const int i = min(i0 + q * nt, n - 1);
-        const int h = i / hs, d = i % hs;
-        ph[q] = f.part + (size_t)(h / kvm) * kAttnMaxChunks * cstride + (size_t)(h % kvm) * hstride + 2 + d;
-        w[q] = wt + h * kAttnMaxChunks;
-        num[q] = 0.f;
-      }
-      for (int k0 = 0; k0 < nch; k0 += kCh) {
-        float v[kOut][kCh];
-#pragma unroll
-        for (int q = 0; q < kOut; ++q)
-#pragma unroll
-          for (int j = 0; j < kCh; ++j) v[q][j] = k0 + j < nch ? __ldcg(ph[q] + (size_t)(k0 + j) * cstride) : 0.f;
-#pragma unroll
-        for (int q = 0; q < kOut; ++q)
-#pragma unroll
-          for (int j = 0; j < kCh; ++j)
-            if (k0 + j < nch) num[q] = fmaf(w[q][k0 + j], v[q][j], num[q]);
-      }
-#pragma unroll
-      for (int q = 0; q < kOut; ++q) {
-        const int i = i0 + q * nt;
-        if (i < n) xs[i] = __fdiv_rn(num[q], den[i / hs]);
-      }
-    }
-    __syncthreads();
-    return;
-  }
   constexpr int kMaxE = kPrologueMaxE;
   if (n <= kMaxE * nt) {
     // every input this thread needs, loaded in one round, then the passes in registers
-    const bool merge = f.in_mode == IN_MOE_MERGE, embed = f.in_mode == IN_EMBED_NORM;
-    const bool resid = f.in_mode == IN_RESID_NORM || merge;
+    const bool merge = mode == IN_MOE_MERGE, embed = mode == IN_EMBED_NORM;
+    const bool resid = mode == IN_RESID_NORM || merge;
     float xv[kMaxE], rv[kMaxE], wr[kMaxE], mv[kMaxE], wm[kMaxE], wi[kMaxE];
     long long ebase = 0;
     if (embed) {
@@ -198,13 +127,13 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
     return;
   }
   float ss = 0.f;
-  if (f.in_mode == IN_NORM) {
+  if (mode == IN_NORM) {
     for (int i = tid; i < n; i += nt) {
       const float v = x[i];
       xs[i] = v;
       ss = __fadd_rn(ss, __fmul_rn(v, v));
     }
-  } else if (f.in_mode == IN_EMBED_NORM) {
+  } else if (mode == IN_EMBED_NORM) {
     // Llama.kt:112-113: x = tokenEmbeddingTable.get(token * dim + i) * sqrt(dim)
     const int s = *f.step;
     int tok = f.in_tok[s];
@@ -225,7 +154,7 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
       s_r = rms_scale(block_sum(sr, red), n, f.eps);
     }
     float s_m = 0.f;
-    if (f.in_mode == IN_MOE_MERGE) {
+    if (mode == IN_MOE_MERGE) {
       // xb = rmsnorm(shared, post_ffw_norm_1) + moeOutput (Llama.kt:237-243, 349)
       float st = 0.f;
       for (int i = tid; i < n; i += nt) {
@@ -237,7 +166,7 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
     }
     for (int i = tid; i < n; i += nt) {
       float v = x[i];
-      if (f.in_mode == IN_MOE_MERGE) v = __fadd_rn(v, __fmul_rn(f.w_m[i], __fmul_rn(s_m, xs[i])));
+      if (mode == IN_MOE_MERGE) v = __fadd_rn(v, __fmul_rn(f.w_m[i], __fmul_rn(s_m, xs[i])));
       else if (f.r) v = __fadd_rn(v, __fmul_rn(f.w_r[i], __fmul_rn(s_r, f.r[i])));
       if (f.scale != 1.f) v = __fmul_rn(v, f.scale);  // Llama.kt:393-397
       xs[i] = v;

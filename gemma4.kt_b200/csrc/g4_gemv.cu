@@ -119,12 +119,13 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
   // flight before this waits for them (programmatic dependent launch; both
   // are no-ops for a plain launch).  Dependents launch only after the wait,
   // so everything two kernels back has completed when they start.
+  issue_l2_prefetch(a.f);
   grid_dep_wait();
   grid_dep_launch();
   float* misc = reinterpret_cast<float*>(smem + p.misc_off);
   const float* src = a.x;
   if (a.f.in_mode != IN_PLAIN) {
-    fused_prologue(a.f, a.x, xs, misc, p.cols, reinterpret_cast<float*>(smem + p.extra_off));
+    fused_prologue(a.f, a.x, xs, misc, p.cols);
     src = xs;
   }
 
@@ -445,7 +446,6 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   const bool quantized = type == Q8_0 || type == Q4_K || type == Q6_K;
   // a fused prologue stages the fp32 activation in shared memory for every format
   const int xbytes = quantized && !fused ? 0 : ((cols * 4 + 127) / 128) * 128;
-  const int extra = fused ? (o.fused_extra + 127) / 128 * 128 : 0;
   constexpr int kMiscBytes = 512;  // block reductions and the argmax epilogue
   // per-16 and per-32 column sums, per-32 int16 scales; int16 activations
   const int xsbytes = (((cols / 16 + 2 * (cols / 32)) * 4 + 127) / 128) * 128;
@@ -484,7 +484,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   size_t stage = (size_t)rows_per_group * p.pitch;
   const size_t optin = dev.smem_optin > 0 ? dev.smem_optin : 227 * 1024;
   const size_t budget = max_smem > 0 ? std::min(max_smem, optin) : optin;
-  const size_t fixed = (size_t)xbytes + extra + xsbytes + xqbytes + kMiscBytes + 256;
+  const size_t fixed = (size_t)xbytes + xsbytes + xqbytes + kMiscBytes + 256;
   if (small) {
     p.split = std::min(p.nchunks, 8);
     p.warps = p.split;
@@ -517,9 +517,8 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
     }
   }
   p.xs_off = 0;
-  p.extra_off = xbytes;
-  p.xsum_off = xbytes + extra;
-  p.xq_off = xbytes + extra + xsbytes;
+  p.xsum_off = xbytes;
+  p.xq_off = xbytes + xsbytes;
   p.xq2_off = p.xq_off + xq1;
   p.misc_off = p.xq_off + xqbytes;
   p.bar_off = p.misc_off + kMiscBytes;

@@ -27,7 +27,6 @@ struct GemvPlan {
   int fast;          // 1: streaming kernel; 0: generic fallback
   int fused;         // planned for a fused prologue (fp32 activation staged in shared memory)
   int x2;            // two-part int16 activations (fp32-level products) for the quantized formats
-  int extra_off;     // fused prologue work space (GemvOpts::fused_extra bytes)
 };
 
 // Plan of the decoder's GEMV (gemv_dec_kernel): CTAs of kDecWarps warps, each
@@ -38,6 +37,7 @@ struct GemvPlan {
 // slots, the next group's in flight while this one is decoded.  Q8_0 / Q4_K /
 // Q6_K rows of whole blocks, two-part activations.
 constexpr int kDecWarps = 8;
+constexpr int kDecGemvMaxSlots = 3;
 struct DecGemvPlan {
   int type, rows, cols;
   int pair;          // 1: rows (2i, 2i + 1) -> one output each (gelu(gate) * up)
@@ -46,8 +46,10 @@ struct DecGemvPlan {
   int seg_cap;       // bytes of a row-segment slot (16-byte multiple)
   int ngroups;       // row groups of 8
   int grid;
-  int xs_off, extra_off, xsum_off, xq_off, xq2_off, misc_off, red_off, stage_off;
-  int stage_bytes;   // per warp: 2 slots x 8 rows x seg_cap
+  int fused;         // room for a fused prologue (fp32 activation in shared memory at xs_off)
+  int xs_off, xsum_off, xq_off, xq2_off, misc_off, red_off, stage_off;
+  int ns;            // slots per warp (groups in flight), 1..kDecGemvMaxSlots
+  int stage_bytes;   // per warp: ns slots x 8 rows x seg_cap
   size_t smem;
   int fast;
 };
@@ -55,21 +57,11 @@ struct DecGemvPlan {
 // Options of plan_gemv.
 struct GemvOpts {
   bool fused = false;     // room for a fused prologue (fp32 activation in shared memory)
-  int fused_extra = 0;    // further shared memory for the prologue (IN_ATTN_COMBINE weights)
   size_t max_smem = 0;    // cap on the plan's shared memory (0: the device maximum)
   bool exact_x = false;   // two-part int16 activations (Q8_0 / Q4_K / Q6_K, rows of whole blocks)
   bool latency = false;   // decode-size matrix: persistent CTAs with a warp (or half) per row
   bool pair_rows = false; // the epilogue pairs rows 2i, 2i + 1 (needs two rows per warp)
 };
-
-// Position chunks of the decoder's attention (shared by the attention kernel
-// and the combine prologue): at most kAttnMaxChunks per KV head, about len / 8
-// positions each, a multiple of 16, at most ch_max (the shared-memory tile).
-constexpr int kAttnMaxChunks = 128;
-__host__ __device__ __forceinline__ int attn_chunk(int len, int ch_max) {
-  int ch = ((len + 7) / 8 + 15) / 16 * 16;
-  return ch < 16 ? 16 : ch > ch_max ? ch_max : ch;
-}
 
 // Fused prologue / epilogue of the decoder's GEMV launches (GemvFuse.in_mode /
 // out_mode).  The prologue turns the kernel's inputs into the activation
@@ -80,7 +72,6 @@ enum FuseIn : int {
   IN_RESID_NORM = 2,  // xn = (x + rmsnorm(r, w_r)) * scale [r optional]; act = rmsnorm(xn, w_in)
   IN_EMBED_NORM = 3,  // xn = emb.get(tok * dim + i) * sqrt(dim); act = rmsnorm(xn, w_in)  Llama.kt:112-113
   IN_MOE_MERGE = 4,   // xn = (x + rmsnorm(rmsnorm(r, w_r) + m, w_m)) * scale; act = rmsnorm(xn, w_in)  Llama.kt:349-353
-  IN_ATTN_COMBINE = 5,  // act = attention output from the per-chunk softmax partials   Llama.kt:201-218
 };
 enum FuseOut : int {
   OUT_PLAIN = 0,           // y[row] = dot
@@ -106,11 +97,34 @@ struct GemvFuse {
   const int* in_tok = nullptr;
   const int* next_tok = nullptr;
   unsigned long long* argmax = nullptr;  // OUT_SOFTCAP_ARGMAX: atomicMax of (ordered value << 32 | ~row)
-  // IN_ATTN_COMBINE: partials [n_kv][kAttnMaxChunks][kv_mul][hs + 2] = (max, sum, acc[hs]) per head
-  const float* part = nullptr;
-  const int* in_pos = nullptr;  // with step: the position, for the chunk geometry
-  int hs = 0, kv_mul = 1, window = 0, ch_max = 16;
+  // Weights of later kernels to pull into L2 while this one runs (16-byte
+  // aligned ranges, sizes rounded up to 16 inside the tensors' padding); the
+  // CTAs split each range and request it before they wait for their inputs.
+  static constexpr int kPrefetch = 4;
+  const uint8_t* pf[kPrefetch] = {nullptr, nullptr, nullptr, nullptr};
+  long long pf_bytes[kPrefetch] = {0, 0, 0, 0};
 };
+
+// Bulk prefetch of global memory into L2 (no shared-memory destination).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// This CTA's share of the GemvFuse prefetch ranges, issued by one thread.
+__device__ __forceinline__ void issue_l2_prefetch(const GemvFuse& f) {
+  if (threadIdx.x != 0) return;
+#pragma unroll
+  for (int k = 0; k < GemvFuse::kPrefetch; ++k) {
+    if (!f.pf[k] || f.pf_bytes[k] <= 0) continue;
+    const long long n = (f.pf_bytes[k] + 15) & ~15ll;
+    const long long share = ((n + gridDim.x - 1) / gridDim.x + 15) & ~15ll;
+    const long long b0 = share * blockIdx.x, b1 = b0 + share < n ? b0 + share : n;
+    for (long long o = b0; o < b1; o += 65536) {
+      const long long len = b1 - o < 65536 ? b1 - o : 65536;
+      prefetch_l2(f.pf[k] + o, (uint32_t)len);
+    }
+  }
+}
 
 // Magic-number int->float: 2^23 + b as float bits, then subtract 2^23 (+bias).
 // Exact for 0 <= b < 2^23 and avoids the quarter-rate I2F path.

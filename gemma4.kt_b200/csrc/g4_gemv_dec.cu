@@ -12,8 +12,8 @@
 //    shared-memory broadcast) and each lane decodes whole units (a Q8_0
 //    block, a 64-column group of a Q4_K block, half a Q6_K block);
 //  * each warp copies its 8 row segments (16-byte aligned supersets) with
-//    16-byte cp.async into its own slots, NS - 1 groups ahead of the one it
-//    decodes; the first NS groups are requested before the kernel waits for
+//    16-byte cp.async into its own slots, ns - 1 groups ahead of the one it
+//    decodes; the first ns groups are requested before the kernel waits for
 //    its predecessor (programmatic dependent launch: weights never change);
 //  * the 8 warps' partial sums meet in shared memory (one barrier per group)
 //    and warp 0 finishes the rows in a fixed order: plain, gelu(gate) * up on
@@ -37,6 +37,16 @@ struct DecGemvArgs {
   unsigned* status;
   GemvFuse f;
 };
+
+// x rounded to the nearest integer (ties to even) for |x| < 2^22, as a float
+// and as an int, on the FMA / ALU pipes (adding 1.5 * 2^23 leaves the integer
+// in the low mantissa bits).
+__device__ __forceinline__ float round_small(float x, int& i) {
+  constexpr float kMagic = 12582912.0f;
+  const float t = __fadd_rn(x, kMagic);
+  i = __float_as_int(t) - 0x4B400000;
+  return __fsub_rn(t, kMagic);
+}
 
 // 16-byte global -> shared copy (cp.async, L2 only); completion by commit groups.
 __device__ __forceinline__ void cp16(void* dst, const void* src) {
@@ -170,8 +180,16 @@ __device__ __forceinline__ float dec_unit(const uint8_t* blk, int sub, int e0, c
   }
 }
 
-// NS slots per warp: groups it + 1 .. it + NS - 1 stream in while group it is decoded.
-template <int FMT, int NS>
+// Waits until at most n of this thread's cp.async groups are pending (n < kDecGemvMaxSlots).
+__device__ __forceinline__ void cp_wait_n(int n) {
+  if (n <= 0) cp_wait<0>();
+  else if (n == 1) cp_wait<1>();
+  else cp_wait<2>();
+}
+
+// p.ns slots per warp: groups it + 1 .. it + ns - 1 stream in while group it
+// is decoded.  IN: the prologue mode (each kernel holds only its own code).
+template <int FMT, int IN>
 __global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __grid_constant__ DecGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecGemvPlan& p = a.p;
@@ -180,7 +198,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __gri
   const int rs = lane & 7, sl = lane >> 3;  // row of the group, lane of the row
   const int b0 = warp * p.bps, b1 = min(p.bpr, b0 + p.bps);  // this warp's blocks of each row
   const int seg_len = b1 > b0 ? (b1 - b0) * TS : 0;
-  uint8_t* slots = smem + p.stage_off + (size_t)warp * p.stage_bytes;  // NS x 8 rows x seg_cap
+  uint8_t* slots = smem + p.stage_off + (size_t)warp * p.stage_bytes;  // ns x 8 rows x seg_cap
   float* xs = reinterpret_cast<float*>(smem + p.xs_off);
   float* xsum16 = reinterpret_cast<float*>(smem + p.xsum_off);
   float* xsum32 = xsum16 + p.cols / 16;
@@ -204,27 +222,36 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __gri
     cp_commit();  // one commit group per group, empty or not
   };
   PrologueConst pc;
-  prologue_const(a.f, p.cols, pc);  // constant inputs: before the dependency wait
-  const int g0 = blockIdx.x, G = gridDim.x;
-#pragma unroll
-  for (int k = 0; k < NS; ++k) issue(g0 + k * G, k);  // weights only: before the dependency wait
+  prologue_const<IN>(a.f, p.cols, pc);  // constant inputs: before the dependency wait
+  const int g0 = blockIdx.x, G = gridDim.x, ns = p.ns;
+  for (int k = 0; k < ns; ++k) issue(g0 + k * G, k);  // weights only: before the dependency wait
+  issue_l2_prefetch(a.f);
   grid_dep_wait();
   grid_dep_launch();
 
   // activation: fused prologue (or x itself), then two-part int16 per 32 columns
-  const float* src = a.x;
-  if (a.f.in_mode != IN_PLAIN) {
-    fused_prologue(a.f, a.x, xs, misc, p.cols, reinterpret_cast<float*>(smem + p.extra_off), &pc);
-    src = xs;
-  }
+  if constexpr (IN != IN_PLAIN)
+    fused_prologue<IN>(a.f, a.x, xs, misc, p.cols, &pc);
   {
+    constexpr int kQ = 6;  // float4s per thread loaded in one round
     const int n4 = p.cols / 4;
-    for (int i0 = 0; i0 < n4; i0 += blockDim.x) {
-      const int i = i0 + (int)threadIdx.x;
+    for (int i0 = 0; i0 < n4; i0 += kQ * (int)blockDim.x) {
+      float4 vq[kQ];
+#pragma unroll
+      for (int q = 0; q < kQ; ++q) {
+        const int i = i0 + q * (int)blockDim.x + (int)threadIdx.x;
+        vq[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n4) {
+          if constexpr (IN == IN_PLAIN) vq[q] = __ldcg(reinterpret_cast<const float4*>(a.x) + i);
+          else vq[q] = reinterpret_cast<const float4*>(xs)[i];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kQ; ++q) {
+      if (i0 + q * (int)blockDim.x >= n4) break;  // uniform over the CTA
+      const int i = i0 + q * (int)blockDim.x + (int)threadIdx.x;
       const bool act = i < n4;
-      const float4 v = !act ? make_float4(0.f, 0.f, 0.f, 0.f)
-                       : src == a.x ? __ldcg(reinterpret_cast<const float4*>(a.x) + i)
-                                    : reinterpret_cast<const float4*>(src)[i];
+      const float4 v = vq[q];
       float s16 = (v.x + v.y) + (v.z + v.w);
       s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
       s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
@@ -241,21 +268,25 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __gri
       const float inv = nz ? __uint_as_float(0x7F000000u - e) : 1.0f;
       if (act) {
         const float f0 = v.x * inv, f1 = v.y * inv, f2 = v.z * inv, f3 = v.w * inv;  // exact (power of two)
-        const int i0q = __float2int_rn(f0), i1q = __float2int_rn(f1), i2q = __float2int_rn(f2), i3q = __float2int_rn(f3);
+        int i0q, i1q, i2q, i3q;
+        const float r0 = round_small(f0, i0q), r1 = round_small(f1, i1q);
+        const float r2 = round_small(f2, i2q), r3 = round_small(f3, i3q);
         *reinterpret_cast<uint2*>(xq + xq_at(4 * i)) =
             make_uint2((uint32_t)(uint16_t)i0q | ((uint32_t)(uint16_t)i1q << 16),
                        (uint32_t)(uint16_t)i2q | ((uint32_t)(uint16_t)i3q << 16));
-        auto lo16 = [](float sv, int iv) {
-          const int r = __float2int_rn((sv - (float)iv) * 65536.0f);
+        auto lo16 = [](float sv, float rv) {  // the remainder in units of 2^-16
+          int r;
+          round_small(__fmul_rn(__fsub_rn(sv, rv), 65536.0f), r);
           return (uint32_t)(uint16_t)max(-32767, min(32767, r));
         };
         *reinterpret_cast<uint2*>(xql + xq_at(4 * i)) =
-            make_uint2(lo16(f0, i0q) | (lo16(f1, i1q) << 16), lo16(f2, i2q) | (lo16(f3, i3q) << 16));
+            make_uint2(lo16(f0, r0) | (lo16(f1, r1) << 16), lo16(f2, r2) | (lo16(f3, r3) << 16));
         if ((i & 3) == 0) xsum16[i >> 2] = s16;
         if ((i & 7) == 0) {
           xsum32[i >> 3] = s32;
           xsc32[i >> 3] = nz ? __uint_as_float(e) : 1.0f;
         }
+      }
       }
     }
   }
@@ -264,9 +295,9 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __gri
   const int out_mode = a.f.out_mode;
   const int nunits = (b1 - b0) * UPB;
   unsigned long long best = 0ull;
+  int slot = 0;
   for (int g = g0, it = 0; g < p.ngroups; g += G, ++it) {
-    const int slot = it % NS;
-    cp_wait<NS - 1>();  // this warp's copies of group it have landed
+    cp_wait_n(ns - 1);  // this warp's copies of group it have landed
     __syncwarp();
     float acc = 0.f;
     const int row = g * 8 + rs;
@@ -283,7 +314,8 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __gri
     float* rb = red + (it & 1) * 64;
     if (lane < 8) rb[warp * 8 + lane] = acc;
     __syncwarp();
-    issue(g + NS * G, slot);  // this warp is done with the slot
+    issue(g + ns * G, slot);  // this warp is done with the slot
+    slot = slot + 1 == ns ? 0 : slot + 1;
     __syncthreads();
     if (warp == 0) {
       float s = 0.f;
@@ -322,23 +354,27 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3) gemv_dec_kernel(const __gri
 using DecFnG = void (*)(const DecGemvArgs);
 
 template <int FMT>
-static DecFnG dec_fn_ns(int ns) {
-  return ns >= 3 ? gemv_dec_kernel<FMT, 3> : ns == 2 ? gemv_dec_kernel<FMT, 2> : gemv_dec_kernel<FMT, 1>;
-}
-
-static DecFnG dec_gemv_fn(int type, int ns) {
-  switch (type) {
-    case Q8_0: return dec_fn_ns<Q8_0>(ns);
-    case Q4_K: return dec_fn_ns<Q4_K>(ns);
-    case Q6_K: return dec_fn_ns<Q6_K>(ns);
+static DecFnG dec_fn_in(int in_mode) {
+  switch (in_mode) {
+    case IN_PLAIN: return gemv_dec_kernel<FMT, IN_PLAIN>;
+    case IN_NORM: return gemv_dec_kernel<FMT, IN_NORM>;
+    case IN_RESID_NORM: return gemv_dec_kernel<FMT, IN_RESID_NORM>;
+    case IN_EMBED_NORM: return gemv_dec_kernel<FMT, IN_EMBED_NORM>;
+    case IN_MOE_MERGE: return gemv_dec_kernel<FMT, IN_MOE_MERGE>;
     default: return nullptr;
   }
 }
 
-static int dec_ns(const DecGemvPlan& p) { return (p.stage_bytes / (8 * std::max(p.seg_cap, 16))); }
+static DecFnG dec_gemv_fn(int type, int in_mode) {
+  switch (type) {
+    case Q8_0: return dec_fn_in<Q8_0>(in_mode);
+    case Q4_K: return dec_fn_in<Q4_K>(in_mode);
+    case Q6_K: return dec_fn_in<Q6_K>(in_mode);
+    default: return nullptr;
+  }
+}
 
-DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, bool pair, bool fused,
-                          int fused_extra) {
+DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, bool pair, bool fused) {
   DecGemvPlan p{};
   p.type = type;
   p.rows = rows;
@@ -357,9 +393,9 @@ DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, b
   p.seg_cap = nch * 16;
   p.ngroups = (rows + 7) / 8;
   auto al = [](size_t v) { return (int)((v + 127) / 128 * 128); };
+  p.fused = fused ? 1 : 0;
   p.xs_off = 0;
-  p.extra_off = fused ? al((size_t)cols * 4) : 0;
-  p.xsum_off = p.extra_off + al((size_t)std::max(fused_extra, 0));
+  p.xsum_off = fused ? al((size_t)cols * 4) : 0;
   p.xq_off = p.xsum_off + al((size_t)(cols / 16 + 2 * (cols / 32)) * 4);
   const int xq1 = al((size_t)(cols + 8 * ((cols + 255) / 256)) * 2);
   p.xq2_off = p.xq_off + xq1;
@@ -376,18 +412,23 @@ DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, b
     q.stage_bytes = ns * slot_bytes;
     q.smem = (size_t)q.stage_off + (size_t)kDecWarps * q.stage_bytes;
     if (q.smem > dev.smem_optin) break;
-    DecFnG fn = dec_gemv_fn(type, ns);
-    // the attribute is per kernel and device, shared by every plan: the device maximum
-    if (!fn || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dev.smem_optin)) {
+    // every prologue mode's kernel: the attribute is per kernel and device and
+    // shared by every plan, so the device maximum; the occupancy is the least
+    int occ = 3;
+    bool ok = true;
+    for (int in = IN_PLAIN; in <= IN_MOE_MERGE && ok; ++in) {
+      DecFnG fn = dec_gemv_fn(type, in);
+      int o = 0;
+      ok = fn && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dev.smem_optin) ==
+                     cudaSuccess &&
+           cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, kDecWarps * 32, q.smem) == cudaSuccess && o >= 1;
+      occ = std::min(occ, o);
+    }
+    if (!ok) {
       cudaGetLastError();
       break;
     }
-    int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kDecWarps * 32, q.smem) != cudaSuccess || occ < 1) {
-      cudaGetLastError();
-      break;
-    }
-    occ = std::min(occ, 3);
+    q.ns = ns;
     const int slots_total = occ * dev.sms;
     const int gpc = (q.ngroups + slots_total - 1) / slots_total;  // groups per CTA
     q.grid = (q.ngroups + gpc - 1) / gpc;
@@ -407,7 +448,7 @@ DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, b
 int launch_gemv_dec(const DecGemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvFuse& f,
                     unsigned* status, cudaStream_t st, bool pdl) {
   cudaGetLastError();
-  if (!p.fast || (f.out_mode == OUT_GELU_PAIR) != (p.pair != 0) || (f.in_mode != IN_PLAIN && p.extra_off == 0))
+  if (!p.fast || (f.out_mode == OUT_GELU_PAIR) != (p.pair != 0) || (f.in_mode != IN_PLAIN && !p.fused))
     return (int)cudaErrorInvalidValue;
   DecGemvArgs a{p, w, x, y, status, f};
   cudaLaunchConfig_t cfg = {};
@@ -420,7 +461,9 @@ int launch_gemv_dec(const DecGemvPlan& p, const uint8_t* w, const float* x, floa
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return (int)cudaLaunchKernelEx(&cfg, dec_gemv_fn(p.type, dec_ns(p)), a);
+  DecFnG fn = dec_gemv_fn(p.type, f.in_mode);
+  if (!fn) return (int)cudaErrorInvalidValue;
+  return (int)cudaLaunchKernelEx(&cfg, fn, a);
 }
 
 }  // namespace g4

@@ -26,10 +26,8 @@ int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, u
                 cudaStream_t st);
 struct DecGemvPlan;
 // The decoder's GEMV (g4_gemv_dec.cu): Q8_0 / Q4_K / Q6_K rows of whole blocks;
-// fast == 0 when it does not apply.  fused: room for a fused prologue;
-// fused_extra: its further work space.
-DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, bool pair, bool fused,
-                          int fused_extra);
+// fast == 0 when it does not apply.  fused: room for a fused prologue.
+DecGemvPlan plan_gemv_dec(const DeviceInfo& dev, int type, int rows, int cols, bool pair, bool fused);
 int launch_gemv_dec(const DecGemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvFuse& f,
                     unsigned* status, cudaStream_t st, bool pdl);
 // Same with a fused prologue / epilogue; pdl launches with programmatic

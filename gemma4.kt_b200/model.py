@@ -79,13 +79,16 @@ class ModelConfig:
             n_kv.append(int(kd[1]) // hs if kd is not None else n_heads)
         shared = int(md.get("gemma4.attention.shared_kv_layers", 0))
         vocab = len(md["tokenizer.ggml.tokens"])
+        def f32(key, default):  # FLOAT32 metadata, read as a Kotlin Float
+            return float(np.float32(md.get(key, default)))
+
         return ModelConfig(
             dim=int(md["gemma4.embedding_length"]), n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_kv, ff=ff,
-            vocab=vocab, ctx_len=ctx, eps=float(md.get("gemma4.attention.layer_norm_rms_epsilon", 1e-6)),
-            rope_theta=float(md.get("gemma4.rope.freq_base", 1000000.0)),
-            rope_theta_swa=float(md.get("gemma4.rope.freq_base_swa", 10000.0)),
+            vocab=vocab, ctx_len=ctx, eps=f32("gemma4.attention.layer_norm_rms_epsilon", 1e-6),
+            rope_theta=f32("gemma4.rope.freq_base", 1000000.0),
+            rope_theta_swa=f32("gemma4.rope.freq_base_swa", 10000.0),
             head_size_full=hf, head_size_swa=hsw, sliding_window=int(md["gemma4.attention.sliding_window"]),
-            logit_softcap=float(md.get("gemma4.final_logit_softcapping", 0.0)), is_swa=is_swa,
+            logit_softcap=f32("gemma4.final_logit_softcapping", 0.0), is_swa=is_swa,
             n_layer_kv_from_start=n_layers - shared, n_expert=int(md.get("gemma4.expert_count", 0)),
             n_expert_used=int(md.get("gemma4.expert_used_count", 0)),
             expert_ff=int(md.get("gemma4.expert_feed_forward_length", 0)))

@@ -130,3 +130,24 @@ def test_c4_dense_greedy_64_tokens(g4, ctx):
     assert first_diff >= 64, (first_diff, got[:first_diff + 1], ref[:first_diff + 1])
     st.free()
     model.free()
+
+
+def test_decoder_from_gguf_file(g4, ctx, tmp_path):
+    """GemmaModel.load's path: a synthetic decoder written as a GGUF file and
+    loaded with DecoderModel.load (mmapped blocks uploaded as they lie)
+    decodes the same greedy stream as the oracle."""
+    from gemma4_kt_b200 import gguf, synth
+
+    m = synth.SynthDecoder(SPECS["q4k"], seed=14)
+    path = tmp_path / "q4k.gguf"
+    m.write(path)
+    prompt = m.prompt(12)
+    del m
+    model = g4.DecoderModel.load(ctx, path)
+    orc = oracle.ModelOracle(g4.TensorSource.from_gguf(gguf.GGUFFile(path)))
+    ref = orc.greedy(prompt, 24)
+    st = model.new_state()
+    got = st.generate(np.concatenate([[2], prompt]).astype(np.int32), 24)
+    assert np.array_equal(got, ref), (got, ref)
+    st.free()
+    model.free()
