@@ -114,24 +114,50 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def make_cases(seed: int = 1):
-    import __graft_entry__
+def make_cases(seed: int = 1, quantize=None):
+    """The C2 sweep's matrices and activations.  quantize: fp32 -> blocks
+    (default: the package's generator; the reference arm passes the copy built
+    under oracle/ so that it loads no library of the package)."""
+    if quantize is None:
+        import __graft_entry__
 
-    __graft_entry__.load_package()  # registers the package (its directory name holds a dot); no GPU library
-    from gemma4_kt_b200 import synth
+        __graft_entry__.load_package()  # registers the package (its directory name holds a dot)
+        from gemma4_kt_b200 import synth
 
+        quantize = synth.quantize
     cases = []
     for rows, cols in SHAPES:
         rng = np.random.default_rng(seed)
-        w = synth.normal(rng, rows * cols)
+        w = rng.standard_normal(rows * cols, dtype=np.float32)
+        w *= np.float32(0.02)  # N(0, 0.02), as synth.normal
         x = rng.standard_normal(cols, dtype=np.float32)
         for name, t in FORMATS:
-            cases.append({"name": name, "type": t, "rows": rows, "cols": cols, "raw": synth.quantize(t, w), "x": x})
+            cases.append({"name": name, "type": t, "rows": rows, "cols": cols, "raw": quantize(t, w), "x": x})
         del w
     return cases
 
 
+def sweep_config(world: int) -> dict:
+    """The `config` of both arms' JSON lines (the same workload)."""
+    return {"workload": "C2 quantized GEMV sweep: 4 shapes x {Q8_0,Q4_K,Q6_K,BF16}, batch 1, seed 1",
+            "shapes": [f"{r}x{c}" for r, c in SHAPES],
+            "bytes_per_step": sum(alg_bytes(t, r, c) for r, c in SHAPES for _, t in FORMATS),
+            "l2": "inputs larger than L2 (1.9 GB streamed per step)",
+            "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU"}
+
+
 # ------------------------------------------------------------------ CPU arm
+def loaded_repo_libraries() -> list:
+    """Shared objects of this repository mapped into this process."""
+    try:
+        maps = Path("/proc/self/maps").read_text().splitlines()
+    except OSError:
+        return []
+    root = str(ROOT)
+    return sorted({ln.split()[-1][len(root) + 1:] for ln in maps
+                   if ln.split() and ln.split()[-1].startswith(root) and ln.split()[-1].endswith(".so")})
+
+
 def cpu_sample_run(cases, budget_rows: int, threads: int):
     """Oracle (reference restatement) over a bounded row sample of every case:
     returns (bytes processed, seconds)."""
@@ -153,7 +179,7 @@ def run_reference(args, rank: int, world: int):
     from oracle import oracle
 
     oracle.build()
-    cases = make_cases()
+    cases = make_cases(quantize=oracle.quantize)
     threads = os.cpu_count() or 1
     budget = 16384  # rows per case per step: about 10 s of CPU work per step on 8 cores
     for _ in range(args.warmup):
@@ -169,13 +195,13 @@ def run_reference(args, rank: int, world: int):
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_tot / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "C2 quantized GEMV sweep (4 shapes x Q8_0/Q4_K/Q6_K/BF16), batch 1",
-                   "l2": "n/a (host CPU)"},
+        "config": sweep_config(world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference Kotlin/JVM path cannot run on this image (no JVM); timed: the C restatement of its "
                 "512-bit vectorDot kernels in oracle/",
+        "native_libraries": loaded_repo_libraries(),
     }
     print(json.dumps(line), flush=True)
 
@@ -399,7 +425,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     moe = None
     if world == 1 and rank == 0 and not args.no_moe:
-        moe = bench_moe(g4, ctx, torch, dev)
+        moe = bench_moe(g4, ctx, torch, dev, with_cpu=not args.no_cpu)
     elif world > 1 and not args.no_moe:
         moe = bench_moe_ep(g4, ctx, torch, dev, rank, world)
     decode = None
@@ -411,10 +437,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
-            "config": {"workload": "C2 quantized GEMV sweep: 4 shapes x {Q8_0,Q4_K,Q6_K,BF16}, batch 1, seed 1",
-                       "shapes": [f"{r}x{c}" for r, c in SHAPES], "bytes_per_step": step_bytes,
-                       "l2": "inputs larger than L2 (1.9 GB streamed per step)",
-                       "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU"},
+            "config": sweep_config(world),
             "roofline": {"bound": "hbm", "kernel": breakdown[dom]["case"], "achieved": round(achieved, 1),
                          "peak": hbm, "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": MEASURED_TRAFFIC.get(breakdown[dom]["case"]) if world == 1 else None,
@@ -545,8 +568,11 @@ def bench_decode(g4, ctx, torch, dev, with_cpu: bool = True):
     return res
 
 
-def bench_moe(g4, ctx, torch, dev):
-    """MoE layer (config 3) microseconds per token at T = 1, 16, 256, 4096."""
+def bench_moe(g4, ctx, torch, dev, with_cpu: bool = True):
+    """MoE layer (config 3) microseconds per token at T = 1, 16, 256, 4096;
+    end to end through g4_moe_layer_host (host arrays in and out) at T = 1
+    and 16; the oracle's restatement of the reference MoE block on all host
+    cores at T = 1 and 16."""
     from gemma4_kt_b200 import synth
 
     d = synth.MoeLayerData(seed=2)
@@ -603,9 +629,42 @@ def bench_moe(g4, ctx, torch, dev):
                         "path": "tcgen05 grouped GEMM" if 4 * T * d.n_used >= d.n_expert
                         else "one-wave decode kernels" if T <= 2 else "CUDA-core rows"}
     ctx.sync()
+    # end to end through the host-buffer entry point: x from host memory, the
+    # layer, out back to host memory, one synchronous call each
+    e2e = {}
+    for T in (1, 16):
+        xh = np.ascontiguousarray(d.tokens(T, seed=77 + T))
+        oh = np.empty((T, d.dim), np.float32)
+        for _ in range(3):
+            layer.forward(xh, oh, T)
+        n = 50
+        t0 = time.perf_counter()
+        for _ in range(n):
+            layer.forward(xh, oh, T)
+        us = (time.perf_counter() - t0) / n * 1e6
+        e2e[f"T{T}"] = {"value": round(us / T, 3), "unit": "us/token", "us_per_call": round(us, 2),
+                        "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(oh.nbytes)}
+    cpu = None
+    if with_cpu:
+        from oracle import oracle
+
+        orc = oracle.MoeOracle(d, int(g4.GGMLType.Q4_K), int(g4.GGMLType.Q4_K))
+        threads = os.cpu_count() or 1
+        cpu = {}
+        for T in (1, 16):
+            xs = d.tokens(T, seed=77 + T)
+            orc.token(xs[0], threads)  # warm
+            t0 = time.perf_counter()
+            for t in range(T):
+                orc.token(xs[t], threads)
+            cpu[f"T{T}"] = round((time.perf_counter() - t0) / T * 1e6, 1)
+        cpu = {"value": cpu["T1"], "unit": "us/token", "by_batch": cpu, "cores": threads, "kind": "port",
+               "sample": "1 and 16 tokens through the oracle's restatement of the MoE block (Llama.kt:226-346: "
+                         "router, top-8, 8 expert FFNs, weighted combine), experts split over all host threads"}
     return {"metric": "MoE layer us/token", "config": "hidden 2816, 128 experts top-8, ff 704, Q4_K, seed 2",
+            "e2e": e2e, "cpu_baseline": cpu,
             "timing": "CUDA graph of one g4_moe_layer call, replayed; L2 flushed (256 MB read) before each "
-                      "timed replay, outside its event pair",
+                      "timed replay, outside its event pair; e2e: host wall clock per g4_moe_layer_host call",
             "roofline": "hbm_frac = (touched experts' Q4_K bytes + router + activations) / time / measured HBM; "
                         "tensor_frac = 2*T*8*5947392 flops / time / measured bf16 dense peak",
             **res}

@@ -16,15 +16,43 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "libg4oracle.so"
+GEN = HERE / "libg4gen.so"
+GEN_SRC = HERE.parent / "gemma4.kt_b200" / "csrc" / "g4_synth.c"
 
 _lib = None
+_gen = None
 
 
 def build() -> Path:
     src = [HERE / "g4_oracle.c", HERE / "g4_oracle.h", HERE / "Makefile"]
-    if not LIB.exists() or any(s.stat().st_mtime > LIB.stat().st_mtime for s in src):
+    stale = not LIB.exists() or any(s.stat().st_mtime > LIB.stat().st_mtime for s in src)
+    stale = stale or (GEN_SRC.exists() and (not GEN.exists() or GEN_SRC.stat().st_mtime > GEN.stat().st_mtime))
+    if stale:
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB
+
+
+def quantize(ggml_type: int, w: np.ndarray, threads: int | None = None) -> np.ndarray:
+    """fp32 weights -> GGUF block bytes with the benchmark-input generator
+    (the same source as the package's synth.quantize, built under oracle/)."""
+    global _gen
+    if _gen is None:
+        if not GEN.exists():
+            build()
+        _gen = C.CDLL(str(GEN))
+        _gen.g4s_quantize.restype = C.c_int
+        _gen.g4s_quantize.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_void_p, C.c_int]
+        _gen.g4s_nbytes.restype = C.c_int64
+        _gen.g4s_nbytes.argtypes = [C.c_int, C.c_int64]
+    w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+    nb = _gen.g4s_nbytes(int(ggml_type), w.size)
+    if nb < 0:
+        raise ValueError(f"cannot quantize {w.size} elements as type {ggml_type}")
+    out = np.empty(nb, dtype=np.uint8)
+    if _gen.g4s_quantize(int(ggml_type), w.ctypes.data_as(C.c_void_p), w.size, out.ctypes.data_as(C.c_void_p),
+                         threads or os.cpu_count() or 1):
+        raise ValueError(f"cannot quantize {w.size} elements as type {ggml_type}")
+    return out
 
 
 class MoeW(C.Structure):
