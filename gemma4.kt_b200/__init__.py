@@ -15,5 +15,5 @@ from .floattensor import (  # noqa: F401
     QK_K,
     row_shard,
 )
-from .moe import MoeLayer, topk  # noqa: F401
+from .moe import FfnMoeBlock, MoeLayer, topk  # noqa: F401
 from .model import DecoderModel, DecoderState, ModelConfig, TensorSource  # noqa: F401

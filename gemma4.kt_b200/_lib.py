@@ -44,6 +44,8 @@ SIGNATURES = {
     "g4_moe_topk": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp, _vp]),
     "g4_moe_layer_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "g4_moe_layer_ep": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
+    "g4_ffn_moe_block": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "g4_ffn_moe_block_host": (_i, [_vp, _vp, _vp, _i]),
     "g4_dist_unique_id": (_i, [_vp]),
     "g4_dist_init": (_i, [_vp, _i, _i, _vp]),
     "g4_dist_init_timeout": (_i, [_vp, _i, _i, _vp, _i]),
@@ -87,6 +89,14 @@ class MoeWeightsStruct(C.Structure):
         ("pre_ffw_norm_2", C.c_void_p),
         ("post_ffw_norm_2", C.c_void_p),
     ]
+
+
+class FfnMoeWeightsStruct(C.Structure):
+    """g4_ffn_moe_weights (include/g4.h)."""
+
+    _fields_ = [("moe", C.POINTER(MoeWeightsStruct)), ("ff", C.c_int)] + \
+               [(n, C.c_void_p) for n in ("ffn_gate", "ffn_up", "ffn_down", "ffn_norm", "post_ffw_norm_1",
+                                          "post_ffw_norm")] + [("layer_output_scale", C.c_float)]
 
 
 class ModelConfigStruct(C.Structure):

@@ -37,23 +37,30 @@ int g4_ctx::bind() {
   return e == cudaSuccess ? 0 : cuda_fail(e, "cudaSetDevice");
 }
 
-void* g4_ctx::scratch(size_t bytes) {
-  if (bytes <= scratch_bytes) return scratch_ptr;
-  if (scratch_ptr) {
+// A growable device arena: reallocated (after the queued work that may still
+// read the old one) when a call needs more; slack: room for growth.
+static void* grow_arena(void** p, size_t* have, size_t bytes, bool slack) {
+  if (bytes <= *have) return *p;
+  if (*p) {
     cudaDeviceSynchronize();  // the old arena may still be read by queued work
-    cudaFree(scratch_ptr);
-    scratch_ptr = nullptr;
-    scratch_bytes = 0;
+    cudaFree(*p);
   }
-  size_t want = bytes + bytes / 4 + (1u << 20);
-  if (cudaMalloc(&scratch_ptr, want) != cudaSuccess) {
+  *p = nullptr;
+  *have = 0;
+  const size_t want = slack ? bytes + bytes / 4 + (1u << 20) : bytes;
+  if (cudaMalloc(p, want) != cudaSuccess) {
     cudaGetLastError();
-    scratch_ptr = nullptr;
+    *p = nullptr;
     return nullptr;
   }
-  scratch_bytes = want;
-  return scratch_ptr;
+  *have = want;
+  return *p;
 }
+
+void* g4_ctx::scratch(size_t bytes) { return grow_arena(&scratch_ptr, &scratch_bytes, bytes, true); }
+void* g4_ctx::io(size_t bytes) { return grow_arena(&io_ptr, &io_bytes, bytes, false); }
+void* g4_ctx::ep(size_t bytes) { return grow_arena(&ep_ptr, &ep_bytes, bytes, true); }
+void* g4_ctx::blk(size_t bytes) { return grow_arena(&blk_ptr, &blk_bytes, bytes, true); }
 
 void* g4_ctx::pinned(size_t bytes) {
   if (bytes <= pinned_bytes) return pinned_ptr;
@@ -67,41 +74,6 @@ void* g4_ctx::pinned(size_t bytes) {
   }
   pinned_bytes = bytes;
   return pinned_ptr;
-}
-
-void* g4_ctx::io(size_t bytes) {
-  if (bytes <= io_bytes) return io_ptr;
-  if (io_ptr) {
-    cudaDeviceSynchronize();
-    cudaFree(io_ptr);
-  }
-  io_ptr = nullptr;
-  io_bytes = 0;
-  if (cudaMalloc(&io_ptr, bytes) != cudaSuccess) {
-    cudaGetLastError();
-    io_ptr = nullptr;
-    return nullptr;
-  }
-  io_bytes = bytes;
-  return io_ptr;
-}
-
-void* g4_ctx::ep(size_t bytes) {
-  if (bytes <= ep_bytes) return ep_ptr;
-  if (ep_ptr) {
-    cudaDeviceSynchronize();
-    cudaFree(ep_ptr);
-  }
-  ep_ptr = nullptr;
-  ep_bytes = 0;
-  const size_t want = bytes + bytes / 4 + (1u << 20);
-  if (cudaMalloc(&ep_ptr, want) != cudaSuccess) {
-    cudaGetLastError();
-    ep_ptr = nullptr;
-    return nullptr;
-  }
-  ep_bytes = want;
-  return ep_ptr;
 }
 
 int g4_ctx::check_status(cudaStream_t st) {
@@ -192,6 +164,7 @@ int g4_destroy(g4_ctx* c) {
   if (c->pinned_ptr) cudaFreeHost(c->pinned_ptr);
   if (c->io_ptr) cudaFree(c->io_ptr);
   if (c->ep_ptr) cudaFree(c->ep_ptr);
+  if (c->blk_ptr) cudaFree(c->blk_ptr);
   if (c->status) cudaFree(c->status);
   if (c->status_host) cudaFreeHost(c->status_host);
   delete c;

@@ -26,6 +26,8 @@ struct g4_ctx {
   size_t io_bytes = 0;
   void* ep_ptr = nullptr;      // receive-side buffers of the expert-parallel MoE layer
   size_t ep_bytes = 0;
+  void* blk_ptr = nullptr;     // work buffers of the MoE FFN block (beside the MoE layer's own)
+  size_t blk_bytes = 0;
   void* comm = nullptr;        // ncclComm_t when g4_dist_init has run
   int rank = 0;
   int world = 1;
@@ -41,6 +43,7 @@ struct g4_ctx {
   void* pinned(size_t bytes);
   void* io(size_t bytes);
   void* ep(size_t bytes);
+  void* blk(size_t bytes);
   int check_status(cudaStream_t st);
 };
 

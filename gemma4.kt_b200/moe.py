@@ -4,7 +4,9 @@ The reference inlines the block in Llama.forward (Llama.kt:226-353) and keeps
 its weights in LlamaWeights (LlamaWeights.kt:50-65: ffnGateInp,
 ffnGateInpScale, ffnGateUpExps, ffnDownExps, ffnDownExpsScale, preFfwNorm2,
 ffnPostNorm2).  `MoeLayer.forward` runs the expert half (Llama.kt:247-346)
-for a batch of tokens in one call of g4_moe_layer.
+for a batch of tokens in one call of g4_moe_layer; `FfnMoeBlock.forward` the
+whole FFN half of the layer (shared MLP, experts, merge: Llama.kt:226-353) in
+one call of g4_ffn_moe_block.
 """
 from __future__ import annotations
 
@@ -12,7 +14,7 @@ import ctypes as C
 
 import numpy as np
 
-from ._lib import MoeWeightsStruct, check, lib
+from ._lib import FfnMoeWeightsStruct, MoeWeightsStruct, check, lib
 from .floattensor import Context, CudaFloatTensor, FloatTensorFactory, GGMLType, _is_torch, _stream_ptr
 
 
@@ -103,6 +105,46 @@ class MoeLayer:
             rc = lib().g4_moe_layer_host(self.ctx.handle, C.byref(self.w), p(xa), p(out), n_tokens, p(topk_idx),
                                          p(topk_prob))
             check(rc, self.ctx.handle, "g4_moe_layer_host")
+
+
+class FfnMoeBlock:
+    """The FFN half of a MoE layer (Llama.kt:226-353): the shared MLP
+    (ffn_norm, ffn_gate / ffn_up / ffn_down, post_ffw_norm_1), the expert half
+    (a MoeLayer) and the merge (post_ffw_norm), plus the layer output scale."""
+
+    def __init__(self, moe: MoeLayer, ff: int, ffn_gate: CudaFloatTensor, ffn_up: CudaFloatTensor,
+                 ffn_down: CudaFloatTensor, ffn_norm: CudaFloatTensor, post_ffw_norm_1: CudaFloatTensor,
+                 post_ffw_norm: CudaFloatTensor, layer_output_scale: float = 1.0):
+        self.moe, self.ctx, self.ff = moe, moe.ctx, ff
+        self._tensors = [ffn_gate, ffn_up, ffn_down, ffn_norm, post_ffw_norm_1, post_ffw_norm]
+        self.w = FfnMoeWeightsStruct(C.pointer(moe.w), ff, ffn_gate.handle, ffn_up.handle, ffn_down.handle,
+                                     ffn_norm.handle, post_ffw_norm_1.handle, post_ffw_norm.handle,
+                                     float(layer_output_scale))
+
+    @staticmethod
+    def upload(ctx: Context, moe: MoeLayer, shared) -> "FfnMoeBlock":
+        """shared: an object with ff, gate_type, ffn_gate / ffn_up / ffn_down (block bytes), ffn_norm,
+        post_ffw_norm_1, post_ffw_norm (F32) and layer_output_scale (synth.SharedMlpData)."""
+        up = FloatTensorFactory.create
+        dim, ff, t, f32 = moe.dim, shared.ff, GGMLType(int(shared.gate_type)), GGMLType.F32
+        return FfnMoeBlock(moe, ff, up(ctx, t, shared.ffn_gate, ff * dim), up(ctx, t, shared.ffn_up, ff * dim),
+                           up(ctx, t, shared.ffn_down, dim * ff), up(ctx, f32, shared.ffn_norm, dim),
+                           up(ctx, f32, shared.post_ffw_norm_1, dim), up(ctx, f32, shared.post_ffw_norm, dim),
+                           shared.layer_output_scale)
+
+    def forward(self, x, n_tokens: int, stream=None) -> None:
+        """x: [n_tokens, dim] residual stream, updated in place (torch CUDA
+        tensor: asynchronous on `stream`; numpy array: synchronous)."""
+        if _is_torch(x):
+            rc = lib().g4_ffn_moe_block(self.ctx.handle, C.byref(self.w), C.c_void_p(x.data_ptr()), n_tokens,
+                                        C.c_void_p(_stream_ptr(stream)))
+            check(rc, self.ctx.handle, "g4_ffn_moe_block")
+        else:
+            if not (isinstance(x, np.ndarray) and x.dtype == np.float32 and x.flags.c_contiguous):
+                raise TypeError("x must be a C-contiguous float32 array (updated in place)")
+            rc = lib().g4_ffn_moe_block_host(self.ctx.handle, C.byref(self.w), x.ctypes.data_as(C.c_void_p),
+                                             n_tokens)
+            check(rc, self.ctx.handle, "g4_ffn_moe_block_host")
 
 
 def topk(ctx: Context, logits, n_tokens: int, n_expert: int, k: int, idx_out, prob_out, stream=None) -> None:

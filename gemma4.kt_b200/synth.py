@@ -84,6 +84,23 @@ class MoeLayerData:
         return rng.standard_normal((n_tokens, self.dim), dtype=np.float32)
 
 
+class SharedMlpData:
+    """Host copy of the shared-MLP half of a synthetic MoE layer (ffn_gate /
+    ffn_up [dim, ff], ffn_down [ff, dim] N(0, 0.02) quantized; ffn_norm,
+    post_ffw_norm_1, post_ffw_norm N(1, 0.1); layer output scale U(0.5, 1))."""
+
+    def __init__(self, dim: int, ff: int, seed: int = 5, gate_type=GGMLType.Q8_0):
+        rng = np.random.default_rng([seed, 77])
+        self.dim, self.ff, self.gate_type = dim, ff, GGMLType(int(gate_type))
+        self.ffn_gate = quantize(self.gate_type, normal(rng, dim * ff))
+        self.ffn_up = quantize(self.gate_type, normal(rng, dim * ff))
+        self.ffn_down = quantize(self.gate_type, normal(rng, dim * ff))
+        self.ffn_norm = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+        self.post_ffw_norm_1 = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+        self.post_ffw_norm = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+        self.layer_output_scale = float(np.float32(rng.uniform(0.5, 1.0)))
+
+
 def random_blocks(ggml_type, n_elems: int, rng: np.random.Generator) -> np.ndarray:
     """Valid block streams for the formats without a quantizer here (F16, Q4_0,
     Q4_1, Q5_1, Q5_K, MXFP4): random code bytes, fp16 scale fields ~ N(0, 0.01)

@@ -188,6 +188,34 @@ int g4_moe_layer_noalloc(g4_ctx *ctx, const g4_moe_weights *w, const float *x_de
 int g4_moe_layer_ep(g4_ctx *ctx, const g4_moe_weights *w_local, const float *x_dev, float *out_dev,
                     int n_tokens, int32_t *topk_idx_dev, float *topk_prob_dev, void *stream);
 
+/* ---------------- MoE FFN block (Llama.kt:226-353) ----------------
+ * The whole FFN half of a MoE layer, in place on n_tokens rows of the
+ * residual stream x (state.x after the attention residual):
+ *   shared MLP   h = rmsnorm(x, ffn_norm); xb = ffn_down . (gelu(ffn_gate . h) * (ffn_up . h));
+ *                xb = rmsnorm(xb, post_ffw_norm_1)                        Llama.kt:231-243
+ *   experts      moeOutput = g4_moe_layer(x) (pre_ffw_norm_2 ... post_ffw_norm_2)  Llama.kt:247-346
+ *   merge        xb += moeOutput; x += rmsnorm(xb, post_ffw_norm)          Llama.kt:349-353
+ *   layer scale  x *= layer_output_scale when it is not 1                  Llama.kt:393-397
+ * Pass layer_output_scale = 1 when the model has a per-layer-embedding step
+ * (Llama.kt:366-391) between the merge and the scale.  The shared MLP
+ * tensors take any format g4_matmul takes; the norms are F32 [dim]. */
+typedef struct {
+  const g4_moe_weights *moe;       /* the expert half; its dim and eps serve the whole block */
+  int ff;                          /* gemma4.feed_forward_length of the layer */
+  const g4_tensor *ffn_gate;       /* blk.N.ffn_gate.weight [dim, ff] */
+  const g4_tensor *ffn_up;         /* blk.N.ffn_up.weight   [dim, ff] */
+  const g4_tensor *ffn_down;       /* blk.N.ffn_down.weight [ff, dim] */
+  const g4_tensor *ffn_norm;       /* blk.N.ffn_norm.weight */
+  const g4_tensor *post_ffw_norm_1; /* blk.N.post_ffw_norm_1.weight */
+  const g4_tensor *post_ffw_norm;  /* blk.N.post_ffw_norm.weight */
+  float layer_output_scale;        /* blk.N.layer_output_scale.weight[0], or 1 */
+} g4_ffn_moe_weights;
+
+/* x_dev: [n_tokens, dim], updated in place, on `stream`. */
+int g4_ffn_moe_block(g4_ctx *ctx, const g4_ffn_moe_weights *w, float *x_dev, int n_tokens, void *stream);
+/* Host-buffer variant (synchronous): x_host updated in place. */
+int g4_ffn_moe_block_host(g4_ctx *ctx, const g4_ffn_moe_weights *w, float *x_host, int n_tokens);
+
 /* ---------------- whole-model decode (Llama.kt:105-477) ----------------
  * A GPU-resident Llama.forward: the residual stream, the KV cache and the
  * greedy sampler stay in HBM; one decode step is one CUDA graph.

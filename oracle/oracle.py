@@ -131,6 +131,38 @@ def gelu(x: float) -> float:
     return float(lib().o_gelu(x))
 
 
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """Llama.rmsnorm (Llama.kt:27-37)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().o_rmsnorm(_p(out), _p(x), _p(w), x.size, float(eps))
+    return out
+
+
+def ffn_moe_block(x: np.ndarray, moe: "MoeOracle", shared, eps: float) -> np.ndarray:
+    """The FFN half of a MoE layer for one token, as Llama.forward runs it
+    (Llama.kt:226-353) followed by the layer output scale (Llama.kt:393-397);
+    returns the new residual stream.  shared: ffn_gate / ffn_up / ffn_down
+    blocks of shared.gate_type, ffn_norm, post_ffw_norm_1, post_ffw_norm,
+    layer_output_scale."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    dim, ff, t = x.size, shared.ff, int(shared.gate_type)
+    h = rmsnorm(x, shared.ffn_norm, eps)                                   # :232
+    hb = matmul(t, shared.ffn_gate, h, ff, dim)                            # :233
+    hb2 = matmul(t, shared.ffn_up, h, ff, dim)                             # :234
+    hb = np.array([gelu(float(v)) for v in hb], dtype=np.float32) * hb2    # :235-236
+    xb = matmul(t, shared.ffn_down, hb, dim, ff)                           # :237
+    xb = rmsnorm(xb, shared.post_ffw_norm_1, eps)                          # :238-243
+    moe_out, _, _, _ = moe.token(x)                                        # :247-346 (state.x)
+    xb = (xb + moe_out).astype(np.float32)                                 # :349
+    xb = rmsnorm(xb, shared.post_ffw_norm, eps)                            # :352
+    out = (x + xb).astype(np.float32)                                      # :353
+    if shared.layer_output_scale != 1.0:
+        out = (out * np.float32(shared.layer_output_scale)).astype(np.float32)  # :393-397
+    return out
+
+
 def softmax(x: np.ndarray) -> np.ndarray:
     y = np.array(x, dtype=np.float32, copy=True)
     lib().o_softmax(_p(y), y.size)
