@@ -29,7 +29,7 @@ NVCC_FLAGS = ARCH + [
     "-Xcompiler", "-fPIC,-O3", "-I", str(INCLUDE), "-I", str(CSRC),
 ]
 
-CU_SOURCES = ["g4_capi.cu", "g4_gemv.cu", "g4_moe.cu", "g4_moe_tc.cu", "g4_decode.cu", "g4_gemv_dec.cu", "g4_block.cu"]
+CU_SOURCES = ["g4_capi.cu", "g4_gemv.cu", "g4_moe.cu", "g4_moe_tc.cu", "g4_decode.cu", "g4_gemv_dec.cu", "g4_gemv_mma.cu", "g4_block.cu"]
 CU_HEADERS = ["g4_common.cuh", "g4_gemv.cuh", "g4_gemv_rows.cuh", "g4_internal.h", "g4_ctx.h", "g4_moe_tc.h", "g4_fuse.cuh"]
 
 

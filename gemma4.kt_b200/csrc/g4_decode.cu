@@ -324,11 +324,16 @@ struct LayerDev {
   g4_moe_weights moe{};
   GemvPlan p_qkv{}, p_wo{}, p_gu{}, p_down{};        // general GEMV plans (BF16 / F32 and other layouts)
   DecGemvPlan d_qkv{}, d_wo{}, d_gu{}, d_down{};     // decoder GEMV (Q8_0 / Q4_K / Q6_K), used when fast
+  MmaGemvPlan m_qkv{}, m_wo{}, m_gu{}, m_down{};     // Q8_0 on the tensor cores, used when fast
+  uint8_t *k_qkv = nullptr, *k_wo = nullptr, *k_gu = nullptr, *k_down = nullptr;  // their repacked weights
 };
 
-// One of a layer's projections: the decoder GEMV when it applies, else the general one.
-static int launch_proj(const DecGemvPlan& d, const GemvPlan& g, const g4_tensor* w, const float* x, float* y,
-                       const GemvFuse& f, unsigned* status, cudaStream_t st, bool pdl) {
+// One of a layer's projections: the tensor-core Q8_0 GEMV (repacked weights),
+// else the decoder GEMV when it applies, else the general one.
+static int launch_proj(const MmaGemvPlan& mm, const uint8_t* packed, const DecGemvPlan& d, const GemvPlan& g,
+                       const g4_tensor* w, const float* x, float* y, const GemvFuse& f, unsigned* status,
+                       cudaStream_t st, bool pdl) {
+  if (mm.fast && packed) return launch_gemv_mma(mm, packed, x, y, f, status, st, pdl);
   if (d.fast) return launch_gemv_dec(d, (const uint8_t*)w->d, x, y, f, status, st, pdl);
   return launch_gemv_fused(g, (const uint8_t*)w->d, x, y, f, status, st, pdl);
 }
@@ -603,6 +608,34 @@ static void drop(g4_model* m, const std::string& n) {
   }
 }
 
+// The tensor-core Q8_0 GEMV (g4_gemv_mma.cu) is the decoder's Q8_0 path
+// unless G4_DEC_MMA=0 selects the CUDA-core decoder GEMV.
+static bool mma_wanted() {
+  const char* e = getenv("G4_DEC_MMA");
+  return !(e && e[0] == '0');
+}
+
+// A Q8_0 projection's copy in the tensor-core tile layout, and its plan;
+// other types (or shapes the plan rejects) keep plan.fast == 0.
+static int make_mma(g4_ctx* c, const g4_tensor* w, int rows, int cols, bool pair, bool fused, MmaGemvPlan& plan,
+                    uint8_t*& packed) {
+  if (!w || w->type != G4_TYPE_Q8_0 || w->n_elems != (uint64_t)rows * (uint64_t)cols) return 0;
+  MmaGemvPlan p = plan_gemv_mma(c->dev, rows, cols, pair, fused);
+  if (!p.fast) return 0;
+  const size_t bytes = mma_packed_bytes(rows, cols);
+  if (cudaMalloc(&packed, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    packed = nullptr;
+    c->set_err("g4_model_finalize: cannot allocate %zu bytes of repacked Q8_0 weights", bytes);
+    return G4_E_NOMEM;
+  }
+  cudaError_t e = (cudaError_t)repack_q8_0_mma((const uint8_t*)w->d, rows, cols, packed, nullptr);
+  if (!e) e = cudaStreamSynchronize(nullptr);
+  if (e) return c->cuda_fail(e, "g4_model_finalize: Q8_0 repack");
+  plan = p;
+  return 0;
+}
+
 extern "C" int g4_model_finalize(g4_model* m) {
   if (!m) return G4_E_ARG;
   g4_ctx* c = m->ctx;
@@ -717,6 +750,12 @@ extern "C" int g4_model_finalize(g4_model* m) {
     L.d_wo = plan_gemv_dec(c->dev, L.wo->type, dim, L.qdim, false, false);
     L.d_gu = plan_gemv_dec(c->dev, L.gate_up->type, 2 * L.ff, dim, true, true);
     L.d_down = plan_gemv_dec(c->dev, L.down->type, dim, L.ff, false, false);
+    if (mma_wanted()) {
+      if (int r = make_mma(c, L.qkv, qkv_rows, dim, false, true, L.m_qkv, L.k_qkv)) return r;
+      if (int r = make_mma(c, L.wo, dim, L.qdim, false, false, L.m_wo, L.k_wo)) return r;
+      if (int r = make_mma(c, L.gate_up, 2 * L.ff, dim, true, true, L.m_gu, L.k_gu)) return r;
+      if (int r = make_mma(c, L.down, dim, L.ff, false, false, L.m_down, L.k_down)) return r;
+    }
     if ((!L.p_qkv.fast && !L.d_qkv.fast) || (!L.p_gu.fast && !L.d_gu.fast) || (!L.p_wo.fast && !L.d_wo.fast) ||
         (!L.p_down.fast && !L.d_down.fast)) {
       c->set_err("g4_model_finalize: layer %d: the projections need a streaming-kernel format "
@@ -751,6 +790,8 @@ extern "C" int g4_model_free(g4_model* m) {
   for (LayerDev& L : m->L) {
     if (L.qkv) g4_tensor_free(L.qkv);
     if (L.gate_up) g4_tensor_free(L.gate_up);
+    for (uint8_t* p : {L.k_qkv, L.k_wo, L.k_gu, L.k_down})
+      if (p) cudaFree(p);
   }
   for (float* p : {m->cr_full, m->ci_full, m->cr_swa, m->ci_swa})
     if (p) cudaFree(p);
@@ -884,12 +925,24 @@ static cudaError_t launch_pdl_k(void (*kern)(KArgs...), int grid, int block, siz
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-static void set_prefetch(GemvFuse& f, std::initializer_list<const g4_tensor*> ts) {
+// A projection's weights as a kernel streams them: the repacked tensor-core
+// copy when there is one, else the GGUF blocks.
+struct ProjW {
+  const g4_tensor* t;
+  const uint8_t* packed;
+  size_t packed_bytes;
+};
+
+static ProjW proj_w(const g4_tensor* t, const uint8_t* packed, const MmaGemvPlan& p) {
+  return ProjW{t, packed, packed && p.fast ? mma_packed_bytes(p.rows, p.cols) : 0};
+}
+
+static void set_prefetch(GemvFuse& f, std::initializer_list<ProjW> ts) {
   int k = 0;
-  for (const g4_tensor* t : ts)
-    if (t && k < GemvFuse::kPrefetch) {
-      f.pf[k] = (const uint8_t*)t->d;
-      f.pf_bytes[k] = (long long)t->nbytes;
+  for (const ProjW& w : ts)
+    if (w.t && k < GemvFuse::kPrefetch) {
+      f.pf[k] = w.packed_bytes ? w.packed : (const uint8_t*)w.t->d;
+      f.pf_bytes[k] = w.packed_bytes ? (long long)w.packed_bytes : (long long)w.t->nbytes;
       ++k;
     }
 }
@@ -938,8 +991,8 @@ static int enqueue_step(g4_state* s) {
       f.scale = branch_scale;
     }
     // this layer's remaining projections stream into L2 during q|k|v and the attention
-    set_prefetch(f, {L.wo, L.gate_up, L.down});
-    int e = launch_proj(L.d_qkv, L.p_qkv, L.qkv, s->x[cur], s->qkv, f, c->status, st, l > 0);
+    set_prefetch(f, {proj_w(L.wo, L.k_wo, L.m_wo), proj_w(L.gate_up, L.k_gu, L.m_gu), proj_w(L.down, L.k_down, L.m_down)});
+    int e = launch_proj(L.m_qkv, L.k_qkv, L.d_qkv, L.p_qkv, L.qkv, s->x[cur], s->qkv, f, c->status, st, l > 0);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: qkv projection");
     cur ^= 1;
     // ---- attention
@@ -974,7 +1027,7 @@ static int enqueue_step(g4_state* s) {
     cudaError_t ce = launch_pdl_k(dec_attention_kernel, k.n_heads * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
     if (ce) return c->cuda_fail(ce, "decode: attention");
     // ---- output projection of the attention output
-    e = launch_proj(L.d_wo, L.p_wo, L.wo, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);
+    e = launch_proj(L.m_wo, L.k_wo, L.d_wo, L.p_wo, L.wo, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: output projection");
     // ---- gate / up, prologue: x += rmsnorm(xb2, post_attention_norm); rmsnorm(x, ffn_norm)
     GemvFuse g;
@@ -985,11 +1038,14 @@ static int enqueue_step(g4_state* s) {
     g.w_r = L.post_attn_norm;
     g.w_in = L.ffn_norm;
     g.x_out = s->x[cur ^ 1];
-    if (l + 1 < k.n_layers) set_prefetch(g, {m->L[l + 1].qkv});  // the next layer's first projection
-    e = launch_proj(L.d_gu, L.p_gu, L.gate_up, s->x[cur], s->hb, g, c->status, st, true);
+    if (l + 1 < k.n_layers) {
+      const LayerDev& N = m->L[l + 1];
+      set_prefetch(g, {proj_w(N.qkv, N.k_qkv, N.m_qkv)});
+    }  // the next layer's first projection
+    e = launch_proj(L.m_gu, L.k_gu, L.d_gu, L.p_gu, L.gate_up, s->x[cur], s->hb, g, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: gate/up projection");
     cur ^= 1;
-    e = launch_proj(L.d_down, L.p_down, L.down, s->hb, s->sh, GemvFuse{}, c->status, st, true);
+    e = launch_proj(L.m_down, L.k_down, L.d_down, L.p_down, L.down, s->hb, s->sh, GemvFuse{}, c->status, st, true);
     if (e) return c->cuda_fail((cudaError_t)e, "decode: down projection");
     branch = s->sh;
     branch_scale = L.scale;
@@ -1017,7 +1073,7 @@ static int enqueue_step(g4_state* s) {
   f.w_in = m->f32("output_norm.weight");
   f.softcap = k.logit_softcap;
   f.argmax = s->argmax;
-  set_prefetch(f, {m->L[0].qkv});  // the next step's first projection
+  set_prefetch(f, {proj_w(m->L[0].qkv, m->L[0].k_qkv, m->L[0].m_qkv)});  // the next step's first projection
   int e = launch_gemv_fused(m->p_logits, (const uint8_t*)m->wcls->d, s->x[cur], s->logits, f, c->status, st, true);
   if (e) return c->cuda_fail((cudaError_t)e, "decode: logits");
   cudaError_t ce = launch_pdl_k(dec_sample_kernel, 1, 32, 0, st, s->ctl, s->out_tok(), s->argmax);

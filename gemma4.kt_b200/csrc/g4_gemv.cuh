@@ -54,6 +54,21 @@ struct DecGemvPlan {
   int fast;
 };
 
+// Plan of the decoder's Q8_0 GEMV on the tensor cores (gemv_mma_kernel,
+// g4_gemv_mma.cu): weights repacked into 16-row x 32-column mma tiles.
+struct MmaGemvPlan {
+  int rows, cols, pair, fused;
+  int nrt, nkb;        // row tiles of 16, column blocks of 32
+  size_t tiles_total;  // nrt * nkb (the scale words follow the tiles' code bytes)
+  int ks;              // warps sharing one row tile (K split)
+  int tiles;           // row tiles per CTA task (8 / ks)
+  int kpw;             // blocks per warp
+  int ntasks, grid;
+  int xs_off, lim_off, xsc_off, misc_off, red_off;
+  size_t smem;
+  int fast;
+};
+
 // Options of plan_gemv.
 struct GemvOpts {
   bool fused = false;     // room for a fused prologue (fp32 activation in shared memory)

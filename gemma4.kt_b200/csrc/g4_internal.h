@@ -24,6 +24,14 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
 // Returns the cudaError_t of the launch.
 int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, unsigned* status,
                 cudaStream_t st);
+struct MmaGemvPlan;
+// The decoder's Q8_0 GEMV on the tensor cores (g4_gemv_mma.cu): the repacked
+// layout's size, the repack of a GGUF Q8_0 matrix into it, plan and launch.
+size_t mma_packed_bytes(int rows, int cols);
+int repack_q8_0_mma(const uint8_t* raw, int rows, int cols, uint8_t* packed, cudaStream_t st);
+MmaGemvPlan plan_gemv_mma(const DeviceInfo& dev, int rows, int cols, bool pair, bool fused);
+int launch_gemv_mma(const MmaGemvPlan& p, const uint8_t* packed, const float* x, float* y, const GemvFuse& f,
+                    unsigned* status, cudaStream_t st, bool pdl);
 struct DecGemvPlan;
 // The decoder's GEMV (g4_gemv_dec.cu): Q8_0 / Q4_K / Q6_K rows of whole blocks;
 // fast == 0 when it does not apply.  fused: room for a fused prologue.

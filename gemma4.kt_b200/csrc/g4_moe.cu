@@ -1718,13 +1718,14 @@ static int launch_expert(g4_ctx* c, int type, bool gu, const uint8_t* w, const f
   return launch_status();
 }
 
-// Q4_K for NB tokens on int16 activations (quantize_x16 layout: xq[j] is token
-// j's padded int16 row, xsc[j] its per-32-column scales, xs16[j] its fp32
-// per-16-column sums), the dp2a form of blk_nb's Q4_K branch.
+// Q4_K for NB tokens on two-part int16 activations (quantize_x16 layout: xq[j]
+// is token j's padded int16 row, xql[j] the remainders in units of 2^-16 of
+// the scale, xsc[j] its per-32-column scales, xs16[j] its fp32 per-16-column
+// sums), the dp2a form of blk_nb's Q4_K branch with fp32-level products.
 template <int PR, int NB>
 __device__ __forceinline__ void blk_q4k_nb_i16(const uint8_t* blk, int e0, int cols, const int16_t* const* xq,
-                                               const float* const* xsc, const float* const* xs16, int nbv,
-                                               float (&acc)[NB][PR]) {
+                                               const int16_t* const* xql, const float* const* xsc,
+                                               const float* const* xs16, int nbv, float (&acc)[NB][PR]) {
   const uint4 h = lds128(blk);
   const float d = f16_bits_to_f32((uint16_t)(h.x & 0xFFFFu));
   const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
@@ -1738,9 +1739,9 @@ __device__ __forceinline__ void blk_q4k_nb_i16(const uint8_t* blk, int e0, int c
     const int rr = PR == 1 ? 0 : eg / cols;
     const int xo = xq_at(col);
     const uint4 qa = lds128(blk + 16 + 32 * g), qb = lds128(blk + 32 + 32 * g);
-    int alo[NB], ahi[NB];
+    int alo[NB], ahi[NB], alo2[NB], ahi2[NB];
 #pragma unroll
-    for (int j = 0; j < NB; ++j) alo[j] = ahi[j] = 0;
+    for (int j = 0; j < NB; ++j) alo[j] = ahi[j] = alo2[j] = ahi2[j] = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const uint32_t w = k == 0 ? qa.x : k == 1 ? qa.y : k == 2 ? qa.z : k == 3 ? qa.w
@@ -1751,10 +1752,16 @@ __device__ __forceinline__ void blk_q4k_nb_i16(const uint8_t* blk, int e0, int c
         if (j < nbv) {
           const uint2 xl = *reinterpret_cast<const uint2*>(xq[j] + xo + 4 * k);
           const uint2 xh = *reinterpret_cast<const uint2*>(xq[j] + xo + 32 + 4 * k);
+          const uint2 yl = *reinterpret_cast<const uint2*>(xql[j] + xo + 4 * k);
+          const uint2 yh = *reinterpret_cast<const uint2*>(xql[j] + xo + 32 + 4 * k);
           alo[j] = dp2a_lo_su(xl.x, lo, alo[j]);
           alo[j] = dp2a_hi_su(xl.y, lo, alo[j]);
           ahi[j] = dp2a_lo_su(xh.x, hi, ahi[j]);
           ahi[j] = dp2a_hi_su(xh.y, hi, ahi[j]);
+          alo2[j] = dp2a_lo_su(yl.x, lo, alo2[j]);
+          alo2[j] = dp2a_hi_su(yl.y, lo, alo2[j]);
+          ahi2[j] = dp2a_lo_su(yh.x, hi, ahi2[j]);
+          ahi2[j] = dp2a_hi_su(yh.y, hi, ahi2[j]);
         }
       }
     }
@@ -1768,8 +1775,10 @@ __device__ __forceinline__ void blk_q4k_nb_i16(const uint8_t* blk, int e0, int c
         const float* q = xs16[j] + col / 16;
         const float xlo = q[0] + q[1], xhi = q[2] + q[3];
         const float s_lo = xsc[j][col / 32], s_hi = xsc[j][col / 32 + 1] * 0.0625f;
-        float v = dsl * (s_lo * (float)alo[j]);
-        v = fmaf(dsh, s_hi * (float)ahi[j], v);
+        const float flo = fmaf((float)alo2[j], kLoScale, (float)alo[j]);
+        const float fhi = fmaf((float)ahi2[j], kLoScale, (float)ahi[j]);
+        float v = dsl * (s_lo * flo);
+        v = fmaf(dsh, s_hi * fhi, v);
         v = fmaf(-dmin, fmaf(mn_lo, xlo, mn_hi * xhi), v);
         add_row<PR>(acc[j], rr, v);
       }
@@ -1811,7 +1820,7 @@ struct DecArgs {
   int rs, ns, pitch;     // units per stage, ring stages, bytes per physical row slot
   int stage_bytes;
   int tab_at, red_at, act_at, s16_at, ring_at;  // shared-memory layout (bytes)
-  int xq_at_, xsc_at, xq_stride;                // Q4_K: int16 activations (padded rows), per-32 scales
+  int xq_at_, xql_at, xsc_at, xq_stride;        // Q4_K: two-part int16 activations (padded rows), per-32 scales
   int red_stride;        // floats of one of the two partial-sum buffers
   int n_slots;           // T * n_used
   long long expert_elems;
@@ -1843,6 +1852,7 @@ __global__ void __launch_bounds__(512, 1) moe_dec_kernel(const __grid_constant__
   float* s_act = reinterpret_cast<float*>(smem + a.act_at);            // [act_rows][cols]
   float* s_s16 = reinterpret_cast<float*>(smem + a.s16_at);            // [act_rows][cols/16]
   int16_t* s_xq = reinterpret_cast<int16_t*>(smem + a.xq_at_);         // Q4_K: [act_rows][xq_stride]
+  int16_t* s_xql = reinterpret_cast<int16_t*>(smem + a.xql_at);        // Q4_K: remainders, same layout
   float* s_xsc = reinterpret_cast<float*>(smem + a.xsc_at);            // Q4_K: [act_rows][cols/32]
   uint8_t* ring = smem + a.ring_at;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
@@ -2002,7 +2012,12 @@ __global__ void __launch_bounds__(512, 1) moe_dec_kernel(const __grid_constant__
       if (t & 0x007FFFFFu) e += 0x00800000u;
       const bool nz = m > 0.f && e != 0u;
       const float inv = nz ? __uint_as_float(0x7F000000u - e) : 1.0f;
-      s_xq[(size_t)r * a.xq_stride + xq_at(32 * b + lane)] = (int16_t)__float2int_rn(v * inv);
+      const float f = v * inv;  // exact (power of two)
+      const float fq = rintf(f);
+      const int lo = __float2int_rn(__fmul_rn(__fsub_rn(f, fq), 65536.0f));  // remainder, units of 2^-16
+      const size_t xo = (size_t)r * a.xq_stride + xq_at(32 * b + lane);
+      s_xq[xo] = (int16_t)__float2int_rn(fq);
+      s_xql[xo] = (int16_t)max(-32767, min(32767, lo));
       if (lane == 0) s_xsc[(size_t)r * c32 + b] = nz ? __uint_as_float(e) : 1.0f;
     }
   }
@@ -2037,13 +2052,15 @@ __global__ void __launch_bounds__(512, 1) moe_dec_kernel(const __grid_constant__
           const uint8_t* blk = sbase + (size_t)r * a.pitch + d.off[ph] + (size_t)b * TS;
           if constexpr (FMT == Q4_K) {
             const int16_t* xq[NB];
+            const int16_t* xql[NB];
             const float* xsc[NB];
 #pragma unroll
             for (int j = 0; j < NB; ++j) {
               xq[j] = s_xq + (size_t)d.arow[j] * a.xq_stride;
+              xql[j] = s_xql + (size_t)d.arow[j] * a.xq_stride;
               xsc[j] = s_xsc + (size_t)d.arow[j] * (a.cols / 32);
             }
-            blk_q4k_nb_i16<PR, NB>(blk, b * BS, a.cols, xq, xsc, xs16, d.nbv, acc);
+            blk_q4k_nb_i16<PR, NB>(blk, b * BS, a.cols, xq, xql, xsc, xs16, d.nbv, acc);
           } else {
             blk_nb<FMT, PR, NB>(blk, b * BS, a.cols, xr, xs16, 0, d.nbv, acc);
           }
@@ -2340,6 +2357,9 @@ static bool dec_plan(const g4_ctx* c, int type, bool gu, int E, int K, int dim, 
     o += (size_t)a.act_rows * (a.cols / 16) * 4;
     o = align_up(o, 16);
     a.xq_at_ = (int)o;
+    o += type == Q4_K ? (size_t)a.act_rows * a.xq_stride * 2 : 0;
+    o = align_up(o, 16);
+    a.xql_at = (int)o;
     o += type == Q4_K ? (size_t)a.act_rows * a.xq_stride * 2 : 0;
     o = align_up(o, 16);
     a.xsc_at = (int)o;

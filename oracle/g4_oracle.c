@@ -439,6 +439,34 @@ void o_softmax(float *x, int n) {
   for (int i = 0; i < n; i++) x[i] = x[i] / sum;
 }
 
+/* Smallest routing margin seen since the last reset: the gap between the
+ * k-th and (k+1)-th largest router probability of a token.  Test
+ * infrastructure: a fixture whose margin is at the level of fp32 rounding
+ * (~1e-7) cannot pin an expert choice, since any implementation within the
+ * tolerance may take the other expert there. */
+static double g_topk_margin = INFINITY;
+
+void o_reset_topk_margin(void) { g_topk_margin = INFINITY; }
+double o_topk_margin(void) { return g_topk_margin; }
+
+void o_note_topk_margin(const float *probs, int n, int k) {
+  if (k <= 0 || k >= n || k > 64) return;
+  float top[65]; /* the k+1 largest so far, descending */
+  int m = 0;
+  for (int e = 0; e < n; e++) {
+    float v = probs[e];
+    if (m == k + 1 && !(v > top[k])) continue;
+    int i = m < k + 1 ? m++ : k; /* slot to fill, then move up */
+    while (i > 0 && top[i - 1] < v) {
+      top[i] = top[i - 1];
+      i--;
+    }
+    top[i] = v;
+  }
+  double gap = (double)top[k - 1] - (double)top[k];
+  if (gap < g_topk_margin) g_topk_margin = gap;
+}
+
 /* Llama.kt:276-293 */
 void o_topk(float *probs, int n, int k, int32_t *idx, float *val) {
   for (int ki = 0; ki < k; ki++) {
@@ -489,6 +517,7 @@ void o_moe_token(const o_moe_weights *w, const float *x, float *out, int32_t *to
   o_moe_router_logits(w, x, probs);
   if (router_logits_out) memcpy(router_logits_out, probs, sizeof(float) * w->n_expert);
   o_softmax(probs, w->n_expert); /* Llama.kt:273 */
+  o_note_topk_margin(probs, w->n_expert, w->n_used);
   o_topk(probs, w->n_expert, w->n_used, topk_idx, topk_prob);
   for (int i = 0; i < dim; i++) out[i] = 0.0f; /* Llama.kt:298 */
   for (int ki = 0; ki < w->n_used; ki++) {       /* Llama.kt:300-337 */

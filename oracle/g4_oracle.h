@@ -75,6 +75,11 @@ void o_softmax(float *x, int n);
 /* Llama.kt:276-293: iterative argmax, strict '>', lowest index wins ties.
  * probs is modified (picked entries set to -inf). */
 void o_topk(float *probs, int n, int k, int32_t *idx, float *val);
+/* Routing margin (test infrastructure): smallest gap between the k-th and
+ * (k+1)-th router probability over the o_moe_token calls since the reset. */
+void o_note_topk_margin(const float *probs, int n, int k);
+void o_reset_topk_margin(void);
+double o_topk_margin(void);
 
 /* The expert half of the MoE block for one token, Llama.kt:248-346.
  * x is the residual stream state.x (dim floats).  Writes the rms-normalised

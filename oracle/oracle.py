@@ -85,6 +85,9 @@ def lib() -> C.CDLL:
             "o_topk": (None, [vp, i, i, vp, vp]),
             "o_moe_token": (None, [C.POINTER(MoeW), vp, vp, vp, vp, vp, i]),
             "o_moe_router_logits": (None, [C.POINTER(MoeW), vp, vp]),
+            "o_reset_topk_margin": (None, []),
+            "o_note_topk_margin": (None, [vp, i, i]),
+            "o_topk_margin": (C.c_double, []),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -245,6 +248,19 @@ def _model_lib():
         L.o_rope_table.argtypes = [C.c_int, C.c_int, C.c_double, C.c_void_p, C.c_void_p, C.c_void_p]
         L._model_sigs = True
     return L
+
+
+def reset_topk_margin() -> None:
+    """Start a new routing-margin window (see topk_margin)."""
+    lib().o_reset_topk_margin()
+
+
+def topk_margin() -> float:
+    """Smallest gap between the k-th and (k+1)-th router probability over the
+    oracle's MoE tokens since reset_topk_margin (inf if none ran).  A gap at
+    the level of fp32 rounding means the expert choice there is a tie that
+    any implementation within the 1e-3 tolerance may break either way."""
+    return float(lib().o_topk_margin())
 
 
 def set_vector_api(on: bool) -> None:

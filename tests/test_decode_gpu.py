@@ -42,6 +42,20 @@ SPECS = {
     "moe": _spec(n_layers=3, ff=512, n_expert=16, n_expert_used=4, expert_ff=256, shared_kv_layers=0),
 }
 
+# Seeds of the MoE model: an expert choice is only reproducible where the
+# k-th and (k+1)-th router probabilities differ by more than fp32 rounding.
+# With 16 experts and ~250 routings per run, many seeds hold a gap near
+# 1e-7 somewhere (a tie: the oracle's own Vector-API and scalarDot modes
+# differ by that much), so these seeds keep every gap of the run above
+# MIN_MARGIN, which the tests check on the oracle.
+SEEDS = {"moe": 39}
+MIN_MARGIN = 2e-6
+
+
+def _check_margin(name):
+    if SPECS[name].n_expert:
+        assert oracle.topk_margin() >= MIN_MARGIN, (name, "ill-conditioned fixture", oracle.topk_margin())
+
 
 def _models(g4, ctx, spec, seed):
     from gemma4_kt_b200 import synth
@@ -55,10 +69,11 @@ def _models(g4, ctx, spec, seed):
 def test_decode_steps_vs_oracle(g4, ctx, name):
     """Prompt and greedy steps one at a time through g4_decode_step: logits of
     every step vs the oracle, and the argmax fed back identically."""
-    m, src, model, orc = _models(g4, ctx, SPECS[name], seed=11)
+    m, src, model, orc = _models(g4, ctx, SPECS[name], seed=SEEDS.get(name, 11))
     st = model.new_state()
     prompt = m.prompt(40)
     token, pos, errs = 2, 0, []
+    oracle.reset_topk_margin()
     for i in range(80):
         lg, nt = st.step(token, pos)
         ref = orc.step(token, pos)
@@ -71,6 +86,7 @@ def test_decode_steps_vs_oracle(g4, ctx, name):
             assert nt == int(np.argmax(ref)), (name, pos)
             token = nt
         pos += 1
+    _check_margin(name)
     print(f"\n{name}: per-step logits rel L2 max {max(errs):.2e} mean {np.mean(errs):.2e}")
     st.free()
     model.free()
@@ -81,9 +97,11 @@ def test_greedy_stream_gpu_resident(g4, ctx, name):
     """g4_decode_greedy (argmax fed back on the device, no host round trip)
     gives the oracle's token stream over 64 generated tokens, and a second
     run on a fresh state repeats it exactly."""
-    m, src, model, orc = _models(g4, ctx, SPECS[name], seed=12)
+    m, src, model, orc = _models(g4, ctx, SPECS[name], seed=SEEDS.get(name, 12))
     prompt = m.prompt(24)
+    oracle.reset_topk_margin()
     ref = orc.greedy(prompt, 64)
+    _check_margin(name)
     st = model.new_state()
     got = st.generate(np.concatenate([[2], prompt]).astype(np.int32), 64)
     assert np.array_equal(got, ref), (name, got, ref)

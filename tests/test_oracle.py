@@ -111,3 +111,20 @@ def test_more_formats_gemv_fixture(golden_more, name):
     raw, x, y = golden_more[f"gemv_{name}_raw"], golden_more[f"gemv_{name}_x"], golden_more[f"gemv_{name}_y"]
     got = oracle.matmul(MORE_IDS[name], raw, x, int(rows), int(cols))
     assert rel_l2(got, y) < 1e-5
+
+
+def test_topk_margin():
+    """The routing-margin probe the MoE decoder tests use to reject fixtures
+    with router ties: the gap between the k-th and (k+1)-th probability."""
+    p = np.array([0.1, 0.5, 0.2, 0.15, 0.05], np.float32)
+    oracle.reset_topk_margin()
+    assert oracle.topk_margin() == float("inf")
+    oracle.lib().o_note_topk_margin(p.ctypes.data, p.size, 2)  # 0.2 - 0.15
+    assert abs(oracle.topk_margin() - (np.float64(np.float32(0.2)) - np.float64(np.float32(0.15)))) < 1e-12
+    oracle.lib().o_note_topk_margin(p.ctypes.data, p.size, 1)  # 0.5 - 0.2: larger, minimum kept
+    assert abs(oracle.topk_margin() - 0.05) < 1e-7
+    oracle.lib().o_note_topk_margin(p.ctypes.data, p.size, 4)  # 0.1 - 0.05
+    assert abs(oracle.topk_margin() - 0.05) < 1e-7
+    q = np.array([0.3, 0.3, 0.4], np.float32)  # an exact tie at the boundary
+    oracle.lib().o_note_topk_margin(q.ctypes.data, q.size, 2)
+    assert oracle.topk_margin() == 0.0
