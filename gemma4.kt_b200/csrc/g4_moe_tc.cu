@@ -10,10 +10,11 @@
 // Q4_K blocks in HBM and are dequantized inside the kernel to fp16
 // (w = q*d*sc - dmin*m, Q4_KFloatTensor.kt:23-55, in packed fp16 arithmetic
 // with the scale and min split into fp16 high and low parts, so the result is
-// within about one fp16 rounding of the exact weight); activations enter the
-// tensor cores as fp16; products accumulate in fp32 in tensor memory.  The
-// result differs from the fp32 reference by the fp16 roundings of weights and
-// activations (about 3.5e-4 relative L2 per product).
+// within about one fp16 rounding of the exact weight).  Activations enter the
+// tensor cores as two fp16 parts, x = hi + lo (lo = fp16(x - hi), about 22
+// bits between them): every K step issues one MMA on the high parts and one
+// on the low parts into the same fp32 accumulator in tensor memory, so the
+// result differs from the fp32 reference by the weights' fp16 rounding only.
 //
 // K order inside every aligned group of four columns is (0, 2, 1, 3) in the
 // fp16 operands on both sides (weights as dequantized, activations as the
@@ -80,8 +81,9 @@ struct TcArgs {
   const int4* tiles;       // {expert, first sorted position, tokens, box index}
   const int32_t* n_tiles;
   const int32_t* perm;     // sorted position -> slot
-  __half* g16;             // gate_up output [sorted position][ff]
+  __half* g16;             // gate_up output [2][sorted position][ff]: high parts, then low parts
   float* D;                // down output [slot][dim]
+  int lo_row;              // row of a position's low part in the token matrices (= positions)
   unsigned* status;
 };
 
@@ -312,7 +314,8 @@ __global__ void __launch_bounds__(256) moe_tc_tiles_kernel(const int32_t* __rest
   }
 }
 
-// x16[p][:] = fp16(moe_in[token of slot perm[p]][:]) in stored K order, one warp per sorted position.
+// x16[p][:] = fp16(moe_in[token of slot perm[p]][:]) in stored K order and
+// x16[n_pos + p][:] the remainders fp16(x - hi), one warp per sorted position.
 __global__ void __launch_bounds__(256) moe_tc_gather_kernel(const float* __restrict__ moe_in,
                                                             const int32_t* __restrict__ perm,
                                                             __half* __restrict__ x16, int n_pos, int dim, int K) {
@@ -325,6 +328,10 @@ __global__ void __launch_bounds__(256) moe_tc_gather_kernel(const float* __restr
     const float4 v = __ldg(src + i);  // K 4i..4i+3 stored in the order (0, 2, 1, 3)
     const __half2 a = __floats2half2_rn(v.x, v.z), b = __floats2half2_rn(v.y, v.w);
     dst[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    const __half2 al = __floats2half2_rn(v.x - fa.x, v.z - fa.y), bl = __floats2half2_rn(v.y - fb.x, v.w - fb.y);
+    dst[(size_t)n_pos * dim / 4 + i] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&al), *reinterpret_cast<const uint32_t*>(&bl));
   }
 }
 
@@ -359,8 +366,8 @@ __global__ void __launch_bounds__(P * tc_threads(NG), 1)
                 (size_t)pp * a.pipe_bytes;
   const int S = a.stages, bsub = a.b_stage_bytes;
   uint8_t* a_st = sm;                                   // [S][KSUB] x [128 rows x 128 B] (unless TMEM_A)
-  uint8_t* b_st = sm + (TMEM_A ? 0 : (size_t)S * KSUB * kATile);  // [S][KSUB] x [cap rows x 128 B]
-  uint8_t* raw = b_st + (size_t)S * KSUB * bsub;        // [NG groups][kDepth] x [128 rows x kRowRaw]
+  uint8_t* b_st = sm + (TMEM_A ? 0 : (size_t)S * KSUB * kATile);  // [S][KSUB][hi, lo] x [cap rows x 128 B]
+  uint8_t* raw = b_st + (size_t)S * KSUB * 2 * bsub;    // [NG groups][kDepth] x [128 rows x kRowRaw]
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw + tc_raw_bytes(NG));
   uint64_t* full = bars;                                // producers (4 warps) + TMA bytes -> MMA
   uint64_t* empty = bars + kMaxStages;                  // MMA -> producers and TMA (tcgen05.commit)
@@ -425,17 +432,23 @@ __global__ void __launch_bounds__(P * tc_threads(NG), 1)
 #pragma unroll
           for (int sub = 0; sub < KSUB; ++sub) {
             if (sub < nsub) {
-              const uint64_t bd = sw128_desc(b_st + (size_t)(s * KSUB + sub) * bsub);
+              // token tile: high parts, then low parts (bsub bytes each)
+              const uint64_t bd = sw128_desc(b_st + (size_t)(s * KSUB + sub) * 2 * bsub);
+              const uint64_t bl = sw128_desc(b_st + ((size_t)(s * KSUB + sub) * 2 + 1) * bsub);
               if (TMEM_A) {
                 const uint32_t at = tmem_base + a.tmem_a_col + (uint32_t)(s * KSUB + sub) * 32u;
 #pragma unroll
-                for (int kk = 0; kk < kKB / kMmaK; ++kk)  // 16 K = 8 columns of A, 32 bytes of B
+                for (int kk = 0; kk < kKB / kMmaK; ++kk) {  // 16 K = 8 columns of A, 32 bytes of B
                   tc_mma_f16_ts(d_tmem, at + 8u * kk, bd + 2 * kk, idesc, (st | sub | kk) != 0);
+                  tc_mma_f16_ts(d_tmem, at + 8u * kk, bl + 2 * kk, idesc, 1u);
+                }
               } else {
                 const uint64_t ad = sw128_desc(a_st + (size_t)(s * KSUB + sub) * kATile);
 #pragma unroll
-                for (int kk = 0; kk < kKB / kMmaK; ++kk)  // +32 bytes of K per step, inside the swizzle row
+                for (int kk = 0; kk < kKB / kMmaK; ++kk) {  // +32 bytes of K per step, inside the swizzle row
                   tc_mma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (st | sub | kk) != 0);
+                  tc_mma_f16(d_tmem, ad + 2 * kk, bl + 2 * kk, idesc, 1u);
+                }
               }
             }
           }
@@ -472,9 +485,12 @@ __global__ void __launch_bounds__(P * tc_threads(NG), 1)
             break;
           }
           const int nsub = nsub_of(st);
-          mbar_arrive_expect_tx(&full[s], (uint32_t)nsub * box_bytes);
-          for (int sub = 0; sub < nsub; ++sub)
-            tma_load_2d(b_st + (size_t)(s * KSUB + sub) * bsub, map, (st * KSUB + sub) * kKB, tl.y, &full[s]);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)nsub * 2u * box_bytes);
+          for (int sub = 0; sub < nsub; ++sub) {
+            uint8_t* dst = b_st + (size_t)(s * KSUB + sub) * 2 * bsub;
+            tma_load_2d(dst, map, (st * KSUB + sub) * kKB, tl.y, &full[s]);
+            tma_load_2d(dst + bsub, map, (st * KSUB + sub) * kKB, a.lo_row + tl.y, &full[s]);
+          }
           ++n_issued;
           if (++s == S) {
             s = 0;
@@ -681,7 +697,12 @@ __global__ void __launch_bounds__(P * tc_threads(NG), 1)
             const float gate = odd ? recv : v[jj];
             const float up = odd ? v[jj + 1] : recv;
             const int tok = c0 + jj + (odd ? 1 : 0);
-            if (tok < n) a.g16[(size_t)(p0 + tok) * a.out_ld + col] = __float2half_rn(gelu_f(gate) * up);
+            if (tok < n) {
+              const float gv = gelu_f(gate) * up;
+              const __half hi = __float2half_rn(gv);
+              a.g16[(size_t)(p0 + tok) * a.out_ld + col] = hi;
+              a.g16[(size_t)(a.lo_row + p0 + tok) * a.out_ld + col] = __float2half_rn(gv - __half2float(hi));
+            }
           }
         } else {
           const int my_slot = (c0 + lane < n) ? a.perm[p0 + c0 + lane] : 0;
@@ -748,10 +769,10 @@ TcWork carve_tc(void* base, int T, int dim, int E, int K, int ff) {
   TcWork w;
   uint8_t* p = static_cast<uint8_t*>(base);
   const size_t n_pos = (size_t)T * K;
-  w.x16 = reinterpret_cast<__half*>(p);
-  p += al256(n_pos * dim * 2);
+  w.x16 = reinterpret_cast<__half*>(p);  // high parts, then low parts
+  p += al256(2 * n_pos * dim * 2);
   w.g16 = reinterpret_cast<__half*>(p);
-  p += al256(n_pos * ff * 2);
+  p += al256(2 * n_pos * ff * 2);
   w.tiles = reinterpret_cast<int4*>(p);
   p += al256((n_pos / 16 + E + 1) * sizeof(int4));
   w.n_tiles = reinterpret_cast<int32_t*>(p);
@@ -767,7 +788,7 @@ int token_cap(int T, int K, int E) {
 
 size_t moe_tc_scratch_bytes(int T, int dim, int E, int K, int ff) {
   const size_t n_pos = (size_t)T * K;
-  return al256(n_pos * dim * 2) + al256(n_pos * ff * 2) + al256((n_pos / 16 + E + 1) * sizeof(int4)) + 256;
+  return al256(2 * n_pos * dim * 2) + al256(2 * n_pos * ff * 2) + al256((n_pos / 16 + E + 1) * sizeof(int4)) + 256;
 }
 
 bool moe_tc_supported(int gate_up_type, int down_type, int dim, int ff, int E) {
@@ -796,8 +817,8 @@ cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* do
 
   CUtensorMap mx[kNumBoxes], mg[kNumBoxes];
   for (int b = 0; b < kNumBoxes; ++b) {
-    if (!make_map(enc, &mx[b], w.x16, (uint64_t)n_pos, (uint64_t)dim, 16u << b) ||
-        !make_map(enc, &mg[b], w.g16, (uint64_t)n_pos, (uint64_t)ff, 16u << b))
+    if (!make_map(enc, &mx[b], w.x16, 2ull * n_pos, (uint64_t)dim, 16u << b) ||
+        !make_map(enc, &mg[b], w.g16, 2ull * n_pos, (uint64_t)ff, 16u << b))
       return cudaErrorInvalidValue;
   }
   const int bsub = cap * 128;  // one 64-column token sub-tile
@@ -812,7 +833,7 @@ cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* do
   const size_t optin = c->dev.smem_optin;
   const size_t a_bytes = tmem_a ? 0 : (size_t)kATile;
   const size_t raw_bytes = (size_t)tc_raw_bytes(ng);
-  const size_t stage_bytes = (size_t)ksub * (a_bytes + bsub);
+  const size_t stage_bytes = (size_t)ksub * (a_bytes + 2 * bsub);  // token tiles: high and low parts
   const size_t pipe_budget = (optin - 1024) / P;
   if (pipe_budget < raw_bytes + kBarBytes + 2 * stage_bytes) return cudaErrorInvalidConfiguration;
   int stages = (int)((pipe_budget - raw_bytes - kBarBytes) / stage_bytes);
@@ -843,6 +864,7 @@ cudaError_t launch_moe_tc(g4_ctx* c, const uint8_t* gate_up_w, const uint8_t* do
   ga.perm = perm;
   ga.g16 = w.g16;
   ga.D = nullptr;
+  ga.lo_row = n_pos;
   ga.status = c->status;
 
   TcArgs da = ga;
