@@ -16,4 +16,4 @@ from .floattensor import (  # noqa: F401
     row_shard,
 )
 from .moe import FfnMoeBlock, MoeLayer, topk  # noqa: F401
-from .model import DecoderModel, DecoderState, ModelConfig, TensorSource  # noqa: F401
+from .model import DecoderBatch, DecoderModel, DecoderState, ModelConfig, TensorSource  # noqa: F401

@@ -65,6 +65,10 @@ SIGNATURES = {
     "g4_decode_enqueue": (_i, [_vp, _i]),
     "g4_decode_read_tokens": (_i, [_vp, _i, _i, _vp]),
     "g4_state_stream": (_vp, [_vp]),
+    "g4_batch_create": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
+    "g4_batch_free": (_i, [_vp]),
+    "g4_batch_step": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
+    "g4_batch_stream": (_vp, [_vp]),
 }
 
 

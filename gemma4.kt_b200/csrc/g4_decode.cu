@@ -76,6 +76,13 @@ struct AttnArgs {
   float* out;              // [n_heads * hs] attention output
   int ch_max;              // positions per chunk that fit the shared-memory tiles (multiple of 16)
   unsigned* status;
+  // Batched decode (g4_batch_step): sequence blockIdx.y at position pos_arr[y]
+  // with its own rows of qkv / cache / partials / tickets / out (strides in
+  // elements); chunk_stride CTAs per query head along x.  Single-sequence
+  // decode: pos_arr == nullptr, strides 0, chunk_stride kAttnMaxChunks.
+  const int* pos_arr;
+  long long qkv_stride, kv_stride, part_stride, out_stride;
+  int tick_stride, chunk_stride;
 };
 
 // Llama.kt:39-59 per-head rmsnorm, (w * ss) * x left to right (w == nullptr:
@@ -112,12 +119,19 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   const int hs = a.hs, half = hs / 2;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, NW = kAttnThreads / 32;
   // the step's position is staged by the host before the step's first kernel
-  const int pos = a.in_pos[*a.step];
+  const int sq = blockIdx.y;
+  const int pos = a.pos_arr ? a.pos_arr[sq] : a.in_pos[*a.step];
   const int start = a.window > 0 ? max(0, pos - a.window + 1) : 0;
   const int len = pos - start + 1;
   const int ch = attn_chunk(len, a.ch_max);
   const int nch = (len + ch - 1) / ch;
-  const int hq = blockIdx.x / kAttnMaxChunks, c = blockIdx.x % kAttnMaxChunks;
+  const int hq = blockIdx.x / a.chunk_stride, c = blockIdx.x % a.chunk_stride;
+  const float* qkv = a.qkv + sq * a.qkv_stride;
+  float* kc = a.kc + sq * a.kv_stride;
+  float* vc = a.vc + sq * a.kv_stride;
+  float* part_base = a.part + sq * a.part_stride;
+  unsigned* tickets = a.tickets + sq * a.tick_stride;
+  float* out = a.out + sq * a.out_stride;
   const int g = hq / a.kv_mul;
   if (c >= nch) return;
   const int t0 = start + c * ch, t1 = min(t0 + ch, pos + 1), n = t1 - t0;
@@ -144,8 +158,8 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
     __syncwarp();
     for (int j = lane; j < n_pre; j += 32) {
       const size_t src = (size_t)(t0 + j) * a.kvdim + (size_t)g * hs;
-      bulk_g2s(kt + (size_t)j * hs, a.kc + src, row_bytes, bar);
-      bulk_g2s(vt + (size_t)j * hs, a.vc + src, row_bytes, bar);
+      bulk_g2s(kt + (size_t)j * hs, kc + src, row_bytes, bar);
+      bulk_g2s(vt + (size_t)j * hs, vc + src, row_bytes, bar);
     }
   }
   const bool has_pos = t1 == pos + 1;
@@ -160,12 +174,12 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   // q of the head (Llama.kt:158-168) and, in the chunk holding the position,
   // its K/V row: computed (Llama.kt:174-195) or, for a layer that shares an
   // earlier layer's cache, read from it
-  for (int i = tid; i < hs; i += kAttnThreads) qs[i] = a.qkv[(size_t)hq * hs + i];
+  for (int i = tid; i < hs; i += kAttnThreads) qs[i] = qkv[(size_t)hq * hs + i];
   if (has_pos) {
     const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
-      kp[i] = a.write_kv ? a.qkv[a.k_off + (size_t)g * hs + i] : a.kc[row + i];
-      vp[i] = a.write_kv ? a.qkv[a.v_off + (size_t)g * hs + i] : a.vc[row + i];
+      kp[i] = a.write_kv ? qkv[a.k_off + (size_t)g * hs + i] : kc[row + i];
+      vp[i] = a.write_kv ? qkv[a.v_off + (size_t)g * hs + i] : vc[row + i];
     }
   }
   __syncthreads();
@@ -185,8 +199,8 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   if (has_pos && a.write_kv && hq % a.kv_mul == 0) {
     const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
-      a.kc[row + i] = kp[i];
-      a.vc[row + i] = vp[i];
+      kc[row + i] = kp[i];
+      vc[row + i] = vp[i];
     }
   }
   if (!mbar_wait_bounded(bar, 0)) {
@@ -225,7 +239,7 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   }
   __syncthreads();
   // partial V sums (Llama.kt:211-217)
-  float* part = a.part + ((size_t)hq * kAttnMaxChunks + c) * (hs + 2);
+  float* part = part_base + ((size_t)hq * kAttnMaxChunks + c) * (hs + 2);
   for (int d = tid; d < hs; d += kAttnThreads) {
     float acc = 0.f;
     for (int j = 0; j < n; ++j) acc = fmaf(sc[j], vt[(size_t)j * hs + d], acc);
@@ -239,13 +253,13 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   __syncthreads();
   if (tid == 0) {
     __threadfence();
-    const unsigned done = atomicAdd(a.tickets + hq, 1u);
+    const unsigned done = atomicAdd(tickets + hq, 1u);
     st[3] = done + 1 == (unsigned)nch ? 1.f : 0.f;
   }
   __syncthreads();
   if (st[3] == 0.f) return;
   __threadfence();  // acquire: the other chunks' partials are visible
-  const float* ph = a.part + (size_t)hq * kAttnMaxChunks * (hs + 2);
+  const float* ph = part_base + (size_t)hq * kAttnMaxChunks * (hs + 2);
   // out = sum_c w_c acc_c / sum_c w_c l_c, w_c = exp(m_c - max m) (Llama.kt:201-218 over the chunks)
   if (warp == 0) {
     float mc[kAttnMaxChunks / 32], lc[kAttnMaxChunks / 32];
@@ -285,9 +299,9 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
       for (int j = 0; j < kCh; ++j)
         if (k0 + j < nch) num = fmaf(wc[k0 + j], v[j], num);
     }
-    a.out[(size_t)hq * hs + d] = __fdiv_rn(num, st[2]);
+    out[(size_t)hq * hs + d] = __fdiv_rn(num, st[2]);
   }
-  if (tid == 0) a.tickets[hq] = 0u;  // every chunk has arrived: ready for the next launch
+  if (tid == 0) tickets[hq] = 0u;  // every chunk has arrived: ready for the next launch
 }
 
 // Greedy sampling (Sampler.ARGMAX, FloatTensor.argmax): the logits GEMV left
@@ -358,6 +372,7 @@ struct g4_model {
   std::vector<LayerDev> L;
   const g4_tensor* wcls = nullptr;
   GemvPlan p_logits{};
+  uint8_t* k_cls = nullptr;  // the output matrix repacked for the batched decoder (g4_batch_create)
   float *cr_full = nullptr, *ci_full = nullptr, *cr_swa = nullptr, *ci_swa = nullptr;
   bool finalized = false;
   int max_q = 0, max_kv = 0, max_ff = 0, max_hs = 0;
@@ -793,6 +808,7 @@ extern "C" int g4_model_free(g4_model* m) {
     for (uint8_t* p : {L.k_qkv, L.k_wo, L.k_gu, L.k_down})
       if (p) cudaFree(p);
   }
+  if (m->k_cls) cudaFree(m->k_cls);
   for (float* p : {m->cr_full, m->ci_full, m->cr_swa, m->ci_swa})
     if (p) cudaFree(p);
   delete m;
@@ -1020,6 +1036,7 @@ static int enqueue_step(g4_state* s) {
     aa.out = s->xbk;
     aa.ch_max = attn_ch_max(L.hs);
     aa.status = c->status;
+    aa.chunk_stride = kAttnMaxChunks;
     const size_t asmem = attn_smem(L.hs);
     if (asmem > 48 * 1024 &&
         cudaFuncSetAttribute(dec_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem))
@@ -1223,3 +1240,368 @@ int g4_decode_read_tokens(g4_state* s, int first_step, int n, int* out) {
 void* g4_state_stream(g4_state* s) { return s ? (void*)s->st : nullptr; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- batched decode
+// Many sequences advanced one position each per call (
+// 64 concurrent sequences).  The reference runs one LlamaState per sequence
+// (Llama.kt:105-408 per token); here the n sequences of a step share each
+// weight read: per layer a per-token prologue kernel, the T-token int8 mma GEMM
+// on the repacked Q8_0 tiles, the attention kernel with a sequence grid axis,
+// and g4_moe_layer on the n tokens.  Sequence i owns KV-cache slot i.
+
+struct g4_batch {
+  g4_model* m = nullptr;
+  int n_max = 0, max_pos = 0;
+  cudaStream_t st = nullptr;
+  float* buf = nullptr;  // activations, attention partials, KV caches
+  float *x[2] = {nullptr, nullptr}, *qkv = nullptr, *xbk = nullptr, *xb2 = nullptr, *hb = nullptr, *sh = nullptr;
+  float *moe_out = nullptr, *logits = nullptr, *part = nullptr;
+  std::vector<float*> kc, vc;   // per KV-owning layer: [n_max][max_pos][kvdim]
+  size_t part_stride = 0;       // floats of one sequence's attention partials
+  uint8_t* small = nullptr;     // limbs, scales, keys, tokens, positions, tickets
+  int8_t* lim = nullptr;
+  float* lsc = nullptr;
+  unsigned long long* keys = nullptr;
+  int *d_tok = nullptr, *d_pos = nullptr;
+  unsigned* tickets = nullptr;
+  int* h_io = nullptr;          // pinned: tokens [n_max], positions [n_max]
+  unsigned long long* h_keys = nullptr;  // pinned [n_max]
+  std::map<std::tuple<int, int, int>, MmaBatchPlan> plans;
+
+  const MmaBatchPlan* plan(int rows, int cols, int T) {
+    const int ng = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
+    auto key = std::make_tuple(rows, cols, ng);
+    auto it = plans.find(key);
+    if (it == plans.end()) it = plans.emplace(key, plan_gemm_mma_batch(m->ctx->dev, rows, cols, 8 * ng)).first;
+    return it->second.fast ? &it->second : nullptr;
+  }
+};
+
+extern "C" int g4_batch_free(g4_batch* b);
+
+// The Q8_0 projections of every layer and the output matrix in the tile layout
+// of the tensor-core GEMMs (kept by the model; the single-sequence decoder uses
+// the layer copies only when it planned them itself).
+static int batch_repack(g4_model* m) {
+  g4_ctx* c = m->ctx;
+  auto pack = [&](const g4_tensor* w, int rows, int cols, uint8_t*& packed) -> int {
+    if (packed) return 0;
+    if (!w || w->type != G4_TYPE_Q8_0 || w->n_elems != (uint64_t)rows * (uint64_t)cols || cols % 32) {
+      c->set_err("g4_batch_create: batched decode needs every projection and the output matrix in Q8_0");
+      return G4_E_TYPE;
+    }
+    const size_t bytes = mma_packed_bytes(rows, cols);
+    if (cudaMalloc(&packed, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      packed = nullptr;
+      c->set_err("g4_batch_create: cannot allocate %zu bytes of repacked weights", bytes);
+      return G4_E_NOMEM;
+    }
+    cudaError_t e = (cudaError_t)repack_q8_0_mma((const uint8_t*)w->d, rows, cols, packed, nullptr);
+    if (!e) e = cudaStreamSynchronize(nullptr);
+    return e ? c->cuda_fail(e, "g4_batch_create: repack") : 0;
+  };
+  const int dim = m->cfg.dim;
+  for (LayerDev& L : m->L) {
+    const int qkv_rows = (int)(L.qkv->n_elems / dim);
+    if (int r = pack(L.qkv, qkv_rows, dim, L.k_qkv)) return r;
+    if (int r = pack(L.wo, dim, L.qdim, L.k_wo)) return r;
+    if (int r = pack(L.gate_up, 2 * L.ff, dim, L.k_gu)) return r;
+    if (int r = pack(L.down, dim, L.ff, L.k_down)) return r;
+  }
+  return pack(m->wcls, m->cfg.vocab, dim, m->k_cls);
+}
+
+extern "C" int g4_batch_create(g4_model* m, int n_max, int max_positions, g4_batch** out) {
+  if (!m) return G4_E_ARG;
+  g4_ctx* c = m->ctx;
+  const g4_model_config& k = m->cfg;
+  if (!out || !m->finalized || n_max < 1 || n_max > kBatchMaxT || max_positions < 1 || max_positions > k.ctx_len) {
+    c->set_err("g4_batch_create: bad arguments (finalized model, 1..%d sequences, 1..%d positions)", kBatchMaxT,
+               k.ctx_len);
+    return G4_E_ARG;
+  }
+  if (int r = c->bind()) return r;
+  if (int r = batch_repack(m)) return r;
+  g4_batch* b = new (std::nothrow) g4_batch();
+  if (!b) return G4_E_NOMEM;
+  b->m = m;
+  b->n_max = n_max;
+  b->max_pos = max_positions;
+  auto al = [](size_t n) { return (n + 63) / 64 * 64; };  // floats, 256-byte multiples
+  const size_t N = n_max, dim = k.dim;
+  const size_t qkv_w = m->max_q + 2 * m->max_kv;
+  b->part_stride = al((size_t)k.n_heads * kAttnMaxChunks * (m->max_hs + 2));
+  size_t off = 0;
+  const size_t o_x0 = off; off += al(N * dim);
+  const size_t o_x1 = off; off += al(N * dim);
+  const size_t o_qkv = off; off += al(N * qkv_w);
+  const size_t o_xbk = off; off += al(N * m->max_q);
+  const size_t o_xb2 = off; off += al(N * dim);
+  const size_t o_hb = off; off += al(N * m->max_ff);
+  const size_t o_sh = off; off += al(N * dim);
+  const size_t o_moe = off; off += al(N * dim);
+  const size_t o_log = off; off += al(N * k.vocab);
+  const size_t o_part = off; off += N * b->part_stride;
+  std::vector<size_t> o_kc, o_vc;
+  for (int l = 0; l < k.n_layer_kv_from_start; ++l) {
+    const int hs = m->is_swa[l] ? k.head_size_swa : k.head_size_full;
+    const size_t n = al(N * max_positions * m->n_kv[l] * hs);
+    o_kc.push_back(off);
+    off += n;
+    o_vc.push_back(off);
+    off += n;
+  }
+  const size_t widest = std::max<size_t>(dim, std::max<size_t>(m->max_q, m->max_ff));
+  const size_t lim_bytes = (N * (widest / 32) * 96 + 255) / 256 * 256;
+  const size_t lsc_bytes = (N * (widest / 32) * 4 + 255) / 256 * 256;
+  const size_t small = lim_bytes + lsc_bytes + 256 + 3 * ((N * 8 + 255) / 256 * 256) + N * k.n_heads * 4;
+  if (cudaMalloc(&b->buf, off * 4) != cudaSuccess || cudaMalloc(&b->small, small) != cudaSuccess ||
+      cudaMallocHost(&b->h_io, N * 8) != cudaSuccess || cudaMallocHost(&b->h_keys, N * 8) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    g4_batch_free(b);
+    c->set_err("g4_batch_create: cannot allocate %zu bytes of activations and KV cache", off * 4);
+    return G4_E_NOMEM;
+  }
+  cudaMemset(b->buf, 0, off * 4);
+  cudaMemset(b->small, 0, small);
+  b->x[0] = b->buf + o_x0;
+  b->x[1] = b->buf + o_x1;
+  b->qkv = b->buf + o_qkv;
+  b->xbk = b->buf + o_xbk;
+  b->xb2 = b->buf + o_xb2;
+  b->hb = b->buf + o_hb;
+  b->sh = b->buf + o_sh;
+  b->moe_out = b->buf + o_moe;
+  b->logits = b->buf + o_log;
+  b->part = b->buf + o_part;
+  for (int l = 0; l < k.n_layer_kv_from_start; ++l) {
+    b->kc.push_back(b->buf + o_kc[l]);
+    b->vc.push_back(b->buf + o_vc[l]);
+  }
+  uint8_t* p = b->small;
+  b->lim = reinterpret_cast<int8_t*>(p);
+  p += lim_bytes;
+  b->lsc = reinterpret_cast<float*>(p);
+  p += lsc_bytes + 256;
+  b->keys = reinterpret_cast<unsigned long long*>(p);
+  p += (N * 8 + 255) / 256 * 256;
+  b->d_tok = reinterpret_cast<int*>(p);
+  p += (N * 8 + 255) / 256 * 256;
+  b->d_pos = reinterpret_cast<int*>(p);
+  p += (N * 8 + 255) / 256 * 256;
+  b->tickets = reinterpret_cast<unsigned*>(p);
+  // attention kernel set-up, and the MoE layers' work buffers at the widest batch
+  size_t asmem = 0;
+  for (const LayerDev& L : m->L) asmem = std::max(asmem, attn_smem(L.hs));
+  if (asmem > 48 * 1024 &&
+      cudaFuncSetAttribute(dec_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem)) {
+    g4_batch_free(b);
+    return c->cuda_fail(cudaGetLastError(), "g4_batch_create: attention set-up");
+  }
+  if (k.n_expert > 0) {
+    int r = g4_moe_layer(c, &m->L[0].moe, b->x[0], b->moe_out, n_max, nullptr, nullptr, b->st);
+    if (!r) r = c->check_status(b->st);
+    if (r) {
+      g4_batch_free(b);
+      return r;
+    }
+  }
+  if (cudaError_t e = cudaStreamSynchronize(b->st)) {
+    g4_batch_free(b);
+    return c->cuda_fail(e, "g4_batch_create");
+  }
+  *out = b;
+  return 0;
+}
+
+extern "C" int g4_batch_free(g4_batch* b) {
+  if (!b) return G4_E_ARG;
+  cudaSetDevice(b->m->ctx->dev.device);
+  if (b->st) cudaStreamSynchronize(b->st);
+  if (b->buf) cudaFree(b->buf);
+  if (b->small) cudaFree(b->small);
+  if (b->h_io) cudaFreeHost(b->h_io);
+  if (b->h_keys) cudaFreeHost(b->h_keys);
+  if (b->st) cudaStreamDestroy(b->st);
+  delete b;
+  return 0;
+}
+
+// One projection of the batch: activation limbs already in b->lim / b->lsc.
+static int batch_gemm(g4_batch* b, const uint8_t* packed, int rows, int cols, int n, float* y, int ldy, int out_mode,
+                      float softcap, unsigned long long* keys, const char* what) {
+  g4_ctx* c = b->m->ctx;
+  const MmaBatchPlan* p = b->plan(rows, cols, n);
+  if (!p) {
+    c->set_err("g4_batch_step: no GEMM plan for %s (%d x %d)", what, rows, cols);
+    return G4_E_DEVICE;
+  }
+  const int e = launch_gemm_mma_batch(*p, packed, b->lim, b->lsc, n, y, ldy, out_mode, softcap, keys, b->st);
+  return e ? c->cuda_fail((cudaError_t)e, what) : 0;
+}
+
+static int batch_prologue(g4_batch* b, const GemvFuse& f, const float* x, int dim, int n, const char* what) {
+  const int e = launch_batch_prologue(f, x, dim, n, b->lim, b->lsc, b->st);
+  return e ? b->m->ctx->cuda_fail((cudaError_t)e, what) : 0;
+}
+
+extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* positions, int n, float* logits_host,
+                             int* next_tokens_host) {
+  if (!b) return G4_E_ARG;
+  g4_model* m = b->m;
+  g4_ctx* c = m->ctx;
+  const g4_model_config& k = m->cfg;
+  if (!tokens || !positions || n < 1 || n > b->n_max) {
+    c->set_err("g4_batch_step: bad arguments (%d sequences, at most %d)", n, b->n_max);
+    return G4_E_ARG;
+  }
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= k.vocab || positions[i] < 0 || positions[i] >= b->max_pos) {
+      c->set_err("g4_batch_step: sequence %d: token %d / position %d out of range (vocab %d, %d positions)", i,
+                 tokens[i], positions[i], k.vocab, b->max_pos);
+      return G4_E_ARG;
+    }
+  if (int r = c->bind()) return r;
+  cudaStream_t st = b->st;
+  if (cudaError_t e = cudaStreamSynchronize(st)) return c->cuda_fail(e, "g4_batch_step");
+  std::memcpy(b->h_io, tokens, (size_t)n * 4);
+  std::memcpy(b->h_io + b->n_max, positions, (size_t)n * 4);
+  cudaError_t ce = cudaMemcpyAsync(b->d_tok, b->h_io, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+  if (!ce) ce = cudaMemcpyAsync(b->d_pos, b->h_io + b->n_max, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+  if (ce) return c->cuda_fail(ce, "g4_batch_step: staging");
+  const int dim = k.dim;
+  int cur = 0;
+  const float* branch = nullptr;
+  const float* branch_w = nullptr;
+  float branch_scale = 1.f;
+  const float* moe_prev = nullptr;
+  const float* moe_w = nullptr;
+  for (int l = 0; l < k.n_layers; ++l) {
+    const LayerDev& L = m->L[l];
+    const int qkv_n = (int)(L.qkv->n_elems / dim);  // rows of q | k | v (no v rows without attn_v)
+    // ---- q | k | v, prologue as the single-sequence decoder's (enqueue_step)
+    GemvFuse f;
+    f.eps = k.eps;
+    f.w_in = L.attn_norm;
+    f.x_out = b->x[cur ^ 1];
+    if (l == 0) {
+      f.in_mode = IN_EMBED_NORM;
+      const g4_tensor* emb = m->get("token_embd.weight");
+      f.emb = (const uint8_t*)emb->d;
+      f.emb_type = emb->type;
+      f.sqrt_dim = (float)sqrt((double)dim);
+      f.in_tok = b->d_tok;
+    } else if (moe_prev) {
+      f.in_mode = IN_MOE_MERGE;
+      f.r = branch;
+      f.w_r = branch_w;
+      f.m = moe_prev;
+      f.w_m = moe_w;
+      f.scale = branch_scale;
+    } else {
+      f.in_mode = IN_RESID_NORM;
+      f.r = branch;
+      f.w_r = branch_w;
+      f.scale = branch_scale;
+    }
+    if (int r = batch_prologue(b, f, l == 0 ? nullptr : b->x[cur], dim, n, "batch: qkv prologue")) return r;
+    if (int r = batch_gemm(b, L.k_qkv, qkv_n, dim, n, b->qkv, qkv_n, OUT_PLAIN, 0.f, nullptr, "batch: qkv")) return r;
+    cur ^= 1;
+    // ---- attention, one grid row per sequence
+    AttnArgs aa{};
+    aa.qkv = b->qkv;
+    aa.hs = L.hs;
+    aa.kv_mul = k.n_heads / L.n_kv;
+    aa.kvdim = L.kvdim;
+    const bool own = l < k.n_layer_kv_from_start;
+    aa.k_off = L.qdim;
+    aa.v_off = L.has_v ? L.qdim + L.kvdim : L.qdim;
+    aa.q_norm = L.q_norm;
+    aa.k_norm = L.k_norm;
+    aa.eps = k.eps;
+    aa.cr = L.swa ? m->cr_swa : m->cr_full;
+    aa.ci = L.swa ? m->ci_swa : m->ci_full;
+    aa.kc = b->kc[L.kv_src];
+    aa.vc = b->vc[L.kv_src];
+    aa.write_kv = own ? 1 : 0;
+    aa.window = L.swa ? k.sliding_window : 0;
+    aa.part = b->part;
+    aa.tickets = b->tickets;
+    aa.out = b->xbk;
+    aa.ch_max = attn_ch_max(L.hs);
+    aa.status = c->status;
+    aa.pos_arr = b->d_pos;
+    aa.qkv_stride = qkv_n;
+    aa.kv_stride = (long long)b->max_pos * L.kvdim;
+    aa.part_stride = (long long)b->part_stride;
+    aa.out_stride = L.qdim;
+    aa.tick_stride = k.n_heads;
+    int nch_max = 1;
+    for (int i = 0; i < n; ++i) {
+      const int pos = positions[i];
+      const int start = aa.window > 0 ? std::max(0, pos - aa.window + 1) : 0;
+      const int len = pos - start + 1;
+      const int ch = attn_chunk(len, aa.ch_max);
+      nch_max = std::max(nch_max, (len + ch - 1) / ch);
+    }
+    aa.chunk_stride = nch_max;
+    dec_attention_kernel<<<dim3(k.n_heads * nch_max, n), kAttnThreads, attn_smem(L.hs), st>>>(aa);
+    if (cudaError_t e = cudaGetLastError()) return c->cuda_fail(e, "batch: attention");
+    // ---- output projection
+    GemvFuse plain;
+    if (int r = batch_prologue(b, plain, b->xbk, L.qdim, n, "batch: o prologue")) return r;
+    if (int r = batch_gemm(b, L.k_wo, dim, L.qdim, n, b->xb2, dim, OUT_PLAIN, 0.f, nullptr, "batch: o")) return r;
+    // ---- gate / up: x += rmsnorm(xb2, post_attention_norm); rmsnorm(x, ffn_norm); gelu(gate) * up
+    GemvFuse g;
+    g.in_mode = IN_RESID_NORM;
+    g.eps = k.eps;
+    g.r = b->xb2;
+    g.w_r = L.post_attn_norm;
+    g.w_in = L.ffn_norm;
+    g.x_out = b->x[cur ^ 1];
+    if (int r = batch_prologue(b, g, b->x[cur], dim, n, "batch: gate/up prologue")) return r;
+    if (int r = batch_gemm(b, L.k_gu, 2 * L.ff, dim, n, b->hb, L.ff, OUT_GELU_PAIR, 0.f, nullptr, "batch: gate/up"))
+      return r;
+    cur ^= 1;
+    if (int r = batch_prologue(b, plain, b->hb, L.ff, n, "batch: down prologue")) return r;
+    if (int r = batch_gemm(b, L.k_down, dim, L.ff, n, b->sh, dim, OUT_PLAIN, 0.f, nullptr, "batch: down")) return r;
+    branch = b->sh;
+    branch_scale = L.scale;
+    if (k.n_expert > 0) {
+      if (int r = g4_moe_layer(c, &L.moe, b->x[cur], b->moe_out, n, nullptr, nullptr, st)) return r;
+      branch_w = L.post_ffw_norm_1;
+      moe_prev = b->moe_out;
+      moe_w = L.post_ffw_norm;
+    } else {
+      branch_w = L.post_ffw_norm;
+      moe_prev = nullptr;
+    }
+  }
+  // ---- logits: last residual, rmsnorm(output_norm), projection, softcap, arg-max per sequence
+  GemvFuse f;
+  f.in_mode = moe_prev ? IN_MOE_MERGE : IN_RESID_NORM;
+  f.eps = k.eps;
+  f.r = branch;
+  f.w_r = branch_w;
+  f.m = moe_prev;
+  f.w_m = moe_w;
+  f.scale = branch_scale;
+  f.w_in = m->f32("output_norm.weight");
+  if (int r = batch_prologue(b, f, b->x[cur], dim, n, "batch: logits prologue")) return r;
+  if (cudaError_t e = cudaMemsetAsync(b->keys, 0, (size_t)n * 8, st)) return c->cuda_fail(e, "batch: keys");
+  if (int r = batch_gemm(b, m->k_cls, k.vocab, dim, n, b->logits, k.vocab, OUT_SOFTCAP_ARGMAX, k.logit_softcap,
+                         b->keys, "batch: logits"))
+    return r;
+  ce = cudaMemcpyAsync(b->h_keys, b->keys, (size_t)n * 8, cudaMemcpyDeviceToHost, st);
+  if (!ce && logits_host)
+    ce = cudaMemcpyAsync(logits_host, b->logits, (size_t)n * k.vocab * 4, cudaMemcpyDeviceToHost, st);
+  if (ce) return c->cuda_fail(ce, "g4_batch_step: read back");
+  if (int r = c->check_status(st)) return r;  // synchronises the stream
+  if (next_tokens_host)
+    for (int i = 0; i < n; ++i) next_tokens_host[i] = (int)(0xFFFFFFFFu - (uint32_t)(b->h_keys[i] & 0xFFFFFFFFull));
+  return 0;
+}
+
+extern "C" void* g4_batch_stream(g4_batch* b) { return b ? (void*)b->st : nullptr; }

@@ -47,7 +47,7 @@ static __device__ void fused_prologue(const GemvFuse& f, const float* __restrict
                                       const PrologueConst* pc = nullptr) {
   const int mode = IN >= 0 ? IN : f.in_mode;
   const int tid = threadIdx.x, nt = blockDim.x;
-  const bool store = f.x_out != nullptr && blockIdx.x == 0;
+  const bool store = f.x_out != nullptr && (f.store_all || blockIdx.x == 0);
   constexpr int kMaxE = kPrologueMaxE;
   if (n <= kMaxE * nt) {
     // every input this thread needs, loaded in one round, then the passes in registers

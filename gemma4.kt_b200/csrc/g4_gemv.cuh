@@ -69,6 +69,18 @@ struct MmaGemvPlan {
   int fast;
 };
 
+// Plan of the batched decode GEMM (gemm_mma_batch_kernel, g4_gemv_mma.cu):
+// T <= kBatchMaxT tokens on the repacked Q8_0 tiles, groups of 8 tokens.
+constexpr int kBatchMaxT = 64;
+struct MmaBatchPlan {
+  int rows, cols, nrt, nkb;
+  int ng;              // token groups of 8 the kernel is compiled for (1, 2, 4, 8)
+  int ks, tiles, kpw;  // warps per row tile (K split), row tiles per task, blocks per warp
+  int ntasks, grid;
+  size_t smem;
+  int fast;
+};
+
 // Options of plan_gemv.
 struct GemvOpts {
   bool fused = false;     // room for a fused prologue (fp32 activation in shared memory)
@@ -106,6 +118,7 @@ struct GemvFuse {
   const float* m = nullptr;   // IN_MOE_MERGE: the expert half's output
   const float* w_m = nullptr;
   float* x_out = nullptr;     // CTA 0 stores xn (the new residual stream) here; must not alias x
+  int store_all = 0;          // every CTA stores (batched prologues: one CTA per token, pointers offset)
   const uint8_t* emb = nullptr;  // IN_EMBED_NORM: embedding table (GGUF blocks)
   int emb_type = 0;
   const int* step = nullptr;     // IN_EMBED_NORM: token = in_tok[*step] >= 0 ? in_tok[*step] : *next_tok

@@ -89,6 +89,65 @@ __global__ void repack_q8_0_mma_kernel(const uint8_t* __restrict__ raw, int rows
   }
 }
 
+// The activation of one CTA as three int8 limbs per value (layout [nkb][96]:
+// limb h at +0, m at +32, l at +64 of each 32-column block) and the block's
+// power-of-two scale.  kGlobal: src is global memory written by an earlier
+// grid (read through L2), else shared memory.
+template <bool kGlobal>
+__device__ __forceinline__ void limbs_cta(const float* src, int cols, int8_t* lim, float* xsc) {
+  constexpr int kQ = 6;
+  const int n4 = cols / 4;
+  for (int i0 = 0; i0 < n4; i0 += kQ * (int)blockDim.x) {
+    float4 vq[kQ];
+#pragma unroll
+    for (int qq = 0; qq < kQ; ++qq) {
+      const int i = i0 + qq * (int)blockDim.x + (int)threadIdx.x;
+      vq[qq] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < n4) {
+        if constexpr (kGlobal) vq[qq] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+        else vq[qq] = reinterpret_cast<const float4*>(src)[i];
+      }
+    }
+#pragma unroll
+    for (int qq = 0; qq < kQ; ++qq) {
+      if (i0 + qq * (int)blockDim.x >= n4) break;  // uniform over the CTA
+      const int i = i0 + qq * (int)blockDim.x + (int)threadIdx.x;
+      const float4 v = vq[qq];
+      float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+      // smallest power of two sc with m / sc <= 127 (1 for an all-zero block)
+      const uint32_t tt = __float_as_uint(m * (1.0f / 127.0f));
+      uint32_t e = tt & 0x7F800000u;
+      if (tt & 0x007FFFFFu) e += 0x00800000u;
+      const bool nz = m > 0.f && e != 0u;
+      const float inv = nz ? __uint_as_float(0x7F000000u - e) : 1.0f;
+      if (i < n4) {
+        const float f[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};  // exact (power of two)
+        uint32_t wh = 0, wm = 0, wl = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int h, mi, li;
+          const float hr = rint_small(f[j], h);
+          const float r1 = __fsub_rn(f[j], hr);  // exact, |r1| <= 1/2
+          const float mr = rint_small(__fmul_rn(r1, 254.f), mi);
+          const float r2 = fmaf(r1, 254.f, -mr);  // |r2| <= 1/2
+          rint_small(__fmul_rn(r2, 254.f), li);
+          wh |= (uint32_t)(uint8_t)h << (8 * j);
+          wm |= (uint32_t)(uint8_t)mi << (8 * j);
+          wl |= (uint32_t)(uint8_t)li << (8 * j);
+        }
+        const int c = 4 * i, kb = c >> 5, cc = c & 31;
+        *reinterpret_cast<uint32_t*>(lim + kb * 96 + cc) = wh;
+        *reinterpret_cast<uint32_t*>(lim + kb * 96 + 32 + cc) = wm;
+        *reinterpret_cast<uint32_t*>(lim + kb * 96 + 64 + cc) = wl;
+        if ((i & 7) == 0) xsc[kb] = nz ? __uint_as_float(e) : 1.0f;
+      }
+    }
+  }
+}
+
 template <int IN>
 __global__ void __launch_bounds__(kMmaWarps * 32, 3) gemv_mma_kernel(const __grid_constant__ MmaGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -129,59 +188,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 3) gemv_mma_kernel(const __gri
 
   // activation: fused prologue (or x), then three int8 limbs per value
   if constexpr (IN != IN_PLAIN) fused_prologue<IN>(a.f, a.x, xs, misc, p.cols, &pc);
-  {
-    constexpr int kQ = 6;
-    const int n4 = p.cols / 4;
-    for (int i0 = 0; i0 < n4; i0 += kQ * (int)blockDim.x) {
-      float4 vq[kQ];
-#pragma unroll
-      for (int qq = 0; qq < kQ; ++qq) {
-        const int i = i0 + qq * (int)blockDim.x + (int)threadIdx.x;
-        vq[qq] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n4) {
-          if constexpr (IN == IN_PLAIN) vq[qq] = __ldcg(reinterpret_cast<const float4*>(a.x) + i);
-          else vq[qq] = reinterpret_cast<const float4*>(xs)[i];
-        }
-      }
-#pragma unroll
-      for (int qq = 0; qq < kQ; ++qq) {
-        if (i0 + qq * (int)blockDim.x >= n4) break;  // uniform over the CTA
-        const int i = i0 + qq * (int)blockDim.x + (int)threadIdx.x;
-        const float4 v = vq[qq];
-        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        // smallest power of two sc with m / sc <= 127 (1 for an all-zero block)
-        const uint32_t tt = __float_as_uint(m * (1.0f / 127.0f));
-        uint32_t e = tt & 0x7F800000u;
-        if (tt & 0x007FFFFFu) e += 0x00800000u;
-        const bool nz = m > 0.f && e != 0u;
-        const float inv = nz ? __uint_as_float(0x7F000000u - e) : 1.0f;
-        if (i < n4) {
-          const float f[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};  // exact (power of two)
-          uint32_t wh = 0, wm = 0, wl = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            int h, mi, li;
-            const float hr = rint_small(f[j], h);
-            const float r1 = __fsub_rn(f[j], hr);  // exact, |r1| <= 1/2
-            const float mr = rint_small(__fmul_rn(r1, 254.f), mi);
-            const float r2 = fmaf(r1, 254.f, -mr);  // |r2| <= 1/2
-            rint_small(__fmul_rn(r2, 254.f), li);
-            wh |= (uint32_t)(uint8_t)h << (8 * j);
-            wm |= (uint32_t)(uint8_t)mi << (8 * j);
-            wl |= (uint32_t)(uint8_t)li << (8 * j);
-          }
-          const int c = 4 * i, kb = c >> 5, cc = c & 31;
-          *reinterpret_cast<uint32_t*>(lim + kb * 96 + cc) = wh;
-          *reinterpret_cast<uint32_t*>(lim + kb * 96 + 32 + cc) = wm;
-          *reinterpret_cast<uint32_t*>(lim + kb * 96 + 64 + cc) = wl;
-          if ((i & 7) == 0) xsc[kb] = nz ? __uint_as_float(e) : 1.0f;
-        }
-      }
-    }
-  }
+  if constexpr (IN == IN_PLAIN) limbs_cta<true>(a.x, p.cols, lim, xsc);
+  else limbs_cta<false>(xs, p.cols, lim, xsc);
   __syncthreads();
 
   const int out_mode = a.f.out_mode;
@@ -364,6 +372,242 @@ int launch_gemv_mma(const MmaGemvPlan& p, const uint8_t* packed, const float* x,
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return (int)cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+// ---------------------------------------------------------------- batched decode
+// Many sequences at one step each (g4_batch_step): T <= kBatchMaxT tokens.
+
+// An int32 product sum as float (|v| < 2^22, exact): magic-number conversion
+// on the FP32 pipe instead of the quarter-rate integer-to-float unit.
+__device__ __forceinline__ float small_i2f(int v) {
+  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+
+__device__ int g_batch_step0 = 0;  // step index 0: the batched embedding prologue reads in_tok[0]
+
+struct BatchPrologueArgs {
+  GemvFuse f;        // token 0's pointers; token s adds s * dim to x, f.r, f.m, f.x_out; f.in_tok = tokens[T]
+  const float* x;    // [T][dim]: the residual stream (norm modes) or the activation (IN_PLAIN)
+  int dim;
+  int8_t* lim;       // [T][dim/32][96] int8 limbs
+  float* lsc;        // [T][dim/32] block scales
+};
+
+// One CTA per token: the decoder's fused prologue of that token (norms,
+// residual, embedding, MoE merge; the new residual stored by every CTA), then
+// its activation as int8 limbs for gemm_mma_batch_kernel.
+__global__ void __launch_bounds__(512) batch_prologue_kernel(const __grid_constant__ BatchPrologueArgs a) {
+  extern __shared__ __align__(16) float bxs[];  // [dim] activation, then 64 floats of reduction space
+  const int s = blockIdx.x, nkb = a.dim / 32;
+  const size_t off = (size_t)s * a.dim;
+  int8_t* lim = a.lim + (size_t)s * nkb * 96;
+  float* lsc = a.lsc + (size_t)s * nkb;
+  if (a.f.in_mode == IN_PLAIN) {
+    limbs_cta<true>(a.x + off, a.dim, lim, lsc);
+    return;
+  }
+  GemvFuse f = a.f;
+  f.store_all = 1;
+  if (f.r) f.r += off;
+  if (f.m) f.m += off;
+  if (f.x_out) f.x_out += off;
+  if (f.in_mode == IN_EMBED_NORM) {
+    f.in_tok = a.f.in_tok + s;
+    f.step = &g_batch_step0;
+  }
+  fused_prologue<-1>(f, a.x ? a.x + off : nullptr, bxs, bxs + a.dim, a.dim, nullptr);
+  limbs_cta<false>(bxs, a.dim, lim, lsc);
+}
+
+struct MmaBatchArgs {
+  MmaBatchPlan p;
+  const uint4* q;       // repacked weights (repack_q8_0_mma)
+  const uint32_t* sc;
+  const int8_t* lim;    // [T][nkb][96]
+  const float* lsc;     // [T][nkb]
+  float* y;             // [T][ldy]
+  int T, ldy, out_mode;
+  float softcap;
+  unsigned long long* argmax;  // OUT_SOFTCAP_ARGMAX: [T] keys (atomicMax)
+};
+
+// Y[t][row] = W[row] . x_t for T tokens on the repacked tiles: a warp takes a
+// row tile and its share of the blocks (K) and, per block, one mma per limb
+// and group of 8 tokens (the tokens are the B operand's 8 columns).  The ks
+// warps of a row tile meet in shared memory; the epilogue runs a warp per
+// token (plain, gelu(gate) * up on interleaved rows, or softcap + arg-max).
+template <int NG>
+__global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const __grid_constant__ MmaBatchArgs a) {
+  extern __shared__ __align__(16) float red[];  // [8 warps][16 rows][RS]
+  constexpr int TT = 8 * NG, RS = TT + 1;
+  const MmaBatchPlan& p = a.p;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int sub = warp / p.ks, kw = warp % p.ks;
+  const int kb0 = kw * p.kpw, kb1 = min(p.nkb, kb0 + p.kpw);
+  const int T = a.T;
+  constexpr float kInv1 = 1.0f / 254.0f, kInv2 = 1.0f / 64516.0f;
+  for (int task = blockIdx.x; task < p.ntasks; task += gridDim.x) {
+    const int rt = task * p.tiles + sub;
+    float acc[NG][4];
+#pragma unroll
+    for (int G = 0; G < NG; ++G) acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.f;
+    if (rt < p.nrt) {
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const size_t tile = (size_t)rt * p.nkb + kb;
+        const uint4 A = __ldg(a.q + tile * 32 + lane);
+        const uint32_t S = __ldg(a.sc + tile * 8 + g);
+        const float d0 = f16_bits_to_f32((uint16_t)(S & 0xFFFFu)), d8 = f16_bits_to_f32((uint16_t)(S >> 16));
+#pragma unroll
+        for (int G = 0; G < NG; ++G) {
+          if (G * 8 < T) {  // uniform over the warp
+            const int tb = G * 8 + g;  // this lane's B column (token)
+            uint32_t b[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+            if (tb < T) {
+              const uint32_t* lp = reinterpret_cast<const uint32_t*>(a.lim + ((size_t)tb * p.nkb + kb) * 96 + 4 * t);
+#pragma unroll
+              for (int j = 0; j < 6; ++j) b[j] = __ldg(lp + 4 * j);  // limb j/2, K half j%2
+            }
+            int dh[4], dm[4], dl[4];
+            mma_s8(dh, A, b[0], b[1]);
+            mma_s8(dm, A, b[2], b[3]);
+            mma_s8(dl, A, b[4], b[5]);
+            const int t0 = G * 8 + 2 * t;  // tokens of this lane's D columns: t0, t0 + 1
+            const float s0 = t0 < T ? __ldg(a.lsc + (size_t)t0 * p.nkb + kb) : 0.f;
+            const float s1 = t0 + 1 < T ? __ldg(a.lsc + (size_t)(t0 + 1) * p.nkb + kb) : 0.f;
+            const float sc[4] = {d0 * s0, d0 * s1, d8 * s0, d8 * s1};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float v = fmaf(small_i2f(dl[i]), kInv2, fmaf(small_i2f(dm[i]), kInv1, small_i2f(dh[i])));
+              acc[G][i] = fmaf(v, sc[i], acc[G][i]);
+            }
+          }
+        }
+      }
+    }
+    // partial sums of this warp: rows g, g + 8 of its tile, tokens G*8 + 2t (+1)
+#pragma unroll
+    for (int G = 0; G < NG; ++G) {
+      const int tk = G * 8 + 2 * t;
+      red[(warp * 16 + g) * RS + tk] = acc[G][0];
+      red[(warp * 16 + g) * RS + tk + 1] = acc[G][1];
+      red[(warp * 16 + g + 8) * RS + tk] = acc[G][2];
+      red[(warp * 16 + g + 8) * RS + tk + 1] = acc[G][3];
+    }
+    __syncthreads();
+    const int erows = p.tiles * 16;  // 16, 32, 64 or 128
+    const unsigned emask = erows >= 32 ? 0xffffffffu : 0x0000ffffu;
+    for (int tk = warp; tk < T; tk += kMmaWarps) {
+      unsigned long long best = 0ull;
+      if (lane < erows) {
+        for (int r = lane; r < erows; r += 32) {
+          const int sr = r >> 4, rr = r & 15;
+          float sum = 0.f;
+          for (int w = 0; w < p.ks; ++w) sum += red[((sr * p.ks + w) * 16 + rr) * RS + tk];
+          const int row = (task * p.tiles + sr) * 16 + rr;
+          const bool ok = row < p.rows;
+          float* yt = a.y + (size_t)tk * a.ldy;
+          if (a.out_mode == OUT_GELU_PAIR) {
+            const float up = __shfl_xor_sync(emask, sum, 1);
+            if (ok && !(row & 1)) yt[row >> 1] = __fmul_rn(gelu_ref(sum), up);
+          } else if (a.out_mode == OUT_SOFTCAP_ARGMAX) {
+            if (ok) {
+              const float c = softcap_ref(sum, a.softcap);
+              yt[row] = c;
+              const unsigned long long key = argmax_key(c, row);
+              best = key > best ? key : best;
+            }
+          } else if (ok) {
+            yt[row] = sum;
+          }
+        }
+        if (a.out_mode == OUT_SOFTCAP_ARGMAX) {
+          for (int o = erows >= 32 ? 16 : 8; o > 0; o >>= 1) {
+            const unsigned long long v = __shfl_xor_sync(emask, best, o);
+            best = v > best ? v : best;
+          }
+          if (lane == 0 && best) atomicMax(a.argmax + tk, best);
+        }
+      }
+    }
+    __syncthreads();  // red is rewritten by the next task
+  }
+}
+
+using BatchFn = void (*)(const MmaBatchArgs);
+
+static BatchFn batch_fn(int ng) {
+  switch (ng) {
+    case 1: return gemm_mma_batch_kernel<1>;
+    case 2: return gemm_mma_batch_kernel<2>;
+    case 4: return gemm_mma_batch_kernel<4>;
+    case 8: return gemm_mma_batch_kernel<8>;
+    default: return nullptr;
+  }
+}
+
+MmaBatchPlan plan_gemm_mma_batch(const DeviceInfo& dev, int rows, int cols, int T) {
+  MmaBatchPlan p{};
+  p.rows = rows;
+  p.cols = cols;
+  if (rows <= 0 || cols <= 0 || cols % 32 || T <= 0 || T > kBatchMaxT) return p;
+  p.ng = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
+  p.nrt = (rows + 15) / 16;
+  p.nkb = cols / 32;
+  p.smem = (size_t)kMmaWarps * 16 * (8 * p.ng + 1) * 4;
+  BatchFn fn = batch_fn(p.ng);
+  int occ = 0;
+  if (!fn || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dev.smem_optin) ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kMmaWarps * 32, p.smem) || occ < 1) {
+    cudaGetLastError();
+    return p;
+  }
+  // K split as plan_gemv_mma: shortest critical path in task waves x blocks per warp
+  const int resident = occ * dev.sms;
+  long long best = -1;
+  for (int ks = 1; ks <= kMmaWarps; ks *= 2) {
+    const int tiles = kMmaWarps / ks;
+    const int ntasks = (p.nrt + tiles - 1) / tiles;
+    const int grid = std::min(ntasks, resident);
+    const int waves = (ntasks + grid - 1) / grid;
+    const int kpw = (p.nkb + ks - 1) / ks;
+    const long long cost = (long long)waves * kpw;
+    if (best < 0 || cost < best || (cost == best && grid > p.grid)) {
+      best = cost;
+      p.ks = ks;
+      p.tiles = tiles;
+      p.kpw = kpw;
+      p.ntasks = ntasks;
+      p.grid = grid;
+    }
+  }
+  p.fast = 1;
+  return p;
+}
+
+int launch_gemm_mma_batch(const MmaBatchPlan& p, const uint8_t* packed, const int8_t* lim, const float* lsc, int T,
+                          float* y, int ldy, int out_mode, float softcap, unsigned long long* argmax,
+                          cudaStream_t st) {
+  cudaGetLastError();
+  if (!p.fast || T <= 0 || T > 8 * p.ng || (out_mode == OUT_SOFTCAP_ARGMAX && !argmax) ||
+      (out_mode == OUT_GELU_PAIR && p.rows % 2))
+    return (int)cudaErrorInvalidValue;
+  BatchFn fn = batch_fn(p.ng);
+  const size_t tiles_total = (size_t)p.nrt * p.nkb;
+  MmaBatchArgs a{p, reinterpret_cast<const uint4*>(packed),
+                 reinterpret_cast<const uint32_t*>(packed + tiles_total * 512), lim, lsc, y, T, ldy, out_mode,
+                 softcap, argmax};
+  fn<<<p.grid, kMmaWarps * 32, p.smem, st>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int launch_batch_prologue(const GemvFuse& f, const float* x, int dim, int T, int8_t* lim, float* lsc,
+                          cudaStream_t st) {
+  cudaGetLastError();
+  if (T <= 0 || dim <= 0 || dim % 32 || dim > 4096) return (int)cudaErrorInvalidValue;
+  BatchPrologueArgs a{f, x, dim, lim, lsc};
+  const size_t smem = (size_t)(dim + 64) * 4;
+  batch_prologue_kernel<<<T, 512, smem, st>>>(a);
+  return (int)cudaGetLastError();
 }
 
 }  // namespace g4

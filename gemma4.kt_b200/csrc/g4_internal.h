@@ -32,6 +32,15 @@ int repack_q8_0_mma(const uint8_t* raw, int rows, int cols, uint8_t* packed, cud
 MmaGemvPlan plan_gemv_mma(const DeviceInfo& dev, int rows, int cols, bool pair, bool fused);
 int launch_gemv_mma(const MmaGemvPlan& p, const uint8_t* packed, const float* x, float* y, const GemvFuse& f,
                     unsigned* status, cudaStream_t st, bool pdl);
+struct MmaBatchPlan;
+// Batched decode (g4_gemv_mma.cu): the per-token prologue into int8 limbs and
+// the T-token GEMM on the repacked Q8_0 tiles.
+MmaBatchPlan plan_gemm_mma_batch(const DeviceInfo& dev, int rows, int cols, int T);
+int launch_gemm_mma_batch(const MmaBatchPlan& p, const uint8_t* packed, const int8_t* lim, const float* lsc, int T,
+                          float* y, int ldy, int out_mode, float softcap, unsigned long long* argmax,
+                          cudaStream_t st);
+int launch_batch_prologue(const GemvFuse& f, const float* x, int dim, int T, int8_t* lim, float* lsc,
+                          cudaStream_t st);
 struct DecGemvPlan;
 // The decoder's GEMV (g4_gemv_dec.cu): Q8_0 / Q4_K / Q6_K rows of whole blocks;
 // fast == 0 when it does not apply.  fused: room for a fused prologue.

@@ -199,6 +199,9 @@ class DecoderModel:
     def new_state(self) -> "DecoderState":
         return DecoderState(self)
 
+    def new_batch(self, n_max: int, max_positions: int) -> "DecoderBatch":
+        return DecoderBatch(self, n_max, max_positions)
+
 
 class DecoderState:
     """LlamaState on the device (KV cache, activations, step control)."""
@@ -257,3 +260,46 @@ class DecoderState:
         check(lib().g4_decode_read_tokens(self.handle, int(first_step), int(n), out.ctypes.data_as(C.c_void_p)),
               self.model.ctx.handle, "g4_decode_read_tokens")
         return out
+
+
+class DecoderBatch:
+    """Many sequences decoded together (g4_batch): one LlamaState's worth of
+    KV cache per sequence, every step advances sequences 0..n-1 by one
+    position each with the weight reads shared across them."""
+
+    def __init__(self, model: DecoderModel, n_max: int, max_positions: int):
+        self.model, self.n_max, self.max_positions = model, int(n_max), int(max_positions)
+        h = C.c_void_p()
+        check(lib().g4_batch_create(model.handle, self.n_max, self.max_positions, C.byref(h)), model.ctx.handle,
+              "g4_batch_create")
+        self.handle = h
+
+    def free(self) -> None:
+        if getattr(self, "handle", None):
+            lib().g4_batch_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return int(lib().g4_batch_stream(self.handle) or 0)
+
+    def step(self, tokens, positions, want_logits: bool = True):
+        """Llama.forward for sequences 0..n-1: (logits [n, vocab] or None, argmax [n])."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        if t.shape != p.shape or t.ndim != 1:
+            raise ValueError("tokens and positions must be 1-D and of equal length")
+        n = t.size
+        lg = np.empty((n, self.model.cfg.vocab), np.float32) if want_logits else None
+        nt = np.empty(n, np.int32)
+        check(lib().g4_batch_step(self.handle, t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p), n,
+                                  lg.ctypes.data_as(C.c_void_p) if want_logits else None,
+                                  nt.ctypes.data_as(C.c_void_p)),
+              self.model.ctx.handle, "g4_batch_step")
+        return lg, nt

@@ -293,6 +293,25 @@ int g4_decode_read_tokens(g4_state *state, int first_step, int n, int *out);
 /* The state's cudaStream_t. */
 void *g4_state_stream(g4_state *state);
 
+/* Batched decode: many sequences, one position each per step.  The reference
+ * runs one LlamaState per sequence and Llama.forward per token (Llama.kt:105-408,
+ * GemmaModel.kt:73); a g4_batch holds n_max <= 64 sequences (KV cache of
+ * max_positions positions each, slot i = sequence i) and advances n of them
+ * per g4_batch_step, every weight read shared by the n tokens.  Needs every
+ * projection and the output matrix in Q8_0 (G4_E_TYPE otherwise); the model
+ * keeps a repacked copy of them.  Not thread-safe; its own stream. */
+typedef struct g4_batch g4_batch;
+int g4_batch_create(g4_model *model, int n_max, int max_positions, g4_batch **out);
+int g4_batch_free(g4_batch *batch);
+/* Llama.forward for sequences 0..n-1: tokens[i] at positions[i] (positions of
+ * one sequence must be fed in order from 0, as generateTokens does).
+ * logits_host [n][vocab] (after softcapping) and next_tokens_host [n] (argmax,
+ * first maximum) may be NULL.  Synchronous. */
+int g4_batch_step(g4_batch *batch, const int *tokens, const int *positions, int n, float *logits_host,
+                  int *next_tokens_host);
+/* The batch's cudaStream_t. */
+void *g4_batch_stream(g4_batch *batch);
+
 /* Router top-k alone on given logits (Llama.kt:273-293 + softmaxInPlace,
  * MutableFloatTensor.kt:54-59): probs_dev/idx_dev [n_tokens, k]. */
 int g4_moe_topk(g4_ctx *ctx, const float *logits_dev, int n_tokens, int n_expert, int k,
