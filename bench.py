@@ -431,6 +431,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     decode = None
     if world == 1 and rank == 0 and not args.no_decode:
         decode = bench_decode(g4, ctx, torch, dev, with_cpu=not args.no_cpu)
+    c5 = None
+    if world == 1 and rank == 0 and not args.no_decode and not args.no_c5:
+        c5 = bench_c5(g4, ctx, torch, dev, with_cpu=not args.no_cpu)
 
     if rank == 0:
         line = {
@@ -453,6 +456,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             line["moe"] = moe
         if decode:
             line["decode"] = decode
+        if c5:
+            line["c5"] = c5
         print(json.dumps(line), flush=True)
     for cc in cases:
         cc["w"].free()
@@ -564,6 +569,105 @@ def bench_decode(g4, ctx, torch, dev, with_cpu: bool = True):
                                                          "same model through the oracle's Llama.forward restatement"}
         orc.close()
     st.free()
+    model.free()
+    return res
+
+
+def c5_bytes_per_step(cfg, n_seq, positions, e_touched):
+    """Algorithmic HBM bytes of one batched C5 step: every dense matrix once
+    (Q8_0), the touched experts' Q4_K blocks and the routers, the output
+    matrix, and each sequence's K and V rows of the attended positions."""
+    dim, q8 = cfg.dim, 34 / 32
+    b = 0.0
+    for l in range(cfg.n_layers):
+        hs, nkv = cfg.head_size(l), cfg.n_kv_heads[l]
+        qd, kvd, ff = cfg.n_heads * hs, nkv * hs, cfg.ff[l]
+        b += (dim * (qd + 2 * kvd) + qd * dim + 3 * dim * ff) * q8
+        b += e_touched * (3 * cfg.expert_ff * dim) * 144 / 256 + dim * cfg.n_expert * 4
+        window = cfg.sliding_window if cfg.is_swa[l] else 0
+        for p in positions:
+            span = min(p + 1, window) if window else p + 1
+            b += n_seq / len(positions) * span * kvd * 4 * 2
+    return b + cfg.vocab * dim * q8
+
+
+def bench_c5(g4, ctx, torch, dev, with_cpu: bool = True):
+    """Configuration 5 (MoE decoder, seed 4): 64 sequences decoded together
+    through g4_batch_step, <bos> + 512 random prompt ids each, then 256 greedy
+    tokens each (768 batched steps)."""
+    import dataclasses
+
+    from gemma4_kt_b200 import synth
+
+    t0 = time.time()
+    spec = dataclasses.replace(synth.C5_MOE, replicate_layers=True)
+    m = synth.SynthDecoder(spec, seed=4)
+    src = g4.TensorSource.from_synth(m)
+    model = g4.DecoderModel(ctx, src)
+    cfg = model.cfg
+    n_seq, n_prompt, n_gen = 64, 512, 256
+    steps = n_prompt + n_gen
+    prompts = np.stack([np.concatenate([[2], m.prompt(n_prompt, seed=4000 + i)]) for i in range(n_seq)]).astype(np.int32)
+    batch = model.new_batch(n_seq, steps)
+    build_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(batch.stream, device=dev)
+    for p in range(3):  # warm-up (kernels set up, weights touched); the timed run rewrites these positions
+        batch.step(prompts[:, p], np.full(n_seq, p, np.int32), want_logits=False)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    tok = prompts[:, 0].copy()
+    gen = np.zeros((n_seq, n_gen), np.int32)
+    ev[0].record(stream)
+    for p in range(steps):
+        if p == n_prompt:
+            ev[1].record(stream)
+        _, nt = batch.step(tok, np.full(n_seq, p, np.int32), want_logits=False)
+        if p >= n_prompt:
+            gen[:, p - n_prompt] = nt
+        tok = prompts[:, p + 1] if p + 1 <= n_prompt else nt
+    ev[2].record(stream)
+    torch.cuda.synchronize()
+    prompt_ms, gen_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    hbm, hbm_kind = peaks()
+    e_touched = cfg.n_expert * (1 - (1 - cfg.n_expert_used / cfg.n_expert) ** n_seq)
+    bytes_gen = c5_bytes_per_step(cfg, n_seq, list(range(n_prompt, steps)), e_touched) * n_gen
+    achieved = bytes_gen / (gen_ms * 1e-3) / 1e9
+    res = {
+        "metric": "batched decode tok/s",
+        "config": "C5 MoE decoder: 30 layers, hidden 2816, 16 q / 8 kv heads x 256, 128 experts top-8 ff 704 Q4_K, "
+                  "shared FFN 2112 Q8_0, vocab 262144, seed 4; 64 sequences x (<bos> + 512 random prompt ids), "
+                  "256 greedy tokens each, fp32 KV cache",
+        "generation_tok_s": round(n_seq * n_gen / (gen_ms * 1e-3), 1),
+        "prompt_tok_s": round(n_seq * n_prompt / (prompt_ms * 1e-3), 1),
+        "ms_per_step": round(gen_ms / n_gen, 3),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "peak_kind": hbm_kind,
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "bytes_per_step": round(bytes_gen / n_gen),
+                     "note": "dense and output matrices once per step, expected touched experts "
+                             f"({e_touched:.1f} of {cfg.n_expert}), KV rows of every attended position"},
+        "e2e": {"value": round(n_seq * n_gen / (gen_ms * 1e-3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": n_seq * 8, "d2h_bytes_per_step": n_seq * 8,
+                "note": "every step is one synchronous g4_batch_step call from host arrays (ids and positions in, "
+                        "argmax ids out), so the timed loop is the end-to-end figure"},
+        "timing": "CUDA events on the batch's stream around the 512 prompt steps and the 256 generating steps",
+        "data": "synthetic: seeded generator (normal_fast), layer matrices generated once and uploaded to each of "
+                "the 30 layers (same shapes, types and HBM bytes per layer as distinct weights)",
+        "model_build_s": round(build_s, 1),
+    }
+    if with_cpu:
+        from oracle import oracle
+
+        orc = oracle.ModelOracle(src)
+        n_cpu = 2
+        tc = time.perf_counter()
+        for p in range(n_cpu):
+            orc.step(int(prompts[0, p]), p)
+        cpu_s = (time.perf_counter() - tc) / n_cpu
+        res["cpu_baseline"] = {"value": round(1.0 / cpu_s, 3), "unit": "tok/s", "cores": os.cpu_count() or 1,
+                               "kind": "port", "sample": f"{n_cpu} forward steps of one sequence of the same model "
+                                                         "through the oracle's Llama.forward restatement"}
+        orc.close()
+    batch.free()
     model.free()
     return res
 
@@ -774,6 +878,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=0,
                     help="profiling mode: run this many C4 decode steps (graph launches) and exit")
     ap.add_argument("--decode-only", action="store_true", help="time only the C4 decoder (prints its object)")
+    ap.add_argument("--c5-only", action="store_true", help="time only the C5 batched decoder (prints its object)")
+    ap.add_argument("--no-c5", action="store_true")
     ap.add_argument("--only", default=None,
                     help="profiling mode: run one sweep case FORMAT:ROWSxCOLS (e.g. Q4_K:262144x1536) --reps times")
     ap.add_argument("--reps", type=int, default=3)
@@ -791,6 +897,16 @@ def main():
         g4 = __graft_entry__.load_package()
         ctx = g4.Context(0)
         print(json.dumps(bench_decode(g4, ctx, torch, torch.device("cuda", 0), with_cpu=not args.no_cpu)), flush=True)
+        ctx.close()
+        return
+    if args.c5_only:
+        import torch
+
+        import __graft_entry__
+
+        g4 = __graft_entry__.load_package()
+        ctx = g4.Context(0)
+        print(json.dumps(bench_c5(g4, ctx, torch, torch.device("cuda", 0), with_cpu=not args.no_cpu)), flush=True)
         ctx.close()
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -140,6 +140,8 @@ def synth() -> C.CDLL:
         S = C.CDLL(str(SYNTH_PATH))
         S.g4s_quantize.restype = C.c_int
         S.g4s_quantize.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_void_p, C.c_int]
+        S.g4s_normal.restype = C.c_int
+        S.g4s_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_void_p, C.c_int64, C.c_double, C.c_int]
         S.g4s_nbytes.restype = C.c_int64
         S.g4s_nbytes.argtypes = [C.c_int, C.c_int64]
         _synth = S

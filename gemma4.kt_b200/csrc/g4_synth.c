@@ -202,3 +202,86 @@ int64_t g4s_nbytes(int type, int64_t n) {
   if (bb == 0 || n % be) return -1;
   return n / be * bb;
 }
+
+/* ------------------------------------------------------------------ fast normals
+ * Seeded N(0, std) float32 values for large synthetic models, generated by
+ * all host threads: value i belongs to chunk i >> 20, and each chunk has its
+ * own xoshiro256** stream seeded by splitmix64 from (seed, stream, chunk), so
+ * the output depends only on (seed, stream, n, std), not on the thread count.
+ * Normals by the Marsaglia polar method in double, rounded to float. */
+#define G4S_CHUNK_SHIFT 20
+
+static uint64_t splitmix64(uint64_t *s) {
+  uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+static inline uint64_t rotl64(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+
+typedef struct {
+  uint64_t s[4];
+} xoshiro;
+
+static inline uint64_t xoshiro_next(xoshiro *r) {
+  const uint64_t out = rotl64(r->s[1] * 5, 7) * 9, t = r->s[1] << 17;
+  r->s[2] ^= r->s[0];
+  r->s[3] ^= r->s[1];
+  r->s[1] ^= r->s[2];
+  r->s[0] ^= r->s[3];
+  r->s[2] ^= t;
+  r->s[3] = rotl64(r->s[3], 45);
+  return out;
+}
+
+static inline double unit_open(xoshiro *r) { /* uniform in (-1, 1) */
+  return ((double)(xoshiro_next(r) >> 11) + 0.5) * (2.0 / 9007199254740992.0) - 1.0;
+}
+
+typedef struct {
+  uint64_t seed, stream;
+  float *out;
+  int64_t n, c0, c1;
+  double std;
+} njob;
+
+static void *nworker(void *p) {
+  njob *j = (njob *)p;
+  for (int64_t c = j->c0; c < j->c1; c++) {
+    uint64_t sm = j->seed * 0xD1B54A32D192ED03ull ^ j->stream * 0x8CB92BA72F3D8DD7ull ^ (uint64_t)c;
+    xoshiro r;
+    for (int k = 0; k < 4; k++) r.s[k] = splitmix64(&sm);
+    const int64_t a = c << G4S_CHUNK_SHIFT;
+    const int64_t b = a + ((int64_t)1 << G4S_CHUNK_SHIFT) < j->n ? a + ((int64_t)1 << G4S_CHUNK_SHIFT) : j->n;
+    for (int64_t i = a; i < b; i += 2) {
+      double u, v, s;
+      do {
+        u = unit_open(&r);
+        v = unit_open(&r);
+        s = u * u + v * v;
+      } while (s >= 1.0 || s == 0.0);
+      const double f = sqrt(-2.0 * log(s) / s) * j->std;
+      j->out[i] = (float)(u * f);
+      if (i + 1 < b) j->out[i + 1] = (float)(v * f);
+    }
+  }
+  return NULL;
+}
+
+int g4s_normal(uint64_t seed, uint64_t stream, float *out, int64_t n, double std, int nthreads) {
+  if (!out || n < 0) return -1;
+  const int64_t chunks = (n + ((int64_t)1 << G4S_CHUNK_SHIFT) - 1) >> G4S_CHUNK_SHIFT;
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > 256) nthreads = 256;
+  if (nthreads > chunks) nthreads = chunks > 0 ? (int)chunks : 1;
+  pthread_t th[256];
+  njob jobs[256];
+  for (int t = 0; t < nthreads; t++) {
+    jobs[t] = (njob){seed, stream, out, n, chunks * t / nthreads, chunks * (t + 1) / nthreads, std};
+  }
+  for (int t = 1; t < nthreads; t++) pthread_create(&th[t], NULL, nworker, &jobs[t]);
+  nworker(&jobs[0]);
+  for (int t = 1; t < nthreads; t++) pthread_join(th[t], NULL);
+  return 0;
+}

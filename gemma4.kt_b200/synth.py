@@ -35,6 +35,19 @@ def normal(rng: np.random.Generator, n: int, std: float = 0.02) -> np.ndarray:
     return x
 
 
+def normal_fast(seed: int, stream: int, n: int, std: float = 0.02, threads: int | None = None) -> np.ndarray:
+    """n N(0, std) float32 values from the C generator of g4_synth.c (xoshiro256**
+    streams per 2^20-value chunk, seeded from (seed, stream, chunk); the result
+    does not depend on the thread count).  For models too large for numpy's
+    single-threaded generator."""
+    out = np.empty(n, dtype=np.float32)
+    rc = synth().g4s_normal(int(seed) & (2**64 - 1), int(stream) & (2**64 - 1), out.ctypes.data_as(C.c_void_p), n,
+                            float(std), threads or os.cpu_count() or 1)
+    if rc != 0:
+        raise ValueError("g4s_normal failed")
+    return out
+
+
 def q8_0_random_blocks(rng: np.random.Generator, n_elems: int) -> np.ndarray:
     """Config-1 blocks: int8 q uniform in [-127, 127], fp16 d = |N(0, 0.02)| / 127."""
     nb = n_elems // 32
@@ -173,6 +186,8 @@ class DecoderSpec:
     expert_type: int = GGMLType.Q4_K
     layer_scale: bool = True
     qk_temperature: bool = True     # q/k norm weights scaled by head_size^-1/4 (see SynthDecoder)
+    fast_rng: bool = False          # matrices from normal_fast (all host threads) instead of numpy
+    replicate_layers: bool = False  # layers > 0 reuse layer 0's matrices (benchmark models: same bytes per layer)
     extra: dict = field(default_factory=dict)
 
     def hs(self, layer: int) -> int:
@@ -186,7 +201,7 @@ class DecoderSpec:
 C4_DENSE = DecoderSpec("C4 dense decoder", n_layers=35, dim=1536, n_heads=8, n_kv_heads=1, head_size=256, ff=6144,
                        vocab=262144)
 C5_MOE = DecoderSpec("C5 MoE decoder", n_layers=30, dim=2816, n_heads=16, n_kv_heads=8, head_size=256, ff=2112,
-                     vocab=262144, n_expert=128, n_expert_used=8, expert_ff=704)
+                     vocab=262144, n_expert=128, n_expert_used=8, expert_ff=704, fast_rng=True)
 
 # special tokens the reference tokenizer and chat format look up
 # (GemmaTokenizer.kt:18-28, GemmaChatFormat.kt:6-13, Llama.kt:18)
@@ -230,6 +245,7 @@ class SynthDecoder:
         self.spec, self.seed = spec, seed
         s = spec
         self._i = 0
+        self._layer0 = {}
         self.tensors = []
         self.threads = threads
         tokens, scores, types = vocabulary(s.vocab)
@@ -316,13 +332,24 @@ class SynthDecoder:
         self.tensors.append((name, (a.size,), GGMLType.F32, a.view(np.uint8)))
 
     def _mat(self, name, t, *dims):
+        if self.spec.replicate_layers and name.startswith("blk."):
+            layer, suffix = name.split(".", 2)[1:]
+            if layer != "0":
+                _, d0, t0, raw0 = self._layer0[suffix]
+                self.tensors.append((name, d0, t0, raw0))
+                return
         n = 1
         for x in dims:
             n *= x
-        rng = self._rng()
-        w = normal(rng, n)
+        if self.spec.fast_rng:
+            w = normal_fast(self.seed, self._i, n, threads=self.threads)
+            self._i += 1
+        else:
+            w = normal(self._rng(), n)
         raw = w.view(np.uint8) if int(t) == GGMLType.F32 else quantize(t, w, self.threads)
         self.tensors.append((name, tuple(dims), GGMLType(int(t)), raw))
+        if self.spec.replicate_layers and name.startswith("blk.0."):
+            self._layer0[name.split(".", 2)[2]] = self.tensors[-1]
 
     def tensor(self, name: str) -> np.ndarray:
         for n, _, _, raw in self.tensors:
