@@ -827,7 +827,20 @@ def profile_mode(args):
     from gemma4_kt_b200 import synth
 
     ctx = g4.Context(0)
-    if args.decode_steps:
+    if args.c5_steps:
+        import dataclasses
+
+        m = synth.SynthDecoder(dataclasses.replace(synth.C5_MOE, replicate_layers=True), seed=4)
+        model = g4.DecoderModel(ctx, g4.TensorSource.from_synth(m))
+        batch = model.new_batch(64, 768)
+        toks = np.full(64, 1000, np.int32)
+        for p in range(args.c5_steps):  # positions 600.. (the cache rows read are whatever they hold)
+            batch.step(toks, np.full(64, 600 + p, np.int32), want_logits=False)
+        torch.cuda.synchronize()
+        print(f"ran {args.c5_steps} C5 batched steps of 64 sequences (positions 600..)")
+        batch.free()
+        model.free()
+    elif args.decode_steps:
         m = synth.SynthDecoder(synth.C4_DENSE, seed=3)
         model = g4.DecoderModel(ctx, g4.TensorSource.from_synth(m))
         st = model.new_state()
@@ -880,13 +893,15 @@ def main():
     ap.add_argument("--decode-only", action="store_true", help="time only the C4 decoder (prints its object)")
     ap.add_argument("--c5-only", action="store_true", help="time only the C5 batched decoder (prints its object)")
     ap.add_argument("--no-c5", action="store_true")
+    ap.add_argument("--c5-steps", type=int, default=0,
+                    help="profiling mode: run this many C5 batched steps (64 sequences) and exit")
     ap.add_argument("--only", default=None,
                     help="profiling mode: run one sweep case FORMAT:ROWSxCOLS (e.g. Q4_K:262144x1536) --reps times")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--moe-only", default=None,
                     help="profiling mode: run the MoE layer --reps times for these token counts (e.g. 1,256)")
     args = ap.parse_args()
-    if args.only or args.moe_only or args.decode_steps:
+    if args.only or args.moe_only or args.decode_steps or args.c5_steps:
         profile_mode(args)
         return
     if args.decode_only:

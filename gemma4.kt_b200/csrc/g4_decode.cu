@@ -48,11 +48,13 @@ constexpr int kMaxKvHeads = 64;      // KV heads per layer
 constexpr size_t kAttnTileBudget = 160 * 1024;  // shared memory for a chunk's K and V rows
 
 // Position chunks of the decoder's attention: at most kAttnMaxChunks per
-// query head, about len / 8 positions each, a multiple of 16, at most ch_max
-// (the shared-memory tile).
+// KV head, about len / target positions each, a multiple of 16, at most
+// ch_max (the shared-memory tile).
 constexpr int kAttnMaxChunks = 128;
-__host__ __device__ __forceinline__ int attn_chunk(int len, int ch_max) {
-  int ch = ((len + 7) / 8 + 15) / 16 * 16;
+constexpr int kAttnMaxHs = 512;     // head size
+constexpr int kAttnMaxGroup = 16;   // query heads per KV head
+__host__ __device__ __forceinline__ int attn_chunk(int len, int ch_max, int target) {
+  int ch = ((len + target - 1) / target + 15) / 16 * 16;
   return ch < 16 ? 16 : ch > ch_max ? ch_max : ch;
 }
 
@@ -83,6 +85,8 @@ struct AttnArgs {
   const int* pos_arr;
   long long qkv_stride, kv_stride, part_stride, out_stride;
   int tick_stride, chunk_stride;
+  int target_chunks;       // chunks per KV head aimed at (attn_chunk)
+  int heads_per_cta;       // query heads of a KV group served by one CTA (divides kv_mul)
 };
 
 // Llama.kt:39-59 per-head rmsnorm, (w * ss) * x left to right (w == nullptr:
@@ -108,42 +112,46 @@ __device__ __forceinline__ void head_rope(float* v, const float* fr, const float
   __syncwarp();
 }
 
-// Attention of one layer (Llama.kt:157-218) for query head hq and position
-// chunk c of this CTA.  The chunk's K and V rows of earlier positions are
-// final before the step starts, so their bulk copies into shared memory (and
-// the RoPE row of the position) are issued before waiting for the q/k/v
-// projection.  Each chunk leaves (max, sum, acc) partials; the last chunk of
-// the head to finish (a ticket counter) combines them into the head's output.
-__global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __grid_constant__ AttnArgs a) {
+// Attention of one layer (Llama.kt:157-218) for KV head g and position chunk
+// c of this CTA: every query head of the group (kv_mul of them, Llama.kt:200)
+// reads the same K and V rows, so the CTA stages the chunk's rows once and
+// serves all of them.  The chunk's rows of earlier positions are final before
+// the step starts, so their bulk copies into shared memory (and the RoPE row
+// of the position) are issued before waiting for the q/k/v projection.  Each
+// (query head, chunk) leaves (max, sum, acc) partials; the group's last chunk
+// to finish (a ticket counter) combines them into the heads' outputs.
+template <int HMAX>  // heads_per_cta <= HMAX
+__global__ void __launch_bounds__(kAttnThreads, HMAX == 1 ? 1 : 3) dec_attention_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smraw[];
-  const int hs = a.hs, half = hs / 2;
+  const int hs = a.hs, half = hs / 2, H = a.heads_per_cta, nsub = a.kv_mul / H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, NW = kAttnThreads / 32;
   // the step's position is staged by the host before the step's first kernel
   const int sq = blockIdx.y;
   const int pos = a.pos_arr ? a.pos_arr[sq] : a.in_pos[*a.step];
   const int start = a.window > 0 ? max(0, pos - a.window + 1) : 0;
   const int len = pos - start + 1;
-  const int ch = attn_chunk(len, a.ch_max);
+  const int ch = attn_chunk(len, a.ch_max, a.target_chunks);
   const int nch = (len + ch - 1) / ch;
-  const int hq = blockIdx.x / a.chunk_stride, c = blockIdx.x % a.chunk_stride;
+  // CTA x index: (KV head g, subset hsub of its query heads, chunk c)
+  const int gs = blockIdx.x / a.chunk_stride, c = blockIdx.x % a.chunk_stride;
+  const int g = gs / nsub, hq0 = g * a.kv_mul + (gs % nsub) * H;  // first query head of this CTA
   const float* qkv = a.qkv + sq * a.qkv_stride;
   float* kc = a.kc + sq * a.kv_stride;
   float* vc = a.vc + sq * a.kv_stride;
   float* part_base = a.part + sq * a.part_stride;
   unsigned* tickets = a.tickets + sq * a.tick_stride;
   float* out = a.out + sq * a.out_stride;
-  const int g = hq / a.kv_mul;
   if (c >= nch) return;
   const int t0 = start + c * ch, t1 = min(t0 + ch, pos + 1), n = t1 - t0;
   float* kt = reinterpret_cast<float*>(smraw);        // [ch_max][hs]
   float* vt = kt + (size_t)a.ch_max * hs;             // [ch_max][hs]
-  float* qs = vt + (size_t)a.ch_max * hs;             // [hs]
-  float* fr = qs + hs;                                // [hs/2] RoPE row of pos
+  float* qs = vt + (size_t)a.ch_max * hs;             // [H][hs]
+  float* fr = qs + (size_t)H * hs;                    // [hs/2] RoPE row of pos
   float* fi = fr + half;
-  float* sc = fi + half;                              // [ch_max] scores, then exp
-  float* wc = sc + a.ch_max;                          // [kAttnMaxChunks] combine weights
-  float* st = wc + kAttnMaxChunks;                    // max, sum, denominator, last flag
-  uint64_t* bar = reinterpret_cast<uint64_t*>(st + 4);
+  float* sc = fi + half;                              // [H][ch_max] scores, then exp
+  float* wc = sc + (size_t)H * a.ch_max;              // [H][kAttnMaxChunks] combine weights
+  float* st = wc + (size_t)H * kAttnMaxChunks;        // [H][4]: max, sum, denominator; [4H] last flag
+  uint64_t* bar = reinterpret_cast<uint64_t*>(st + ((4 * H + 2) & ~1));
 
   // rows t < pos of the chunk: bulk copies before the wait
   const int n_pre = max(0, min(t1, pos) - t0);
@@ -171,10 +179,10 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
   grid_dep_launch();
   float* kp = kt + (size_t)(pos - t0) * hs;  // the row of this position (when has_pos)
   float* vp = vt + (size_t)(pos - t0) * hs;
-  // q of the head (Llama.kt:158-168) and, in the chunk holding the position,
-  // its K/V row: computed (Llama.kt:174-195) or, for a layer that shares an
-  // earlier layer's cache, read from it
-  for (int i = tid; i < hs; i += kAttnThreads) qs[i] = qkv[(size_t)hq * hs + i];
+  // q of the group's heads (Llama.kt:158-168) and, in the chunk holding the
+  // position, its K/V row: computed (Llama.kt:174-195) or, for a layer that
+  // shares an earlier layer's cache, read from it
+  for (int i = tid; i < H * hs; i += kAttnThreads) qs[i] = qkv[(size_t)hq0 * hs + i];
   if (has_pos) {
     const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
@@ -183,20 +191,22 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    head_rmsnorm(qs, a.q_norm, hs, a.eps, lane);
-    head_rope(qs, fr, fi, hs, lane);
-  } else if (has_pos && a.write_kv) {
-    // K: learned norm then RoPE; V: bare norm (Llama.kt:183-195)
-    if (warp == 1) {
-      head_rmsnorm(kp, a.k_norm, hs, a.eps, lane);
-      head_rope(kp, fr, fi, hs, lane);
-    } else if (warp == 2) {
-      head_rmsnorm(vp, nullptr, hs, a.eps, lane);
+  // per warp: query heads, then (own row) K: learned norm and RoPE, V: bare norm (Llama.kt:183-195)
+  for (int j = warp; j < H + 2; j += NW) {
+    if (j < H) {
+      head_rmsnorm(qs + (size_t)j * hs, a.q_norm, hs, a.eps, lane);
+      head_rope(qs + (size_t)j * hs, fr, fi, hs, lane);
+    } else if (has_pos && a.write_kv) {
+      if (j == H) {
+        head_rmsnorm(kp, a.k_norm, hs, a.eps, lane);
+        head_rope(kp, fr, fi, hs, lane);
+      } else {
+        head_rmsnorm(vp, nullptr, hs, a.eps, lane);
+      }
     }
   }
   __syncthreads();
-  if (has_pos && a.write_kv && hq % a.kv_mul == 0) {
+  if (has_pos && a.write_kv && gs % nsub == 0) {
     const size_t row = (size_t)pos * a.kvdim + (size_t)g * hs;
     for (int i = tid; i < hs; i += kAttnThreads) {
       kc[row + i] = kp[i];
@@ -210,98 +220,136 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const __gri
     return;
   }
 
-  // scores q . k_t (Llama.kt:204-208)
-  for (int j = warp; j < n; j += NW) {
-    const float* kr = kt + (size_t)j * hs;
-    float acc = 0.f;
-    for (int i = lane; i < hs; i += 32) acc = fmaf(qs[i], kr[i], acc);
-    acc = warp_sum(acc);
-    if (lane == 0) sc[j] = acc;
+  // scores q_j . k_t (Llama.kt:204-208): a warp per position, the K row in
+  // registers, every head of the group against it
+  for (int p = warp; p < n; p += NW) {
+    const float* kr = kt + (size_t)p * hs;
+    float kreg[kAttnMaxHs / 32];
+#pragma unroll
+    for (int u = 0; u < kAttnMaxHs / 32; ++u) kreg[u] = lane + 32 * u < hs ? kr[lane + 32 * u] : 0.f;
+    for (int j = 0; j < H; ++j) {
+      const float* qj = qs + (size_t)j * hs;
+      float acc = 0.f;
+#pragma unroll
+      for (int u = 0; u < kAttnMaxHs / 32; ++u)
+        if (lane + 32 * u < hs) acc = fmaf(qj[lane + 32 * u], kreg[u], acc);
+      acc = warp_sum(acc);
+      if (lane == 0) sc[(size_t)j * a.ch_max + p] = acc;
+    }
   }
   __syncthreads();
-  // chunk softmax statistics: exp((s - m) as double), as softmaxInPlace (MutableFloatTensor.kt:54-59)
-  if (warp == 0) {
+  // chunk softmax statistics per head: exp((s - m) as double), as softmaxInPlace (MutableFloatTensor.kt:54-59)
+  for (int j = warp; j < H; j += NW) {
+    float* sj = sc + (size_t)j * a.ch_max;
     float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[j]);
+    for (int p = lane; p < n; p += 32) m = fmaxf(m, sj[p]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const float e = (float)exp((double)__fsub_rn(sc[j], m));
-      sc[j] = e;
+    for (int p = lane; p < n; p += 32) {
+      const float e = (float)exp((double)__fsub_rn(sj[p], m));
+      sj[p] = e;
       l += e;
     }
     l = warp_sum(l);
     if (lane == 0) {
-      st[0] = m;
-      st[1] = l;
+      st[4 * j] = m;
+      st[4 * j + 1] = l;
     }
   }
   __syncthreads();
-  // partial V sums (Llama.kt:211-217)
-  float* part = part_base + ((size_t)hq * kAttnMaxChunks + c) * (hs + 2);
+  // partial V sums per head (Llama.kt:211-217): each V element read once for all heads
   for (int d = tid; d < hs; d += kAttnThreads) {
-    float acc = 0.f;
-    for (int j = 0; j < n; ++j) acc = fmaf(sc[j], vt[(size_t)j * hs + d], acc);
-    part[2 + d] = acc;
+    float acc[HMAX];
+#pragma unroll
+    for (int j = 0; j < HMAX; ++j) acc[j] = 0.f;
+    for (int p = 0; p < n; ++p) {
+      const float v = vt[(size_t)p * hs + d];
+#pragma unroll
+      for (int j = 0; j < HMAX; ++j)
+        if (j < H) acc[j] = fmaf(sc[(size_t)j * a.ch_max + p], v, acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < HMAX; ++j)
+      if (j < H) part_base[((size_t)(hq0 + j) * kAttnMaxChunks + c) * (hs + 2) + 2 + d] = acc[j];
   }
-  if (tid == 0) {
-    part[0] = st[0];
-    part[1] = st[1];
+  if (tid < H) {
+    float* pj = part_base + ((size_t)(hq0 + tid) * kAttnMaxChunks + c) * (hs + 2);
+    pj[0] = st[4 * tid];
+    pj[1] = st[4 * tid + 1];
   }
-  // the head's last chunk to finish combines the partials (release: fence, then the ticket)
+  // the group's last chunk to finish combines the partials (release: fence, then the ticket)
   __syncthreads();
   if (tid == 0) {
     __threadfence();
-    const unsigned done = atomicAdd(tickets + hq, 1u);
-    st[3] = done + 1 == (unsigned)nch ? 1.f : 0.f;
+    const unsigned done = atomicAdd(tickets + gs, 1u);
+    st[4 * H] = done + 1 == (unsigned)nch ? 1.f : 0.f;
   }
   __syncthreads();
-  if (st[3] == 0.f) return;
+  if (st[4 * H] == 0.f) return;
   __threadfence();  // acquire: the other chunks' partials are visible
-  const float* ph = part_base + (size_t)hq * kAttnMaxChunks * (hs + 2);
-  // out = sum_c w_c acc_c / sum_c w_c l_c, w_c = exp(m_c - max m) (Llama.kt:201-218 over the chunks)
-  if (warp == 0) {
+  // out_j = sum_c w_c acc_c / sum_c w_c l_c, w_c = exp(m_c - max m) (Llama.kt:201-218 over the chunks)
+  for (int j = warp; j < H; j += NW) {
+    const float* ph = part_base + (size_t)(hq0 + j) * kAttnMaxChunks * (hs + 2);
+    float* wj = wc + (size_t)j * kAttnMaxChunks;
     float mc[kAttnMaxChunks / 32], lc[kAttnMaxChunks / 32];
 #pragma unroll
-    for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
-      const int k = lane + 32 * j;
-      mc[j] = k < nch ? __ldcg(ph + (size_t)k * (hs + 2)) : -INFINITY;
-      lc[j] = k < nch ? __ldcg(ph + (size_t)k * (hs + 2) + 1) : 0.f;
+    for (int u = 0; u < kAttnMaxChunks / 32; ++u) {
+      const int k = lane + 32 * u;
+      mc[u] = k < nch ? __ldcg(ph + (size_t)k * (hs + 2)) : -INFINITY;
+      lc[u] = k < nch ? __ldcg(ph + (size_t)k * (hs + 2) + 1) : 0.f;
     }
     float M = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kAttnMaxChunks / 32; ++j) M = fmaxf(M, mc[j]);
+    for (int u = 0; u < kAttnMaxChunks / 32; ++u) M = fmaxf(M, mc[u]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float dsum = 0.f;
 #pragma unroll
-    for (int j = 0; j < kAttnMaxChunks / 32; ++j) {
-      const int k = lane + 32 * j;
+    for (int u = 0; u < kAttnMaxChunks / 32; ++u) {
+      const int k = lane + 32 * u;
       if (k < nch) {
-        const float w = (float)exp((double)__fsub_rn(mc[j], M));
-        wc[k] = w;
-        dsum = fmaf(w, lc[j], dsum);
+        const float w = (float)exp((double)__fsub_rn(mc[u], M));
+        wj[k] = w;
+        dsum = fmaf(w, lc[u], dsum);
       }
     }
     dsum = warp_sum(dsum);
-    if (lane == 0) st[2] = dsum;
+    if (lane == 0) st[4 * j + 2] = dsum;
   }
   __syncthreads();
-  constexpr int kCh = 8;  // chunk loads issued together
-  for (int d = tid; d < hs; d += kAttnThreads) {
-    float num = 0.f;
+  // every output of this thread (up to kEl) and kCh chunks per round: one
+  // round of memory latency for up to kCh chunks
+  constexpr int kCh = 8, kEl = HMAX < 4 ? HMAX : 4;
+  for (int e0 = tid; e0 < H * hs; e0 += kEl * kAttnThreads) {
+    float num[kEl];
+#pragma unroll
+    for (int i = 0; i < kEl; ++i) num[i] = 0.f;
     for (int k0 = 0; k0 < nch; k0 += kCh) {
-      float v[kCh];
+      float v[kEl][kCh];
 #pragma unroll
-      for (int j = 0; j < kCh; ++j) v[j] = k0 + j < nch ? __ldcg(ph + (size_t)(k0 + j) * (hs + 2) + 2 + d) : 0.f;
+      for (int i = 0; i < kEl; ++i) {
+        const int e = e0 + i * kAttnThreads, j = e / hs, d = e - j * hs;
+        const float* ph = part_base + (size_t)(hq0 + j) * kAttnMaxChunks * (hs + 2) + 2 + d;
 #pragma unroll
-      for (int j = 0; j < kCh; ++j)
-        if (k0 + j < nch) num = fmaf(wc[k0 + j], v[j], num);
+        for (int u = 0; u < kCh; ++u)
+          v[i][u] = (e < H * hs && k0 + u < nch) ? __ldcg(ph + (size_t)(k0 + u) * (hs + 2)) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < kEl; ++i) {
+        const int e = e0 + i * kAttnThreads, j = e / hs;
+#pragma unroll
+        for (int u = 0; u < kCh; ++u)
+          if (e < H * hs && k0 + u < nch) num[i] = fmaf(wc[(size_t)j * kAttnMaxChunks + k0 + u], v[i][u], num[i]);
+      }
     }
-    out[(size_t)hq * hs + d] = __fdiv_rn(num, st[2]);
+#pragma unroll
+    for (int i = 0; i < kEl; ++i) {
+      const int e = e0 + i * kAttnThreads, j = e / hs, d = e - j * hs;
+      if (e < H * hs) out[(size_t)(hq0 + j) * hs + d] = __fdiv_rn(num[i], st[4 * j + 2]);
+    }
   }
-  if (tid == 0) tickets[hq] = 0u;  // every chunk has arrived: ready for the next launch
+  if (tid == 0) tickets[gs] = 0u;  // every chunk has arrived: ready for the next launch
 }
 
 // Greedy sampling (Sampler.ARGMAX, FloatTensor.argmax): the logits GEMV left
@@ -692,6 +740,11 @@ extern "C" int g4_model_finalize(g4_model* m) {
       c->set_err("g4_model_finalize: layer %d has no KV source layer", l);
       return G4_E_ARG;
     }
+    if (L.hs > kAttnMaxHs || L.hs % 4 || k.n_heads / L.n_kv > kAttnMaxGroup) {
+      c->set_err("g4_model_finalize: layer %d: head size %d (at most %d, a multiple of 4) or %d query heads per "
+                 "KV head (at most %d) not supported", l, L.hs, kAttnMaxHs, k.n_heads / L.n_kv, kAttnMaxGroup);
+      return G4_E_ARG;
+    }
     L.scale = m->layer_scale[l];
     const bool own_kv = l < k.n_layer_kv_from_start;
     if (!need(p + "attn_norm.weight", G4_TYPE_F32, dim) || !need(p + "attn_q_norm.weight", G4_TYPE_F32, L.hs) ||
@@ -917,12 +970,21 @@ extern "C" int g4_state_free(g4_state* s) {
   return 0;
 }
 
+// The attention kernel compiled for at least `heads` query heads per CTA.
+using AttnFn = void (*)(const AttnArgs);
+static AttnFn attn_fn(int heads) {
+  return heads <= 1 ? dec_attention_kernel<1> : heads <= 2 ? dec_attention_kernel<2> : heads <= 4 ? dec_attention_kernel<4>
+       : heads <= 8 ? dec_attention_kernel<8> : dec_attention_kernel<16>;
+}
+
 // Positions per attention chunk that fit kAttnTileBudget (K and V rows), a multiple of 16.
 static int attn_ch_max(int hs) { return (int)std::min<size_t>(256, kAttnTileBudget / ((size_t)hs * 8) / 16 * 16); }
-// K and V tiles, q, the RoPE row, scores, combine weights, 4 statistics, the mbarrier
-static size_t attn_smem(int hs) {
-  const size_t ch = (size_t)attn_ch_max(hs);
-  return ((2 * ch * hs + 2 * (size_t)hs + ch + kAttnMaxChunks + 4) * 4 + 7) / 8 * 8 + 8;
+// K and V tiles, the group's q rows, the RoPE row, scores and combine weights
+// per head, 4 statistics per head and a flag, the mbarrier
+static size_t attn_smem(int hs, int group, int ch_max) {
+  const size_t ch = (size_t)ch_max, H = (size_t)group;
+  return ((2 * ch * hs + H * hs + (size_t)hs + H * ch + H * kAttnMaxChunks + ((4 * H + 2) & ~(size_t)1)) * 4 + 7) /
+             8 * 8 + 8;
 }
 
 template <typename... KArgs, typename... Args>
@@ -1037,11 +1099,14 @@ static int enqueue_step(g4_state* s) {
     aa.ch_max = attn_ch_max(L.hs);
     aa.status = c->status;
     aa.chunk_stride = kAttnMaxChunks;
-    const size_t asmem = attn_smem(L.hs);
-    if (asmem > 48 * 1024 &&
-        cudaFuncSetAttribute(dec_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem))
+    aa.target_chunks = 8;
+    aa.heads_per_cta = 1;  // one sequence: a CTA per (query head, chunk) keeps the grid wide
+    const size_t asmem = attn_smem(L.hs, aa.heads_per_cta, aa.ch_max);
+    // the attribute is a cap shared by every user of the kernel (single and batched decode): the device's limit
+    if (asmem > (size_t)c->dev.smem_optin ||
+        cudaFuncSetAttribute(attn_fn(1), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->dev.smem_optin))
       return c->cuda_fail(cudaGetLastError(), "decode: attention set-up");
-    cudaError_t ce = launch_pdl_k(dec_attention_kernel, k.n_heads * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
+    cudaError_t ce = launch_pdl_k(attn_fn(1), k.n_heads * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
     if (ce) return c->cuda_fail(ce, "decode: attention");
     // ---- output projection of the attention output
     e = launch_proj(L.m_wo, L.k_wo, L.d_wo, L.p_wo, L.wo, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);
@@ -1279,6 +1344,11 @@ struct g4_batch {
 
 extern "C" int g4_batch_free(g4_batch* b);
 
+// Batched attention: chunks of at most 32 positions, so that a few CTAs (their
+// K/V tiles) are resident per SM while the sequences fill the grid.
+static int batch_ch_max(int hs) { return std::min(32, attn_ch_max(hs)); }
+
+
 // The Q8_0 projections of every layer and the output matrix in the tile layout
 // of the tensor-core GEMMs (kept by the model; the single-sequence decoder uses
 // the layer copies only when it planned them itself).
@@ -1393,12 +1463,13 @@ extern "C" int g4_batch_create(g4_model* m, int n_max, int max_positions, g4_bat
   p += (N * 8 + 255) / 256 * 256;
   b->tickets = reinterpret_cast<unsigned*>(p);
   // attention kernel set-up, and the MoE layers' work buffers at the widest batch
-  size_t asmem = 0;
-  for (const LayerDev& L : m->L) asmem = std::max(asmem, attn_smem(L.hs));
-  if (asmem > 48 * 1024 &&
-      cudaFuncSetAttribute(dec_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem)) {
-    g4_batch_free(b);
-    return c->cuda_fail(cudaGetLastError(), "g4_batch_create: attention set-up");
+  for (const LayerDev& L : m->L) {
+    const int grp = k.n_heads / L.n_kv;
+    if (attn_smem(L.hs, grp, batch_ch_max(L.hs)) > (size_t)c->dev.smem_optin ||
+        cudaFuncSetAttribute(attn_fn(grp), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->dev.smem_optin)) {
+      g4_batch_free(b);
+      return c->cuda_fail(cudaGetLastError(), "g4_batch_create: attention set-up");
+    }
   }
   if (k.n_expert > 0) {
     int r = g4_moe_layer(c, &m->L[0].moe, b->x[0], b->moe_out, n_max, nullptr, nullptr, b->st);
@@ -1530,7 +1601,7 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
     aa.part = b->part;
     aa.tickets = b->tickets;
     aa.out = b->xbk;
-    aa.ch_max = attn_ch_max(L.hs);
+    aa.ch_max = batch_ch_max(L.hs);
     aa.status = c->status;
     aa.pos_arr = b->d_pos;
     aa.qkv_stride = qkv_n;
@@ -1538,16 +1609,18 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
     aa.part_stride = (long long)b->part_stride;
     aa.out_stride = L.qdim;
     aa.tick_stride = k.n_heads;
+    aa.target_chunks = 8;  // the sequences give the grid its width
+    aa.heads_per_cta = aa.kv_mul;  // K/V rows staged once for the whole group
     int nch_max = 1;
     for (int i = 0; i < n; ++i) {
       const int pos = positions[i];
       const int start = aa.window > 0 ? std::max(0, pos - aa.window + 1) : 0;
       const int len = pos - start + 1;
-      const int ch = attn_chunk(len, aa.ch_max);
+      const int ch = attn_chunk(len, aa.ch_max, aa.target_chunks);
       nch_max = std::max(nch_max, (len + ch - 1) / ch);
     }
     aa.chunk_stride = nch_max;
-    dec_attention_kernel<<<dim3(k.n_heads * nch_max, n), kAttnThreads, attn_smem(L.hs), st>>>(aa);
+    attn_fn(aa.kv_mul)<<<dim3(L.n_kv * nch_max, n), kAttnThreads, attn_smem(L.hs, aa.kv_mul, aa.ch_max), st>>>(aa);
     if (cudaError_t e = cudaGetLastError()) return c->cuda_fail(e, "batch: attention");
     // ---- output projection
     GemvFuse plain;
