@@ -1329,6 +1329,8 @@ struct g4_batch {
   unsigned long long* keys = nullptr;
   int *d_tok = nullptr, *d_pos = nullptr;
   unsigned* tickets = nullptr;
+  float* gemm_part = nullptr;   // split-K partial sums of the batched GEMMs
+  unsigned* gemm_tickets = nullptr;
   int* h_io = nullptr;          // pinned: tokens [n_max], positions [n_max]
   unsigned long long* h_keys = nullptr;  // pinned [n_max]
   std::map<std::tuple<int, int, int>, MmaBatchPlan> plans;
@@ -1462,6 +1464,33 @@ extern "C" int g4_batch_create(g4_model* m, int n_max, int max_positions, g4_bat
   b->d_pos = reinterpret_cast<int*>(p);
   p += (N * 8 + 255) / 256 * 256;
   b->tickets = reinterpret_cast<unsigned*>(p);
+  // split-K scratch of the batched GEMMs (plans at the widest batch)
+  size_t part_floats = 0;
+  int max_nrb = 0;
+  auto need = [&](int rows, int cols) -> bool {
+    const MmaBatchPlan* p = b->plan(rows, cols, n_max);
+    if (!p) return false;
+    part_floats = std::max(part_floats, mma_batch_partials(*p, n_max));
+    max_nrb = std::max(max_nrb, p->nrb);
+    return true;
+  };
+  bool ok = need(k.vocab, (int)dim);
+  for (const LayerDev& L : m->L)
+    ok = ok && need((int)(L.qkv->n_elems / dim), (int)dim) && need((int)dim, L.qdim) && need(2 * L.ff, (int)dim) &&
+         need((int)dim, L.ff);
+  if (!ok) {
+    g4_batch_free(b);
+    c->set_err("g4_batch_create: no batched GEMM plan for the model's projections");
+    return G4_E_DEVICE;
+  }
+  if (cudaMalloc(&b->gemm_part, part_floats * 4 + (size_t)max_nrb * 4 + 256) != cudaSuccess) {
+    cudaGetLastError();
+    g4_batch_free(b);
+    c->set_err("g4_batch_create: cannot allocate the GEMM partial sums");
+    return G4_E_NOMEM;
+  }
+  b->gemm_tickets = reinterpret_cast<unsigned*>(b->gemm_part + (part_floats + 63) / 64 * 64);
+  cudaMemset(b->gemm_tickets, 0, (size_t)max_nrb * 4);
   // attention kernel set-up, and the MoE layers' work buffers at the widest batch
   for (const LayerDev& L : m->L) {
     const int grp = k.n_heads / L.n_kv;
@@ -1493,6 +1522,7 @@ extern "C" int g4_batch_free(g4_batch* b) {
   if (b->st) cudaStreamSynchronize(b->st);
   if (b->buf) cudaFree(b->buf);
   if (b->small) cudaFree(b->small);
+  if (b->gemm_part) cudaFree(b->gemm_part);
   if (b->h_io) cudaFreeHost(b->h_io);
   if (b->h_keys) cudaFreeHost(b->h_keys);
   if (b->st) cudaStreamDestroy(b->st);
@@ -1509,7 +1539,8 @@ static int batch_gemm(g4_batch* b, const uint8_t* packed, int rows, int cols, in
     c->set_err("g4_batch_step: no GEMM plan for %s (%d x %d)", what, rows, cols);
     return G4_E_DEVICE;
   }
-  const int e = launch_gemm_mma_batch(*p, packed, b->lim, b->lsc, n, y, ldy, out_mode, softcap, keys, b->st);
+  const int e = launch_gemm_mma_batch(*p, packed, b->lim, b->lsc, n, y, ldy, out_mode, softcap, keys, b->gemm_part,
+                                      b->gemm_tickets, b->st);
   return e ? c->cuda_fail((cudaError_t)e, what) : 0;
 }
 

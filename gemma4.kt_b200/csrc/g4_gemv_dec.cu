@@ -48,15 +48,6 @@ __device__ __forceinline__ float round_small(float x, int& i) {
   return __fsub_rn(t, kMagic);
 }
 
-// 16-byte global -> shared copy (cp.async, L2 only); completion by commit groups.
-__device__ __forceinline__ void cp16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // Units a block is decoded in (one lane each).
 template <int FMT>

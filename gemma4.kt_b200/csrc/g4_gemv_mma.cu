@@ -429,107 +429,207 @@ struct MmaBatchArgs {
   int T, ldy, out_mode;
   float softcap;
   unsigned long long* argmax;  // OUT_SOFTCAP_ARGMAX: [T] keys (atomicMax)
+  float* part;          // [splits][T][nrb * 128] partial sums (splits > 1)
+  unsigned* tickets;    // [nrb] splits finished per row block
 };
 
-// Y[t][row] = W[row] . x_t for T tokens on the repacked tiles: a warp takes a
-// row tile and its share of the blocks (K) and, per block, one mma per limb
-// and group of 8 tokens (the tokens are the B operand's 8 columns).  The ks
-// warps of a row tile meet in shared memory; the epilogue runs a warp per
-// token (plain, gelu(gate) * up on interleaved rows, or softcap + arg-max).
+constexpr int kBatchKc = 4;      // blocks (32 columns) per staged chunk of the activations
+constexpr int kBatchRow = 112;   // bytes per token in a staged block: 96 limb bytes + 16 (bank spread)
+constexpr int kBatchRt = 8;      // row tiles per row block (a warp each)
+
+// One output of the batched GEMM: plain, gelu(gate) * up (value of the even
+// row, `up` its odd neighbour), or softcap with the token's arg-max key.
+__device__ __forceinline__ void batch_out(const MmaBatchArgs& a, int row, int tk, float v, float up,
+                                          unsigned long long& best) {
+  if (a.out_mode == OUT_GELU_PAIR) {
+    if (!(row & 1)) a.y[(size_t)tk * a.ldy + (row >> 1)] = __fmul_rn(gelu_ref(v), up);
+  } else if (a.out_mode == OUT_SOFTCAP_ARGMAX) {
+    const float c = softcap_ref(v, a.softcap);
+    a.y[(size_t)tk * a.ldy + row] = c;
+    const unsigned long long key = argmax_key(c, row);
+    best = key > best ? key : best;
+  } else {
+    a.y[(size_t)tk * a.ldy + row] = v;
+  }
+}
+
+// Y[t][row] = W[row] . x_t for T tokens on the repacked tiles.  A CTA task is
+// a row block (kBatchRt row tiles, a warp each) x one of `splits` K ranges;
+// per block of 32 columns a warp runs one mma per limb and group of 8 tokens
+// (the group's tokens are the B operand's columns), its next weight tile in
+// flight.  The tokens' limbs travel through shared memory in chunks of
+// kBatchKc blocks (cp.async, two stages) that the CTA's warps share.  With
+// one split the warps finish their outputs directly; otherwise each split
+// stores its partial sums, and the row block's last split to finish (a ticket
+// counter) adds them in split order and finishes the outputs.
 template <int NG>
 __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const __grid_constant__ MmaBatchArgs a) {
-  extern __shared__ __align__(16) float red[];  // [8 warps][16 rows][RS]
-  constexpr int TT = 8 * NG, RS = TT + 1;
+  // [2][kBatchKc][8 NG][kBatchRow] limbs, [2][kBatchKc][8 NG] scales, [8 NG] arg-max keys, the last-split flag
+  extern __shared__ __align__(16) uint8_t bsm[];
+  constexpr int TT = 8 * NG;
+  constexpr int kStage = kBatchKc * TT * kBatchRow;
+  float* ssc = reinterpret_cast<float*>(bsm + 2 * kStage);
+  unsigned long long* sbest = reinterpret_cast<unsigned long long*>(ssc + 2 * kBatchKc * TT);
+  int& s_last = *reinterpret_cast<int*>(sbest + TT);
   const MmaBatchPlan& p = a.p;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int sub = warp / p.ks, kw = warp % p.ks;
-  const int kb0 = kw * p.kpw, kb1 = min(p.nkb, kb0 + p.kpw);
-  const int T = a.T;
+  const int T = a.T, nkb = p.nkb;
   constexpr float kInv1 = 1.0f / 254.0f, kInv2 = 1.0f / 64516.0f;
+  unsigned long long best[NG][2];
+#pragma unroll
+  for (int G = 0; G < NG; ++G) best[G][0] = best[G][1] = 0ull;
+  if (a.out_mode == OUT_SOFTCAP_ARGMAX)
+    for (int i = threadIdx.x; i < TT; i += blockDim.x) sbest[i] = 0ull;
+
+  auto stage = [&](int kb0, int kb_end, int b) {
+    uint8_t* dst = bsm + b * kStage;
+    for (int i = threadIdx.x; i < kBatchKc * T * 6; i += blockDim.x) {
+      const int piece = i % 6, r = i / 6, tok = r % T, kk = r / T, kb = kb0 + kk;
+      if (kb < kb_end)
+        cp16(dst + (kk * TT + tok) * kBatchRow + 16 * piece, a.lim + ((size_t)tok * nkb + kb) * 96 + 16 * piece);
+    }
+    for (int i = threadIdx.x; i < kBatchKc * T; i += blockDim.x) {
+      const int tok = i % T, kk = i / T, kb = kb0 + kk;
+      if (kb < kb_end) ssc[(b * kBatchKc + kk) * TT + tok] = __ldcg(a.lsc + (size_t)tok * nkb + kb);
+    }
+    cp_commit();
+  };
+
   for (int task = blockIdx.x; task < p.ntasks; task += gridDim.x) {
-    const int rt = task * p.tiles + sub;
+    const int rb = task / p.splits, sp = task % p.splits;
+    const int rt = rb * kBatchRt + warp;
+    const bool ract = rt < p.nrt;
+    const int kb_beg = sp * p.kps, kb_end = min(nkb, kb_beg + p.kps);
+    const int nch = (kb_end - kb_beg + kBatchKc - 1) / kBatchKc;
     float acc[NG][4];
 #pragma unroll
     for (int G = 0; G < NG; ++G) acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.f;
-    if (rt < p.nrt) {
-      for (int kb = kb0; kb < kb1; ++kb) {
-        const size_t tile = (size_t)rt * p.nkb + kb;
-        const uint4 A = __ldg(a.q + tile * 32 + lane);
-        const uint32_t S = __ldg(a.sc + tile * 8 + g);
-        const float d0 = f16_bits_to_f32((uint16_t)(S & 0xFFFFu)), d8 = f16_bits_to_f32((uint16_t)(S >> 16));
+    const uint4* qt = a.q + (size_t)rt * nkb * 32 + lane;
+    const uint32_t* st = a.sc + (size_t)rt * nkb * 8 + g;
+    uint4 An = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t Sn = 0u;
+    if (ract && kb_beg < kb_end) {
+      An = __ldg(qt + (size_t)kb_beg * 32);
+      Sn = __ldg(st + (size_t)kb_beg * 8);
+    }
+    if (nch > 0) stage(kb_beg, kb_end, 0);
+    for (int ch = 0; ch < nch; ++ch) {
+      if (ch + 1 < nch) {
+        stage(kb_beg + (ch + 1) * kBatchKc, kb_end, (ch + 1) & 1);
+        cp_wait<1>();
+      } else {
+        cp_wait<0>();
+      }
+      __syncthreads();  // chunk ch is in shared memory for every warp
+      const uint8_t* bsrc = bsm + (ch & 1) * kStage;
+      const float* scs = ssc + (ch & 1) * kBatchKc * TT;
+      const int kn = min(kBatchKc, kb_end - kb_beg - ch * kBatchKc);
+      for (int kk = 0; kk < kn; ++kk) {
+        const int kb = kb_beg + ch * kBatchKc + kk;
+        const uint4 A = An;
+        const uint32_t S = Sn;
+        if (ract && kb + 1 < kb_end) {  // the next weight tile in flight
+          An = __ldg(qt + (size_t)(kb + 1) * 32);
+          Sn = __ldg(st + (size_t)(kb + 1) * 8);
+        }
+        if (ract) {
+          const float d0 = f16_bits_to_f32((uint16_t)(S & 0xFFFFu)), d8 = f16_bits_to_f32((uint16_t)(S >> 16));
+#pragma unroll
+          for (int G = 0; G < NG; ++G) {
+            if (G * 8 < T) {  // uniform
+              const uint32_t* bp =
+                  reinterpret_cast<const uint32_t*>(bsrc + (kk * TT + G * 8 + g) * kBatchRow + 4 * t);
+              int dh[4], dm[4], dl[4];
+              mma_s8(dh, A, bp[0], bp[4]);
+              mma_s8(dm, A, bp[8], bp[12]);
+              mma_s8(dl, A, bp[16], bp[20]);
+              const float s0 = scs[kk * TT + G * 8 + 2 * t], s1 = scs[kk * TT + G * 8 + 2 * t + 1];
+              const float sc[4] = {d0 * s0, d0 * s1, d8 * s0, d8 * s1};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float v = fmaf(small_i2f(dl[i]), kInv2, fmaf(small_i2f(dm[i]), kInv1, small_i2f(dh[i])));
+                acc[G][i] = fmaf(v, sc[i], acc[G][i]);
+              }
+            }
+          }
+        }
+      }
+      __syncthreads();  // buffer (ch & 1) is free for chunk ch + 2
+    }
+    // lane: rows r0 = rt*16 + g and r0 + 8; tokens G*8 + 2t and G*8 + 2t + 1
+    const int r0 = rt * 16 + g;
+    if (p.splits == 1) {
+      if (ract) {
 #pragma unroll
         for (int G = 0; G < NG; ++G) {
-          if (G * 8 < T) {  // uniform over the warp
-            const int tb = G * 8 + g;  // this lane's B column (token)
-            uint32_t b[6] = {0u, 0u, 0u, 0u, 0u, 0u};
-            if (tb < T) {
-              const uint32_t* lp = reinterpret_cast<const uint32_t*>(a.lim + ((size_t)tb * p.nkb + kb) * 96 + 4 * t);
+          if (G * 8 < T) {
+            float o[4];
 #pragma unroll
-              for (int j = 0; j < 6; ++j) b[j] = __ldg(lp + 4 * j);  // limb j/2, K half j%2
-            }
-            int dh[4], dm[4], dl[4];
-            mma_s8(dh, A, b[0], b[1]);
-            mma_s8(dm, A, b[2], b[3]);
-            mma_s8(dl, A, b[4], b[5]);
-            const int t0 = G * 8 + 2 * t;  // tokens of this lane's D columns: t0, t0 + 1
-            const float s0 = t0 < T ? __ldg(a.lsc + (size_t)t0 * p.nkb + kb) : 0.f;
-            const float s1 = t0 + 1 < T ? __ldg(a.lsc + (size_t)(t0 + 1) * p.nkb + kb) : 0.f;
-            const float sc[4] = {d0 * s0, d0 * s1, d8 * s0, d8 * s1};
+            for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, acc[G][i], 4);  // row g ^ 1
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const float v = fmaf(small_i2f(dl[i]), kInv2, fmaf(small_i2f(dm[i]), kInv1, small_i2f(dh[i])));
-              acc[G][i] = fmaf(v, sc[i], acc[G][i]);
+              const int row = r0 + 8 * (i >> 1), tk = G * 8 + 2 * t + (i & 1);
+              if (row < p.rows && tk < T) batch_out(a, row, tk, acc[G][i], o[i], best[G][i & 1]);
             }
           }
         }
       }
+      continue;
     }
-    // partial sums of this warp: rows g, g + 8 of its tile, tokens G*8 + 2t (+1)
+    // split-K: partial sums of this split, then the row block's last split finishes
+    float* pp = a.part + (size_t)sp * T * (p.nrb * 128);
+    if (ract) {
 #pragma unroll
-    for (int G = 0; G < NG; ++G) {
-      const int tk = G * 8 + 2 * t;
-      red[(warp * 16 + g) * RS + tk] = acc[G][0];
-      red[(warp * 16 + g) * RS + tk + 1] = acc[G][1];
-      red[(warp * 16 + g + 8) * RS + tk] = acc[G][2];
-      red[(warp * 16 + g + 8) * RS + tk + 1] = acc[G][3];
+      for (int G = 0; G < NG; ++G) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = r0 + 8 * (i >> 1), tk = G * 8 + 2 * t + (i & 1);
+          if (tk < T) pp[(size_t)tk * (p.nrb * 128) + row] = acc[G][i];
+        }
+      }
     }
     __syncthreads();
-    const int erows = p.tiles * 16;  // 16, 32, 64 or 128
-    const unsigned emask = erows >= 32 ? 0xffffffffu : 0x0000ffffu;
-    for (int tk = warp; tk < T; tk += kMmaWarps) {
-      unsigned long long best = 0ull;
-      if (lane < erows) {
-        for (int r = lane; r < erows; r += 32) {
-          const int sr = r >> 4, rr = r & 15;
-          float sum = 0.f;
-          for (int w = 0; w < p.ks; ++w) sum += red[((sr * p.ks + w) * 16 + rr) * RS + tk];
-          const int row = (task * p.tiles + sr) * 16 + rr;
-          const bool ok = row < p.rows;
-          float* yt = a.y + (size_t)tk * a.ldy;
-          if (a.out_mode == OUT_GELU_PAIR) {
-            const float up = __shfl_xor_sync(emask, sum, 1);
-            if (ok && !(row & 1)) yt[row >> 1] = __fmul_rn(gelu_ref(sum), up);
-          } else if (a.out_mode == OUT_SOFTCAP_ARGMAX) {
-            if (ok) {
-              const float c = softcap_ref(sum, a.softcap);
-              yt[row] = c;
-              const unsigned long long key = argmax_key(c, row);
-              best = key > best ? key : best;
-            }
-          } else if (ok) {
-            yt[row] = sum;
-          }
-        }
-        if (a.out_mode == OUT_SOFTCAP_ARGMAX) {
-          for (int o = erows >= 32 ? 16 : 8; o > 0; o >>= 1) {
-            const unsigned long long v = __shfl_xor_sync(emask, best, o);
-            best = v > best ? v : best;
-          }
-          if (lane == 0 && best) atomicMax(a.argmax + tk, best);
-        }
-      }
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_last = atomicAdd(a.tickets + rb, 1u) + 1 == (unsigned)p.splits;
     }
-    __syncthreads();  // red is rewritten by the next task
+    __syncthreads();
+    if (!s_last) continue;
+    __threadfence();  // acquire: the other splits' partials are visible
+    // thread -> (token, row pair) of the row block; sums in split order
+    for (int e = threadIdx.x; e < T * 64; e += blockDim.x) {
+      const int tk = e / 64, row = rb * 128 + 2 * (e % 64);
+      float v0 = 0.f, v1 = 0.f;
+      for (int s2 = 0; s2 < p.splits; ++s2) {
+        const float* q2 = a.part + ((size_t)s2 * T + tk) * (p.nrb * 128) + row;
+        v0 += __ldcg(q2);
+        v1 += __ldcg(q2 + 1);
+      }
+      unsigned long long bb = 0ull;
+      if (row < p.rows) batch_out(a, row, tk, v0, v1, bb);
+      if (row + 1 < p.rows && a.out_mode != OUT_GELU_PAIR) batch_out(a, row + 1, tk, v1, 0.f, bb);
+      if (bb) atomicMax(&sbest[tk], bb);
+    }
+    if (threadIdx.x == 0) a.tickets[rb] = 0u;  // ready for the next launch
+  }
+  if (a.out_mode == OUT_SOFTCAP_ARGMAX) {
+    // per token: the warps' bests (lanes g of one column t) and the split-K finishers' into shared memory
+#pragma unroll
+    for (int G = 0; G < NG; ++G)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        unsigned long long b = best[G][j];
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          const unsigned long long v = __shfl_xor_sync(0xffffffffu, b, o);
+          b = v > b ? v : b;
+        }
+        const int tk = G * 8 + 2 * t + j;
+        if (g == 0 && b && tk < T) atomicMax(&sbest[tk], b);
+      }
+    __syncthreads();
+    for (int i = threadIdx.x; i < T; i += blockDim.x)
+      if (sbest[i]) atomicMax(a.argmax + i, sbest[i]);
   }
 }
 
@@ -553,7 +653,9 @@ MmaBatchPlan plan_gemm_mma_batch(const DeviceInfo& dev, int rows, int cols, int 
   p.ng = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
   p.nrt = (rows + 15) / 16;
   p.nkb = cols / 32;
-  p.smem = (size_t)kMmaWarps * 16 * (8 * p.ng + 1) * 4;
+  p.nrb = (p.nrt + kBatchRt - 1) / kBatchRt;
+  p.smem = (size_t)2 * kBatchKc * 8 * p.ng * kBatchRow + (size_t)2 * kBatchKc * 8 * p.ng * 4 +
+           (size_t)8 * p.ng * 8 + 16;
   BatchFn fn = batch_fn(p.ng);
   int occ = 0;
   if (!fn || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dev.smem_optin) ||
@@ -561,41 +663,29 @@ MmaBatchPlan plan_gemm_mma_batch(const DeviceInfo& dev, int rows, int cols, int 
     cudaGetLastError();
     return p;
   }
-  // K split as plan_gemv_mma: shortest critical path in task waves x blocks per warp
+  // K splits: enough tasks for every resident CTA, whole staged chunks per split
   const int resident = occ * dev.sms;
-  long long best = -1;
-  for (int ks = 1; ks <= kMmaWarps; ks *= 2) {
-    const int tiles = kMmaWarps / ks;
-    const int ntasks = (p.nrt + tiles - 1) / tiles;
-    const int grid = std::min(ntasks, resident);
-    const int waves = (ntasks + grid - 1) / grid;
-    const int kpw = (p.nkb + ks - 1) / ks;
-    const long long cost = (long long)waves * kpw;
-    if (best < 0 || cost < best || (cost == best && grid > p.grid)) {
-      best = cost;
-      p.ks = ks;
-      p.tiles = tiles;
-      p.kpw = kpw;
-      p.ntasks = ntasks;
-      p.grid = grid;
-    }
-  }
+  int splits = std::max(1, std::min(16, (resident + p.nrb - 1) / p.nrb));
+  p.kps = ((p.nkb + splits - 1) / splits + kBatchKc - 1) / kBatchKc * kBatchKc;
+  p.splits = (p.nkb + p.kps - 1) / p.kps;
+  p.ntasks = p.nrb * p.splits;
+  p.grid = std::min(p.ntasks, resident);
   p.fast = 1;
   return p;
 }
 
 int launch_gemm_mma_batch(const MmaBatchPlan& p, const uint8_t* packed, const int8_t* lim, const float* lsc, int T,
                           float* y, int ldy, int out_mode, float softcap, unsigned long long* argmax,
-                          cudaStream_t st) {
+                          float* partials, unsigned* tickets, cudaStream_t st) {
   cudaGetLastError();
   if (!p.fast || T <= 0 || T > 8 * p.ng || (out_mode == OUT_SOFTCAP_ARGMAX && !argmax) ||
-      (out_mode == OUT_GELU_PAIR && p.rows % 2))
+      (out_mode == OUT_GELU_PAIR && p.rows % 2) || (p.splits > 1 && (!partials || !tickets)))
     return (int)cudaErrorInvalidValue;
   BatchFn fn = batch_fn(p.ng);
   const size_t tiles_total = (size_t)p.nrt * p.nkb;
   MmaBatchArgs a{p, reinterpret_cast<const uint4*>(packed),
                  reinterpret_cast<const uint32_t*>(packed + tiles_total * 512), lim, lsc, y, T, ldy, out_mode,
-                 softcap, argmax};
+                 softcap, argmax, partials, tickets};
   fn<<<p.grid, kMmaWarps * 32, p.smem, st>>>(a);
   return (int)cudaGetLastError();
 }

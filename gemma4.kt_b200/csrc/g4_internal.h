@@ -36,9 +36,10 @@ struct MmaBatchPlan;
 // Batched decode (g4_gemv_mma.cu): the per-token prologue into int8 limbs and
 // the T-token GEMM on the repacked Q8_0 tiles.
 MmaBatchPlan plan_gemm_mma_batch(const DeviceInfo& dev, int rows, int cols, int T);
+// partials: mma_batch_partials(p, T) floats; tickets: p.nrb words, zero between launches
 int launch_gemm_mma_batch(const MmaBatchPlan& p, const uint8_t* packed, const int8_t* lim, const float* lsc, int T,
                           float* y, int ldy, int out_mode, float softcap, unsigned long long* argmax,
-                          cudaStream_t st);
+                          float* partials, unsigned* tickets, cudaStream_t st);
 int launch_batch_prologue(const GemvFuse& f, const float* x, int dim, int T, int8_t* lim, float* lsc,
                           cudaStream_t st);
 struct DecGemvPlan;
