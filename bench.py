@@ -143,7 +143,8 @@ def sweep_config(world: int) -> dict:
             "shapes": [f"{r}x{c}" for r, c in SHAPES],
             "bytes_per_step": sum(alg_bytes(t, r, c) for r, c in SHAPES for _, t in FORMATS),
             "l2": "inputs larger than L2 (1.9 GB streamed per step)",
-            "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU"}
+            "parallelism": f"{world} GPUs, each streaming the whole sweep (its own inputs; the row-sharded product "
+                           "with its all-gather is reported beside as row_sharded)" if world > 1 else "single GPU"}
 
 
 # ------------------------------------------------------------------ CPU arm
@@ -226,11 +227,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     cases = make_cases()
     step_bytes = sum(alg_bytes(c["type"], c["rows"], c["cols"]) for c in cases)
     for c in cases:
+        # the full matrix on every GPU (the headline: each GPU runs its own copy of the sweep, weak
+        # scaling) and, at N > 1, each rank's row shard (the row-sharded product with its all-gather)
+        c["wf"] = g4.FloatTensorFactory.create(ctx, c["type"], c["raw"], c["rows"] * c["cols"])
         if world > 1:
             begin, per = g4.row_shard(c["rows"], world, rank)
             c["w"] = g4.FloatTensorFactory.create_rows(ctx, c["type"], c["raw"], c["cols"], begin, per)
         else:
-            c["w"] = g4.FloatTensorFactory.create(ctx, c["type"], c["raw"], c["rows"] * c["cols"])
+            c["w"] = c["wf"]
         c["xd"] = torch.from_numpy(c["x"]).to(dev)
         c["yd"] = torch.empty(c["rows"], dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(dev)
@@ -306,13 +310,39 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     # The step (all 16 launches) as one CUDA graph at N=1: the GPU sees the same
     # kernels back to back without Python launch gaps.
-    step_graph = None
-    if world == 1:
-        step_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            step_graph.capture_begin()
+    def step_full():  # every case on this GPU's full matrix
+        for c in cases:
+            rc = L.g4_matmul(ctx.handle, c["wf"].handle, 0, C.c_void_p(c["xd"].data_ptr()),
+                             C.c_void_p(c["yd"].data_ptr()), c["rows"], c["cols"], C.c_void_p(sp))
+            if rc:
+                raise RuntimeError(ctx.last_error())
+
+    row_sharded = None
+    if world > 1:
+        # strong scaling of the row-sharded product (local rows + NCCL all-gather of y), reported beside
+        import torch.distributed as dist
+
+        barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(args.steps):
             step()
-            step_graph.capture_end()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        tt = torch.tensor([s0.elapsed_time(s1) / args.steps], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_sh = float(tt.item())
+        row_sharded = {"value": round(step_bytes / (ms_sh * 1e-3) / 1e9, 3), "unit": "GB/s", "scaling": "strong",
+                       "ms_per_step": round(ms_sh, 4),
+                       "note": "each matrix split by output rows over the GPUs (g4_matmul_sharded), y all-gathered "
+                               "over NCCL after every product; CUDA events, max over ranks"}
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        step_graph.capture_begin()
+        step_full()
+        step_graph.capture_end()
         with torch.cuda.stream(stream):
             step_graph.replay()
         torch.cuda.synchronize()
@@ -324,10 +354,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     with torch.cuda.stream(stream):  # graph replays launch on the current stream
         t0e.record(stream)
         for _ in range(args.steps):
-            if step_graph is not None:
-                step_graph.replay()
-            else:
-                step()
+            step_graph.replay()
         t1e.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -341,7 +368,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
-    value = step_bytes / (ms * 1e-3) / 1e9
+    value = world * step_bytes / (ms * 1e-3) / 1e9  # every GPU streams the whole sweep
 
     # roofline of the dominant kernel
     hbm, hbm_kind = peaks()
@@ -355,65 +382,38 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         breakdown.append({"case": f"{cc['name']} {cc['rows']}x{cc['cols']}", "us": round(per_case[i] * 1e3, 2),
                           "GBps": round(b / (per_case[i] * 1e-3) / 1e9, 1)})
 
-    # end to end through the host-buffer API (pinned host arrays), N=1
-    e2e = None
-    if world == 1:
-        xs = [torch.from_numpy(cc["x"]).pin_memory() for cc in cases]
-        ys = [torch.empty(cc["rows"], dtype=torch.float32).pin_memory() for cc in cases]
-        h2d = sum(cc["cols"] * 4 for cc in cases)
-        d2h = sum(cc["rows"] * 4 for cc in cases)
+    # end to end through the host-buffer API (g4_matmul_host: host x in, host y out, synchronous), every GPU
+    xs = [torch.from_numpy(cc["x"]).pin_memory() for cc in cases]
+    ys = [torch.empty(cc["rows"], dtype=torch.float32).pin_memory() for cc in cases]
+    h2d = sum(cc["cols"] * 4 for cc in cases)
+    d2h = sum(cc["rows"] * 4 for cc in cases)
 
-        def e2e_step():
-            for i, cc in enumerate(cases):
-                rc = L.g4_matmul_host(ctx.handle, cc["w"].handle, 0, C.c_void_p(xs[i].data_ptr()),
-                                      C.c_void_p(ys[i].data_ptr()), cc["rows"], cc["cols"])
-                if rc:
-                    raise RuntimeError(ctx.last_error())
+    def e2e_step():
+        for i, cc in enumerate(cases):
+            rc = L.g4_matmul_host(ctx.handle, cc["wf"].handle, 0, C.c_void_p(xs[i].data_ptr()),
+                                  C.c_void_p(ys[i].data_ptr()), cc["rows"], cc["cols"])
+            if rc:
+                raise RuntimeError(ctx.last_error())
 
-        for _ in range(2):
-            e2e_step()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            e2e_step()
-        e2e_s = (time.perf_counter() - t0) / args.steps
-        ok = all(np.allclose(ys[i].numpy(), cc["yd"].cpu().numpy(), rtol=0, atol=1e-5 * float(
-            np.abs(cc["yd"].cpu().numpy()).max() + 1)) for i, cc in enumerate(cases))
-        e2e = {"value": round(step_bytes / e2e_s / 1e9, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_s * 1e3, 3), "matches_device_path": bool(ok)}
-    else:
-        # N > 1: every step copies x from pinned host memory to each GPU, runs the
-        # sharded GEMV (local rows + NCCL all-gather) and reads the full y back.
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if world > 1:
         import torch.distributed as dist
 
-        xs = [torch.from_numpy(cc["x"]).pin_memory() for cc in cases]
-        ys = [torch.empty(cc["rows"], dtype=torch.float32).pin_memory() for cc in cases]
-        h2d = sum(cc["cols"] * 4 for cc in cases)
-        d2h = sum(cc["rows"] * 4 for cc in cases)
-
-        def e2e_step():
-            with torch.cuda.stream(stream):
-                for i, cc in enumerate(cases):
-                    cc["xd"].copy_(xs[i], non_blocking=True)
-                    rc = L.g4_matmul_sharded(ctx.handle, cc["w"].handle, C.c_void_p(cc["xd"].data_ptr()),
-                                             C.c_void_p(cc["yd"].data_ptr()), cc["rows"], cc["cols"], C.c_void_p(sp))
-                    if rc:
-                        raise RuntimeError(ctx.last_error())
-                    ys[i].copy_(cc["yd"], non_blocking=True)
-            stream.synchronize()
-
-        for _ in range(2):
-            e2e_step()
-        dist.barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            e2e_step()
-        e2e_s = (time.perf_counter() - t0) / args.steps
         tt = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_s = float(tt.item())
-        e2e = {"value": round(step_bytes / e2e_s / 1e9, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
-               "d2h_bytes_per_step": d2h * world, "ms_per_step": round(e2e_s * 1e3, 3),
-               "timing": "host wall clock per rank, max over ranks"}
+    ok = all(np.allclose(ys[i].numpy(), cc["yd"].cpu().numpy(), rtol=0, atol=1e-5 * float(
+        np.abs(cc["yd"].cpu().numpy()).max() + 1)) for i, cc in enumerate(cases))
+    e2e = {"value": round(world * step_bytes / e2e_s / 1e9, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
+           "d2h_bytes_per_step": d2h * world, "ms_per_step": round(e2e_s * 1e3, 3), "matches_device_path": bool(ok),
+           "timing": "host wall clock per step (pinned host arrays through g4_matmul_host)"
+                     + (", max over ranks" if world > 1 else "")}
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
@@ -434,12 +434,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     c5 = None
     if world == 1 and rank == 0 and not args.no_decode and not args.no_c5:
         c5 = bench_c5(g4, ctx, torch, dev, with_cpu=not args.no_cpu)
+    elif world > 1 and not args.no_decode and not args.no_c5:
+        c5 = bench_c5(g4, ctx, torch, dev, with_cpu=False, rank=rank, world=world)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
             "config": sweep_config(world),
             "roofline": {"bound": "hbm", "kernel": breakdown[dom]["case"], "achieved": round(achieved, 1),
                          "peak": hbm, "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
@@ -458,9 +460,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             line["decode"] = decode
         if c5:
             line["c5"] = c5
+        if row_sharded:
+            line["row_sharded"] = row_sharded
         print(json.dumps(line), flush=True)
     for cc in cases:
-        cc["w"].free()
+        if cc["w"] is not cc["wf"]:
+            cc["w"].free()
+        cc["wf"].free()
     ctx.close()
 
 
@@ -591,10 +597,13 @@ def c5_bytes_per_step(cfg, n_seq, positions, e_touched):
     return b + cfg.vocab * dim * q8
 
 
-def bench_c5(g4, ctx, torch, dev, with_cpu: bool = True):
+def bench_c5(g4, ctx, torch, dev, with_cpu: bool = True, rank: int = 0, world: int = 1):
     """Configuration 5 (MoE decoder, seed 4): 64 sequences decoded together
     through g4_batch_step, <bos> + 512 random prompt ids each, then 256 greedy
-    tokens each (768 batched steps)."""
+    tokens each (768 batched steps).  On N GPUs each rank decodes 64/N of the
+    sequences (data-parallel attention and dense layers) and the experts are
+    split over the ranks (g4_batch_expert_parallel: token rows exchanged over
+    NCCL in every MoE layer); time = max over ranks."""
     import dataclasses
 
     from gemma4_kt_b200 import synth
@@ -605,15 +614,23 @@ def bench_c5(g4, ctx, torch, dev, with_cpu: bool = True):
     src = g4.TensorSource.from_synth(m)
     model = g4.DecoderModel(ctx, src)
     cfg = model.cfg
-    n_seq, n_prompt, n_gen = 64, 512, 256
+    n_total, n_prompt, n_gen = 64, 512, 256
+    n_seq = n_total // world
     steps = n_prompt + n_gen
-    prompts = np.stack([np.concatenate([[2], m.prompt(n_prompt, seed=4000 + i)]) for i in range(n_seq)]).astype(np.int32)
+    prompts = np.stack([np.concatenate([[2], m.prompt(n_prompt, seed=4000 + rank * n_seq + i)])
+                        for i in range(n_seq)]).astype(np.int32)
     batch = model.new_batch(n_seq, steps)
+    if world > 1:
+        batch.expert_parallel()
     build_s = time.time() - t0
     stream = torch.cuda.ExternalStream(batch.stream, device=dev)
     for p in range(3):  # warm-up (kernels set up, weights touched); the timed run rewrites these positions
         batch.step(prompts[:, p], np.full(n_seq, p, np.int32), want_logits=False)
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     tok = prompts[:, 0].copy()
     gen = np.zeros((n_seq, n_gen), np.int32)
@@ -628,25 +645,33 @@ def bench_c5(g4, ctx, torch, dev, with_cpu: bool = True):
     ev[2].record(stream)
     torch.cuda.synchronize()
     prompt_ms, gen_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    if world > 1:
+        tt = torch.tensor([prompt_ms, gen_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        prompt_ms, gen_ms = (float(v) for v in tt.tolist())
     hbm, hbm_kind = peaks()
-    e_touched = cfg.n_expert * (1 - (1 - cfg.n_expert_used / cfg.n_expert) ** n_seq)
-    bytes_gen = c5_bytes_per_step(cfg, n_seq, list(range(n_prompt, steps)), e_touched) * n_gen
+    e_touched = cfg.n_expert * (1 - (1 - cfg.n_expert_used / cfg.n_expert) ** n_total)
+    bytes_gen = c5_bytes_per_step(cfg, n_total, list(range(n_prompt, steps)), e_touched) * n_gen
     achieved = bytes_gen / (gen_ms * 1e-3) / 1e9
     res = {
         "metric": "batched decode tok/s",
         "config": "C5 MoE decoder: 30 layers, hidden 2816, 16 q / 8 kv heads x 256, 128 experts top-8 ff 704 Q4_K, "
                   "shared FFN 2112 Q8_0, vocab 262144, seed 4; 64 sequences x (<bos> + 512 random prompt ids), "
                   "256 greedy tokens each, fp32 KV cache",
-        "generation_tok_s": round(n_seq * n_gen / (gen_ms * 1e-3), 1),
-        "prompt_tok_s": round(n_seq * n_prompt / (prompt_ms * 1e-3), 1),
+        "n_gpus": world,
+        "parallelism": (f"{n_seq} sequences per GPU (data-parallel attention and dense layers), "
+                        f"{cfg.n_expert // world} experts per GPU (expert-parallel, NCCL token exchange)")
+                       if world > 1 else "single GPU",
+        "generation_tok_s": round(n_total * n_gen / (gen_ms * 1e-3), 1),
+        "prompt_tok_s": round(n_total * n_prompt / (prompt_ms * 1e-3), 1),
         "ms_per_step": round(gen_ms / n_gen, 3),
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "peak_kind": hbm_kind,
-                     "unit": "GB/s", "frac": round(achieved / hbm, 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm * world, "peak_kind": hbm_kind,
+                     "unit": "GB/s", "frac": round(achieved / (hbm * world), 4),
                      "bytes_per_step": round(bytes_gen / n_gen),
                      "note": "dense and output matrices once per step, expected touched experts "
                              f"({e_touched:.1f} of {cfg.n_expert}), KV rows of every attended position"},
-        "e2e": {"value": round(n_seq * n_gen / (gen_ms * 1e-3), 1), "unit": "tok/s",
-                "h2d_bytes_per_step": n_seq * 8, "d2h_bytes_per_step": n_seq * 8,
+        "e2e": {"value": round(n_total * n_gen / (gen_ms * 1e-3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": n_total * 8, "d2h_bytes_per_step": n_total * 8,
                 "note": "every step is one synchronous g4_batch_step call from host arrays (ids and positions in, "
                         "argmax ids out), so the timed loop is the end-to-end figure"},
         "timing": "CUDA events on the batch's stream around the 512 prompt steps and the 256 generating steps",

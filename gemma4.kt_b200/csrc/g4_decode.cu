@@ -1334,6 +1334,11 @@ struct g4_batch {
   int* h_io = nullptr;          // pinned: tokens [n_max], positions [n_max]
   unsigned long long* h_keys = nullptr;  // pinned [n_max]
   std::map<std::tuple<int, int, int>, MmaBatchPlan> plans;
+  // expert parallelism (g4_batch_expert_parallel): per layer, this rank's experts
+  // as views into the model's expert tensors
+  bool ep = false;
+  std::vector<g4_tensor> ep_views;  // [layer][gate_up, down]
+  std::vector<g4_moe_weights> ep_moe;
 
   const MmaBatchPlan* plan(int rows, int cols, int T) {
     const int ng = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
@@ -1674,7 +1679,9 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
     branch = b->sh;
     branch_scale = L.scale;
     if (k.n_expert > 0) {
-      if (int r = g4_moe_layer(c, &L.moe, b->x[cur], b->moe_out, n, nullptr, nullptr, st)) return r;
+      const int r = b->ep ? g4_moe_layer_ep(c, &b->ep_moe[l], b->x[cur], b->moe_out, n, nullptr, nullptr, st)
+                          : g4_moe_layer(c, &L.moe, b->x[cur], b->moe_out, n, nullptr, nullptr, st);
+      if (r) return r;
       branch_w = L.post_ffw_norm_1;
       moe_prev = b->moe_out;
       moe_w = L.post_ffw_norm;
@@ -1709,3 +1716,53 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
 }
 
 extern "C" void* g4_batch_stream(g4_batch* b) { return b ? (void*)b->st : nullptr; }
+
+// Expert parallelism for a batch: rank r of the context's communicator
+// (g4_dist_init) computes experts [r*E/W, (r+1)*E/W) of every MoE layer for
+// all ranks' tokens, through g4_moe_layer_ep; attention and the dense layers
+// stay with the rank's own sequences (data parallel).  The expert tensors are
+// not re-uploaded: each layer's local experts are a view into the model's
+// tensors.  From this call on every rank must run g4_batch_step together.
+extern "C" int g4_batch_expert_parallel(g4_batch* b) {
+  if (!b) return G4_E_ARG;
+  g4_model* m = b->m;
+  g4_ctx* c = m->ctx;
+  const g4_model_config& k = m->cfg;
+  if (c->world < 2 || !c->comm) {
+    c->set_err("g4_batch_expert_parallel: needs g4_dist_init with two or more ranks");
+    return G4_E_ARG;
+  }
+  if (k.n_expert <= 0 || k.n_expert % c->world) {
+    c->set_err("g4_batch_expert_parallel: %d experts do not split over %d ranks", k.n_expert, c->world);
+    return G4_E_ARG;
+  }
+  const int El = k.n_expert / c->world;
+  b->ep_views.assign(2 * (size_t)k.n_layers, g4_tensor{});
+  b->ep_moe.assign(k.n_layers, g4_moe_weights{});
+  for (int l = 0; l < k.n_layers; ++l) {
+    const LayerDev& L = m->L[l];
+    g4_moe_weights w = L.moe;
+    const g4_tensor* full[2] = {L.moe.gate_up_exps, L.moe.down_exps};
+    for (int i = 0; i < 2; ++i) {
+      const g4_tensor* t = full[i];
+      const uint64_t per = t->n_elems / (uint64_t)k.n_expert;  // elements of one expert
+      const int bs = block_size(t->type), ts = type_size(t->type);
+      if (t->n_elems % (uint64_t)k.n_expert || bs <= 0 || per % (uint64_t)bs) {
+        c->set_err("g4_batch_expert_parallel: layer %d: experts are not whole blocks", l);
+        return G4_E_TYPE;
+      }
+      const uint64_t bytes = per / (uint64_t)bs * (uint64_t)ts;
+      g4_tensor& v = b->ep_views[2 * (size_t)l + i];
+      v.ctx = c;
+      v.type = t->type;
+      v.d = static_cast<uint8_t*>(t->d) + (size_t)c->rank * El * bytes;
+      v.nbytes = (uint64_t)El * bytes;
+      v.n_elems = (uint64_t)El * per;
+    }
+    w.gate_up_exps = &b->ep_views[2 * (size_t)l];
+    w.down_exps = &b->ep_views[2 * (size_t)l + 1];
+    b->ep_moe[l] = w;
+  }
+  b->ep = true;
+  return 0;
+}

@@ -289,6 +289,11 @@ class DecoderBatch:
     def stream(self) -> int:
         return int(lib().g4_batch_stream(self.handle) or 0)
 
+    def expert_parallel(self) -> None:
+        """Experts split over the ranks of the context's communicator
+        (Context.dist_init); from now on every rank steps together."""
+        check(lib().g4_batch_expert_parallel(self.handle), self.model.ctx.handle, "g4_batch_expert_parallel")
+
     def step(self, tokens, positions, want_logits: bool = True):
         """Llama.forward for sequences 0..n-1: (logits [n, vocab] or None, argmax [n])."""
         t = np.ascontiguousarray(tokens, np.int32)

@@ -311,6 +311,13 @@ int g4_batch_step(g4_batch *batch, const int *tokens, const int *positions, int 
                   int *next_tokens_host);
 /* The batch's cudaStream_t. */
 void *g4_batch_stream(g4_batch *batch);
+/* Expert parallelism for a batch (no counterpart in the reference, which runs
+ * in one process): after g4_dist_init on W >= 2 ranks, rank r computes experts
+ * [r*E/W, (r+1)*E/W) of every MoE layer for all ranks' tokens (the layer runs
+ * as g4_moe_layer_ep); attention and the dense layers stay with the rank's
+ * own sequences.  Every rank then calls g4_batch_step together, each with its
+ * own sequences.  Q4_K experts; E divisible by W. */
+int g4_batch_expert_parallel(g4_batch *batch);
 
 /* Router top-k alone on given logits (Llama.kt:273-293 + softmaxInPlace,
  * MutableFloatTensor.kt:54-59): probs_dev/idx_dev [n_tokens, k]. */

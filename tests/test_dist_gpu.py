@@ -217,3 +217,71 @@ def test_dist_init_gives_up_when_a_peer_never_joins():
     assert 2.5 < waited < 60, waited
     ref = oracle.matmul(int(g4.GGMLType.Q8_0), raw, x, 256, 2048)
     assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < TOL
+
+
+def _batch_ep_rank_main(rank, world, port, q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from gemma4_kt_b200 import synth
+    from tests.test_decode_gpu import SPECS
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        torch.cuda.set_device(rank)
+        ctx = g4.Context(rank)
+        obj = [g4.Context.dist_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.dist_init(rank, world, obj[0])
+        m = synth.SynthDecoder(SPECS["moe"], seed=39)
+        model = g4.DecoderModel(ctx, g4.TensorSource.from_synth(m))
+        n_seq, steps = 3, 16
+        ep = model.new_batch(n_seq, steps)
+        ep.expert_parallel()
+        local = model.new_batch(n_seq, steps)  # the same sequences, every expert on this GPU
+        prompts = np.stack([np.concatenate([[2], m.prompt(steps, seed=500 + 10 * rank + i)]) for i in range(n_seq)])
+        res = []
+        for p in range(steps):
+            tok = prompts[:, p].astype(np.int32)
+            pos = np.full(n_seq, p, np.int32)
+            lg_ep, nt_ep = ep.step(tok, pos)
+            lg_lo, nt_lo = local.step(tok, pos)
+            res.append((lg_ep, nt_ep, lg_lo, nt_lo))
+        q.put((rank, res))
+        dist.barrier()
+        ep.free()
+        local.free()
+        model.free()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_batch_expert_parallel_two_gpus():
+    """Batched decode with data-parallel sequences and expert-parallel MoE
+    layers (g4_batch_expert_parallel, 8 of 16 experts per GPU): every rank's
+    logits and argmax equal those of a batch that runs all experts on the
+    rank's own GPU for the same sequences (teacher-forced prompt tokens)."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_batch_ep_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        for step, (lg_ep, nt_ep, lg_lo, nt_lo) in enumerate(got[r]):
+            for i in range(lg_ep.shape[0]):
+                err = np.linalg.norm(lg_ep[i] - lg_lo[i]) / np.linalg.norm(lg_lo[i])
+                assert err < 1e-5, (r, step, i, err)
+            assert np.array_equal(nt_ep, nt_lo), (r, step)
