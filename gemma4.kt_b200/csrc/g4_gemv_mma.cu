@@ -41,13 +41,19 @@ struct MmaGemvArgs {
   GemvFuse f;
 };
 
+// D = A.B + C with C = 0x4B400000 in every element: each int32 sum s (|s| <
+// 2^22; a block's code x limb sums stay below 32*127*127) comes out as the bit
+// pattern of the float 1.5*2^23 + s, so one subtraction (mma_f32) turns it into
+// an exact float instead of an integer-to-float conversion.
+constexpr int kMmaMagic = 0x4B400000;
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%11,%12,%13};"
+      "{%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(kMmaMagic));
 }
+__device__ __forceinline__ float mma_f32(int d) { return __fsub_rn(__int_as_float(d), 12582912.0f); }
 
 // x rounded to the nearest integer (ties to even), |x| < 2^22, as float and int
 __device__ __forceinline__ float rint_small(float x, int& i) {
@@ -223,10 +229,10 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 3) gemv_mma_kernel(const __gri
           const float s = xsc[kb];
           const float dg = __fmul_rn(f16_bits_to_f32((uint16_t)(Sc[u] & 0xFFFFu)), s);
           const float dg8 = __fmul_rn(f16_bits_to_f32((uint16_t)(Sc[u] >> 16)), s);
-          acc0 = fmaf((float)d[0], dg, acc0);
-          acc1 = fmaf((float)d[1], dg, acc1);
-          acc2 = fmaf((float)d[2], dg8, acc2);
-          acc3 = fmaf((float)d[3], dg8, acc3);
+          acc0 = fmaf(mma_f32(d[0]), dg, acc0);
+          acc1 = fmaf(mma_f32(d[1]), dg, acc1);
+          acc2 = fmaf(mma_f32(d[2]), dg8, acc2);
+          acc3 = fmaf(mma_f32(d[3]), dg8, acc3);
         }
       }
     }
@@ -376,12 +382,6 @@ int launch_gemv_mma(const MmaGemvPlan& p, const uint8_t* packed, const float* x,
 
 // ---------------------------------------------------------------- batched decode
 // Many sequences at one step each (g4_batch_step): T <= kBatchMaxT tokens.
-
-// An int32 product sum as float (|v| < 2^22, exact): magic-number conversion
-// on the FP32 pipe instead of the quarter-rate integer-to-float unit.
-__device__ __forceinline__ float small_i2f(int v) {
-  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
-}
 
 __device__ int g_batch_step0 = 0;  // step index 0: the batched embedding prologue reads in_tok[0]
 
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
               const float sc[4] = {d0 * s0, d0 * s1, d8 * s0, d8 * s1};
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
-                const float v = fmaf(small_i2f(dl[i]), kInv2, fmaf(small_i2f(dm[i]), kInv1, small_i2f(dh[i])));
+                const float v = fmaf(mma_f32(dl[i]), kInv2, fmaf(mma_f32(dm[i]), kInv1, mma_f32(dh[i])));
                 acc[G][i] = fmaf(v, sc[i], acc[G][i]);
               }
             }
