@@ -43,7 +43,10 @@ struct GemvArgs {
 
 // LPR lanes share a row: a warp covers 32/LPR rows; lane l owns row slot
 // l % (32/LPR) and, within each chunk, the blocks b with b % LPR == l / (32/LPR).
-template <int FMT, int PR, int LPR, bool X2>
+// FUSED: the decoder's variant with the fused prologue / epilogue and L2
+// prefetch compiled in; the plain variant (g4_matmul) keeps them out, so its
+// register count (and CTAs per SM) is that of the bare product.
+template <int FMT, int PR, int LPR, bool X2, bool FUSED>
 __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const GemvPlan& p = a.p;
@@ -119,14 +122,16 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
   // flight before this waits for them (programmatic dependent launch; both
   // are no-ops for a plain launch).  Dependents launch only after the wait,
   // so everything two kernels back has completed when they start.
-  issue_l2_prefetch(a.f);
+  if constexpr (FUSED) issue_l2_prefetch(a.f);
   grid_dep_wait();
   grid_dep_launch();
   float* misc = reinterpret_cast<float*>(smem + p.misc_off);
   const float* src = a.x;
-  if (a.f.in_mode != IN_PLAIN) {
-    fused_prologue(a.f, a.x, xs, misc, p.cols);
-    src = xs;
+  if constexpr (FUSED) {
+    if (a.f.in_mode != IN_PLAIN) {
+      fused_prologue(a.f, a.x, xs, misc, p.cols);
+      src = xs;
+    }
   }
 
   // x -> shared memory while the first weight stages are in flight, in one
@@ -190,7 +195,7 @@ __global__ void __launch_bounds__(512) gemv_rows_kernel(const __grid_constant__ 
   float acc[PR];
 #pragma unroll
   for (int r = 0; r < PR; ++r) acc[r] = 0.f;
-  const int out_mode = a.f.out_mode;
+  const int out_mode = FUSED ? a.f.out_mode : (int)OUT_PLAIN;
   unsigned long long best = 0ull;  // OUT_SOFTCAP_ARGMAX: this lane's best key
 
   int g = g_first, c = c_first;  // consume pointer
@@ -368,35 +373,37 @@ static int gcd_i(int a, int b) {
 
 using KernelFn = void (*)(const GemvArgs);
 
+template <int FMT, bool X2, bool F>
+static KernelFn pick_pr1(int lpr) {
+  return lpr == 32 ? gemv_rows_kernel<FMT, 1, 32, X2, F> : lpr == 16 ? gemv_rows_kernel<FMT, 1, 16, X2, F>
+       : lpr == 4  ? gemv_rows_kernel<FMT, 1, 4, X2, F>  : lpr == 2  ? gemv_rows_kernel<FMT, 1, 2, X2, F>
+                                                                     : gemv_rows_kernel<FMT, 1, 1, X2, F>;
+}
+
 template <int FMT>
-static KernelFn pick_kernel(int pr, int lpr, bool x2) {
+static KernelFn pick_kernel(int pr, int lpr, bool x2, bool fused) {
   if (x2) {
     // two-part activations: the decoder's row-aligned projections only
     if constexpr (FMT == Q8_0 || FMT == Q4_K || FMT == Q6_K)
-      if (pr == 1)
-        return lpr == 32 ? gemv_rows_kernel<FMT, 1, 32, true> : lpr == 16 ? gemv_rows_kernel<FMT, 1, 16, true>
-             : lpr == 4  ? gemv_rows_kernel<FMT, 1, 4, true>  : lpr == 2  ? gemv_rows_kernel<FMT, 1, 2, true>
-                                                                          : gemv_rows_kernel<FMT, 1, 1, true>;
+      if (pr == 1) return fused ? pick_pr1<FMT, true, true>(lpr) : pick_pr1<FMT, true, false>(lpr);
     return nullptr;
   }
-  if (pr == 1)
-    return lpr == 32 ? gemv_rows_kernel<FMT, 1, 32, false> : lpr == 16 ? gemv_rows_kernel<FMT, 1, 16, false>
-         : lpr == 4  ? gemv_rows_kernel<FMT, 1, 4, false>  : lpr == 2  ? gemv_rows_kernel<FMT, 1, 2, false>
-                                                                       : gemv_rows_kernel<FMT, 1, 1, false>;
+  if (pr == 1) return fused ? pick_pr1<FMT, false, true>(lpr) : pick_pr1<FMT, false, false>(lpr);
   if constexpr (FMT == Q4_K || FMT == Q6_K) {
-    if (pr == 2) return lpr == 2 ? gemv_rows_kernel<FMT, 2, 2, false> : gemv_rows_kernel<FMT, 2, 1, false>;
-    if (pr == 4) return lpr == 2 ? gemv_rows_kernel<FMT, 4, 2, false> : gemv_rows_kernel<FMT, 4, 1, false>;
+    if (fused) return nullptr;  // fused prologues / epilogues take one row per lane group
+    if (pr == 2) return lpr == 2 ? gemv_rows_kernel<FMT, 2, 2, false, false> : gemv_rows_kernel<FMT, 2, 1, false, false>;
+    if (pr == 4) return lpr == 2 ? gemv_rows_kernel<FMT, 4, 2, false, false> : gemv_rows_kernel<FMT, 4, 1, false, false>;
   }
   return nullptr;
 }
 
-static KernelFn kernel_for(int type, int pr, int lpr, bool x2 = false) {
+static KernelFn kernel_for(int type, int pr, int lpr, bool x2, bool fused) {
   switch (type) {
-    case Q8_0: return pick_kernel<Q8_0>(pr, lpr, x2);
-    case Q4_K: return pick_kernel<Q4_K>(pr, lpr, x2);
-    case Q6_K: return pick_kernel<Q6_K>(pr, lpr, x2);
-    case BF16: return pick_kernel<BF16>(pr, lpr, false);
-    case F32: return pick_kernel<F32>(pr, lpr, false);
+    case Q8_0: return pick_kernel<Q8_0>(pr, lpr, x2, fused);
+    case Q4_K: return pick_kernel<Q4_K>(pr, lpr, x2, fused);
+    case Q6_K: return pick_kernel<Q6_K>(pr, lpr, x2, fused);
+    case BF16: return pick_kernel<BF16>(pr, lpr, false, fused);
+    case F32: return pick_kernel<F32>(pr, lpr, false, fused);
     default: return nullptr;
   }
 }
@@ -525,7 +532,7 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
   p.ring_off = p.bar_off + 128 * ((p.warps * p.ns * 8 + 127) / 128);
   p.red_off = (int)(p.ring_off + (size_t)p.warps * p.ns * stage);
   p.smem = (size_t)p.red_off + (p.split > 1 ? (size_t)p.warps * rows_per_group * pr * 4 : 0);
-  KernelFn k = kernel_for(type, pr, p.lpr, p.x2 != 0);
+  KernelFn k = kernel_for(type, pr, p.lpr, p.x2 != 0, p.fused != 0);
   if (!k) return p;
   int occ = 0;
   // The attribute belongs to the kernel, not to this plan: always allow the
@@ -547,10 +554,11 @@ GemvPlan plan_gemv(const DeviceInfo& dev, int type, long long off, int rows, int
 int launch_gemv_fused(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvFuse& f,
                       unsigned* status, cudaStream_t st, bool pdl) {
   cudaGetLastError();
-  if (!p.fast || (f.in_mode != IN_PLAIN && !p.fused) || (f.out_mode != OUT_PLAIN && p.pr != 1))
+  if (!p.fast || ((f.in_mode != IN_PLAIN || f.out_mode != OUT_PLAIN || f.pf[0]) && !p.fused) ||
+      (f.out_mode != OUT_PLAIN && p.pr != 1))
     return (int)cudaErrorInvalidValue;
   GemvArgs a{p, w, x, y, status, f};
-  KernelFn k = kernel_for(p.type, p.pr, p.lpr, p.x2 != 0);
+  KernelFn k = kernel_for(p.type, p.pr, p.lpr, p.x2 != 0, p.fused != 0);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(32 * p.warps);
@@ -569,7 +577,7 @@ int launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, u
   cudaGetLastError();  // launch errors below must not be confused with stale ones
   if (p.fast) {
     GemvArgs a{p, w, x, y, status, GemvFuse{}};
-    KernelFn k = kernel_for(p.type, p.pr, p.lpr, p.x2 != 0);
+    KernelFn k = kernel_for(p.type, p.pr, p.lpr, p.x2 != 0, p.fused != 0);
     k<<<p.grid, 32 * p.warps, p.smem, st>>>(a);
   } else {
     int wpb = 8;
