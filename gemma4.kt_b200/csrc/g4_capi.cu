@@ -8,6 +8,7 @@
 #include <nccl.h>
 
 #include <time.h>
+#include <sched.h>
 #include <unistd.h>
 
 #include <cstdarg>
@@ -412,7 +413,16 @@ static int default_dist_timeout_ms() {
 // NCCL finishes it in the background.  Poll its state until it settles or the
 // deadline passes; on expiry (or any error) abort the communicator so no rank
 // is left waiting on it, and report G4_E_DIST.
+// Pause between polls of an operation in progress: the first polls only yield
+// the CPU (a collective that is being enqueued finishes within microseconds;
+// a sleep would add its whole length to every call), later ones sleep.
+static void poll_pause(int& it) {
+  if (++it < 4000) sched_yield();
+  else usleep(it < 8000 ? 20 : 200);
+}
+
 static int nccl_settle(g4_ctx* c, ncclComm_t comm, ncclResult_t r, long long deadline_ms, const char* what) {
+  int it = 0;
   while (r == ncclInProgress) {
     if (now_ms() > deadline_ms) {
       g_nccl.commAbort(comm);
@@ -424,7 +434,7 @@ static int nccl_settle(g4_ctx* c, ncclComm_t comm, ncclResult_t r, long long dea
       c->set_err("%s: timed out (a peer rank did not answer); communicator aborted", what);
       return G4_E_DIST;
     }
-    usleep(200);
+    poll_pause(it);
     if (g_nccl.commGetAsyncError(comm, &r) != ncclSuccess) r = ncclSystemError;
   }
   if (r != ncclSuccess) {
@@ -550,6 +560,7 @@ int g4_nccl_alltoallv(g4_ctx* c, const void* send, const size_t* soff, const siz
 // answering ends in G4_E_DIST (communicator aborted) rather than a hung host.
 int g4_dist_stream_wait(g4_ctx* c, cudaStream_t st) {
   const long long deadline = now_ms() + c->dist_timeout_ms;
+  int it = 0;
   for (;;) {
     const cudaError_t q = cudaStreamQuery(st);
     if (q == cudaSuccess) return 0;
@@ -569,6 +580,6 @@ int g4_dist_stream_wait(g4_ctx* c, cudaStream_t st) {
                  c->dist_timeout_ms);
       return G4_E_DIST;
     }
-    usleep(50);
+    poll_pause(it);
   }
 }
