@@ -498,6 +498,37 @@ def decode_bytes_per_token(cfg, src, position: int) -> int:
     return total
 
 
+def bench_prefill(model, toks, generated, torch, dev, chunk: int = 64):
+    """The prompt (<bos> + 128 ids) through g4_batch_step as chunks of up to 64
+    consecutive positions of one slot (batched prefill); CUDA events on the
+    batch's stream around the chunks, after two warm-up passes."""
+    b = model.new_batch(chunk, len(toks))
+    stream = torch.cuda.ExternalStream(b.stream, device=dev)
+    chunks = [(p0, min(p0 + chunk, len(toks))) for p0 in range(0, len(toks), chunk)]
+
+    def run():
+        nt = None
+        for p0, p1 in chunks:
+            _, nt = b.step(toks[p0:p1], np.arange(p0, p1, dtype=np.int32), want_logits=False,
+                           slots=np.zeros(p1 - p0, np.int32))
+        return nt
+
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    nt = run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    b.free()
+    return {"tok_s": round(len(toks) / (ms * 1e-3), 1), "ms": round(ms, 3), "chunk": chunk,
+            "first_generated_matches": bool(int(nt[-1]) == int(generated[0])),
+            "note": "prompt positions fed as chunks of one KV slot through g4_batch_step (K/V rows of a chunk "
+                    "written before its attention); the last row's argmax is the decoder's first generated token"}
+
+
 def bench_decode(g4, ctx, torch, dev, with_cpu: bool = True):
     """Configuration 4 (dense decoder, seed 3): greedy decode of 256 tokens
     after <bos> + 128 random prompt ids, one CUDA graph per step, every step
@@ -554,6 +585,7 @@ def bench_decode(g4, ctx, torch, dev, with_cpu: bool = True):
                 "h2d_bytes_per_step": int(toks.nbytes), "d2h_bytes_per_step": int(n_gen * 4),
                 "note": "one g4_decode_greedy call: 129 prompt ids in from host memory, 256 generated ids out"},
         "stream_matches_e2e": bool(np.array_equal(out, generated)),
+        "prefill": bench_prefill(model, toks, generated, torch, dev),
         "gpu_launches_per_token": cfg.n_layers * 5 + 2,
         "timing": "CUDA events on the state's stream around 128 prompt steps and 256 generating steps "
                   "(graph launches, no host synchronisation between steps); weights 1.7 GB >> L2",
@@ -855,7 +887,10 @@ def profile_mode(args):
     if args.c5_steps:
         import dataclasses
 
-        m = synth.SynthDecoder(dataclasses.replace(synth.C5_MOE, replicate_layers=True), seed=4)
+        spec = dataclasses.replace(synth.C5_MOE, replicate_layers=True)
+        if args.c5_layers:
+            spec = dataclasses.replace(spec, n_layers=args.c5_layers)
+        m = synth.SynthDecoder(spec, seed=4)
         model = g4.DecoderModel(ctx, g4.TensorSource.from_synth(m))
         batch = model.new_batch(64, 768)
         toks = np.full(64, 1000, np.int32)
@@ -920,6 +955,7 @@ def main():
     ap.add_argument("--no-c5", action="store_true")
     ap.add_argument("--c5-steps", type=int, default=0,
                     help="profiling mode: run this many C5 batched steps (64 sequences) and exit")
+    ap.add_argument("--c5-layers", type=int, default=0, help="profiling mode: C5 with this many layers (small captures)")
     ap.add_argument("--only", default=None,
                     help="profiling mode: run one sweep case FORMAT:ROWSxCOLS (e.g. Q4_K:262144x1536) --reps times")
     ap.add_argument("--reps", type=int, default=3)

@@ -67,7 +67,7 @@ SIGNATURES = {
     "g4_state_stream": (_vp, [_vp]),
     "g4_batch_create": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
     "g4_batch_free": (_i, [_vp]),
-    "g4_batch_step": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
+    "g4_batch_step": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "g4_batch_stream": (_vp, [_vp]),
     "g4_batch_expert_parallel": (_i, [_vp]),
 }

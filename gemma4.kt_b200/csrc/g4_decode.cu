@@ -83,6 +83,7 @@ struct AttnArgs {
   // elements); chunk_stride CTAs per query head along x.  Single-sequence
   // decode: pos_arr == nullptr, strides 0, chunk_stride kAttnMaxChunks.
   const int* pos_arr;
+  const int* slot_arr;     // batched: KV-cache slot of each grid row (nullptr: slot = row)
   long long qkv_stride, kv_stride, part_stride, out_stride;
   int tick_stride, chunk_stride;
   int target_chunks;       // chunks per KV head aimed at (attn_chunk)
@@ -136,8 +137,9 @@ __global__ void __launch_bounds__(kAttnThreads, HMAX == 1 ? 1 : 3) dec_attention
   const int gs = blockIdx.x / a.chunk_stride, c = blockIdx.x % a.chunk_stride;
   const int g = gs / nsub, hq0 = g * a.kv_mul + (gs % nsub) * H;  // first query head of this CTA
   const float* qkv = a.qkv + sq * a.qkv_stride;
-  float* kc = a.kc + sq * a.kv_stride;
-  float* vc = a.vc + sq * a.kv_stride;
+  const long long slot = a.slot_arr ? a.slot_arr[sq] : sq;
+  float* kc = a.kc + slot * a.kv_stride;
+  float* vc = a.vc + slot * a.kv_stride;
   float* part_base = a.part + sq * a.part_stride;
   unsigned* tickets = a.tickets + sq * a.tick_stride;
   float* out = a.out + sq * a.out_stride;
@@ -350,6 +352,31 @@ __global__ void __launch_bounds__(kAttnThreads, HMAX == 1 ? 1 : 3) dec_attention
     }
   }
   if (tid == 0) tickets[gs] = 0u;  // every chunk has arrived: ready for the next launch
+}
+
+// Batched steps: the K/V rows of every token of the step (Llama.kt:174-195:
+// K learned norm then RoPE, V bare norm) written to its sequence's cache
+// before any attention of the step reads them, so that tokens of one
+// sequence at consecutive positions (a prompt chunk) see each other's rows.
+// Grid (KV head, token); warp 0 K, warp 1 V.
+__global__ void __launch_bounds__(64) batch_kv_write_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(16) float kvrow[];  // [2][hs]
+  const int g = blockIdx.x, sq = blockIdx.y, hs = a.hs, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = a.pos_arr[sq];
+  const long long slot = a.slot_arr ? a.slot_arr[sq] : sq;
+  const float* qkv = a.qkv + sq * a.qkv_stride;
+  float* v = kvrow + warp * hs;
+  const float* src = qkv + (warp == 0 ? a.k_off : a.v_off) + (size_t)g * hs;
+  for (int i = lane; i < hs; i += 32) v[i] = src[i];
+  __syncwarp();
+  if (warp == 0) {
+    head_rmsnorm(v, a.k_norm, hs, a.eps, lane);
+    head_rope(v, a.cr + (size_t)pos * (hs / 2), a.ci + (size_t)pos * (hs / 2), hs, lane);
+  } else {
+    head_rmsnorm(v, nullptr, hs, a.eps, lane);
+  }
+  float* dst = (warp == 0 ? a.kc : a.vc) + slot * a.kv_stride + (size_t)pos * a.kvdim + (size_t)g * hs;
+  for (int i = lane; i < hs; i += 32) dst[i] = v[i];
 }
 
 // Greedy sampling (Sampler.ARGMAX, FloatTensor.argmax): the logits GEMV left
@@ -1327,11 +1354,11 @@ struct g4_batch {
   int8_t* lim = nullptr;
   float* lsc = nullptr;
   unsigned long long* keys = nullptr;
-  int *d_tok = nullptr, *d_pos = nullptr;
+  int *d_tok = nullptr, *d_pos = nullptr, *d_slot = nullptr;
   unsigned* tickets = nullptr;
   float* gemm_part = nullptr;   // split-K partial sums of the batched GEMMs
   unsigned* gemm_tickets = nullptr;
-  int* h_io = nullptr;          // pinned: tokens [n_max], positions [n_max]
+  int* h_io = nullptr;          // pinned: tokens [n_max], positions [n_max], slots [n_max]
   unsigned long long* h_keys = nullptr;  // pinned [n_max]
   std::map<std::tuple<int, int, int>, MmaBatchPlan> plans;
   // expert parallelism (g4_batch_expert_parallel): per layer, this rank's experts
@@ -1432,9 +1459,9 @@ extern "C" int g4_batch_create(g4_model* m, int n_max, int max_positions, g4_bat
   const size_t widest = std::max<size_t>(dim, std::max<size_t>(m->max_q, m->max_ff));
   const size_t lim_bytes = (N * (widest / 32) * 96 + 255) / 256 * 256;
   const size_t lsc_bytes = (N * (widest / 32) * 4 + 255) / 256 * 256;
-  const size_t small = lim_bytes + lsc_bytes + 256 + 3 * ((N * 8 + 255) / 256 * 256) + N * k.n_heads * 4;
+  const size_t small = lim_bytes + lsc_bytes + 256 + 4 * ((N * 8 + 255) / 256 * 256) + N * k.n_heads * 4;
   if (cudaMalloc(&b->buf, off * 4) != cudaSuccess || cudaMalloc(&b->small, small) != cudaSuccess ||
-      cudaMallocHost(&b->h_io, N * 8) != cudaSuccess || cudaMallocHost(&b->h_keys, N * 8) != cudaSuccess ||
+      cudaMallocHost(&b->h_io, N * 12) != cudaSuccess || cudaMallocHost(&b->h_keys, N * 8) != cudaSuccess ||
       cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking) != cudaSuccess) {
     cudaGetLastError();
     g4_batch_free(b);
@@ -1467,6 +1494,8 @@ extern "C" int g4_batch_create(g4_model* m, int n_max, int max_positions, g4_bat
   b->d_tok = reinterpret_cast<int*>(p);
   p += (N * 8 + 255) / 256 * 256;
   b->d_pos = reinterpret_cast<int*>(p);
+  p += (N * 8 + 255) / 256 * 256;
+  b->d_slot = reinterpret_cast<int*>(p);
   p += (N * 8 + 255) / 256 * 256;
   b->tickets = reinterpret_cast<unsigned*>(p);
   // split-K scratch of the batched GEMMs (plans at the widest batch)
@@ -1554,8 +1583,8 @@ static int batch_prologue(g4_batch* b, const GemvFuse& f, const float* x, int di
   return e ? b->m->ctx->cuda_fail((cudaError_t)e, what) : 0;
 }
 
-extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* positions, int n, float* logits_host,
-                             int* next_tokens_host) {
+extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* positions, const int* slots, int n,
+                             float* logits_host, int* next_tokens_host) {
   if (!b) return G4_E_ARG;
   g4_model* m = b->m;
   g4_ctx* c = m->ctx;
@@ -1564,19 +1593,30 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
     c->set_err("g4_batch_step: bad arguments (%d sequences, at most %d)", n, b->n_max);
     return G4_E_ARG;
   }
-  for (int i = 0; i < n; ++i)
-    if (tokens[i] < 0 || tokens[i] >= k.vocab || positions[i] < 0 || positions[i] >= b->max_pos) {
-      c->set_err("g4_batch_step: sequence %d: token %d / position %d out of range (vocab %d, %d positions)", i,
-                 tokens[i], positions[i], k.vocab, b->max_pos);
+  for (int i = 0; i < n; ++i) {
+    const int sl = slots ? slots[i] : i;
+    if (tokens[i] < 0 || tokens[i] >= k.vocab || positions[i] < 0 || positions[i] >= b->max_pos || sl < 0 ||
+        sl >= b->n_max) {
+      c->set_err("g4_batch_step: row %d: token %d / position %d / slot %d out of range (vocab %d, %d positions, "
+                 "%d slots)", i, tokens[i], positions[i], sl, k.vocab, b->max_pos, b->n_max);
       return G4_E_ARG;
     }
+    if (slots)
+      for (int j = 0; j < i; ++j)
+        if (slots[j] == sl && positions[j] == positions[i]) {
+          c->set_err("g4_batch_step: rows %d and %d both write position %d of slot %d", j, i, positions[i], sl);
+          return G4_E_ARG;
+        }
+  }
   if (int r = c->bind()) return r;
   cudaStream_t st = b->st;
   if (cudaError_t e = cudaStreamSynchronize(st)) return c->cuda_fail(e, "g4_batch_step");
   std::memcpy(b->h_io, tokens, (size_t)n * 4);
   std::memcpy(b->h_io + b->n_max, positions, (size_t)n * 4);
+  for (int i = 0; i < n; ++i) b->h_io[2 * b->n_max + i] = slots ? slots[i] : i;
   cudaError_t ce = cudaMemcpyAsync(b->d_tok, b->h_io, (size_t)n * 4, cudaMemcpyHostToDevice, st);
   if (!ce) ce = cudaMemcpyAsync(b->d_pos, b->h_io + b->n_max, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+  if (!ce) ce = cudaMemcpyAsync(b->d_slot, b->h_io + 2 * b->n_max, (size_t)n * 4, cudaMemcpyHostToDevice, st);
   if (ce) return c->cuda_fail(ce, "g4_batch_step: staging");
   const int dim = k.dim;
   int cur = 0;
@@ -1632,7 +1672,7 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
     aa.ci = L.swa ? m->ci_swa : m->ci_full;
     aa.kc = b->kc[L.kv_src];
     aa.vc = b->vc[L.kv_src];
-    aa.write_kv = own ? 1 : 0;
+    aa.write_kv = 0;  // the step's K/V rows are written first, by batch_kv_write_kernel
     aa.window = L.swa ? k.sliding_window : 0;
     aa.part = b->part;
     aa.tickets = b->tickets;
@@ -1640,6 +1680,7 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
     aa.ch_max = batch_ch_max(L.hs);
     aa.status = c->status;
     aa.pos_arr = b->d_pos;
+    aa.slot_arr = b->d_slot;
     aa.qkv_stride = qkv_n;
     aa.kv_stride = (long long)b->max_pos * L.kvdim;
     aa.part_stride = (long long)b->part_stride;
@@ -1656,6 +1697,10 @@ extern "C" int g4_batch_step(g4_batch* b, const int* tokens, const int* position
       nch_max = std::max(nch_max, (len + ch - 1) / ch);
     }
     aa.chunk_stride = nch_max;
+    if (own) {
+      batch_kv_write_kernel<<<dim3(L.n_kv, n), 64, (size_t)2 * L.hs * 4, st>>>(aa);
+      if (cudaError_t e = cudaGetLastError()) return c->cuda_fail(e, "batch: K/V rows");
+    }
     attn_fn(aa.kv_mul)<<<dim3(L.n_kv * nch_max, n), kAttnThreads, attn_smem(L.hs, aa.kv_mul, aa.ch_max), st>>>(aa);
     if (cudaError_t e = cudaGetLastError()) return c->cuda_fail(e, "batch: attention");
     // ---- output projection

@@ -693,7 +693,8 @@ int launch_gemm_mma_batch(const MmaBatchPlan& p, const uint8_t* packed, const in
 int launch_batch_prologue(const GemvFuse& f, const float* x, int dim, int T, int8_t* lim, float* lsc,
                           cudaStream_t st) {
   cudaGetLastError();
-  if (T <= 0 || dim <= 0 || dim % 32 || dim > 4096) return (int)cudaErrorInvalidValue;
+  // the activation row and the reduction space fit the default 48 KB of shared memory
+  if (T <= 0 || dim <= 0 || dim % 32 || (size_t)(dim + 64) * 4 > 48 * 1024) return (int)cudaErrorInvalidValue;
   BatchPrologueArgs a{f, x, dim, lim, lsc};
   const size_t smem = (size_t)(dim + 64) * 4;
   batch_prologue_kernel<<<T, 512, smem, st>>>(a);

@@ -294,16 +294,23 @@ class DecoderBatch:
         (Context.dist_init); from now on every rank steps together."""
         check(lib().g4_batch_expert_parallel(self.handle), self.model.ctx.handle, "g4_batch_expert_parallel")
 
-    def step(self, tokens, positions, want_logits: bool = True):
-        """Llama.forward for sequences 0..n-1: (logits [n, vocab] or None, argmax [n])."""
+    def step(self, tokens, positions, want_logits: bool = True, slots=None):
+        """Llama.forward for n rows (row i: tokens[i] at positions[i] of the
+        sequence in slot slots[i], default i): (logits [n, vocab] or None,
+        argmax [n]).  Rows of one slot at consecutive positions prefill a
+        prompt chunk in one step."""
         t = np.ascontiguousarray(tokens, np.int32)
         p = np.ascontiguousarray(positions, np.int32)
         if t.shape != p.shape or t.ndim != 1:
             raise ValueError("tokens and positions must be 1-D and of equal length")
+        s = None if slots is None else np.ascontiguousarray(slots, np.int32)
+        if s is not None and s.shape != t.shape:
+            raise ValueError("slots must match tokens")
         n = t.size
         lg = np.empty((n, self.model.cfg.vocab), np.float32) if want_logits else None
         nt = np.empty(n, np.int32)
-        check(lib().g4_batch_step(self.handle, t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p), n,
+        check(lib().g4_batch_step(self.handle, t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p),
+                                  None if s is None else s.ctypes.data_as(C.c_void_p), n,
                                   lg.ctypes.data_as(C.c_void_p) if want_logits else None,
                                   nt.ctypes.data_as(C.c_void_p)),
               self.model.ctx.handle, "g4_batch_step")

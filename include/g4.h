@@ -303,12 +303,15 @@ void *g4_state_stream(g4_state *state);
 typedef struct g4_batch g4_batch;
 int g4_batch_create(g4_model *model, int n_max, int max_positions, g4_batch **out);
 int g4_batch_free(g4_batch *batch);
-/* Llama.forward for sequences 0..n-1: tokens[i] at positions[i] (positions of
- * one sequence must be fed in order from 0, as generateTokens does).
- * logits_host [n][vocab] (after softcapping) and next_tokens_host [n] (argmax,
- * first maximum) may be NULL.  Synchronous. */
-int g4_batch_step(g4_batch *batch, const int *tokens, const int *positions, int n, float *logits_host,
-                  int *next_tokens_host);
+/* Llama.forward for n rows at once: row i feeds tokens[i] at positions[i] of
+ * the sequence in KV slot slots[i] (slots NULL: slot i).  Several rows may
+ * belong to one slot at distinct positions (a prompt chunk, prefilled in one
+ * step: every row's K/V row is written before any row attends); every
+ * earlier position of a slot must have been fed before, as generateTokens
+ * does.  logits_host [n][vocab] (after softcapping) and next_tokens_host [n]
+ * (argmax, first maximum) may be NULL.  Synchronous. */
+int g4_batch_step(g4_batch *batch, const int *tokens, const int *positions, const int *slots, int n,
+                  float *logits_host, int *next_tokens_host);
 /* The batch's cudaStream_t. */
 void *g4_batch_stream(g4_batch *batch);
 /* Expert parallelism for a batch (no counterpart in the reference, which runs

@@ -12,7 +12,7 @@ import pytest
 
 from oracle import oracle
 from tests.conftest import rel_l2
-from tests.test_decode_gpu import MIN_MARGIN, SEEDS, SPECS, _models
+from tests.test_decode_gpu import MIN_MARGIN, SEEDS, SPECS, _models, _spec
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
@@ -79,6 +79,46 @@ def test_batch_64_sequences(g4, ctx):
     B operand) on the dense model."""
     worst = run_batch(g4, ctx, "q8-gqa8", n_seq=64, steps=70, prompt_len=3, stagger=1)
     print(f"\n64 sequences: batched logits rel L2 max {worst:.2e}")
+
+
+def test_batch_prefill_vs_oracle(g4, ctx):
+    """Prompts prefilled in chunks: rows of one slot at consecutive positions
+    in one step (each row's K/V row is written before any row attends, so the
+    chunk's tokens see each other causally), two sequences interleaved in
+    slots 0 and 1 with chunk sizes that cross the sliding window, then greedy
+    decode of both.  Vocab 2050: the output GEMM's last row tile is partial."""
+    from gemma4_kt_b200 import synth
+
+    spec = _spec(shared_kv_layers=1, vocab=2050)
+    m = synth.SynthDecoder(spec, seed=21)
+    src = g4.TensorSource.from_synth(m)
+    model = g4.DecoderModel(ctx, src)
+    batch = model.new_batch(24, 64)
+    orcs = [oracle.ModelOracle(src) for _ in range(2)]
+    toks = [list(np.concatenate([[2], m.prompt(30, seed=700 + i)]).astype(int)) for i in range(2)]
+    # (sequence, first position, rows) per step: prompt chunks, then single greedy steps
+    plan = [[(0, 0, 20), (1, 0, 4)], [(0, 20, 11), (1, 4, 13)], [(1, 17, 14)]] + [[(0, 31 + k, 1), (1, 31 + k, 1)]
+                                                                                 for k in range(8)]
+    worst = 0.0
+    for step in plan:
+        rows = [(sq, p) for sq, p0, n in step for p in range(p0, p0 + n)]
+        tk = [toks[sq][p] for sq, p in rows]
+        lg, nt = batch.step(tk, [p for _, p in rows], slots=[sq for sq, _ in rows])
+        for i, (sq, p) in enumerate(rows):
+            ref = orcs[sq].step(toks[sq][p], p)
+            err = rel_l2(lg[i], ref)
+            worst = max(worst, err)
+            assert err < TOL, (sq, p, err)
+            if p + 1 >= len(toks[sq]):  # generated: the argmax feeds the next step
+                assert nt[i] == int(np.argmax(ref)), (sq, p)
+                toks[sq].append(int(nt[i]))
+    print(f"\nprefill + decode: logits rel L2 max {worst:.2e}")
+    with pytest.raises(g4.G4Error):
+        batch.step([5, 6], [40, 40], slots=[0, 0])  # one position of one slot written twice
+    for o in orcs:
+        o.close()
+    batch.free()
+    model.free()
 
 
 def test_batch_rejects(g4, ctx):
