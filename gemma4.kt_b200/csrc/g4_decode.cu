@@ -997,6 +997,15 @@ extern "C" int g4_state_free(g4_state* s) {
   return 0;
 }
 
+// Query heads per attention CTA of the single-sequence decoder: G4_ATTN_HEADS
+// (a divisor of the group size; default 1).
+static int attn_heads_per_cta(int kv_mul) {
+  const char* e = getenv("G4_ATTN_HEADS");
+  int h = e ? atoi(e) : 1;
+  if (h < 1 || h > kv_mul || kv_mul % h) h = 1;
+  return h;
+}
+
 // The attention kernel compiled for at least `heads` query heads per CTA.
 using AttnFn = void (*)(const AttnArgs);
 static AttnFn attn_fn(int heads) {
@@ -1127,13 +1136,15 @@ static int enqueue_step(g4_state* s) {
     aa.status = c->status;
     aa.chunk_stride = kAttnMaxChunks;
     aa.target_chunks = 8;
-    aa.heads_per_cta = 1;  // one sequence: a CTA per (query head, chunk) keeps the grid wide
+    aa.heads_per_cta = attn_heads_per_cta(aa.kv_mul);  // one sequence: keep the grid wide
     const size_t asmem = attn_smem(L.hs, aa.heads_per_cta, aa.ch_max);
     // the attribute is a cap shared by every user of the kernel (single and batched decode): the device's limit
     if (asmem > (size_t)c->dev.smem_optin ||
-        cudaFuncSetAttribute(attn_fn(1), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->dev.smem_optin))
+        cudaFuncSetAttribute(attn_fn(aa.heads_per_cta), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)c->dev.smem_optin))
       return c->cuda_fail(cudaGetLastError(), "decode: attention set-up");
-    cudaError_t ce = launch_pdl_k(attn_fn(1), k.n_heads * kAttnMaxChunks, kAttnThreads, asmem, st, aa);
+    cudaError_t ce = launch_pdl_k(attn_fn(aa.heads_per_cta), k.n_heads / aa.heads_per_cta * kAttnMaxChunks,
+                                  kAttnThreads, asmem, st, aa);
     if (ce) return c->cuda_fail(ce, "decode: attention");
     // ---- output projection of the attention output
     e = launch_proj(L.m_wo, L.k_wo, L.d_wo, L.p_wo, L.wo, s->xbk, s->xb2, GemvFuse{}, c->status, st, true);
