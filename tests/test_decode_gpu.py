@@ -169,3 +169,65 @@ def test_decoder_from_gguf_file(g4, ctx, tmp_path):
     assert np.array_equal(got, ref), (got, ref)
     st.free()
     model.free()
+
+
+C5_GOLDEN = Path(__file__).resolve().parent / "golden" / "c5_greedy.npz"
+
+
+def _batched_stream(model, toks, n):
+    """<bos> + prompt prefilled in 64-row chunks of one slot, then n - 1 single-row steps."""
+    b = model.new_batch(64, toks.size + n)
+    nt = None
+    for p0 in range(0, toks.size, 64):
+        p1 = min(p0 + 64, toks.size)
+        _, nt = b.step(toks[p0:p1], np.arange(p0, p1, dtype=np.int32), want_logits=False,
+                       slots=np.zeros(p1 - p0, np.int32))
+    gen = [int(nt[-1])]
+    for i in range(n - 1):
+        _, nt = b.step([gen[-1]], [toks.size + i], want_logits=False)
+        gen.append(int(nt[0]))
+    b.free()
+    return np.array(gen, np.int32)
+
+
+def test_c5_moe_greedy_64_tokens(g4, ctx, monkeypatch):
+    """Configuration 5 geometry at full size (MoE decoder, seed 4; the layer
+    matrices shared by the 30 layers as in the benchmark), one sequence:
+    <bos> + 512 random prompt ids, then greedy decode.  The single-sequence
+    decoder (one CUDA graph per step, the MoE layers on the one-token decode
+    kernels) must give the oracle's 64 tokens (fixture,
+    tests/golden/make_c5_golden.py), and so must the batched decoder (the
+    prompt prefilled in 64-row chunks of one slot) with the chunks' MoE
+    layers on the fp32 CUDA-core expert kernels.  With the chunks' experts on
+    the tensor-core path (fp16 weights, ~5e-4 per token) the stream is only
+    reported: it leaves the oracle's after about 20 tokens on this fixture."""
+    import dataclasses
+
+    from gemma4_kt_b200 import synth
+
+    gold = np.load(C5_GOLDEN)
+    m = synth.SynthDecoder(dataclasses.replace(synth.C5_MOE, replicate_layers=True), seed=int(gold["seed"]))
+    prompt = m.prompt(512)
+    np.testing.assert_array_equal(prompt, gold["prompt"])
+    model = g4.DecoderModel(ctx, g4.TensorSource.from_synth(m))
+    del m
+    ref = gold["generated"]
+    n = ref.size
+    toks = np.concatenate([[2], prompt]).astype(np.int32)
+    st = model.new_state()
+    got = st.generate(toks, n)
+    st.free()
+
+    def first_diff(a):
+        return int(np.argmax(a != ref)) if np.any(a != ref) else n
+
+    monkeypatch.setenv("G4_MOE_TC", "0")
+    first_cc = first_diff(_batched_stream(model, toks, n))
+    monkeypatch.setenv("G4_MOE_TC", "1")
+    first_tc = first_diff(_batched_stream(model, toks, n))
+    model.free()
+    print(f"\nC5 greedy (smallest routing margin of the oracle run {float(gold['topk_margin']):.1e}): first "
+          f"difference at generated token {first_diff(got)} of {n} (decoder); batched prefill + decode: "
+          f"{first_cc} (CUDA-core experts), {first_tc} (tensor-core experts)")
+    assert first_diff(got) == n, (got, ref)
+    assert first_cc == n, first_cc
