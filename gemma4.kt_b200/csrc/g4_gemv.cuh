@@ -75,7 +75,7 @@ constexpr int kBatchMaxT = 64;
 struct MmaBatchPlan {
   int rows, cols, nrt, nkb;
   int ng;              // token groups of 8 the kernel is compiled for (1, 2, 4, 8)
-  int nrb;             // row blocks of 8 row tiles (128 rows)
+  int nrb, rb_rows;    // row blocks (of 8 row tiles, or 4 from 16 tokens on) and their rows
   int splits, kps;     // K splits over CTAs and blocks per split (a multiple of the staged chunk)
   int ntasks, grid;
   size_t smem;
@@ -83,7 +83,7 @@ struct MmaBatchPlan {
 };
 // Partial sums (floats) and tickets (row blocks) the batched GEMM needs for T tokens.
 inline size_t mma_batch_partials(const MmaBatchPlan& p, int T) {
-  return p.splits > 1 ? (size_t)p.splits * (size_t)T * (size_t)p.nrb * 128 : 0;
+  return p.splits > 1 ? (size_t)p.splits * (size_t)T * (size_t)p.nrb * (size_t)p.rb_rows : 0;
 }
 
 // Options of plan_gemv.

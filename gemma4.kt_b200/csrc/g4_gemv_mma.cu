@@ -429,13 +429,16 @@ struct MmaBatchArgs {
   int T, ldy, out_mode;
   float softcap;
   unsigned long long* argmax;  // OUT_SOFTCAP_ARGMAX: [T] keys (atomicMax)
-  float* part;          // [splits][T][nrb * 128] partial sums (splits > 1)
+  float* part;          // [splits][T][nrb * rows per block] partial sums (splits > 1)
   unsigned* tickets;    // [nrb] splits finished per row block
 };
 
 constexpr int kBatchKc = 4;      // blocks (32 columns) per staged chunk of the activations
 constexpr int kBatchRow = 112;   // bytes per token in a staged block: 96 limb bytes + 16 (bank spread)
-constexpr int kBatchRt = 8;      // row tiles per row block (a warp each)
+// Warps per row tile: two (each with half of the token groups) from 16 tokens
+// on, so a warp holds fewer accumulators and more warps fit an SM.
+__host__ __device__ constexpr int batch_wt(int ng) { return ng >= 2 ? 2 : 1; }
+__host__ __device__ constexpr int batch_rt(int ng) { return 8 / batch_wt(ng); }  // row tiles per row block
 
 // One output of the batched GEMM: plain, gelu(gate) * up (value of the even
 // row, `up` its odd neighbour), or softcap with the token's arg-max key.
@@ -454,7 +457,8 @@ __device__ __forceinline__ void batch_out(const MmaBatchArgs& a, int row, int tk
 }
 
 // Y[t][row] = W[row] . x_t for T tokens on the repacked tiles.  A CTA task is
-// a row block (kBatchRt row tiles, a warp each) x one of `splits` K ranges;
+// a row block (batch_rt row tiles; batch_wt warps per tile, each with its share
+// of the token groups) x one of `splits` K ranges;
 // per block of 32 columns a warp runs one mma per limb and group of 8 tokens
 // (the group's tokens are the B operand's columns), its next weight tile in
 // flight.  The tokens' limbs travel through shared memory in chunks of
@@ -463,10 +467,11 @@ __device__ __forceinline__ void batch_out(const MmaBatchArgs& a, int row, int tk
 // stores its partial sums, and the row block's last split to finish (a ticket
 // counter) adds them in split order and finishes the outputs.
 template <int NG>
-__global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const __grid_constant__ MmaBatchArgs a) {
+__global__ void __launch_bounds__(kMmaWarps * 32, 3) gemm_mma_batch_kernel(const __grid_constant__ MmaBatchArgs a) {
   // [2][kBatchKc][8 NG][kBatchRow] limbs, [2][kBatchKc][8 NG] scales, [8 NG] arg-max keys, the last-split flag
   extern __shared__ __align__(16) uint8_t bsm[];
   constexpr int TT = 8 * NG;
+  constexpr int WT = batch_wt(NG), RT = batch_rt(NG), NGW = NG / WT, RB = RT * 16;
   constexpr int kStage = kBatchKc * TT * kBatchRow;
   float* ssc = reinterpret_cast<float*>(bsm + 2 * kStage);
   unsigned long long* sbest = reinterpret_cast<unsigned long long*>(ssc + 2 * kBatchKc * TT);
@@ -475,9 +480,10 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int T = a.T, nkb = p.nkb;
   constexpr float kInv1 = 1.0f / 254.0f, kInv2 = 1.0f / 64516.0f;
-  unsigned long long best[NG][2];
+  const int sub = warp % RT, half = warp / RT;  // row tile of the block, share of the token groups
+  unsigned long long best[NGW][2];
 #pragma unroll
-  for (int G = 0; G < NG; ++G) best[G][0] = best[G][1] = 0ull;
+  for (int gg = 0; gg < NGW; ++gg) best[gg][0] = best[gg][1] = 0ull;
   if (a.out_mode == OUT_SOFTCAP_ARGMAX)
     for (int i = threadIdx.x; i < TT; i += blockDim.x) sbest[i] = 0ull;
 
@@ -497,13 +503,13 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
 
   for (int task = blockIdx.x; task < p.ntasks; task += gridDim.x) {
     const int rb = task / p.splits, sp = task % p.splits;
-    const int rt = rb * kBatchRt + warp;
-    const bool ract = rt < p.nrt;
+    const int rt = rb * RT + sub;
+    const bool ract = rt < p.nrt && half * NGW * 8 < T;
     const int kb_beg = sp * p.kps, kb_end = min(nkb, kb_beg + p.kps);
     const int nch = (kb_end - kb_beg + kBatchKc - 1) / kBatchKc;
-    float acc[NG][4];
+    float acc[NGW][4];
 #pragma unroll
-    for (int G = 0; G < NG; ++G) acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.f;
+    for (int gg = 0; gg < NGW; ++gg) acc[gg][0] = acc[gg][1] = acc[gg][2] = acc[gg][3] = 0.f;
     const uint4* qt = a.q + (size_t)rt * nkb * 32 + lane;
     const uint32_t* st = a.sc + (size_t)rt * nkb * 8 + g;
     uint4 An = make_uint4(0u, 0u, 0u, 0u);
@@ -535,7 +541,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
         if (ract) {
           const float d0 = f16_bits_to_f32((uint16_t)(S & 0xFFFFu)), d8 = f16_bits_to_f32((uint16_t)(S >> 16));
 #pragma unroll
-          for (int G = 0; G < NG; ++G) {
+          for (int gg = 0; gg < NGW; ++gg) {
+            const int G = half * NGW + gg;
             if (G * 8 < T) {  // uniform
               const uint32_t* bp =
                   reinterpret_cast<const uint32_t*>(bsrc + (kk * TT + G * 8 + g) * kBatchRow + 4 * t);
@@ -548,7 +555,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const float v = fmaf(mma_f32(dl[i]), kInv2, fmaf(mma_f32(dm[i]), kInv1, mma_f32(dh[i])));
-                acc[G][i] = fmaf(v, sc[i], acc[G][i]);
+                acc[gg][i] = fmaf(v, sc[i], acc[gg][i]);
               }
             }
           }
@@ -561,15 +568,16 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
     if (p.splits == 1) {
       if (ract) {
 #pragma unroll
-        for (int G = 0; G < NG; ++G) {
+        for (int gg = 0; gg < NGW; ++gg) {
+          const int G = half * NGW + gg;
           if (G * 8 < T) {
             float o[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, acc[G][i], 4);  // row g ^ 1
+            for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, acc[gg][i], 4);  // row g ^ 1
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int row = r0 + 8 * (i >> 1), tk = G * 8 + 2 * t + (i & 1);
-              if (row < p.rows && tk < T) batch_out(a, row, tk, acc[G][i], o[i], best[G][i & 1]);
+              if (row < p.rows && tk < T) batch_out(a, row, tk, acc[gg][i], o[i], best[gg][i & 1]);
             }
           }
         }
@@ -577,14 +585,15 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
       continue;
     }
     // split-K: partial sums of this split, then the row block's last split finishes
-    float* pp = a.part + (size_t)sp * T * (p.nrb * 128);
+    float* pp = a.part + (size_t)sp * T * (p.nrb * RB);
     if (ract) {
 #pragma unroll
-      for (int G = 0; G < NG; ++G) {
+      for (int gg = 0; gg < NGW; ++gg) {
+        const int G = half * NGW + gg;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int row = r0 + 8 * (i >> 1), tk = G * 8 + 2 * t + (i & 1);
-          if (tk < T) pp[(size_t)tk * (p.nrb * 128) + row] = acc[G][i];
+          if (tk < T) pp[(size_t)tk * (p.nrb * RB) + row] = acc[gg][i];
         }
       }
     }
@@ -597,11 +606,11 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
     if (!s_last) continue;
     __threadfence();  // acquire: the other splits' partials are visible
     // thread -> (token, row pair) of the row block; sums in split order
-    for (int e = threadIdx.x; e < T * 64; e += blockDim.x) {
-      const int tk = e / 64, row = rb * 128 + 2 * (e % 64);
+    for (int e = threadIdx.x; e < T * (RB / 2); e += blockDim.x) {
+      const int tk = e / (RB / 2), row = rb * RB + 2 * (e % (RB / 2));
       float v0 = 0.f, v1 = 0.f;
       for (int s2 = 0; s2 < p.splits; ++s2) {
-        const float* q2 = a.part + ((size_t)s2 * T + tk) * (p.nrb * 128) + row;
+        const float* q2 = a.part + ((size_t)s2 * T + tk) * (p.nrb * RB) + row;
         v0 += __ldcg(q2);
         v1 += __ldcg(q2 + 1);
       }
@@ -615,10 +624,11 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) gemm_mma_batch_kernel(const
   if (a.out_mode == OUT_SOFTCAP_ARGMAX) {
     // per token: the warps' bests (lanes g of one column t) and the split-K finishers' into shared memory
 #pragma unroll
-    for (int G = 0; G < NG; ++G)
+    for (int gg = 0; gg < NGW; ++gg)
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        unsigned long long b = best[G][j];
+        const int G = half * NGW + gg;
+        unsigned long long b = best[gg][j];
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) {
           const unsigned long long v = __shfl_xor_sync(0xffffffffu, b, o);
@@ -653,7 +663,8 @@ MmaBatchPlan plan_gemm_mma_batch(const DeviceInfo& dev, int rows, int cols, int 
   p.ng = T <= 8 ? 1 : T <= 16 ? 2 : T <= 32 ? 4 : 8;
   p.nrt = (rows + 15) / 16;
   p.nkb = cols / 32;
-  p.nrb = (p.nrt + kBatchRt - 1) / kBatchRt;
+  p.nrb = (p.nrt + batch_rt(p.ng) - 1) / batch_rt(p.ng);
+  p.rb_rows = 16 * batch_rt(p.ng);
   p.smem = (size_t)2 * kBatchKc * 8 * p.ng * kBatchRow + (size_t)2 * kBatchKc * 8 * p.ng * 4 +
            (size_t)8 * p.ng * 8 + 16;
   BatchFn fn = batch_fn(p.ng);
