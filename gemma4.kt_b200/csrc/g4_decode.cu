@@ -22,9 +22,18 @@
 // with programmatic stream serialization: a GEMV streams its first weight
 // stages before waiting for its predecessor.  The step index, the input token
 // and the position live in device memory, so a greedy generation of N tokens
-// is N graph launches with no host round trip.  The GEMVs use two-part int16
-// activations (fp32-level products): with attention scale 1.0 on normalised
-// q and k, activation errors of a few 1e-5 visibly move the attention weights.
+// is N graph launches with no host round trip.  The GEMVs use fp32-level
+// activations (three int8 limbs on the Q8_0 tensor-core tiles, two-part int16
+// on the CUDA-core decoders): with attention scale 1.0 on normalised q and k,
+// activation errors of a few 1e-5 visibly move the attention weights.
+//
+// The second half of the file is the batched decoder (g4_batch_*): up to 64
+// rows per step, each a (token, position, KV slot), so many sequences advance
+// together (configuration 5) or one sequence's prompt is prefilled in chunks;
+// per layer a per-token prologue into int8 limbs, the T-token GEMM on the
+// repacked Q8_0 tiles (g4_gemv_mma.cu), a K/V-row pre-pass, the attention
+// kernel with a row grid axis, and the MoE layer on the step's tokens (across
+// GPUs: expert-parallel, g4_batch_expert_parallel).
 #include "g4.h"
 #include "g4_ctx.h"
 #include "g4_gemv.cuh"

@@ -20,6 +20,11 @@
 // shared memory for the epilogue (plain, gelu(gate) * up on interleaved rows,
 // or softcap + arg-max).  The first task's weights are requested before the
 // kernel waits for its predecessor (programmatic dependent launch).
+//
+// The batched decoder's kernels follow: batch_prologue_kernel (a token's fused
+// prologue and its limbs, one CTA per token) and gemm_mma_batch_kernel (the
+// same tiles for up to 64 tokens, the tokens as the B operand's columns, the
+// limbs staged in shared memory, split-K with a deterministic reduction).
 #include "g4_fuse.cuh"
 #include "g4_gemv.cuh"
 #include "g4_internal.h"
