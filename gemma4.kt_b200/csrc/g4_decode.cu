@@ -456,7 +456,8 @@ struct g4_model {
   std::vector<LayerDev> L;
   const g4_tensor* wcls = nullptr;
   GemvPlan p_logits{};
-  uint8_t* k_cls = nullptr;  // the output matrix repacked for the batched decoder (g4_batch_create)
+  MmaGemvPlan m_logits{};    // the output projection on the tensor-core tiles (Q8_0), used when fast
+  uint8_t* k_cls = nullptr;  // the output matrix repacked (the decoder's logits, the batched decoder)
   float *cr_full = nullptr, *ci_full = nullptr, *cr_swa = nullptr, *ci_swa = nullptr;
   bool finalized = false;
   int max_q = 0, max_kv = 0, max_ff = 0, max_hs = 0;
@@ -875,6 +876,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
     c->set_err("g4_model_finalize: the output projection needs a streaming-kernel format");
     return G4_E_TYPE;
   }
+  if (mma_wanted())  // a Q8_0 output matrix also runs on the tensor-core tiles
+    if (int r = make_mma(c, m->wcls, k.vocab, dim, false, true, m->m_logits, m->k_cls)) return r;
   // ModelLoader.loadWeights (ModelLoader.kt:154-166): SWA tables from theta_swa, full from rope_freqs
   std::vector<float> cr, ci;
   rope_table(k.ctx_len, k.head_size_swa, (double)k.rope_theta_swa, nullptr, cr, ci);
@@ -1203,7 +1206,10 @@ static int enqueue_step(g4_state* s) {
   f.softcap = k.logit_softcap;
   f.argmax = s->argmax;
   set_prefetch(f, {proj_w(m->L[0].qkv, m->L[0].k_qkv, m->L[0].m_qkv)});  // the next step's first projection
-  int e = launch_gemv_fused(m->p_logits, (const uint8_t*)m->wcls->d, s->x[cur], s->logits, f, c->status, st, true);
+  int e = m->m_logits.fast && m->k_cls
+              ? launch_gemv_mma(m->m_logits, m->k_cls, s->x[cur], s->logits, f, c->status, st, true)
+              : launch_gemv_fused(m->p_logits, (const uint8_t*)m->wcls->d, s->x[cur], s->logits, f, c->status, st,
+                                  true);
   if (e) return c->cuda_fail((cudaError_t)e, "decode: logits");
   cudaError_t ce = launch_pdl_k(dec_sample_kernel, 1, 32, 0, st, s->ctl, s->out_tok(), s->argmax);
   if (ce) return c->cuda_fail(ce, "decode: sampling");
